@@ -1,0 +1,173 @@
+/*
+ * moe_layer.h -- B200-native MoE FFN block of a GLM-4.x decoder layer.
+ *
+ * These entry points have no counterpart in the reference's C-ABI: the
+ * reference's libkernels/libcublaswrap cannot express block-scaled FP8,
+ * grouped expert GEMMs, bf16 activations or expert parallelism
+ * (csrc/kernels.h:12-31, csrc/cublas_wrappers.h:51-67).  They replace the MoE
+ * branch of the reference's layer forward, src/terra/engine.t:1310-1369
+ * (post-attention RMSNorm -> moe_gate -> moe_topk -> moe_dispatch -> per-slot
+ * dequant + SGEMM gate/up -> swiglu -> dequant + SGEMM down -> moe_combine ->
+ * add_residual), whose intended semantics are spelled out in
+ * src/futhark/kernels.fut:324-368 (moe_router, moe_expert_mlp, moe_forward).
+ *
+ * Conventions
+ *   - Plain pointers and sizes only.  Device pointers unless stated.  The
+ *     caller owns every buffer; nothing here allocates device memory except
+ *     moe_layer_create (its handle's small state) -- the forward takes a
+ *     caller-provided workspace.
+ *   - Layouts are row-major.  Activations: [tokens][hidden] bf16.  Weights
+ *     are [out][in] (K-major) e4m3 bytes with fp32 block scales over 128x128
+ *     blocks, scale layout [out/128][in/128] per expert ("weight_scale_inv"
+ *     convention: real weight = decode(q) * scale).
+ *   - Streams are cwStream_t (a cudaStream_t, cuda_wrappers.h).
+ *   - Every function returns an moe_status_t; 0 is success.  A device-side
+ *     wait that gave up (no progress for ~2 s) is reported as
+ *     MOE_ERR_DEVICE_TIMEOUT by moe_layer_check_error / the forward.
+ */
+#ifndef MOE_LAYER_H
+#define MOE_LAYER_H
+
+#include <stdint.h>
+#include <stddef.h>
+#include "cuda_wrappers.h"
+#include "nccl_wrappers.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    MOE_OK = 0,
+    MOE_ERR_INVALID_ARGUMENT = 1,
+    MOE_ERR_CUDA = 2,
+    MOE_ERR_UNSUPPORTED = 3,
+    MOE_ERR_DEVICE_TIMEOUT = 4,
+    MOE_ERR_NCCL = 5,
+    MOE_ERR_WORKSPACE = 6
+} moe_status_t;
+
+const char* moe_status_string(moe_status_t status);
+
+/* ------------------------------------------------------------------ layer */
+
+typedef struct {
+    int hidden;          /* H, multiple of 128 */
+    int num_experts;     /* E routed experts (global) */
+    int top_k;           /* 1..16 */
+    int intermediate;    /* I, multiple of 128 */
+    int num_shared;      /* 0 or 1 shared expert */
+    float rms_eps;       /* post-attention RMSNorm epsilon */
+    int max_tokens;      /* tokens per forward call on this rank */
+    int ep_size;         /* expert-parallel ranks (1 = single GPU) */
+    int ep_rank;         /* this rank; owns experts [r*E/ep, (r+1)*E/ep) */
+} moe_layer_config_t;
+
+typedef struct {
+    const float* norm_gamma;   /* [H] fp32 */
+    const float* router_w;     /* [E][H] fp32 (all experts, replicated) */
+    const float* router_bias;  /* [E] fp32 or NULL, added to the logits */
+    /* Local experts first (E/ep_size of them, in global order), then the
+     * shared expert if num_shared == 1.  Gate rows [0,I) then up rows [I,2I). */
+    const void* w13;           /* [E_local+S][2I][H] e4m3 */
+    const float* s13;          /* [E_local+S][2I/128][H/128] */
+    const void* w2;            /* [E_local+S][H][I] e4m3 */
+    const float* s2;           /* [E_local+S][H/128][I/128] */
+} moe_layer_weights_t;
+
+typedef struct moe_layer moe_layer_t;
+
+/* Validates the shapes, encodes the weight TMA descriptors and allocates the
+ * handle's device error word.  `comm` is an ncwComm_t over the ep_size ranks
+ * (NULL when ep_size == 1).  Weight pointers must stay valid. */
+moe_status_t moe_layer_create(const moe_layer_config_t* cfg, const moe_layer_weights_t* w,
+                              ncwComm_t comm, moe_layer_t** out);
+moe_status_t moe_layer_destroy(moe_layer_t* layer);
+
+/* Workspace the forward needs for max_tokens tokens (bytes). */
+size_t moe_layer_workspace_bytes(const moe_layer_t* layer);
+
+/* out = x + MoE(RMSNorm(x)) for `num_tokens` <= max_tokens tokens:
+ *   RMSNorm (reference order) -> router logits (fp32) -> top-k (reference
+ *   tie-break) -> stable expert permutation -> FP8 1x128 activation quant ->
+ *   grouped block-scaled FP8 gate/up GEMM + SwiGLU + FP8 requant -> grouped
+ *   down GEMM (bf16) -> weighted combine + shared expert + residual (bf16).
+ * x and out may not alias.  Stream-ordered; no host synchronisation when
+ * ep_size == 1.  With ep_size > 1 the per-peer token counts are exchanged
+ * through NCCL and read back once per call (one host sync). */
+moe_status_t moe_layer_forward(moe_layer_t* layer, const void* x_bf16, void* out_bf16,
+                               int num_tokens, void* workspace, size_t workspace_bytes,
+                               cwStream_t stream);
+
+/* Same, with the routing supplied by the caller ([T][top_k] expert ids and
+ * weights on the device) instead of computed from router_w. */
+moe_status_t moe_layer_forward_routed(moe_layer_t* layer, const void* x_bf16,
+                                      const int32_t* topk_idx, const float* topk_w,
+                                      void* out_bf16, int num_tokens, void* workspace,
+                                      size_t workspace_bytes, cwStream_t stream);
+
+/* Routing of the last forward (device pointers into the workspace):
+ * topk_idx [T][k] int32, topk_w [T][k] fp32, counts [E_local+S] int32. */
+moe_status_t moe_layer_last_routing(const moe_layer_t* layer, const void* workspace,
+                                    const int32_t** topk_idx, const float** topk_w,
+                                    const int32_t** group_counts);
+
+/* Reads and clears the device error word (synchronises `stream`). */
+moe_status_t moe_layer_check_error(moe_layer_t* layer, cwStream_t stream);
+
+/* -------------------------------------------------------------- components
+ * The stages of the forward, exposed for the engine and for parity tests.
+ * T = tokens, H = hidden, E = experts, k = top_k, G = groups (experts + shared).
+ */
+
+/* Per token: rms = sqrtf(sum(x^2)/H + eps) with the reference's reduction
+ * order (csrc/kernels.cu:61-85); n = (x / rms) * gamma (fp32); then n is
+ * quantised per 128-column block: xq = e4m3_rne(n * 448/amax),
+ * xs[blk][t] = amax/448 (xs is [H/128][xs_ld]).  rms_out may be NULL. */
+moe_status_t moe_rmsnorm_quant(const void* x_bf16, const float* gamma, int T, int H, float eps,
+                               float* rms_out, void* xq_out, float* xs_out, int xs_ld,
+                               cwStream_t stream);
+
+/* Router: logits[t][e] = fma-chain over i = 0..H-1 of n[t][i]*W[e][i]
+ * (+ bias[e]), n recomputed from x, rms, gamma exactly as above; then the
+ * reference's top-k (strict '>' from -FLT_MAX: lower index wins ties, NaN
+ * never chosen; csrc/kernels.cu:437-471) and weights exp(v)/sum exp(v) over
+ * the selected slots (max-subtracted when the top logit exceeds 80).
+ * logits_out may be NULL. */
+moe_status_t moe_router_topk(const void* x_bf16, const float* rms, const float* gamma,
+                             const float* router_w, const float* router_bias,
+                             int T, int H, int E, int k,
+                             float* logits_out, int32_t* topk_idx, float* topk_w,
+                             cwStream_t stream);
+
+/* Stable counting sort of the (token, slot) pairs by expert id (the pair
+ * order t*k+s is kept within an expert), experts [e_begin, e_end) only,
+ * followed by `num_shared` groups holding every token in order.  Segments
+ * start at multiples of 16 rows.  Outputs (device): counts[G], seg_start[G],
+ * pos[T*k] (row of each pair, -1 when its expert is not local or invalid),
+ * row_token[row_capacity] (token of each row, -1 for padding/unused rows),
+ * total_rows[1].  Fails on the device (error word) if row_capacity is too
+ * small. */
+moe_status_t moe_permute(const int32_t* topk_idx, int T, int k, int e_begin, int e_end,
+                         int num_shared, int32_t* counts, int32_t* seg_start, int32_t* pos,
+                         int32_t* row_token, int32_t* total_rows, int row_capacity,
+                         int* error_word, cwStream_t stream);
+
+/* xp[r] = xq[row_token[r]] (zero row when row_token[r] < 0) and
+ * xps[blk][r] = xs[blk][row_token[r]] for r < row_capacity. */
+moe_status_t moe_gather_rows(const void* xq, const float* xs, int xs_ld, const int32_t* row_token,
+                             int row_capacity, int H, void* xp, float* xps, int xps_ld,
+                             cwStream_t stream);
+
+/* out[t] = bf16( x[t] + sum_{shared g} y[seg_start[g]+t]
+ *               + sum_s w[t][s] * y[pos[t*k+s]] )   (pos < 0 skipped).
+ * The additions run in that order in fp32 (fma for the weighted terms). */
+moe_status_t moe_combine(const void* x_bf16, const void* y_bf16, const int32_t* pos,
+                         const float* topk_w, const int32_t* shared_rows, int num_shared,
+                         int T, int k, int H, void* out_bf16, cwStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOE_LAYER_H */

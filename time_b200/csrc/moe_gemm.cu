@@ -1,0 +1,552 @@
+// moe_gemm.cu -- grouped, 128x128 block-scaled FP8 expert GEMM for sm_100a.
+//
+// Replaces the reference's per-top-k-slot "launch_fp8_dequantize + cbwSgemm"
+// expert loop (src/terra/engine.t:1321-1346; intended semantics
+// src/futhark/kernels.fut:343-368) with one persistent kernel per projection:
+//
+//   gate/up  (CBW_GEMM_GATED_SWIGLU): h = silu(W_gate x) * (W_up x), quantised
+//            to e4m3 with one fp32 scale per 128 output columns (the input
+//            format of the down projection);
+//   down     (CBW_GEMM_DOWN_BF16):    y = W_down h, written as bf16.
+//
+// Design (one CTA per SM, persistent over a device-built tile list):
+//   * Operands are "swap-AB": the UMMA M side (128 lanes of TMEM) is 128
+//     weight rows -- exactly one 128x128 scale block -- and the N side is up
+//     to N_MAX tokens of one expert, so ragged expert groups pad only to 16
+//     tokens.  Tiles of one (expert, weight-row block) are adjacent in the
+//     list, so concurrently running CTAs share each weight tile through L2.
+//   * warp 0: TMA producer (weights box 128x128 B, tokens in 32-row boxes,
+//     token scales by bulk copy) into a STAGES-deep shared-memory ring.
+//   * warp 1: allocates TMEM (512 columns) and issues tcgen05.mma kind::f8f6f4
+//     (4 x K=32 per 128-wide K block) into one of two TMEM partial buffers;
+//     a fresh partial per K block, since the fp32 block scales differ per K
+//     block and tcgen05's own block scaling only takes power-of-two scales.
+//   * warp 2: folds the K block's weight scale into the token scales
+//     (c[n] = a_scale[n] * w_scale) once per CTA per K block.
+//   * warps 3..18: "promotion": tcgen05.ld the partial, acc += partial * c
+//     with packed fp32x2 FMAs in registers, release the TMEM buffer; at the
+//     end of a tile run the fused epilogue (SwiGLU + requant, or bf16) through
+//     a transposing shared-memory stage so global stores are row-contiguous.
+//   * Every mbarrier wait is bounded (~2 s); on timeout the CTA raises an
+//     abort flag, drains its own TMA/MMA work, frees TMEM and reports through
+//     the error word instead of hanging the GPU.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "sm100.cuh"
+#include "cublas_wrappers.h"
+
+namespace {
+
+using namespace tb;
+
+constexpr int kBlockK = 128;            // K bytes (e4m3 elements) per stage
+constexpr int kTileM = 128;             // weight rows per UMMA (TMEM lanes)
+constexpr int kFirstPromoWarp = 3;
+constexpr int kNumPromoWarps = 16;
+constexpr int kNumThreads = (kFirstPromoWarp + kNumPromoWarps) * 32;   // 608
+constexpr int kMaxGroups = 512;
+constexpr int kTmemCols = 512;
+constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
+constexpr uint64_t kDrainTimeoutNs = 200000000ull;
+
+template <bool kGated>
+struct GemmCfg {
+    static constexpr int kNMax = kGated ? 128 : 256;       // tokens per tile
+    static constexpr int kStages = 3;
+    static constexpr int kATiles = kGated ? 2 : 1;          // gate + up
+    static constexpr int kABytes = kATiles * kTileM * kBlockK;
+    static constexpr int kBBytes = kNMax * kBlockK;
+    static constexpr int kStageBytes = kABytes + kBBytes;   // 48 KB either way
+    static constexpr int kNumCombined = kGated ? 2 : 1;
+    static constexpr int kBufCols = 256;                    // TMEM columns per partial buffer
+    static constexpr int kColsPerWarp = kNMax / 4;          // 32 (gated) / 64 (down)
+    static constexpr int kOutStageBytes = kGated ? kNMax * 128 * 4 : kNMax * 128 * 2;
+    // shared-memory carve-up (offsets from the 1024-aligned base)
+    static constexpr int kOffStages = 0;
+    static constexpr int kOffOut = kOffStages + kStages * kStageBytes;
+    static constexpr int kOffRawScale = kOffOut + kOutStageBytes;
+    static constexpr int kOffCombScale = kOffRawScale + kStages * kNMax * 4;
+    static constexpr int kOffTables = kOffCombScale + kStages * kNumCombined * kNMax * 4;
+    static constexpr int kOffBars = kOffTables + (4 * kMaxGroups + 2) * 4;   // prefix, chunks, start, count
+    static constexpr int kNumBars = 3 * kStages + 4;
+    static constexpr int kOffMisc = kOffBars + kNumBars * 8;
+    static constexpr int kSmemBytes = kOffMisc + 64 + 1024;  // + alignment slack
+    static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+};
+
+struct GemmParams {
+    const float* a_scale;   // [K/128][a_ld]
+    int a_ld;
+    const float* w_scale;   // [G][w_rows/128][K/128]
+    const int32_t* count;   // [G]
+    const int32_t* start;   // [G]
+    void* out;
+    float* out_scale;
+    int out_ld;
+    int G;
+    int K;
+    int N;                  // output columns per group
+    int w_rows;             // weight rows per group (2N gated, N down)
+    int* error_word;
+};
+
+struct TileCoord {
+    int g, nb, row0, nrows, ntile;
+};
+
+__device__ __forceinline__ TileCoord decode_tile(int tile, const int* prefix, const int* chunks,
+                                                 const int* starts, const int* counts, int G,
+                                                 int n_max) {
+    int lo = 0, hi = G - 1;
+    while (lo < hi) {
+        int mid = (lo + hi + 1) >> 1;
+        if (prefix[mid] <= tile) lo = mid; else hi = mid - 1;
+    }
+    TileCoord c;
+    c.g = lo;
+    int local = tile - prefix[lo];
+    int C = chunks[lo];
+    c.nb = local / C;
+    int chunk = local - c.nb * C;
+    c.row0 = starts[lo] + chunk * n_max;
+    c.nrows = min(n_max, counts[lo] - chunk * n_max);
+    c.ntile = (c.nrows + 15) & ~15;
+    return c;
+}
+
+// Wait that ignores the abort flag (used only to drain own async work).
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (globaltimer_ns() - t0 > kDrainTimeoutNs) break;
+    }
+}
+
+template <bool kGated>
+__global__ void __maxnreg__(104)
+grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
+                        const __grid_constant__ CUtensorMap tmap_a,
+                        const GemmParams p) {
+    using C = GemmCfg<kGated>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+
+    float* raw_scale = reinterpret_cast<float*>(smem + C::kOffRawScale);
+    float* comb_scale = reinterpret_cast<float*>(smem + C::kOffCombScale);
+    int* t_prefix = reinterpret_cast<int*>(smem + C::kOffTables);           // [G+1]
+    int* t_chunks = t_prefix + (kMaxGroups + 1);                            // [G]
+    int* t_start = t_chunks + kMaxGroups;                                   // [G]
+    int* counts_smem = t_start + kMaxGroups;                                // [G]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBars);
+    uint64_t* full_bar = bars;
+    uint64_t* empty_bar = bars + C::kStages;
+    uint64_t* cready_bar = bars + 2 * C::kStages;
+    uint64_t* tfull_bar = bars + 3 * C::kStages;
+    uint64_t* tempty_bar = tfull_bar + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffMisc);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kOffMisc + 8);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int G = p.G;
+    const int KB = p.K / kBlockK;
+
+    // ---------------------------------------------------------------- setup
+    if (warp == 0 && lane == 0) {
+        for (int s = 0; s < C::kStages; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1 + kNumPromoWarps);
+            mbar_init(&cready_bar[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull_bar[b], 1);
+            mbar_init(&tempty_bar[b], kNumPromoWarps);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+        prefetch_tmap(&tmap_w);
+        prefetch_tmap(&tmap_a);
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+    if (warp == 2) {
+        // tiles per group: ceil(count / N_MAX) token chunks x (N / 128) row blocks
+        const int nbt = p.N / 128;
+        int per_lane = (G + 31) / 32;
+        int g0 = lane * per_lane;
+        int local = 0;
+        for (int i = 0; i < per_lane; ++i) {
+            int g = g0 + i;
+            if (g < G) {
+                int cnt = p.count[g];
+                int ch = (cnt + C::kNMax - 1) / C::kNMax;
+                t_chunks[g] = ch;
+                t_start[g] = p.start[g];
+                counts_smem[g] = cnt;
+                local += ch * nbt;
+            }
+        }
+        int incl = local;
+        for (int o = 1; o < 32; o <<= 1) {
+            int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        int run = incl - local;
+        for (int i = 0; i < per_lane; ++i) {
+            int g = g0 + i;
+            if (g < G) {
+                t_prefix[g] = run;
+                run += t_chunks[g] * nbt;
+            }
+        }
+        if (lane == 31) t_prefix[G] = incl;
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int total_tiles = t_prefix[G];
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            int s = 0;
+            uint32_t phase = 0;
+            uint32_t armed_mask = 0, armed_phase = 0;   // per stage: last arm and its phase
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+                TileCoord tc = decode_tile(tile, t_prefix, t_chunks, t_start, counts_smem, G, C::kNMax);
+                const int b_loads = (tc.ntile + 31) >> 5;
+                const uint32_t bytes = C::kABytes + b_loads * 32 * kBlockK + tc.ntile * 4;
+                const int wrow = tc.g * p.w_rows + tc.nb * kTileM;
+                for (int kb = 0; kb < KB; ++kb) {
+                    if (!mbar_wait_bounded(&empty_bar[s], phase ^ 1, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
+                    uint8_t* st = smem + C::kOffStages + s * C::kStageBytes;
+                    mbar_arrive_expect_tx(&full_bar[s], bytes);
+                    tma_load_2d(&tmap_w, &full_bar[s], st, kb * kBlockK, wrow);
+                    if (kGated) tma_load_2d(&tmap_w, &full_bar[s], st + kTileM * kBlockK, kb * kBlockK, wrow + p.N);
+                    for (int r = 0; r < b_loads; ++r)
+                        tma_load_2d(&tmap_a, &full_bar[s], st + C::kABytes + r * 32 * kBlockK, kb * kBlockK, tc.row0 + 32 * r);
+                    bulk_load(raw_scale + s * C::kNMax, p.a_scale + (size_t)kb * p.a_ld + tc.row0,
+                              tc.ntile * 4, &full_bar[s]);
+                    armed_mask |= 1u << s;
+                    armed_phase = (armed_phase & ~(1u << s)) | (phase << s);
+                    if (++s == C::kStages) { s = 0; phase ^= 1; }
+                }
+            }
+            if (!ok) {
+                // let every copy this thread issued land before the CTA can exit
+                for (int ss = 0; ss < C::kStages; ++ss)
+                    if (armed_mask & (1u << ss)) mbar_drain(&full_bar[ss], (armed_phase >> ss) & 1u);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            int s = 0, b = 0;
+            uint32_t phase = 0, tphase = 0;
+            bool ok = true;
+            bool issued = false;
+            for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+                TileCoord tc = decode_tile(tile, t_prefix, t_chunks, t_start, counts_smem, G, C::kNMax);
+                const uint32_t idesc = idesc_e4m3_f32(kTileM, tc.ntile);
+                for (int kb = 0; kb < KB; ++kb) {
+                    if (!mbar_wait_bounded(&full_bar[s], phase, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
+                    if (!mbar_wait_bounded(&tempty_bar[b], tphase ^ 1, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(smem + C::kOffStages + s * C::kStageBytes);
+                    const uint32_t b_addr = a_addr + C::kABytes;
+                    const uint32_t d = tmem_base + b * C::kBufCols;
+#pragma unroll
+                    for (int k = 0; k < kBlockK / 32; ++k) {
+                        const uint64_t bdesc = umma_desc_sw128(b_addr + k * 32);
+                        umma_f8(d, umma_desc_sw128(a_addr + k * 32), bdesc, idesc, k > 0 ? 1u : 0u);
+                        if (kGated)
+                            umma_f8(d + 128, umma_desc_sw128(a_addr + kTileM * kBlockK + k * 32), bdesc, idesc,
+                                    k > 0 ? 1u : 0u);
+                    }
+                    umma_commit(&empty_bar[s]);
+                    umma_commit(&tfull_bar[b]);
+                    issued = true;
+                    if (++s == C::kStages) { s = 0; phase ^= 1; }
+                    b ^= 1;
+                    if (b == 0) tphase ^= 1;
+                }
+            }
+            if (!ok && issued) {
+                // the last commit lands after every MMA this thread issued
+                int lb = b ^ 1;
+                uint32_t lph = (b == 0) ? (tphase ^ 1) : tphase;
+                mbar_drain(&tfull_bar[lb], lph);
+            }
+        }
+    } else if (warp == 2) {
+        // ------------------------------------------------------------ scale folding
+        int s = 0;
+        uint32_t phase = 0;
+        bool ok = true;
+        const int wsb = p.w_rows / kTileM;
+        for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+            TileCoord tc = decode_tile(tile, t_prefix, t_chunks, t_start, counts_smem, G, C::kNMax);
+            const float* wsg = p.w_scale + ((size_t)tc.g * wsb + tc.nb) * KB;
+            const float* wsu = p.w_scale + ((size_t)tc.g * wsb + (p.N / kTileM) + tc.nb) * KB;
+            for (int kb = 0; kb < KB; ++kb) {
+                const float sg = __ldg(wsg + kb);
+                const float su = kGated ? __ldg(wsu + kb) : 0.0f;
+                if (!mbar_wait_bounded(&full_bar[s], phase, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
+                const float* rs = raw_scale + s * C::kNMax;
+                float* cs = comb_scale + s * C::kNumCombined * C::kNMax;
+                for (int c = lane; c < tc.ntile; c += 32) {
+                    const float a = rs[c];
+                    cs[c] = a * sg;
+                    if (kGated) cs[C::kNMax + c] = a * su;
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&cready_bar[s]);
+                if (++s == C::kStages) { s = 0; phase ^= 1; }
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ promotion + epilogue
+        const int pw = warp - kFirstPromoWarp;        // 0..15
+        const int quarter = warp & 3;                  // TMEM lane quarter this warp may access
+        const int colgrp = pw >> 2;                    // 0..3
+        const int col0 = colgrp * C::kColsPerWarp;
+        const int row_in_tile = quarter * 32 + lane;   // weight row within the 128-row block
+        const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+        int s = 0, b = 0;
+        uint32_t phase = 0, tphase = 0;
+        bool ok = true;
+
+        constexpr int kChunk = kGated ? 8 : 16;                  // columns per TMEM load
+        constexpr int kChunks = C::kColsPerWarp / kChunk;        // 4 either way
+        constexpr int kAcc = C::kColsPerWarp * C::kNumCombined;  // 64 either way
+
+        for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+            TileCoord tc = decode_tile(tile, t_prefix, t_chunks, t_start, counts_smem, G, C::kNMax);
+            const int active_chunks = max(0, min(kChunks, (tc.ntile - col0 + kChunk - 1) / kChunk));
+            float acc[kAcc];
+#pragma unroll
+            for (int i = 0; i < kAcc; ++i) acc[i] = 0.0f;
+
+            for (int kb = 0; kb < KB; ++kb) {
+                if (!mbar_wait_bounded(&cready_bar[s], phase, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
+                if (!mbar_wait_bounded(&tfull_bar[b], tphase, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
+                tc_fence_after();
+                const float* cs = comb_scale + s * C::kNumCombined * C::kNMax + col0;
+                const uint32_t tbuf = lane_addr + b * C::kBufCols + col0;
+#pragma unroll
+                for (int ch = 0; ch < kChunks; ++ch) {
+                    if (ch < active_chunks) {
+                        if (kGated) {
+                            uint32_t pg[16];
+                            // gate columns [ch*8, ch*8+8) and up columns at +128, one x16-shaped
+                            // request each half: load 8+8 via two x16 requests would waste
+                            // registers, so issue x16 over gate cols and reuse the upper half
+                            // for the up partial of the same columns.
+                            asm volatile(
+                                "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                                : "=r"(pg[0]), "=r"(pg[1]), "=r"(pg[2]), "=r"(pg[3]), "=r"(pg[4]),
+                                  "=r"(pg[5]), "=r"(pg[6]), "=r"(pg[7])
+                                : "r"(tbuf + ch * kChunk));
+                            asm volatile(
+                                "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                                : "=r"(pg[8]), "=r"(pg[9]), "=r"(pg[10]), "=r"(pg[11]), "=r"(pg[12]),
+                                  "=r"(pg[13]), "=r"(pg[14]), "=r"(pg[15])
+                                : "r"(tbuf + 128 + ch * kChunk));
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int j = 0; j < kChunk; j += 2) {
+                                const float2 cg = *reinterpret_cast<const float2*>(cs + ch * kChunk + j);
+                                const float2 cu = *reinterpret_cast<const float2*>(cs + C::kNMax + ch * kChunk + j);
+                                float2 ag = make_float2(acc[ch * kChunk + j], acc[ch * kChunk + j + 1]);
+                                float2 au = make_float2(acc[C::kColsPerWarp + ch * kChunk + j],
+                                                        acc[C::kColsPerWarp + ch * kChunk + j + 1]);
+                                ag = ffma2(make_float2(__uint_as_float(pg[j]), __uint_as_float(pg[j + 1])), cg, ag);
+                                au = ffma2(make_float2(__uint_as_float(pg[8 + j]), __uint_as_float(pg[8 + j + 1])), cu, au);
+                                acc[ch * kChunk + j] = ag.x;
+                                acc[ch * kChunk + j + 1] = ag.y;
+                                acc[C::kColsPerWarp + ch * kChunk + j] = au.x;
+                                acc[C::kColsPerWarp + ch * kChunk + j + 1] = au.y;
+                            }
+                        } else {
+                            uint32_t pv[16];
+                            tmem_ld16(tbuf + ch * kChunk, pv);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int j = 0; j < kChunk; j += 2) {
+                                const float2 c2 = *reinterpret_cast<const float2*>(cs + ch * kChunk + j);
+                                float2 a2 = make_float2(acc[ch * kChunk + j], acc[ch * kChunk + j + 1]);
+                                a2 = ffma2(make_float2(__uint_as_float(pv[j]), __uint_as_float(pv[j + 1])), c2, a2);
+                                acc[ch * kChunk + j] = a2.x;
+                                acc[ch * kChunk + j + 1] = a2.y;
+                            }
+                        }
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&tempty_bar[b]);
+                    mbar_arrive(&empty_bar[s]);
+                }
+                if (++s == C::kStages) { s = 0; phase ^= 1; }
+                b ^= 1;
+                if (b == 0) tphase ^= 1;
+            }
+            if (!ok || *abort_flag) { ok = false; break; }
+
+            // ---------------------------------------------------------- epilogue
+            if (kGated) {
+                float* stage = reinterpret_cast<float*>(smem + C::kOffOut);   // [N_MAX][128] fp32
+#pragma unroll
+                for (int c = 0; c < C::kColsPerWarp; ++c) {
+                    const float g = acc[c];
+                    const float u = acc[C::kColsPerWarp + c];
+                    const float h = (g / (1.0f + expf(-g))) * u;
+                    stage[(col0 + c) * 128 + row_in_tile] = h;
+                }
+                named_bar_sync(1, kNumPromoWarps * 32);
+                uint8_t* outq = reinterpret_cast<uint8_t*>(p.out);
+                for (int c = pw; c < tc.ntile; c += kNumPromoWarps) {
+                    const size_t row = static_cast<size_t>(tc.row0 + c);
+                    uint32_t packed = 0;
+                    float scale = 0.0f;
+                    if (c < tc.nrows) {
+                        const float4 v = *reinterpret_cast<const float4*>(stage + c * 128 + lane * 4);
+                        float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+                        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+                        if (amax > 0.0f) {
+                            const float inv = 448.0f / amax;
+                            const uint32_t lo = cvt_e4m3x2(v.x * inv, v.y * inv);
+                            const uint32_t hi = cvt_e4m3x2(v.z * inv, v.w * inv);
+                            packed = lo | (hi << 16);
+                            scale = amax / 448.0f;
+                        }
+                    }
+                    *reinterpret_cast<uint32_t*>(outq + row * p.N + tc.nb * 128 + lane * 4) = packed;
+                    if (lane == 0) p.out_scale[(size_t)tc.nb * p.out_ld + row] = scale;
+                }
+                named_bar_sync(1, kNumPromoWarps * 32);
+            } else {
+                __nv_bfloat16* stage = reinterpret_cast<__nv_bfloat16*>(smem + C::kOffOut);  // [N_MAX][128]
+#pragma unroll
+                for (int c = 0; c < C::kColsPerWarp; ++c)
+                    stage[(col0 + c) * 128 + row_in_tile] = __float2bfloat16_rn(acc[c]);
+                named_bar_sync(1, kNumPromoWarps * 32);
+                __nv_bfloat16* outy = reinterpret_cast<__nv_bfloat16*>(p.out);
+                for (int c = pw; c < tc.nrows; c += kNumPromoWarps) {
+                    const uint2 v = *reinterpret_cast<const uint2*>(stage + c * 128 + lane * 4);
+                    *reinterpret_cast<uint2*>(outy + static_cast<size_t>(tc.row0 + c) * p.N + tc.nb * 128 + lane * 4) = v;
+                }
+                named_bar_sync(1, kNumPromoWarps * 32);
+            }
+        }
+    }
+
+    // ---------------------------------------------------------------- teardown
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kTmemCols);
+    }
+    if (threadIdx.x == 0 && *abort_flag && p.error_word) atomicExch(p.error_word, 1);
+}
+
+// ------------------------------------------------------------------ host side
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000,
+                                             cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    });
+    return fn;
+}
+
+// 2-D uint8 tensor [rows][cols] (row pitch = cols bytes), box [box_rows][128],
+// 128-byte swizzle, out-of-bounds rows read as zero.
+bool encode_u8_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+    auto fn = get_encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {cols};
+    cuuint32_t box[2] = {128, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+template <bool kGated>
+cbwStatus_t launch_gemm(const cbwGroupedGemmArgs* a, int* error_word, cudaStream_t stream) {
+    using C = GemmCfg<kGated>;
+    const int w_rows = kGated ? 2 * a->N : a->N;
+    CUtensorMap tw, ta;
+    if (!encode_u8_2d(&tw, a->w, static_cast<uint64_t>(a->num_groups) * w_rows, a->K, kTileM)) return CBW_ERROR_INTERNAL;
+    if (!encode_u8_2d(&ta, a->a, static_cast<uint64_t>(a->rows), a->K, 32)) return CBW_ERROR_INTERNAL;
+
+    static int sm_count = 0;
+    static bool attr_set[2] = {false, false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (sm_count == 0) cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev);
+    if (!attr_set[kGated ? 1 : 0]) {
+        if (cudaFuncSetAttribute(grouped_fp8_gemm_kernel<kGated>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 C::kSmemBytes) != cudaSuccess)
+            return CBW_ERROR_EXECUTION_FAILED;
+        attr_set[kGated ? 1 : 0] = true;
+    }
+    GemmParams p;
+    p.a_scale = a->a_scale;
+    p.a_ld = a->a_ld;
+    p.w_scale = a->w_scale;
+    p.count = a->count;
+    p.start = a->start;
+    p.out = a->out;
+    p.out_scale = a->out_scale;
+    p.out_ld = a->out_ld;
+    p.G = a->num_groups;
+    p.K = a->K;
+    p.N = a->N;
+    p.w_rows = w_rows;
+    p.error_word = error_word;
+    grouped_fp8_gemm_kernel<kGated><<<sm_count, kNumThreads, C::kSmemBytes, stream>>>(tw, ta, p);
+    return cudaGetLastError() == cudaSuccess ? CBW_SUCCESS : CBW_ERROR_EXECUTION_FAILED;
+}
+
+}  // namespace
+
+extern "C" cbwStatus_t cbwFp8BlockScaledGroupedGemm(const cbwGroupedGemmArgs* args, int* error_word,
+                                                    cwStream_t stream) {
+    if (!args) return CBW_ERROR_INVALID_VALUE;
+    const cbwGroupedGemmArgs& a = *args;
+    if (a.num_groups <= 0 || a.num_groups > kMaxGroups) return CBW_ERROR_INVALID_VALUE;
+    if (a.K <= 0 || a.K % 128 || a.N <= 0 || a.N % 128 || a.rows <= 0) return CBW_ERROR_INVALID_VALUE;
+    if (!a.a || !a.a_scale || !a.w || !a.w_scale || !a.count || !a.start || !a.out) return CBW_ERROR_INVALID_VALUE;
+    if (a.a_ld < a.rows || a.a_ld % 4) return CBW_ERROR_INVALID_VALUE;
+    if ((reinterpret_cast<uintptr_t>(a.a) | reinterpret_cast<uintptr_t>(a.w) |
+         reinterpret_cast<uintptr_t>(a.a_scale) | reinterpret_cast<uintptr_t>(a.out)) & 15)
+        return CBW_ERROR_INVALID_VALUE;
+    if (a.mode == CBW_GEMM_GATED_SWIGLU) {
+        if (!a.out_scale || a.out_ld < a.rows) return CBW_ERROR_INVALID_VALUE;
+        return launch_gemm<true>(&a, error_word, static_cast<cudaStream_t>(stream));
+    }
+    if (a.mode == CBW_GEMM_DOWN_BF16) return launch_gemm<false>(&a, error_word, static_cast<cudaStream_t>(stream));
+    return CBW_ERROR_INVALID_VALUE;
+}

@@ -1,0 +1,247 @@
+// moe_layer.cu -- the MoE FFN block forward (include/moe_layer.h): owns the
+// workspace layout and issues the stage kernels in stream order.  Replaces
+// the MoE branch of src/terra/engine.t:1310-1369.
+//
+// Data layout in HBM for one call (T tokens, G = local experts + shared):
+//   rms        [T] f32
+//   xq         [T][H] e4m3         token order, 1x128-quantised RMSNorm output
+//   xs         [H/128][T_ld] f32   its scales (transposed: one K block's scales
+//                                  of consecutive rows are contiguous, so the
+//                                  GEMM fetches them with one bulk copy)
+//   topk_idx   [T][k] i32, topk_w [T][k] f32
+//   counts/seg_start [G] i32, total_rows [1] i32, pos [T*k] i32
+//   row_token  [R_cap] i32         token of every expert-ordered row
+//   xp         [R_cap][H] e4m3     rows grouped by expert, segments padded to 16
+//   xps        [H/128][R_cap] f32
+//   hq         [R_cap][I] e4m3     SwiGLU output, 1x128-quantised
+//   hs         [I/128][R_cap] f32
+//   y          [R_cap][H] bf16     expert outputs
+// R_cap = T*k + S*T + 16*G rounded up to 16: every assignment plus the shared
+// expert's T rows plus worst-case segment padding.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <new>
+
+#include "cublas_wrappers.h"
+#include "moe_layer.h"
+
+extern "C" moe_status_t moe_gather_rows_n(const void* xq, const float* xs, int xs_ld, const int32_t* row_token,
+                                          const int32_t* total_rows, int row_capacity, int H, void* xp, float* xps,
+                                          int xps_ld, cwStream_t stream);
+
+struct moe_layer {
+    moe_layer_config_t cfg;
+    moe_layer_weights_t w;
+    ncwComm_t comm;
+    int e_begin, e_end, groups;
+    int* error_word;      // device
+    // workspace layout (byte offsets)
+    size_t off_rms, off_xq, off_xs, off_idx, off_w, off_counts, off_start, off_total, off_pos, off_rowtok,
+        off_xp, off_xps, off_hq, off_hs, off_y, bytes;
+    int xs_ld, rcap;
+};
+
+namespace {
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+void plan_workspace(moe_layer* L) {
+    const moe_layer_config_t& c = L->cfg;
+    const size_t T = static_cast<size_t>(c.max_tokens);
+    const size_t H = c.hidden, I = c.intermediate, K = c.top_k;
+    L->xs_ld = static_cast<int>(align_up(T, 4));
+    L->rcap = static_cast<int>(align_up(T * K + static_cast<size_t>(c.num_shared) * T + 16 * static_cast<size_t>(L->groups), 16));
+    const size_t R = L->rcap;
+    size_t o = 0;
+    auto take = [&o](size_t bytes) { size_t at = o; o = align_up(o + bytes, 256); return at; };
+    L->off_rms = take(T * 4);
+    L->off_xq = take(T * H);
+    L->off_xs = take((H / 128) * L->xs_ld * 4);
+    L->off_idx = take(T * K * 4);
+    L->off_w = take(T * K * 4);
+    L->off_counts = take(L->groups * 4);
+    L->off_start = take(L->groups * 4);
+    L->off_total = take(16);
+    L->off_pos = take(T * K * 4);
+    L->off_rowtok = take(R * 4);
+    L->off_xp = take(R * H);
+    L->off_xps = take((H / 128) * R * 4);
+    L->off_hq = take(R * I);
+    L->off_hs = take((I / 128) * R * 4);
+    L->off_y = take(R * H * 2);
+    L->bytes = o;
+}
+
+template <typename T>
+T* at(void* ws, size_t off) { return reinterpret_cast<T*>(static_cast<char*>(ws) + off); }
+
+moe_status_t cbw_to_moe(cbwStatus_t s) {
+    return s == CBW_SUCCESS ? MOE_OK : (s == CBW_ERROR_INVALID_VALUE ? MOE_ERR_INVALID_ARGUMENT : MOE_ERR_CUDA);
+}
+
+#define MOE_TRY(expr)                      \
+    do {                                   \
+        moe_status_t _s = (expr);          \
+        if (_s != MOE_OK) return _s;       \
+    } while (0)
+
+moe_status_t run_experts(moe_layer* L, const void* x, const int32_t* idx, const float* wts, void* out, int T,
+                         void* ws, cudaStream_t st) {
+    const moe_layer_config_t& c = L->cfg;
+    const int H = c.hidden, I = c.intermediate, K = c.top_k, S = c.num_shared;
+    int32_t* counts = at<int32_t>(ws, L->off_counts);
+    int32_t* start = at<int32_t>(ws, L->off_start);
+    int32_t* total = at<int32_t>(ws, L->off_total);
+    int32_t* pos = at<int32_t>(ws, L->off_pos);
+    int32_t* rowtok = at<int32_t>(ws, L->off_rowtok);
+    MOE_TRY(moe_permute(idx, T, K, L->e_begin, L->e_end, S, counts, start, pos, rowtok, total, L->rcap,
+                        L->error_word, st));
+    MOE_TRY(moe_gather_rows_n(at<void>(ws, L->off_xq), at<float>(ws, L->off_xs), L->xs_ld, rowtok, total, L->rcap, H,
+                              at<void>(ws, L->off_xp), at<float>(ws, L->off_xps), L->rcap, st));
+    cbwGroupedGemmArgs g1;
+    std::memset(&g1, 0, sizeof(g1));
+    g1.mode = CBW_GEMM_GATED_SWIGLU;
+    g1.num_groups = L->groups;
+    g1.K = H;
+    g1.N = I;
+    g1.rows = L->rcap;
+    g1.a = at<void>(ws, L->off_xp);
+    g1.a_scale = at<float>(ws, L->off_xps);
+    g1.a_ld = L->rcap;
+    g1.w = L->w.w13;
+    g1.w_scale = L->w.s13;
+    g1.count = counts;
+    g1.start = start;
+    g1.out = at<void>(ws, L->off_hq);
+    g1.out_scale = at<float>(ws, L->off_hs);
+    g1.out_ld = L->rcap;
+    MOE_TRY(cbw_to_moe(cbwFp8BlockScaledGroupedGemm(&g1, L->error_word, st)));
+    cbwGroupedGemmArgs g2 = g1;
+    g2.mode = CBW_GEMM_DOWN_BF16;
+    g2.K = I;
+    g2.N = H;
+    g2.a = at<void>(ws, L->off_hq);
+    g2.a_scale = at<float>(ws, L->off_hs);
+    g2.w = L->w.w2;
+    g2.w_scale = L->w.s2;
+    g2.out = at<void>(ws, L->off_y);
+    g2.out_scale = nullptr;
+    g2.out_ld = 0;
+    MOE_TRY(cbw_to_moe(cbwFp8BlockScaledGroupedGemm(&g2, L->error_word, st)));
+    const int32_t* shared_rows = start + (L->e_end - L->e_begin);
+    return moe_combine(x, at<void>(ws, L->off_y), pos, wts, shared_rows, S, T, K, H, out, st);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* moe_status_string(moe_status_t s) {
+    switch (s) {
+        case MOE_OK: return "ok";
+        case MOE_ERR_INVALID_ARGUMENT: return "invalid argument";
+        case MOE_ERR_CUDA: return "CUDA error";
+        case MOE_ERR_UNSUPPORTED: return "unsupported configuration";
+        case MOE_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
+        case MOE_ERR_NCCL: return "NCCL error";
+        case MOE_ERR_WORKSPACE: return "workspace too small or row capacity exceeded";
+        default: return "unknown status";
+    }
+}
+
+moe_status_t moe_layer_create(const moe_layer_config_t* cfg, const moe_layer_weights_t* w, ncwComm_t comm,
+                              moe_layer_t** out) {
+    if (!cfg || !w || !out) return MOE_ERR_INVALID_ARGUMENT;
+    *out = nullptr;
+    const moe_layer_config_t& c = *cfg;
+    if (c.hidden <= 0 || c.hidden % 128 || c.intermediate <= 0 || c.intermediate % 128) return MOE_ERR_INVALID_ARGUMENT;
+    if (c.num_experts <= 0 || c.num_experts > 256 || c.top_k <= 0 || c.top_k > 16 || c.top_k > c.num_experts)
+        return MOE_ERR_INVALID_ARGUMENT;
+    if (c.num_shared < 0 || c.num_shared > 1 || c.max_tokens <= 0) return MOE_ERR_INVALID_ARGUMENT;
+    if (c.ep_size <= 0 || c.ep_rank < 0 || c.ep_rank >= c.ep_size || c.num_experts % c.ep_size) return MOE_ERR_INVALID_ARGUMENT;
+    if (c.ep_size > 1 && !comm) return MOE_ERR_INVALID_ARGUMENT;
+    if (c.ep_size > 1) return MOE_ERR_UNSUPPORTED;
+    if (!w->norm_gamma || !w->router_w || !w->w13 || !w->s13 || !w->w2 || !w->s2) return MOE_ERR_INVALID_ARGUMENT;
+    moe_layer* L = new (std::nothrow) moe_layer;
+    if (!L) return MOE_ERR_INVALID_ARGUMENT;
+    std::memset(L, 0, sizeof(*L));
+    L->cfg = c;
+    L->w = *w;
+    L->comm = comm;
+    const int per = c.num_experts / c.ep_size;
+    L->e_begin = c.ep_rank * per;
+    L->e_end = L->e_begin + per;
+    L->groups = per + c.num_shared;
+    if (cudaMalloc(&L->error_word, sizeof(int)) != cudaSuccess) { delete L; return MOE_ERR_CUDA; }
+    if (cudaMemset(L->error_word, 0, sizeof(int)) != cudaSuccess) { cudaFree(L->error_word); delete L; return MOE_ERR_CUDA; }
+    plan_workspace(L);
+    *out = L;
+    return MOE_OK;
+}
+
+moe_status_t moe_layer_destroy(moe_layer_t* L) {
+    if (!L) return MOE_OK;
+    cudaFree(L->error_word);
+    delete L;
+    return MOE_OK;
+}
+
+size_t moe_layer_workspace_bytes(const moe_layer_t* L) { return L ? L->bytes : 0; }
+
+moe_status_t moe_layer_forward_routed(moe_layer_t* L, const void* x, const int32_t* idx, const float* wts, void* out,
+                                      int T, void* ws, size_t ws_bytes, cwStream_t stream) {
+    if (!L || !x || !out || !ws || !idx || !wts) return MOE_ERR_INVALID_ARGUMENT;
+    if (T < 0 || T > L->cfg.max_tokens) return MOE_ERR_INVALID_ARGUMENT;
+    if (ws_bytes < L->bytes) return MOE_ERR_WORKSPACE;
+    if (T == 0) return MOE_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const moe_layer_config_t& c = L->cfg;
+    MOE_TRY(moe_rmsnorm_quant(x, L->w.norm_gamma, T, c.hidden, c.rms_eps, at<float>(ws, L->off_rms),
+                              at<void>(ws, L->off_xq), at<float>(ws, L->off_xs), L->xs_ld, stream));
+    return run_experts(L, x, idx, wts, out, T, ws, st);
+}
+
+moe_status_t moe_layer_forward(moe_layer_t* L, const void* x, void* out, int T, void* ws, size_t ws_bytes,
+                               cwStream_t stream) {
+    if (!L || !x || !out || !ws) return MOE_ERR_INVALID_ARGUMENT;
+    if (T < 0 || T > L->cfg.max_tokens) return MOE_ERR_INVALID_ARGUMENT;
+    if (ws_bytes < L->bytes) return MOE_ERR_WORKSPACE;
+    if (T == 0) return MOE_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const moe_layer_config_t& c = L->cfg;
+    float* rms = at<float>(ws, L->off_rms);
+    MOE_TRY(moe_rmsnorm_quant(x, L->w.norm_gamma, T, c.hidden, c.rms_eps, rms, at<void>(ws, L->off_xq),
+                              at<float>(ws, L->off_xs), L->xs_ld, stream));
+    int32_t* idx = at<int32_t>(ws, L->off_idx);
+    float* wts = at<float>(ws, L->off_w);
+    MOE_TRY(moe_router_topk(x, rms, L->w.norm_gamma, L->w.router_w, L->w.router_bias, T, c.hidden, c.num_experts,
+                            c.top_k, nullptr, idx, wts, stream));
+    return run_experts(L, x, idx, wts, out, T, ws, st);
+}
+
+moe_status_t moe_layer_last_routing(const moe_layer_t* L, const void* ws, const int32_t** idx, const float** wts,
+                                    const int32_t** counts) {
+    if (!L || !ws) return MOE_ERR_INVALID_ARGUMENT;
+    void* w = const_cast<void*>(ws);
+    if (idx) *idx = at<int32_t>(w, L->off_idx);
+    if (wts) *wts = at<float>(w, L->off_w);
+    if (counts) *counts = at<int32_t>(w, L->off_counts);
+    return MOE_OK;
+}
+
+moe_status_t moe_layer_check_error(moe_layer_t* L, cwStream_t stream) {
+    if (!L) return MOE_ERR_INVALID_ARGUMENT;
+    int h = 0;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (cudaMemcpyAsync(&h, L->error_word, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess) return MOE_ERR_CUDA;
+    if (cudaStreamSynchronize(st) != cudaSuccess) return MOE_ERR_CUDA;
+    if (h == 0) return MOE_OK;
+    cudaMemsetAsync(L->error_word, 0, sizeof(int), st);
+    cudaStreamSynchronize(st);
+    return h == 2 ? MOE_ERR_WORKSPACE : MOE_ERR_DEVICE_TIMEOUT;
+}
+
+}  // extern "C"

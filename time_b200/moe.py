@@ -1,0 +1,192 @@
+"""ctypes bindings of include/moe_layer.h and the new entry points of
+include/cublas_wrappers.h / nccl_wrappers.h, plus a small host-side driver in
+the style of the reference's ctypes engine wrapper
+(src/server/engine_wrapper.py:64-98): explicit argtypes, device pointers as
+integers, status codes turned into exceptions.
+
+Device memory and streams come from torch (plumbing only); every computation
+runs in the package's CUDA libraries.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+from . import load
+
+c_int, c_float, c_size_t, c_void_p = ctypes.c_int, ctypes.c_float, ctypes.c_size_t, ctypes.c_void_p
+c_i32p = ctypes.POINTER(ctypes.c_int32)
+
+STATUS = {0: "ok", 1: "invalid argument", 2: "CUDA error", 3: "unsupported configuration",
+          4: "device-side wait timed out", 5: "NCCL error", 6: "workspace too small or row capacity exceeded"}
+
+
+class MoEError(RuntimeError):
+    def __init__(self, fn: str, code: int):
+        super().__init__(f"{fn} failed: {STATUS.get(code, code)} ({code})")
+        self.code = code
+
+
+class LayerConfig(ctypes.Structure):
+    _fields_ = [("hidden", c_int), ("num_experts", c_int), ("top_k", c_int), ("intermediate", c_int),
+                ("num_shared", c_int), ("rms_eps", c_float), ("max_tokens", c_int), ("ep_size", c_int),
+                ("ep_rank", c_int)]
+
+
+class LayerWeights(ctypes.Structure):
+    _fields_ = [("norm_gamma", c_void_p), ("router_w", c_void_p), ("router_bias", c_void_p), ("w13", c_void_p),
+                ("s13", c_void_p), ("w2", c_void_p), ("s2", c_void_p)]
+
+
+class GroupedGemmArgs(ctypes.Structure):
+    _fields_ = [("mode", c_int), ("num_groups", c_int), ("K", c_int), ("N", c_int), ("rows", c_int),
+                ("a", c_void_p), ("a_scale", c_void_p), ("a_ld", c_int), ("w", c_void_p), ("w_scale", c_void_p),
+                ("count", c_void_p), ("start", c_void_p), ("out", c_void_p), ("out_scale", c_void_p),
+                ("out_ld", c_int)]
+
+
+GEMM_GATED_SWIGLU = 0
+GEMM_DOWN_BF16 = 1
+
+_bound = False
+
+
+def libs():
+    global _bound
+    L = load()
+    if not _bound:
+        k = L["libkernels.so"]
+        k.moe_layer_create.argtypes = [ctypes.POINTER(LayerConfig), ctypes.POINTER(LayerWeights), c_void_p,
+                                       ctypes.POINTER(c_void_p)]
+        k.moe_layer_destroy.argtypes = [c_void_p]
+        k.moe_layer_workspace_bytes.argtypes = [c_void_p]
+        k.moe_layer_workspace_bytes.restype = c_size_t
+        k.moe_layer_forward.argtypes = [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_size_t, c_void_p]
+        k.moe_layer_forward_routed.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p,
+                                               c_size_t, c_void_p]
+        k.moe_layer_last_routing.argtypes = [c_void_p, c_void_p, ctypes.POINTER(c_void_p), ctypes.POINTER(c_void_p),
+                                             ctypes.POINTER(c_void_p)]
+        k.moe_layer_check_error.argtypes = [c_void_p, c_void_p]
+        k.moe_rmsnorm_quant.argtypes = [c_void_p, c_void_p, c_int, c_int, c_float, c_void_p, c_void_p, c_void_p,
+                                        c_int, c_void_p]
+        k.moe_router_topk.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
+                                      c_void_p, c_void_p, c_void_p, c_void_p]
+        k.moe_permute.argtypes = [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p,
+                                  c_void_p, c_void_p, c_int, c_void_p, c_void_p]
+        k.moe_gather_rows.argtypes = [c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p, c_int,
+                                      c_void_p]
+        k.moe_combine.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
+                                  c_void_p, c_void_p]
+        k.moe_status_string.restype = ctypes.c_char_p
+        k.kernels_last_error.restype = c_int
+        b = L["libcublaswrap.so"]
+        b.cbwFp8BlockScaledGroupedGemm.argtypes = [ctypes.POINTER(GroupedGemmArgs), c_void_p, c_void_p]
+        _bound = True
+    return L
+
+
+def check(fn: str, code: int) -> None:
+    if code != 0:
+        raise MoEError(fn, code)
+
+
+def ptr(t) -> int | None:
+    """Device pointer of a torch tensor (None passes NULL)."""
+    return None if t is None else t.data_ptr()
+
+
+def stream_ptr(stream=None) -> int:
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+@dataclass
+class MoELayer:
+    """A MoE FFN block bound to device weights (dict from time_b200.synth or
+    real checkpoint tensors) -- the object the engine would hold per layer."""
+    shape: object
+    weights: dict
+    max_tokens: int
+    ep_size: int = 1
+    ep_rank: int = 0
+    comm: int | None = None
+
+    def __post_init__(self):
+        self._k = libs()["libkernels.so"]
+        sh = self.shape
+        self._cfg = LayerConfig(sh.hidden, sh.num_experts, sh.top_k, sh.intermediate, sh.num_shared, sh.eps,
+                                self.max_tokens, self.ep_size, self.ep_rank)
+        w = self.weights
+        self._w = LayerWeights(ptr(w["gamma"]), ptr(w["router_w"]), ptr(w.get("router_bias")), ptr(w["w13"]),
+                               ptr(w["s13"]), ptr(w["w2"]), ptr(w["s2"]))
+        h = c_void_p()
+        check("moe_layer_create", self._k.moe_layer_create(ctypes.byref(self._cfg), ctypes.byref(self._w),
+                                                           self.comm, ctypes.byref(h)))
+        self._h = h
+        self.workspace_bytes = self._k.moe_layer_workspace_bytes(h)
+        self.workspace = None
+
+    def ensure_workspace(self):
+        import torch
+        if self.workspace is None:
+            dev = self.weights["w13"].device
+            self.workspace = torch.empty(self.workspace_bytes, dtype=torch.uint8, device=dev)
+        return self.workspace
+
+    def forward(self, x, out=None, stream=None, routing=None):
+        import torch
+        ws = self.ensure_workspace()
+        if out is None:
+            out = torch.empty_like(x)
+        T = x.shape[0]
+        if routing is None:
+            rc = self._k.moe_layer_forward(self._h, ptr(x), ptr(out), T, ptr(ws), self.workspace_bytes,
+                                           stream_ptr(stream))
+            check("moe_layer_forward", rc)
+        else:
+            idx, wts = routing
+            rc = self._k.moe_layer_forward_routed(self._h, ptr(x), ptr(idx), ptr(wts), ptr(out), T, ptr(ws),
+                                                  self.workspace_bytes, stream_ptr(stream))
+            check("moe_layer_forward_routed", rc)
+        return out
+
+    def check_error(self, stream=None):
+        check("moe_layer_check_error", self._k.moe_layer_check_error(self._h, stream_ptr(stream)))
+
+    def last_routing(self, T: int):
+        """(topk_idx [T][k] int32, topk_w [T][k] f32, group counts [G]) copied to host tensors."""
+        import torch
+        a, b, c = c_void_p(), c_void_p(), c_void_p()
+        check("moe_layer_last_routing", self._k.moe_layer_last_routing(self._h, ptr(self.workspace), ctypes.byref(a),
+                                                                       ctypes.byref(b), ctypes.byref(c)))
+        k = self.shape.top_k
+        G = self.shape.num_experts // self.ep_size + self.shape.num_shared
+        dev = self.workspace.device
+        base = self.workspace.data_ptr()
+
+        def view(p, n, dt):
+            off = p.value - base
+            return self.workspace[off: off + n * torch.tensor([], dtype=dt).element_size()].view(dt).clone()
+
+        return view(a, T * k, torch.int32).view(T, k), view(b, T * k, torch.float32).view(T, k), view(c, G, torch.int32)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self._k.moe_layer_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def grouped_gemm(mode: int, a, a_scale, a_ld: int, w, w_scale, count, start, out, out_scale, out_ld: int,
+                 K: int, N: int, rows: int, error_word=None, stream=None):
+    L = libs()
+    args = GroupedGemmArgs(mode, count.numel(), K, N, rows, ptr(a), ptr(a_scale), a_ld, ptr(w), ptr(w_scale),
+                           ptr(count), ptr(start), ptr(out), ptr(out_scale), out_ld)
+    rc = L["libcublaswrap.so"].cbwFp8BlockScaledGroupedGemm(ctypes.byref(args), ptr(error_word), stream_ptr(stream))
+    check("cbwFp8BlockScaledGroupedGemm", rc)

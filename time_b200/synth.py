@@ -1,0 +1,112 @@
+"""Seeded synthetic inputs for the MoE FFN block (shapes of BASELINE.json's
+configurations), generated with torch so the same code runs on the CPU (small
+parity cases) and on the GPU (full-size benchmark weights).
+
+Draw order for one seed: x, router weight, router bias permutation, then for
+every expert e = 0..E-1 its gate, up and down matrices, then the shared
+expert.  Weights ~ N(0, 0.02) are quantised to E4M3 per 128x128 block with
+scale = amax / 448 (q = rne(w * 448/amax)); the zipf bias is
+b_e = -1.1 * ln(pi_e) for a seeded permutation pi of 1..E.
+"""
+from __future__ import annotations
+
+import dataclasses
+import math
+
+import torch
+
+
+@dataclasses.dataclass(frozen=True)
+class MoEShape:
+    hidden: int
+    num_experts: int
+    top_k: int
+    intermediate: int
+    num_shared: int = 1
+    eps: float = 1e-5
+
+    @property
+    def groups(self) -> int:
+        return self.num_experts + self.num_shared
+
+
+# BASELINE.json configs[0] (tiny CPU layer) and configs[1] (GLM-4.x MoE FFN)
+TINY = MoEShape(hidden=256, num_experts=8, top_k=2, intermediate=512, num_shared=1, eps=1e-5)
+GLM = MoEShape(hidden=5120, num_experts=160, top_k=8, intermediate=1536, num_shared=1, eps=1e-5)
+
+
+def quantize_blocks(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """[rows][cols] fp32 -> (e4m3 bytes [rows][cols] uint8, scales [rows/128][cols/128] fp32)."""
+    rows, cols = w.shape
+    assert rows % 128 == 0 and cols % 128 == 0
+    blk = w.reshape(rows // 128, 128, cols // 128, 128)
+    amax = blk.abs().amax(dim=(1, 3))                      # [rb][cb]
+    safe = torch.where(amax > 0, amax, torch.ones_like(amax))
+    inv = torch.where(amax > 0, 448.0 / safe, torch.zeros_like(amax))
+    q = (blk * inv[:, None, :, None]).reshape(rows, cols).to(torch.float8_e4m3fn)
+    scale = torch.where(amax > 0, amax / 448.0, torch.zeros_like(amax)).to(torch.float32)
+    return q.view(torch.uint8), scale.contiguous()
+
+
+def make_moe_weights(shape: MoEShape, seed: int = 0, device="cpu", zipf_bias: bool = False,
+                     gen: torch.Generator | None = None, skip_x: bool = True) -> dict:
+    """Router + expert weights (see module docstring for the draw order)."""
+    g = gen or torch.Generator(device=device).manual_seed(seed)
+    H, E, I, S = shape.hidden, shape.num_experts, shape.intermediate, shape.num_shared
+    out = {"gamma": torch.ones(H, dtype=torch.float32, device=device)}
+    out["router_w"] = torch.randn(E, H, generator=g, device=device, dtype=torch.float32) * 0.02
+    if zipf_bias:
+        perm = torch.randperm(E, generator=g, device=device).to(torch.float32) + 1.0
+        out["router_bias"] = (-1.1 * torch.log(perm)).to(torch.float32)
+    else:
+        out["router_bias"] = None
+    G = E + S
+    w13 = torch.empty(G, 2 * I, H, dtype=torch.uint8, device=device)
+    s13 = torch.empty(G, 2 * I // 128, H // 128, dtype=torch.float32, device=device)
+    w2 = torch.empty(G, H, I, dtype=torch.uint8, device=device)
+    s2 = torch.empty(G, H // 128, I // 128, dtype=torch.float32, device=device)
+    for e in range(G):
+        gate = torch.randn(I, H, generator=g, device=device, dtype=torch.float32) * 0.02
+        up = torch.randn(I, H, generator=g, device=device, dtype=torch.float32) * 0.02
+        down = torch.randn(H, I, generator=g, device=device, dtype=torch.float32) * 0.02
+        q, s = quantize_blocks(torch.cat([gate, up], 0))
+        w13[e].copy_(q)
+        s13[e].copy_(s)
+        q, s = quantize_blocks(down)
+        w2[e].copy_(q)
+        s2[e].copy_(s)
+    out.update(w13=w13, s13=s13, w2=w2, s2=s2)
+    return out
+
+
+def make_x(shape: MoEShape, tokens: int, seed: int = 0, device="cpu",
+           gen: torch.Generator | None = None) -> torch.Tensor:
+    g = gen or torch.Generator(device=device).manual_seed(seed)
+    return torch.randn(tokens, shape.hidden, generator=g, device=device, dtype=torch.float32).to(torch.bfloat16)
+
+
+def make_case(shape: MoEShape, tokens: int, seed: int = 0, device="cpu", zipf_bias: bool = False) -> dict:
+    """x then weights from one generator (the documented draw order)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    x = make_x(shape, tokens, device=device, gen=g)
+    w = make_moe_weights(shape, device=device, zipf_bias=zipf_bias, gen=g)
+    w["x"] = x
+    return w
+
+
+def zipf_bias(E: int, seed: int = 0) -> torch.Tensor:
+    g = torch.Generator().manual_seed(seed)
+    perm = torch.randperm(E, generator=g).to(torch.float32) + 1.0
+    return (-1.1 * torch.log(perm)).to(torch.float32)
+
+
+def uniform_routing(tokens: int, E: int, k: int, seed: int = 0, device="cpu"):
+    """Router logits ~ U(0,1) [T][E]; returns the logits."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    return torch.rand(tokens, E, generator=g, device=device, dtype=torch.float32)
+
+
+def expected_distinct_ranks(E: int, k: int, ep: int) -> float:
+    """Mean number of distinct EP ranks a token's k experts land on."""
+    per = E // ep
+    return ep * (1.0 - math.comb(E - per, k) / math.comb(E, k))
