@@ -130,7 +130,7 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
 }
 
 template <bool kGated>
-__global__ void __maxnreg__(104)
+__global__ void __launch_bounds__(kNumThreads, 1)
 grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
                         const __grid_constant__ CUtensorMap tmap_a,
                         const GemmParams p) {
@@ -325,8 +325,8 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
         uint32_t phase = 0, tphase = 0;
         bool ok = true;
 
-        constexpr int kChunk = kGated ? 8 : 16;                  // columns per TMEM load
-        constexpr int kChunks = C::kColsPerWarp / kChunk;        // 4 either way
+        constexpr int kChunk = 8;                                // columns per TMEM load
+        constexpr int kChunks = C::kColsPerWarp / kChunk;        // 4 (gated) / 8 (down)
         constexpr int kAcc = C::kColsPerWarp * C::kNumCombined;  // 64 either way
 
         for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
@@ -345,48 +345,25 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
 #pragma unroll
                 for (int ch = 0; ch < kChunks; ++ch) {
                     if (ch < active_chunks) {
-                        if (kGated) {
-                            uint32_t pg[16];
-                            // gate columns [ch*8, ch*8+8) and up columns at +128, one x16-shaped
-                            // request each half: load 8+8 via two x16 requests would waste
-                            // registers, so issue x16 over gate cols and reuse the upper half
-                            // for the up partial of the same columns.
+#pragma unroll
+                        for (int half = 0; half < C::kNumCombined; ++half) {
+                            uint32_t pv[8];
                             asm volatile(
                                 "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                                : "=r"(pg[0]), "=r"(pg[1]), "=r"(pg[2]), "=r"(pg[3]), "=r"(pg[4]),
-                                  "=r"(pg[5]), "=r"(pg[6]), "=r"(pg[7])
-                                : "r"(tbuf + ch * kChunk));
-                            asm volatile(
-                                "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                                : "=r"(pg[8]), "=r"(pg[9]), "=r"(pg[10]), "=r"(pg[11]), "=r"(pg[12]),
-                                  "=r"(pg[13]), "=r"(pg[14]), "=r"(pg[15])
-                                : "r"(tbuf + 128 + ch * kChunk));
+                                : "=r"(pv[0]), "=r"(pv[1]), "=r"(pv[2]), "=r"(pv[3]), "=r"(pv[4]),
+                                  "=r"(pv[5]), "=r"(pv[6]), "=r"(pv[7])
+                                : "r"(tbuf + half * 128 + ch * kChunk));
                             tmem_wait_ld();
+                            const float* cc = cs + half * C::kNMax + ch * kChunk;
+                            float* a = acc + half * C::kColsPerWarp + ch * kChunk;
 #pragma unroll
-                            for (int j = 0; j < kChunk; j += 2) {
-                                const float2 cg = *reinterpret_cast<const float2*>(cs + ch * kChunk + j);
-                                const float2 cu = *reinterpret_cast<const float2*>(cs + C::kNMax + ch * kChunk + j);
-                                float2 ag = make_float2(acc[ch * kChunk + j], acc[ch * kChunk + j + 1]);
-                                float2 au = make_float2(acc[C::kColsPerWarp + ch * kChunk + j],
-                                                        acc[C::kColsPerWarp + ch * kChunk + j + 1]);
-                                ag = ffma2(make_float2(__uint_as_float(pg[j]), __uint_as_float(pg[j + 1])), cg, ag);
-                                au = ffma2(make_float2(__uint_as_float(pg[8 + j]), __uint_as_float(pg[8 + j + 1])), cu, au);
-                                acc[ch * kChunk + j] = ag.x;
-                                acc[ch * kChunk + j + 1] = ag.y;
-                                acc[C::kColsPerWarp + ch * kChunk + j] = au.x;
-                                acc[C::kColsPerWarp + ch * kChunk + j + 1] = au.y;
-                            }
-                        } else {
-                            uint32_t pv[16];
-                            tmem_ld16(tbuf + ch * kChunk, pv);
-                            tmem_wait_ld();
-#pragma unroll
-                            for (int j = 0; j < kChunk; j += 2) {
-                                const float2 c2 = *reinterpret_cast<const float2*>(cs + ch * kChunk + j);
-                                float2 a2 = make_float2(acc[ch * kChunk + j], acc[ch * kChunk + j + 1]);
-                                a2 = ffma2(make_float2(__uint_as_float(pv[j]), __uint_as_float(pv[j + 1])), c2, a2);
-                                acc[ch * kChunk + j] = a2.x;
-                                acc[ch * kChunk + j + 1] = a2.y;
+                            for (int j = 0; j < kChunk; j += 4) {
+                                const float4 c4 = *reinterpret_cast<const float4*>(cc + j);
+                                float2 lo = ffma2(make_float2(__uint_as_float(pv[j]), __uint_as_float(pv[j + 1])),
+                                                  make_float2(c4.x, c4.y), make_float2(a[j], a[j + 1]));
+                                float2 hi = ffma2(make_float2(__uint_as_float(pv[j + 2]), __uint_as_float(pv[j + 3])),
+                                                  make_float2(c4.z, c4.w), make_float2(a[j + 2], a[j + 3]));
+                                a[j] = lo.x; a[j + 1] = lo.y; a[j + 2] = hi.x; a[j + 3] = hi.y;
                             }
                         }
                     }
@@ -507,9 +484,13 @@ cbwStatus_t launch_gemm(const cbwGroupedGemmArgs* a, int* error_word, cudaStream
     cudaGetDevice(&dev);
     if (sm_count == 0) cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev);
     if (!attr_set[kGated ? 1 : 0]) {
-        if (cudaFuncSetAttribute(grouped_fp8_gemm_kernel<kGated>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 C::kSmemBytes) != cudaSuccess)
+        cudaError_t e = cudaFuncSetAttribute(grouped_fp8_gemm_kernel<kGated>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+        if (e != cudaSuccess) {
+            std::fprintf(stderr, "cbwFp8BlockScaledGroupedGemm: shared memory opt-in (%d B) failed: %s\n",
+                         C::kSmemBytes, cudaGetErrorString(e));
             return CBW_ERROR_EXECUTION_FAILED;
+        }
         attr_set[kGated ? 1 : 0] = true;
     }
     GemmParams p;
@@ -527,7 +508,16 @@ cbwStatus_t launch_gemm(const cbwGroupedGemmArgs* a, int* error_word, cudaStream
     p.w_rows = w_rows;
     p.error_word = error_word;
     grouped_fp8_gemm_kernel<kGated><<<sm_count, kNumThreads, C::kSmemBytes, stream>>>(tw, ta, p);
-    return cudaGetLastError() == cudaSuccess ? CBW_SUCCESS : CBW_ERROR_EXECUTION_FAILED;
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        cudaFuncAttributes fa;
+        cudaFuncGetAttributes(&fa, grouped_fp8_gemm_kernel<kGated>);
+        std::fprintf(stderr,
+                     "cbwFp8BlockScaledGroupedGemm: launch failed: %s (regs %d, max threads %d, smem %d B)\n",
+                     cudaGetErrorString(e), fa.numRegs, fa.maxThreadsPerBlock, C::kSmemBytes);
+        return CBW_ERROR_EXECUTION_FAILED;
+    }
+    return CBW_SUCCESS;
 }
 
 }  // namespace
