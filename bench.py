@@ -1,0 +1,358 @@
+#!/usr/bin/env python
+"""MoE-layer tokens/s on B200 (BASELINE.json metric) for the GLM-4.x-shape MoE
+FFN block: hidden 5120, 160 routed experts top-8 + 1 shared expert,
+intermediate 1536, 4096 tokens, zipf-skewed router.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one forward of the MoE FFN block (RMSNorm -> router/top-k ->
+permute -> gate/up GEMM + SwiGLU -> down GEMM -> combine + residual) over the
+4096 tokens, inputs resident in HBM.  With N > 1 the 4096 tokens are split
+over N expert-parallel ranks (strong scaling) when the EP path is built, and
+rank 0 prints one JSON line with the max-over-ranks time.
+
+`e2e` is the same metric through the public layer call with host buffers:
+pinned host x -> device, forward, device -> pinned host output, every step.
+`cpu_baseline` / `--impl reference` time the CPU restatement of the
+reference's path (the oracle, fp32 activations -- the reference has no CPU
+MoE path of its own that builds here) on the host cores on a bounded sample.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "MoE-layer tokens/sec at 1/2/4/8 B200 (EP); % of FP8/HBM/NVLink roofline"
+UNIT = "tokens/s"
+TOKENS = 4096
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--tokens", type=int, default=TOKENS)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU-baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+# ---------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi sampling during the timed region (SM clock, max, reasons)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.path or not os.path.exists(self.path):
+            return None
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[3]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "power_w_max": max(r[2] for r in rows), "samples": len(rows), "reasons": reasons}
+
+
+# ---------------------------------------------------------------- CPU baseline
+
+def cpu_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_baseline(shape, weights_cpu, x_cpu, budget_s: float, fixed_tokens: int | None = None):
+    """The oracle (fp32-activation "ref" mode, OpenMP over tokens, all host
+    threads) on a bounded sample of the workload's tokens; tokens/s."""
+    import numpy as np
+    from oracle import oracle as orc   # CPU-baseline leg: the checker timed as the reference's CPU path
+    ow = orc.OracleWeights(shape, weights_cpu)
+    xb = x_cpu.contiguous().view(__import__("torch").int16).numpy().view(np.uint16)
+    th = cpu_threads()
+    if fixed_tokens is None:
+        n = min(th, xb.shape[0])
+        t0 = time.perf_counter()
+        orc.moe_ffn_forward(ow, xb[:n], mode=1, threads=th)
+        dt = time.perf_counter() - t0
+        n = int(max(n, min(xb.shape[0], n * budget_s / max(dt, 1e-3))))
+        n = max(th, (n // th) * th)
+        n = min(n, xb.shape[0])
+    else:
+        n = fixed_tokens
+    t0 = time.perf_counter()
+    orc.moe_ffn_forward(ow, xb[:n], mode=1, threads=th)
+    dt = time.perf_counter() - t0
+    return {"value": n / dt, "unit": UNIT, "cores": th, "kind": "port",
+            "sample": f"{n} of {xb.shape[0]} tokens, full layer incl. all routed + shared experts, "
+                      f"oracle ref mode (fp32 activations), {dt:.1f} s"}, n, dt
+
+
+# ---------------------------------------------------------------- algorithmic work
+
+def algorithmic(shape, counts, T):
+    """Bytes / FLOPs the layer must move or do, from the actual routing."""
+    H, I, E, S, k = shape.hidden, shape.intermediate, shape.num_experts, shape.num_shared, shape.top_k
+    counts = [int(c) for c in counts]
+    touched = [c > 0 for c in counts]
+    rows = sum(counts)
+    w13 = 2 * I * H + (2 * I // 128) * (H // 128) * 4
+    w2 = H * I + (H // 128) * (I // 128) * 4
+    g1_bytes = sum(w13 for t in touched if t) + rows * (H + H // 128 * 4) + rows * (I + I // 128 * 4)
+    g2_bytes = sum(w2 for t in touched if t) + rows * (I + I // 128 * 4) + rows * H * 2
+    g1_flops = 2.0 * rows * H * 2 * I
+    g2_flops = 2.0 * rows * I * H
+    layer_bytes = sum(w13 + w2 for t in touched if t) + T * H * 2 * 2 + E * H * 4
+    layer_flops = g1_flops + g2_flops + 2.0 * T * H * E
+    return {"gemm_gate_up": (g1_bytes, g1_flops), "gemm_down": (g2_bytes, g2_flops),
+            "layer": (layer_bytes, layer_flops), "rows": rows}
+
+
+def load_traffic(kernel: str):
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    try:
+        return json.loads(p.read_text()).get(kernel)
+    except Exception:
+        return None
+
+
+# ---------------------------------------------------------------- arms
+
+def run_reference(args):
+    """--impl reference: the reference's CPU path (the oracle restatement; the
+    reference's Futhark/Terra CPU builds are not available), bounded samples."""
+    import torch
+    from time_b200 import synth
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    shape = synth.GLM
+    torch.manual_seed(0)
+    w = synth.make_moe_weights(shape, seed=0, device="cpu", zipf_bias=True)
+    x = synth.make_x(shape, args.tokens, seed=1, device="cpu")
+    th = cpu_threads()
+    # size one step to ~budget/steps seconds so the whole run stays within minutes
+    per_step = max(2.0, min(20.0, 120.0 / max(1, args.steps + args.warmup)))
+    _, n, _ = cpu_baseline(shape, w, x, per_step)
+    times = []
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        from oracle import oracle as orc
+        ow = orc.OracleWeights(shape, w) if i == 0 else ow
+        import numpy as np
+        xb = x[:n].contiguous().view(torch.int16).numpy().view(np.uint16)
+        t1 = time.perf_counter()
+        orc.moe_ffn_forward(ow, xb, mode=1, threads=th)
+        dt = time.perf_counter() - t1
+        if i >= args.warmup:
+            times.append(dt)
+    ms = 1000.0 * sum(times) / len(times)
+    value = n / (ms / 1000.0)
+    line = {"metric": METRIC, "impl": "reference", "value": value, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "glm4x_moe_ffn_prefill", "tokens": args.tokens, "hidden": shape.hidden,
+                       "experts": shape.num_experts, "top_k": shape.top_k, "intermediate": shape.intermediate,
+                       "shared_experts": shape.num_shared, "router": "softmax top-k, zipf(1.1) bias",
+                       "sample_tokens_per_step": n},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": th, "kind": "port",
+                             "sample": f"{n} tokens per step of the {args.tokens}-token workload, oracle ref mode"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from time_b200 import synth
+    from time_b200 import moe as M
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "error": "expert-parallel path not built in this revision",
+                              "n_gpus": world}), flush=True)
+        dist.barrier()
+        dist.destroy_process_group()
+        return 0
+
+    shape = synth.GLM
+    T = args.tokens
+    w = synth.make_moe_weights(shape, seed=0, device=dev, zipf_bias=True)
+    x = synth.make_x(shape, T, seed=1, device=dev)
+    out = torch.empty_like(x)
+    layer = M.MoELayer(shape, w, max_tokens=T)
+    stream = torch.cuda.current_stream()
+
+    for _ in range(max(3, args.warmup)):
+        layer.forward(x, out)
+    torch.cuda.synchronize()
+    layer.check_error()
+    _, _, counts = layer.last_routing(T)
+
+    # ---- device-resident timed region with per-stage events
+    K = args.steps
+    stage_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(M.NUM_STAGES + 1)] for _ in range(K)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        start.record(stream)
+        for i in range(K):
+            layer.set_stage_events(stage_ev[i])
+            layer.forward(x, out)
+        end.record(stream)
+        torch.cuda.synchronize()
+    layer.set_stage_events(None)
+    layer.check_error()
+    total_ms = start.elapsed_time(end)
+    ms_per_step = total_ms / K
+    stages = {}
+    for s, name in enumerate(M.STAGE_NAMES):
+        stages[name] = statistics.mean(stage_ev[i][s].elapsed_time(stage_ev[i][s + 1]) for i in range(K))
+    clocks = clk.summary()
+
+    # ---- end to end through the public call with host buffers
+    x_host = x.cpu().pin_memory()
+    out_host = torch.empty(x_host.shape, dtype=x_host.dtype).pin_memory()
+    x_dev = torch.empty_like(x)
+    for _ in range(2):
+        x_dev.copy_(x_host, non_blocking=True)
+        layer.forward(x_dev, out)
+        out_host.copy_(out, non_blocking=True)
+    torch.cuda.synchronize()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for _ in range(K):
+        x_dev.copy_(x_host, non_blocking=True)
+        layer.forward(x_dev, out)
+        out_host.copy_(out, non_blocking=True)
+    e_end.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e_start.elapsed_time(e_end) / K
+    h2d = x.numel() * x.element_size()
+    d2h = out.numel() * out.element_size()
+
+    # ---- roofline of the dominant kernel
+    peaks = load_peaks()
+    work = algorithmic(shape, counts.tolist(), T)
+    dom = max(("gemm_gate_up", "gemm_down"), key=lambda n: stages[n])
+    dom_bytes, dom_flops = work[dom]
+    dom_s = stages[dom] / 1000.0
+    achieved_gbs = dom_bytes / dom_s / 1e9
+    roofline = {"kernel": dom, "bound": "hbm", "achieved": achieved_gbs, "peak": peaks["hbm_gbs"],
+                "unit": "GB/s", "frac": achieved_gbs / peaks["hbm_gbs"], "traffic": load_traffic(dom),
+                "peak_source": peaks["source"], "algorithmic_bytes": dom_bytes,
+                "tensor_tflops": dom_flops / dom_s / 1e12}
+    lb, lf = work["layer"]
+    layer_s = ms_per_step / 1000.0
+    fp8_peak = 2 * peaks["bf16_tflops"]
+    t_roof = max(lb / (peaks["hbm_gbs"] * 1e9), lf / (fp8_peak * 1e12))
+    layer_roofline = {"bound": "hbm" if lb / (peaks["hbm_gbs"] * 1e9) >= lf / (fp8_peak * 1e12) else "tensor",
+                      "t_roof_us": t_roof * 1e6, "t_us": layer_s * 1e6, "frac": t_roof / layer_s,
+                      "bytes": lb, "flops": lf, "fp8_peak_tflops_assumed": fp8_peak,
+                      "note": "fp8 peak = 2x measured bf16 (no fp8 measurement in MEASURED_PEAKS.json)"}
+
+    cpu = None
+    if not args.no_cpu_baseline and world == 1:
+        wc = {k_: (v.cpu() if isinstance(v, torch.Tensor) else v) for k_, v in w.items()}
+        cpu, _, _ = cpu_baseline(shape, wc, x.cpu(), args.cpu_seconds)
+
+    line = {"metric": METRIC, "value": T * 1000.0 / ms_per_step, "unit": UNIT, "n_gpus": world,
+            "steps": K, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "e4m3 x e4m3 -> f32 (bf16 in/out)",
+            "data": "synthetic",
+            "config": {"workload": "glm4x_moe_ffn_prefill (BASELINE configs[1])", "tokens": T,
+                       "hidden": shape.hidden, "experts": shape.num_experts, "top_k": shape.top_k,
+                       "intermediate": shape.intermediate, "shared_experts": shape.num_shared,
+                       "router": "fp32 softmax top-k, zipf(1.1) bias", "parallelism": f"ep{world}",
+                       "l2": "inputs larger than L2: 3.8 GB of expert weights streamed per step"},
+            "e2e": {"value": T * 1000.0 / e2e_ms, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+            "roofline": roofline, "layer_roofline": layer_roofline,
+            "stages_ms": stages, "rows": work["rows"],
+            "expert_tokens": {"max": int(counts[:shape.num_experts].max()),
+                              "min": int(counts[:shape.num_experts].min()),
+                              "mean": float(counts[:shape.num_experts].float().mean())},
+            "gpu_launches": K * M.NUM_STAGES, "clocks": clocks, "cpu_baseline": cpu}
+    print(json.dumps(line), flush=True)
+    layer.close()
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -112,6 +112,15 @@ moe_status_t moe_layer_last_routing(const moe_layer_t* layer, const void* worksp
                                     const int32_t** topk_idx, const float** topk_w,
                                     const int32_t** group_counts);
 
+/* Stage timing: when `events` is non-NULL, every later forward records
+ * events[i] on its stream right before stage i and events[MOE_NUM_STAGES]
+ * after the last one (stages: 0 RMSNorm+quant, 1 router+top-k, 2 permute,
+ * 3 gather, 4 gate/up GEMM, 5 down GEMM, 6 combine; a routed forward records
+ * an empty router stage).  Pass NULL to stop.  The events stay owned by the
+ * caller. */
+#define MOE_NUM_STAGES 7
+moe_status_t moe_layer_set_stage_events(moe_layer_t* layer, cwEvent_t* events);
+
 /* Reads and clears the device error word (synchronises `stream`). */
 moe_status_t moe_layer_check_error(moe_layer_t* layer, cwStream_t stream);
 

@@ -38,6 +38,8 @@ struct moe_layer {
     ncwComm_t comm;
     int e_begin, e_end, groups;
     int* error_word;      // device
+    cudaEvent_t stage_ev[MOE_NUM_STAGES + 1];
+    bool timing;
     // workspace layout (byte offsets)
     size_t off_rms, off_xq, off_xs, off_idx, off_w, off_counts, off_start, off_total, off_pos, off_rowtok,
         off_xp, off_xps, off_hq, off_hs, off_y, bytes;
@@ -78,6 +80,10 @@ void plan_workspace(moe_layer* L) {
 template <typename T>
 T* at(void* ws, size_t off) { return reinterpret_cast<T*>(static_cast<char*>(ws) + off); }
 
+inline void mark(moe_layer* L, int stage, cudaStream_t st) {
+    if (L->timing) cudaEventRecord(L->stage_ev[stage], st);
+}
+
 moe_status_t cbw_to_moe(cbwStatus_t s) {
     return s == CBW_SUCCESS ? MOE_OK : (s == CBW_ERROR_INVALID_VALUE ? MOE_ERR_INVALID_ARGUMENT : MOE_ERR_CUDA);
 }
@@ -97,8 +103,10 @@ moe_status_t run_experts(moe_layer* L, const void* x, const int32_t* idx, const 
     int32_t* total = at<int32_t>(ws, L->off_total);
     int32_t* pos = at<int32_t>(ws, L->off_pos);
     int32_t* rowtok = at<int32_t>(ws, L->off_rowtok);
+    mark(L, 2, st);
     MOE_TRY(moe_permute(idx, T, K, L->e_begin, L->e_end, S, counts, start, pos, rowtok, total, L->rcap,
                         L->error_word, st));
+    mark(L, 3, st);
     MOE_TRY(moe_gather_rows_n(at<void>(ws, L->off_xq), at<float>(ws, L->off_xs), L->xs_ld, rowtok, total, L->rcap, H,
                               at<void>(ws, L->off_xp), at<float>(ws, L->off_xps), L->rcap, st));
     cbwGroupedGemmArgs g1;
@@ -118,6 +126,7 @@ moe_status_t run_experts(moe_layer* L, const void* x, const int32_t* idx, const 
     g1.out = at<void>(ws, L->off_hq);
     g1.out_scale = at<float>(ws, L->off_hs);
     g1.out_ld = L->rcap;
+    mark(L, 4, st);
     MOE_TRY(cbw_to_moe(cbwFp8BlockScaledGroupedGemm(&g1, L->error_word, st)));
     cbwGroupedGemmArgs g2 = g1;
     g2.mode = CBW_GEMM_DOWN_BF16;
@@ -130,9 +139,13 @@ moe_status_t run_experts(moe_layer* L, const void* x, const int32_t* idx, const 
     g2.out = at<void>(ws, L->off_y);
     g2.out_scale = nullptr;
     g2.out_ld = 0;
+    mark(L, 5, st);
     MOE_TRY(cbw_to_moe(cbwFp8BlockScaledGroupedGemm(&g2, L->error_word, st)));
     const int32_t* shared_rows = start + (L->e_end - L->e_begin);
-    return moe_combine(x, at<void>(ws, L->off_y), pos, wts, shared_rows, S, T, K, H, out, st);
+    mark(L, 6, st);
+    MOE_TRY(moe_combine(x, at<void>(ws, L->off_y), pos, wts, shared_rows, S, T, K, H, out, st));
+    mark(L, MOE_NUM_STAGES, st);
+    return MOE_OK;
 }
 
 }  // namespace
@@ -199,8 +212,10 @@ moe_status_t moe_layer_forward_routed(moe_layer_t* L, const void* x, const int32
     if (T == 0) return MOE_OK;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const moe_layer_config_t& c = L->cfg;
+    mark(L, 0, st);
     MOE_TRY(moe_rmsnorm_quant(x, L->w.norm_gamma, T, c.hidden, c.rms_eps, at<float>(ws, L->off_rms),
                               at<void>(ws, L->off_xq), at<float>(ws, L->off_xs), L->xs_ld, stream));
+    mark(L, 1, st);
     return run_experts(L, x, idx, wts, out, T, ws, st);
 }
 
@@ -213,10 +228,12 @@ moe_status_t moe_layer_forward(moe_layer_t* L, const void* x, void* out, int T, 
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const moe_layer_config_t& c = L->cfg;
     float* rms = at<float>(ws, L->off_rms);
+    mark(L, 0, st);
     MOE_TRY(moe_rmsnorm_quant(x, L->w.norm_gamma, T, c.hidden, c.rms_eps, rms, at<void>(ws, L->off_xq),
                               at<float>(ws, L->off_xs), L->xs_ld, stream));
     int32_t* idx = at<int32_t>(ws, L->off_idx);
     float* wts = at<float>(ws, L->off_w);
+    mark(L, 1, st);
     MOE_TRY(moe_router_topk(x, rms, L->w.norm_gamma, L->w.router_w, L->w.router_bias, T, c.hidden, c.num_experts,
                             c.top_k, nullptr, idx, wts, stream));
     return run_experts(L, x, idx, wts, out, T, ws, st);
@@ -229,6 +246,14 @@ moe_status_t moe_layer_last_routing(const moe_layer_t* L, const void* ws, const 
     if (idx) *idx = at<int32_t>(w, L->off_idx);
     if (wts) *wts = at<float>(w, L->off_w);
     if (counts) *counts = at<int32_t>(w, L->off_counts);
+    return MOE_OK;
+}
+
+moe_status_t moe_layer_set_stage_events(moe_layer_t* L, cwEvent_t* events) {
+    if (!L) return MOE_ERR_INVALID_ARGUMENT;
+    L->timing = events != nullptr;
+    for (int i = 0; i <= MOE_NUM_STAGES; ++i)
+        L->stage_ev[i] = events ? static_cast<cudaEvent_t>(events[i]) : nullptr;
     return MOE_OK;
 }
 

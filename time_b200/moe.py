@@ -45,6 +45,9 @@ class GroupedGemmArgs(ctypes.Structure):
                 ("out_ld", c_int)]
 
 
+NUM_STAGES = 7
+STAGE_NAMES = ("rmsnorm_quant", "router_topk", "permute", "gather", "gemm_gate_up", "gemm_down", "combine")
+
 GEMM_GATED_SWIGLU = 0
 GEMM_DOWN_BF16 = 1
 
@@ -67,6 +70,7 @@ def libs():
         k.moe_layer_last_routing.argtypes = [c_void_p, c_void_p, ctypes.POINTER(c_void_p), ctypes.POINTER(c_void_p),
                                              ctypes.POINTER(c_void_p)]
         k.moe_layer_check_error.argtypes = [c_void_p, c_void_p]
+        k.moe_layer_set_stage_events.argtypes = [c_void_p, c_void_p]
         k.moe_rmsnorm_quant.argtypes = [c_void_p, c_void_p, c_int, c_int, c_float, c_void_p, c_void_p, c_void_p,
                                         c_int, c_void_p]
         k.moe_router_topk.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
@@ -150,6 +154,20 @@ class MoELayer:
                                                   self.workspace_bytes, stream_ptr(stream))
             check("moe_layer_forward_routed", rc)
         return out
+
+    def set_stage_events(self, events):
+        """events: list of MOE_NUM_STAGES + 1 torch.cuda.Event (created with
+        enable_timing) or None to stop recording."""
+        if events is None:
+            self._ev_arr = None
+            check("moe_layer_set_stage_events", self._k.moe_layer_set_stage_events(self._h, None))
+            return
+        assert len(events) == NUM_STAGES + 1
+        for e in events:
+            if not e.cuda_event:        # torch creates the CUDA event on first record
+                e.record()
+        self._ev_arr = (c_void_p * len(events))(*[e.cuda_event for e in events])
+        check("moe_layer_set_stage_events", self._k.moe_layer_set_stage_events(self._h, self._ev_arr))
 
     def check_error(self, stream=None):
         check("moe_layer_check_error", self._k.moe_layer_check_error(self._h, stream_ptr(stream)))
