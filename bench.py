@@ -44,6 +44,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--tokens", type=int, default=TOKENS)
+    ap.add_argument("--experts", type=int, default=160,
+                    help="routed experts (profiling captures of a smaller case only; the metric uses 160)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -245,6 +247,9 @@ def run_ours(args):
         return 0
 
     shape = synth.GLM
+    if args.experts != shape.num_experts:
+        import dataclasses
+        shape = dataclasses.replace(shape, num_experts=args.experts)
     T = args.tokens
     w = synth.make_moe_weights(shape, seed=0, device=dev, zipf_bias=True)
     x = synth.make_x(shape, T, seed=1, device=dev)
