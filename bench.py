@@ -8,8 +8,9 @@ intermediate 1536, 4096 tokens, zipf-skewed router.
 One step = one forward of the MoE FFN block (RMSNorm -> router/top-k ->
 permute -> gate/up GEMM + SwiGLU -> down GEMM -> combine + residual) over the
 4096 tokens, inputs resident in HBM.  With N > 1 the 4096 tokens are split
-over N expert-parallel ranks (strong scaling) when the EP path is built, and
-rank 0 prints one JSON line with the max-over-ranks time.
+over N expert-parallel ranks (strong scaling: rank r owns 160/N experts and
+4096/N tokens, NCCL all-to-all dispatch/combine), and rank 0 prints one JSON
+line with the max-over-ranks time.
 
 `e2e` is the same metric through the public layer call with host buffers:
 pinned host x -> device, forward, device -> pinned host output, every step.
@@ -225,6 +226,9 @@ def run_reference(args):
     return 0
 
 
+NVLINK_GBS = 770.0   # measured peer copy per direction on this pool's B200s (no NVLink figure in MEASURED_PEAKS.json)
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -236,37 +240,54 @@ def run_ours(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    comm = None
     if world > 1:
         import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-        if rank == 0:
-            print(json.dumps({"metric": METRIC, "error": "expert-parallel path not built in this revision",
-                              "n_gpus": world}), flush=True)
-        dist.barrier()
-        dist.destroy_process_group()
-        return 0
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        comm = M.nccl_comm(rank, world)
 
     shape = synth.GLM
     if args.experts != shape.num_experts:
         import dataclasses
         shape = dataclasses.replace(shape, num_experts=args.experts)
+    if shape.num_experts % world:
+        raise SystemExit(f"{shape.num_experts} experts do not split over {world} ranks")
     T = args.tokens
-    w = synth.make_moe_weights(shape, seed=0, device=dev, zipf_bias=True)
-    x = synth.make_x(shape, T, seed=1, device=dev)
+    w_all = synth.make_moe_weights(shape, seed=0, device=dev, zipf_bias=True)
+    w = synth.expert_slice(w_all, shape, world, rank) if world > 1 else w_all
+    del w_all
+    x_all = synth.make_x(shape, T, seed=1, device=dev)
+    t0, t1 = synth.token_slice(T, world, rank)
+    x = x_all[t0:t1].contiguous()
+    del x_all
+    Tr = t1 - t0
+    max_tokens = -(-T // world)
     out = torch.empty_like(x)
-    layer = M.MoELayer(shape, w, max_tokens=T)
+    layer = M.MoELayer(shape, w, max_tokens=max_tokens, ep_size=world, ep_rank=rank, comm=comm)
     stream = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
 
     for _ in range(max(3, args.warmup)):
         layer.forward(x, out)
     torch.cuda.synchronize()
     layer.check_error()
-    _, _, counts = layer.last_routing(T)
+    idx, _, counts = layer.last_routing(Tr)
 
     # ---- device-resident timed region with per-stage events
     K = args.steps
     stage_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(M.NUM_STAGES + 1)] for _ in range(K)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
         start.record(stream)
@@ -275,13 +296,13 @@ def run_ours(args):
             layer.forward(x, out)
         end.record(stream)
         torch.cuda.synchronize()
+    barrier()
     layer.set_stage_events(None)
     layer.check_error()
-    total_ms = start.elapsed_time(end)
-    ms_per_step = total_ms / K
+    ms_per_step = max_over_ranks(start.elapsed_time(end) / K)
     stages = {}
-    for s, name in enumerate(M.STAGE_NAMES):
-        stages[name] = statistics.mean(stage_ev[i][s].elapsed_time(stage_ev[i][s + 1]) for i in range(K))
+    for s_, name in enumerate(M.STAGE_NAMES):
+        stages[name] = statistics.mean(stage_ev[i][s_].elapsed_time(stage_ev[i][s_ + 1]) for i in range(K))
     clocks = clk.summary()
 
     # ---- end to end through the public call with host buffers
@@ -293,6 +314,7 @@ def run_ours(args):
         layer.forward(x_dev, out)
         out_host.copy_(out, non_blocking=True)
     torch.cuda.synchronize()
+    barrier()
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_start.record(stream)
     for _ in range(K):
@@ -301,13 +323,19 @@ def run_ours(args):
         out_host.copy_(out, non_blocking=True)
     e_end.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = e_start.elapsed_time(e_end) / K
+    barrier()
+    e2e_ms = max_over_ranks(e_start.elapsed_time(e_end) / K)
     h2d = x.numel() * x.element_size()
     d2h = out.numel() * out.element_size()
 
-    # ---- roofline of the dominant kernel
+    # ---- roofline of the dominant kernel (this rank) and of the layer
     peaks = load_peaks()
-    work = algorithmic(shape, counts.tolist(), T)
+    G_local = shape.num_experts // world
+    local_shape = shape
+    if world > 1:
+        import dataclasses
+        local_shape = dataclasses.replace(shape, num_experts=G_local)
+    work = algorithmic(local_shape, counts.tolist(), Tr)
     dom = max(("gemm_gate_up", "gemm_down"), key=lambda n: stages[n])
     dom_bytes, dom_flops = work[dom]
     dom_s = stages[dom] / 1000.0
@@ -317,38 +345,63 @@ def run_ours(args):
                 "peak_source": peaks["source"], "algorithmic_bytes": dom_bytes,
                 "tensor_tflops": dom_flops / dom_s / 1e12}
     lb, lf = work["layer"]
-    layer_s = ms_per_step / 1000.0
+    if world > 1:
+        lb += (shape.num_experts - G_local) * shape.hidden * 4      # router weights are replicated
+        lf += 2.0 * Tr * shape.hidden * (shape.num_experts - G_local)
+    e_lo, e_hi = rank * G_local, (rank + 1) * G_local
+    idx_h = idx.flatten().tolist()
+    own_local = sum(1 for e in idx_h if e_lo <= e < e_hi)
+    sent_remote = sum(1 for e in idx_h if e >= 0) - own_local
+    recv_remote = int(sum(counts[:G_local].tolist())) - own_local
+    rb = M.libs()["libkernels.so"].moe_ep_row_bytes(shape.hidden)
+    a2a_bytes = max(sent_remote * rb + recv_remote * shape.hidden * 2,
+                    recv_remote * rb + sent_remote * shape.hidden * 2) if world > 1 else 0
     fp8_peak = 2 * peaks["bf16_tflops"]
-    t_roof = max(lb / (peaks["hbm_gbs"] * 1e9), lf / (fp8_peak * 1e12))
-    layer_roofline = {"bound": "hbm" if lb / (peaks["hbm_gbs"] * 1e9) >= lf / (fp8_peak * 1e12) else "tensor",
+    t_hbm = lb / (peaks["hbm_gbs"] * 1e9)
+    t_fp8 = lf / (fp8_peak * 1e12)
+    t_nvl = a2a_bytes / (NVLINK_GBS * 1e9)
+    t_roof = max(t_hbm, t_fp8, t_nvl)
+    t_roof = max_over_ranks(t_roof)
+    layer_s = ms_per_step / 1000.0
+    layer_roofline = {"bound": ("hbm", "tensor", "nvlink")[[t_hbm, t_fp8, t_nvl].index(max(t_hbm, t_fp8, t_nvl))],
                       "t_roof_us": t_roof * 1e6, "t_us": layer_s * 1e6, "frac": t_roof / layer_s,
-                      "bytes": lb, "flops": lf, "fp8_peak_tflops_assumed": fp8_peak,
-                      "note": "fp8 peak = 2x measured bf16 (no fp8 measurement in MEASURED_PEAKS.json)"}
+                      "bytes_rank0": lb, "flops_rank0": lf, "a2a_bytes_per_direction_rank0": a2a_bytes,
+                      "fp8_peak_tflops_assumed": fp8_peak, "nvlink_gbs_assumed": NVLINK_GBS,
+                      "note": "per rank, max over ranks; fp8 peak = 2x measured bf16 (no fp8 measurement "
+                              "in MEASURED_PEAKS.json); nvlink = measured peer copy per direction"}
 
     cpu = None
     if not args.no_cpu_baseline and world == 1:
         wc = {k_: (v.cpu() if isinstance(v, torch.Tensor) else v) for k_, v in w.items()}
         cpu, _, _ = cpu_baseline(shape, wc, x.cpu(), args.cpu_seconds)
 
+    launches_per_step = M.NUM_STAGES if world == 1 else 10
     line = {"metric": METRIC, "value": T * 1000.0 / ms_per_step, "unit": UNIT, "n_gpus": world,
             "steps": K, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "e4m3 x e4m3 -> f32 (bf16 in/out)",
             "data": "synthetic",
             "config": {"workload": "glm4x_moe_ffn_prefill (BASELINE configs[1])", "tokens": T,
+                       "tokens_per_rank": max_tokens,
                        "hidden": shape.hidden, "experts": shape.num_experts, "top_k": shape.top_k,
                        "intermediate": shape.intermediate, "shared_experts": shape.num_shared,
                        "router": "fp32 softmax top-k, zipf(1.1) bias", "parallelism": f"ep{world}",
-                       "l2": "inputs larger than L2: 3.8 GB of expert weights streamed per step"},
+                       "dispatch": "fp8 rows + 1x128 scales, combine bf16 (NCCL send/recv)" if world > 1 else None,
+                       "l2": "inputs larger than L2: %.1f GB of expert weights streamed per step per rank"
+                             % (sum(v.numel() for k_, v in w.items() if k_ in ("w13", "w2")) / 1e9)},
             "e2e": {"value": T * 1000.0 / e2e_ms, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
             "roofline": roofline, "layer_roofline": layer_roofline,
-            "stages_ms": stages, "rows": work["rows"],
-            "expert_tokens": {"max": int(counts[:shape.num_experts].max()),
-                              "min": int(counts[:shape.num_experts].min()),
-                              "mean": float(counts[:shape.num_experts].float().mean())},
-            "gpu_launches": K * M.NUM_STAGES, "clocks": clocks, "cpu_baseline": cpu}
-    print(json.dumps(line), flush=True)
+            "stages_ms_rank0": stages, "rows_rank0": work["rows"],
+            "expert_tokens_rank0": {"max": int(counts[:G_local].max()), "min": int(counts[:G_local].min()),
+                                    "mean": float(counts[:G_local].float().mean())},
+            "gpu_launches": K * launches_per_step, "clocks": clocks, "cpu_baseline": cpu}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
     layer.close()
+    if world > 1:
+        barrier()
+        M.nccl_comm_destroy(comm)
+        dist.destroy_process_group()
     return 0
 
 

@@ -77,9 +77,12 @@ typedef struct {
 
 typedef struct moe_layer moe_layer_t;
 
-/* Validates the shapes, encodes the weight TMA descriptors and allocates the
- * handle's device error word.  `comm` is an ncwComm_t over the ep_size ranks
- * (NULL when ep_size == 1).  Weight pointers must stay valid. */
+/* Validates the shapes and allocates the handle's small state (device error
+ * word; with ep_size > 1 a pinned host buffer for the exchanged counts).
+ * `comm` is an ncwComm_t over the ep_size ranks, rank ep_rank being this
+ * process (NULL when ep_size == 1).  Weight pointers must stay valid.  With
+ * ep_size > 1 every rank must call the forward with the same max_tokens and
+ * may pass at most max_tokens tokens. */
 moe_status_t moe_layer_create(const moe_layer_config_t* cfg, const moe_layer_weights_t* w,
                               ncwComm_t comm, moe_layer_t** out);
 moe_status_t moe_layer_destroy(moe_layer_t* layer);
@@ -174,6 +177,70 @@ moe_status_t moe_gather_rows(const void* xq, const float* xs, int xs_ld, const i
 moe_status_t moe_combine(const void* x_bf16, const void* y_bf16, const int32_t* pos,
                          const float* topk_w, const int32_t* shared_rows, int num_shared,
                          int T, int k, int H, void* out_bf16, cwStream_t stream);
+
+/* moe_permute with segment starts aligned to `pad` rows (1..128) instead of
+ * 16; pad = 1 gives the dense expert-sorted order the EP dispatch sends. */
+moe_status_t moe_permute_padded(const int32_t* topk_idx, int T, int k, int e_begin, int e_end,
+                                int num_shared, int32_t* counts, int32_t* seg_start, int32_t* pos,
+                                int32_t* row_token, int32_t* total_rows, int row_capacity,
+                                int* error_word, int pad, cwStream_t stream);
+
+/* moe_combine with the shared expert's rows read from y_shared_bf16 (at
+ * shared_rows[g] + t) and the routed rows from y_bf16 (at pos). */
+moe_status_t moe_combine_split(const void* x_bf16, const void* y_bf16, const int32_t* pos,
+                               const float* topk_w, const void* y_shared_bf16,
+                               const int32_t* shared_rows, int num_shared, int T, int k, int H,
+                               void* out_bf16, cwStream_t stream);
+
+/* ------------------------------------------------------ expert parallelism
+ * Rank r of ep_size owns routed experts [r*E/ep, (r+1)*E/ep) (the spec's
+ * shard_experts, src/futhark/kernels.fut:640-647) and tokens of its own; the
+ * exchange is the spec's all_to_all (kernels.fut:612-617) done with
+ * ncwAllToAllv.  A dispatched row is "packed": H e4m3 bytes, H/128 fp32
+ * scales, zero padding to moe_ep_row_bytes(H) bytes. */
+
+/* Bytes of one packed row (0 if H is not a positive multiple of 128). */
+size_t moe_ep_row_bytes(int H);
+
+/* Host-side plan of both all-to-alls.  send_expert_counts[E] = this rank's
+ * pairs per global expert (E = ep_size * experts_per_rank); recv_counts
+ * [ep_size][experts_per_rank] = rows peer p sends for each local expert.
+ * Outputs per peer (arrays of ep_size): rows sent/received and their
+ * first-row offsets in the dense send/receive buffers, plus both totals
+ * (either total pointer may be NULL). */
+moe_status_t moe_ep_plan_host(int ep_size, int experts_per_rank, const int32_t* send_expert_counts,
+                              const int32_t* recv_counts, size_t* send_rows, size_t* send_offsets,
+                              size_t* recv_rows, size_t* recv_offsets, size_t* send_total,
+                              size_t* recv_total);
+
+/* packed[r] = (xq[row_token[r]], xs[:, row_token[r]]) for r < *num_rows
+ * (num_rows on the device, clamped to row_capacity). */
+moe_status_t moe_ep_pack_rows(const void* xq, const float* xs, int xs_ld, const int32_t* row_token,
+                              const int32_t* num_rows, int row_capacity, int H, void* packed,
+                              cwStream_t stream);
+
+/* From recv_counts[ep_size][experts_per_rank] (device) build the local GEMM
+ * row layout: local expert j's segment holds the rows of source 0, 1, ... in
+ * their received order, segments start at multiples of 16, and `num_shared`
+ * (0 or 1) shared-expert segment of T_local rows follows.  Outputs (device):
+ * counts[G], seg_start[G], total_rows[1], row_src[row_capacity] (received row,
+ * -1 padding, -(t+2) own token t) and recv_dst[received rows] (GEMM row of
+ * every received row).  Over capacity: zero counts and error word 2. */
+moe_status_t moe_ep_recv_plan(const int32_t* recv_counts, int ep_size, int experts_per_rank,
+                              int T_local, int num_shared, int32_t* counts, int32_t* seg_start,
+                              int32_t* total_rows, int32_t* row_src, int32_t* recv_dst,
+                              int row_capacity, int recv_capacity, int* error_word,
+                              cwStream_t stream);
+
+/* GEMM input rows: xp[r] / xps[:, r] from packed row row_src[r] (>= 0), from
+ * own token -(row_src[r]+2) of xq/xs (<= -2), or zeros (-1); r < *total_rows. */
+moe_status_t moe_ep_gather(const void* packed, const void* xq, const float* xs, int xs_ld,
+                           const int32_t* row_src, const int32_t* total_rows, int row_capacity,
+                           int H, void* xp, float* xps, int xps_ld, cwStream_t stream);
+
+/* ysend[i] = y[recv_dst[i]] for i < n (bf16 rows of H). */
+moe_status_t moe_ep_pack_y(const void* y_bf16, const int32_t* recv_dst, int n, int H,
+                           void* ysend_bf16, cwStream_t stream);
 
 #ifdef __cplusplus
 }

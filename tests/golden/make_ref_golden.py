@@ -1,0 +1,161 @@
+"""Generate tests/golden/ref_kernels.npz: outputs of the REFERENCE's own CUDA
+kernels (csrc/kernels.cu of kollarsandor/time, compiled unmodified by
+`make -C oracle ref` into oracle/_ref/libref_kernels.so) on seeded inputs.
+
+Run on a machine with a GPU and the built oracle/_ref library:
+
+    python tests/golden/make_ref_golden.py [--out tests/golden/ref_kernels.npz]
+
+The fixture pins the CPU oracle (tests/test_golden_ref.py, no GPU) and this
+package's drop-in launch_* kernels (tests/test_gpu_legacy.py) to the
+reference itself.  Inputs are stored beside the outputs, so the tests never
+need the reference or this script.  Kernels covered (reference
+csrc/kernels.h:12-31): fp8_dequantize, f32_to_fp8, rms_norm, moe_gate,
+moe_topk, swiglu, moe_combine, add_residual, argmax, rope.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parents[2]
+c_int, c_float, c_size_t, c_void_p = ctypes.c_int, ctypes.c_float, ctypes.c_size_t, ctypes.c_void_p
+
+
+def load_ref():
+    lib = ctypes.CDLL(str(ROOT / "oracle" / "_ref" / "libref_kernels.so"))
+    lib.launch_fp8_dequantize.argtypes = [c_void_p, c_void_p, c_size_t, c_void_p]
+    lib.launch_f32_to_fp8.argtypes = [c_void_p, c_void_p, c_size_t, c_void_p]
+    lib.launch_rms_norm.argtypes = [c_void_p, c_void_p, c_void_p, c_int, c_int, c_float, c_void_p]
+    lib.launch_moe_gate.argtypes = [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p]
+    lib.launch_moe_topk.argtypes = [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]
+    lib.launch_swiglu.argtypes = [c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]
+    lib.launch_moe_combine.argtypes = [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]
+    lib.launch_add_residual.argtypes = [c_void_p, c_void_p, c_size_t, c_void_p]
+    lib.launch_argmax.argtypes = [c_void_p, c_void_p, c_int, c_int, c_void_p]
+    lib.launch_rope.argtypes = [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_float, c_void_p]
+    return lib
+
+
+def dev(a: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def host(t: torch.Tensor) -> np.ndarray:
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--out", default=str(ROOT / "tests" / "golden" / "ref_kernels.npz"))
+    a = ap.parse_args()
+    lib = load_ref()
+    rng = np.random.default_rng(20261201)
+    st = None   # legacy default stream, as the reference engine passes its context stream
+    g = {}
+
+    # fp8 decode: every code
+    codes = np.arange(256, dtype=np.uint8)
+    out = torch.empty(256, dtype=torch.float32, device="cuda")
+    lib.launch_fp8_dequantize(dev(codes).data_ptr(), out.data_ptr(), 256, st)
+    g["dequant_in"], g["dequant_out"] = codes, host(out)
+
+    # fp8 encode: the reference test's values, specials, a log-uniform sweep and
+    # all rounding midpoints between adjacent e4m3 values
+    pos = np.array([0.0, 1.0, 0.5, 2.0, 0.125, 100.0, 448.0, 464.0, 500.0, 1e6, 2.0 ** -6, 2.0 ** -9, 2.0 ** -10,
+                    1e-30, 3.0, 7.5, 0.3, 240.0, 0.001953125], dtype=np.float32)
+    sweep = (np.exp(rng.uniform(np.log(1e-4), np.log(600.0), 4000)) * rng.choice([-1, 1], 4000)).astype(np.float32)
+    dec = host(out)
+    finite = np.sort(np.unique(dec[np.isfinite(dec) & (dec >= 0)]))
+    mids = ((finite[1:] + finite[:-1]) / 2).astype(np.float32)
+    enc_in = np.concatenate([pos, -pos, np.array([np.inf, -np.inf, np.nan], np.float32), sweep, mids, -mids])
+    enc_out = torch.empty(enc_in.size, dtype=torch.uint8, device="cuda")
+    lib.launch_f32_to_fp8(dev(enc_in).data_ptr(), enc_out.data_ptr(), enc_in.size, st)
+    g["encode_in"], g["encode_out"] = enc_in, host(enc_out)
+
+    # rms_norm: rows of varied scale, hidden 512 and 5120
+    for H, T in ((512, 8), (5120, 4)):
+        x = (rng.standard_normal((T, H)) * np.exp(rng.standard_normal((T, 1)))).astype(np.float32)
+        gam = (1.0 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+        o = torch.empty(T, H, dtype=torch.float32, device="cuda")
+        lib.launch_rms_norm(dev(x).data_ptr(), dev(gam).data_ptr(), o.data_ptr(), H, T, 1e-5, st)
+        g[f"rms_x_{H}"], g[f"rms_gamma_{H}"], g[f"rms_out_{H}"] = x, gam, host(o)
+
+    # moe_gate: router logits (gate dtype argument ignored by the reference)
+    for H, E, T in ((512, 64, 16), (5120, 160, 4)):
+        x = rng.standard_normal((T, H)).astype(np.float32)
+        W = (0.02 * rng.standard_normal((E, H))).astype(np.float32)
+        o = torch.empty(T, E, dtype=torch.float32, device="cuda")
+        lib.launch_moe_gate(dev(x).data_ptr(), dev(W).data_ptr(), o.data_ptr(), H, E, T, 4, st)
+        g[f"gate_x_{H}_{E}"], g[f"gate_w_{H}_{E}"], g[f"gate_out_{H}_{E}"] = x, W, host(o)
+
+    # moe_topk: ties, NaN and large logits included
+    T, E, K = 64, 160, 8
+    lg = rng.standard_normal((T, E)).astype(np.float32)
+    lg[1, :] = 0.5                                   # all tied
+    lg[2, 10:20] = 3.0                               # a block of ties at the top
+    lg[3, ::7] = np.nan                              # NaN never selected
+    lg[4, :] = np.nan
+    lg[4, [5, 77]] = [1.0, 2.0]                      # fewer finite than K
+    lg[5, 3] = 50.0                                  # large (no overflow below 88)
+    lg[6] = np.round(lg[6] * 4) / 4                  # many ties
+    ti = torch.empty(T, K, dtype=torch.int32, device="cuda")
+    tw = torch.empty(T, K, dtype=torch.float32, device="cuda")
+    lib.launch_moe_topk(dev(lg).data_ptr(), ti.data_ptr(), tw.data_ptr(), E, K, T, st)
+    g["topk_logits"], g["topk_idx"], g["topk_w"] = lg, host(ti), host(tw)
+    lg2 = rng.standard_normal((37, 8)).astype(np.float32)
+    ti2 = torch.empty(37, 2, dtype=torch.int32, device="cuda")
+    tw2 = torch.empty(37, 2, dtype=torch.float32, device="cuda")
+    lib.launch_moe_topk(dev(lg2).data_ptr(), ti2.data_ptr(), tw2.data_ptr(), 8, 2, 37, st)
+    g["topk2_logits"], g["topk2_idx"], g["topk2_w"] = lg2, host(ti2), host(tw2)
+
+    # swiglu
+    n = 4096
+    gt = (3 * rng.standard_normal(n)).astype(np.float32)
+    up = rng.standard_normal(n).astype(np.float32)
+    o = torch.empty(n, dtype=torch.float32, device="cuda")
+    lib.launch_swiglu(dev(gt).data_ptr(), dev(up).data_ptr(), o.data_ptr(), n, st)
+    g["swiglu_gate"], g["swiglu_up"], g["swiglu_out"] = gt, up, host(o)
+
+    # moe_combine: [T][k][H] expert outputs with [T][k] weights
+    T, K, H = 5, 3, 256
+    eo = rng.standard_normal((T, K, H)).astype(np.float32)
+    ew = rng.random((T, K)).astype(np.float32)
+    o = torch.empty(T, H, dtype=torch.float32, device="cuda")
+    lib.launch_moe_combine(dev(eo).data_ptr(), dev(ew).data_ptr(), o.data_ptr(), H, K, T, st)
+    g["combine_eo"], g["combine_w"], g["combine_out"] = eo, ew, host(o)
+
+    # add_residual (in place on a)
+    aa = rng.standard_normal(1000).astype(np.float32)
+    bb = rng.standard_normal(1000).astype(np.float32)
+    ta = dev(aa)
+    lib.launch_add_residual(ta.data_ptr(), dev(bb).data_ptr(), 1000, st)
+    g["resid_a"], g["resid_b"], g["resid_out"] = aa, bb, host(ta)
+
+    # argmax with ties (first index wins)
+    lg = rng.standard_normal((6, 1000)).astype(np.float32)
+    lg[2, [10, 500]] = 9.0
+    am = torch.empty(6, dtype=torch.int64, device="cuda")
+    lib.launch_argmax(dev(lg).data_ptr(), am.data_ptr(), 1000, 6, st)
+    g["argmax_in"], g["argmax_out"] = lg, host(am)
+
+    # rope: q, k both [seq][heads][d] (the reference strides k by num_heads)
+    S_, NH, D = 5, 4, 64
+    q = rng.standard_normal((S_, NH, D)).astype(np.float32)
+    k = rng.standard_normal((S_, NH, D)).astype(np.float32)
+    tq, tk = dev(q), dev(k)
+    lib.launch_rope(tq.data_ptr(), tk.data_ptr(), D, NH, S_, 7, 10000.0, st)
+    g["rope_q"], g["rope_k"], g["rope_q_out"], g["rope_k_out"] = q, k, host(tq), host(tk)
+
+    np.savez_compressed(a.out, **g)
+    print(f"wrote {a.out}: {len(g)} arrays")
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

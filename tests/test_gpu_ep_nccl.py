@@ -1,0 +1,49 @@
+"""Expert-parallel MoE FFN block over real NCCL, one process per GPU
+(tests/ep_worker.py under torch.distributed.run): the EP output must be
+bit-identical to the single-GPU layer.  Needs at least 2 GPUs; skipped on a
+1-GPU box (the single-GPU emulation in test_gpu_ep.py covers every EP kernel
+there)."""
+import os
+import socket
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def n_gpus() -> int:
+    import torch
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+def free_port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def launch(nproc: int, *args: str) -> subprocess.CompletedProcess:
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", TIME_B200_EP_TIMEOUT_MS="60000")
+    cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           f"--nproc-per-node={nproc}", "--master-addr", "127.0.0.1", "--master-port", str(free_port()),
+           str(ROOT / "tests" / "ep_worker.py"), *args]
+    return subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=str(ROOT))
+
+
+@pytest.mark.parametrize("args", [("--shape", "tiny", "--tokens", "64"), ("--shape", "tiny", "--tokens", "3"),
+                                  ("--shape", "glm", "--tokens", "4096"),
+                                  ("--shape", "glm", "--tokens", "256", "--uniform-logits")])
+def test_ep_nccl_bit_identical(gpu, args):
+    n = n_gpus()
+    if n < 2:
+        pytest.skip("needs >= 2 GPUs")
+    nproc = 8 if n >= 8 else (4 if n >= 4 else 2)
+    r = launch(nproc, *args)
+    assert r.returncode == 0 and "EP_OK" in r.stdout, (r.stdout[-3000:], r.stderr[-3000:])

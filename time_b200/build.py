@@ -7,7 +7,7 @@ Outputs (time_b200/lib/):
     libcudawrap.so    csrc/cuda_wrappers.cu                       (reference libcudawrap)
     libncclwrap.so    csrc/nccl_wrappers.cu                       (reference libncclwrap)
     libcublaswrap.so  csrc/cublas_wrappers.cu + csrc/moe_gemm.cu  (reference libcublaswrap + grouped GEMM)
-    libkernels.so     csrc/kernels.cu + csrc/moe_prep.cu + csrc/moe_layer.cu
+    libkernels.so     csrc/kernels.cu + csrc/moe_prep.cu + csrc/moe_ep.cu + csrc/moe_layer.cu
                       (reference libkernels + the MoE layer; links the two above)
 
 Every library links the shared CUDA runtime so that device pointers and streams
@@ -37,7 +37,7 @@ LIBS = {
     "libcudawrap.so": (["cuda_wrappers.cu"], ["-lcudart"], []),
     "libncclwrap.so": (["nccl_wrappers.cu"], ["-lcudart", "-lnccl"], []),
     "libcublaswrap.so": (["cublas_wrappers.cu", "moe_gemm.cu"], ["-lcudart", "-lcublas", "-lcublasLt"], []),
-    "libkernels.so": (["kernels.cu", "moe_prep.cu", "moe_layer.cu"], ["-lcudart"], ["libcublaswrap.so", "libncclwrap.so"]),
+    "libkernels.so": (["kernels.cu", "moe_prep.cu", "moe_ep.cu", "moe_layer.cu"], ["-lcudart"], ["libcublaswrap.so", "libncclwrap.so"]),
 }
 
 

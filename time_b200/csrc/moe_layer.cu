@@ -18,12 +18,26 @@
 //   y          [R_cap][H] bf16     expert outputs
 // R_cap = T*k + S*T + 16*G rounded up to 16: every assignment plus the shared
 // expert's T rows plus worst-case segment padding.
+//
+// With expert parallelism (ep_size > 1, the exchange is described in
+// moe_ep.cu) the workspace also holds, for T_r = max_tokens own tokens and
+// recv_cap = ep * T_r * min(k, E/ep) received rows (every peer's every token
+// routed here as often as it can be):
+//   ecounts/rcounts [E] + [E] i32  pairs sent per global expert / received
+//                                  per (source, local expert); one D2H copy
+//   estart [E], stotal, spos [T*k], stok [T*k]   the dense send order
+//   psend  [T*k][rb] / precv [recv_cap][rb]      packed rows (rb bytes each)
+//   row_src [R_cap], recv_dst [recv_cap]          received row <-> GEMM row
+//   ysend  [recv_cap][H] bf16 / yrecv [T*k][H] bf16  combine exchange
+// and R_cap = recv_cap + S*T + 16*G (rounded to 16).
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <new>
+#include <vector>
 
 #include "cublas_wrappers.h"
 #include "moe_layer.h"
@@ -44,6 +58,12 @@ struct moe_layer {
     size_t off_rms, off_xq, off_xs, off_idx, off_w, off_counts, off_start, off_total, off_pos, off_rowtok,
         off_xp, off_xps, off_hq, off_hs, off_y, bytes;
     int xs_ld, rcap;
+    // expert parallelism
+    size_t off_ecounts, off_estart, off_stotal, off_stok, off_psend, off_precv, off_rdst, off_ysend, off_yrecv;
+    size_t row_bytes;
+    int recv_cap;
+    int32_t* h_counts;    // pinned [2E]
+    int sync_timeout_ms;
 };
 
 namespace {
@@ -54,8 +74,13 @@ void plan_workspace(moe_layer* L) {
     const moe_layer_config_t& c = L->cfg;
     const size_t T = static_cast<size_t>(c.max_tokens);
     const size_t H = c.hidden, I = c.intermediate, K = c.top_k;
+    const bool ep = c.ep_size > 1;
+    const size_t epr = static_cast<size_t>(c.num_experts / c.ep_size);
     L->xs_ld = static_cast<int>(align_up(T, 4));
-    L->rcap = static_cast<int>(align_up(T * K + static_cast<size_t>(c.num_shared) * T + 16 * static_cast<size_t>(L->groups), 16));
+    L->recv_cap = ep ? static_cast<int>(static_cast<size_t>(c.ep_size) * T * std::min(K, epr)) : 0;
+    const size_t routed_rows = ep ? static_cast<size_t>(L->recv_cap) : T * K;
+    L->rcap = static_cast<int>(align_up(routed_rows + static_cast<size_t>(c.num_shared) * T + 16 * static_cast<size_t>(L->groups), 16));
+    L->row_bytes = moe_ep_row_bytes(c.hidden);
     const size_t R = L->rcap;
     size_t o = 0;
     auto take = [&o](size_t bytes) { size_t at = o; o = align_up(o + bytes, 256); return at; };
@@ -74,6 +99,18 @@ void plan_workspace(moe_layer* L) {
     L->off_hq = take(R * I);
     L->off_hs = take((I / 128) * R * 4);
     L->off_y = take(R * H * 2);
+    if (ep) {
+        const size_t E = c.num_experts, RC = L->recv_cap;
+        L->off_ecounts = take(2 * E * 4);
+        L->off_estart = take(E * 4);
+        L->off_stotal = take(16);
+        L->off_stok = take(T * K * 4);
+        L->off_psend = take(T * K * L->row_bytes);
+        L->off_precv = take(RC * L->row_bytes);
+        L->off_rdst = take(RC * 4);
+        L->off_ysend = take(RC * H * 2);
+        L->off_yrecv = take(T * K * H * 2);
+    }
     L->bytes = o;
 }
 
@@ -94,10 +131,45 @@ moe_status_t cbw_to_moe(cbwStatus_t s) {
         if (_s != MOE_OK) return _s;       \
     } while (0)
 
+moe_status_t nccl_to_moe(ncwResult_t r) { return r == NCW_SUCCESS ? MOE_OK : MOE_ERR_NCCL; }
+
+cbwGroupedGemmArgs gemm_args(const moe_layer* L, void* ws, bool down) {
+    const moe_layer_config_t& c = L->cfg;
+    cbwGroupedGemmArgs g;
+    std::memset(&g, 0, sizeof(g));
+    g.num_groups = L->groups;
+    g.rows = L->rcap;
+    g.a_ld = L->rcap;
+    g.count = at<int32_t>(ws, L->off_counts);
+    g.start = at<int32_t>(ws, L->off_start);
+    if (!down) {
+        g.mode = CBW_GEMM_GATED_SWIGLU;
+        g.K = c.hidden;
+        g.N = c.intermediate;
+        g.a = at<void>(ws, L->off_xp);
+        g.a_scale = at<float>(ws, L->off_xps);
+        g.w = L->w.w13;
+        g.w_scale = L->w.s13;
+        g.out = at<void>(ws, L->off_hq);
+        g.out_scale = at<float>(ws, L->off_hs);
+        g.out_ld = L->rcap;
+    } else {
+        g.mode = CBW_GEMM_DOWN_BF16;
+        g.K = c.intermediate;
+        g.N = c.hidden;
+        g.a = at<void>(ws, L->off_hq);
+        g.a_scale = at<float>(ws, L->off_hs);
+        g.w = L->w.w2;
+        g.w_scale = L->w.s2;
+        g.out = at<void>(ws, L->off_y);
+    }
+    return g;
+}
+
 moe_status_t run_experts(moe_layer* L, const void* x, const int32_t* idx, const float* wts, void* out, int T,
                          void* ws, cudaStream_t st) {
     const moe_layer_config_t& c = L->cfg;
-    const int H = c.hidden, I = c.intermediate, K = c.top_k, S = c.num_shared;
+    const int H = c.hidden, K = c.top_k, S = c.num_shared;
     int32_t* counts = at<int32_t>(ws, L->off_counts);
     int32_t* start = at<int32_t>(ws, L->off_start);
     int32_t* total = at<int32_t>(ws, L->off_total);
@@ -109,36 +181,9 @@ moe_status_t run_experts(moe_layer* L, const void* x, const int32_t* idx, const 
     mark(L, 3, st);
     MOE_TRY(moe_gather_rows_n(at<void>(ws, L->off_xq), at<float>(ws, L->off_xs), L->xs_ld, rowtok, total, L->rcap, H,
                               at<void>(ws, L->off_xp), at<float>(ws, L->off_xps), L->rcap, st));
-    cbwGroupedGemmArgs g1;
-    std::memset(&g1, 0, sizeof(g1));
-    g1.mode = CBW_GEMM_GATED_SWIGLU;
-    g1.num_groups = L->groups;
-    g1.K = H;
-    g1.N = I;
-    g1.rows = L->rcap;
-    g1.a = at<void>(ws, L->off_xp);
-    g1.a_scale = at<float>(ws, L->off_xps);
-    g1.a_ld = L->rcap;
-    g1.w = L->w.w13;
-    g1.w_scale = L->w.s13;
-    g1.count = counts;
-    g1.start = start;
-    g1.out = at<void>(ws, L->off_hq);
-    g1.out_scale = at<float>(ws, L->off_hs);
-    g1.out_ld = L->rcap;
+    cbwGroupedGemmArgs g1 = gemm_args(L, ws, false), g2 = gemm_args(L, ws, true);
     mark(L, 4, st);
     MOE_TRY(cbw_to_moe(cbwFp8BlockScaledGroupedGemm(&g1, L->error_word, st)));
-    cbwGroupedGemmArgs g2 = g1;
-    g2.mode = CBW_GEMM_DOWN_BF16;
-    g2.K = I;
-    g2.N = H;
-    g2.a = at<void>(ws, L->off_hq);
-    g2.a_scale = at<float>(ws, L->off_hs);
-    g2.w = L->w.w2;
-    g2.w_scale = L->w.s2;
-    g2.out = at<void>(ws, L->off_y);
-    g2.out_scale = nullptr;
-    g2.out_ld = 0;
     mark(L, 5, st);
     MOE_TRY(cbw_to_moe(cbwFp8BlockScaledGroupedGemm(&g2, L->error_word, st)));
     const int32_t* shared_rows = start + (L->e_end - L->e_begin);
@@ -146,6 +191,83 @@ moe_status_t run_experts(moe_layer* L, const void* x, const int32_t* idx, const 
     MOE_TRY(moe_combine(x, at<void>(ws, L->off_y), pos, wts, shared_rows, S, T, K, H, out, st));
     mark(L, MOE_NUM_STAGES, st);
     return MOE_OK;
+}
+
+// Expert-parallel expert stage (moe_ep.cu has the exchange protocol).  Every
+// rank takes the same collective steps in the same order; a rank with no
+// tokens still exchanges (empty) counts and rows.
+moe_status_t run_experts_ep(moe_layer* L, const int32_t* idx, const float* wts, const void* x, void* out, int T,
+                            void* ws, cudaStream_t st) {
+    const moe_layer_config_t& c = L->cfg;
+    const int H = c.hidden, K = c.top_k, S = c.num_shared, E = c.num_experts, ep = c.ep_size;
+    const int epr = E / ep;
+    int32_t* ecounts = at<int32_t>(ws, L->off_ecounts);
+    int32_t* rcounts = ecounts + E;
+    int32_t* spos = at<int32_t>(ws, L->off_pos);
+    int32_t* stok = at<int32_t>(ws, L->off_stok);
+    int32_t* stotal = at<int32_t>(ws, L->off_stotal);
+    int32_t* counts = at<int32_t>(ws, L->off_counts);
+    int32_t* start = at<int32_t>(ws, L->off_start);
+    int32_t* total = at<int32_t>(ws, L->off_total);
+    int32_t* row_src = at<int32_t>(ws, L->off_rowtok);
+    int32_t* recv_dst = at<int32_t>(ws, L->off_rdst);
+    const size_t rb = L->row_bytes;
+
+    mark(L, 2, st);
+    MOE_TRY(moe_permute_padded(idx, T, K, 0, E, 0, ecounts, at<int32_t>(ws, L->off_estart), spos, stok, stotal,
+                               T * K, L->error_word, 1, st));
+    MOE_TRY(moe_ep_pack_rows(at<void>(ws, L->off_xq), at<float>(ws, L->off_xs), L->xs_ld, stok, stotal, T * K, H,
+                             at<void>(ws, L->off_psend), st));
+    std::vector<size_t> cc(ep, static_cast<size_t>(epr)), co(ep);
+    for (int p = 0; p < ep; ++p) co[p] = static_cast<size_t>(p) * epr;
+    MOE_TRY(nccl_to_moe(ncwAllToAllv(ecounts, cc.data(), co.data(), rcounts, cc.data(), co.data(), NCW_INT32,
+                                     L->comm, st)));
+    if (cudaMemcpyAsync(L->h_counts, ecounts, 2 * static_cast<size_t>(E) * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+        return MOE_ERR_CUDA;
+    MOE_TRY(nccl_to_moe(ncwStreamSynchronizeTimeout(L->comm, st, L->sync_timeout_ms)));
+    std::vector<size_t> srows(ep), soff(ep), rrows(ep), roff(ep);
+    size_t stot = 0, rtot = 0;
+    MOE_TRY(moe_ep_plan_host(ep, epr, L->h_counts, L->h_counts + E, srows.data(), soff.data(), rrows.data(),
+                             roff.data(), &stot, &rtot));
+    // Cannot trigger while every rank keeps T <= max_tokens (recv_cap is the
+    // worst case); a peer that broke that contract has already sent.
+    if (rtot > static_cast<size_t>(L->recv_cap) || stot > static_cast<size_t>(T) * K) return MOE_ERR_WORKSPACE;
+
+    mark(L, 3, st);
+    {
+        std::vector<size_t> sb(ep), sbo(ep), rbn(ep), rbo(ep);
+        for (int p = 0; p < ep; ++p) { sb[p] = srows[p] * rb; sbo[p] = soff[p] * rb; rbn[p] = rrows[p] * rb; rbo[p] = roff[p] * rb; }
+        MOE_TRY(nccl_to_moe(ncwAllToAllv(at<void>(ws, L->off_psend), sb.data(), sbo.data(), at<void>(ws, L->off_precv),
+                                         rbn.data(), rbo.data(), NCW_UINT8, L->comm, st)));
+    }
+    MOE_TRY(moe_ep_recv_plan(rcounts, ep, epr, T, S, counts, start, total, row_src, recv_dst, L->rcap, L->recv_cap,
+                             L->error_word, st));
+    MOE_TRY(moe_ep_gather(at<void>(ws, L->off_precv), at<void>(ws, L->off_xq), at<float>(ws, L->off_xs), L->xs_ld,
+                          row_src, total, L->rcap, H, at<void>(ws, L->off_xp), at<float>(ws, L->off_xps), L->rcap, st));
+    cbwGroupedGemmArgs g1 = gemm_args(L, ws, false), g2 = gemm_args(L, ws, true);
+    mark(L, 4, st);
+    MOE_TRY(cbw_to_moe(cbwFp8BlockScaledGroupedGemm(&g1, L->error_word, st)));
+    mark(L, 5, st);
+    MOE_TRY(cbw_to_moe(cbwFp8BlockScaledGroupedGemm(&g2, L->error_word, st)));
+    mark(L, 6, st);
+    MOE_TRY(moe_ep_pack_y(at<void>(ws, L->off_y), recv_dst, static_cast<int>(rtot), H, at<void>(ws, L->off_ysend), st));
+    {
+        const size_t hw = static_cast<size_t>(H);
+        std::vector<size_t> sn(ep), so(ep), rn(ep), ro(ep);
+        for (int p = 0; p < ep; ++p) { sn[p] = rrows[p] * hw; so[p] = roff[p] * hw; rn[p] = srows[p] * hw; ro[p] = soff[p] * hw; }
+        MOE_TRY(nccl_to_moe(ncwAllToAllv(at<void>(ws, L->off_ysend), sn.data(), so.data(), at<void>(ws, L->off_yrecv),
+                                         rn.data(), ro.data(), NCW_BFLOAT16, L->comm, st)));
+    }
+    MOE_TRY(moe_combine_split(x, at<void>(ws, L->off_yrecv), spos, wts, at<void>(ws, L->off_y), start + epr, S, T, K,
+                              H, out, st));
+    mark(L, MOE_NUM_STAGES, st);
+    return MOE_OK;
+}
+
+moe_status_t run_experts_any(moe_layer* L, const void* x, const int32_t* idx, const float* wts, void* out, int T,
+                             void* ws, cudaStream_t st) {
+    if (L->cfg.ep_size > 1) return run_experts_ep(L, idx, wts, x, out, T, ws, st);
+    return run_experts(L, x, idx, wts, out, T, ws, st);
 }
 
 }  // namespace
@@ -176,7 +298,7 @@ moe_status_t moe_layer_create(const moe_layer_config_t* cfg, const moe_layer_wei
     if (c.num_shared < 0 || c.num_shared > 1 || c.max_tokens <= 0) return MOE_ERR_INVALID_ARGUMENT;
     if (c.ep_size <= 0 || c.ep_rank < 0 || c.ep_rank >= c.ep_size || c.num_experts % c.ep_size) return MOE_ERR_INVALID_ARGUMENT;
     if (c.ep_size > 1 && !comm) return MOE_ERR_INVALID_ARGUMENT;
-    if (c.ep_size > 1) return MOE_ERR_UNSUPPORTED;
+    if (c.ep_size > 1 && c.num_experts > 1024) return MOE_ERR_UNSUPPORTED;
     if (!w->norm_gamma || !w->router_w || !w->w13 || !w->s13 || !w->w2 || !w->s2) return MOE_ERR_INVALID_ARGUMENT;
     moe_layer* L = new (std::nothrow) moe_layer;
     if (!L) return MOE_ERR_INVALID_ARGUMENT;
@@ -190,6 +312,15 @@ moe_status_t moe_layer_create(const moe_layer_config_t* cfg, const moe_layer_wei
     L->groups = per + c.num_shared;
     if (cudaMalloc(&L->error_word, sizeof(int)) != cudaSuccess) { delete L; return MOE_ERR_CUDA; }
     if (cudaMemset(L->error_word, 0, sizeof(int)) != cudaSuccess) { cudaFree(L->error_word); delete L; return MOE_ERR_CUDA; }
+    if (c.ep_size > 1) {
+        if (cudaMallocHost(&L->h_counts, 2 * static_cast<size_t>(c.num_experts) * sizeof(int32_t)) != cudaSuccess) {
+            cudaFree(L->error_word);
+            delete L;
+            return MOE_ERR_CUDA;
+        }
+        const char* tm = std::getenv("TIME_B200_EP_TIMEOUT_MS");
+        L->sync_timeout_ms = (tm && std::atoi(tm) > 0) ? std::atoi(tm) : 120000;
+    }
     plan_workspace(L);
     *out = L;
     return MOE_OK;
@@ -197,6 +328,7 @@ moe_status_t moe_layer_create(const moe_layer_config_t* cfg, const moe_layer_wei
 
 moe_status_t moe_layer_destroy(moe_layer_t* L) {
     if (!L) return MOE_OK;
+    if (L->h_counts) cudaFreeHost(L->h_counts);
     cudaFree(L->error_word);
     delete L;
     return MOE_OK;
@@ -206,25 +338,25 @@ size_t moe_layer_workspace_bytes(const moe_layer_t* L) { return L ? L->bytes : 0
 
 moe_status_t moe_layer_forward_routed(moe_layer_t* L, const void* x, const int32_t* idx, const float* wts, void* out,
                                       int T, void* ws, size_t ws_bytes, cwStream_t stream) {
-    if (!L || !x || !out || !ws || !idx || !wts) return MOE_ERR_INVALID_ARGUMENT;
+    if (!L || !ws || (T > 0 && (!x || !out || !idx || !wts))) return MOE_ERR_INVALID_ARGUMENT;
     if (T < 0 || T > L->cfg.max_tokens) return MOE_ERR_INVALID_ARGUMENT;
     if (ws_bytes < L->bytes) return MOE_ERR_WORKSPACE;
-    if (T == 0) return MOE_OK;
+    if (T == 0 && L->cfg.ep_size == 1) return MOE_OK;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const moe_layer_config_t& c = L->cfg;
     mark(L, 0, st);
     MOE_TRY(moe_rmsnorm_quant(x, L->w.norm_gamma, T, c.hidden, c.rms_eps, at<float>(ws, L->off_rms),
                               at<void>(ws, L->off_xq), at<float>(ws, L->off_xs), L->xs_ld, stream));
     mark(L, 1, st);
-    return run_experts(L, x, idx, wts, out, T, ws, st);
+    return run_experts_any(L, x, idx, wts, out, T, ws, st);
 }
 
 moe_status_t moe_layer_forward(moe_layer_t* L, const void* x, void* out, int T, void* ws, size_t ws_bytes,
                                cwStream_t stream) {
-    if (!L || !x || !out || !ws) return MOE_ERR_INVALID_ARGUMENT;
+    if (!L || !ws || (T > 0 && (!x || !out))) return MOE_ERR_INVALID_ARGUMENT;
     if (T < 0 || T > L->cfg.max_tokens) return MOE_ERR_INVALID_ARGUMENT;
     if (ws_bytes < L->bytes) return MOE_ERR_WORKSPACE;
-    if (T == 0) return MOE_OK;
+    if (T == 0 && L->cfg.ep_size == 1) return MOE_OK;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const moe_layer_config_t& c = L->cfg;
     float* rms = at<float>(ws, L->off_rms);
@@ -236,7 +368,7 @@ moe_status_t moe_layer_forward(moe_layer_t* L, const void* x, void* out, int T, 
     mark(L, 1, st);
     MOE_TRY(moe_router_topk(x, rms, L->w.norm_gamma, L->w.router_w, L->w.router_bias, T, c.hidden, c.num_experts,
                             c.top_k, nullptr, idx, wts, stream));
-    return run_experts(L, x, idx, wts, out, T, ws, st);
+    return run_experts_any(L, x, idx, wts, out, T, ws, st);
 }
 
 moe_status_t moe_layer_last_routing(const moe_layer_t* L, const void* ws, const int32_t** idx, const float** wts,

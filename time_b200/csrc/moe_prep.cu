@@ -221,18 +221,19 @@ router_topk_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict_
 
 // ---------------------------------------------------------------- permutation
 // Single block (1024 threads).  Pass 1 counts pairs per local expert; the
-// padded exclusive scan gives the segment starts; pass 2 assigns each pair its
+// exclusive scan of the counts rounded up to `pad` rows gives the segment
+// starts (pad 16 for the GEMM's row segments, 1 for a dense send order); pass 2 assigns each pair its
 // row with a stable rank: within a warp by __match_any_sync + popc of the
 // lower lanes, across the 32 warps of a 1024-pair chunk by a [32][G] table of
 // per-warp counts, across chunks by a running count per group.
 constexpr int kPermThreads = 1024;
-constexpr int kRowPad = 16;
+constexpr int kRowPad = 16;   // segment alignment of the GEMM's row layout
 
 __global__ void __launch_bounds__(kPermThreads)
 permute_kernel(const int32_t* __restrict__ idx, int T, int K, int e_begin, int e_end, int num_shared,
                int32_t* __restrict__ counts, int32_t* __restrict__ seg_start, int32_t* __restrict__ pos,
                int32_t* __restrict__ row_token, int32_t* __restrict__ total_rows, int row_capacity,
-               int* __restrict__ error_word) {
+               int* __restrict__ error_word, int pad) {
     extern __shared__ int sh[];
     const int Gr = e_end - e_begin;
     const int G = Gr + num_shared;
@@ -257,7 +258,7 @@ permute_kernel(const int32_t* __restrict__ idx, int T, int K, int e_begin, int e
         int local = 0;
         for (int i = 0; i < per; ++i) {
             const int g = lane * per + i;
-            if (g < G) local += (cnt[g] + kRowPad - 1) / kRowPad * kRowPad;
+            if (g < G) local += (cnt[g] + pad - 1) / pad * pad;
         }
         int incl = local;
         for (int o = 1; o < 32; o <<= 1) {
@@ -267,7 +268,7 @@ permute_kernel(const int32_t* __restrict__ idx, int T, int K, int e_begin, int e
         int run = incl - local;
         for (int i = 0; i < per; ++i) {
             const int g = lane * per + i;
-            if (g < G) { start[g] = run; run += (cnt[g] + kRowPad - 1) / kRowPad * kRowPad; }
+            if (g < G) { start[g] = run; run += (cnt[g] + pad - 1) / pad * pad; }
         }
         if (lane == 31) s_total = incl;
     }
@@ -349,12 +350,15 @@ gather_rows_kernel(const uint8_t* __restrict__ xq, const float* __restrict__ xs,
 }
 
 // ---------------------------------------------------------------- combine
-// out[t] = bf16(x + sum shared y + sum_s fma(w, y[pos]) ), 8 columns per thread.
+// out[t] = bf16(x + sum shared ys[shared_rows[g] + t] + sum_s fma(w, y[pos]) ),
+// 8 columns per thread.  y holds the routed rows, ys the shared expert's (the
+// same buffer on one GPU; with expert parallelism the routed rows come back
+// from the owning ranks into their own buffer).
 __global__ void __launch_bounds__(128)
 combine_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ y,
                const int32_t* __restrict__ pos, const float* __restrict__ topk_w,
-               const int32_t* __restrict__ shared_rows, int num_shared, int T, int K, int H,
-               __nv_bfloat16* __restrict__ out) {
+               const __nv_bfloat16* __restrict__ ys, const int32_t* __restrict__ shared_rows, int num_shared,
+               int T, int K, int H, __nv_bfloat16* __restrict__ out) {
     const int t = blockIdx.x;
     if (t >= T) return;
     __shared__ int s_row[16 + 2];
@@ -370,7 +374,7 @@ combine_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restr
         float a[8] = {bf16_lo(xv.x), bf16_hi(xv.x), bf16_lo(xv.y), bf16_hi(xv.y),
                       bf16_lo(xv.z), bf16_hi(xv.z), bf16_lo(xv.w), bf16_hi(xv.w)};
         for (int sidx = 0; sidx < num_shared; ++sidx) {
-            const uint4 yv = *reinterpret_cast<const uint4*>(y + static_cast<size_t>(s_row[16 + sidx]) * H + c);
+            const uint4 yv = *reinterpret_cast<const uint4*>(ys + static_cast<size_t>(s_row[16 + sidx]) * H + c);
             a[0] = __fadd_rn(a[0], bf16_lo(yv.x)); a[1] = __fadd_rn(a[1], bf16_hi(yv.x));
             a[2] = __fadd_rn(a[2], bf16_lo(yv.y)); a[3] = __fadd_rn(a[3], bf16_hi(yv.y));
             a[4] = __fadd_rn(a[4], bf16_lo(yv.z)); a[5] = __fadd_rn(a[5], bf16_hi(yv.z));
@@ -408,9 +412,10 @@ extern "C" {
 moe_status_t moe_rmsnorm_quant(const void* x_bf16, const float* gamma, int T, int H, float eps,
                                float* rms_out, void* xq_out, float* xs_out, int xs_ld,
                                cwStream_t stream) {
-    if (T < 0 || H <= 0 || H % 128 || !x_bf16 || !gamma || !xq_out || !xs_out || xs_ld < T) return MOE_ERR_INVALID_ARGUMENT;
-    if (!aligned16(x_bf16) || !aligned16(gamma) || !aligned16(xq_out)) return MOE_ERR_INVALID_ARGUMENT;
+    if (T < 0 || H <= 0 || H % 128 || xs_ld < T) return MOE_ERR_INVALID_ARGUMENT;
     if (T == 0) return MOE_OK;
+    if (!x_bf16 || !gamma || !xq_out || !xs_out) return MOE_ERR_INVALID_ARGUMENT;
+    if (!aligned16(x_bf16) || !aligned16(gamma) || !aligned16(xq_out)) return MOE_ERR_INVALID_ARGUMENT;
     const int blocks = (T + 7) / 8;
     rmsnorm_quant_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const __nv_bfloat16*>(x_bf16), gamma, T, H, eps, rms_out,
@@ -424,8 +429,8 @@ moe_status_t moe_router_topk(const void* x_bf16, const float* rms, const float* 
                              float* logits_out, int32_t* topk_idx, float* topk_w,
                              cwStream_t stream) {
     if (T < 0 || H <= 0 || H % kRouterKC || E <= 0 || E > 256 || k <= 0 || k > 16 || k > E) return MOE_ERR_INVALID_ARGUMENT;
-    if (!x_bf16 || !rms || !gamma || !router_w || !topk_idx || !topk_w) return MOE_ERR_INVALID_ARGUMENT;
     if (T == 0) return MOE_OK;
+    if (!x_bf16 || !rms || !gamma || !router_w || !topk_idx || !topk_w) return MOE_ERR_INVALID_ARGUMENT;
     const int blocks = (T + kRouterTok - 1) / kRouterTok;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x_bf16);
@@ -445,12 +450,13 @@ moe_status_t moe_router_topk(const void* x_bf16, const float* rms, const float* 
     return launch_status();
 }
 
-moe_status_t moe_permute(const int32_t* topk_idx, int T, int k, int e_begin, int e_end,
-                         int num_shared, int32_t* counts, int32_t* seg_start, int32_t* pos,
-                         int32_t* row_token, int32_t* total_rows, int row_capacity,
-                         int* error_word, cwStream_t stream) {
+moe_status_t moe_permute_padded(const int32_t* topk_idx, int T, int k, int e_begin, int e_end,
+                                int num_shared, int32_t* counts, int32_t* seg_start, int32_t* pos,
+                                int32_t* row_token, int32_t* total_rows, int row_capacity,
+                                int* error_word, int pad, cwStream_t stream) {
     const int G = (e_end - e_begin) + num_shared;
     if (T < 0 || k <= 0 || e_begin < 0 || e_end < e_begin || num_shared < 0 || G <= 0 || G > 1024) return MOE_ERR_INVALID_ARGUMENT;
+    if (pad < 1 || pad > 128) return MOE_ERR_INVALID_ARGUMENT;
     if (!topk_idx || !counts || !seg_start || !pos || !row_token || !total_rows || row_capacity < 0) return MOE_ERR_INVALID_ARGUMENT;
     const size_t smem = static_cast<size_t>(3 * G + 32 * G) * sizeof(int);
     if (smem > 200 * 1024) return MOE_ERR_UNSUPPORTED;
@@ -461,8 +467,16 @@ moe_status_t moe_permute(const int32_t* topk_idx, int T, int k, int e_begin, int
     }
     permute_kernel<<<1, kPermThreads, smem, static_cast<cudaStream_t>(stream)>>>(
         topk_idx, T, k, e_begin, e_end, num_shared, counts, seg_start, pos, row_token, total_rows,
-        row_capacity, error_word);
+        row_capacity, error_word, pad);
     return launch_status();
+}
+
+moe_status_t moe_permute(const int32_t* topk_idx, int T, int k, int e_begin, int e_end,
+                         int num_shared, int32_t* counts, int32_t* seg_start, int32_t* pos,
+                         int32_t* row_token, int32_t* total_rows, int row_capacity,
+                         int* error_word, cwStream_t stream) {
+    return moe_permute_padded(topk_idx, T, k, e_begin, e_end, num_shared, counts, seg_start, pos, row_token,
+                              total_rows, row_capacity, error_word, kRowPad, stream);
 }
 
 moe_status_t moe_gather_rows_n(const void* xq, const float* xs, int xs_ld, const int32_t* row_token,
@@ -485,17 +499,27 @@ moe_status_t moe_gather_rows(const void* xq, const float* xs, int xs_ld, const i
     return moe_gather_rows_n(xq, xs, xs_ld, row_token, nullptr, row_capacity, H, xp, xps, xps_ld, stream);
 }
 
+moe_status_t moe_combine_split(const void* x_bf16, const void* y_bf16, const int32_t* pos,
+                               const float* topk_w, const void* y_shared_bf16, const int32_t* shared_rows,
+                               int num_shared, int T, int k, int H, void* out_bf16, cwStream_t stream) {
+    if (T < 0 || k <= 0 || k > 16 || H <= 0 || H % 8 || num_shared < 0 || num_shared > 2) return MOE_ERR_INVALID_ARGUMENT;
+    if (T == 0) return MOE_OK;
+    if (!x_bf16 || !y_bf16 || !pos || !topk_w || !out_bf16 || (num_shared && (!shared_rows || !y_shared_bf16)))
+        return MOE_ERR_INVALID_ARGUMENT;
+    if (!aligned16(x_bf16) || !aligned16(y_bf16) || !aligned16(out_bf16) || (num_shared && !aligned16(y_shared_bf16)))
+        return MOE_ERR_INVALID_ARGUMENT;
+    combine_kernel<<<T, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const __nv_bfloat16*>(x_bf16), static_cast<const __nv_bfloat16*>(y_bf16), pos, topk_w,
+        static_cast<const __nv_bfloat16*>(y_shared_bf16), shared_rows, num_shared, T, k, H,
+        static_cast<__nv_bfloat16*>(out_bf16));
+    return launch_status();
+}
+
 moe_status_t moe_combine(const void* x_bf16, const void* y_bf16, const int32_t* pos,
                          const float* topk_w, const int32_t* shared_rows, int num_shared,
                          int T, int k, int H, void* out_bf16, cwStream_t stream) {
-    if (T < 0 || k <= 0 || k > 16 || H <= 0 || H % 8 || num_shared < 0 || num_shared > 2) return MOE_ERR_INVALID_ARGUMENT;
-    if (!x_bf16 || !y_bf16 || !pos || !topk_w || !out_bf16 || (num_shared && !shared_rows)) return MOE_ERR_INVALID_ARGUMENT;
-    if (!aligned16(x_bf16) || !aligned16(y_bf16) || !aligned16(out_bf16)) return MOE_ERR_INVALID_ARGUMENT;
-    if (T == 0) return MOE_OK;
-    combine_kernel<<<T, 128, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const __nv_bfloat16*>(x_bf16), static_cast<const __nv_bfloat16*>(y_bf16), pos, topk_w,
-        shared_rows, num_shared, T, k, H, static_cast<__nv_bfloat16*>(out_bf16));
-    return launch_status();
+    return moe_combine_split(x_bf16, y_bf16, pos, topk_w, y_bf16, shared_rows, num_shared, T, k, H, out_bf16,
+                             stream);
 }
 
 }  // extern "C"

@@ -75,6 +75,25 @@ ncclRedOp_t rop(ncwReduceOp_t o) {
 inline ncclComm_t C(ncwComm_t c) { return static_cast<ncclComm_t>(c); }
 inline cudaStream_t S(cwStream_t s) { return static_cast<cudaStream_t>(s); }
 
+// A non-blocking communicator (ncwCommInitRankTimeout) may answer a call with
+// ncclInProgress while it is still enqueueing; the next call on it must wait
+// until the state settles.  Bounded: after 60 s the communicator is aborted.
+ncclResult_t settle(ncclComm_t comm, ncclResult_t e) {
+    if (e != ncclInProgress) return e;
+    const auto t0 = std::chrono::steady_clock::now();
+    ncclResult_t st = ncclInProgress;
+    while (true) {
+        const ncclResult_t q = ncclCommGetAsyncError(comm, &st);
+        if (q != ncclSuccess) return q;
+        if (st != ncclInProgress) return st;
+        if (std::chrono::steady_clock::now() - t0 > std::chrono::seconds(60)) {
+            ncclCommAbort(comm);
+            return ncclSystemError;
+        }
+        std::this_thread::yield();
+    }
+}
+
 }  // namespace
 
 extern "C" {
@@ -177,15 +196,15 @@ ncwResult_t ncwAllToAllv(const void* sendbuff, const size_t* send_counts, const 
         if (p == me) continue;
         if (send_counts[p]) {
             e = ncclSend(sb + send_offsets[p] * es, send_counts[p], t, p, C(comm), S(stream));
-            if (e != ncclSuccess) break;
+            if (e != ncclSuccess && e != ncclInProgress) break;
         }
         if (recv_counts[p]) {
             e = ncclRecv(rb + recv_offsets[p] * es, recv_counts[p], t, p, C(comm), S(stream));
-            if (e != ncclSuccess) break;
+            if (e != ncclSuccess && e != ncclInProgress) break;
         }
     }
-    ncclResult_t e2 = ncclGroupEnd();
-    if (e != ncclSuccess) return report(e, "ncwAllToAllv send/recv");
+    ncclResult_t e2 = settle(C(comm), ncclGroupEnd());
+    if (e != ncclSuccess && e != ncclInProgress) return report(e, "ncwAllToAllv send/recv");
     return report(e2, "ncwAllToAllv group");
 }
 

@@ -81,12 +81,84 @@ def libs():
                                       c_void_p]
         k.moe_combine.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
                                   c_void_p, c_void_p]
+        k.moe_combine_split.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
+                                        c_int, c_int, c_void_p, c_void_p]
+        k.moe_permute_padded.argtypes = [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p,
+                                         c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p]
+        k.moe_ep_row_bytes.argtypes = [c_int]
+        k.moe_ep_row_bytes.restype = c_size_t
+        sz_p = ctypes.POINTER(c_size_t)
+        k.moe_ep_plan_host.argtypes = [c_int, c_int, c_i32p, c_i32p, sz_p, sz_p, sz_p, sz_p, sz_p, sz_p]
+        k.moe_ep_pack_rows.argtypes = [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_void_p,
+                                       c_void_p]
+        k.moe_ep_recv_plan.argtypes = [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
+                                       c_void_p, c_int, c_int, c_void_p, c_void_p]
+        k.moe_ep_gather.argtypes = [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_void_p,
+                                    c_void_p, c_int, c_void_p]
+        k.moe_ep_pack_y.argtypes = [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]
         k.moe_status_string.restype = ctypes.c_char_p
         k.kernels_last_error.restype = c_int
         b = L["libcublaswrap.so"]
         b.cbwFp8BlockScaledGroupedGemm.argtypes = [ctypes.POINTER(GroupedGemmArgs), c_void_p, c_void_p]
+        n = L["libncclwrap.so"]
+        n.ncwGetUniqueId.argtypes = [ctypes.POINTER(UniqueId)]
+        n.ncwCommInitRank.argtypes = [ctypes.POINTER(c_void_p), c_int, UniqueId, c_int]
+        n.ncwCommInitRankTimeout.argtypes = [ctypes.POINTER(c_void_p), c_int, UniqueId, c_int, c_int]
+        n.ncwCommDestroy.argtypes = [c_void_p]
+        n.ncwCommAbort.argtypes = [c_void_p]
+        n.ncwCommGetAsyncError.argtypes = [c_void_p]
+        n.ncwGetErrorString.restype = ctypes.c_char_p
         _bound = True
     return L
+
+
+class UniqueId(ctypes.Structure):
+    _fields_ = [("internal", ctypes.c_char * 128)]
+
+
+def ep_plan_host(ep_size: int, experts_per_rank: int, send_expert_counts, recv_counts):
+    """moe_ep_plan_host on host int32 sequences; returns
+    (send_rows, send_offsets, recv_rows, recv_offsets, send_total, recv_total)."""
+    import numpy as np
+    k = libs()["libkernels.so"]
+    a = np.ascontiguousarray(send_expert_counts, dtype=np.int32)
+    b = np.ascontiguousarray(recv_counts, dtype=np.int32)
+    assert a.size == ep_size * experts_per_rank and b.size == ep_size * experts_per_rank
+    outs = [(c_size_t * ep_size)() for _ in range(4)]
+    st, rt = c_size_t(), c_size_t()
+    check("moe_ep_plan_host", k.moe_ep_plan_host(ep_size, experts_per_rank, a.ctypes.data_as(c_i32p),
+                                                 b.ctypes.data_as(c_i32p), *outs, ctypes.byref(st),
+                                                 ctypes.byref(rt)))
+    return tuple(list(o) for o in outs) + (st.value, rt.value)
+
+
+def nccl_comm(rank: int, world: int, timeout_ms: int | None = None) -> int:
+    """An ncwComm_t over the torch.distributed world: rank 0 draws the NCCL
+    unique id (ncwGetUniqueId) and torch.distributed broadcasts it."""
+    import torch.distributed as dist
+    n = libs()["libncclwrap.so"]
+    uid = UniqueId()
+    if rank == 0:
+        rc = n.ncwGetUniqueId(ctypes.byref(uid))
+        if rc != 0:
+            raise RuntimeError(f"ncwGetUniqueId failed: {n.ncwGetErrorString(rc).decode()}")
+    raw = bytes(ctypes.string_at(ctypes.addressof(uid), 128)) if rank == 0 else None
+    box = [raw]
+    dist.broadcast_object_list(box, src=0)
+    ctypes.memmove(ctypes.addressof(uid), box[0], 128)
+    comm = c_void_p()
+    if timeout_ms is None:
+        rc = n.ncwCommInitRank(ctypes.byref(comm), world, uid, rank)
+    else:
+        rc = n.ncwCommInitRankTimeout(ctypes.byref(comm), world, uid, rank, timeout_ms)
+    if rc != 0:
+        raise RuntimeError(f"ncwCommInitRank failed: {n.ncwGetErrorString(rc).decode()}")
+    return comm.value
+
+
+def nccl_comm_destroy(comm: int | None) -> None:
+    if comm:
+        libs()["libncclwrap.so"].ncwCommDestroy(comm)
 
 
 def check(fn: str, code: int) -> None:

@@ -79,6 +79,27 @@ def make_moe_weights(shape: MoEShape, seed: int = 0, device="cpu", zipf_bias: bo
     return out
 
 
+def expert_slice(w: dict, shape: MoEShape, ep_size: int, ep_rank: int) -> dict:
+    """The weights expert-parallel rank `ep_rank` holds: routed experts
+    [r*E/ep, (r+1)*E/ep) then the shared expert(s), as contiguous copies; the
+    router stays replicated."""
+    E, S = shape.num_experts, shape.num_shared
+    per = E // ep_size
+    keep = list(range(ep_rank * per, (ep_rank + 1) * per)) + list(range(E, E + S))
+    out = {k: v for k, v in w.items() if k not in ("w13", "s13", "w2", "s2")}
+    for k in ("w13", "s13", "w2", "s2"):
+        out[k] = w[k][keep].contiguous()
+    return out
+
+
+def token_slice(tokens: int, ep_size: int, ep_rank: int) -> tuple[int, int]:
+    """[begin, end) of the global tokens rank `ep_rank` owns (contiguous,
+    the first tokens % ep_size ranks one longer)."""
+    base, extra = divmod(tokens, ep_size)
+    begin = ep_rank * base + min(ep_rank, extra)
+    return begin, begin + base + (1 if ep_rank < extra else 0)
+
+
 def make_x(shape: MoEShape, tokens: int, seed: int = 0, device="cpu",
            gen: torch.Generator | None = None) -> torch.Tensor:
     g = gen or torch.Generator(device=device).manual_seed(seed)
