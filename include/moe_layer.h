@@ -140,6 +140,23 @@ moe_status_t moe_rmsnorm_quant(const void* x_bf16, const float* gamma, int T, in
                                float* rms_out, void* xq_out, float* xs_out, int xs_ld,
                                cwStream_t stream);
 
+/* moe_rmsnorm_quant that also stores n = (x/rms)*gamma in fp32 ([T][H],
+ * 16-byte aligned) when n_out is not NULL -- the router's input. */
+moe_status_t moe_rmsnorm_quant_n(const void* x_bf16, const float* gamma, int T, int H, float eps,
+                                 float* rms_out, float* n_out, void* xq_out, float* xs_out,
+                                 int xs_ld, cwStream_t stream);
+
+/* Router logits from the stored n: logits[t][e] = fma-chain over
+ * i = 0..H-1 of n[t][i]*W[e][i] from +0.0f (+ bias[e]) -- bit-identical to
+ * the logits moe_router_topk computes; H a multiple of 128, E <= 256. */
+moe_status_t moe_router_logits(const float* n, const float* router_w, const float* router_bias,
+                               int T, int H, int E, float* logits, cwStream_t stream);
+
+/* Top-k + weights of given logits [T][E] with the same rule as
+ * moe_router_topk. */
+moe_status_t moe_topk_softmax(const float* logits, int T, int E, int k, int32_t* topk_idx,
+                              float* topk_w, cwStream_t stream);
+
 /* Router: logits[t][e] = fma-chain over i = 0..H-1 of n[t][i]*W[e][i]
  * (+ bias[e]), n recomputed from x, rms, gamma exactly as above; then the
  * reference's top-k (strict '>' from -FLT_MAX: lower index wins ties, NaN

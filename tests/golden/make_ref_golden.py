@@ -41,8 +41,16 @@ def load_ref():
     return lib
 
 
+_KEEP = []
+
+
 def dev(a: np.ndarray) -> torch.Tensor:
-    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    """Device copy that stays alive until the end of the run: a temporary
+    freed right after .data_ptr() could be handed to the next copy by the
+    caching allocator before the asynchronous kernel has read it."""
+    t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    _KEEP.append(t)
+    return t
 
 
 def host(t: torch.Tensor) -> np.ndarray:

@@ -4,8 +4,9 @@ oracle/_ref/ and run on a B200 by tests/golden/make_ref_golden.py) on seeded
 inputs.  No GPU needed here.
 
 Bars: bit-exact for the codec, RMSNorm, router logits and top-k indices; the
-top-k weights within 2 ulp (the reference's device expf against the host
-libm expf).
+top-k weights within rtol 1e-6 (about 8 ulp): the reference calls the device
+expf (documented maximum error 2 ulp) eight times and divides by their sum,
+the oracle the correctly rounded host expf.
 """
 from pathlib import Path
 
@@ -52,4 +53,4 @@ def test_topk(g, oracle, name, k):
     idx, w = oracle.moe_topk_ref(g[f"{name}_logits"], k)
     assert np.array_equal(idx, g[f"{name}_idx"])
     ref_w = g[f"{name}_w"]
-    assert np.allclose(w, ref_w, rtol=2.5e-7, atol=1e-30), np.max(np.abs(w - ref_w))
+    assert np.allclose(w, ref_w, rtol=1e-6, atol=1e-30), np.max(np.abs(w - ref_w))

@@ -91,6 +91,49 @@ def test_router_topk_bit_exact(gpu, oracle, T, H, E, K, bias):
     assert np.allclose(w.cpu().numpy(), ow, rtol=2e-6, atol=1e-7)
 
 
+@pytest.mark.parametrize("T,H,E,K,bias", [(5, 256, 8, 2, False), (70, 512, 160, 8, True), (33, 256, 64, 16, False),
+                                          (300, 5120, 160, 8, True), (17, 384, 200, 4, True)])
+def test_tiled_router_bit_exact(gpu, oracle, T, H, E, K, bias):
+    """The layer's router (stored n -> tiled logits -> top-k kernel) against
+    the oracle and against moe_router_topk: identical bits."""
+    k = M.libs()["libkernels.so"]
+    g = torch.Generator().manual_seed(E * 11 + T)
+    x = (torch.randn(T, H, generator=g) * torch.exp(torch.randn(T, 1, generator=g))).to(torch.bfloat16)
+    gamma = (1 + 0.1 * torch.randn(H, generator=g)).float()
+    W = torch.randn(E, H, generator=g) * 0.02
+    b = synth.zipf_bias(E, seed=2) if bias else None
+    xd, gd, Wd = x.to(gpu), gamma.to(gpu), W.to(gpu)
+    bd = b.to(gpu) if b is not None else None
+    rms = torch.empty(T, device=gpu)
+    n = torch.empty(T, H, device=gpu)
+    xq = torch.empty(T, H, dtype=torch.uint8, device=gpu)
+    ld = (T + 3) // 4 * 4
+    xs = torch.empty(H // 128, ld, device=gpu)
+    M.check("rmsnorm_n", k.moe_rmsnorm_quant_n(M.ptr(xd), M.ptr(gd), T, H, 1e-5, M.ptr(rms), M.ptr(n), M.ptr(xq),
+                                               M.ptr(xs), ld, stream()))
+    logits = torch.empty(T, E, device=gpu)
+    M.check("router_logits", k.moe_router_logits(M.ptr(n), M.ptr(Wd), M.ptr(bd), T, H, E, M.ptr(logits), stream()))
+    idx = torch.empty(T, K, dtype=torch.int32, device=gpu)
+    w = torch.empty(T, K, device=gpu)
+    M.check("topk_softmax", k.moe_topk_softmax(M.ptr(logits), T, E, K, M.ptr(idx), M.ptr(w), stream()))
+    logits2 = torch.empty(T, E, device=gpu)
+    idx2 = torch.empty(T, K, dtype=torch.int32, device=gpu)
+    w2 = torch.empty(T, K, device=gpu)
+    M.check("router", k.moe_router_topk(M.ptr(xd), M.ptr(rms), M.ptr(gd), M.ptr(Wd), M.ptr(bd), T, H, E, K,
+                                        M.ptr(logits2), M.ptr(idx2), M.ptr(w2), stream()))
+    torch.cuda.synchronize()
+    nref = oracle.rmsnorm_ref(x.float().numpy(), gamma.numpy(), 1e-5)
+    assert np.array_equal(n.cpu().numpy().view(np.uint32), nref.view(np.uint32))
+    lg = oracle.moe_gate_seq(nref, W.numpy(), b.numpy() if b is not None else None)
+    assert np.array_equal(logits.cpu().numpy().view(np.uint32), lg.view(np.uint32))
+    assert np.array_equal(logits.cpu().numpy().view(np.uint32), logits2.cpu().numpy().view(np.uint32))
+    oi, ow = oracle.moe_topk_ref(lg, K)
+    assert np.array_equal(idx.cpu().numpy(), oi)
+    assert np.array_equal(idx.cpu().numpy(), idx2.cpu().numpy())
+    assert np.array_equal(w.cpu().numpy().view(np.uint32), w2.cpu().numpy().view(np.uint32))
+    assert np.allclose(w.cpu().numpy(), ow, rtol=2e-6, atol=1e-7)
+
+
 @pytest.mark.parametrize("T,K,E,shared", [(1, 1, 4, 1), (37, 4, 9, 1), (4096, 8, 160, 1), (300, 2, 8, 0),
                                           (2048, 8, 160, 1)])
 def test_permute_bit_exact(gpu, oracle, T, K, E, shared):

@@ -4,6 +4,8 @@
 //
 // Data layout in HBM for one call (T tokens, G = local experts + shared):
 //   rms        [T] f32
+//   n          [T][H] f32          RMSNorm output (the router's input)
+//   logits     [T][E] f32          router logits
 //   xq         [T][H] e4m3         token order, 1x128-quantised RMSNorm output
 //   xs         [H/128][T_ld] f32   its scales (transposed: one K block's scales
 //                                  of consecutive rows are contiguous, so the
@@ -55,7 +57,7 @@ struct moe_layer {
     cudaEvent_t stage_ev[MOE_NUM_STAGES + 1];
     bool timing;
     // workspace layout (byte offsets)
-    size_t off_rms, off_xq, off_xs, off_idx, off_w, off_counts, off_start, off_total, off_pos, off_rowtok,
+    size_t off_rms, off_n, off_logits, off_xq, off_xs, off_idx, off_w, off_counts, off_start, off_total, off_pos, off_rowtok,
         off_xp, off_xps, off_hq, off_hs, off_y, bytes;
     int xs_ld, rcap;
     // expert parallelism
@@ -85,6 +87,8 @@ void plan_workspace(moe_layer* L) {
     size_t o = 0;
     auto take = [&o](size_t bytes) { size_t at = o; o = align_up(o + bytes, 256); return at; };
     L->off_rms = take(T * 4);
+    L->off_n = take(T * H * 4);
+    L->off_logits = take(T * static_cast<size_t>(c.num_experts) * 4);
     L->off_xq = take(T * H);
     L->off_xs = take((H / 128) * L->xs_ld * 4);
     L->off_idx = take(T * K * 4);
@@ -360,14 +364,16 @@ moe_status_t moe_layer_forward(moe_layer_t* L, const void* x, void* out, int T, 
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const moe_layer_config_t& c = L->cfg;
     float* rms = at<float>(ws, L->off_rms);
+    float* n = at<float>(ws, L->off_n);
+    float* logits = at<float>(ws, L->off_logits);
     mark(L, 0, st);
-    MOE_TRY(moe_rmsnorm_quant(x, L->w.norm_gamma, T, c.hidden, c.rms_eps, rms, at<void>(ws, L->off_xq),
-                              at<float>(ws, L->off_xs), L->xs_ld, stream));
+    MOE_TRY(moe_rmsnorm_quant_n(x, L->w.norm_gamma, T, c.hidden, c.rms_eps, rms, n, at<void>(ws, L->off_xq),
+                                at<float>(ws, L->off_xs), L->xs_ld, stream));
     int32_t* idx = at<int32_t>(ws, L->off_idx);
     float* wts = at<float>(ws, L->off_w);
     mark(L, 1, st);
-    MOE_TRY(moe_router_topk(x, rms, L->w.norm_gamma, L->w.router_w, L->w.router_bias, T, c.hidden, c.num_experts,
-                            c.top_k, nullptr, idx, wts, stream));
+    MOE_TRY(moe_router_logits(n, L->w.router_w, L->w.router_bias, T, c.hidden, c.num_experts, logits, stream));
+    MOE_TRY(moe_topk_softmax(logits, T, c.num_experts, c.top_k, idx, wts, stream));
     return run_experts_any(L, x, idx, wts, out, T, ws, st);
 }
 

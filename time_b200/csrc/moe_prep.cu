@@ -48,10 +48,11 @@ __device__ __forceinline__ float rowsumsq_ref_order(const __nv_bfloat16* x, int 
     return __shfl_sync(0xffffffffu, s, 0);
 }
 
-// One warp per token: rms, n = (x/rms)*gamma, 1x128 e4m3 quantisation of n.
+// One warp per token: rms, n = (x/rms)*gamma (stored in fp32 when n_out is
+// given, for the router), 1x128 e4m3 quantisation of n.
 __global__ void __launch_bounds__(256)
 rmsnorm_quant_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ gamma, int T, int H,
-                     float eps, float* __restrict__ rms_out, uint8_t* __restrict__ xq,
+                     float eps, float* __restrict__ rms_out, float* __restrict__ n_out, uint8_t* __restrict__ xq,
                      float* __restrict__ xs, int xs_ld) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
@@ -69,6 +70,7 @@ rmsnorm_quant_kernel(const __nv_bfloat16* __restrict__ x, const float* __restric
         float v1 = __fmul_rn(__fdiv_rn(bf16_hi(raw.x), rms), g.y);
         float v2 = __fmul_rn(__fdiv_rn(bf16_lo(raw.y), rms), g.z);
         float v3 = __fmul_rn(__fdiv_rn(bf16_hi(raw.y), rms), g.w);
+        if (n_out) *reinterpret_cast<float4*>(n_out + static_cast<size_t>(warp) * H + c) = make_float4(v0, v1, v2, v3);
         float amax = fmaxf(fmaxf(fabsf(v0), fabsf(v1)), fmaxf(fabsf(v2), fabsf(v3)));
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
@@ -82,6 +84,60 @@ rmsnorm_quant_kernel(const __nv_bfloat16* __restrict__ x, const float* __restric
         }
         *reinterpret_cast<uint32_t*>(qr + c) = packed;
         if (lane == 0) xs[static_cast<size_t>(b) * xs_ld + warp] = scale;
+    }
+}
+
+// ---------------------------------------------------------------- top-k
+// One warp selects the top K of one row of E <= 32*EPT logits with the
+// reference's rule (csrc/kernels.cu:437-471): scanning e = 0..E-1, a value
+// enters only if strictly greater (so the lower index wins a tie), NaN and
+// values <= -FLT_MAX never enter; empty slots get index -1 and weight 0.  The
+// weights are exp(v - shift) / sum over the selected slots, shift = v_max when
+// v_max > 80 (the reference overflows there) and 0 otherwise.  Lane l holds
+// e = l + 32j; each round takes the warp-wide (max value, min index).
+template <int EPT>
+__device__ __forceinline__ void topk_row(const float* row, int E, int K, int lane, int32_t* idx_out,
+                                         float* w_out) {
+    float v[EPT];
+    bool taken[EPT];
+#pragma unroll
+    for (int j = 0; j < EPT; ++j) {
+        const int e = lane + 32 * j;
+        const float lv = (e < E) ? row[e] : -FLT_MAX;
+        v[j] = (lv > -FLT_MAX) ? lv : -INFINITY;
+        taken[j] = false;
+    }
+    float sel_v[16];
+    int sel_i[16];
+    for (int s = 0; s < K; ++s) {
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int j = 0; j < EPT; ++j) {
+            const int e = lane + 32 * j;
+            if (!taken[j] && (v[j] > bv || (v[j] == bv && e < bi)) && v[j] > -INFINITY) { bv = v[j]; bi = e; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+        }
+        if (bi == 0x7fffffff) { sel_v[s] = -FLT_MAX; sel_i[s] = -1; continue; }
+        sel_v[s] = bv;
+        sel_i[s] = bi;
+#pragma unroll
+        for (int j = 0; j < EPT; ++j)
+            if (lane + 32 * j == bi) taken[j] = true;
+    }
+    if (lane == 0) {
+        const float shift = (sel_v[0] > 80.0f) ? sel_v[0] : 0.0f;
+        float sum = 0.0f;
+        for (int s = 0; s < K; ++s) sum += expf(sel_v[s] - shift);
+        for (int s = 0; s < K; ++s) {
+            idx_out[s] = sel_i[s];
+            w_out[s] = expf(sel_v[s] - shift) / sum;
+        }
     }
 }
 
@@ -173,50 +229,109 @@ router_topk_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict_
     for (int tl = warp; tl < kRouterTok; tl += 8) {
         const int t = t0 + tl;
         if (t >= T) break;
-        float v[EPT];
-        bool taken[EPT];
-#pragma unroll
-        for (int j = 0; j < EPT; ++j) {
-            const int e = lane + 32 * j;
-            const float lv = (e < E) ? lg_s[tl][e] : -FLT_MAX;
-            if (logits_out && e < E) logits_out[static_cast<size_t>(t) * E + e] = lv;
-            // NaN and values <= -FLT_MAX can never win the reference's strict '>' insertion
-            v[j] = (lv > -FLT_MAX) ? lv : -INFINITY;
-            taken[j] = false;
-        }
-        float sel_v[16];
-        int sel_i[16];
-        for (int s = 0; s < K; ++s) {
-            float bv = -INFINITY;
-            int bi = 0x7fffffff;
-#pragma unroll
-            for (int j = 0; j < EPT; ++j) {
-                const int e = lane + 32 * j;
-                if (!taken[j] && (v[j] > bv || (v[j] == bv && e < bi)) && v[j] > -INFINITY) { bv = v[j]; bi = e; }
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-            }
-            if (bi == 0x7fffffff) { sel_v[s] = -FLT_MAX; sel_i[s] = -1; continue; }
-            sel_v[s] = bv;
-            sel_i[s] = bi;
-#pragma unroll
-            for (int j = 0; j < EPT; ++j)
-                if (lane + 32 * j == bi) taken[j] = true;
-        }
-        if (lane == 0) {
-            const float shift = (sel_v[0] > 80.0f) ? sel_v[0] : 0.0f;
-            float sum = 0.0f;
-            for (int s = 0; s < K; ++s) sum += expf(sel_v[s] - shift);
-            for (int s = 0; s < K; ++s) {
-                topk_idx[static_cast<size_t>(t) * K + s] = sel_i[s];
-                topk_w[static_cast<size_t>(t) * K + s] = expf(sel_v[s] - shift) / sum;
-            }
-        }
+        if (logits_out)
+            for (int e = lane; e < E; e += 32) logits_out[static_cast<size_t>(t) * E + e] = lg_s[tl][e];
+        topk_row<EPT>(lg_s[tl], E, K, lane, topk_idx + static_cast<size_t>(t) * K, topk_w + static_cast<size_t>(t) * K);
     }
+}
+
+// ---------------------------------------------------------------- tiled router
+// logits[t][e] = (fma chain over k = 0..H-1 of n[t][k] * W[e][k], from +0.0f)
+// + bias[e]: the same per-(t, e) order as router_topk_kernel, laid out for
+// throughput instead of one block per 32 tokens.  Block: 16 tokens x 32
+// experts, 128 threads; thread (tp = lane & 7, ep = (lane >> 3) + 4 * warp)
+// owns tokens tp, tp+8 x experts ep, ep+16 (four independent chains, two
+// fma.rn.f32x2 per k).  K is staged through shared memory in chunks of 128
+// with cp.async double buffering; rows are padded by 4 floats (row r starts
+// at bank 4r mod 32), so the eight token rows tp and the four expert rows ep a
+// warp reads per 16-byte load land in distinct banks.  Grid: (expert tiles, token tiles) -- the expert tiles
+// of one token tile run back to back and share its n rows in L2.
+constexpr int kRtTok = 16, kRtExp = 32, kRtKC = 128, kRtLd = kRtKC + 4, kRtThreads = 128;
+constexpr size_t kRtSmem = 2 * (kRtTok + kRtExp) * kRtLd * sizeof(float);   // 50,688 B: 4 blocks per SM
+
+__global__ void __launch_bounds__(kRtThreads, 4)
+router_logits_kernel(const float* __restrict__ n, const float* __restrict__ W, const float* __restrict__ bias,
+                     int T, int H, int E, float* __restrict__ logits) {
+    extern __shared__ __align__(16) float rt_smem[];
+    auto n_s = reinterpret_cast<float (*)[kRtTok][kRtLd]>(rt_smem);                       // [2][16][132]
+    auto w_s = reinterpret_cast<float (*)[kRtExp][kRtLd]>(rt_smem + 2 * kRtTok * kRtLd);  // [2][32][132]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int e0 = blockIdx.x * kRtExp, t0 = blockIdx.y * kRtTok;
+    const int tp = lane & 7, ep = (lane >> 3) + 4 * warp;
+
+    auto load = [&](int stage, int k0) {
+        // 48 rows x 32 chunks of 16 bytes; rows past T / E are zero-filled
+        for (int c = tid; c < (kRtTok + kRtExp) * (kRtKC / 4); c += kRtThreads) {
+            const int row = c >> 5, q = c & 31;
+            if (row < kRtTok) {
+                const int t = t0 + row;
+                const float* src = n + static_cast<size_t>(t < T ? t : 0) * H + k0 + q * 4;
+                cp_async16(&n_s[stage][row][q * 4], src, t < T ? 16u : 0u);
+            } else {
+                const int r = row - kRtTok, e = e0 + r;
+                const float* src = W + static_cast<size_t>(e < E ? e : 0) * H + k0 + q * 4;
+                cp_async16(&w_s[stage][r][q * 4], src, e < E ? 16u : 0u);
+            }
+        }
+        cp_async_commit();
+    };
+
+    float2 acc0 = make_float2(0.0f, 0.0f);   // token tp:   experts ep, ep+16
+    float2 acc1 = make_float2(0.0f, 0.0f);   // token tp+8: experts ep, ep+16
+    const int nchunks = H / kRtKC;
+    load(0, 0);
+    for (int c = 0; c < nchunks; ++c) {
+        if (c + 1 < nchunks) {
+            load((c + 1) & 1, (c + 1) * kRtKC);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        const int s = c & 1;
+        const float* na = &n_s[s][tp][0];
+        const float* nb = &n_s[s][tp + 8][0];
+        const float* wa = &w_s[s][ep][0];
+        const float* wb = &w_s[s][ep + 16][0];
+#pragma unroll 8
+        for (int kk = 0; kk < kRtKC; kk += 4) {
+            const float4 a = *reinterpret_cast<const float4*>(na + kk);
+            const float4 b = *reinterpret_cast<const float4*>(nb + kk);
+            const float4 u = *reinterpret_cast<const float4*>(wa + kk);
+            const float4 v = *reinterpret_cast<const float4*>(wb + kk);
+            acc0 = ffma2(make_float2(a.x, a.x), make_float2(u.x, v.x), acc0);
+            acc1 = ffma2(make_float2(b.x, b.x), make_float2(u.x, v.x), acc1);
+            acc0 = ffma2(make_float2(a.y, a.y), make_float2(u.y, v.y), acc0);
+            acc1 = ffma2(make_float2(b.y, b.y), make_float2(u.y, v.y), acc1);
+            acc0 = ffma2(make_float2(a.z, a.z), make_float2(u.z, v.z), acc0);
+            acc1 = ffma2(make_float2(b.z, b.z), make_float2(u.z, v.z), acc1);
+            acc0 = ffma2(make_float2(a.w, a.w), make_float2(u.w, v.w), acc0);
+            acc1 = ffma2(make_float2(b.w, b.w), make_float2(u.w, v.w), acc1);
+        }
+        __syncthreads();
+    }
+    const int ta = t0 + tp, ea = e0 + ep;
+    const float ba = (bias && ea < E) ? bias[ea] : 0.0f;
+    const float bb = (bias && ea + 16 < E) ? bias[ea + 16] : 0.0f;
+    auto put = [&](int t, int e, float v, float b) {
+        if (t < T && e < E) logits[static_cast<size_t>(t) * E + e] = bias ? __fadd_rn(v, b) : v;
+    };
+    put(ta, ea, acc0.x, ba);
+    put(ta, ea + 16, acc0.y, bb);
+    put(ta + 8, ea, acc1.x, ba);
+    put(ta + 8, ea + 16, acc1.y, bb);
+}
+
+// Top-k + softmax of the selected logits, one warp per token (8 tokens per
+// 256-thread block), with the reference's selection rule (see topk_row).
+template <int EPT>
+__global__ void __launch_bounds__(256)
+topk_softmax_kernel(const float* __restrict__ logits, int T, int E, int K, int32_t* __restrict__ topk_idx,
+                    float* __restrict__ topk_w) {
+    const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (t >= T) return;
+    topk_row<EPT>(logits + static_cast<size_t>(t) * E, E, K, threadIdx.x & 31, topk_idx + static_cast<size_t>(t) * K,
+                  topk_w + static_cast<size_t>(t) * K);
 }
 
 // ---------------------------------------------------------------- permutation
@@ -409,17 +524,65 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 extern "C" {
 
-moe_status_t moe_rmsnorm_quant(const void* x_bf16, const float* gamma, int T, int H, float eps,
-                               float* rms_out, void* xq_out, float* xs_out, int xs_ld,
-                               cwStream_t stream) {
+moe_status_t moe_rmsnorm_quant_n(const void* x_bf16, const float* gamma, int T, int H, float eps,
+                                 float* rms_out, float* n_out, void* xq_out, float* xs_out, int xs_ld,
+                                 cwStream_t stream) {
     if (T < 0 || H <= 0 || H % 128 || xs_ld < T) return MOE_ERR_INVALID_ARGUMENT;
     if (T == 0) return MOE_OK;
     if (!x_bf16 || !gamma || !xq_out || !xs_out) return MOE_ERR_INVALID_ARGUMENT;
     if (!aligned16(x_bf16) || !aligned16(gamma) || !aligned16(xq_out)) return MOE_ERR_INVALID_ARGUMENT;
     const int blocks = (T + 7) / 8;
+    if (n_out && !aligned16(n_out)) return MOE_ERR_INVALID_ARGUMENT;
     rmsnorm_quant_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const __nv_bfloat16*>(x_bf16), gamma, T, H, eps, rms_out,
+        static_cast<const __nv_bfloat16*>(x_bf16), gamma, T, H, eps, rms_out, n_out,
         static_cast<uint8_t*>(xq_out), xs_out, xs_ld);
+    return launch_status();
+}
+
+moe_status_t moe_rmsnorm_quant(const void* x_bf16, const float* gamma, int T, int H, float eps,
+                               float* rms_out, void* xq_out, float* xs_out, int xs_ld,
+                               cwStream_t stream) {
+    return moe_rmsnorm_quant_n(x_bf16, gamma, T, H, eps, rms_out, nullptr, xq_out, xs_out, xs_ld, stream);
+}
+
+moe_status_t moe_router_logits(const float* n, const float* router_w, const float* router_bias, int T, int H,
+                               int E, float* logits, cwStream_t stream) {
+    if (T < 0 || H <= 0 || H % kRtKC || E <= 0 || E > 256) return MOE_ERR_INVALID_ARGUMENT;
+    if (T == 0) return MOE_OK;
+    if (!n || !router_w || !logits || !aligned16(n) || !aligned16(router_w)) return MOE_ERR_INVALID_ARGUMENT;
+    const dim3 grid((E + kRtExp - 1) / kRtExp, (T + kRtTok - 1) / kRtTok);
+    if (grid.y > 65535) return MOE_ERR_UNSUPPORTED;
+    static bool attr = false;
+    if (!attr) {
+        if (cudaFuncSetAttribute(router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(kRtSmem)) != cudaSuccess)
+            return MOE_ERR_CUDA;
+        attr = true;
+    }
+    router_logits_kernel<<<grid, kRtThreads, kRtSmem, static_cast<cudaStream_t>(stream)>>>(n, router_w, router_bias,
+                                                                                           T, H, E, logits);
+    return launch_status();
+}
+
+moe_status_t moe_topk_softmax(const float* logits, int T, int E, int k, int32_t* topk_idx, float* topk_w,
+                              cwStream_t stream) {
+    if (T < 0 || E <= 0 || E > 256 || k <= 0 || k > 16 || k > E) return MOE_ERR_INVALID_ARGUMENT;
+    if (T == 0) return MOE_OK;
+    if (!logits || !topk_idx || !topk_w) return MOE_ERR_INVALID_ARGUMENT;
+    const int blocks = (T + 7) / 8;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+#define TB_TOPK(EPTV) topk_softmax_kernel<EPTV><<<blocks, 256, 0, s>>>(logits, T, E, k, topk_idx, topk_w)
+    switch ((E + 31) / 32) {
+        case 1: TB_TOPK(1); break;
+        case 2: TB_TOPK(2); break;
+        case 3: TB_TOPK(3); break;
+        case 4: TB_TOPK(4); break;
+        case 5: TB_TOPK(5); break;
+        case 6: TB_TOPK(6); break;
+        case 7: TB_TOPK(7); break;
+        default: TB_TOPK(8); break;
+    }
+#undef TB_TOPK
     return launch_status();
 }
 
