@@ -24,9 +24,7 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
 import time
 from pathlib import Path
 
@@ -63,56 +61,60 @@ def load_peaks():
 # ---------------------------------------------------------------- clocks
 
 class ClockSampler:
-    """nvidia-smi sampling during the timed region (SM clock, max, reasons)."""
+    """SM clock, max clock, power and throttle reasons sampled DURING the timed
+    region by an NVML thread every 5 ms (the timed region can be shorter than
+    nvidia-smi's loop period); no samples (clocks: null) without NVML."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event reason bits (nvml.h nvmlClocksEventReason*)
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown", 0x4: "sw_power_cap",
+               0x80: "hw_power_brake_slowdown", 0x1: "gpu_idle", 0x2: "applications_clocks_setting"}
 
     def __init__(self, index: int):
         self.index = index
-        self.proc = None
-        self.path = None
+        self.rows = []
+        self._stop = None
+        self._thread = None
 
     def __enter__(self):
-        fd, self.path = tempfile.mkstemp(suffix=".csv")
-        os.close(fd)
+        import threading
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            import pynvml
+            pynvml.nvmlInit()
+            handle = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self._max = pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM)
         except Exception:
-            self.proc = None
-        time.sleep(0.3)
+            self._thread = None
+            return self
+        self._stop = threading.Event()
+
+        def loop():
+            while not self._stop.is_set():
+                try:
+                    sm = pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM)
+                    pw = pynvml.nvmlDeviceGetPowerUsage(handle) / 1000.0
+                    rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(handle)
+                    self.rows.append((float(sm), float(self._max), pw, int(rs)))
+                except Exception:
+                    pass
+                self._stop.wait(0.005)
+
+        self._thread = threading.Thread(target=loop, daemon=True)
+        self._thread.start()
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=2)
 
     def summary(self):
-        if not self.path or not os.path.exists(self.path):
+        if not self.rows:
             return None
-        rows = []
-        for line in open(self.path):
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
-            except ValueError:
-                continue
-        os.unlink(self.path)
-        if not rows:
-            return None
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[3]) if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
-                "power_w_max": max(r[2] for r in rows), "samples": len(rows), "reasons": reasons}
+        reasons = sorted({name for r in self.rows for bit, name in self.REASONS.items()
+                          if r[3] & bit and name not in ("gpu_idle", "applications_clocks_setting")})
+        return {"sm_mhz": statistics.median(r[0] for r in self.rows), "sm_max_mhz": max(r[1] for r in self.rows),
+                "power_w_max": max(r[2] for r in self.rows), "samples": len(self.rows), "reasons": reasons,
+                "source": "nvml, 5 ms"}
 
 
 # ---------------------------------------------------------------- CPU baseline
