@@ -15,16 +15,20 @@
 //     to N_MAX tokens of one expert, so ragged expert groups pad only to 16
 //     tokens.  Tiles of one (expert, weight-row block) are adjacent in the
 //     list, so concurrently running CTAs share each weight tile through L2.
-//   * warp 0: TMA producer (weights box 128x128 B, tokens in 32-row boxes,
-//     token scales by bulk copy) into a STAGES-deep shared-memory ring.
+//   * warp 0: TMA producer (weights box 128x128 B, tokens in 32-row boxes)
+//     into a 3-deep operand ring that the MMA commit alone releases, and the
+//     K block's token scales (bulk copy) into a separate 8-deep scale ring that
+//     the promotion warps release -- so operand loads never wait for promotion.
 //   * warp 1: allocates TMEM (512 columns) and issues tcgen05.mma kind::f8f6f4
 //     (4 x K=32 per 128-wide K block) into one of two TMEM partial buffers;
 //     a fresh partial per K block, since the fp32 block scales differ per K
 //     block and tcgen05's own block scaling only takes power-of-two scales.
-//   * warp 2: folds the K block's weight scale into the token scales
+//   * warp 2: folds the K block's weight scale into the token scales in place
 //     (c[n] = a_scale[n] * w_scale) once per CTA per K block.
-//   * warps 3..18: "promotion": tcgen05.ld the partial, acc += partial * c
-//     with packed fp32x2 FMAs in registers, release the TMEM buffer; at the
+//   * warps 4..19 (warpgroups 1-4, 112 registers each after setmaxnreg; the
+//     role warpgroup drops to 32): "promotion": tcgen05.ld the partial (16
+//     columns per load, four per K block), acc += partial * c with packed fp32x2 FMAs in
+//     registers, release the TMEM buffer and the scale entry; at the
 //     end of a tile run the fused epilogue (SwiGLU + requant, or bf16) through
 //     a transposing shared-memory stage so global stores are row-contiguous.
 //   * Every mbarrier wait is bounded (~2 s); on timeout the CTA raises an
@@ -48,9 +52,16 @@ using namespace tb;
 
 constexpr int kBlockK = 128;            // K bytes (e4m3 elements) per stage
 constexpr int kTileM = 128;             // weight rows per UMMA (TMEM lanes)
-constexpr int kFirstPromoWarp = 3;
-constexpr int kNumPromoWarps = 16;
-constexpr int kNumThreads = (kFirstPromoWarp + kNumPromoWarps) * 32;   // 608
+constexpr int kFirstPromoWarp = 4;      // warpgroup 0: TMA, MMA, scale folding, idle
+constexpr int kNumPromoWarps = 16;      // warpgroups 1..4
+constexpr int kNumThreads = (kFirstPromoWarp + kNumPromoWarps) * 32;   // 640
+// Register split (setmaxnreg): launched at 96 per thread (640 x 96 = 61440),
+// warpgroup 0 gives back to 32, the four promotion warpgroups take 112:
+// 128 x 32 + 512 x 112 = 61440, and per SM sub-partition 1 x 32 x 32 +
+// 4 x 32 x 112 = 15360 <= 16384.
+constexpr int kRoleRegs = 32;
+constexpr int kPromoRegs = 112;
+static_assert(128 * kRoleRegs + 512 * kPromoRegs <= kNumThreads * 96, "register split exceeds the launch");
 constexpr int kMaxGroups = 512;
 constexpr int kTmemCols = 512;
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
@@ -59,25 +70,30 @@ constexpr uint64_t kDrainTimeoutNs = 200000000ull;
 template <bool kGated>
 struct GemmCfg {
     static constexpr int kNMax = kGated ? 128 : 256;       // tokens per tile
-    static constexpr int kStages = 3;
+    static constexpr int kStages = 3;                       // operand ring
+    static constexpr int kSStages = 8;                      // token-scale ring
     static constexpr int kATiles = kGated ? 2 : 1;          // gate + up
     static constexpr int kABytes = kATiles * kTileM * kBlockK;
     static constexpr int kBBytes = kNMax * kBlockK;
     static constexpr int kStageBytes = kABytes + kBBytes;   // 48 KB either way
     static constexpr int kNumCombined = kGated ? 2 : 1;
+    static constexpr int kScaleFloats = kNumCombined * kNMax;   // one scale-ring entry
+    static constexpr int kRawSlot = kNumCombined - 1;       // where the bulk copy lands in an entry
     static constexpr int kBufCols = 256;                    // TMEM columns per partial buffer
     static constexpr int kColsPerWarp = kNMax / 4;          // 32 (gated) / 64 (down)
     static constexpr int kOutStageBytes = kGated ? kNMax * 128 * 4 : kNMax * 128 * 2;
     // shared-memory carve-up (offsets from the 1024-aligned base)
     static constexpr int kOffStages = 0;
     static constexpr int kOffOut = kOffStages + kStages * kStageBytes;
-    static constexpr int kOffRawScale = kOffOut + kOutStageBytes;
-    static constexpr int kOffCombScale = kOffRawScale + kStages * kNMax * 4;
-    static constexpr int kOffTables = kOffCombScale + kStages * kNumCombined * kNMax * 4;
+    static constexpr int kOffScale = kOffOut + kOutStageBytes;
+    static constexpr int kOffTables = kOffScale + kSStages * kScaleFloats * 4;
     static constexpr int kOffBars = kOffTables + (4 * kMaxGroups + 2) * 4;   // prefix, chunks, start, count
-    static constexpr int kNumBars = 3 * kStages + 4;
+    // full/empty per operand stage; sfull/sempty/cready per scale entry;
+    // tfull/tempty per TMEM buffer; one epilogue group barrier
+    static constexpr int kNumBars = 2 * kStages + 3 * kSStages + 4 + 1;
     static constexpr int kOffMisc = kOffBars + kNumBars * 8;
     static constexpr int kSmemBytes = kOffMisc + 64 + 1024;  // + alignment slack
+    static_assert(kOffBars % 8 == 0, "mbarrier alignment");
     static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
@@ -139,8 +155,7 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
 
-    float* raw_scale = reinterpret_cast<float*>(smem + C::kOffRawScale);
-    float* comb_scale = reinterpret_cast<float*>(smem + C::kOffCombScale);
+    float* scale_ring = reinterpret_cast<float*>(smem + C::kOffScale);
     int* t_prefix = reinterpret_cast<int*>(smem + C::kOffTables);           // [G+1]
     int* t_chunks = t_prefix + (kMaxGroups + 1);                            // [G]
     int* t_start = t_chunks + kMaxGroups;                                   // [G]
@@ -148,9 +163,12 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBars);
     uint64_t* full_bar = bars;
     uint64_t* empty_bar = bars + C::kStages;
-    uint64_t* cready_bar = bars + 2 * C::kStages;
-    uint64_t* tfull_bar = bars + 3 * C::kStages;
+    uint64_t* sfull_bar = bars + 2 * C::kStages;
+    uint64_t* sempty_bar = sfull_bar + C::kSStages;
+    uint64_t* cready_bar = sempty_bar + C::kSStages;
+    uint64_t* tfull_bar = cready_bar + C::kSStages;
     uint64_t* tempty_bar = tfull_bar + 2;
+    uint64_t* epi_bar = tempty_bar + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffMisc);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kOffMisc + 8);
 
@@ -163,13 +181,18 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
     if (warp == 0 && lane == 0) {
         for (int s = 0; s < C::kStages; ++s) {
             mbar_init(&full_bar[s], 1);
-            mbar_init(&empty_bar[s], 1 + kNumPromoWarps);
+            mbar_init(&empty_bar[s], 1);
+        }
+        for (int s = 0; s < C::kSStages; ++s) {
+            mbar_init(&sfull_bar[s], 1);
+            mbar_init(&sempty_bar[s], kNumPromoWarps);
             mbar_init(&cready_bar[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tfull_bar[b], 1);
             mbar_init(&tempty_bar[b], kNumPromoWarps);
         }
+        mbar_init(epi_bar, kNumPromoWarps);
         *abort_flag = 0;
         fence_mbar_init();
         prefetch_tmap(&tmap_w);
@@ -214,17 +237,20 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
     const uint32_t tmem_base = *tmem_slot;
     const int total_tiles = t_prefix[G];
 
-    if (warp == 0) {
+    if (warp < kFirstPromoWarp) {
+      asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" :: "n"(kRoleRegs));
+      if (warp == 0) {
         // ------------------------------------------------------------ TMA producer
         if (lane == 0) {
-            int s = 0;
-            uint32_t phase = 0;
-            uint32_t armed_mask = 0, armed_phase = 0;   // per stage: last arm and its phase
+            int s = 0, ss = 0;
+            uint32_t phase = 0, sphase = 0;
+            uint32_t armed_mask = 0, armed_phase = 0;     // operand ring: last arm per stage and its phase
+            uint32_t sarmed_mask = 0, sarmed_phase = 0;   // scale ring
             bool ok = true;
             for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
                 TileCoord tc = decode_tile(tile, t_prefix, t_chunks, t_start, counts_smem, G, C::kNMax);
                 const int b_loads = (tc.ntile + 31) >> 5;
-                const uint32_t bytes = C::kABytes + b_loads * 32 * kBlockK + tc.ntile * 4;
+                const uint32_t bytes = C::kABytes + b_loads * 32 * kBlockK;
                 const int wrow = tc.g * p.w_rows + tc.nb * kTileM;
                 for (int kb = 0; kb < KB; ++kb) {
                     if (!mbar_wait_bounded(&empty_bar[s], phase ^ 1, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
@@ -234,20 +260,28 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
                     if (kGated) tma_load_2d(&tmap_w, &full_bar[s], st + kTileM * kBlockK, kb * kBlockK, wrow + p.N);
                     for (int r = 0; r < b_loads; ++r)
                         tma_load_2d(&tmap_a, &full_bar[s], st + C::kABytes + r * 32 * kBlockK, kb * kBlockK, tc.row0 + 32 * r);
-                    bulk_load(raw_scale + s * C::kNMax, p.a_scale + (size_t)kb * p.a_ld + tc.row0,
-                              tc.ntile * 4, &full_bar[s]);
                     armed_mask |= 1u << s;
                     armed_phase = (armed_phase & ~(1u << s)) | (phase << s);
                     if (++s == C::kStages) { s = 0; phase ^= 1; }
+
+                    if (!mbar_wait_bounded(&sempty_bar[ss], sphase ^ 1, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&sfull_bar[ss], tc.ntile * 4);
+                    bulk_load(scale_ring + ss * C::kScaleFloats + C::kRawSlot * C::kNMax,
+                              p.a_scale + (size_t)kb * p.a_ld + tc.row0, tc.ntile * 4, &sfull_bar[ss]);
+                    sarmed_mask |= 1u << ss;
+                    sarmed_phase = (sarmed_phase & ~(1u << ss)) | (sphase << ss);
+                    if (++ss == C::kSStages) { ss = 0; sphase ^= 1; }
                 }
             }
             if (!ok) {
                 // let every copy this thread issued land before the CTA can exit
-                for (int ss = 0; ss < C::kStages; ++ss)
-                    if (armed_mask & (1u << ss)) mbar_drain(&full_bar[ss], (armed_phase >> ss) & 1u);
+                for (int i = 0; i < C::kStages; ++i)
+                    if (armed_mask & (1u << i)) mbar_drain(&full_bar[i], (armed_phase >> i) & 1u);
+                for (int i = 0; i < C::kSStages; ++i)
+                    if (sarmed_mask & (1u << i)) mbar_drain(&sfull_bar[i], (sarmed_phase >> i) & 1u);
             }
         }
-    } else if (warp == 1) {
+      } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
             int s = 0, b = 0;
@@ -287,10 +321,10 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
                 mbar_drain(&tfull_bar[lb], lph);
             }
         }
-    } else if (warp == 2) {
+      } else if (warp == 2) {
         // ------------------------------------------------------------ scale folding
-        int s = 0;
-        uint32_t phase = 0;
+        int ss = 0;
+        uint32_t sphase = 0;
         bool ok = true;
         const int wsb = p.w_rows / kTileM;
         for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
@@ -300,20 +334,23 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
             for (int kb = 0; kb < KB; ++kb) {
                 const float sg = __ldg(wsg + kb);
                 const float su = kGated ? __ldg(wsu + kb) : 0.0f;
-                if (!mbar_wait_bounded(&full_bar[s], phase, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
-                const float* rs = raw_scale + s * C::kNMax;
-                float* cs = comb_scale + s * C::kNumCombined * C::kNMax;
+                if (!mbar_wait_bounded(&sfull_bar[ss], sphase, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
+                float* e = scale_ring + ss * C::kScaleFloats;
                 for (int c = lane; c < tc.ntile; c += 32) {
-                    const float a = rs[c];
-                    cs[c] = a * sg;
-                    if (kGated) cs[C::kNMax + c] = a * su;
+                    const float a = e[C::kRawSlot * C::kNMax + c];
+                    e[c] = a * sg;
+                    if (kGated) e[C::kNMax + c] = a * su;
                 }
+                // the entry is overwritten by the async proxy (bulk copy) next
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&cready_bar[s]);
-                if (++s == C::kStages) { s = 0; phase ^= 1; }
+                if (lane == 0) mbar_arrive(&cready_bar[ss]);
+                if (++ss == C::kSStages) { ss = 0; sphase ^= 1; }
             }
         }
+      }
     } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" :: "n"(kPromoRegs));
         // ------------------------------------------------------------ promotion + epilogue
         const int pw = warp - kFirstPromoWarp;        // 0..15
         const int quarter = warp & 3;                  // TMEM lane quarter this warp may access
@@ -321,50 +358,57 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
         const int col0 = colgrp * C::kColsPerWarp;
         const int row_in_tile = quarter * 32 + lane;   // weight row within the 128-row block
         const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
-        int s = 0, b = 0;
-        uint32_t phase = 0, tphase = 0;
+        int ss = 0, b = 0;
+        uint32_t sphase = 0, tphase = 0, ephase = 0;
         bool ok = true;
 
-        constexpr int kChunk = 8;                                // columns per TMEM load
-        constexpr int kChunks = C::kColsPerWarp / kChunk;        // 4 (gated) / 8 (down)
-        constexpr int kAcc = C::kColsPerWarp * C::kNumCombined;  // 64 either way
+        // 32-column pieces per K block: gated = gate cols [col0, +32) and the
+        // matching up cols (TMEM +128); down = cols [col0, +32) and [col0+32, +32).
+        constexpr int kPieces = 2;
+        constexpr int kAcc2 = C::kColsPerWarp * C::kNumCombined / 2;   // 32 float2 either way
+        // bounded group barrier of the 16 promotion warps (epilogue staging)
+        auto group_sync = [&]() -> bool {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(epi_bar);
+            const bool r = mbar_wait_bounded(epi_bar, ephase, abort_flag, kWaitTimeoutNs);
+            ephase ^= 1;
+            return r;
+        };
 
         for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
             TileCoord tc = decode_tile(tile, t_prefix, t_chunks, t_start, counts_smem, G, C::kNMax);
-            const int active_chunks = max(0, min(kChunks, (tc.ntile - col0 + kChunk - 1) / kChunk));
-            float acc[kAcc];
+            bool live[kPieces];
 #pragma unroll
-            for (int i = 0; i < kAcc; ++i) acc[i] = 0.0f;
+            for (int q = 0; q < kPieces; ++q) live[q] = (kGated ? col0 : col0 + 32 * q) < tc.ntile;
+            float2 acc2[kAcc2];
+#pragma unroll
+            for (int i = 0; i < kAcc2; ++i) acc2[i] = make_float2(0.0f, 0.0f);
 
             for (int kb = 0; kb < KB; ++kb) {
-                if (!mbar_wait_bounded(&cready_bar[s], phase, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
+                if (!mbar_wait_bounded(&cready_bar[ss], sphase, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
                 if (!mbar_wait_bounded(&tfull_bar[b], tphase, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
                 tc_fence_after();
-                const float* cs = comb_scale + s * C::kNumCombined * C::kNMax + col0;
-                const uint32_t tbuf = lane_addr + b * C::kBufCols + col0;
+                const float* e = scale_ring + ss * C::kScaleFloats;
+                const uint32_t tbuf = lane_addr + b * C::kBufCols;
 #pragma unroll
-                for (int ch = 0; ch < kChunks; ++ch) {
-                    if (ch < active_chunks) {
+                for (int q = 0; q < kPieces; ++q) {
+                    if (!live[q]) continue;
+                    const int tcol = kGated ? (q * 128 + col0) : (col0 + 32 * q);
+                    const float* cs = kGated ? (e + q * C::kNMax + col0) : (e + col0 + 32 * q);
 #pragma unroll
-                        for (int half = 0; half < C::kNumCombined; ++half) {
-                            uint32_t pv[8];
-                            asm volatile(
-                                "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                                : "=r"(pv[0]), "=r"(pv[1]), "=r"(pv[2]), "=r"(pv[3]), "=r"(pv[4]),
-                                  "=r"(pv[5]), "=r"(pv[6]), "=r"(pv[7])
-                                : "r"(tbuf + half * 128 + ch * kChunk));
-                            tmem_wait_ld();
-                            const float* cc = cs + half * C::kNMax + ch * kChunk;
-                            float* a = acc + half * C::kColsPerWarp + ch * kChunk;
+                    for (int h = 0; h < 2; ++h) {
+                        uint32_t pv[16];
+                        tmem_ld16(tbuf + tcol + 16 * h, pv);
+                        tmem_wait_ld();
 #pragma unroll
-                            for (int j = 0; j < kChunk; j += 4) {
-                                const float4 c4 = *reinterpret_cast<const float4*>(cc + j);
-                                float2 lo = ffma2(make_float2(__uint_as_float(pv[j]), __uint_as_float(pv[j + 1])),
-                                                  make_float2(c4.x, c4.y), make_float2(a[j], a[j + 1]));
-                                float2 hi = ffma2(make_float2(__uint_as_float(pv[j + 2]), __uint_as_float(pv[j + 3])),
-                                                  make_float2(c4.z, c4.w), make_float2(a[j + 2], a[j + 3]));
-                                a[j] = lo.x; a[j + 1] = lo.y; a[j + 2] = hi.x; a[j + 3] = hi.y;
-                            }
+                        for (int j = 0; j < 16; j += 4) {
+                            const float4 c4 = *reinterpret_cast<const float4*>(cs + 16 * h + j);
+                            float2& a0 = acc2[q * 16 + 8 * h + j / 2];
+                            float2& a1 = acc2[q * 16 + 8 * h + j / 2 + 1];
+                            a0 = ffma2(make_float2(__uint_as_float(pv[j]), __uint_as_float(pv[j + 1])),
+                                       make_float2(c4.x, c4.y), a0);
+                            a1 = ffma2(make_float2(__uint_as_float(pv[j + 2]), __uint_as_float(pv[j + 3])),
+                                       make_float2(c4.z, c4.w), a1);
                         }
                     }
                 }
@@ -372,25 +416,28 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
                 __syncwarp();
                 if (lane == 0) {
                     mbar_arrive(&tempty_bar[b]);
-                    mbar_arrive(&empty_bar[s]);
+                    mbar_arrive(&sempty_bar[ss]);
                 }
-                if (++s == C::kStages) { s = 0; phase ^= 1; }
+                if (++ss == C::kSStages) { ss = 0; sphase ^= 1; }
                 b ^= 1;
                 if (b == 0) tphase ^= 1;
             }
             if (!ok || *abort_flag) { ok = false; break; }
 
             // ---------------------------------------------------------- epilogue
+            // acc2[i] holds columns 2i, 2i+1 of this warp's 64 accumulators:
+            // gated: [0, 32) gate cols col0.., [32, 64) the matching up cols;
+            // down: cols col0 .. col0+63.
             if (kGated) {
                 float* stage = reinterpret_cast<float*>(smem + C::kOffOut);   // [N_MAX][128] fp32
 #pragma unroll
                 for (int c = 0; c < C::kColsPerWarp; ++c) {
-                    const float g = acc[c];
-                    const float u = acc[C::kColsPerWarp + c];
+                    const float g = (c & 1) ? acc2[c >> 1].y : acc2[c >> 1].x;
+                    const float u = (c & 1) ? acc2[16 + (c >> 1)].y : acc2[16 + (c >> 1)].x;
                     const float h = (g / (1.0f + expf(-g))) * u;
                     stage[(col0 + c) * 128 + row_in_tile] = h;
                 }
-                named_bar_sync(1, kNumPromoWarps * 32);
+                if (!group_sync()) { ok = false; break; }
                 uint8_t* outq = reinterpret_cast<uint8_t*>(p.out);
                 for (int c = pw; c < tc.ntile; c += kNumPromoWarps) {
                     const size_t row = static_cast<size_t>(tc.row0 + c);
@@ -412,19 +459,21 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
                     *reinterpret_cast<uint32_t*>(outq + row * p.N + tc.nb * 128 + lane * 4) = packed;
                     if (lane == 0) p.out_scale[(size_t)tc.nb * p.out_ld + row] = scale;
                 }
-                named_bar_sync(1, kNumPromoWarps * 32);
+                if (!group_sync()) { ok = false; break; }
             } else {
                 __nv_bfloat16* stage = reinterpret_cast<__nv_bfloat16*>(smem + C::kOffOut);  // [N_MAX][128]
 #pragma unroll
-                for (int c = 0; c < C::kColsPerWarp; ++c)
-                    stage[(col0 + c) * 128 + row_in_tile] = __float2bfloat16_rn(acc[c]);
-                named_bar_sync(1, kNumPromoWarps * 32);
+                for (int c = 0; c < C::kColsPerWarp; ++c) {
+                    const float v = (c & 1) ? acc2[c >> 1].y : acc2[c >> 1].x;
+                    stage[(col0 + c) * 128 + row_in_tile] = __float2bfloat16_rn(v);
+                }
+                if (!group_sync()) { ok = false; break; }
                 __nv_bfloat16* outy = reinterpret_cast<__nv_bfloat16*>(p.out);
                 for (int c = pw; c < tc.nrows; c += kNumPromoWarps) {
                     const uint2 v = *reinterpret_cast<const uint2*>(stage + c * 128 + lane * 4);
                     *reinterpret_cast<uint2*>(outy + static_cast<size_t>(tc.row0 + c) * p.N + tc.nb * 128 + lane * 4) = v;
                 }
-                named_bar_sync(1, kNumPromoWarps * 32);
+                if (!group_sync()) { ok = false; break; }
             }
         }
     }
