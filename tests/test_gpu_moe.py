@@ -225,9 +225,9 @@ def _gemm_ref(A, A_s, W, W_s, starts, counts, K):
     return out
 
 
-@pytest.mark.parametrize("counts", [[16], [1, 0, 130, 255, 300], [128, 129, 17, 0, 0, 1000]])
-def test_grouped_gemm_down(gpu, counts):
-    K, N = 384, 256
+@pytest.mark.parametrize("counts,K,N", [([16], 384, 256), ([1, 0, 130, 255, 300], 384, 256),
+                                        ([128, 129, 17, 0, 0, 1000], 384, 256), ([40, 257], 1536, 512)])
+def test_grouped_gemm_down(gpu, counts, K, N):
     g = torch.Generator().manual_seed(sum(counts))
     starts, rows, A, A_s, a_ld, W, W_s = _make_groups(counts, K, N, g)
     out = torch.full((rows, N), float("nan"), dtype=torch.bfloat16, device=gpu)
@@ -247,9 +247,10 @@ def test_grouped_gemm_down(gpu, counts):
         assert rel < 8e-3, (gi, float(rel))
 
 
-@pytest.mark.parametrize("counts", [[16], [3, 0, 128, 129, 260], [1000, 1]])
-def test_grouped_gemm_gated_swiglu(gpu, oracle, counts):
-    K, N = 256, 256            # weights hold 2N rows: gate [0,N), up [N,2N)
+@pytest.mark.parametrize("counts,K,N", [([16], 256, 256), ([3, 0, 128, 129, 260], 256, 256), ([1000, 1], 256, 256),
+                                        ([70, 300], 640, 384)])
+def test_grouped_gemm_gated_swiglu(gpu, oracle, counts, K, N):
+    # weights hold 2N rows: gate [0,N), up [N,2N)
     g = torch.Generator().manual_seed(7 + sum(counts))
     starts, rows, A, A_s, a_ld, W, W_s = _make_groups(counts, K, 2 * N, g)
     hq = torch.full((rows, N), 0x55, dtype=torch.uint8, device=gpu)
