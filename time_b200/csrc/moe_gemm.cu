@@ -390,26 +390,53 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
                 tc_fence_after();
                 const float* e = scale_ring + ss * C::kScaleFloats;
                 const uint32_t tbuf = lane_addr + b * C::kBufCols;
-#pragma unroll
-                for (int q = 0; q < kPieces; ++q) {
-                    if (!live[q]) continue;
+                // four 16-column chunks c = (piece q, half h); the TMEM load of
+                // chunk c+1 is in flight while chunk c is folded
+                auto ld_chunk = [&](int c, uint32_t (&pv)[16]) {
+                    const int q = c >> 1, h = c & 1;
                     const int tcol = kGated ? (q * 128 + col0) : (col0 + 32 * q);
-                    const float* cs = kGated ? (e + q * C::kNMax + col0) : (e + col0 + 32 * q);
+                    tmem_ld16(tbuf + tcol + 16 * h, pv);
+                };
+                auto fold_chunk = [&](int c, const uint32_t (&pv)[16]) {
+                    const int q = c >> 1, h = c & 1;
+                    const float* cs = (kGated ? (e + q * C::kNMax + col0) : (e + col0 + 32 * q)) + 16 * h;
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
+                    for (int j = 0; j < 16; j += 4) {
+                        const float4 c4 = *reinterpret_cast<const float4*>(cs + j);
+                        float2& a0 = acc2[q * 16 + 8 * h + j / 2];
+                        float2& a1 = acc2[q * 16 + 8 * h + j / 2 + 1];
+                        a0 = ffma2(make_float2(__uint_as_float(pv[j]), __uint_as_float(pv[j + 1])),
+                                   make_float2(c4.x, c4.y), a0);
+                        a1 = ffma2(make_float2(__uint_as_float(pv[j + 2]), __uint_as_float(pv[j + 3])),
+                                   make_float2(c4.z, c4.w), a1);
+                    }
+                };
+                const int nch = live[1] ? 4 : (live[0] ? 2 : 0);
+                if (!kGated) {
+                    // down: one 16-register set (two sets spill next to its 64 accumulators)
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        if (c >= nch) break;
                         uint32_t pv[16];
-                        tmem_ld16(tbuf + tcol + 16 * h, pv);
+                        ld_chunk(c, pv);
                         tmem_wait_ld();
-#pragma unroll
-                        for (int j = 0; j < 16; j += 4) {
-                            const float4 c4 = *reinterpret_cast<const float4*>(cs + 16 * h + j);
-                            float2& a0 = acc2[q * 16 + 8 * h + j / 2];
-                            float2& a1 = acc2[q * 16 + 8 * h + j / 2 + 1];
-                            a0 = ffma2(make_float2(__uint_as_float(pv[j]), __uint_as_float(pv[j + 1])),
-                                       make_float2(c4.x, c4.y), a0);
-                            a1 = ffma2(make_float2(__uint_as_float(pv[j + 2]), __uint_as_float(pv[j + 3])),
-                                       make_float2(c4.z, c4.w), a1);
-                        }
+                        fold_chunk(c, pv);
+                    }
+                } else if (nch) {
+                    uint32_t pa[16], pb[16];
+                    ld_chunk(0, pa);
+                    tmem_wait_ld();
+                    ld_chunk(1, pb);
+                    fold_chunk(0, pa);
+                    tmem_wait_ld();
+                    if (nch > 2) ld_chunk(2, pa);
+                    fold_chunk(1, pb);
+                    if (nch > 2) {
+                        tmem_wait_ld();
+                        ld_chunk(3, pb);
+                        fold_chunk(2, pa);
+                        tmem_wait_ld();
+                        fold_chunk(3, pb);
                     }
                 }
                 tc_fence_before();
