@@ -45,6 +45,8 @@ def parse():
     ap.add_argument("--tokens", type=int, default=TOKENS)
     ap.add_argument("--experts", type=int, default=160,
                     help="routed experts (profiling captures of a smaller case only; the metric uses 160)")
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                    help="expert-parallel exchange for N > 1: NVLink peer memory (own kernels) or NCCL send/recv")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -266,6 +268,8 @@ def run_ours(args):
     max_tokens = -(-T // world)
     out = torch.empty_like(x)
     layer = M.MoELayer(shape, w, max_tokens=max_tokens, ep_size=world, ep_rank=rank, comm=comm)
+    if world > 1 and args.exchange == "peer":
+        layer.use_peer_memory()
     stream = torch.cuda.current_stream()
 
     def barrier():
@@ -377,7 +381,10 @@ def run_ours(args):
         wc = {k_: (v.cpu() if isinstance(v, torch.Tensor) else v) for k_, v in w.items()}
         cpu, _, _ = cpu_baseline(shape, wc, x.cpu(), args.cpu_seconds)
 
-    launches_per_step = M.NUM_STAGES if world == 1 else 10
+    # our kernels per forward: rmsnorm, router logits, top-k, permute, gather, 2 GEMMs, combine; EP adds
+    # (NCCL) row pack, receive plan, output pack or (peer memory) counts, dispatch, 2 signal/waits,
+    # receive plan, output send
+    launches_per_step = 8 if world == 1 else (11 if args.exchange == "nccl" else 13)
     line = {"metric": METRIC, "value": T * 1000.0 / ms_per_step, "unit": UNIT, "n_gpus": world,
             "steps": K, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "e4m3 x e4m3 -> f32 (bf16 in/out)",
@@ -387,7 +394,10 @@ def run_ours(args):
                        "hidden": shape.hidden, "experts": shape.num_experts, "top_k": shape.top_k,
                        "intermediate": shape.intermediate, "shared_experts": shape.num_shared,
                        "router": "fp32 softmax top-k, zipf(1.1) bias", "parallelism": f"ep{world}",
-                       "dispatch": "fp8 rows + 1x128 scales, combine bf16 (NCCL send/recv)" if world > 1 else None,
+                       "dispatch": (("fp8 rows + 1x128 scales, combine bf16, " +
+                                     ("NVLink peer-memory stores from own kernels, no host sync"
+                                      if args.exchange == "peer" else "NCCL send/recv, one host sync"))
+                                    if world > 1 else None),
                        "l2": "inputs larger than L2: %.1f GB of expert weights streamed per step per rank"
                              % (sum(v.numel() for k_, v in w.items() if k_ in ("w13", "w2")) / 1e9)},
             "e2e": {"value": T * 1000.0 / e2e_ms, "unit": UNIT, "h2d_bytes_per_step": h2d,

@@ -96,8 +96,9 @@ size_t moe_layer_workspace_bytes(const moe_layer_t* layer);
  *   grouped block-scaled FP8 gate/up GEMM + SwiGLU + FP8 requant -> grouped
  *   down GEMM (bf16) -> weighted combine + shared expert + residual (bf16).
  * x and out may not alias.  Stream-ordered; no host synchronisation when
- * ep_size == 1.  With ep_size > 1 the per-peer token counts are exchanged
- * through NCCL and read back once per call (one host sync). */
+ * ep_size == 1 or with peer buffers set (moe_layer_set_peer_buffers).  With
+ * the NCCL exchange (ep_size > 1, no peer buffers) the per-peer token counts
+ * are read back once per call (one host sync). */
 moe_status_t moe_layer_forward(moe_layer_t* layer, const void* x_bf16, void* out_bf16,
                                int num_tokens, void* workspace, size_t workspace_bytes,
                                cwStream_t stream);
@@ -123,6 +124,19 @@ moe_status_t moe_layer_last_routing(const moe_layer_t* layer, const void* worksp
  * caller. */
 #define MOE_NUM_STAGES 7
 moe_status_t moe_layer_set_stage_events(moe_layer_t* layer, cwEvent_t* events);
+
+/* Expert parallelism over NVLink peer memory instead of NCCL.  Every rank
+ * allocates one buffer of moe_layer_peer_bytes() bytes that all ranks map
+ * (CUDA IPC / a symmetric-memory allocator), zero-fills it, and -- after every
+ * rank has zero-filled its own -- passes the n = ep_size pointers as mapped in
+ * this process (peer_bufs[ep_rank] is its own, 256-byte aligned).  From then on
+ * the forward exchanges counts, rows and outputs with its own kernels (P2P
+ * stores, system-scope flags with bounded waits): no NCCL call and no host
+ * synchronisation; a peer that stops answering ends the waits after at most
+ * 20 s with MOE_ERR_DEVICE_TIMEOUT from moe_layer_check_error.  NULL switches
+ * back to the NCCL exchange.  0 bytes when ep_size == 1. */
+size_t moe_layer_peer_bytes(const moe_layer_t* layer);
+moe_status_t moe_layer_set_peer_buffers(moe_layer_t* layer, void* const* peer_bufs, int n);
 
 /* Reads and clears the device error word (synchronises `stream`). */
 moe_status_t moe_layer_check_error(moe_layer_t* layer, cwStream_t stream);

@@ -1,5 +1,6 @@
 """One rank of the expert-parallel parity check (launched by
-test_gpu_ep_nccl.py under torch.distributed.run, one process per GPU).
+test_gpu_ep_nccl.py under torch.distributed.run, one process per GPU), with
+the exchange over NCCL or over NVLink peer memory (--exchange).
 
 Every rank builds the same seeded weights and tokens, keeps its expert slice
 and token slice, and runs the EP layer over a real NCCL communicator
@@ -28,6 +29,7 @@ def main() -> int:
     ap.add_argument("--tokens", type=int, default=64)
     ap.add_argument("--uniform-logits", action="store_true")
     ap.add_argument("--repeats", type=int, default=2)
+    ap.add_argument("--exchange", choices=["nccl", "peer"], default="nccl")
     a = ap.parse_args()
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -47,6 +49,8 @@ def main() -> int:
     t0, t1 = synth.token_slice(T, world, rank)
     w = synth.expert_slice(w_all, shape, world, rank)
     layer = M.MoELayer(shape, w, max_tokens=-(-T // world), ep_size=world, ep_rank=rank, comm=comm)
+    if a.exchange == "peer":
+        layer.use_peer_memory()
     x = x_all[t0:t1].contiguous()
     r_local = None if routing is None else (routing[0][t0:t1].contiguous(), routing[1][t0:t1].contiguous())
     outs = []

@@ -1,6 +1,7 @@
-"""Expert-parallel MoE FFN block over real NCCL, one process per GPU
-(tests/ep_worker.py under torch.distributed.run): the EP output must be
-bit-identical to the single-GPU layer.  Needs at least 2 GPUs; skipped on a
+"""Expert-parallel MoE FFN block across real GPUs, one process per GPU
+(tests/ep_worker.py under torch.distributed.run), with the exchange over NCCL
+and over NVLink peer memory: the EP output must be bit-identical to the
+single-GPU layer.  Needs at least 2 GPUs; skipped on a
 1-GPU box (the single-GPU emulation in test_gpu_ep.py covers every EP kernel
 there)."""
 import os
@@ -37,13 +38,15 @@ def launch(nproc: int, *args: str) -> subprocess.CompletedProcess:
     return subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=str(ROOT))
 
 
-@pytest.mark.parametrize("args", [("--shape", "tiny", "--tokens", "64"), ("--shape", "tiny", "--tokens", "3"),
+@pytest.mark.parametrize("exchange", ["nccl", "peer"])
+@pytest.mark.parametrize("args", [("--shape", "tiny", "--tokens", "64", "--repeats", "3"),
+                                  ("--shape", "tiny", "--tokens", "3"),
                                   ("--shape", "glm", "--tokens", "4096"),
                                   ("--shape", "glm", "--tokens", "256", "--uniform-logits")])
-def test_ep_nccl_bit_identical(gpu, args):
+def test_ep_bit_identical(gpu, args, exchange):
     n = n_gpus()
     if n < 2:
         pytest.skip("needs >= 2 GPUs")
     nproc = 8 if n >= 8 else (4 if n >= 4 else 2)
-    r = launch(nproc, *args)
+    r = launch(nproc, *args, "--exchange", exchange)
     assert r.returncode == 0 and "EP_OK" in r.stdout, (r.stdout[-3000:], r.stderr[-3000:])

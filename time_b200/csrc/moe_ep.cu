@@ -29,13 +29,35 @@
 //
 // Packed row (moe_ep_row_bytes(H) bytes, a multiple of 16): H e4m3 bytes, then
 // H/128 fp32 scales, then zero padding.
+//
+// Peer-memory exchange (moe_layer_set_peer_buffers): the same protocol with no
+// NCCL and no host synchronisation.  Every rank owns a symmetric buffer that
+// all ranks have mapped (NVLink peer memory):
+//   flags [3][kMaxEpRanks] u32   counts / dispatch / combine epochs, one per source
+//   table [ep][E] i32            every rank's per-expert send counts
+//   recv  [recv_cap][rb]         packed rows dispatched to this rank
+//   yrecv [T*k][H] bf16          expert outputs returned to this rank
+// Per forward (epoch e = 1, 2, ...): ep_counts_kernel writes this rank's
+// counts into every table and raises flags[0][me] = e on every rank, waits for
+// all ranks' flags, then derives the whole exchange plan on the device;
+// ep_dispatch_kernel packs each sent row straight into its destination's recv
+// buffer; ep_signal_wait_kernel raises flags[1][me] and waits for every
+// source; after the GEMMs ep_combine_send_kernel writes each expert output row
+// into its token owner's yrecv, and flags[2] closes the step.  Writers fence
+// (system scope) before a release store of the flag; waiters acquire.  Every
+// wait is a bounded spin of one thread (error word 3 on timeout).
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstring>
 
+#include "sm100.cuh"
 #include "moe_layer.h"
+#include "moe_ep_peer.h"
 
 namespace {
+
+using namespace tb;
 
 inline moe_status_t launch_status() {
     return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
@@ -178,6 +200,168 @@ ep_pack_y_kernel(const uint8_t* __restrict__ y, const int32_t* __restrict__ recv
     }
 }
 
+// ---------------------------------------------------------------- peer memory
+
+constexpr int kMaxEpRanks = 64;
+enum { kFlagCounts = 0, kFlagDispatch = 1, kFlagCombine = 2 };
+// plan[] layout (int32, device): per rank d: soff, srows, roff_in (where my
+// rows land in d's recv), recv_off, rrows (from d), ysoff (where d's outputs
+// for my experts land in d's send order); then stot, rtot.
+enum { kPlanSoff = 0, kPlanSrows = 1, kPlanRoffIn = 2, kPlanRecvOff = 3, kPlanRrows = 4, kPlanYsoff = 5 };
+
+struct EpPeers {
+    uint8_t* base[kMaxEpRanks];   // rank r's symmetric buffer as mapped in this process
+    int ep, me, E, epr;
+    size_t off_flags, off_table, off_recv, off_yrecv;
+    unsigned long long timeout_ns;
+};
+
+__device__ __forceinline__ uint32_t* flag_ptr(const EpPeers& P, int rank, int phase, int src) {
+    return reinterpret_cast<uint32_t*>(P.base[rank] + P.off_flags) + phase * kMaxEpRanks + src;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// One thread: raise this rank's flag for `phase` on every rank, then wait
+// until every source has raised its flag here.  False on timeout.
+__device__ bool signal_and_wait(const EpPeers& P, int phase, uint32_t epoch) {
+    __threadfence_system();
+    for (int d = 0; d < P.ep; ++d) st_release_sys(flag_ptr(P, d, phase, P.me), epoch);
+    const uint64_t t0 = globaltimer_ns();
+    for (int s = 0; s < P.ep; ++s) {
+        const uint32_t* f = flag_ptr(P, P.me, phase, s);
+        while (ld_acquire_sys(f) != epoch) {
+            if (globaltimer_ns() - t0 > P.timeout_ns) return false;
+            __nanosleep(64);
+        }
+    }
+    return true;
+}
+
+// Single block: counts into every table, barrier, then the exchange plan.
+__global__ void __launch_bounds__(256)
+ep_counts_kernel(const EpPeers P, const int32_t* __restrict__ ecounts, uint32_t epoch, int32_t* __restrict__ plan,
+                 int32_t* __restrict__ rcounts, int* __restrict__ error_word) {
+    const int tid = threadIdx.x;
+    for (int d = 0; d < P.ep; ++d) {
+        int32_t* tab = reinterpret_cast<int32_t*>(P.base[d] + P.off_table) + static_cast<size_t>(P.me) * P.E;
+        for (int e = tid; e < P.E; e += blockDim.x) tab[e] = ecounts[e];
+    }
+    __threadfence_system();
+    __syncthreads();
+    __shared__ int ok;
+    if (tid == 0) ok = signal_and_wait(P, kFlagCounts, epoch) ? 1 : 0;
+    __syncthreads();
+    if (!ok) {
+        if (tid == 0) {
+            if (error_word) atomicExch(error_word, 3);
+            for (int i = 0; i < 6 * P.ep + 2; ++i) plan[i] = 0;   // nothing moves
+        }
+        for (int i = tid; i < P.ep * P.epr; i += blockDim.x) rcounts[i] = 0;
+        return;
+    }
+    const int32_t* tab = reinterpret_cast<const int32_t*>(P.base[P.me] + P.off_table);   // [ep][E], all sources
+    for (int i = tid; i < P.ep * P.epr; i += blockDim.x) {
+        const int s = i / P.epr, j = i % P.epr;
+        rcounts[i] = tab[static_cast<size_t>(s) * P.E + P.me * P.epr + j];
+    }
+    if (tid == 0) {
+        const int ep = P.ep, epr = P.epr, me = P.me;
+        int32_t* pl = plan;
+        int so = 0, ro = 0;
+        for (int d = 0; d < ep; ++d) {
+            int sn = 0, rn = 0, before = 0, ys = 0;
+            for (int j = 0; j < epr; ++j) {
+                sn += ecounts[d * epr + j];                                  // my rows for d
+                rn += tab[static_cast<size_t>(d) * P.E + me * epr + j];     // d's rows for me
+            }
+            for (int s = 0; s < me; ++s)                                      // earlier sources' rows for d
+                for (int j = 0; j < epr; ++j) before += tab[static_cast<size_t>(s) * P.E + d * epr + j];
+            for (int e = 0; e < me * epr; ++e) ys += tab[static_cast<size_t>(d) * P.E + e];   // d's rows before mine
+            pl[6 * d + kPlanSoff] = so;
+            pl[6 * d + kPlanSrows] = sn;
+            pl[6 * d + kPlanRoffIn] = before;
+            pl[6 * d + kPlanRecvOff] = ro;
+            pl[6 * d + kPlanRrows] = rn;
+            pl[6 * d + kPlanYsoff] = ys;
+            so += sn;
+            ro += rn;
+        }
+        pl[6 * ep] = so;       // stot
+        pl[6 * ep + 1] = ro;   // rtot
+    }
+}
+
+// Warp per sent row: pack (values + scales) straight into the destination's recv.
+__global__ void __launch_bounds__(256)
+ep_dispatch_kernel(const EpPeers P, const uint8_t* __restrict__ xq, const float* __restrict__ xs, int xs_ld,
+                   const int32_t* __restrict__ stok, const int32_t* __restrict__ plan, int H, size_t row_bytes,
+                   int recv_cap) {
+    __shared__ int s_soff[kMaxEpRanks], s_roff[kMaxEpRanks];
+    for (int d = threadIdx.x; d < P.ep; d += blockDim.x) {
+        s_soff[d] = plan[6 * d + kPlanSoff];
+        s_roff[d] = plan[6 * d + kPlanRoffIn];
+    }
+    __syncthreads();
+    const int stot = plan[6 * P.ep];
+    const int lane = threadIdx.x & 31;
+    const int nwarps = (gridDim.x * blockDim.x) >> 5;
+    const int vec = H / 16, nblk = H / 128;
+    const int nscale_padded = (nblk * 4 + 15) / 16 * 4;
+    for (int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < stot; r += nwarps) {
+        int d = P.ep - 1;
+        while (d > 0 && s_soff[d] > r) --d;
+        const int dest = s_roff[d] + (r - s_soff[d]);
+        if (dest >= recv_cap) continue;          // cannot happen within max_tokens (checked by the plan)
+        uint8_t* dst = P.base[d] + P.off_recv + static_cast<size_t>(dest) * row_bytes;
+        const int t = stok[r];
+        const int4* src = reinterpret_cast<const int4*>(xq + static_cast<size_t>(t) * H);
+        for (int i = lane; i < vec; i += 32) reinterpret_cast<int4*>(dst)[i] = src[i];
+        float* ds = reinterpret_cast<float*>(dst + H);
+        for (int b = lane; b < nscale_padded; b += 32) ds[b] = (b < nblk) ? xs[static_cast<size_t>(b) * xs_ld + t] : 0.0f;
+    }
+    __threadfence_system();
+}
+
+// Warp per received row: its expert output goes back into the token owner's yrecv.
+__global__ void __launch_bounds__(256)
+ep_combine_send_kernel(const EpPeers P, const uint8_t* __restrict__ y, const int32_t* __restrict__ recv_dst,
+                       const int32_t* __restrict__ plan, size_t row_bytes, int ycap, int y_rows) {
+    __shared__ int s_roff[kMaxEpRanks], s_ys[kMaxEpRanks];
+    for (int d = threadIdx.x; d < P.ep; d += blockDim.x) {
+        s_roff[d] = plan[6 * d + kPlanRecvOff];
+        s_ys[d] = plan[6 * d + kPlanYsoff];
+    }
+    __syncthreads();
+    const int rtot = plan[6 * P.ep + 1];
+    const int lane = threadIdx.x & 31;
+    const int nwarps = (gridDim.x * blockDim.x) >> 5;
+    const int vec = static_cast<int>(row_bytes / 16);
+    for (int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < rtot; i += nwarps) {
+        int s = P.ep - 1;
+        while (s > 0 && s_roff[s] > i) --s;
+        const int dest = s_ys[s] + (i - s_roff[s]);
+        const int yr = recv_dst[i];
+        if (dest >= ycap || yr < 0 || yr >= y_rows) continue;
+        const int4* src = reinterpret_cast<const int4*>(y + static_cast<size_t>(yr) * row_bytes);
+        int4* dst = reinterpret_cast<int4*>(P.base[s] + P.off_yrecv + static_cast<size_t>(dest) * row_bytes);
+        for (int c = lane; c < vec; c += 32) dst[c] = src[c];
+    }
+    __threadfence_system();
+}
+
+__global__ void ep_signal_wait_kernel(const EpPeers P, int phase, uint32_t epoch, int* __restrict__ error_word) {
+    if (threadIdx.x == 0 && !signal_and_wait(P, phase, epoch) && error_word) atomicExch(error_word, 3);
+}
+
 inline int grid_for_rows(int rows) {
     int blocks = (rows + 7) / 8;
     if (blocks > 148 * 16) blocks = 148 * 16;
@@ -277,3 +461,71 @@ moe_status_t moe_ep_pack_y(const void* y_bf16, const int32_t* recv_dst, int n, i
 }
 
 }  // extern "C"
+
+namespace tbep {
+
+namespace {
+
+EpPeers to_dev(const Peers& P) {
+    EpPeers d;
+    std::memset(&d, 0, sizeof(d));
+    for (int r = 0; r < P.ep && r < kMaxRanks; ++r) d.base[r] = static_cast<uint8_t*>(P.base[r]);
+    d.ep = P.ep;
+    d.me = P.me;
+    d.E = P.E;
+    d.epr = P.epr;
+    d.off_flags = P.lay.off_flags;
+    d.off_table = P.lay.off_table;
+    d.off_recv = P.lay.off_recv;
+    d.off_yrecv = P.lay.off_yrecv;
+    d.timeout_ns = P.timeout_ns;
+    return d;
+}
+
+size_t up256(size_t v) { return (v + 255) / 256 * 256; }
+
+}  // namespace
+
+Layout layout(int ep, int E, int recv_cap, size_t row_bytes, size_t y_rows, int H) {
+    Layout L;
+    size_t o = 0;
+    L.off_flags = o;
+    o = up256(o + 3 * kMaxEpRanks * sizeof(uint32_t));
+    L.off_table = o;
+    o = up256(o + static_cast<size_t>(ep) * E * sizeof(int32_t));
+    L.off_recv = o;
+    o = up256(o + static_cast<size_t>(recv_cap) * row_bytes);
+    L.off_yrecv = o;
+    o = up256(o + y_rows * static_cast<size_t>(H) * 2);
+    L.bytes = o;
+    return L;
+}
+
+moe_status_t counts(const Peers& P, const int32_t* ecounts, uint32_t epoch, int32_t* plan, int32_t* rcounts,
+                    int* error_word, cudaStream_t st) {
+    ep_counts_kernel<<<1, 256, 0, st>>>(to_dev(P), ecounts, epoch, plan, rcounts, error_word);
+    return launch_status();
+}
+
+moe_status_t dispatch(const Peers& P, const void* xq, const float* xs, int xs_ld, const int32_t* stok,
+                      const int32_t* plan, int H, size_t row_bytes, int recv_cap, int max_rows, cudaStream_t st) {
+    if (max_rows <= 0) return MOE_OK;
+    ep_dispatch_kernel<<<grid_for_rows(max_rows), 256, 0, st>>>(to_dev(P), static_cast<const uint8_t*>(xq), xs,
+                                                                 xs_ld, stok, plan, H, row_bytes, recv_cap);
+    return launch_status();
+}
+
+moe_status_t signal_wait(const Peers& P, int phase, uint32_t epoch, int* error_word, cudaStream_t st) {
+    ep_signal_wait_kernel<<<1, 32, 0, st>>>(to_dev(P), phase, epoch, error_word);
+    return launch_status();
+}
+
+moe_status_t combine_send(const Peers& P, const void* y_bf16, const int32_t* recv_dst, const int32_t* plan,
+                          int H, int y_cap, int y_rows, int max_rows, cudaStream_t st) {
+    if (max_rows <= 0) return MOE_OK;
+    ep_combine_send_kernel<<<grid_for_rows(max_rows), 256, 0, st>>>(
+        to_dev(P), static_cast<const uint8_t*>(y_bf16), recv_dst, plan, static_cast<size_t>(H) * 2, y_cap, y_rows);
+    return launch_status();
+}
+
+}  // namespace tbep

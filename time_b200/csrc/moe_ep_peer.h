@@ -1,0 +1,44 @@
+// moe_ep_peer.h -- internal interface between the layer (moe_layer.cu) and the
+// peer-memory expert-parallel exchange kernels (moe_ep.cu).  Not part of the
+// C-ABI.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+
+#include <cuda_runtime.h>
+
+#include "moe_layer.h"
+
+namespace tbep {
+
+constexpr int kMaxRanks = 64;
+
+// Byte layout of one rank's symmetric exchange buffer (identical on every rank).
+struct Layout {
+    size_t off_flags, off_table, off_recv, off_yrecv, bytes;
+};
+
+Layout layout(int ep, int E, int recv_cap, size_t row_bytes, size_t y_rows, int H);
+
+struct Peers {
+    void* base[kMaxRanks];   // rank r's buffer as mapped in this process
+    int ep, me, E, epr;
+    Layout lay;
+    unsigned long long timeout_ns;
+};
+
+// plan (device int32): 6 per rank + stot + rtot
+inline int plan_ints(int ep) { return 6 * ep + 2; }
+
+moe_status_t counts(const Peers& P, const int32_t* ecounts, uint32_t epoch, int32_t* plan, int32_t* rcounts,
+                    int* error_word, cudaStream_t st);
+moe_status_t dispatch(const Peers& P, const void* xq, const float* xs, int xs_ld, const int32_t* stok,
+                      const int32_t* plan, int H, size_t row_bytes, int recv_cap, int max_rows, cudaStream_t st);
+moe_status_t signal_wait(const Peers& P, int phase, uint32_t epoch, int* error_word, cudaStream_t st);
+moe_status_t combine_send(const Peers& P, const void* y_bf16, const int32_t* recv_dst, const int32_t* plan,
+                          int H, int y_cap, int y_rows, int max_rows, cudaStream_t st);
+
+enum Phase { kCounts = 0, kDispatch = 1, kCombine = 2 };
+
+}  // namespace tbep

@@ -43,6 +43,7 @@
 
 #include "cublas_wrappers.h"
 #include "moe_layer.h"
+#include "moe_ep_peer.h"
 
 extern "C" moe_status_t moe_gather_rows_n(const void* xq, const float* xs, int xs_ld, const int32_t* row_token,
                                           const int32_t* total_rows, int row_capacity, int H, void* xp, float* xps,
@@ -66,6 +67,11 @@ struct moe_layer {
     int recv_cap;
     int32_t* h_counts;    // pinned [2E]
     int sync_timeout_ms;
+    // peer-memory exchange (moe_layer_set_peer_buffers)
+    bool peer_mode;
+    tbep::Peers peers;
+    uint32_t epoch;
+    size_t off_plan;
 };
 
 namespace {
@@ -114,6 +120,7 @@ void plan_workspace(moe_layer* L) {
         L->off_rdst = take(RC * 4);
         L->off_ysend = take(RC * H * 2);
         L->off_yrecv = take(T * K * H * 2);
+        L->off_plan = take(tbep::plan_ints(c.ep_size) * 4);
     }
     L->bytes = o;
 }
@@ -216,6 +223,40 @@ moe_status_t run_experts_ep(moe_layer* L, const int32_t* idx, const float* wts, 
     int32_t* row_src = at<int32_t>(ws, L->off_rowtok);
     int32_t* recv_dst = at<int32_t>(ws, L->off_rdst);
     const size_t rb = L->row_bytes;
+
+    if (L->peer_mode) {
+        // device-driven exchange over the symmetric peer buffers: no host synchronisation
+        const tbep::Peers& P = L->peers;
+        uint8_t* mine = static_cast<uint8_t*>(P.base[c.ep_rank]);
+        int32_t* plan = at<int32_t>(ws, L->off_plan);
+        const uint32_t epoch = ++L->epoch;
+        const int y_cap = c.max_tokens * K;
+        mark(L, 2, st);
+        MOE_TRY(moe_permute_padded(idx, T, K, 0, E, 0, ecounts, at<int32_t>(ws, L->off_estart), spos, stok, stotal,
+                                   T * K, L->error_word, 1, st));
+        MOE_TRY(tbep::counts(P, ecounts, epoch, plan, rcounts, L->error_word, st));
+        mark(L, 3, st);
+        MOE_TRY(tbep::dispatch(P, at<void>(ws, L->off_xq), at<float>(ws, L->off_xs), L->xs_ld, stok, plan, H, rb,
+                               L->recv_cap, T * K, st));
+        MOE_TRY(tbep::signal_wait(P, tbep::kDispatch, epoch, L->error_word, st));
+        MOE_TRY(moe_ep_recv_plan(rcounts, ep, epr, T, S, counts, start, total, row_src, recv_dst, L->rcap, L->recv_cap,
+                                 L->error_word, st));
+        MOE_TRY(moe_ep_gather(mine + P.lay.off_recv, at<void>(ws, L->off_xq), at<float>(ws, L->off_xs), L->xs_ld,
+                              row_src, total, L->rcap, H, at<void>(ws, L->off_xp), at<float>(ws, L->off_xps), L->rcap,
+                              st));
+        cbwGroupedGemmArgs g1 = gemm_args(L, ws, false), g2 = gemm_args(L, ws, true);
+        mark(L, 4, st);
+        MOE_TRY(cbw_to_moe(cbwFp8BlockScaledGroupedGemm(&g1, L->error_word, st)));
+        mark(L, 5, st);
+        MOE_TRY(cbw_to_moe(cbwFp8BlockScaledGroupedGemm(&g2, L->error_word, st)));
+        mark(L, 6, st);
+        MOE_TRY(tbep::combine_send(P, at<void>(ws, L->off_y), recv_dst, plan, H, y_cap, L->rcap, L->recv_cap, st));
+        MOE_TRY(tbep::signal_wait(P, tbep::kCombine, epoch, L->error_word, st));
+        MOE_TRY(moe_combine_split(x, mine + P.lay.off_yrecv, spos, wts, at<void>(ws, L->off_y), start + epr, S, T, K,
+                                  H, out, st));
+        mark(L, MOE_NUM_STAGES, st);
+        return MOE_OK;
+    }
 
     mark(L, 2, st);
     MOE_TRY(moe_permute_padded(idx, T, K, 0, E, 0, ecounts, at<int32_t>(ws, L->off_estart), spos, stok, stotal,
@@ -395,6 +436,35 @@ moe_status_t moe_layer_set_stage_events(moe_layer_t* L, cwEvent_t* events) {
     return MOE_OK;
 }
 
+size_t moe_layer_peer_bytes(const moe_layer_t* L) {
+    if (!L || L->cfg.ep_size <= 1) return 0;
+    const moe_layer_config_t& c = L->cfg;
+    return tbep::layout(c.ep_size, c.num_experts, L->recv_cap, L->row_bytes,
+                        static_cast<size_t>(c.max_tokens) * c.top_k, c.hidden).bytes;
+}
+
+moe_status_t moe_layer_set_peer_buffers(moe_layer_t* L, void* const* peer_bufs, int n) {
+    if (!L) return MOE_ERR_INVALID_ARGUMENT;
+    const moe_layer_config_t& c = L->cfg;
+    if (!peer_bufs) { L->peer_mode = false; return MOE_OK; }
+    if (c.ep_size <= 1 || n != c.ep_size || n > tbep::kMaxRanks) return MOE_ERR_INVALID_ARGUMENT;
+    for (int r = 0; r < n; ++r)
+        if (!peer_bufs[r] || (reinterpret_cast<uintptr_t>(peer_bufs[r]) & 255)) return MOE_ERR_INVALID_ARGUMENT;
+    std::memset(&L->peers, 0, sizeof(L->peers));
+    for (int r = 0; r < n; ++r) L->peers.base[r] = peer_bufs[r];
+    L->peers.ep = c.ep_size;
+    L->peers.me = c.ep_rank;
+    L->peers.E = c.num_experts;
+    L->peers.epr = c.num_experts / c.ep_size;
+    L->peers.lay = tbep::layout(c.ep_size, c.num_experts, L->recv_cap, L->row_bytes,
+                                static_cast<size_t>(c.max_tokens) * c.top_k, c.hidden);
+    const int ms = L->sync_timeout_ms < 20000 ? L->sync_timeout_ms : 20000;   // device waits: at most 20 s
+    L->peers.timeout_ns = static_cast<unsigned long long>(ms) * 1000000ull;
+    L->epoch = 0;
+    L->peer_mode = true;
+    return MOE_OK;
+}
+
 moe_status_t moe_layer_check_error(moe_layer_t* L, cwStream_t stream) {
     if (!L) return MOE_ERR_INVALID_ARGUMENT;
     int h = 0;
@@ -404,7 +474,7 @@ moe_status_t moe_layer_check_error(moe_layer_t* L, cwStream_t stream) {
     if (h == 0) return MOE_OK;
     cudaMemsetAsync(L->error_word, 0, sizeof(int), st);
     cudaStreamSynchronize(st);
-    return h == 2 ? MOE_ERR_WORKSPACE : MOE_ERR_DEVICE_TIMEOUT;
+    return h == 2 ? MOE_ERR_WORKSPACE : MOE_ERR_DEVICE_TIMEOUT;   // 1: GEMM wait, 3: peer exchange wait
 }
 
 }  // extern "C"

@@ -89,6 +89,9 @@ def libs():
                                         c_int, c_int, c_void_p, c_void_p]
         k.moe_permute_padded.argtypes = [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p,
                                          c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p]
+        k.moe_layer_peer_bytes.argtypes = [c_void_p]
+        k.moe_layer_peer_bytes.restype = c_size_t
+        k.moe_layer_set_peer_buffers.argtypes = [c_void_p, c_void_p, c_int]
         k.moe_ep_row_bytes.argtypes = [c_int]
         k.moe_ep_row_bytes.restype = c_size_t
         sz_p = ctypes.POINTER(c_size_t)
@@ -245,6 +248,28 @@ class MoELayer:
         self._ev_arr = (c_void_p * len(events))(*[e.cuda_event for e in events])
         check("moe_layer_set_stage_events", self._k.moe_layer_set_stage_events(self._h, self._ev_arr))
 
+    def use_peer_memory(self, group=None):
+        """Switch the expert-parallel exchange to NVLink peer memory: allocate
+        this rank's buffer with torch's symmetric-memory allocator (every rank
+        maps every other rank's), zero it, rendezvous, and hand the mapped
+        pointers to the layer.  Collective over the torch.distributed group."""
+        import torch
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+        nbytes = self._k.moe_layer_peer_bytes(self._h)
+        if nbytes == 0:
+            raise ValueError("peer memory needs ep_size > 1")
+        group = group or dist.group.WORLD
+        dev = self.weights["w13"].device
+        buf = symm.empty(nbytes, dtype=torch.uint8, device=dev)
+        buf.zero_()
+        handle = symm.rendezvous(buf, group.group_name)
+        torch.cuda.synchronize()
+        dist.barrier(group=group)                 # every rank zeroed its buffer before any peer writes
+        ptrs = (c_void_p * len(handle.buffer_ptrs))(*handle.buffer_ptrs)
+        check("moe_layer_set_peer_buffers", self._k.moe_layer_set_peer_buffers(self._h, ptrs, len(handle.buffer_ptrs)))
+        self._peer = (buf, handle, ptrs)          # keep the mapping alive with the layer
+
     def check_error(self, stream=None):
         check("moe_layer_check_error", self._k.moe_layer_check_error(self._h, stream_ptr(stream)))
 
@@ -269,6 +294,7 @@ class MoELayer:
         if getattr(self, "_h", None):
             self._k.moe_layer_destroy(self._h)
             self._h = None
+        self._peer = None
 
     def __del__(self):
         try:
