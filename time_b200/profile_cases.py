@@ -82,8 +82,17 @@ def gemm(tokens: int, experts: int, iters: int) -> dict:
     out = torch.empty_like(x)
     ms = _time(lambda: layer.forward(x, out), iters)
     layer.check_error()
+    _, _, counts = layer.last_routing(tokens)
     layer.close()
-    return {"layer_forward_ms": ms}
+    # algorithmic bytes per launch of each grouped GEMM (the bench's definition)
+    H, I = shape.hidden, shape.intermediate
+    rows = int(counts.sum())
+    touched = int((counts > 0).sum())
+    w13 = 2 * I * H + (2 * I // 128) * (H // 128) * 4
+    w2 = H * I + (H // 128) * (I // 128) * 4
+    return {"layer_forward_ms": ms, "rows": rows, "touched_groups": touched,
+            "gemm_gate_up_bytes": touched * w13 + rows * (H + H // 128 * 4) + rows * (I + I // 128 * 4),
+            "gemm_down_bytes": touched * w2 + rows * (I + I // 128 * 4) + rows * H * 2}
 
 
 def main() -> int:
