@@ -171,6 +171,27 @@ moe_status_t moe_router_logits(const float* n, const float* router_w, const floa
 moe_status_t moe_topk_softmax(const float* logits, int T, int E, int k, int32_t* topk_idx,
                               float* topk_w, cwStream_t stream);
 
+/* No counterpart in the reference.  moe_router_logits followed by
+ * moe_topk_softmax for callers that cannot provide device memory beyond their
+ * inputs and outputs -- an engine that carves all of its device memory out of
+ * its own arena at start-up, or a plain C / FFI host that must not call
+ * cudaMalloc on its hot path (it synchronises the whole device).  The [T][E]
+ * fp32 logits between the two kernels live in a fixed array inside this
+ * library (4 MB on every GPU that loads it, held until the process exits);
+ * the call allocates nothing.  Same results, bit for bit, as the two-call
+ * path.  Limits and rules:
+ *   - T * E <= 1048576 (e.g. 4096 tokens x 256 experts); larger requests
+ *     return MOE_ERR_WORKSPACE and launch nothing.
+ *   - The first call on a device looks up the array's device address for
+ *     that device (make it before any stream capture on that device).
+ *   - Every call on a device uses the same array: calls that can overlap on
+ *     the GPU (different streams without ordering between them) race.  No
+ *     part of the array needs to start at zero: every logit read is first
+ *     written by the same call. */
+moe_status_t moe_router_topk_noalloc(const float* n, const float* router_w,
+                                     const float* router_bias, int T, int H, int E, int k,
+                                     int32_t* topk_idx, float* topk_w, cwStream_t stream);
+
 /* Router: logits[t][e] = fma-chain over i = 0..H-1 of n[t][i]*W[e][i]
  * (+ bias[e]), n recomputed from x, rms, gamma exactly as above; then the
  * reference's top-k (strict '>' from -FLT_MAX: lower index wins ties, NaN

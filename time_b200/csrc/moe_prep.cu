@@ -6,6 +6,7 @@
 #include <cuda_bf16.h>
 #include <cfloat>
 #include <cstdint>
+#include <mutex>
 
 #include "sm100.cuh"
 #include "moe_layer.h"
@@ -686,3 +687,58 @@ moe_status_t moe_combine(const void* x_bf16, const void* y_bf16, const int32_t* 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- allocation-free router
+// Some callers cannot hand this library any device memory beyond their inputs
+// and outputs: an engine whose whole device budget is carved out of its own
+// arena at start-up, or a plain C / FFI host that binds only this library and
+// must not call cudaMalloc on its hot path (cudaMalloc synchronises the whole
+// device).  moe_router_topk_noalloc serves them: the [T][E] fp32 logits that
+// moe_router_logits + moe_topk_softmax pass between them live in this fixed
+// array instead of a caller buffer.  Every GPU that loads the library holds
+// it (4 MB) until the process exits.
+constexpr int kNoAllocLogits = 1 << 20;   // T * E <= 1,048,576 (e.g. 4096 tokens x 256 experts)
+static __device__ __align__(256) float g_router_logits_scratch[kNoAllocLogits];
+
+namespace {
+
+// The array's device address, looked up once per device with that device
+// current (host code cannot use the array's name as a device pointer).
+float* router_scratch_address(moe_status_t* status) {
+    constexpr int kMaxDevices = 64;
+    static std::mutex mu;
+    static float* addr[kMaxDevices] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        *status = MOE_ERR_CUDA;
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_router_logits_scratch) != cudaSuccess || !p) {
+            *status = MOE_ERR_CUDA;
+            return nullptr;
+        }
+        addr[dev] = static_cast<float*>(p);
+    }
+    *status = MOE_OK;
+    return addr[dev];
+}
+
+}  // namespace
+
+extern "C" moe_status_t moe_router_topk_noalloc(const float* n, const float* router_w, const float* router_bias,
+                                                int T, int H, int E, int k, int32_t* topk_idx, float* topk_w,
+                                                cwStream_t stream) {
+    if (T < 0 || E <= 0) return MOE_ERR_INVALID_ARGUMENT;
+    if (static_cast<long long>(T) * E > kNoAllocLogits) return MOE_ERR_WORKSPACE;   // beyond the fixed array
+    if (T == 0) return MOE_OK;
+    moe_status_t st = MOE_OK;
+    float* logits = router_scratch_address(&st);
+    if (!logits) return st;
+    // every logit the top-k reads is written first: nothing needs clearing
+    st = moe_router_logits(n, router_w, router_bias, T, H, E, logits, stream);
+    if (st != MOE_OK) return st;
+    return moe_topk_softmax(logits, T, E, k, topk_idx, topk_w, stream);
+}
