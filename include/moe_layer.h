@@ -237,6 +237,18 @@ moe_status_t moe_permute_padded(const int32_t* topk_idx, int T, int k, int e_beg
                                 int32_t* row_token, int32_t* total_rows, int row_capacity,
                                 int* error_word, int pad, cwStream_t stream);
 
+/* moe_permute_padded spread over many blocks (one 256-pair block per slice
+ * of the pairs, a scan block, a scatter pass): identical outputs, for large
+ * T*k.  `scratch` (device, moe_permute_mb_scratch_bytes(T, k, e_begin, e_end)
+ * bytes) holds per-block counts.  On refusal (row_capacity too small)
+ * total_rows is -1, counts are zero and the error word is 2. */
+size_t moe_permute_mb_scratch_bytes(int T, int k, int e_begin, int e_end);
+moe_status_t moe_permute_mb(const int32_t* topk_idx, int T, int k, int e_begin, int e_end,
+                            int num_shared, int32_t* counts, int32_t* seg_start, int32_t* pos,
+                            int32_t* row_token, int32_t* total_rows, int row_capacity,
+                            int* error_word, int pad, void* scratch, size_t scratch_bytes,
+                            cwStream_t stream);
+
 /* moe_combine with the shared expert's rows read from y_shared_bf16 (at
  * shared_rows[g] + t) and the routed rows from y_bf16 (at pos). */
 moe_status_t moe_combine_split(const void* x_bf16, const void* y_bf16, const int32_t* pos,

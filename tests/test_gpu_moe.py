@@ -166,6 +166,79 @@ def test_permute_bit_exact(gpu, oracle, T, K, E, shared):
     assert np.array_equal(rowtok.cpu().numpy()[:R], rt)
 
 
+@pytest.mark.parametrize("T,K,E,eb,ee,shared,pad", [(1, 1, 4, 0, 4, 1, 16), (37, 4, 9, 0, 9, 1, 16),
+                                                     (4096, 8, 160, 0, 160, 1, 16), (4096, 8, 160, 0, 160, 0, 1),
+                                                     (2048, 8, 160, 40, 60, 1, 16), (300, 2, 8, 0, 8, 0, 1),
+                                                     (513, 8, 160, 0, 160, 1, 16)])
+def test_permute_multiblock_matches_single_block(gpu, oracle, T, K, E, eb, ee, shared, pad):
+    """moe_permute_mb (the layer's permutation) against moe_permute_padded:
+    identical counts, segment starts, pair rows and row tokens; and against
+    the oracle for the 16-row padding."""
+    k = M.libs()["libkernels.so"]
+    rng = np.random.default_rng(T * 3 + E + eb)
+    if T == 2048:   # one hot group, the rest empty
+        idx = np.tile(np.arange(eb, eb + K, dtype=np.int32) % E, (T, 1))
+    else:
+        idx = np.stack([rng.choice(E, K, replace=False) for _ in range(T)]).astype(np.int32)
+    if T > 5:
+        idx[3, 0] = -1
+        idx[T - 1, K - 1] = -1
+    G = (ee - eb) + shared
+    cap = T * K + shared * T + pad * G
+    d_idx = torch.from_numpy(idx).to(gpu)
+    outs = []
+    for which in ("single", "multi"):
+        counts = torch.full((G,), -5, dtype=torch.int32, device=gpu)
+        start = torch.full((G,), -5, dtype=torch.int32, device=gpu)
+        pos = torch.full((T * K,), -5, dtype=torch.int32, device=gpu)
+        rowtok = torch.full((cap,), -7, dtype=torch.int32, device=gpu)
+        total = torch.full((1,), -5, dtype=torch.int32, device=gpu)
+        err = torch.zeros(1, dtype=torch.int32, device=gpu)
+        if which == "single":
+            M.check("permute_padded", k.moe_permute_padded(M.ptr(d_idx), T, K, eb, ee, shared, M.ptr(counts),
+                                                           M.ptr(start), M.ptr(pos), M.ptr(rowtok), M.ptr(total),
+                                                           cap, M.ptr(err), pad, stream()))
+        else:
+            nbytes = k.moe_permute_mb_scratch_bytes(T, K, eb, ee)
+            scratch = torch.full((max(nbytes, 4),), 0x5A, dtype=torch.uint8, device=gpu)
+            M.check("permute_mb", k.moe_permute_mb(M.ptr(d_idx), T, K, eb, ee, shared, M.ptr(counts), M.ptr(start),
+                                                   M.ptr(pos), M.ptr(rowtok), M.ptr(total), cap, M.ptr(err), pad,
+                                                   M.ptr(scratch), nbytes, stream()))
+        torch.cuda.synchronize()
+        assert err.item() == 0
+        R = total.item()
+        outs.append((counts.cpu(), start.cpu(), pos.cpu(), rowtok.cpu()[:R], R))
+    a, b = outs
+    assert a[4] == b[4]
+    for x, y in zip(a[:4], b[:4]):
+        assert torch.equal(x, y)
+    if pad == 16 and eb == 0 and ee == E:
+        c, st_, p_, rt, R = oracle.moe_permute(idx, E, shared)
+        assert b[4] == R and np.array_equal(b[2].numpy(), p_.reshape(-1)) and np.array_equal(b[3].numpy(), rt)
+
+
+def test_permute_multiblock_refuses_overflow(gpu):
+    k = M.libs()["libkernels.so"]
+    T, K, E = 1000, 8, 160
+    idx = torch.zeros(T, K, dtype=torch.int32, device=gpu)       # all pairs to expert 0
+    counts = torch.empty(E + 1, dtype=torch.int32, device=gpu)
+    start = torch.empty(E + 1, dtype=torch.int32, device=gpu)
+    pos = torch.empty(T * K, dtype=torch.int32, device=gpu)
+    rowtok = torch.full((100,), -7, dtype=torch.int32, device=gpu)
+    total = torch.empty(1, dtype=torch.int32, device=gpu)
+    err = torch.zeros(1, dtype=torch.int32, device=gpu)
+    nbytes = k.moe_permute_mb_scratch_bytes(T, K, 0, E)
+    scratch = torch.empty(nbytes, dtype=torch.uint8, device=gpu)
+    M.check("permute_mb", k.moe_permute_mb(M.ptr(idx), T, K, 0, E, 1, M.ptr(counts), M.ptr(start), M.ptr(pos),
+                                           M.ptr(rowtok), M.ptr(total), 100, M.ptr(err), 16, M.ptr(scratch), nbytes,
+                                           stream()))
+    torch.cuda.synchronize()
+    assert err.item() == 2 and total.item() == -1
+    assert (counts == 0).all() and (pos == -1).all() and (rowtok == -7).all()
+    assert k.moe_permute_mb(M.ptr(idx), T, K, 0, E, 1, M.ptr(counts), M.ptr(start), M.ptr(pos), M.ptr(rowtok),
+                            M.ptr(total), 100, M.ptr(err), 16, M.ptr(scratch), nbytes - 4, stream()) == 6
+
+
 def test_permute_capacity_overflow_reports(gpu):
     k = M.libs()["libkernels.so"]
     T, K, E = 64, 4, 8

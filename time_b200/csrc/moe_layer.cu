@@ -58,6 +58,7 @@ struct moe_layer {
     cudaEvent_t stage_ev[MOE_NUM_STAGES + 1];
     bool timing;
     // workspace layout (byte offsets)
+    size_t off_bcounts, bcounts_bytes;
     size_t off_rms, off_n, off_logits, off_xq, off_xs, off_idx, off_w, off_counts, off_start, off_total, off_pos, off_rowtok,
         off_xp, off_xps, off_hq, off_hs, off_y, bytes;
     int xs_ld, rcap;
@@ -93,6 +94,8 @@ void plan_workspace(moe_layer* L) {
     size_t o = 0;
     auto take = [&o](size_t bytes) { size_t at = o; o = align_up(o + bytes, 256); return at; };
     L->off_rms = take(T * 4);
+    L->bcounts_bytes = moe_permute_mb_scratch_bytes(static_cast<int>(T), c.top_k, 0, c.num_experts);
+    L->off_bcounts = take(L->bcounts_bytes);
     L->off_n = take(T * H * 4);
     L->off_logits = take(T * static_cast<size_t>(c.num_experts) * 4);
     L->off_xq = take(T * H);
@@ -187,8 +190,8 @@ moe_status_t run_experts(moe_layer* L, const void* x, const int32_t* idx, const 
     int32_t* pos = at<int32_t>(ws, L->off_pos);
     int32_t* rowtok = at<int32_t>(ws, L->off_rowtok);
     mark(L, 2, st);
-    MOE_TRY(moe_permute(idx, T, K, L->e_begin, L->e_end, S, counts, start, pos, rowtok, total, L->rcap,
-                        L->error_word, st));
+    MOE_TRY(moe_permute_mb(idx, T, K, L->e_begin, L->e_end, S, counts, start, pos, rowtok, total, L->rcap,
+                           L->error_word, 16, at<void>(ws, L->off_bcounts), L->bcounts_bytes, st));
     mark(L, 3, st);
     MOE_TRY(moe_gather_rows_n(at<void>(ws, L->off_xq), at<float>(ws, L->off_xs), L->xs_ld, rowtok, total, L->rcap, H,
                               at<void>(ws, L->off_xp), at<float>(ws, L->off_xps), L->rcap, st));
@@ -232,8 +235,8 @@ moe_status_t run_experts_ep(moe_layer* L, const int32_t* idx, const float* wts, 
         const uint32_t epoch = ++L->epoch;
         const int y_cap = c.max_tokens * K;
         mark(L, 2, st);
-        MOE_TRY(moe_permute_padded(idx, T, K, 0, E, 0, ecounts, at<int32_t>(ws, L->off_estart), spos, stok, stotal,
-                                   T * K, L->error_word, 1, st));
+        MOE_TRY(moe_permute_mb(idx, T, K, 0, E, 0, ecounts, at<int32_t>(ws, L->off_estart), spos, stok, stotal,
+                                   T * K, L->error_word, 1, at<void>(ws, L->off_bcounts), L->bcounts_bytes, st));
         MOE_TRY(tbep::counts(P, ecounts, epoch, plan, rcounts, L->error_word, st));
         mark(L, 3, st);
         MOE_TRY(tbep::dispatch(P, at<void>(ws, L->off_xq), at<float>(ws, L->off_xs), L->xs_ld, stok, plan, H, rb,
@@ -259,8 +262,8 @@ moe_status_t run_experts_ep(moe_layer* L, const int32_t* idx, const float* wts, 
     }
 
     mark(L, 2, st);
-    MOE_TRY(moe_permute_padded(idx, T, K, 0, E, 0, ecounts, at<int32_t>(ws, L->off_estart), spos, stok, stotal,
-                               T * K, L->error_word, 1, st));
+    MOE_TRY(moe_permute_mb(idx, T, K, 0, E, 0, ecounts, at<int32_t>(ws, L->off_estart), spos, stok, stotal,
+                               T * K, L->error_word, 1, at<void>(ws, L->off_bcounts), L->bcounts_bytes, st));
     MOE_TRY(moe_ep_pack_rows(at<void>(ws, L->off_xq), at<float>(ws, L->off_xs), L->xs_ld, stok, stotal, T * K, H,
                              at<void>(ws, L->off_psend), st));
     std::vector<size_t> cc(ep, static_cast<size_t>(epr)), co(ep);

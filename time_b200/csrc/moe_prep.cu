@@ -441,6 +441,125 @@ permute_kernel(const int32_t* __restrict__ idx, int T, int K, int e_begin, int e
     }
 }
 
+// ---------------------------------------------------------------- multi-block permutation
+// The same stable counting sort as permute_kernel, spread over many blocks:
+//   mp_count:   block b counts the local-expert pairs of its 256 pairs;
+//   mp_scan:    one block turns the [block][group] counts into each block's
+//               first row per group (exclusive over blocks), the segment
+//               starts (padded) and the capacity check, and resets row_token;
+//   mp_scatter: block b ranks its pairs per group (warp match_any + a
+//               [warp][group] table, stable in pair order) and writes pos and
+//               row_token from its block offsets.
+// Results are identical to permute_kernel.
+constexpr int kMpPairs = 256;   // pairs per block (one per thread)
+
+__global__ void __launch_bounds__(kMpPairs)
+mp_count_kernel(const int32_t* __restrict__ idx, int P, int e_begin, int e_end, int32_t* __restrict__ bcounts) {
+    extern __shared__ int mp_sh[];
+    const int Gr = e_end - e_begin;
+    for (int g = threadIdx.x; g < Gr; g += kMpPairs) mp_sh[g] = 0;
+    __syncthreads();
+    const int p = blockIdx.x * kMpPairs + threadIdx.x;
+    if (p < P) {
+        const int e = idx[p];
+        if (e >= e_begin && e < e_end) atomicAdd(&mp_sh[e - e_begin], 1);
+    }
+    __syncthreads();
+    for (int g = threadIdx.x; g < Gr; g += kMpPairs) bcounts[static_cast<size_t>(blockIdx.x) * Gr + g] = mp_sh[g];
+}
+
+__global__ void __launch_bounds__(1024)
+mp_scan_kernel(int32_t* __restrict__ bcounts, int nblocks, int Gr, int num_shared, int T, int pad,
+               int32_t* __restrict__ counts, int32_t* __restrict__ seg_start, int32_t* __restrict__ total_rows,
+               int32_t* __restrict__ row_token, int row_capacity, int* __restrict__ error_word) {
+    extern __shared__ int mp_sh[];
+    const int G = Gr + num_shared;
+    int* cnt = mp_sh;          // [G]
+    int* start = cnt + G;      // [G]
+    __shared__ int s_total;
+    const int tid = threadIdx.x;
+    for (int g = tid; g < Gr; g += blockDim.x) {
+        int run = 0;
+        for (int b = 0; b < nblocks; ++b) {
+            int32_t* c = bcounts + static_cast<size_t>(b) * Gr + g;
+            const int v = *c;
+            *c = run;                 // this block's first rank within group g
+            run += v;
+        }
+        cnt[g] = run;
+    }
+    for (int g = Gr + tid; g < G; g += blockDim.x) cnt[g] = T;
+    __syncthreads();
+    if (tid < 32) {
+        const int lane = tid;
+        const int per = (G + 31) / 32;
+        int local = 0;
+        for (int i = 0; i < per; ++i) {
+            const int g = lane * per + i;
+            if (g < G) local += (cnt[g] + pad - 1) / pad * pad;
+        }
+        int incl = local;
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        int run = incl - local;
+        for (int i = 0; i < per; ++i) {
+            const int g = lane * per + i;
+            if (g < G) { start[g] = run; run += (cnt[g] + pad - 1) / pad * pad; }
+        }
+        if (lane == 31) s_total = incl;
+    }
+    __syncthreads();
+    const int R = s_total;
+    if (R > row_capacity) {
+        // refuse: zero counts so no downstream kernel touches rows past capacity
+        for (int g = tid; g < G; g += blockDim.x) { counts[g] = 0; seg_start[g] = 0; }
+        if (tid == 0) { *total_rows = -1; if (error_word) atomicExch(error_word, 2); }
+        return;
+    }
+    for (int g = tid; g < G; g += blockDim.x) { counts[g] = cnt[g]; seg_start[g] = start[g]; }
+    if (tid == 0) *total_rows = R;
+    for (int r = tid; r < R; r += blockDim.x) row_token[r] = -1;
+    __syncthreads();     // every reset lands before the shared-expert rows are written
+    for (int g = Gr; g < G; ++g)
+        for (int t = tid; t < T; t += blockDim.x) row_token[start[g] + t] = t;
+}
+
+__global__ void __launch_bounds__(kMpPairs)
+mp_scatter_kernel(const int32_t* __restrict__ idx, int P, int K, int e_begin, int e_end,
+                  const int32_t* __restrict__ bcounts, const int32_t* __restrict__ seg_start,
+                  int32_t* __restrict__ total_rows, int32_t* __restrict__ pos, int32_t* __restrict__ row_token) {
+    extern __shared__ int mp_sh[];
+    const int Gr = e_end - e_begin;
+    int* wtab = mp_sh;     // [8 warps][Gr]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int p = blockIdx.x * kMpPairs + tid;
+    const bool refused = *total_rows < 0;
+    for (int i = tid; i < 8 * Gr; i += kMpPairs) wtab[i] = 0;
+    __syncthreads();
+    int g = -1;
+    if (p < P && !refused) {
+        const int e = idx[p];
+        if (e >= e_begin && e < e_end) g = e - e_begin;
+    }
+    const unsigned m = __match_any_sync(0xffffffffu, g);
+    const int rank = __popc(m & ((1u << lane) - 1u));
+    if (g >= 0 && rank == 0) wtab[warp * Gr + g] = __popc(m);
+    __syncthreads();
+    if (p < P) {
+        if (g >= 0) {
+            int base = seg_start[g] + bcounts[static_cast<size_t>(blockIdx.x) * Gr + g];
+            for (int w = 0; w < warp; ++w) base += wtab[w * Gr + g];
+            const int r = base + rank;
+            pos[p] = r;
+            row_token[r] = p / K;
+        } else {
+            pos[p] = -1;
+        }
+    }
+}
+
 // ---------------------------------------------------------------- gather
 __global__ void __launch_bounds__(256)
 gather_rows_kernel(const uint8_t* __restrict__ xq, const float* __restrict__ xs, int xs_ld,
@@ -641,6 +760,36 @@ moe_status_t moe_permute(const int32_t* topk_idx, int T, int k, int e_begin, int
                          int* error_word, cwStream_t stream) {
     return moe_permute_padded(topk_idx, T, k, e_begin, e_end, num_shared, counts, seg_start, pos, row_token,
                               total_rows, row_capacity, error_word, kRowPad, stream);
+}
+
+size_t moe_permute_mb_scratch_bytes(int T, int k, int e_begin, int e_end) {
+    if (T < 0 || k <= 0 || e_end <= e_begin) return 0;
+    const size_t nb = (static_cast<size_t>(T) * k + kMpPairs - 1) / kMpPairs;
+    return nb * static_cast<size_t>(e_end - e_begin) * sizeof(int32_t);
+}
+
+moe_status_t moe_permute_mb(const int32_t* topk_idx, int T, int k, int e_begin, int e_end, int num_shared,
+                            int32_t* counts, int32_t* seg_start, int32_t* pos, int32_t* row_token,
+                            int32_t* total_rows, int row_capacity, int* error_word, int pad, void* scratch,
+                            size_t scratch_bytes, cwStream_t stream) {
+    const int Gr = e_end - e_begin;
+    const int G = Gr + num_shared;
+    if (T < 0 || k <= 0 || e_begin < 0 || Gr <= 0 || num_shared < 0 || G > 1024 || pad < 1 || pad > 128)
+        return MOE_ERR_INVALID_ARGUMENT;
+    if (!topk_idx || !counts || !seg_start || !pos || !row_token || !total_rows || row_capacity < 0 || !scratch)
+        return MOE_ERR_INVALID_ARGUMENT;
+    if (scratch_bytes < moe_permute_mb_scratch_bytes(T, k, e_begin, e_end)) return MOE_ERR_WORKSPACE;
+    const int P = T * k;
+    const int nb = (P + kMpPairs - 1) / kMpPairs;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int32_t* bc = static_cast<int32_t*>(scratch);
+    if (nb > 0) mp_count_kernel<<<nb, kMpPairs, Gr * sizeof(int), st>>>(topk_idx, P, e_begin, e_end, bc);
+    mp_scan_kernel<<<1, 1024, 2 * G * sizeof(int), st>>>(bc, nb, Gr, num_shared, T, pad, counts, seg_start,
+                                                         total_rows, row_token, row_capacity, error_word);
+    if (nb > 0)
+        mp_scatter_kernel<<<nb, kMpPairs, 8 * Gr * sizeof(int), st>>>(topk_idx, P, k, e_begin, e_end, bc, seg_start,
+                                                                       total_rows, pos, row_token);
+    return launch_status();
 }
 
 moe_status_t moe_gather_rows_n(const void* xq, const float* xs, int xs_ld, const int32_t* row_token,

@@ -94,6 +94,10 @@ def libs():
         k.moe_layer_peer_bytes.argtypes = [c_void_p]
         k.moe_layer_peer_bytes.restype = c_size_t
         k.moe_layer_set_peer_buffers.argtypes = [c_void_p, c_void_p, c_int]
+        k.moe_permute_mb_scratch_bytes.argtypes = [c_int, c_int, c_int, c_int]
+        k.moe_permute_mb_scratch_bytes.restype = c_size_t
+        k.moe_permute_mb.argtypes = [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p,
+                                     c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_size_t, c_void_p]
         k.moe_ep_row_bytes.argtypes = [c_int]
         k.moe_ep_row_bytes.restype = c_size_t
         sz_p = ctypes.POINTER(c_size_t)
