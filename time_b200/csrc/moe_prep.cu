@@ -239,37 +239,43 @@ router_topk_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict_
 // ---------------------------------------------------------------- tiled router
 // logits[t][e] = (fma chain over k = 0..H-1 of n[t][k] * W[e][k], from +0.0f)
 // + bias[e]: the same per-(t, e) order as router_topk_kernel, laid out for
-// throughput instead of one block per 32 tokens.  Block: 16 tokens x 32
-// experts, 128 threads; thread (tp = lane & 7, ep = (lane >> 3) + 4 * warp)
-// owns tokens tp, tp+8 x experts ep, ep+16 (four independent chains, two
-// fma.rn.f32x2 per k).  K is staged through shared memory in chunks of 128
-// with cp.async double buffering; rows are padded by 4 floats (row r starts
-// at bank 4r mod 32), so the eight token rows tp and the four expert rows ep a
-// warp reads per 16-byte load land in distinct banks.  Grid: (expert tiles, token tiles) -- the expert tiles
-// of one token tile run back to back and share its n rows in L2.
-constexpr int kRtTok = 16, kRtExp = 32, kRtKC = 128, kRtLd = kRtKC + 4, kRtThreads = 128;
-constexpr size_t kRtSmem = 2 * (kRtTok + kRtExp) * kRtLd * sizeof(float);   // 50,688 B: 4 blocks per SM
+// throughput instead of one block per 32 tokens.
+// Scalar-FMA form of the same chains (what moe_router_logits runs): thread
+// tile TI tokens x 4 experts, so one 16-byte load of a token row (four k
+// steps) and of an expert row feed 4*TI FMAs each -- about 1.1 instructions
+// per FMA, against ~2.4 for the packed form whose operand pairs cost register
+// moves.  Block: 128 threads, 16*TI tokens x 32 experts; thread
+// (tg = (lane & 3) + 4 * warp, eg = lane >> 2) owns tokens tg + 16 i and
+// experts eg + 8 j, so the 4 token rows and 8 expert rows a warp reads per
+// load sit in distinct banks (row pitch 68 floats: row r at bank 4r).  K in
+// chunks of 64 through a cp.async double buffer.  Each chain still advances
+// one fma per k in ascending k from +0.0f: bit-identical logits.
+constexpr int kR3Exp = 32, kR3KC = 64, kR3Ld = kR3KC + 4, kR3Threads = 128;
 
-__global__ void __launch_bounds__(kRtThreads, 4)
-router_logits_kernel(const float* __restrict__ n, const float* __restrict__ W, const float* __restrict__ bias,
-                     int T, int H, int E, float* __restrict__ logits) {
-    extern __shared__ __align__(16) float rt_smem[];
-    auto n_s = reinterpret_cast<float (*)[kRtTok][kRtLd]>(rt_smem);                       // [2][16][132]
-    auto w_s = reinterpret_cast<float (*)[kRtExp][kRtLd]>(rt_smem + 2 * kRtTok * kRtLd);  // [2][32][132]
+template <int TI>
+constexpr size_t r3_smem_bytes() { return 2 * static_cast<size_t>(16 * TI + kR3Exp) * kR3Ld * sizeof(float); }
+
+template <int TI>
+__global__ void __launch_bounds__(kR3Threads, 4)
+router_logits_tile_kernel(const float* __restrict__ n, const float* __restrict__ W, const float* __restrict__ bias,
+                          int T, int H, int E, float* __restrict__ logits) {
+    constexpr int TT = 16 * TI;
+    extern __shared__ __align__(16) float r3_smem[];
+    auto n_s = reinterpret_cast<float (*)[TT][kR3Ld]>(r3_smem);                          // [2][TT][68]
+    auto w_s = reinterpret_cast<float (*)[kR3Exp][kR3Ld]>(r3_smem + 2 * TT * kR3Ld);   // [2][32][68]
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int e0 = blockIdx.x * kRtExp, t0 = blockIdx.y * kRtTok;
-    const int tp = lane & 7, ep = (lane >> 3) + 4 * warp;
+    const int tg = (lane & 3) + 4 * warp, eg = lane >> 2;
+    const int t0 = blockIdx.y * TT, e0 = blockIdx.x * kR3Exp;
 
     auto load = [&](int stage, int k0) {
-        // 48 rows x 32 chunks of 16 bytes; rows past T / E are zero-filled
-        for (int c = tid; c < (kRtTok + kRtExp) * (kRtKC / 4); c += kRtThreads) {
-            const int row = c >> 5, q = c & 31;
-            if (row < kRtTok) {
+        for (int c = tid; c < (TT + kR3Exp) * (kR3KC / 4); c += kR3Threads) {
+            const int row = c >> 4, q = c & 15;
+            if (row < TT) {
                 const int t = t0 + row;
                 const float* src = n + static_cast<size_t>(t < T ? t : 0) * H + k0 + q * 4;
                 cp_async16(&n_s[stage][row][q * 4], src, t < T ? 16u : 0u);
             } else {
-                const int r = row - kRtTok, e = e0 + r;
+                const int r = row - TT, e = e0 + r;
                 const float* src = W + static_cast<size_t>(e < E ? e : 0) * H + k0 + q * 4;
                 cp_async16(&w_s[stage][r][q * 4], src, e < E ? 16u : 0u);
             }
@@ -277,50 +283,48 @@ router_logits_kernel(const float* __restrict__ n, const float* __restrict__ W, c
         cp_async_commit();
     };
 
-    float2 acc0 = make_float2(0.0f, 0.0f);   // token tp:   experts ep, ep+16
-    float2 acc1 = make_float2(0.0f, 0.0f);   // token tp+8: experts ep, ep+16
-    const int nchunks = H / kRtKC;
+    float acc[TI][4];
+#pragma unroll
+    for (int i = 0; i < TI; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+    const int nchunks = H / kR3KC;
     load(0, 0);
     for (int c = 0; c < nchunks; ++c) {
         if (c + 1 < nchunks) {
-            load((c + 1) & 1, (c + 1) * kRtKC);
+            load((c + 1) & 1, (c + 1) * kR3KC);
             cp_async_wait<1>();
         } else {
             cp_async_wait<0>();
         }
         __syncthreads();
-        const int s = c & 1;
-        const float* na = &n_s[s][tp][0];
-        const float* nb = &n_s[s][tp + 8][0];
-        const float* wa = &w_s[s][ep][0];
-        const float* wb = &w_s[s][ep + 16][0];
-#pragma unroll 8
-        for (int kk = 0; kk < kRtKC; kk += 4) {
-            const float4 a = *reinterpret_cast<const float4*>(na + kk);
-            const float4 b = *reinterpret_cast<const float4*>(nb + kk);
-            const float4 u = *reinterpret_cast<const float4*>(wa + kk);
-            const float4 v = *reinterpret_cast<const float4*>(wb + kk);
-            acc0 = ffma2(make_float2(a.x, a.x), make_float2(u.x, v.x), acc0);
-            acc1 = ffma2(make_float2(b.x, b.x), make_float2(u.x, v.x), acc1);
-            acc0 = ffma2(make_float2(a.y, a.y), make_float2(u.y, v.y), acc0);
-            acc1 = ffma2(make_float2(b.y, b.y), make_float2(u.y, v.y), acc1);
-            acc0 = ffma2(make_float2(a.z, a.z), make_float2(u.z, v.z), acc0);
-            acc1 = ffma2(make_float2(b.z, b.z), make_float2(u.z, v.z), acc1);
-            acc0 = ffma2(make_float2(a.w, a.w), make_float2(u.w, v.w), acc0);
-            acc1 = ffma2(make_float2(b.w, b.w), make_float2(u.w, v.w), acc1);
+        const int st = c & 1;
+#pragma unroll 4
+        for (int kk = 0; kk < kR3KC; kk += 4) {
+            float4 a[TI], b[4];
+#pragma unroll
+            for (int i = 0; i < TI; ++i) a[i] = *reinterpret_cast<const float4*>(&n_s[st][tg + 16 * i][kk]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) b[j] = *reinterpret_cast<const float4*>(&w_s[st][eg + 8 * j][kk]);
+#pragma unroll
+            for (int i = 0; i < TI; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    acc[i][j] = __fmaf_rn(a[i].x, b[j].x, acc[i][j]);
+                    acc[i][j] = __fmaf_rn(a[i].y, b[j].y, acc[i][j]);
+                    acc[i][j] = __fmaf_rn(a[i].z, b[j].z, acc[i][j]);
+                    acc[i][j] = __fmaf_rn(a[i].w, b[j].w, acc[i][j]);
+                }
         }
         __syncthreads();
     }
-    const int ta = t0 + tp, ea = e0 + ep;
-    const float ba = (bias && ea < E) ? bias[ea] : 0.0f;
-    const float bb = (bias && ea + 16 < E) ? bias[ea + 16] : 0.0f;
-    auto put = [&](int t, int e, float v, float b) {
-        if (t < T && e < E) logits[static_cast<size_t>(t) * E + e] = bias ? __fadd_rn(v, b) : v;
-    };
-    put(ta, ea, acc0.x, ba);
-    put(ta, ea + 16, acc0.y, bb);
-    put(ta + 8, ea, acc1.x, ba);
-    put(ta + 8, ea + 16, acc1.y, bb);
+#pragma unroll
+    for (int i = 0; i < TI; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int t = t0 + tg + 16 * i, e = e0 + eg + 8 * j;
+            if (t < T && e < E) logits[static_cast<size_t>(t) * E + e] = bias ? __fadd_rn(acc[i][j], bias[e]) : acc[i][j];
+        }
 }
 
 // Top-k + softmax of the selected logits, one warp per token (8 tokens per
@@ -667,20 +671,32 @@ moe_status_t moe_rmsnorm_quant(const void* x_bf16, const float* gamma, int T, in
 
 moe_status_t moe_router_logits(const float* n, const float* router_w, const float* router_bias, int T, int H,
                                int E, float* logits, cwStream_t stream) {
-    if (T < 0 || H <= 0 || H % kRtKC || E <= 0 || E > 256) return MOE_ERR_INVALID_ARGUMENT;
+    if (T < 0 || H <= 0 || H % 128 || E <= 0 || E > 256) return MOE_ERR_INVALID_ARGUMENT;
     if (T == 0) return MOE_OK;
     if (!n || !router_w || !logits || !aligned16(n) || !aligned16(router_w)) return MOE_ERR_INVALID_ARGUMENT;
-    const dim3 grid((E + kRtExp - 1) / kRtExp, (T + kRtTok - 1) / kRtTok);
+    // tokens per thread: the largest tile that still gives two blocks per SM
+    // (one for small T)
+    const int etiles = (E + kR3Exp - 1) / kR3Exp;
+    const int ti = ((T + 63) / 64) * etiles >= 2 * 148 ? 4 : (((T + 31) / 32) * etiles >= 148 ? 2 : 1);
+    const dim3 grid(etiles, (T + 16 * ti - 1) / (16 * ti));
     if (grid.y > 65535) return MOE_ERR_UNSUPPORTED;
     static bool attr = false;
     if (!attr) {
-        if (cudaFuncSetAttribute(router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(kRtSmem)) != cudaSuccess)
+        if (cudaFuncSetAttribute(router_logits_tile_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(r3_smem_bytes<4>())) != cudaSuccess)
             return MOE_ERR_CUDA;
         attr = true;
     }
-    router_logits_kernel<<<grid, kRtThreads, kRtSmem, static_cast<cudaStream_t>(stream)>>>(n, router_w, router_bias,
-                                                                                           T, H, E, logits);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (ti == 4)
+        router_logits_tile_kernel<4><<<grid, kR3Threads, r3_smem_bytes<4>(), st>>>(n, router_w, router_bias, T, H, E,
+                                                                                   logits);
+    else if (ti == 2)
+        router_logits_tile_kernel<2><<<grid, kR3Threads, r3_smem_bytes<2>(), st>>>(n, router_w, router_bias, T, H, E,
+                                                                                   logits);
+    else
+        router_logits_tile_kernel<1><<<grid, kR3Threads, r3_smem_bytes<1>(), st>>>(n, router_w, router_bias, T, H, E,
+                                                                                   logits);
     return launch_status();
 }
 
