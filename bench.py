@@ -47,6 +47,8 @@ def parse():
                     help="routed experts (profiling captures of a smaller case only; the metric uses 160)")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
                     help="expert-parallel exchange for N > 1: NVLink peer memory (own kernels) or NCCL send/recv")
+    ap.add_argument("--placement", choices=["balanced", "contiguous"], default="balanced",
+                    help="expert placement for N > 1: load-balanced from a calibration batch, or contiguous slices")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -258,7 +260,13 @@ def run_ours(args):
         raise SystemExit(f"{shape.num_experts} experts do not split over {world} ranks")
     T = args.tokens
     w_all = synth.make_moe_weights(shape, seed=0, device=dev, zipf_bias=True)
-    w = synth.expert_slice(w_all, shape, world, rank) if world > 1 else w_all
+    placement = None
+    if world > 1 and args.placement == "balanced":
+        # per-expert load measured on a calibration batch (not the timed tokens), the same table on every rank
+        load = M.router_load(shape, w_all, synth.make_x(shape, 4096, seed=9, device=dev)).to(dev)
+        dist.broadcast(load, src=0)
+        placement = synth.balanced_placement(load.cpu().tolist(), world)
+    w = synth.expert_slice(w_all, shape, world, rank, slot_of_expert=placement) if world > 1 else w_all
     del w_all
     x_all = synth.make_x(shape, T, seed=1, device=dev)
     t0, t1 = synth.token_slice(T, world, rank)
@@ -268,6 +276,8 @@ def run_ours(args):
     max_tokens = -(-T // world)
     out = torch.empty_like(x)
     layer = M.MoELayer(shape, w, max_tokens=max_tokens, ep_size=world, ep_rank=rank, comm=comm)
+    if placement is not None:
+        layer.set_expert_placement(placement)
     if world > 1 and args.exchange == "peer":
         layer.use_peer_memory()
     stream = torch.cuda.current_stream()
@@ -310,6 +320,11 @@ def run_ours(args):
     for s_, name in enumerate(M.STAGE_NAMES):
         stages[name] = statistics.mean(stage_ev[i][s_].elapsed_time(stage_ev[i][s_ + 1]) for i in range(K))
     clocks = clk.summary()
+    stages_max = stages
+    if world > 1:
+        t = torch.tensor([stages[n] for n in M.STAGE_NAMES], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        stages_max = dict(zip(M.STAGE_NAMES, t.tolist()))
 
     # ---- end to end through the public call with host buffers
     x_host = x.cpu().pin_memory()
@@ -354,11 +369,19 @@ def run_ours(args):
     if world > 1:
         lb += (shape.num_experts - G_local) * shape.hidden * 4      # router weights are replicated
         lf += 2.0 * Tr * shape.hidden * (shape.num_experts - G_local)
-    e_lo, e_hi = rank * G_local, (rank + 1) * G_local
     idx_h = idx.flatten().tolist()
-    own_local = sum(1 for e in idx_h if e_lo <= e < e_hi)
+    owner = [(placement[e] if placement else e) // G_local for e in range(shape.num_experts)]
+    own_local = sum(1 for e in idx_h if e >= 0 and owner[e] == rank)
     sent_remote = sum(1 for e in idx_h if e >= 0) - own_local
-    recv_remote = int(sum(counts[:G_local].tolist())) - own_local
+    routed_rows = int(sum(counts[:G_local].tolist()))
+    recv_remote = routed_rows - own_local
+    rows_max = rows_mean = routed_rows
+    if world > 1:
+        t = torch.tensor([routed_rows, routed_rows], dtype=torch.float64, device=dev)
+        tm = t.clone()
+        dist.all_reduce(t[:1], op=dist.ReduceOp.MAX)
+        dist.all_reduce(tm[1:], op=dist.ReduceOp.SUM)
+        rows_max, rows_mean = int(t[0].item()), float(tm[1].item()) / world
     rb = M.libs()["libkernels.so"].moe_ep_row_bytes(shape.hidden)
     a2a_bytes = max(sent_remote * rb + recv_remote * shape.hidden * 2,
                     recv_remote * rb + sent_remote * shape.hidden * 2) if world > 1 else 0
@@ -394,6 +417,9 @@ def run_ours(args):
                        "hidden": shape.hidden, "experts": shape.num_experts, "top_k": shape.top_k,
                        "intermediate": shape.intermediate, "shared_experts": shape.num_shared,
                        "router": "fp32 softmax top-k, zipf(1.1) bias", "parallelism": f"ep{world}",
+                       "expert_placement": ((args.placement + (" (greedy by routed pairs of a separate 4096-token "
+                                                                "calibration batch)" if placement else ""))
+                                            if world > 1 else None),
                        "dispatch": (("fp8 rows + 1x128 scales, combine bf16, " +
                                      ("NVLink peer-memory stores from own kernels, no host sync"
                                       if args.exchange == "peer" else "NCCL send/recv, one host sync"))
@@ -404,6 +430,8 @@ def run_ours(args):
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
             "roofline": roofline, "layer_roofline": layer_roofline,
             "stages_ms_rank0": stages, "rows_rank0": work["rows"],
+            "stages_ms_max_over_ranks": stages_max,
+            "routed_rows_per_rank": {"max": rows_max, "mean": rows_mean},
             "expert_tokens_rank0": {"max": int(counts[:G_local].max()), "min": int(counts[:G_local].min()),
                                     "mean": float(counts[:G_local].float().mean())},
             "gpu_launches": K * launches_per_step, "clocks": clocks, "cpu_baseline": cpu}

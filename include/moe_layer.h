@@ -138,6 +138,18 @@ moe_status_t moe_layer_set_stage_events(moe_layer_t* layer, cwEvent_t* events);
 size_t moe_layer_peer_bytes(const moe_layer_t* layer);
 moe_status_t moe_layer_set_peer_buffers(moe_layer_t* layer, void* const* peer_bufs, int n);
 
+/* Which rank computes which routed expert (ep_size > 1).  slot_of_expert
+ * (host, [E]) is a permutation of 0..E-1: expert e is computed by rank
+ * slot / (E/ep_size) as its local expert slot % (E/ep_size); the rank's w13 /
+ * s13 / w2 / s2 then hold its experts in local-slot order (then the shared
+ * expert).  Every rank must set the same permutation.  The default is the
+ * contiguous placement of the spec's shard_experts (slot = e); a placement
+ * that spreads the frequently routed experts evens the ranks' work.  Outputs
+ * do not change: every expert row is computed the same way wherever it runs.
+ * Copies the table to the device (the one allocation, freed by
+ * moe_layer_destroy); NULL restores the contiguous placement. */
+moe_status_t moe_layer_set_expert_placement(moe_layer_t* layer, const int32_t* slot_of_expert);
+
 /* Reads and clears the device error word (synchronises `stream`). */
 moe_status_t moe_layer_check_error(moe_layer_t* layer, cwStream_t stream);
 
@@ -301,6 +313,11 @@ moe_status_t moe_ep_recv_plan(const int32_t* recv_counts, int ep_size, int exper
 moe_status_t moe_ep_gather(const void* packed, const void* xq, const float* xs, int xs_ld,
                            const int32_t* row_src, const int32_t* total_rows, int row_capacity,
                            int H, void* xp, float* xps, int xps_ld, cwStream_t stream);
+
+/* vidx[p] = slot_of_expert[topk_idx[p]] for 0 <= topk_idx[p] < E, else -1
+ * (num_pairs = T * k; device arrays). */
+moe_status_t moe_ep_remap_experts(const int32_t* topk_idx, int num_pairs, int E,
+                                  const int32_t* slot_of_expert, int32_t* vidx, cwStream_t stream);
 
 /* ysend[i] = y[recv_dst[i]] for i < n (bf16 rows of H). */
 moe_status_t moe_ep_pack_y(const void* y_bf16, const int32_t* recv_dst, int n, int H,

@@ -30,6 +30,7 @@ def main() -> int:
     ap.add_argument("--uniform-logits", action="store_true")
     ap.add_argument("--repeats", type=int, default=2)
     ap.add_argument("--exchange", choices=["nccl", "peer"], default="nccl")
+    ap.add_argument("--placement", choices=["contiguous", "balanced"], default="contiguous")
     a = ap.parse_args()
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -47,8 +48,16 @@ def main() -> int:
         top = torch.topk(logits, shape.top_k, dim=1)
         routing = (top.indices.to(torch.int32).contiguous(), torch.softmax(top.values, dim=1).contiguous())
     t0, t1 = synth.token_slice(T, world, rank)
-    w = synth.expert_slice(w_all, shape, world, rank)
+    placement = None
+    if a.placement == "balanced":
+        # load measured on a calibration batch on rank 0, the same table everywhere
+        load = M.router_load(shape, w_all, synth.make_x(shape, 1024, seed=9, device=dev)).to(dev)
+        dist.broadcast(load, src=0)
+        placement = synth.balanced_placement(load.cpu().tolist(), world)
+    w = synth.expert_slice(w_all, shape, world, rank, slot_of_expert=placement)
     layer = M.MoELayer(shape, w, max_tokens=-(-T // world), ep_size=world, ep_rank=rank, comm=comm)
+    if placement is not None:
+        layer.set_expert_placement(placement)
     if a.exchange == "peer":
         layer.use_peer_memory()
     x = x_all[t0:t1].contiguous()

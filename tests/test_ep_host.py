@@ -125,3 +125,36 @@ def test_plan_host_offsets():
     srows, soff, rrows, roff, st, rt = M.ep_plan_host(3, 2, [1, 2, 0, 0, 5, 1], [3, 0, 1, 1, 0, 2])
     assert srows == [3, 0, 6] and soff == [0, 3, 3] and st == 9
     assert rrows == [3, 2, 2] and roff == [0, 3, 5] and rt == 7
+
+
+def test_balanced_placement_is_even_permutation():
+    import random
+    from time_b200 import synth
+    rng = random.Random(3)
+    E, ep = 160, 8
+    load = [int(1000 * rng.random() ** 4) for _ in range(E)]
+    slot = synth.balanced_placement(load, ep)
+    assert sorted(slot) == list(range(E))
+    per = E // ep
+    rank_load = [sum(load[e] for e in range(E) if slot[e] // per == r) for r in range(ep)]
+    contiguous = [sum(load[r * per:(r + 1) * per]) for r in range(ep)]
+    assert max(rank_load) <= max(contiguous)
+    assert max(rank_load) - min(rank_load) <= max(load)       # LPT bound with equal slot counts
+    # within a rank the experts keep ascending order
+    for r in range(ep):
+        mine = sorted((slot[e], e) for e in range(E) if slot[e] // per == r)
+        assert [e for _, e in mine] == sorted(e for _, e in mine)
+
+
+def test_expert_slice_follows_placement():
+    import torch
+    from time_b200 import synth
+    shape = synth.TINY
+    w = synth.make_moe_weights(shape, seed=0)
+    slot = [3, 0, 6, 1, 4, 7, 2, 5]                 # expert -> slot, 2 ranks of 4 slots
+    for r in range(2):
+        ws = synth.expert_slice(w, shape, 2, r, slot_of_expert=slot)
+        experts = sorted(range(8), key=lambda e: slot[e])[4 * r:4 * r + 4]
+        for j, e in enumerate(experts):
+            assert torch.equal(ws["w13"][j], w["w13"][e]) and torch.equal(ws["s2"][j], w["s2"][e])
+        assert torch.equal(ws["w13"][4], w["w13"][8])          # shared expert last

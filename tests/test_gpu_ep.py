@@ -38,10 +38,11 @@ def single_gpu(shape, w, x):
     return out, idx
 
 
-def ep_emulated(shape, w_all, x, ep, routing=None):
+def ep_emulated(shape, w_all, x, ep, routing=None, placement=None):
     """The EP forward of every rank, with host-planned device copies for the
-    two exchanges.  Returns the concatenated output and each rank's group
-    counts."""
+    two exchanges.  `placement`: expert -> slot permutation (the send order
+    then sorts by slot, as moe_layer_set_expert_placement makes the layer do).
+    Returns the concatenated output and each rank's group counts."""
     k = M.libs()["libkernels.so"]
     dev = x.device
     T, H, I, E, K, S = x.shape[0], shape.hidden, shape.intermediate, shape.num_experts, shape.top_k, shape.num_shared
@@ -49,6 +50,7 @@ def ep_emulated(shape, w_all, x, ep, routing=None):
     Tmax = -(-T // ep)
     rb = k.moe_ep_row_bytes(H)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
+    slot_of = None if placement is None else torch.tensor(placement, dtype=torch.int32, device=dev)
     ranks = []
     # ---- source side: norm, route, sort by expert, pack
     for r in range(ep):
@@ -71,12 +73,16 @@ def ep_emulated(shape, w_all, x, ep, routing=None):
             idx = routing[0][t0:t1].contiguous()
             wts = routing[1][t0:t1].contiguous()
         P = Tr * K
+        sort_ids = idx
+        if slot_of is not None:
+            sort_ids = torch.full((max(Tr, 1), K), -5, dtype=torch.int32, device=dev)
+            M.check("remap", k.moe_ep_remap_experts(M.ptr(idx), P, E, M.ptr(slot_of), M.ptr(sort_ids), st()))
         ecounts = torch.zeros(E, dtype=torch.int32, device=dev)
         estart = torch.zeros(E, dtype=torch.int32, device=dev)
         spos = torch.full((max(P, 1),), -7, dtype=torch.int32, device=dev)
         stok = torch.full((max(P, 1),), -7, dtype=torch.int32, device=dev)
         stotal = torch.zeros(1, dtype=torch.int32, device=dev)
-        M.check("permute_padded", k.moe_permute_padded(M.ptr(idx), Tr, K, 0, E, 0, M.ptr(ecounts), M.ptr(estart),
+        M.check("permute_padded", k.moe_permute_padded(M.ptr(sort_ids), Tr, K, 0, E, 0, M.ptr(ecounts), M.ptr(estart),
                                                        M.ptr(spos), M.ptr(stok), M.ptr(stotal), P, M.ptr(err), 1,
                                                        st()))
         psend = torch.zeros(max(P, 1), rb, dtype=torch.uint8, device=dev)
@@ -106,7 +112,7 @@ def ep_emulated(shape, w_all, x, ep, routing=None):
         rk["precv"] = precv
     # ---- receiving side: plan, gather, GEMMs, pack outputs
     for r, rk in enumerate(ranks):
-        wr = synth.expert_slice(w_all, shape, ep, r)
+        wr = synth.expert_slice(w_all, shape, ep, r, slot_of_expert=placement)
         G = epr + S
         R = ((recv_cap + S * Tmax + 16 * G) + 15) // 16 * 16
         counts = torch.zeros(G, dtype=torch.int32, device=dev)
@@ -203,3 +209,53 @@ def test_ep_emulated_glm_decode_uniform_logits(gpu):
     assert np.array_equal(bits(out), bits(ref))
     hist = torch.cat([c[:shape.num_experts // ep] for c in counts])
     assert int(hist.sum()) == T * shape.top_k
+
+
+def test_remap_experts_matches_table(gpu):
+    k = M.libs()["libkernels.so"]
+    E, T, K = 160, 777, 8
+    g = torch.Generator().manual_seed(11)
+    slot = torch.randperm(E, generator=g).to(torch.int32)
+    idx = torch.randint(0, E, (T, K), generator=g, dtype=torch.int32)
+    idx[5, 3] = -1                                   # an empty slot of a routed token
+    idx[9, 0] = E                                    # out of range: dropped, as the permutation drops it
+    d_idx, d_slot = idx.to(gpu), slot.to(gpu)
+    vidx = torch.full((T, K), -9, dtype=torch.int32, device=gpu)
+    M.check("remap", k.moe_ep_remap_experts(M.ptr(d_idx), T * K, E, M.ptr(d_slot), M.ptr(vidx), st()))
+    torch.cuda.synchronize()
+    valid = (idx >= 0) & (idx < E)
+    ref = torch.where(valid, slot[idx.clamp(0, E - 1).long()], torch.full_like(idx, -1))
+    assert torch.equal(vidx.cpu(), ref)
+
+
+@pytest.mark.parametrize("ep,T", [(2, 64), (4, 37)])
+def test_ep_emulated_placement_tiny_bit_identical(gpu, ep, T):
+    shape = synth.TINY
+    case = synth.make_case(shape, T, seed=5)
+    w = {kk: (v.to(gpu) if isinstance(v, torch.Tensor) else v) for kk, v in case.items()}
+    x = w.pop("x")
+    ref, _ = single_gpu(shape, w, x)
+    g = torch.Generator().manual_seed(ep)
+    placement = torch.randperm(shape.num_experts, generator=g).tolist()
+    out, counts = ep_emulated(shape, w, x, ep, placement=placement)
+    assert np.array_equal(bits(out), bits(ref))
+
+
+def test_ep_emulated_placement_glm_balanced(gpu):
+    """GLM shape, zipf router bias, 8 emulated ranks: the balanced placement
+    computed from a calibration batch evens the ranks' routed rows and keeps
+    the output bit-identical."""
+    shape, ep, T = synth.GLM, 8, 512
+    w = synth.make_moe_weights(shape, seed=0, device=gpu, zipf_bias=True)
+    x = synth.make_x(shape, T, seed=1, device=gpu)
+    ref, _ = single_gpu(shape, w, x)
+    load = M.router_load(shape, w, synth.make_x(shape, 2048, seed=9, device=gpu))
+    placement = synth.balanced_placement(load.tolist(), ep)
+    out_c, counts_c = ep_emulated(shape, w, x, ep)
+    out_b, counts_b = ep_emulated(shape, w, x, ep, placement=placement)
+    assert np.array_equal(bits(out_b), bits(ref))
+    assert np.array_equal(bits(out_c), bits(ref))
+    routed = lambda cs: [int(c[:shape.num_experts // ep].sum()) for c in cs]
+    rc, rb = routed(counts_c), routed(counts_b)
+    assert sum(rc) == sum(rb) == T * shape.top_k
+    assert max(rb) < max(rc)

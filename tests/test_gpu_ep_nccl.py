@@ -50,3 +50,15 @@ def test_ep_bit_identical(gpu, args, exchange):
     nproc = 8 if n >= 8 else (4 if n >= 4 else 2)
     r = launch(nproc, *args, "--exchange", exchange)
     assert r.returncode == 0 and "EP_OK" in r.stdout, (r.stdout[-3000:], r.stderr[-3000:])
+
+
+@pytest.mark.parametrize("exchange", ["nccl", "peer"])
+def test_ep_balanced_placement_bit_identical(gpu, exchange):
+    """Load-aware expert placement (moe_layer_set_expert_placement): same
+    output bits as the single-GPU layer."""
+    n = n_gpus()
+    if n < 2:
+        pytest.skip("needs >= 2 GPUs")
+    nproc = 8 if n >= 8 else (4 if n >= 4 else 2)
+    r = launch(nproc, "--shape", "glm", "--tokens", "2048", "--placement", "balanced", "--exchange", exchange)
+    assert r.returncode == 0 and "EP_OK" in r.stdout, (r.stdout[-3000:], r.stderr[-3000:])

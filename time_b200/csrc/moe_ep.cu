@@ -65,6 +65,15 @@ inline moe_status_t launch_status() {
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+// vidx[p] = slot_of_expert[idx[p]] for valid expert ids, -1 otherwise.
+__global__ void ep_remap_kernel(const int32_t* __restrict__ idx, int P, int E, const int32_t* __restrict__ slot_of,
+                                int32_t* __restrict__ vidx) {
+    for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < P; p += gridDim.x * blockDim.x) {
+        const int e = idx[p];
+        vidx[p] = (e >= 0 && e < E) ? slot_of[e] : -1;
+    }
+}
+
 // One warp per row: 16-byte copies of the FP8 values, one lane per scale.
 __global__ void __launch_bounds__(256)
 ep_pack_rows_kernel(const uint8_t* __restrict__ xq, const float* __restrict__ xs, int xs_ld,
@@ -404,6 +413,17 @@ moe_status_t moe_ep_plan_host(int ep_size, int experts_per_rank, const int32_t* 
     if (send_total) *send_total = so;
     if (recv_total) *recv_total = ro;
     return MOE_OK;
+}
+
+moe_status_t moe_ep_remap_experts(const int32_t* topk_idx, int num_pairs, int E, const int32_t* slot_of_expert,
+                                  int32_t* vidx, cwStream_t stream) {
+    if (num_pairs < 0 || E <= 0) return MOE_ERR_INVALID_ARGUMENT;
+    if (num_pairs == 0) return MOE_OK;
+    if (!topk_idx || !slot_of_expert || !vidx) return MOE_ERR_INVALID_ARGUMENT;
+    int blocks = (num_pairs + 255) / 256;
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    ep_remap_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(topk_idx, num_pairs, E, slot_of_expert, vidx);
+    return launch_status();
 }
 
 moe_status_t moe_ep_pack_rows(const void* xq, const float* xs, int xs_ld, const int32_t* row_token,

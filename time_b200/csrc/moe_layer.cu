@@ -64,12 +64,13 @@ struct moe_layer {
     int xs_ld, rcap;
     // expert parallelism
     size_t off_ecounts, off_estart, off_stotal, off_stok, off_psend, off_precv, off_rdst, off_ysend, off_yrecv;
-    size_t row_bytes;
+    size_t row_bytes, off_vidx;
     int recv_cap;
     int32_t* h_counts;    // pinned [2E]
     int sync_timeout_ms;
     // peer-memory exchange (moe_layer_set_peer_buffers)
     bool peer_mode;
+    int32_t* slot_of_expert;   // device [E] or NULL (contiguous placement)
     tbep::Peers peers;
     uint32_t epoch;
     size_t off_plan;
@@ -124,6 +125,7 @@ void plan_workspace(moe_layer* L) {
         L->off_ysend = take(RC * H * 2);
         L->off_yrecv = take(T * K * H * 2);
         L->off_plan = take(tbep::plan_ints(c.ep_size) * 4);
+        L->off_vidx = take(T * K * 4);
     }
     L->bytes = o;
 }
@@ -226,6 +228,13 @@ moe_status_t run_experts_ep(moe_layer* L, const int32_t* idx, const float* wts, 
     int32_t* row_src = at<int32_t>(ws, L->off_rowtok);
     int32_t* recv_dst = at<int32_t>(ws, L->off_rdst);
     const size_t rb = L->row_bytes;
+    // expert placement: the send order sorts by virtual expert (rank-major)
+    const int32_t* sort_ids = idx;
+    if (L->slot_of_expert) {
+        int32_t* vidx = at<int32_t>(ws, L->off_vidx);
+        MOE_TRY(moe_ep_remap_experts(idx, T * K, E, L->slot_of_expert, vidx, st));
+        sort_ids = vidx;
+    }
 
     if (L->peer_mode) {
         // device-driven exchange over the symmetric peer buffers: no host synchronisation
@@ -235,7 +244,7 @@ moe_status_t run_experts_ep(moe_layer* L, const int32_t* idx, const float* wts, 
         const uint32_t epoch = ++L->epoch;
         const int y_cap = c.max_tokens * K;
         mark(L, 2, st);
-        MOE_TRY(moe_permute_mb(idx, T, K, 0, E, 0, ecounts, at<int32_t>(ws, L->off_estart), spos, stok, stotal,
+        MOE_TRY(moe_permute_mb(sort_ids, T, K, 0, E, 0, ecounts, at<int32_t>(ws, L->off_estart), spos, stok, stotal,
                                    T * K, L->error_word, 1, at<void>(ws, L->off_bcounts), L->bcounts_bytes, st));
         MOE_TRY(tbep::counts(P, ecounts, epoch, plan, rcounts, L->error_word, st));
         mark(L, 3, st);
@@ -262,7 +271,7 @@ moe_status_t run_experts_ep(moe_layer* L, const int32_t* idx, const float* wts, 
     }
 
     mark(L, 2, st);
-    MOE_TRY(moe_permute_mb(idx, T, K, 0, E, 0, ecounts, at<int32_t>(ws, L->off_estart), spos, stok, stotal,
+    MOE_TRY(moe_permute_mb(sort_ids, T, K, 0, E, 0, ecounts, at<int32_t>(ws, L->off_estart), spos, stok, stotal,
                                T * K, L->error_word, 1, at<void>(ws, L->off_bcounts), L->bcounts_bytes, st));
     MOE_TRY(moe_ep_pack_rows(at<void>(ws, L->off_xq), at<float>(ws, L->off_xs), L->xs_ld, stok, stotal, T * K, H,
                              at<void>(ws, L->off_psend), st));
@@ -376,6 +385,7 @@ moe_status_t moe_layer_create(const moe_layer_config_t* cfg, const moe_layer_wei
 
 moe_status_t moe_layer_destroy(moe_layer_t* L) {
     if (!L) return MOE_OK;
+    if (L->slot_of_expert) cudaFree(L->slot_of_expert);
     if (L->h_counts) cudaFreeHost(L->h_counts);
     cudaFree(L->error_word);
     delete L;
@@ -436,6 +446,30 @@ moe_status_t moe_layer_set_stage_events(moe_layer_t* L, cwEvent_t* events) {
     L->timing = events != nullptr;
     for (int i = 0; i <= MOE_NUM_STAGES; ++i)
         L->stage_ev[i] = events ? static_cast<cudaEvent_t>(events[i]) : nullptr;
+    return MOE_OK;
+}
+
+moe_status_t moe_layer_set_expert_placement(moe_layer_t* L, const int32_t* slot_of_expert) {
+    if (!L) return MOE_ERR_INVALID_ARGUMENT;
+    const int E = L->cfg.num_experts;
+    if (!slot_of_expert) {
+        if (L->slot_of_expert) cudaFree(L->slot_of_expert);
+        L->slot_of_expert = nullptr;
+        return MOE_OK;
+    }
+    if (L->cfg.ep_size <= 1) return MOE_ERR_INVALID_ARGUMENT;
+    std::vector<char> seen(E, 0);
+    for (int e = 0; e < E; ++e) {
+        const int v = slot_of_expert[e];
+        if (v < 0 || v >= E || seen[v]) return MOE_ERR_INVALID_ARGUMENT;   // must be a permutation
+        seen[v] = 1;
+    }
+    if (!L->slot_of_expert && cudaMalloc(&L->slot_of_expert, E * sizeof(int32_t)) != cudaSuccess) {
+        L->slot_of_expert = nullptr;
+        return MOE_ERR_CUDA;
+    }
+    if (cudaMemcpy(L->slot_of_expert, slot_of_expert, E * sizeof(int32_t), cudaMemcpyHostToDevice) != cudaSuccess)
+        return MOE_ERR_CUDA;
     return MOE_OK;
 }
 

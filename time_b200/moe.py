@@ -91,6 +91,8 @@ def libs():
                                         c_int, c_int, c_void_p, c_void_p]
         k.moe_permute_padded.argtypes = [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p,
                                          c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p]
+        k.moe_layer_set_expert_placement.argtypes = [c_void_p, c_void_p]
+        k.moe_ep_remap_experts.argtypes = [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p]
         k.moe_layer_peer_bytes.argtypes = [c_void_p]
         k.moe_layer_peer_bytes.restype = c_size_t
         k.moe_layer_set_peer_buffers.argtypes = [c_void_p, c_void_p, c_int]
@@ -254,6 +256,18 @@ class MoELayer:
         self._ev_arr = (c_void_p * len(events))(*[e.cuda_event for e in events])
         check("moe_layer_set_stage_events", self._k.moe_layer_set_stage_events(self._h, self._ev_arr))
 
+    def set_expert_placement(self, slot_of_expert):
+        """Expert -> slot permutation (list of E ints) for expert parallelism;
+        the weights this layer was built with must hold the rank's experts in
+        slot order (synth.expert_slice(..., slot_of_expert=...))."""
+        import numpy as np
+        if slot_of_expert is None:
+            check("moe_layer_set_expert_placement", self._k.moe_layer_set_expert_placement(self._h, None))
+            return
+        arr = np.ascontiguousarray(slot_of_expert, dtype=np.int32)
+        check("moe_layer_set_expert_placement",
+              self._k.moe_layer_set_expert_placement(self._h, arr.ctypes.data_as(c_void_p)))
+
     def use_peer_memory(self, group=None):
         """Switch the expert-parallel exchange to NVLink peer memory: allocate
         this rank's buffer with torch's symmetric-memory allocator (every rank
@@ -316,3 +330,29 @@ def grouped_gemm(mode: int, a, a_scale, a_ld: int, w, w_scale, count, start, out
                            ptr(count), ptr(start), ptr(out), ptr(out_scale), out_ld)
     rc = L["libcublaswrap.so"].cbwFp8BlockScaledGroupedGemm(ctypes.byref(args), ptr(error_word), stream_ptr(stream))
     check("cbwFp8BlockScaledGroupedGemm", rc)
+
+
+def router_load(shape, weights, x) -> "torch.Tensor":
+    """Per-expert routed pairs of the tokens x under this router (RMSNorm +
+    router logits + top-k on the device, all tokens on this GPU): the load
+    statistics a balanced expert placement is computed from."""
+    import torch
+    k = libs()["libkernels.so"]
+    dev = x.device
+    T, H, E, K = x.shape[0], shape.hidden, shape.num_experts, shape.top_k
+    s = torch.cuda.current_stream().cuda_stream
+    rms = torch.empty(T, device=dev)
+    n = torch.empty(T, H, device=dev)
+    xq = torch.empty(T, H, dtype=torch.uint8, device=dev)
+    ld = (T + 3) // 4 * 4
+    xs = torch.empty(H // 128, ld, device=dev)
+    logits = torch.empty(T, E, device=dev)
+    idx = torch.empty(T, K, dtype=torch.int32, device=dev)
+    w = torch.empty(T, K, device=dev)
+    check("moe_rmsnorm_quant_n", k.moe_rmsnorm_quant_n(ptr(x), ptr(weights["gamma"]), T, H, shape.eps, ptr(rms),
+                                                      ptr(n), ptr(xq), ptr(xs), ld, s))
+    check("moe_router_logits", k.moe_router_logits(ptr(n), ptr(weights["router_w"]), ptr(weights.get("router_bias")),
+                                                   T, H, E, ptr(logits), s))
+    check("moe_topk_softmax", k.moe_topk_softmax(ptr(logits), T, E, K, ptr(idx), ptr(w), s))
+    v = idx.flatten()
+    return torch.bincount(v[v >= 0].long(), minlength=E).cpu()

@@ -79,13 +79,19 @@ def make_moe_weights(shape: MoEShape, seed: int = 0, device="cpu", zipf_bias: bo
     return out
 
 
-def expert_slice(w: dict, shape: MoEShape, ep_size: int, ep_rank: int) -> dict:
-    """The weights expert-parallel rank `ep_rank` holds: routed experts
-    [r*E/ep, (r+1)*E/ep) then the shared expert(s), as contiguous copies; the
-    router stays replicated."""
+def expert_slice(w: dict, shape: MoEShape, ep_size: int, ep_rank: int, slot_of_expert=None) -> dict:
+    """The weights expert-parallel rank `ep_rank` holds: its routed experts in
+    local-slot order -- [r*E/ep, (r+1)*E/ep) for the contiguous placement, or
+    the experts whose slot (slot_of_expert[e]) lies in that range -- then the
+    shared expert(s), as contiguous copies; the router stays replicated."""
     E, S = shape.num_experts, shape.num_shared
     per = E // ep_size
-    keep = list(range(ep_rank * per, (ep_rank + 1) * per)) + list(range(E, E + S))
+    if slot_of_expert is None:
+        routed = list(range(ep_rank * per, (ep_rank + 1) * per))
+    else:
+        by_slot = sorted(range(E), key=lambda e: int(slot_of_expert[e]))
+        routed = by_slot[ep_rank * per:(ep_rank + 1) * per]
+    keep = routed + list(range(E, E + S))
     out = {k: v for k, v in w.items() if k not in ("w13", "s13", "w2", "s2")}
     for k in ("w13", "s13", "w2", "s2"):
         out[k] = w[k][keep].contiguous()
@@ -131,3 +137,28 @@ def expected_distinct_ranks(E: int, k: int, ep: int) -> float:
     """Mean number of distinct EP ranks a token's k experts land on."""
     per = E // ep
     return ep * (1.0 - math.comb(E - per, k) / math.comb(E, k))
+
+
+def balanced_placement(expert_load, ep_size: int) -> list[int]:
+    """Expert -> slot permutation that evens the ranks' expected work
+    (longest-processing-time first: heaviest expert to the least loaded rank
+    that still has a free slot; every rank gets E/ep experts, in ascending
+    expert order within the rank).  `expert_load`: per-expert routed pairs
+    measured on a calibration batch."""
+    load = [float(v) for v in expert_load]
+    E = len(load)
+    per = E // ep_size
+    owner = [0] * E
+    rank_load = [0.0] * ep_size
+    rank_n = [0] * ep_size
+    for e in sorted(range(E), key=lambda i: (-load[i], i)):
+        r = min((r for r in range(ep_size) if rank_n[r] < per), key=lambda r: (rank_load[r], r))
+        owner[e] = r
+        rank_load[r] += load[e]
+        rank_n[r] += 1
+    slot = [0] * E
+    for r in range(ep_size):
+        mine = sorted(e for e in range(E) if owner[e] == r)
+        for j, e in enumerate(mine):
+            slot[e] = r * per + j
+    return slot
