@@ -93,7 +93,8 @@ def test_router_topk_bit_exact(gpu, oracle, T, H, E, K, bias):
 
 @pytest.mark.parametrize("T,H,E,K,bias", [(5, 256, 8, 2, False), (70, 512, 160, 8, True), (33, 256, 64, 16, False),
                                           (300, 5120, 160, 8, True), (17, 384, 200, 4, True),
-                                          (1000, 512, 160, 8, True), (4096, 1024, 160, 8, True),
+                                          (1000, 512, 160, 8, True), (512, 5120, 160, 8, True),
+                                          (4096, 1024, 160, 8, True),
                                           (4096, 5120, 200, 8, False)])
 def test_tiled_router_bit_exact(gpu, oracle, T, H, E, K, bias):
     """The layer's router (stored n -> tiled logits -> top-k kernel) against

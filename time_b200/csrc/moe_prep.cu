@@ -674,10 +674,16 @@ moe_status_t moe_router_logits(const float* n, const float* router_w, const floa
     if (T < 0 || H <= 0 || H % 128 || E <= 0 || E > 256) return MOE_ERR_INVALID_ARGUMENT;
     if (T == 0) return MOE_OK;
     if (!n || !router_w || !logits || !aligned16(n) || !aligned16(router_w)) return MOE_ERR_INVALID_ARGUMENT;
-    // tokens per thread: the largest tile that still gives two blocks per SM
-    // (one for small T)
+    // tokens per thread: the smallest tile whose grid fits in one wave of 148
+    // SMs (a lone block is latency-bound, so a grid of <= 148 blocks finishes
+    // in about one block's time, and a smaller tile is a shorter block); when
+    // even 4 tokens per thread need more than one wave, 2 per thread (several
+    // resident blocks per SM).  Measured on B200, H = 5120, E = 160: T = 256 ->
+    // 1 (76 us), 512 -> 2 (84 us), 1024 -> 4 (123 us), 2048 / 4096 -> 2
+    // (170 / 274 us).
     const int etiles = (E + kR3Exp - 1) / kR3Exp;
-    const int ti = ((T + 63) / 64) * etiles >= 2 * 148 ? 4 : (((T + 31) / 32) * etiles >= 148 ? 2 : 1);
+    auto blocks_for = [&](int t) { return etiles * ((T + 16 * t - 1) / (16 * t)); };
+    const int ti = blocks_for(1) <= 148 ? 1 : (blocks_for(2) <= 148 ? 2 : (blocks_for(4) <= 148 ? 4 : 2));
     const dim3 grid(etiles, (T + 16 * ti - 1) / (16 * ti));
     if (grid.y > 65535) return MOE_ERR_UNSUPPORTED;
     static bool attr = false;
