@@ -66,6 +66,11 @@ def lib():
                                           ctypes.c_int, ctypes.c_int, i32p, f32p, f32p, ctypes.c_int]
         L.orc_moe_ffn_experts.argtypes = [ctypes.POINTER(MoeCfg), ctypes.POINTER(MoeWeights), u16p, i32p, f32p,
                                           u16p, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+        L.orc_gemm_fp8_block.argtypes = [u8p, f32p, ctypes.c_int, u8p, f32p, ctypes.c_int, ctypes.c_int, f32p]
+        L.orc_rope_inv_freq.argtypes = [ctypes.c_int, ctypes.c_float, f32p]
+        L.orc_rope_partial.argtypes = [f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, f32p]
+        L.orc_attn_decode_paged.argtypes = [f32p, f32p, f32p, i32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                            ctypes.c_int, ctypes.c_int, ctypes.c_float, f32p]
         _lib = L
     return _lib
 
@@ -247,3 +252,46 @@ def max_rel_and_mae(y: np.ndarray, ref: np.ndarray):
     ref = np.asarray(ref, dtype=np.float64)
     d = np.abs(y - ref)
     return float(d.max() / max(np.abs(ref).max(), 1e-30)), float(d.mean())
+
+
+# ---------------------------------------------------------------- decode attention (attn_oracle.c)
+
+def gemm_fp8_block(xq: np.ndarray, xs: np.ndarray, w: np.ndarray, ws: np.ndarray) -> np.ndarray:
+    """out [rows][N] = block-scaled FP8 projection (xs [rows][K/128], ws [N/128][K/128])."""
+    xq = np.ascontiguousarray(xq, dtype=np.uint8)
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    rows, K = xq.shape
+    N = w.shape[0]
+    xs, ws = _f32(xs), _f32(ws)
+    out = np.empty((rows, N), dtype=np.float32)
+    lib().orc_gemm_fp8_block(_p(xq, u8p), _p(xs, f32p), rows, _p(w, u8p), _p(ws, f32p), N, K, _p(out, f32p))
+    return out
+
+
+def rope_inv_freq(rot: int, theta: float) -> np.ndarray:
+    out = np.empty(rot // 2, dtype=np.float32)
+    lib().orc_rope_inv_freq(rot, theta, _p(out, f32p))
+    return out
+
+
+def rope_partial(x: np.ndarray, rot: int, pos: int, inv_freq: np.ndarray) -> np.ndarray:
+    """x [heads][d] fp32 -> rotated copy (first `rot` dims, rotate-half)."""
+    y = np.array(x, dtype=np.float32, copy=True, order="C")
+    heads, d = y.shape
+    f = _f32(inv_freq)
+    lib().orc_rope_partial(_p(y, f32p), heads, d, rot, pos, _p(f, f32p))
+    return y
+
+
+def attn_decode_paged(q: np.ndarray, k_cache: np.ndarray, v_cache: np.ndarray, page_table: np.ndarray, seq_len: int,
+                      scale: float) -> np.ndarray:
+    """One sequence: q [nq][d], caches [pages][page_size][nkv][d] (fp32), page_table [pages_of_seq]."""
+    q, kc, vc = _f32(q), _f32(k_cache), _f32(v_cache)
+    pt = np.ascontiguousarray(page_table, dtype=np.int32)
+    nq, d = q.shape
+    _, ps, nkv, _ = kc.shape
+    out = np.empty((nq, d), dtype=np.float32)
+    lib().orc_attn_decode_paged(_p(q, f32p), _p(kc, f32p), _p(vc, f32p), _p(pt, i32p), seq_len, nq, nkv, d, ps,
+                                scale, _p(out, f32p))
+    return out
+

@@ -11,7 +11,9 @@ package's drop-in launch_* kernels (tests/test_gpu_legacy.py) to the
 reference itself.  Inputs are stored beside the outputs, so the tests never
 need the reference or this script.  Kernels covered (reference
 csrc/kernels.h:12-31): fp8_dequantize, f32_to_fp8, rms_norm, moe_gate,
-moe_topk, swiglu, moe_combine, add_residual, argmax, rope.
+moe_topk, swiglu, moe_combine, add_residual, argmax, rope; and into
+tests/golden/ref_attn.npz paged_attention_decode and update_kv_cache
+(`--only attn` writes just that file).
 """
 from __future__ import annotations
 
@@ -38,6 +40,10 @@ def load_ref():
     lib.launch_add_residual.argtypes = [c_void_p, c_void_p, c_size_t, c_void_p]
     lib.launch_argmax.argtypes = [c_void_p, c_void_p, c_int, c_int, c_void_p]
     lib.launch_rope.argtypes = [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_float, c_void_p]
+    lib.launch_paged_attention_decode.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
+                                                  c_int, c_int, c_int, c_int, c_float, c_void_p]
+    lib.launch_update_kv_cache.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                                           c_int, c_int, c_void_p]
     return lib
 
 
@@ -58,11 +64,55 @@ def host(t: torch.Tensor) -> np.ndarray:
     return t.cpu().numpy()
 
 
+def attn_goldens(lib, out_path: str) -> None:
+    """tests/golden/ref_attn.npz: the reference's paged decode attention
+    (kernels.cu:328-392, one sequence per call, caches [page][16][nkv][d] fp32)
+    on GQA cases with shuffled page tables, and its KV-cache scatter
+    (kernels.cu:394-410)."""
+    rng = np.random.default_rng(20261202)
+    st = None
+    g = {}
+    cases = [(8, 2, 64, 77, 12), (12, 1, 128, 300, 24), (4, 4, 128, 16, 3), (16, 2, 128, 1000, 70)]
+    for ci, (nq, nkv, d, past, pages) in enumerate(cases):
+        ps = 16
+        q = rng.standard_normal((nq, d)).astype(np.float32)
+        kc = rng.standard_normal((pages, ps, nkv, d)).astype(np.float32)
+        vc = rng.standard_normal((pages, ps, nkv, d)).astype(np.float32)
+        pt = rng.permutation(pages)[: (past + ps - 1) // ps].astype(np.int32)
+        out = torch.zeros(nq, d, device="cuda")
+        scale = float(1.0 / np.sqrt(d))
+        lib.launch_paged_attention_decode(dev(q).data_ptr(), dev(kc).data_ptr(), dev(vc).data_ptr(), out.data_ptr(),
+                                          dev(pt).data_ptr(), len(pt), ps, nq, nkv, d, past, scale, st)
+        for name, v in (("q", q), ("k", kc), ("v", vc), ("pt", pt), ("out", host(out))):
+            g[f"attn{ci}_{name}"] = v
+        g[f"attn{ci}_shape"] = np.array([nq, nkv, d, past, ps], dtype=np.int32)
+        g[f"attn{ci}_scale"] = np.array([scale], dtype=np.float32)
+    # KV scatter: 5 tokens at start_pos 13 (crossing a page), 2 kv heads
+    S_, nkv, d, ps, pages = 5, 2, 64, 16, 4
+    k = rng.standard_normal((S_, nkv, d)).astype(np.float32)
+    v = rng.standard_normal((S_, nkv, d)).astype(np.float32)
+    pt = np.array([2, 0, 3, 1], dtype=np.int32)
+    kc = torch.zeros(pages, ps, nkv, d, device="cuda")
+    vc = torch.zeros(pages, ps, nkv, d, device="cuda")
+    lib.launch_update_kv_cache(dev(k).data_ptr(), dev(v).data_ptr(), kc.data_ptr(), vc.data_ptr(), dev(pt).data_ptr(),
+                               ps, nkv, d, S_, 13, st)
+    g["kvw_k"], g["kvw_v"], g["kvw_pt"] = k, v, pt
+    g["kvw_kc"], g["kvw_vc"] = host(kc), host(vc)
+    np.savez_compressed(out_path, **g)
+    print(f"wrote {out_path}: {len(g)} arrays")
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", default=str(ROOT / "tests" / "golden" / "ref_kernels.npz"))
+    ap.add_argument("--attn-out", default=str(ROOT / "tests" / "golden" / "ref_attn.npz"))
+    ap.add_argument("--only", choices=["all", "kernels", "attn"], default="all")
     a = ap.parse_args()
     lib = load_ref()
+    if a.only in ("all", "attn"):
+        attn_goldens(lib, a.attn_out)
+    if a.only == "attn":
+        return 0
     rng = np.random.default_rng(20261201)
     st = None   # legacy default stream, as the reference engine passes its context stream
     g = {}
