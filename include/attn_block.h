@@ -34,12 +34,14 @@ extern "C" {
  * theta^(-2i/rot) given by the caller, device [rot/2]) on the q and k heads of
  * each token's qkv row, then k and v written to page slot pos % 16 of page
  * page_table[b][pos / 16] (kernels.cu:394-410 in bf16) and the rotated q to
- * q_out.  A position outside the page table sets *error_word = 4, a page id
- * outside [0, num_cache_pages) sets 6; the token is skipped either way. */
+ * q_out; seq_lens_out (optional, [B]) receives pos + 1, the tokens the
+ * decode step attends over.  A position outside the page table sets
+ * *error_word = 4, a page id outside [0, num_cache_pages) sets 6; the token is
+ * skipped either way. */
 moe_status_t attn_rope_kv_write(const void* qkv_bf16, int B, int nq, int nkv, int head_dim, int rot,
                                 const float* inv_freq, const int32_t* positions, const int32_t* page_table,
                                 int max_pages, int page_size, int num_cache_pages, void* q_out_bf16, void* k_cache,
-                                void* v_cache, int* error_word, cwStream_t stream);
+                                void* v_cache, int32_t* seq_lens_out, int* error_word, cwStream_t stream);
 
 /* Bytes of the split-partials workspace for attn_decode_paged. */
 size_t attn_decode_workspace_bytes(int B, int nq, int max_splits);
@@ -47,7 +49,7 @@ size_t attn_decode_workspace_bytes(int B, int nq, int max_splits);
 /* Decode attention (kernels.fut:245-279; GQA kernels.cu:331):
  * out[b][h] = sum_j softmax_j(q[b][h] . k_j * scale) v_j over positions
  * j < seq_lens[b] of sequence b's pages.  The context is cut into splits of
- * split_tokens (a multiple of 16) tokens, at most max_splits per sequence
+ * split_tokens (a multiple of 16, at most 8192) tokens, at most max_splits per sequence
  * (max_splits * split_tokens >= the longest sequence).  out_bf16: bf16
  * [B][nq][128].  When out_q is given, each head's row is also quantised to
  * e4m3 (1x128, scale = amax / 448) into out_q [B][nq * 128] with scales
@@ -67,6 +69,77 @@ moe_status_t attn_decode_paged(const void* q_bf16, const void* k_cache, const vo
  * buffers mapped into this GPU), each bf16 [T][H]; H % 8 == 0. */
 moe_status_t attn_tp_reduce_residual(const void* const* partials_dev, int tp, const void* residual_bf16, int T, int H,
                                      void* out_bf16, cwStream_t stream);
+
+/* ---------------------------------------------------------------- the block
+ * One decode step of the tensor-parallel attention half of the decoder layer
+ * for one TP rank (the reference's engine.t:1269-1310 sequence with the spec's
+ * all-reduce after o_proj, kernels.fut:605-607):
+ *   h = rmsnorm(x) -> e4m3 1x128;  qkv = W_qkv h (bf16);  partial RoPE, page
+ *   write;  decode attention over pos + 1 tokens;  e4m3 rows;  partial =
+ *   W_o attn (bf16, this rank's heads);  out = x + sum over ranks of partial
+ *   (fp32, rank order).
+ * Weights of this rank: w_qkv e4m3 [(nq + 2 nkv) * 128][hidden] (q heads, k,
+ * v) with fp32 scales [rows / 128][hidden / 128]; w_o e4m3 [hidden][nq * 128]
+ * with scales [hidden / 128][nq]; gamma fp32 [hidden].  The weight and cache
+ * memory stays the caller's. */
+typedef struct attn_block attn_block_t;
+
+typedef struct {
+    int hidden;
+    int num_q_heads;        /* this rank's query heads */
+    int num_kv_heads;       /* this rank's KV heads (a GQA group is at most 16 query heads) */
+    int head_dim;           /* 128 */
+    int rotary_dim;         /* rotated leading dims of each head (even, <= 128) */
+    float rope_theta;
+    float eps;              /* RMSNorm */
+    int max_batch;          /* sequences per call */
+    int max_pages_per_seq;  /* columns of the page table */
+    int max_context;        /* longest sequence (tokens, new one included) */
+    int tp_size, tp_rank;
+} attn_block_config_t;
+
+typedef struct {
+    const float* gamma;
+    const void* w_qkv;
+    const float* s_qkv;
+    const void* w_o;
+    const float* s_o;
+} attn_block_weights_t;
+
+moe_status_t attn_block_create(const attn_block_config_t* cfg, const attn_block_weights_t* weights,
+                               attn_block_t** out);
+moe_status_t attn_block_destroy(attn_block_t* block);
+/* Device workspace of one call (the caller's; one per stream). */
+size_t attn_block_workspace_bytes(const attn_block_t* block);
+/* Context split chosen for the decode kernel (tokens). */
+int attn_block_split_tokens(const attn_block_t* block);
+
+/* tp_size > 1: each rank allocates attn_block_peer_bytes bytes that every rank
+ * maps (CUDA IPC / symmetric memory), zero-fills them, waits until all ranks
+ * have, and passes the mapped pointers (256-byte aligned), rank order.  Every
+ * rank must then call attn_block_decode every step, in the same order. */
+size_t attn_block_peer_bytes(const attn_block_t* block);
+moe_status_t attn_block_set_peer_buffers(attn_block_t* block, void* const* peer_bufs, int n);
+
+/* One decode step: out_bf16 [B][hidden] = x + attention block output.
+ * positions [B]: the new token's position (its K/V go to that slot of the
+ * page table); page_table [B][max_pages_per_seq]; caches bf16
+ * [num_cache_pages][16][num_kv_heads][128]. */
+moe_status_t attn_block_decode(attn_block_t* block, const void* x_bf16, int B, const int32_t* positions,
+                               const int32_t* page_table, int num_cache_pages, void* k_cache, void* v_cache,
+                               void* out_bf16, void* workspace, size_t workspace_bytes, cwStream_t stream);
+
+/* The rank's o_proj partial (bf16 [B][hidden]) without the TP sum or the
+ * residual: for callers that reduce elsewhere, and for checking several
+ * ranks' partials on one GPU (attn_tp_reduce_residual sums them). */
+moe_status_t attn_block_decode_partial(attn_block_t* block, const void* x_bf16, int B, const int32_t* positions,
+                                       const int32_t* page_table, int num_cache_pages, void* k_cache, void* v_cache,
+                                       void* partial_bf16, void* workspace, size_t workspace_bytes, cwStream_t stream);
+
+/* Reads and clears the device error word (synchronises `stream`):
+ * MOE_ERR_DEVICE_TIMEOUT for a wait that gave up, MOE_ERR_INVALID_ARGUMENT for
+ * positions, lengths or page ids outside the given tables. */
+moe_status_t attn_block_check_error(attn_block_t* block, cwStream_t stream);
 
 #ifdef __cplusplus
 }

@@ -295,3 +295,34 @@ def attn_decode_paged(q: np.ndarray, k_cache: np.ndarray, v_cache: np.ndarray, p
                                 scale, _p(out, f32p))
     return out
 
+
+
+def bf16_round(x: np.ndarray) -> np.ndarray:
+    return bf16_bits_to_f32(f32_to_bf16_bits(_f32(x)))
+
+
+def attn_block_partial_ref(w: dict, x: np.ndarray, positions, page_table: np.ndarray, k_cache: np.ndarray,
+                           v_cache: np.ndarray, nq: int, nkv: int, rot: int, theta: float, eps: float) -> np.ndarray:
+    """One TP rank's decode-attention partial with the kernels' rounding points:
+    rmsnorm -> e4m3 1x128 -> QKV (bf16) -> partial RoPE (bf16) -> K/V written
+    into the fp32 copies of the rank's caches (in place) -> decode attention
+    over pos + 1 tokens -> e4m3 1x128 -> o_proj (bf16).  w: numpy gamma, w_qkv,
+    s_qkv, w_o, s_o; x: [B][H] fp32 holding bf16 values."""
+    d = 128
+    n = rmsnorm_ref(x, w["gamma"], eps)
+    q8, s8 = quant_rows_1x128(n)
+    qkv = bf16_round(gemm_fp8_block(q8, s8, w["w_qkv"], w["s_qkv"]))
+    inv = rope_inv_freq(rot, theta)
+    B = x.shape[0]
+    qs = []
+    for b in range(B):
+        pos = int(positions[b])
+        r = bf16_round(rope_partial(qkv[b, :(nq + nkv) * d].reshape(nq + nkv, d), rot, pos, inv))
+        page, slot = page_table[b, pos // 16], pos % 16
+        k_cache[page, slot] = r[nq:]
+        v_cache[page, slot] = qkv[b, (nq + nkv) * d:].reshape(nkv, d)
+        qs.append(r[:nq])
+    attn = np.stack([attn_decode_paged(qs[b], k_cache, v_cache, page_table[b], int(positions[b]) + 1,
+                                       1.0 / np.sqrt(d)).reshape(nq * d) for b in range(B)])
+    aq, as_ = quant_rows_1x128(attn)
+    return bf16_round(gemm_fp8_block(aq, as_, w["w_o"], w["s_o"]))

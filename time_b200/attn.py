@@ -22,18 +22,43 @@ PAGE = 16
 _bound = False
 
 
+class BlockConfig(ctypes.Structure):
+    _fields_ = [("hidden", c_int), ("num_q_heads", c_int), ("num_kv_heads", c_int), ("head_dim", c_int),
+                ("rotary_dim", c_int), ("rope_theta", c_float), ("eps", c_float), ("max_batch", c_int),
+                ("max_pages_per_seq", c_int), ("max_context", c_int), ("tp_size", c_int), ("tp_rank", c_int)]
+
+
+class BlockWeights(ctypes.Structure):
+    _fields_ = [("gamma", c_void_p), ("w_qkv", c_void_p), ("s_qkv", c_void_p), ("w_o", c_void_p), ("s_o", c_void_p)]
+
+
 def lib():
     global _bound
     k = M.libs()["libkernels.so"]
     if not _bound:
         k.attn_rope_kv_write.argtypes = [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p,
-                                         c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]
+                                         c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                         c_void_p]
         k.attn_decode_workspace_bytes.argtypes = [c_int, c_int, c_int]
         k.attn_decode_workspace_bytes.restype = c_size_t
         k.attn_decode_paged.argtypes = [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_int,
                                         c_int, c_int, c_int, c_float, c_int, c_int, c_void_p, c_size_t, c_void_p,
                                         c_void_p, c_void_p, c_int, c_void_p, c_void_p]
         k.attn_tp_reduce_residual.argtypes = [c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p]
+        k.attn_block_create.argtypes = [ctypes.POINTER(BlockConfig), ctypes.POINTER(BlockWeights),
+                                        ctypes.POINTER(c_void_p)]
+        k.attn_block_destroy.argtypes = [c_void_p]
+        k.attn_block_workspace_bytes.argtypes = [c_void_p]
+        k.attn_block_workspace_bytes.restype = c_size_t
+        k.attn_block_split_tokens.argtypes = [c_void_p]
+        k.attn_block_peer_bytes.argtypes = [c_void_p]
+        k.attn_block_peer_bytes.restype = c_size_t
+        k.attn_block_set_peer_buffers.argtypes = [c_void_p, c_void_p, c_int]
+        blk = [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
+               c_void_p]
+        k.attn_block_decode.argtypes = blk
+        k.attn_block_decode_partial.argtypes = blk
+        k.attn_block_check_error.argtypes = [c_void_p, c_void_p]
         _bound = True
     return k
 
@@ -52,13 +77,13 @@ def rope_kv_write(qkv, positions, page_table, k_cache, v_cache, nq: int, nkv: in
     q_out = torch.empty(B, nq, HEAD_DIM, dtype=torch.bfloat16, device=qkv.device)
     M.check("attn_rope_kv_write", lib().attn_rope_kv_write(
         M.ptr(qkv), B, nq, nkv, HEAD_DIM, rot, M.ptr(inv_freq), M.ptr(positions), M.ptr(page_table),
-        page_table.shape[1], PAGE, k_cache.shape[0], M.ptr(q_out), M.ptr(k_cache), M.ptr(v_cache), M.ptr(error_word),
-        M.stream_ptr(stream)))
+        page_table.shape[1], PAGE, k_cache.shape[0], M.ptr(q_out), M.ptr(k_cache), M.ptr(v_cache), None,
+        M.ptr(error_word), M.stream_ptr(stream)))
     return q_out
 
 
 def decode_paged(q, k_cache, v_cache, page_table, seq_lens, nq: int, nkv: int, scale: float,
-                 split_tokens: int = 512, max_splits: int | None = None, quant: bool = False, workspace=None,
+                 split_tokens: int = 2048, max_splits: int | None = None, quant: bool = False, workspace=None,
                  error_word=None, stream=None):
     """Paged decode attention.  Returns (out bf16 [B][nq][128], out_q e4m3 [B][nq*128] or None,
     out_s [nq][ld] or None)."""
@@ -94,3 +119,66 @@ def tp_reduce_residual(partials, residual, stream=None):
         M.ptr(ptrs), len(partials), M.ptr(residual), T, H, M.ptr(out), M.stream_ptr(stream)))
     torch.cuda.current_stream().synchronize() if stream is None else stream.synchronize()
     return out
+
+
+class AttnBlock:
+    """One TP rank of the decode attention block (include/attn_block.h).
+    `weights`: the rank's slice (synth.attn_rank_slice) as device tensors."""
+
+    def __init__(self, shape, weights: dict, max_batch: int, max_pages_per_seq: int, max_context: int,
+                 tp_size: int = 1, tp_rank: int = 0):
+        import torch
+        self.shape, self.tp_size, self.tp_rank = shape, tp_size, tp_rank
+        self.nq, self.nkv = shape.num_q_heads // tp_size, shape.num_kv_heads // tp_size
+        self._w = weights
+        self._k = lib()
+        cfg = BlockConfig(shape.hidden, self.nq, self.nkv, shape.head_dim, shape.rotary_dim, shape.rope_theta,
+                          shape.eps, max_batch, max_pages_per_seq, max_context, tp_size, tp_rank)
+        wts = BlockWeights(*(M.ptr(weights[n]) for n in ("gamma", "w_qkv", "s_qkv", "w_o", "s_o")))
+        h = c_void_p()
+        M.check("attn_block_create", self._k.attn_block_create(ctypes.byref(cfg), ctypes.byref(wts), ctypes.byref(h)))
+        self._h = h
+        dev = weights["w_qkv"].device
+        self.workspace = torch.empty(self._k.attn_block_workspace_bytes(h), dtype=torch.uint8, device=dev)
+        self.split_tokens = self._k.attn_block_split_tokens(h)
+        self._peer = None
+
+    def use_peer_memory(self, group=None):
+        """tp > 1: allocate the peer-visible partial buffers with torch symmetric memory."""
+        import torch
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+        nbytes = self._k.attn_block_peer_bytes(self._h)
+        buf = symm.empty(nbytes, dtype=torch.uint8, device=self.workspace.device)
+        buf.zero_()
+        torch.cuda.synchronize()
+        handle = symm.rendezvous(buf, group if group is not None else dist.group.WORLD)
+        dist.barrier(group=group)
+        ptrs = (c_void_p * self.tp_size)(*[handle.buffer_ptrs[r] for r in range(self.tp_size)])
+        M.check("attn_block_set_peer_buffers", self._k.attn_block_set_peer_buffers(self._h, ptrs, self.tp_size))
+        self._peer = (buf, handle, ptrs)
+
+    def _call(self, fn, x, positions, page_table, k_cache, v_cache, out, stream):
+        M.check(fn.__name__, fn(self._h, M.ptr(x), x.shape[0], M.ptr(positions), M.ptr(page_table), k_cache.shape[0],
+                                M.ptr(k_cache), M.ptr(v_cache), M.ptr(out), M.ptr(self.workspace),
+                                self.workspace.numel(), M.stream_ptr(stream)))
+        return out
+
+    def decode(self, x, positions, page_table, k_cache, v_cache, out=None, stream=None):
+        import torch
+        out = torch.empty_like(x) if out is None else out
+        return self._call(self._k.attn_block_decode, x, positions, page_table, k_cache, v_cache, out, stream)
+
+    def decode_partial(self, x, positions, page_table, k_cache, v_cache, out=None, stream=None):
+        import torch
+        out = torch.empty_like(x) if out is None else out
+        return self._call(self._k.attn_block_decode_partial, x, positions, page_table, k_cache, v_cache, out, stream)
+
+    def check_error(self, stream=None):
+        M.check("attn_block_check_error", self._k.attn_block_check_error(self._h, M.stream_ptr(stream)))
+
+    def close(self):
+        if self._h:
+            self._k.attn_block_destroy(self._h)
+            self._h = None
+

@@ -56,10 +56,12 @@ rope_kv_write_kernel(const __nv_bfloat16* __restrict__ qkv, int nq, int nkv, int
                      const float* __restrict__ inv_freq, const int32_t* __restrict__ positions,
                      const int32_t* __restrict__ page_table, int max_pages, int num_cache_pages,
                      __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ k_cache,
-                     __nv_bfloat16* __restrict__ v_cache, int* __restrict__ error_word) {
+                     __nv_bfloat16* __restrict__ v_cache, int32_t* __restrict__ seq_lens_out,
+                     int* __restrict__ error_word) {
     const int b = blockIdx.x;
     const int pos = positions[b];
     const int pidx = pos / kPage;
+    if (threadIdx.x == 0 && seq_lens_out) seq_lens_out[b] = pos >= 0 ? pos + 1 : 0;
     if (pos < 0 || pidx >= max_pages) {
         if (threadIdx.x == 0 && error_word) atomicExch(error_word, 4);
         return;
@@ -151,7 +153,8 @@ __device__ __forceinline__ int clamp_len(int len, int max_pages, int split_token
 
 constexpr int kWarpRing = kNst * 2 * kPage * kRowPad;   // bf16 elements of one warp's K/V ring
 constexpr int kQElems = kGPad * kRowPad;
-constexpr size_t kDecodeSmem = (static_cast<size_t>(kWarps) * kWarpRing + kQElems) * 2;
+constexpr int kMaxSplitPages = 512;                     // split_tokens <= 8192
+constexpr size_t kDecodeSmem = (static_cast<size_t>(kWarps) * kWarpRing + kQElems) * 2 + kMaxSplitPages * 4;
 // the warp merge reuses the rings: per warp 16 x 128 fp32 O + 16 (m, l)
 static_assert(kWarps * (kGPad * kD + 2 * kGPad) * 4 <= kWarps * kWarpRing * 2, "merge scratch fits the rings");
 
@@ -172,6 +175,18 @@ decode_split_kernel(const DecodeParams p) {
 
     __nv_bfloat16* q_s = sm + kWarps * kWarpRing;
     __nv_bfloat16* ring = sm + warp * kWarpRing;   // [kNst][K 16 rows | V 16 rows][kRowPad]
+    int* pid_s = reinterpret_cast<int*>(q_s + kQElems);   // physical page of each page of the split
+    const int page0 = t0 / kPage;
+    const int npages = (t1 - 1) / kPage - page0 + 1;
+    {
+        const int32_t* ptb = p.page_table + static_cast<size_t>(b) * p.max_pages + page0;
+        for (int i = threadIdx.x; i < npages; i += blockDim.x) {
+            const int phys = ptb[i];
+            // a page id outside the cache reads nothing (zeros) and records error 6
+            if ((phys < 0 || phys >= p.num_cache_pages) && p.error_word) atomicExch(p.error_word, 6);
+            pid_s[i] = (phys < 0 || phys >= p.num_cache_pages) ? -1 : phys;
+        }
+    }
 
     // query rows of the group (rows >= G are zero)
     for (int c = threadIdx.x; c < kGPad * (kD / 8); c += blockDim.x) {
@@ -190,22 +205,13 @@ decode_split_kernel(const DecodeParams p) {
             ldsm_x4(smem_u32(q_s + rr * kRowPad + ks * 16 + 8 * (mi >> 1)), qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3]);
     }
 
-    const int page0 = t0 / kPage;
-    const int npages = (t1 - 1) / kPage - page0 + 1;
     const int my_pages = npages > warp ? (npages - warp + kWarps - 1) / kWarps : 0;
-    const int32_t* pt = p.page_table + static_cast<size_t>(b) * p.max_pages;
     const size_t row_stride = static_cast<size_t>(p.nkv) * kD;   // elements between two slots of a page
 
     auto load_page = [&](int i, int stage) {
-        const int pg = page0 + warp + i * kWarps;
-        int phys = pt[pg];
-        uint32_t nbytes = 16u;
-        if (phys < 0 || phys >= p.num_cache_pages) {
-            // a page id outside the cache: read nothing (zeros), record error 6
-            if (lane == 0 && p.error_word) atomicExch(p.error_word, 6);
-            phys = 0;
-            nbytes = 0u;
-        }
+        int phys = pid_s[warp + i * kWarps];
+        const uint32_t nbytes = phys >= 0 ? 16u : 0u;
+        phys = phys >= 0 ? phys : 0;
         const __nv_bfloat16* kp = p.k_cache + static_cast<size_t>(phys) * kPage * row_stride + kvh * kD;
         const __nv_bfloat16* vp = p.v_cache + static_cast<size_t>(phys) * kPage * row_stride + kvh * kD;
         __nv_bfloat16* dst = ring + stage * 2 * kPage * kRowPad;
@@ -279,10 +285,12 @@ decode_split_kernel(const DecodeParams p) {
             }
             l_r[h] = l_r[h] * alpha[h] + rs;
         }
+        if (alpha[0] != 1.0f || alpha[1] != 1.0f) {   // the running max moved
 #pragma unroll
-        for (int nd = 0; nd < kD / 8; ++nd) {
-            o[nd][0] *= alpha[0]; o[nd][1] *= alpha[0];
-            o[nd][2] *= alpha[1]; o[nd][3] *= alpha[1];
+            for (int nd = 0; nd < kD / 8; ++nd) {
+                o[nd][0] *= alpha[0]; o[nd][1] *= alpha[0];
+                o[nd][2] *= alpha[1]; o[nd][3] *= alpha[1];
+            }
         }
         // O += P V
         uint32_t pa[4];
@@ -431,7 +439,7 @@ extern "C" {
 moe_status_t attn_rope_kv_write(const void* qkv_bf16, int B, int nq, int nkv, int head_dim, int rot,
                                 const float* inv_freq, const int32_t* positions, const int32_t* page_table,
                                 int max_pages, int page_size, int num_cache_pages, void* q_out_bf16, void* k_cache,
-                                void* v_cache, int* error_word, cwStream_t stream) {
+                                void* v_cache, int32_t* seq_lens_out, int* error_word, cwStream_t stream) {
     if (B < 0 || nq <= 0 || nkv <= 0 || nq % nkv || head_dim != kD || page_size != kPage) return MOE_ERR_INVALID_ARGUMENT;
     if (num_cache_pages <= 0) return MOE_ERR_INVALID_ARGUMENT;
     if (rot < 0 || rot > kD || rot % 2 || max_pages <= 0) return MOE_ERR_INVALID_ARGUMENT;
@@ -441,7 +449,7 @@ moe_status_t attn_rope_kv_write(const void* qkv_bf16, int B, int nq, int nkv, in
     rope_kv_write_kernel<<<B, 128, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const __nv_bfloat16*>(qkv_bf16), nq, nkv, rot, inv_freq, positions, page_table, max_pages,
         num_cache_pages, static_cast<__nv_bfloat16*>(q_out_bf16), static_cast<__nv_bfloat16*>(k_cache),
-        static_cast<__nv_bfloat16*>(v_cache), error_word);
+        static_cast<__nv_bfloat16*>(v_cache), seq_lens_out, error_word);
     return launch_status();
 }
 
@@ -457,7 +465,8 @@ moe_status_t attn_decode_paged(const void* q_bf16, const void* k_cache, const vo
                                int out_ld, int* error_word, cwStream_t stream) {
     if (B < 0 || nq <= 0 || nkv <= 0 || nq % nkv || nq / nkv > kGPad || head_dim != kD || page_size != kPage)
         return MOE_ERR_INVALID_ARGUMENT;
-    if (split_tokens <= 0 || split_tokens % kPage || max_splits <= 0 || max_splits > 65535 || max_pages <= 0 ||
+    if (split_tokens <= 0 || split_tokens % kPage || split_tokens > kMaxSplitPages * kPage || max_splits <= 0 ||
+        max_splits > 65535 || max_pages <= 0 ||
         num_cache_pages <= 0)
         return MOE_ERR_INVALID_ARGUMENT;
     if (static_cast<long long>(B) * nkv > 65535) return MOE_ERR_UNSUPPORTED;

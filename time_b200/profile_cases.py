@@ -4,11 +4,16 @@ hundred MB on the device, a handful of launches):
 
     python -m time_b200.profile_cases router [--tokens 4096] [--iters 3]
     python -m time_b200.profile_cases gemm   [--tokens 4096] [--experts 32] [--iters 3]
+    python -m time_b200.profile_cases attention [--batch 64] [--ctx-min 1024] [--ctx-max 32768] [--iters 3]
 
 `router`: RMSNorm+quant (with the fp32 n rows), tiled router logits, top-k
 over T tokens of the GLM shape (hidden 5120, 160 experts; n is 84 MB at 4096
 tokens, larger than L2).  `gemm`: the layer forward on a reduced expert count
 (weights 23.6 MB per expert) -- the grouped GEMMs are its top kernels.
+`attention`: paged decode attention at the per-rank shape of the TP=8
+attention block (12 query heads over 1 KV head, head_dim 128, bf16 pages of
+16 tokens), one new token per sequence with contexts drawn uniformly from
+[ctx-min, ctx-max] (seed 0); its bytes are the K and V pages it must read.
 Prints one line per stage with the mean CUDA-event time per launch.
 """
 from __future__ import annotations
@@ -95,15 +100,57 @@ def gemm(tokens: int, experts: int, iters: int) -> dict:
             "gemm_down_bytes": touched * w2 + rows * (I + I // 128 * 4) + rows * H * 2}
 
 
+def attention(batch: int, ctx_min: int, ctx_max: int, split: int, iters: int, nq: int = 12, nkv: int = 1) -> dict:
+    import numpy as np
+    from . import attn as A
+    dev = torch.device("cuda", 0)
+    rng = np.random.default_rng(0)
+    lens = rng.integers(ctx_min, ctx_max + 1, size=batch)
+    pages = (lens + A.PAGE - 1) // A.PAGE
+    num_pages = int(pages.sum())
+    max_pages = int(pages.max())
+    perm = rng.permutation(num_pages).astype(np.int32)
+    pt = np.full((batch, max_pages), -1, dtype=np.int32)
+    o = 0
+    for b in range(batch):
+        pt[b, :pages[b]] = perm[o:o + pages[b]]
+        o += pages[b]
+    g = torch.Generator(device=dev).manual_seed(1)
+    kc = torch.randn(num_pages, A.PAGE, nkv, A.HEAD_DIM, generator=g, device=dev).to(torch.bfloat16)
+    vc = torch.randn(num_pages, A.PAGE, nkv, A.HEAD_DIM, generator=g, device=dev).to(torch.bfloat16)
+    q = torch.randn(batch, nq, A.HEAD_DIM, generator=g, device=dev).to(torch.bfloat16)
+    pt_d = torch.from_numpy(pt).to(dev)
+    lens_d = torch.from_numpy(lens.astype(np.int32)).to(dev)
+    max_splits = -(-max_pages * A.PAGE // split)
+    k = A.lib()
+    ws = torch.empty(k.attn_decode_workspace_bytes(batch, nq, max_splits), dtype=torch.uint8, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    ms = _time(lambda: A.decode_paged(q, kc, vc, pt_d, lens_d, nq, nkv, 1.0 / 128 ** 0.5, split_tokens=split,
+                                      max_splits=max_splits, quant=True, workspace=ws, error_word=err), iters)
+    assert int(err.item()) == 0
+    kv_bytes = int(lens.sum()) * nkv * A.HEAD_DIM * 2 * 2
+    io_bytes = batch * nq * A.HEAD_DIM * (2 + 2 + 1) + nq * batch * 4
+    return {"decode_ms": ms, "kv_bytes": kv_bytes, "algorithmic_bytes": kv_bytes + io_bytes,
+            "achieved_gbs": (kv_bytes + io_bytes) / (ms * 1e-3) / 1e9, "context_tokens": int(lens.sum()),
+            "split_tokens": split, "max_splits": max_splits}
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["router", "gemm"])
+    ap.add_argument("case", choices=["router", "gemm", "attention"])
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--ctx-min", type=int, default=1024)
+    ap.add_argument("--ctx-max", type=int, default=32768)
+    ap.add_argument("--split", type=int, default=512)
     ap.add_argument("--tokens", type=int, default=4096)
     ap.add_argument("--experts", type=int, default=32)
     ap.add_argument("--iters", type=int, default=3)
     a = ap.parse_args()
     torch.cuda.set_device(0)
-    res = router(a.tokens, a.iters) if a.case == "router" else gemm(a.tokens, a.experts, a.iters)
+    if a.case == "attention":
+        res = attention(a.batch, a.ctx_min, a.ctx_max, a.split, a.iters)
+    else:
+        res = router(a.tokens, a.iters) if a.case == "router" else gemm(a.tokens, a.experts, a.iters)
     print(json.dumps({"case": a.case, "tokens": a.tokens, **res}), flush=True)
     return 0
 

@@ -162,3 +162,52 @@ def balanced_placement(expert_load, ep_size: int) -> list[int]:
         for j, e in enumerate(mine):
             slot[e] = r * per + j
     return slot
+
+
+# ---------------------------------------------------------------- attention block (config 4)
+
+@dataclasses.dataclass(frozen=True)
+class AttnShape:
+    hidden: int
+    num_q_heads: int
+    num_kv_heads: int
+    head_dim: int = 128
+    rotary_dim: int = 64
+    rope_theta: float = 1e6
+    eps: float = 1e-5
+
+
+# GLM-4.x attention, TP = 8 (12 query heads and 1 KV head per rank)
+GLM_ATTN = AttnShape(hidden=5120, num_q_heads=96, num_kv_heads=8)
+
+
+def make_attn_weights(shape: AttnShape, seed: int = 0, device="cpu") -> dict:
+    """Whole-model q/k/v/o projections ~N(0, 0.02) quantised per 128x128 block,
+    gamma = 1 (draw order: q, k, v, o)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    H, d = shape.hidden, shape.head_dim
+    out = {"gamma": torch.ones(H, dtype=torch.float32, device=device)}
+    for name, rows, cols in (("q", shape.num_q_heads * d, H), ("k", shape.num_kv_heads * d, H),
+                             ("v", shape.num_kv_heads * d, H), ("o", H, shape.num_q_heads * d)):
+        w = torch.randn(rows, cols, generator=g, device=device, dtype=torch.float32) * 0.02
+        out["w_" + name], out["s_" + name] = quantize_blocks(w)
+    return out
+
+
+def attn_rank_slice(w: dict, shape: AttnShape, tp: int, rank: int) -> dict:
+    """Rank `rank`'s weights: its query heads [r*nq/tp, (r+1)*nq/tp) and KV heads
+    (shard_heads, kernels.fut:619-630) stacked q, k, v for the QKV projection,
+    and the matching input columns of o_proj (row-parallel)."""
+    d = shape.head_dim
+    nq, nkv = shape.num_q_heads // tp, shape.num_kv_heads // tp
+    q_rows = slice(rank * nq * d, (rank + 1) * nq * d)
+    kv_rows = slice(rank * nkv * d, (rank + 1) * nkv * d)
+    qb, kb = slice(rank * nq * d // 128, (rank + 1) * nq * d // 128), slice(rank * nkv * d // 128, (rank + 1) * nkv * d // 128)
+    return {
+        "gamma": w["gamma"],
+        "w_qkv": torch.cat([w["w_q"][q_rows], w["w_k"][kv_rows], w["w_v"][kv_rows]]).contiguous(),
+        "s_qkv": torch.cat([w["s_q"][qb], w["s_k"][kb], w["s_v"][kb]]).contiguous(),
+        "w_o": w["w_o"][:, q_rows].contiguous(),
+        "s_o": w["s_o"][:, qb].contiguous(),
+    }
+
