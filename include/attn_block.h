@@ -70,6 +70,18 @@ moe_status_t attn_decode_paged(const void* q_bf16, const void* k_cache, const vo
 moe_status_t attn_tp_reduce_residual(const void* const* partials_dev, int tp, const void* residual_bf16, int T, int H,
                                      void* out_bf16, cwStream_t stream);
 
+/* Block-scaled FP8 projection for a few tokens (decode):
+ * out[t][n] = bf16(sum_kb (sum_{k in kb} a[t][k] w[n][k]) * a_scale[kb][t] * w_scale[n/128][kb])
+ * with a e4m3 [T][K], a_scale [K/128][a_ld] (a_ld >= T, a multiple of 4), w
+ * e4m3 [N][K], w_scale [N/128][K/128]; N and K multiples of 128.  The K
+ * blocks are split over the grid; the partial sums are added in split order
+ * (deterministic) in `workspace` (fp8_gemm_small_workspace_bytes).  The same
+ * product as cbwFp8BlockScaledGroupedGemm's down mode for one group, sized
+ * for T up to a few hundred. */
+size_t fp8_gemm_small_workspace_bytes(int T, int N, int K);
+moe_status_t fp8_gemm_small(const void* a, const float* a_scale, int a_ld, int T, const void* w, const float* w_scale,
+                            int N, int K, void* out_bf16, void* workspace, size_t workspace_bytes, cwStream_t stream);
+
 /* ---------------------------------------------------------------- the block
  * One decode step of the tensor-parallel attention half of the decoder layer
  * for one TP rank (the reference's engine.t:1269-1310 sequence with the spec's

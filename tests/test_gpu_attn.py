@@ -187,3 +187,30 @@ def test_tp_reduce_fixed_order(gpu):
         s = s + bf16_np(p)
     ref = torch.from_numpy(bf16_np(res) + s).to(torch.bfloat16)
     assert torch.equal(out.cpu().view(torch.int16), ref.view(torch.int16))
+
+
+@pytest.mark.parametrize("T,N,K", [(1, 128, 128), (3, 768, 512), (64, 1792, 5120), (70, 512, 1536), (200, 256, 1024)])
+def test_small_gemm_matches_oracle(gpu, T, N, K):
+    """fp8_gemm_small (split-K mma.sync) against the oracle's block-scaled
+    projection; equal up to the final bf16 rounding of an fp32 vs float64 sum."""
+    from time_b200 import synth
+    from time_b200 import moe as M
+    rng = np.random.default_rng(T * 7 + N)
+    x = rng.standard_normal((T, K)).astype(np.float32) * np.exp(rng.standard_normal((T, 1))).astype(np.float32)
+    aq, asc = O.quant_rows_1x128(x)                        # [T][K], [T][K/128]
+    wq, ws = synth.quantize_blocks(torch.from_numpy(rng.standard_normal((N, K)).astype(np.float32) * 0.02))
+    ld = (T + 3) // 4 * 4
+    a_scale = np.zeros((K // 128, ld), dtype=np.float32)
+    a_scale[:, :T] = asc.T
+    k = A.lib()
+    wsb = k.fp8_gemm_small_workspace_bytes(T, N, K)
+    work = torch.empty(max(wsb, 16), dtype=torch.uint8, device=gpu)
+    out = torch.empty(T, N, dtype=torch.bfloat16, device=gpu)
+    d_a, d_as = torch.from_numpy(aq).to(gpu), torch.from_numpy(a_scale).to(gpu)
+    d_w, d_ws = wq.to(gpu), ws.to(gpu)
+    M.check("fp8_gemm_small", k.fp8_gemm_small(M.ptr(d_a), M.ptr(d_as), ld, T, M.ptr(d_w), M.ptr(d_ws), N, K, M.ptr(out),
+                                                M.ptr(work), work.numel(), M.stream_ptr()))
+    torch.cuda.synchronize()
+    ref = O.gemm_fp8_block(aq, asc, wq.numpy(), ws.numpy())
+    got = out.float().cpu().numpy()
+    assert np.all(np.abs(got - ref) <= np.abs(ref) * 2 ** -7 + 1e-6), np.abs(got - ref).max()

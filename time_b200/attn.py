@@ -59,6 +59,10 @@ def lib():
         k.attn_block_decode.argtypes = blk
         k.attn_block_decode_partial.argtypes = blk
         k.attn_block_check_error.argtypes = [c_void_p, c_void_p]
+        k.fp8_gemm_small_workspace_bytes.argtypes = [c_int, c_int, c_int]
+        k.fp8_gemm_small_workspace_bytes.restype = c_size_t
+        k.fp8_gemm_small.argtypes = [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_int, c_int, c_void_p,
+                                     c_void_p, c_size_t, c_void_p]
         _bound = True
     return k
 

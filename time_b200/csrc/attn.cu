@@ -49,61 +49,47 @@ inline moe_status_t launch_status() {
 
 // ---------------------------------------------------------------- RoPE + page write
 
-// One block per token: q heads then k heads are rotated on their first `rot`
-// dims (pairs i, i + rot/2), v is copied; k and v go to the token's page slot.
-__global__ void __launch_bounds__(128)
+// One 64-thread block per (token, head): heads 0..nq-1 are queries, the next
+// nkv keys (both rotated on their first `rot` dims, pairs i, i + rot/2), the
+// last nkv values (copied); k and v go to the token's page slot.
+__global__ void __launch_bounds__(64)
 rope_kv_write_kernel(const __nv_bfloat16* __restrict__ qkv, int nq, int nkv, int rot,
                      const float* __restrict__ inv_freq, const int32_t* __restrict__ positions,
                      const int32_t* __restrict__ page_table, int max_pages, int num_cache_pages,
                      __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ k_cache,
                      __nv_bfloat16* __restrict__ v_cache, int32_t* __restrict__ seq_lens_out,
                      int* __restrict__ error_word) {
-    const int b = blockIdx.x;
+    const int b = blockIdx.x, h = blockIdx.y;
     const int pos = positions[b];
     const int pidx = pos / kPage;
-    if (threadIdx.x == 0 && seq_lens_out) seq_lens_out[b] = pos >= 0 ? pos + 1 : 0;
+    if (h == 0 && threadIdx.x == 0 && seq_lens_out) seq_lens_out[b] = pos >= 0 ? pos + 1 : 0;
     if (pos < 0 || pidx >= max_pages) {
-        if (threadIdx.x == 0 && error_word) atomicExch(error_word, 4);
+        if (h == 0 && threadIdx.x == 0 && error_word) atomicExch(error_word, 4);
         return;
     }
     const int phys = page_table[static_cast<size_t>(b) * max_pages + pidx];
     if (phys < 0 || phys >= num_cache_pages) {
-        if (threadIdx.x == 0 && error_word) atomicExch(error_word, 6);
+        if (h == 0 && threadIdx.x == 0 && error_word) atomicExch(error_word, 6);
         return;
     }
     const int slot = pos % kPage;
-    const int W = (nq + 2 * nkv) * kD;
-    const __nv_bfloat16* row = qkv + static_cast<size_t>(b) * W;
-    const int half = rot / 2;
-    // rotated heads: nq query heads then nkv key heads
-    for (int e = threadIdx.x; e < (nq + nkv) * kD; e += blockDim.x) {
-        const int h = e / kD, i = e % kD;
-        const float x = __bfloat162float(row[h * kD + i]);
-        float y = x;
-        if (i < rot) {
-            const int j = i < half ? i : i - half;
-            const float ang = static_cast<float>(pos) * inv_freq[j];
-            float s, c;
-            sincosf(ang, &s, &c);
-            if (i < half) {
-                const float x1 = __bfloat162float(row[h * kD + i + half]);
-                y = x * c - x1 * s;
-            } else {
-                const float x0 = __bfloat162float(row[h * kD + i - half]);
-                y = x0 * s + x * c;
-            }
+    const __nv_bfloat16* src = qkv + static_cast<size_t>(b) * (nq + 2 * nkv) * kD + static_cast<size_t>(h) * kD;
+    __nv_bfloat16* dst;
+    if (h < nq) dst = q_out + (static_cast<size_t>(b) * nq + h) * kD;
+    else if (h < nq + nkv) dst = k_cache + ((static_cast<size_t>(phys) * kPage + slot) * nkv + (h - nq)) * kD;
+    else dst = v_cache + ((static_cast<size_t>(phys) * kPage + slot) * nkv + (h - nq - nkv)) * kD;
+    const int half = (h < nq + nkv) ? rot / 2 : 0;   // values are not rotated
+    for (int i = threadIdx.x; i < kD; i += blockDim.x) {
+        if (i < half) {
+            const float ang = static_cast<float>(pos) * inv_freq[i];
+            float sn, cs;
+            sincosf(ang, &sn, &cs);
+            const float x0 = __bfloat162float(src[i]), x1 = __bfloat162float(src[i + half]);
+            dst[i] = __float2bfloat16_rn(x0 * cs - x1 * sn);
+            dst[i + half] = __float2bfloat16_rn(x0 * sn + x1 * cs);
+        } else if (i >= 2 * half) {
+            dst[i] = src[i];
         }
-        const __nv_bfloat16 yb = __float2bfloat16_rn(y);
-        if (h < nq) {
-            q_out[(static_cast<size_t>(b) * nq + h) * kD + i] = yb;
-        } else {
-            const int kh = h - nq;
-            k_cache[((static_cast<size_t>(phys) * kPage + slot) * nkv + kh) * kD + i] = yb;
-        }
-    }
-    for (int e = threadIdx.x; e < nkv * kD; e += blockDim.x) {
-        const int kh = e / kD, i = e % kD;
-        v_cache[((static_cast<size_t>(phys) * kPage + slot) * nkv + kh) * kD + i] = row[(nq + nkv + kh) * kD + i];
     }
 }
 
@@ -446,7 +432,8 @@ moe_status_t attn_rope_kv_write(const void* qkv_bf16, int B, int nq, int nkv, in
     if (B == 0) return MOE_OK;
     if (!qkv_bf16 || (rot > 0 && !inv_freq) || !positions || !page_table || !q_out_bf16 || !k_cache || !v_cache)
         return MOE_ERR_INVALID_ARGUMENT;
-    rope_kv_write_kernel<<<B, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+    if (nq + 2 * nkv > 65535) return MOE_ERR_UNSUPPORTED;
+    rope_kv_write_kernel<<<dim3(B, nq + 2 * nkv), 64, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const __nv_bfloat16*>(qkv_bf16), nq, nkv, rot, inv_freq, positions, page_table, max_pages,
         num_cache_pages, static_cast<__nv_bfloat16*>(q_out_bf16), static_cast<__nv_bfloat16*>(k_cache),
         static_cast<__nv_bfloat16*>(v_cache), seq_lens_out, error_word);

@@ -2,10 +2,11 @@
 // layer, one call per decode step (one new token per sequence), per TP rank:
 //
 //   rmsnorm + e4m3 1x128   moe_rmsnorm_quant
-//   QKV projection         cbwFp8BlockScaledGroupedGemm, one group, bf16 out
+//   QKV projection         fp8_gemm_small (split-K mma.sync; the tcgen05 grouped
+//                          GEMM with one group above 256 tokens), bf16 out
 //   partial RoPE + pages   attn_rope_kv_write (also seq_lens = pos + 1)
 //   decode attention       attn_decode_paged (bf16 + e4m3 rows for o_proj)
-//   o_proj (row parallel)  cbwFp8BlockScaledGroupedGemm, bf16 partial
+//   o_proj (row parallel)  the same, bf16 partial
 //   TP sum + residual      ranks summed in fp32 in rank order
 //
 // The reference's layer runs the same sequence in fp32 through cbwSgemm and
@@ -36,6 +37,7 @@ using namespace tb;
 constexpr int kD = 128;
 constexpr int kMaxTp = 64;
 constexpr size_t kFlagBytes = 256;
+constexpr int kSmallGemmMaxT = 256;   // up to this batch the projections run on fp8_gemm_small
 
 inline moe_status_t launch_status() {
     return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
@@ -145,7 +147,7 @@ struct attn_block {
     int* error_word;       // device
     // workspace plan
     size_t off_xq, off_xs, off_rms, off_group, off_qkv, off_q, off_lens, off_out, off_aq, off_as, off_dec, off_part,
-        dec_bytes, bytes;
+        off_gsplit, dec_bytes, gsplit_bytes, bytes;
     // peer buffers (tp > 1)
     bool peer_mode;
     PeerSet peers;
@@ -176,11 +178,23 @@ void plan(attn_block* L) {
     L->dec_bytes = attn_decode_workspace_bytes(c.max_batch, c.num_q_heads, L->max_splits);
     L->off_dec = take(L->dec_bytes);
     L->off_part = take(R * H * 2);
+    // split-K partials of the small-batch projections, for any B <= max_batch
+    size_t g = 0;
+    for (int t = 1; t <= c.max_batch && t <= kSmallGemmMaxT; ++t) {
+        const size_t a = fp8_gemm_small_workspace_bytes(t, L->nqkv, H);
+        const size_t b = fp8_gemm_small_workspace_bytes(t, H, c.num_q_heads * kD);
+        g = a > g ? a : g;
+        g = b > g ? b : g;
+    }
+    L->gsplit_bytes = g;
+    L->off_gsplit = take(g > 0 ? g : 16);
     L->bytes = o;
 }
 
-moe_status_t gemm(const attn_block* L, int mode, int K, int N, const void* a, const float* as, const void* w,
+moe_status_t gemm(const attn_block* L, int mode, int B, int K, int N, const void* a, const float* as, const void* w,
                   const float* ws, void* ws_base, void* out, cudaStream_t st) {
+    if (B <= kSmallGemmMaxT)
+        return fp8_gemm_small(a, as, L->ld, B, w, ws, N, K, out, at<void>(ws_base, L->off_gsplit), L->gsplit_bytes, st);
     cbwGroupedGemmArgs g;
     std::memset(&g, 0, sizeof(g));
     g.mode = mode;
@@ -215,9 +229,11 @@ moe_status_t run_partial(attn_block* L, const void* x, int B, const int32_t* pos
     const int H = c.hidden, nq = c.num_q_heads, nkv = c.num_kv_heads;
     ATT_TRY(moe_rmsnorm_quant(x, L->w.gamma, B, H, c.eps, at<float>(ws, L->off_rms), at<void>(ws, L->off_xq),
                               at<float>(ws, L->off_xs), L->ld, st));
-    set_group_kernel<<<1, 1, 0, st>>>(at<int32_t>(ws, L->off_group), B);
-    ATT_TRY(launch_status());
-    ATT_TRY(gemm(L, CBW_GEMM_DOWN_BF16, H, L->nqkv, at<void>(ws, L->off_xq), at<float>(ws, L->off_xs), L->w.w_qkv,
+    if (B > kSmallGemmMaxT) {
+        set_group_kernel<<<1, 1, 0, st>>>(at<int32_t>(ws, L->off_group), B);
+        ATT_TRY(launch_status());
+    }
+    ATT_TRY(gemm(L, CBW_GEMM_DOWN_BF16, B, H, L->nqkv, at<void>(ws, L->off_xq), at<float>(ws, L->off_xs), L->w.w_qkv,
                  L->w.s_qkv, ws, at<void>(ws, L->off_qkv), st));
     ATT_TRY(attn_rope_kv_write(at<void>(ws, L->off_qkv), B, nq, nkv, kD, c.rotary_dim, L->inv_freq, positions,
                                page_table, c.max_pages_per_seq, 16, num_cache_pages, at<void>(ws, L->off_q), k_cache,
@@ -227,7 +243,7 @@ moe_status_t run_partial(attn_block* L, const void* x, int B, const int32_t* pos
                               1.0f / std::sqrt(static_cast<float>(kD)), L->split_tokens, L->max_splits,
                               at<void>(ws, L->off_dec), L->dec_bytes, at<void>(ws, L->off_out), at<void>(ws, L->off_aq),
                               at<float>(ws, L->off_as), L->ld, L->error_word, st));
-    ATT_TRY(gemm(L, CBW_GEMM_DOWN_BF16, nq * kD, H, at<void>(ws, L->off_aq), at<float>(ws, L->off_as), L->w.w_o,
+    ATT_TRY(gemm(L, CBW_GEMM_DOWN_BF16, B, nq * kD, H, at<void>(ws, L->off_aq), at<float>(ws, L->off_as), L->w.w_o,
                  L->w.s_o, ws, partial, st));
     return MOE_OK;
 }

@@ -88,6 +88,86 @@ rmsnorm_quant_kernel(const __nv_bfloat16* __restrict__ x, const float* __restric
     }
 }
 
+constexpr int kRmsRowMax = 16384;   // bf16 elements of the row staged in shared memory
+
+// One 256-thread block per token, for small T (a warp per token leaves most SMs
+// idle and each warp load-latency-bound).  Same arithmetic in the same order:
+// thread (m, lane) = 32m + lane accumulates the p[m] of rowsumsq_ref_order for
+// its lane, the eight partials meet in shared memory, and warp 0 applies the
+// same add tree and shuffle-down reduction; the 1x128 blocks are then split
+// over the eight warps.
+__global__ void __launch_bounds__(256)
+rmsnorm_quant_block_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ gamma, int T, int H,
+                           float eps, float* __restrict__ rms_out, float* __restrict__ n_out,
+                           uint8_t* __restrict__ xq, float* __restrict__ xs, int xs_ld) {
+    __shared__ float part[8][32];
+    __shared__ float s_rms;
+    __shared__ __align__(16) __nv_bfloat16 row_s[kRmsRowMax];
+    const int t = blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const __nv_bfloat16* xr = x + static_cast<size_t>(t) * H;
+    // the row in 16-byte loads (one latency), then the reference order from shared memory
+    for (int c = threadIdx.x; c < H / 8; c += blockDim.x)
+        *reinterpret_cast<uint4*>(row_s + c * 8) = *reinterpret_cast<const uint4*>(xr + c * 8);
+    __syncthreads();
+    {
+        float p = 0.0f;
+        for (int j = 0; j < H; j += 256) {
+            const int i = j + threadIdx.x;
+            if (i < H) {
+                const float v = __bfloat162float(row_s[i]);
+                p = __fmaf_rn(v, v, p);
+            }
+        }
+        part[warp][lane] = p;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        float p[8];
+#pragma unroll
+        for (int m = 0; m < 8; ++m) p[m] = part[m][lane];
+#pragma unroll
+        for (int m = 0; m < 4; ++m) p[m] = __fadd_rn(p[m], p[m + 4]);
+#pragma unroll
+        for (int m = 0; m < 2; ++m) p[m] = __fadd_rn(p[m], p[m + 2]);
+        float s2 = __fadd_rn(p[0], p[1]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s2 = __fadd_rn(s2, __shfl_down_sync(0xffffffffu, s2, o));
+        if (lane == 0) s_rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(s2, static_cast<float>(H)), eps));
+    }
+    __syncthreads();
+    const float rms = s_rms;
+    if (rms_out && threadIdx.x == 0) rms_out[t] = rms;
+    uint8_t* qr = xq + static_cast<size_t>(t) * H;
+    for (int b = warp; b < H / 128; b += 8) {
+        const int c = b * 128 + lane * 4;
+        const uint2 raw = *reinterpret_cast<const uint2*>(row_s + c);
+        const float4 g = *reinterpret_cast<const float4*>(gamma + c);
+        float v0 = __fmul_rn(__fdiv_rn(bf16_lo(raw.x), rms), g.x);
+        float v1 = __fmul_rn(__fdiv_rn(bf16_hi(raw.x), rms), g.y);
+        float v2 = __fmul_rn(__fdiv_rn(bf16_lo(raw.y), rms), g.z);
+        float v3 = __fmul_rn(__fdiv_rn(bf16_hi(raw.y), rms), g.w);
+        if (n_out) *reinterpret_cast<float4*>(n_out + static_cast<size_t>(t) * H + c) = make_float4(v0, v1, v2, v3);
+        float amax = fmaxf(fmaxf(fabsf(v0), fabsf(v1)), fmaxf(fabsf(v2), fabsf(v3)));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        uint32_t packed = 0;
+        float scale = 0.0f;
+        if (amax > 0.0f) {
+            const float inv = __fdiv_rn(448.0f, amax);
+            packed = static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v0, inv), __fmul_rn(v1, inv))) |
+                     (static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v2, inv), __fmul_rn(v3, inv))) << 16);
+            scale = __fdiv_rn(amax, 448.0f);
+        }
+        *reinterpret_cast<uint32_t*>(qr + c) = packed;
+        if (lane == 0) xs[static_cast<size_t>(b) * xs_ld + t] = scale;
+    }
+}
+
+// Up to this many tokens (and hidden sizes) the block-per-token form runs
+// (more SMs busy).
+constexpr int kRmsBlockPerTokenMaxT = 2048;
+
 // ---------------------------------------------------------------- top-k
 // One warp selects the top K of one row of E <= 32*EPT logits with the
 // reference's rule (csrc/kernels.cu:437-471): scanning e = 0..E-1, a value
@@ -657,9 +737,14 @@ moe_status_t moe_rmsnorm_quant_n(const void* x_bf16, const float* gamma, int T, 
     if (!aligned16(x_bf16) || !aligned16(gamma) || !aligned16(xq_out)) return MOE_ERR_INVALID_ARGUMENT;
     const int blocks = (T + 7) / 8;
     if (n_out && !aligned16(n_out)) return MOE_ERR_INVALID_ARGUMENT;
-    rmsnorm_quant_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const __nv_bfloat16*>(x_bf16), gamma, T, H, eps, rms_out, n_out,
-        static_cast<uint8_t*>(xq_out), xs_out, xs_ld);
+    if (T <= kRmsBlockPerTokenMaxT && H <= kRmsRowMax)
+        rmsnorm_quant_block_kernel<<<T, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+            static_cast<const __nv_bfloat16*>(x_bf16), gamma, T, H, eps, rms_out, n_out,
+            static_cast<uint8_t*>(xq_out), xs_out, xs_ld);
+    else
+        rmsnorm_quant_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+            static_cast<const __nv_bfloat16*>(x_bf16), gamma, T, H, eps, rms_out, n_out,
+            static_cast<uint8_t*>(xq_out), xs_out, xs_ld);
     return launch_status();
 }
 

@@ -5,6 +5,7 @@ hundred MB on the device, a handful of launches):
     python -m time_b200.profile_cases router [--tokens 4096] [--iters 3]
     python -m time_b200.profile_cases gemm   [--tokens 4096] [--experts 32] [--iters 3]
     python -m time_b200.profile_cases attention [--batch 64] [--ctx-min 1024] [--ctx-max 32768] [--iters 3]
+    python -m time_b200.profile_cases attn_block [--batch 64] [--ctx-min 1024] [--ctx-max 32768] [--iters 3]
 
 `router`: RMSNorm+quant (with the fp32 n rows), tiled router logits, top-k
 over T tokens of the GLM shape (hidden 5120, 160 experts; n is 84 MB at 4096
@@ -14,6 +15,8 @@ tokens, larger than L2).  `gemm`: the layer forward on a reduced expert count
 attention block (12 query heads over 1 KV head, head_dim 128, bf16 pages of
 16 tokens), one new token per sequence with contexts drawn uniformly from
 [ctx-min, ctx-max] (seed 0); its bytes are the K and V pages it must read.
+`attn_block`: one TP rank's whole decode step of that block (rmsnorm, FP8
+QKV, RoPE + page write, decode, FP8 o_proj, residual) on this GPU.
 Prints one line per stage with the mean CUDA-event time per launch.
 """
 from __future__ import annotations
@@ -135,9 +138,55 @@ def attention(batch: int, ctx_min: int, ctx_max: int, split: int, iters: int, nq
             "split_tokens": split, "max_splits": max_splits}
 
 
+def attn_block(batch: int, ctx_min: int, ctx_max: int, iters: int, tp: int = 8) -> dict:
+    """One TP rank's decode step of the config-4 attention block (rank 0's
+    weight slice, its own cache) with the rank-local residual add in place of
+    the TP sum (tp_size 1 on this GPU)."""
+    import numpy as np
+    from . import attn as A
+    dev = torch.device("cuda", 0)
+    shape = synth.GLM_ATTN
+    rng = np.random.default_rng(0)
+    ctx = rng.integers(ctx_min, ctx_max + 1, size=batch)
+    steps = iters + 2
+    pages = (ctx + steps + A.PAGE - 1) // A.PAGE
+    num_pages, max_pages = int(pages.sum()), int(pages.max())
+    perm = rng.permutation(num_pages).astype(np.int32)
+    pt = np.full((batch, max_pages), -1, dtype=np.int32)
+    o = 0
+    for b in range(batch):
+        pt[b, :pages[b]] = perm[o:o + pages[b]]
+        o += pages[b]
+    nkv = shape.num_kv_heads // tp
+    g = torch.Generator(device=dev).manual_seed(1)
+    kc = torch.randn(num_pages, A.PAGE, nkv, A.HEAD_DIM, generator=g, device=dev).to(torch.bfloat16)
+    vc = torch.randn(num_pages, A.PAGE, nkv, A.HEAD_DIM, generator=g, device=dev).to(torch.bfloat16)
+    x = torch.randn(batch, shape.hidden, generator=g, device=dev).to(torch.bfloat16)
+    w_all = synth.make_attn_weights(shape, seed=3, device=dev)
+    wr = synth.attn_rank_slice(w_all, shape, tp, 0)
+    local = dataclasses.replace(shape, num_q_heads=shape.num_q_heads // tp, num_kv_heads=nkv)
+    blk = A.AttnBlock(local, wr, max_batch=batch, max_pages_per_seq=max_pages, max_context=max_pages * A.PAGE)
+    ptd = torch.from_numpy(pt).to(dev)
+    out = torch.empty_like(x)
+    step = [0]
+
+    def run():
+        pos = torch.from_numpy((ctx + step[0]).astype(np.int32)).to(dev)
+        step[0] += 1
+        blk.decode(x, pos, ptd, kc, vc, out=out)
+
+    ms = _time(run, iters)
+    blk.check_error()
+    blk.close()
+    kv = int(ctx.sum()) * 2 * nkv * A.HEAD_DIM * 2
+    wbytes = sum(v.numel() * v.element_size() for k_, v in wr.items() if k_ != "gamma")
+    return {"block_ms": ms, "kv_bytes": kv, "weight_bytes": wbytes, "context_tokens": int(ctx.sum()),
+            "achieved_gbs": (kv + wbytes) / (ms * 1e-3) / 1e9, "split_tokens": blk.split_tokens}
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["router", "gemm", "attention"])
+    ap.add_argument("case", choices=["router", "gemm", "attention", "attn_block"])
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--ctx-min", type=int, default=1024)
     ap.add_argument("--ctx-max", type=int, default=32768)
@@ -149,6 +198,8 @@ def main() -> int:
     torch.cuda.set_device(0)
     if a.case == "attention":
         res = attention(a.batch, a.ctx_min, a.ctx_max, a.split, a.iters)
+    elif a.case == "attn_block":
+        res = attn_block(a.batch, a.ctx_min, a.ctx_max, a.iters)
     else:
         res = router(a.tokens, a.iters) if a.case == "router" else gemm(a.tokens, a.experts, a.iters)
     print(json.dumps({"case": a.case, "tokens": a.tokens, **res}), flush=True)
