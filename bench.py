@@ -404,10 +404,12 @@ def run_ours(args):
         wc = {k_: (v.cpu() if isinstance(v, torch.Tensor) else v) for k_, v in w.items()}
         cpu, _, _ = cpu_baseline(shape, wc, x.cpu(), args.cpu_seconds)
 
-    # our kernels per forward: rmsnorm, router logits, top-k, permute, gather, 2 GEMMs, combine; EP adds
-    # (NCCL) row pack, receive plan, output pack or (peer memory) counts, dispatch, 2 signal/waits,
-    # receive plan, output send
-    launches_per_step = 8 if world == 1 else (11 if args.exchange == "nccl" else 13)
+    # our kernels per forward: rmsnorm, router logits, top-k, 3 permutation kernels (count, scan,
+    # scatter), gather, 2 GEMMs, combine = 10; EP replaces gather/combine and adds (NCCL) row pack,
+    # receive plan, gather, output pack, split combine = 13 or (peer memory) counts, dispatch,
+    # 2 signal/waits, receive plan, gather, output send, split combine = 16; the expert placement
+    # adds its remap kernel.  NCCL's own kernels are not counted.
+    launches_per_step = 10 if world == 1 else ((13 if args.exchange == "nccl" else 16) + (1 if placement else 0))
     line = {"metric": METRIC, "value": T * 1000.0 / ms_per_step, "unit": UNIT, "n_gpus": world,
             "steps": K, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "e4m3 x e4m3 -> f32 (bf16 in/out)",
