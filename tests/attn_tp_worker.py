@@ -43,6 +43,7 @@ def main() -> int:
     ap.add_argument("--ctx-min", type=int, default=1024)
     ap.add_argument("--ctx-max", type=int, default=4096)
     ap.add_argument("--time", type=int, default=0, help="timed steps (0: parity check)")
+    ap.add_argument("--graph", action="store_true", help="capture one step in a CUDA graph and replay it")
     a = ap.parse_args()
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -76,9 +77,26 @@ def main() -> int:
 
     if a.time == 0:
         outs = []
+        pos_buf = torch.from_numpy(ctx.astype(np.int32)).to(dev)
+        xin = xs[0].clone()
+        out_buf = torch.empty_like(xs[0])
+        graph = None
+        if a.graph:
+            # one plain step first (kernel attributes are set outside the capture; it
+            # writes the same K/V at the same positions as step 0), then capture one step
+            blk.decode(xin, pos_buf, ptd, kc, vc, out=out_buf)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                blk.decode(xin, pos_buf, ptd, kc, vc, out=out_buf)
         for s in range(steps):
-            pos = torch.from_numpy((ctx + s).astype(np.int32)).to(dev)
-            outs.append(blk.decode(xs[s % 2], pos, ptd, kc, vc).clone())
+            pos_buf.copy_(torch.from_numpy((ctx + s).astype(np.int32)))
+            xin.copy_(xs[s % 2])
+            if graph is not None:
+                graph.replay()
+            else:
+                blk.decode(xin, pos_buf, ptd, kc, vc, out=out_buf)
+            outs.append(out_buf.clone())
         torch.cuda.synchronize()
         blk.check_error()
         got = [torch.empty_like(outs[0]) for _ in range(world)] if rank == 0 else None
@@ -112,12 +130,23 @@ def main() -> int:
             blk.decode(xs[s % 2], pos, ptd, kc, vc)
         poss = [torch.from_numpy((ctx + 3 + s).astype(np.int32)).to(dev) for s in range(a.time)]
         out = torch.empty_like(xs[0])
+        pos_buf = poss[0].clone()
+        graph = None
+        if a.graph:
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                blk.decode(xs[0], pos_buf, ptd, kc, vc, out=out)
         torch.cuda.synchronize()
         dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for s in range(a.time):
-            blk.decode(xs[s % 2], poss[s], ptd, kc, vc, out=out)
+            if graph is not None:
+                pos_buf.copy_(poss[s], non_blocking=True)
+                graph.replay()
+            else:
+                blk.decode(xs[s % 2], poss[s], ptd, kc, vc, out=out)
         e1.record()
         torch.cuda.synchronize()
         dist.barrier()
@@ -126,7 +155,8 @@ def main() -> int:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         kv = int(ctx.sum()) * 2 * nkv_l * D * 2
         if rank == 0:
-            print(json.dumps({"block": "attention_decode_tp", "tp": tp, "batch": B, "context_tokens": int(ctx.sum()),
+            print(json.dumps({"block": "attention_decode_tp", "tp": tp, "graph": a.graph, "batch": B,
+                              "context_tokens": int(ctx.sum()),
                               "ms_per_step": t.item(), "kv_bytes_per_rank": kv,
                               "kv_gbs_per_rank": kv / (t.item() * 1e-3) / 1e9, "split_tokens": blk.split_tokens}),
                   flush=True)

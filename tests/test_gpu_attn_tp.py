@@ -1,7 +1,8 @@
 """Tensor-parallel decode attention block across real GPUs (tests/attn_tp_worker.py
 under torch.distributed.run, one process per GPU, TP sum over NVLink peer
 memory): every rank's output bit-identical to every other rank's and to all
-ranks recomputed on one GPU.  Needs at least 2 GPUs; the one-GPU emulation is
+ranks recomputed on one GPU, with plain calls and with each step replayed
+from a CUDA graph.  Needs at least 2 GPUs; the one-GPU emulation is
 tests/test_gpu_attn_block.py."""
 import os
 import socket
@@ -30,7 +31,8 @@ def free_port() -> int:
 
 
 @pytest.mark.parametrize("args", [("--shape", "small", "--batch", "3", "--ctx-min", "0", "--ctx-max", "300"),
-                                  ("--shape", "glm", "--batch", "8")])
+                                  ("--shape", "glm", "--batch", "8"),
+                                  ("--shape", "glm", "--batch", "8", "--graph")])
 def test_attn_tp_bit_identical(gpu, args):
     n = n_gpus()
     if n < 2:

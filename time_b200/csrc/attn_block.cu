@@ -12,10 +12,13 @@
 // The reference's layer runs the same sequence in fp32 through cbwSgemm and
 // its launch_* attention kernels (src/terra/engine.t:1269-1310) with the
 // all-reduce of the spec after o_proj (kernels.fut:605-607, ncclAllReduce).
-// Here, for tp > 1, each rank's partial goes into its peer-visible buffer
-// (double-buffered by call parity), one thread raises the rank's ready flag on
-// every rank (system-scope release), and the reduce kernel waits for every
-// flag (bounded; error 3 on timeout) and reads all partials over NVLink.
+// Here, for tp > 1, each rank's partial goes into its peer-visible buffer,
+// one thread raises the rank's ready flag on every rank (system-scope
+// release), the reduce kernel waits for every flag and reads all partials over
+// NVLink, and a one-thread kernel then raises the rank's done flag; the next
+// call waits for every done flag before overwriting its partial.  The epoch
+// lives in device memory, so a decode step can be captured in a CUDA graph
+// and replayed.  Every wait is bounded (error word 3 on timeout).
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 
@@ -36,7 +39,7 @@ using namespace tb;
 
 constexpr int kD = 128;
 constexpr int kMaxTp = 64;
-constexpr size_t kFlagBytes = 256;
+constexpr size_t kFlagBytes = 512;   // ready[kMaxTp] at 0, done[kMaxTp] at 256, partial after
 constexpr int kSmallGemmMaxT = 256;   // up to this batch the projections run on fp8_gemm_small
 
 inline moe_status_t launch_status() {
@@ -79,30 +82,60 @@ struct PeerSet {
     int tp, me;
 };
 
-// Raise ready[me] = epoch on every rank once this rank's partial is written.
-__global__ void tp_signal_kernel(const PeerSet P, uint32_t epoch) {
+__device__ __forceinline__ uint32_t* ready_flag(const PeerSet& P, int rank, int src) {
+    return reinterpret_cast<uint32_t*>(P.base[rank]) + src;
+}
+__device__ __forceinline__ uint32_t* done_flag(const PeerSet& P, int rank, int src) {
+    return reinterpret_cast<uint32_t*>(P.base[rank] + 256) + src;
+}
+
+// One thread: wait (bounded) until every rank's flag here equals `value`.
+__device__ bool wait_all(const PeerSet& P, bool done, uint32_t value, unsigned long long timeout_ns) {
+    const uint64_t t0 = globaltimer_ns();
+    for (int s = 0; s < P.tp; ++s) {
+        const uint32_t* f = done ? done_flag(P, P.me, s) : ready_flag(P, P.me, s);
+        while (ld_acquire_sys_u32(f) != value) {
+            if (globaltimer_ns() - t0 > timeout_ns) return false;
+            __nanosleep(64);
+        }
+    }
+    return true;
+}
+
+// Before this rank overwrites its partial: every rank has finished reading
+// the previous one (done[s] == current epoch).
+__global__ void tp_wait_done_kernel(const PeerSet P, const uint32_t* __restrict__ epoch, unsigned long long timeout_ns,
+                                    int* __restrict__ error_word) {
     if (threadIdx.x != 0) return;
+    if (!wait_all(P, true, *epoch, timeout_ns) && error_word) atomicExch(error_word, 3);
+}
+
+// The partial is written: epoch += 1, raise ready[me] = epoch on every rank.
+__global__ void tp_signal_kernel(const PeerSet P, uint32_t* __restrict__ epoch) {
+    if (threadIdx.x != 0) return;
+    const uint32_t e = *epoch + 1u;
+    *epoch = e;
     __threadfence_system();
-    for (int d = 0; d < P.tp; ++d) st_release_sys_u32(reinterpret_cast<uint32_t*>(P.base[d]) + P.me, epoch);
+    for (int d = 0; d < P.tp; ++d) st_release_sys_u32(ready_flag(P, d, P.me), e);
+}
+
+// The reduce is done reading: raise done[me] = epoch on every rank.
+__global__ void tp_done_kernel(const PeerSet P, const uint32_t* __restrict__ epoch) {
+    if (threadIdx.x != 0) return;
+    const uint32_t e = *epoch;
+    __threadfence_system();
+    for (int d = 0; d < P.tp; ++d) st_release_sys_u32(done_flag(P, d, P.me), e);
 }
 
 // Each block: one thread waits (bounded) for every rank's ready flag, then
-// the block sums its slice of the partials (buffer `parity`) in rank order.
+// the block sums its slice of the partials in rank order.
 __global__ void __launch_bounds__(256)
-tp_peer_reduce_kernel(const PeerSet P, uint32_t epoch, int parity, size_t part_bytes,
+tp_peer_reduce_kernel(const PeerSet P, const uint32_t* __restrict__ epoch,
                       const __nv_bfloat16* __restrict__ residual, size_t n, __nv_bfloat16* __restrict__ out,
                       unsigned long long timeout_ns, int* __restrict__ error_word) {
     __shared__ int ok;
     if (threadIdx.x == 0) {
-        ok = 1;
-        const uint32_t* flags = reinterpret_cast<const uint32_t*>(P.base[P.me]);
-        const uint64_t t0 = globaltimer_ns();
-        for (int s = 0; s < P.tp && ok; ++s) {
-            while (ld_acquire_sys_u32(flags + s) != epoch) {
-                if (globaltimer_ns() - t0 > timeout_ns) { ok = 0; break; }
-                __nanosleep(64);
-            }
-        }
+        ok = wait_all(P, false, *epoch, timeout_ns) ? 1 : 0;
         if (!ok && error_word) atomicExch(error_word, 3);
     }
     __syncthreads();
@@ -118,8 +151,7 @@ tp_peer_reduce_kernel(const PeerSet P, uint32_t epoch, int parity, size_t part_b
     }
     float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     for (int r = 0; r < P.tp; ++r) {
-        const __nv_bfloat16* part =
-            reinterpret_cast<const __nv_bfloat16*>(P.base[r] + kFlagBytes + parity * part_bytes);
+        const __nv_bfloat16* part = reinterpret_cast<const __nv_bfloat16*>(P.base[r] + kFlagBytes);
         const uint4 pv = *reinterpret_cast<const uint4*>(part + i8);
         const __nv_bfloat16* pb = reinterpret_cast<const __nv_bfloat16*>(&pv);
 #pragma unroll
@@ -151,7 +183,7 @@ struct attn_block {
     // peer buffers (tp > 1)
     bool peer_mode;
     PeerSet peers;
-    uint32_t epoch;
+    uint32_t* epoch_dev;   // device: calls so far (tp > 1)
     unsigned long long timeout_ns;
 };
 
@@ -296,6 +328,7 @@ moe_status_t attn_block_create(const attn_block_config_t* cfg, const attn_block_
 moe_status_t attn_block_destroy(attn_block_t* L) {
     if (!L) return MOE_OK;
     if (L->inv_freq) cudaFree(L->inv_freq);
+    if (L->epoch_dev) cudaFree(L->epoch_dev);
     if (L->error_word) cudaFree(L->error_word);
     delete L;
     return MOE_OK;
@@ -307,7 +340,7 @@ int attn_block_split_tokens(const attn_block_t* L) { return L ? L->split_tokens 
 
 size_t attn_block_peer_bytes(const attn_block_t* L) {
     if (!L || L->cfg.tp_size <= 1) return 0;
-    return kFlagBytes + 2 * static_cast<size_t>(L->rows_pad) * L->cfg.hidden * 2;
+    return kFlagBytes + static_cast<size_t>(L->rows_pad) * L->cfg.hidden * 2;
 }
 
 moe_status_t attn_block_set_peer_buffers(attn_block_t* L, void* const* bufs, int n) {
@@ -318,8 +351,12 @@ moe_status_t attn_block_set_peer_buffers(attn_block_t* L, void* const* bufs, int
     }
     L->peers.tp = n;
     L->peers.me = L->cfg.tp_rank;
+    if (!L->epoch_dev && cudaMalloc(&L->epoch_dev, sizeof(uint32_t)) != cudaSuccess) {
+        L->epoch_dev = nullptr;
+        return MOE_ERR_CUDA;
+    }
+    if (cudaMemset(L->epoch_dev, 0, sizeof(uint32_t)) != cudaSuccess) return MOE_ERR_CUDA;
     L->peer_mode = true;
-    L->epoch = 0;
     return MOE_OK;
 }
 
@@ -357,19 +394,21 @@ moe_status_t attn_block_decode(attn_block_t* L, const void* x_bf16, int B, const
         return launch_status();
     }
     // every rank takes every step (even with B == 0): the flags pair up calls
-    const uint32_t epoch = ++L->epoch;
-    const int parity = static_cast<int>(epoch & 1u);
-    const size_t part_bytes = static_cast<size_t>(L->rows_pad) * L->cfg.hidden * 2;
-    void* part = L->peers.base[L->peers.me] + kFlagBytes + parity * part_bytes;
+    void* part = L->peers.base[L->peers.me] + kFlagBytes;
+    tp_wait_done_kernel<<<1, 32, 0, st>>>(L->peers, L->epoch_dev, L->timeout_ns, L->error_word);
+    ATT_TRY(launch_status());
     if (B > 0)
         ATT_TRY(run_partial(L, x_bf16, B, positions, page_table, num_cache_pages, k_cache, v_cache, part, workspace,
                             st));
-    tp_signal_kernel<<<1, 32, 0, st>>>(L->peers, epoch);
+    tp_signal_kernel<<<1, 32, 0, st>>>(L->peers, L->epoch_dev);
     ATT_TRY(launch_status());
-    if (B == 0) return MOE_OK;
-    tp_peer_reduce_kernel<<<blocks, 256, 0, st>>>(L->peers, epoch, parity, part_bytes,
-                                                  static_cast<const __nv_bfloat16*>(x_bf16), n,
-                                                  static_cast<__nv_bfloat16*>(out_bf16), L->timeout_ns, L->error_word);
+    if (B > 0) {
+        tp_peer_reduce_kernel<<<blocks, 256, 0, st>>>(L->peers, L->epoch_dev, static_cast<const __nv_bfloat16*>(x_bf16),
+                                                      n, static_cast<__nv_bfloat16*>(out_bf16), L->timeout_ns,
+                                                      L->error_word);
+        ATT_TRY(launch_status());
+    }
+    tp_done_kernel<<<1, 32, 0, st>>>(L->peers, L->epoch_dev);
     return launch_status();
 }
 

@@ -138,7 +138,7 @@ def attention(batch: int, ctx_min: int, ctx_max: int, split: int, iters: int, nq
             "split_tokens": split, "max_splits": max_splits}
 
 
-def attn_block(batch: int, ctx_min: int, ctx_max: int, iters: int, tp: int = 8) -> dict:
+def attn_block(batch: int, ctx_min: int, ctx_max: int, iters: int, tp: int = 8, use_graph: bool = False) -> dict:
     """One TP rank's decode step of the config-4 attention block (rank 0's
     weight slice, its own cache) with the rank-local residual add in place of
     the TP sum (tp_size 1 on this GPU)."""
@@ -148,7 +148,7 @@ def attn_block(batch: int, ctx_min: int, ctx_max: int, iters: int, tp: int = 8) 
     shape = synth.GLM_ATTN
     rng = np.random.default_rng(0)
     ctx = rng.integers(ctx_min, ctx_max + 1, size=batch)
-    steps = iters + 2
+    steps = iters + 3
     pages = (ctx + steps + A.PAGE - 1) // A.PAGE
     num_pages, max_pages = int(pages.sum()), int(pages.max())
     perm = rng.permutation(num_pages).astype(np.int32)
@@ -168,19 +168,32 @@ def attn_block(batch: int, ctx_min: int, ctx_max: int, iters: int, tp: int = 8) 
     blk = A.AttnBlock(local, wr, max_batch=batch, max_pages_per_seq=max_pages, max_context=max_pages * A.PAGE)
     ptd = torch.from_numpy(pt).to(dev)
     out = torch.empty_like(x)
+    poss = [torch.from_numpy((ctx + i).astype(np.int32)).to(dev) for i in range(steps)]
+    pos_buf = poss[0].clone()
     step = [0]
+    graph = None
+    if use_graph:
+        blk.decode(x, pos_buf, ptd, kc, vc, out=out)          # kernel attributes outside the capture
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            blk.decode(x, pos_buf, ptd, kc, vc, out=out)
 
     def run():
-        pos = torch.from_numpy((ctx + step[0]).astype(np.int32)).to(dev)
+        pos_buf.copy_(poss[step[0] % steps], non_blocking=True)
         step[0] += 1
-        blk.decode(x, pos, ptd, kc, vc, out=out)
+        if graph is not None:
+            graph.replay()
+        else:
+            blk.decode(x, pos_buf, ptd, kc, vc, out=out)
 
     ms = _time(run, iters)
     blk.check_error()
     blk.close()
     kv = int(ctx.sum()) * 2 * nkv * A.HEAD_DIM * 2
     wbytes = sum(v.numel() * v.element_size() for k_, v in wr.items() if k_ != "gamma")
-    return {"block_ms": ms, "kv_bytes": kv, "weight_bytes": wbytes, "context_tokens": int(ctx.sum()),
+    return {"block_ms": ms, "graph": use_graph, "kv_bytes": kv, "weight_bytes": wbytes,
+            "context_tokens": int(ctx.sum()),
             "achieved_gbs": (kv + wbytes) / (ms * 1e-3) / 1e9, "split_tokens": blk.split_tokens}
 
 
@@ -191,6 +204,7 @@ def main() -> int:
     ap.add_argument("--ctx-min", type=int, default=1024)
     ap.add_argument("--ctx-max", type=int, default=32768)
     ap.add_argument("--split", type=int, default=512)
+    ap.add_argument("--graph", action="store_true", help="attn_block: replay each step from a CUDA graph")
     ap.add_argument("--tokens", type=int, default=4096)
     ap.add_argument("--experts", type=int, default=32)
     ap.add_argument("--iters", type=int, default=3)
@@ -199,7 +213,7 @@ def main() -> int:
     if a.case == "attention":
         res = attention(a.batch, a.ctx_min, a.ctx_max, a.split, a.iters)
     elif a.case == "attn_block":
-        res = attn_block(a.batch, a.ctx_min, a.ctx_max, a.iters)
+        res = attn_block(a.batch, a.ctx_min, a.ctx_max, a.iters, use_graph=a.graph)
     else:
         res = router(a.tokens, a.iters) if a.case == "router" else gemm(a.tokens, a.experts, a.iters)
     print(json.dumps({"case": a.case, "tokens": a.tokens, **res}), flush=True)
