@@ -463,13 +463,8 @@ moe_status_t attn_decode_paged(const void* q_bf16, const void* k_cache, const vo
     if (!a16(q_bf16) || !a16(k_cache) || !a16(v_cache) || !a16(workspace)) return MOE_ERR_INVALID_ARGUMENT;
     if (out_q && (!out_s || out_ld < B)) return MOE_ERR_INVALID_ARGUMENT;
     if (workspace_bytes < attn_decode_workspace_bytes(B, nq, max_splits)) return MOE_ERR_WORKSPACE;
-    static bool attr = false;
-    if (!attr) {
-        if (cudaFuncSetAttribute(decode_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(kDecodeSmem)) != cudaSuccess)
-            return MOE_ERR_CUDA;
-        attr = true;
-    }
+    static bool attr[kMaxDevices] = {};
+    if (smem_optin_once(decode_split_kernel, static_cast<int>(kDecodeSmem), attr) != cudaSuccess) return MOE_ERR_CUDA;
     DecodeParams p;
     p.q = static_cast<const __nv_bfloat16*>(q_bf16);
     p.k_cache = static_cast<const __nv_bfloat16*>(k_cache);

@@ -240,13 +240,9 @@ moe_status_t fp8_gemm_small(const void* a, const float* a_scale, int a_ld, int T
     const size_t need = ks > 1 ? static_cast<size_t>(ks) * T * N * sizeof(float) : 0;
     if (need && (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 15)))
         return MOE_ERR_WORKSPACE;
-    static bool attr = false;
+    static bool attr[kMaxDevices] = {};
     const int smem = kStages * kStageBytes > kToks * kRows * 4 ? kStages * kStageBytes : kToks * kRows * 4;
-    if (!attr) {
-        if (cudaFuncSetAttribute(gemm_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-            return MOE_ERR_CUDA;
-        attr = true;
-    }
+    if (smem_optin_once(gemm_small_kernel, smem, attr) != cudaSuccess) return MOE_ERR_CUDA;
     Params p;
     p.a = static_cast<const uint8_t*>(a);
     p.a_scale = a_scale;

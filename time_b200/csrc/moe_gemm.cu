@@ -554,20 +554,24 @@ cbwStatus_t launch_gemm(const cbwGroupedGemmArgs* a, int* error_word, cudaStream
     if (!encode_u8_2d(&tw, a->w, static_cast<uint64_t>(a->num_groups) * w_rows, a->K, kTileM)) return CBW_ERROR_INTERNAL;
     if (!encode_u8_2d(&ta, a->a, static_cast<uint64_t>(a->rows), a->K, 32)) return CBW_ERROR_INTERNAL;
 
-    static int sm_count = 0;
-    static bool attr_set[2] = {false, false};
+    static int sm_count[kMaxDevices] = {};
+    static bool attr_set[kMaxDevices] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (sm_count == 0) cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev);
-    if (!attr_set[kGated ? 1 : 0]) {
-        cudaError_t e = cudaFuncSetAttribute(grouped_fp8_gemm_kernel<kGated>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    int sms = 0;
+    if (dev >= 0 && dev < kMaxDevices && sm_count[dev] > 0) {
+        sms = sm_count[dev];
+    } else {
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (dev >= 0 && dev < kMaxDevices) sm_count[dev] = sms;
+    }
+    {
+        cudaError_t e = smem_optin_once(grouped_fp8_gemm_kernel<kGated>, C::kSmemBytes, attr_set);
         if (e != cudaSuccess) {
             std::fprintf(stderr, "cbwFp8BlockScaledGroupedGemm: shared memory opt-in (%d B) failed: %s\n",
                          C::kSmemBytes, cudaGetErrorString(e));
             return CBW_ERROR_EXECUTION_FAILED;
         }
-        attr_set[kGated ? 1 : 0] = true;
     }
     GemmParams p;
     p.a_scale = a->a_scale;
@@ -583,7 +587,7 @@ cbwStatus_t launch_gemm(const cbwGroupedGemmArgs* a, int* error_word, cudaStream
     p.N = a->N;
     p.w_rows = w_rows;
     p.error_word = error_word;
-    grouped_fp8_gemm_kernel<kGated><<<sm_count, kNumThreads, C::kSmemBytes, stream>>>(tw, ta, p);
+    grouped_fp8_gemm_kernel<kGated><<<sms, kNumThreads, C::kSmemBytes, stream>>>(tw, ta, p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         cudaFuncAttributes fa;

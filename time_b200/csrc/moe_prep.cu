@@ -771,13 +771,9 @@ moe_status_t moe_router_logits(const float* n, const float* router_w, const floa
     const int ti = blocks_for(1) <= 148 ? 1 : (blocks_for(2) <= 148 ? 2 : (blocks_for(4) <= 148 ? 4 : 2));
     const dim3 grid(etiles, (T + 16 * ti - 1) / (16 * ti));
     if (grid.y > 65535) return MOE_ERR_UNSUPPORTED;
-    static bool attr = false;
-    if (!attr) {
-        if (cudaFuncSetAttribute(router_logits_tile_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(r3_smem_bytes<4>())) != cudaSuccess)
-            return MOE_ERR_CUDA;
-        attr = true;
-    }
+    static bool attr[kMaxDevices] = {};
+    if (smem_optin_once(router_logits_tile_kernel<4>, static_cast<int>(r3_smem_bytes<4>()), attr) != cudaSuccess)
+        return MOE_ERR_CUDA;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (ti == 4)
         router_logits_tile_kernel<4><<<grid, kR3Threads, r3_smem_bytes<4>(), st>>>(n, router_w, router_bias, T, H, E,
@@ -850,11 +846,8 @@ moe_status_t moe_permute_padded(const int32_t* topk_idx, int T, int k, int e_beg
     if (!topk_idx || !counts || !seg_start || !pos || !row_token || !total_rows || row_capacity < 0) return MOE_ERR_INVALID_ARGUMENT;
     const size_t smem = static_cast<size_t>(3 * G + 32 * G) * sizeof(int);
     if (smem > 200 * 1024) return MOE_ERR_UNSUPPORTED;
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        attr = true;
-    }
+    static bool attr[kMaxDevices] = {};
+    if (smem_optin_once(permute_kernel, 200 * 1024, attr) != cudaSuccess) return MOE_ERR_CUDA;
     permute_kernel<<<1, kPermThreads, smem, static_cast<cudaStream_t>(stream)>>>(
         topk_idx, T, k, e_begin, e_end, num_shared, counts, seg_start, pos, row_token, total_rows,
         row_capacity, error_word, pad);

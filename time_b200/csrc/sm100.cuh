@@ -225,4 +225,22 @@ __device__ __forceinline__ uint16_t cvt_e4m3x2(float a, float b) {
     return r;
 }
 
+// ---------------------------------------------------------------- host
+
+constexpr int kMaxDevices = 64;
+
+// The dynamic shared-memory opt-in of `kernel` (an attribute of the current
+// device), made once per device; `done` holds the call site's per-device flags.
+template <typename F>
+inline cudaError_t smem_optin_once(F* kernel, int bytes, bool (&done)[kMaxDevices]) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const bool cached = dev >= 0 && dev < kMaxDevices;
+    if (cached && done[dev]) return cudaSuccess;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess && cached) done[dev] = true;
+    return e;
+}
+
 }  // namespace tb

@@ -103,7 +103,8 @@ def gemm(tokens: int, experts: int, iters: int) -> dict:
             "gemm_down_bytes": touched * w2 + rows * (I + I // 128 * 4) + rows * H * 2}
 
 
-def attention(batch: int, ctx_min: int, ctx_max: int, split: int, iters: int, nq: int = 12, nkv: int = 1) -> dict:
+def attention(batch: int, ctx_min: int, ctx_max: int, split: int, iters: int, nq: int = 12, nkv: int = 1,
+              cpu_sample: int = 0) -> dict:
     import numpy as np
     from . import attn as A
     dev = torch.device("cuda", 0)
@@ -133,9 +134,37 @@ def attention(batch: int, ctx_min: int, ctx_max: int, split: int, iters: int, nq
     assert int(err.item()) == 0
     kv_bytes = int(lens.sum()) * nkv * A.HEAD_DIM * 2 * 2
     io_bytes = batch * nq * A.HEAD_DIM * (2 + 2 + 1) + nq * batch * 4
-    return {"decode_ms": ms, "kv_bytes": kv_bytes, "algorithmic_bytes": kv_bytes + io_bytes,
-            "achieved_gbs": (kv_bytes + io_bytes) / (ms * 1e-3) / 1e9, "context_tokens": int(lens.sum()),
-            "split_tokens": split, "max_splits": max_splits}
+    out = {"decode_ms": ms, "kv_bytes": kv_bytes, "algorithmic_bytes": kv_bytes + io_bytes,
+           "achieved_gbs": (kv_bytes + io_bytes) / (ms * 1e-3) / 1e9, "context_tokens": int(lens.sum()),
+           "split_tokens": split, "max_splits": max_splits}
+    if cpu_sample > 0:
+        out["cpu_baseline"] = _attention_cpu(q, kc, vc, pt, lens, cpu_sample, 1.0 / 128 ** 0.5)
+    return out
+
+
+def _attention_cpu(q, kc, vc, pt, lens, n_seq: int, scale: float) -> dict:
+    """The CPU restatement of the reference's decode attention (the oracle,
+    one thread, float64) on the first n_seq sequences, scaled to the batch by
+    context tokens.  The reference engine has no CPU attention of its own."""
+    import time
+    import numpy as np
+    from oracle import oracle as O
+    qf = q.float().cpu().numpy()
+    tok = 0
+    t_cpu = 0.0
+    for b in range(min(n_seq, len(lens))):
+        n = (int(lens[b]) + 15) // 16
+        pages = pt[b, :n]
+        kb = kc[torch.from_numpy(pages).long().to(kc.device)].float().cpu().numpy()   # this sequence's pages
+        vb = vc[torch.from_numpy(pages).long().to(vc.device)].float().cpu().numpy()
+        t0 = time.perf_counter()
+        O.attn_decode_paged(qf[b], kb, vb, np.arange(n, dtype=np.int32), int(lens[b]), scale)
+        t_cpu += time.perf_counter() - t0
+        tok += int(lens[b])
+    per_tok = t_cpu / tok
+    return {"kind": "port", "cores": 1, "sample": f"{min(n_seq, len(lens))} of {len(lens)} sequences ({tok} tokens)",
+            "step_ms_est": per_tok * float(lens.sum()) * 1e3,
+            "kv_gbs": tok * kc.shape[2] * 128 * 2 * 2 / t_cpu / 1e9}
 
 
 def attn_block(batch: int, ctx_min: int, ctx_max: int, iters: int, tp: int = 8, use_graph: bool = False) -> dict:
@@ -205,13 +234,14 @@ def main() -> int:
     ap.add_argument("--ctx-max", type=int, default=32768)
     ap.add_argument("--split", type=int, default=512)
     ap.add_argument("--graph", action="store_true", help="attn_block: replay each step from a CUDA graph")
+    ap.add_argument("--cpu-sample", type=int, default=0, help="attention: time the CPU oracle on this many sequences")
     ap.add_argument("--tokens", type=int, default=4096)
     ap.add_argument("--experts", type=int, default=32)
     ap.add_argument("--iters", type=int, default=3)
     a = ap.parse_args()
     torch.cuda.set_device(0)
     if a.case == "attention":
-        res = attention(a.batch, a.ctx_min, a.ctx_max, a.split, a.iters)
+        res = attention(a.batch, a.ctx_min, a.ctx_max, a.split, a.iters, cpu_sample=a.cpu_sample)
     elif a.case == "attn_block":
         res = attn_block(a.batch, a.ctx_min, a.ctx_max, a.iters, use_graph=a.graph)
     else:
