@@ -128,7 +128,8 @@ int attn_block_split_tokens(const attn_block_t* block);
 
 /* tp_size > 1: each rank allocates attn_block_peer_bytes bytes that every rank
  * maps (CUDA IPC / symmetric memory), zero-fills them, waits until all ranks
- * have, and passes the mapped pointers (256-byte aligned), rank order.  Every
+ * have, and passes the mapped pointers (256-byte aligned), rank order, once
+ * per block (a second call is refused).  Every
  * rank must then call attn_block_decode every step, in the same order.  The
  * step keeps its pairing state on the device, so a step may be captured in a
  * CUDA graph and replayed (positions and page tables updated in place). */

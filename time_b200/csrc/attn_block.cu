@@ -345,6 +345,7 @@ size_t attn_block_peer_bytes(const attn_block_t* L) {
 
 moe_status_t attn_block_set_peer_buffers(attn_block_t* L, void* const* bufs, int n) {
     if (!L || !bufs || n != L->cfg.tp_size || n <= 1) return MOE_ERR_INVALID_ARGUMENT;
+    if (L->peer_mode) return MOE_ERR_INVALID_ARGUMENT;   // once: the flags in the buffers pair up with the epoch
     for (int r = 0; r < n; ++r) {
         if (!bufs[r] || (reinterpret_cast<uintptr_t>(bufs[r]) & 255)) return MOE_ERR_INVALID_ARGUMENT;
         L->peers.base[r] = static_cast<uint8_t*>(bufs[r]);
