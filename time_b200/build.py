@@ -37,7 +37,8 @@ LIBS = {
     "libcudawrap.so": (["cuda_wrappers.cu"], ["-lcudart"], []),
     "libncclwrap.so": (["nccl_wrappers.cu"], ["-lcudart", "-lnccl"], []),
     "libcublaswrap.so": (["cublas_wrappers.cu", "moe_gemm.cu"], ["-lcudart", "-lcublas", "-lcublasLt"], []),
-    "libkernels.so": (["kernels.cu", "moe_prep.cu", "moe_ep.cu", "moe_layer.cu", "attn.cu", "attn_block.cu", "gemm_small.cu"], ["-lcudart"], ["libcublaswrap.so", "libncclwrap.so"]),
+    "libkernels.so": (["kernels.cu", "moe_prep.cu", "moe_ep.cu", "moe_layer.cu", "attn.cu", "attn_block.cu", "gemm_small.cu",
+                       "st_loader.cpp"], ["-lcudart"], ["libcublaswrap.so", "libncclwrap.so"]),
 }
 
 
