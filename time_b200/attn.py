@@ -132,6 +132,7 @@ class AttnBlock:
     def __init__(self, shape, weights: dict, max_batch: int, max_pages_per_seq: int, max_context: int,
                  tp_size: int = 1, tp_rank: int = 0):
         import torch
+        self._h = None
         self.shape, self.tp_size, self.tp_rank = shape, tp_size, tp_rank
         self.nq, self.nkv = shape.num_q_heads // tp_size, shape.num_kv_heads // tp_size
         self._w = weights
@@ -185,4 +186,10 @@ class AttnBlock:
         if self._h:
             self._k.attn_block_destroy(self._h)
             self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 

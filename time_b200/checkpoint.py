@@ -81,6 +81,7 @@ def _p(a: np.ndarray) -> int:
 
 class Checkpoint:
     def __init__(self, path):
+        self._h = None
         self._k = lib()
         h = c_void_p()
         M.check("st_open", self._k.st_open(str(path).encode(), ctypes.byref(h)))
@@ -90,6 +91,12 @@ class Checkpoint:
         if self._h:
             self._k.st_close(self._h)
             self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
     def __enter__(self):
         return self
