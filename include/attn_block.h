@@ -43,6 +43,16 @@ moe_status_t attn_rope_kv_write(const void* qkv_bf16, int B, int nq, int nkv, in
                                 int max_pages, int page_size, int num_cache_pages, void* q_out_bf16, void* k_cache,
                                 void* v_cache, int32_t* seq_lens_out, int* error_word, cwStream_t stream);
 
+/* The same for rows that are tokens of several sequences (prefill chunks,
+ * batches indexed by request slot): row b uses page-table row row_seq[b] of
+ * page_table [num_seqs][max_pages].  A row whose row_seq is outside
+ * [0, num_seqs) is skipped (seq_lens_out 0) and sets *error_word = 7. */
+moe_status_t attn_rope_kv_write_rows(const void* qkv_bf16, int B, int nq, int nkv, int head_dim, int rot,
+                                     const float* inv_freq, const int32_t* positions, const int32_t* row_seq,
+                                     int num_seqs, const int32_t* page_table, int max_pages, int page_size,
+                                     int num_cache_pages, void* q_out_bf16, void* k_cache, void* v_cache,
+                                     int32_t* seq_lens_out, int* error_word, cwStream_t stream);
+
 /* Bytes of the split-partials workspace for attn_decode_paged. */
 size_t attn_decode_workspace_bytes(int B, int nq, int max_splits);
 
@@ -62,6 +72,16 @@ moe_status_t attn_decode_paged(const void* q_bf16, const void* k_cache, const vo
                                int nkv, int head_dim, int page_size, float scale, int split_tokens, int max_splits,
                                void* workspace, size_t workspace_bytes, void* out_bf16, void* out_q, float* out_s,
                                int out_ld, int* error_word, cwStream_t stream);
+
+/* The same over rows of several sequences: row b attends over the first
+ * seq_lens[b] positions of page-table row row_seq[b] (null: b).  Rows whose
+ * row_seq is outside [0, num_seqs) get zeros. */
+moe_status_t attn_decode_paged_rows(const void* q_bf16, const void* k_cache, const void* v_cache,
+                                    int num_cache_pages, const int32_t* page_table, int max_pages,
+                                    const int32_t* row_seq, int num_seqs, const int32_t* seq_lens, int B, int nq,
+                                    int nkv, int head_dim, int page_size, float scale, int split_tokens,
+                                    int max_splits, void* workspace, size_t workspace_bytes, void* out_bf16,
+                                    void* out_q, float* out_s, int out_ld, int* error_word, cwStream_t stream);
 
 /* out[t][i] = bf16(residual[t][i] + sum_{r < tp} partial_r[t][i]), the ranks
  * summed in fp32 in order 0..tp-1 so every rank gets the same bits.
@@ -151,9 +171,26 @@ moe_status_t attn_block_decode_partial(attn_block_t* block, const void* x_bf16, 
                                        const int32_t* page_table, int num_cache_pages, void* k_cache, void* v_cache,
                                        void* partial_bf16, void* workspace, size_t workspace_bytes, cwStream_t stream);
 
+/* Rows of several sequences in one call -- a prefill chunk (consecutive
+ * positions of one or more prompts) or a decode batch indexed by request
+ * slot: row r is the token at positions[r] of the sequence whose page-table
+ * row is row_seq[r] (page_table [num_seqs][max_pages_per_seq]; row_seq null
+ * means row r -> r).  Every row's K/V is written before any row attends, and
+ * row r attends over positions 0..positions[r] of its sequence, so the rows
+ * of one prompt are causal.  R <= max_batch.  attn_block_decode is this call
+ * with row_seq null and num_seqs = B. */
+moe_status_t attn_block_forward(attn_block_t* block, const void* x_bf16, int R, const int32_t* positions,
+                                const int32_t* row_seq, int num_seqs, const int32_t* page_table, int num_cache_pages,
+                                void* k_cache, void* v_cache, void* out_bf16, void* workspace, size_t workspace_bytes,
+                                cwStream_t stream);
+moe_status_t attn_block_forward_partial(attn_block_t* block, const void* x_bf16, int R, const int32_t* positions,
+                                        const int32_t* row_seq, int num_seqs, const int32_t* page_table,
+                                        int num_cache_pages, void* k_cache, void* v_cache, void* partial_bf16,
+                                        void* workspace, size_t workspace_bytes, cwStream_t stream);
+
 /* Reads and clears the device error word (synchronises `stream`):
  * MOE_ERR_DEVICE_TIMEOUT for a wait that gave up, MOE_ERR_INVALID_ARGUMENT for
- * positions, lengths or page ids outside the given tables. */
+ * positions, lengths, page ids or sequence rows outside the given tables. */
 moe_status_t attn_block_check_error(attn_block_t* block, cwStream_t stream);
 
 #ifdef __cplusplus

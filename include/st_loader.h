@@ -78,6 +78,14 @@ moe_status_t st_moe_layer_host(const st_model_t* model, const char* prefix, cons
                                float* router_w, float* router_bias, int* has_bias, uint8_t* w13, float* s13,
                                uint8_t* w2, float* s2);
 
+/* A dense FFN layer (GLM's first layers), tensors under `prefix`:
+ *   post_attention_layernorm.weight, mlp.{gate,up,down}_proj.weight (+ _scale_inv)
+ * in the layout of a one-expert moe_layer_weights_t: w13 = gate rows then up
+ * rows [2I][H], w2 [H][I] (router sizes 0). */
+moe_status_t st_dense_ffn_sizes(int hidden, int intermediate, st_moe_sizes_t* out);
+moe_status_t st_dense_ffn_host(const st_model_t* model, const char* prefix, int hidden, int intermediate, float* gamma,
+                               uint8_t* w13, float* s13, uint8_t* w2, float* s2);
+
 /* One tensor-parallel rank of an attention layer, tensors under `prefix`:
  *   input_layernorm.weight                     [H]
  *   self_attn.{q,k,v,o}_proj.weight            F8_E4M3 (q [nq*d][H], k/v [nkv*d][H], o [H][nq*d])

@@ -326,3 +326,64 @@ def attn_block_partial_ref(w: dict, x: np.ndarray, positions, page_table: np.nda
                                        1.0 / np.sqrt(d)).reshape(nq * d) for b in range(B)])
     aq, as_ = quant_rows_1x128(attn)
     return bf16_round(gemm_fp8_block(aq, as_, w["w_o"], w["s_o"]))
+
+
+# ---------------------------------------------------------------- serving engine (composition)
+
+class EngineRef:
+    """CPU restatement of the serving engine's forward (include/engine.h),
+    composed from the functions above with the engine's rounding points:
+    embedding rows (bf16 values) -> per layer the attention block
+    (attn_block_partial_ref, tp 1) and bf16(x + partial) -> the FFN block
+    (moe_ffn_experts, mode 0: RMSNorm, experts, shared expert, residual; a
+    dense layer is one expert with weight 1.0) -> final RMSNorm in double,
+    rounded to bf16 -> lm_head (bf16 weights, double dot products) -> fp32
+    logits.  The reference's layer sequence is src/terra/engine.t:1235-1371
+    (run_layer_forward_gpu) and its head engine.t:1432-1445.
+
+    layers: per layer {"attn": numpy gamma / w_qkv / s_qkv / w_o / s_o (the
+    tp 1 rank layout), "ffn": OracleWeights, "dense": bool}.  K/V caches are
+    fp32 copies [num_pages][16][nkv][128] per layer, written by forward()."""
+
+    def __init__(self, layers, embed, final_norm, lm_head, nq: int, nkv: int, rot: int, theta: float, eps: float,
+                 num_pages: int):
+        self.layers = layers
+        self.embed = np.asarray(embed, dtype=np.float32)
+        self.final_norm = np.asarray(final_norm, dtype=np.float64)
+        self.lm_head = np.asarray(lm_head, dtype=np.float64)
+        self.nq, self.nkv, self.rot, self.theta, self.eps = nq, nkv, rot, theta, eps
+        self.k = [np.zeros((num_pages, 16, nkv, 128), np.float32) for _ in layers]
+        self.v = [np.zeros((num_pages, 16, nkv, 128), np.float32) for _ in layers]
+
+    def forward(self, tokens, positions, page_rows: np.ndarray, routing=None, logits: bool = False,
+                own_routing: list | None = None):
+        """Rows = tokens at positions (page_rows [R][max_pages]: each row's page
+        table).  routing: per layer (idx [R][k], w [R][k]) to evaluate the
+        experts with (None for dense layers), or None to route here.
+        own_routing, when a list: receives per MoE layer this oracle's own
+        (idx, w, logits) for the same inputs.  Returns fp32 logits [R][V] or None."""
+        x = self.embed[np.asarray(tokens, dtype=np.int64)].astype(np.float32)
+        positions = np.asarray(positions, dtype=np.int64)
+        R = x.shape[0]
+        for l, L in enumerate(self.layers):
+            part = attn_block_partial_ref(L["attn"], x, positions, page_rows, self.k[l], self.v[l], self.nq,
+                                          self.nkv, self.rot, self.theta, self.eps)
+            x = bf16_round(x + part)
+            xb = f32_to_bf16_bits(x)
+            if L["dense"]:
+                out = moe_ffn_experts(L["ffn"], xb, np.zeros((R, 1), np.int32), np.ones((R, 1), np.float32))
+            else:
+                if own_routing is not None or routing is None:
+                    _, idx, w, lg = moe_ffn_forward(L["ffn"], xb, mode=0)
+                    if own_routing is not None:
+                        own_routing.append((idx, w, lg))
+                if routing is not None:
+                    idx, w = routing[l]
+                out = moe_ffn_experts(L["ffn"], xb, idx, w, mode=0)
+            x = bf16_bits_to_f32(out)
+        if not logits:
+            return None
+        x64 = x.astype(np.float64)
+        inv = 1.0 / np.sqrt((x64 * x64).mean(axis=1, keepdims=True) + self.eps)
+        xn = bf16_round((x64 * inv * self.final_norm).astype(np.float32)).astype(np.float64)
+        return (xn @ self.lm_head.T).astype(np.float32)

@@ -1,7 +1,9 @@
-"""The C-ABI boundary: the four libraries load (no GPU needed to load) and
-export every entry point include/*.h declares, including the full symbol sets
-of the reference's headers (csrc/kernels.h:12-31, cublas_wrappers.h:51-67,
-nccl_wrappers.h:47-61, cuda_wrappers.h:24-45).  No compute calls here."""
+"""The C-ABI boundary: the libraries load (no GPU needed to load) and export
+every entry point include/*.h declares, including the full symbol sets of the
+reference's headers (csrc/kernels.h:12-31, cublas_wrappers.h:51-67,
+nccl_wrappers.h:47-61, cuda_wrappers.h:24-45) and the engine.so functions the
+reference's server binds (src/server/engine_wrapper.py:64-98).  No compute
+calls here."""
 import ctypes
 import re
 import subprocess
@@ -19,6 +21,9 @@ HEADER_LIB = {
     "cublas_wrappers.h": "libcublaswrap.so",
     "kernels.h": "libkernels.so",
     "moe_layer.h": "libkernels.so",
+    "attn_block.h": "libkernels.so",
+    "st_loader.h": "libkernels.so",
+    "engine.h": "engine.so",
 }
 
 # the reference's exported symbol counts per header
@@ -85,3 +90,15 @@ def test_libraries_load_without_gpu(libdir):
     c = libs["libcudawrap.so"]
     c.cwGetErrorString.restype = ctypes.c_char_p
     assert c.cwGetErrorString(2) == b"Out of memory"
+
+
+# the engine.so functions src/server/engine_wrapper.py:64-98 binds
+ENGINE_WRAPPER_SYMBOLS = ["init_engine", "prefill_opaque", "decode_step_opaque", "free_request_opaque", "free_engine",
+                          "get_engine_info", "run_batch_decode_ext"]
+
+
+def test_engine_wrapper_symbols(libdir):
+    syms = exported(libdir / "engine.so")
+    assert all(n in syms for n in ENGINE_WRAPPER_SYMBOLS), [n for n in ENGINE_WRAPPER_SYMBOLS if n not in syms]
+    names = declared_functions(INCLUDE / "engine.h")
+    assert names[:7] == ENGINE_WRAPPER_SYMBOLS, names[:7]

@@ -1,10 +1,10 @@
 """B200-native (sm_100a) MoE decoder-layer forward for the GLM-4.x-FP8 engine
 of kollarsandor/time.
 
-The product is the four C-ABI shared libraries in ``time_b200/lib`` (built by
+The product is the C-ABI shared libraries in ``time_b200/lib`` (built by
 ``python -m time_b200.build``), drop-in replacements for the reference's
-libcudawrap / libncclwrap / libcublaswrap / libkernels plus the MoE entry
-points of ``include/moe_layer.h``.  This Python package only loads them
+libcudawrap / libncclwrap / libcublaswrap / libkernels / engine.so plus the
+MoE, attention and loader entry points of ``include/``.  This Python package only loads them
 (:func:`load`) and mirrors the reference's ctypes-driver style for tests and
 benchmarks (:mod:`time_b200.moe`).  There is no CPU fallback: if the libraries
 are missing, :func:`load` raises.
@@ -15,7 +15,7 @@ import ctypes
 from pathlib import Path
 
 LIB_DIR = Path(__file__).resolve().parent / "lib"
-LIB_NAMES = ("libcudawrap.so", "libncclwrap.so", "libcublaswrap.so", "libkernels.so")
+LIB_NAMES = ("libcudawrap.so", "libncclwrap.so", "libcublaswrap.so", "libkernels.so", "engine.so")
 
 _loaded: dict[str, ctypes.CDLL] = {}
 
@@ -25,7 +25,7 @@ def lib_path(name: str) -> Path:
 
 
 def load() -> dict[str, ctypes.CDLL]:
-    """Load (once) and return the four libraries keyed by file name.
+    """Load (once) and return the libraries keyed by file name.
 
     Raises RuntimeError if any is missing -- the CUDA path is the only path.
     """
@@ -36,6 +36,12 @@ def load() -> dict[str, ctypes.CDLL]:
         raise RuntimeError(
             f"time_b200 native libraries missing: {', '.join(missing)} in {LIB_DIR}; "
             "run `python -m time_b200.build` (needs nvcc)")
+    try:
+        # torch's CUDA library resolves its NCCL symbols at import; loading the
+        # system NCCL globally (through libncclwrap) first would shadow them
+        import torch  # noqa: F401
+    except ImportError:
+        pass
     for n in LIB_NAMES:
         _loaded[n] = ctypes.CDLL(str(lib_path(n)), mode=ctypes.RTLD_GLOBAL)
     return _loaded

@@ -58,6 +58,10 @@ def lib():
                c_void_p]
         k.attn_block_decode.argtypes = blk
         k.attn_block_decode_partial.argtypes = blk
+        rows = [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p,
+                c_void_p, c_size_t, c_void_p]
+        k.attn_block_forward.argtypes = rows
+        k.attn_block_forward_partial.argtypes = rows
         k.attn_block_check_error.argtypes = [c_void_p, c_void_p]
         k.fp8_gemm_small_workspace_bytes.argtypes = [c_int, c_int, c_int]
         k.fp8_gemm_small_workspace_bytes.restype = c_size_t
@@ -178,6 +182,17 @@ class AttnBlock:
         import torch
         out = torch.empty_like(x) if out is None else out
         return self._call(self._k.attn_block_decode_partial, x, positions, page_table, k_cache, v_cache, out, stream)
+
+    def forward(self, x, positions, row_seq, page_table, k_cache, v_cache, out=None, partial=False, stream=None):
+        """Rows of several sequences (prefill chunks, slot-indexed batches):
+        row r is the token at positions[r] of page-table row row_seq[r]."""
+        import torch
+        out = torch.empty_like(x) if out is None else out
+        fn = self._k.attn_block_forward_partial if partial else self._k.attn_block_forward
+        M.check(fn.__name__, fn(self._h, M.ptr(x), x.shape[0], M.ptr(positions), M.ptr(row_seq), page_table.shape[0],
+                                M.ptr(page_table), k_cache.shape[0], M.ptr(k_cache), M.ptr(v_cache), M.ptr(out),
+                                M.ptr(self.workspace), self.workspace.numel(), M.stream_ptr(stream)))
+        return out
 
     def check_error(self, stream=None):
         M.check("attn_block_check_error", self._k.attn_block_check_error(self._h, M.stream_ptr(stream)))

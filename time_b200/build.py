@@ -1,4 +1,4 @@
-"""Build the four C-ABI libraries of this package in-tree for sm_100a.
+"""Build the C-ABI libraries of this package in-tree for sm_100a.
 
     python -m time_b200.build            # incremental
     python -m time_b200.build --force
@@ -8,7 +8,11 @@ Outputs (time_b200/lib/):
     libncclwrap.so    csrc/nccl_wrappers.cu                       (reference libncclwrap)
     libcublaswrap.so  csrc/cublas_wrappers.cu + csrc/moe_gemm.cu  (reference libcublaswrap + grouped GEMM)
     libkernels.so     csrc/kernels.cu + csrc/moe_prep.cu + csrc/moe_ep.cu + csrc/moe_layer.cu
-                      (reference libkernels + the MoE layer; links the two above)
+                      + csrc/attn.cu + csrc/attn_block.cu + csrc/gemm_small.cu + csrc/st_loader.cpp
+                      (reference libkernels + the MoE layer, the attention block and the
+                      checkpoint loader; links the two above)
+    engine.so         csrc/engine.cpp + csrc/engine_kernels.cu
+                      (reference engine.so: the serving engine; links libkernels)
 
 Every library links the shared CUDA runtime so that device pointers and streams
 handed over by a host framework are the same objects on both sides.
@@ -39,6 +43,8 @@ LIBS = {
     "libcublaswrap.so": (["cublas_wrappers.cu", "moe_gemm.cu"], ["-lcudart", "-lcublas", "-lcublasLt"], []),
     "libkernels.so": (["kernels.cu", "moe_prep.cu", "moe_ep.cu", "moe_layer.cu", "attn.cu", "attn_block.cu", "gemm_small.cu",
                        "st_loader.cpp"], ["-lcudart"], ["libcublaswrap.so", "libncclwrap.so"]),
+    "engine.so": (["engine.cpp", "engine_kernels.cu"], ["-lcudart", "-lcublas"],
+                  ["libkernels.so", "libcublaswrap.so", "libncclwrap.so"]),
 }
 
 
@@ -50,7 +56,7 @@ def nvcc() -> str:
 
 
 def _newest_header() -> float:
-    hs = list(CSRC.glob("*.cuh")) + list(INCLUDE.glob("*.h"))
+    hs = list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + list(INCLUDE.glob("*.h"))
     return max((h.stat().st_mtime for h in hs), default=0.0)
 
 
@@ -78,7 +84,7 @@ def build(force: bool = False, verbose: bool = False) -> None:
             msg = fut.result()
             if verbose:
                 print(msg)
-    order = ["libcudawrap.so", "libncclwrap.so", "libcublaswrap.so", "libkernels.so"]
+    order = ["libcudawrap.so", "libncclwrap.so", "libcublaswrap.so", "libkernels.so", "engine.so"]
     for name in order:
         srcs, links, deps = LIBS[name]
         out = LIB / name

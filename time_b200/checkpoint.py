@@ -239,3 +239,70 @@ def glm_tensors_from_synth(moe_w: dict, shape, layer: int, attn_w: dict | None =
             out[P + f"self_attn.{n}_proj.weight"] = ("F8_E4M3", attn_w["w_" + n].cpu().numpy())
             out[P + f"self_attn.{n}_proj.weight_scale_inv"] = ("F32", attn_w["s_" + n].cpu().numpy())
     return out
+
+
+def glm_model_tensors(shape, weights: dict, norm_dtype: str = "F32") -> dict:
+    """Every HF GLM-4.x-named tensor of a whole model from
+    synth.make_model_weights: model.embed_tokens.weight / lm_head.weight
+    (BF16), model.norm.weight, and per layer the attention, the layer norms and
+    the FFN (dense layers as mlp.{gate,up,down}_proj, MoE layers as
+    glm_tensors_from_synth writes them)."""
+    def bf16_bits(t):
+        return t.detach().cpu().contiguous().view(torch_u16()).numpy()
+
+    out = {
+        "model.embed_tokens.weight": ("BF16", bf16_bits(weights["embed"])),
+        "lm_head.weight": ("BF16", bf16_bits(weights["lm_head"])),
+        "model.norm.weight": ("F32", weights["final_norm"].detach().cpu().numpy().astype(np.float32)),
+    }
+    for l, layer in enumerate(weights["layers"]):
+        if not layer["dense"]:
+            out.update(glm_tensors_from_synth(layer["ffn"], shape.moe(), l, attn_w=layer["attn"],
+                                              router_dtype="F32", norm_dtype=norm_dtype))
+            continue
+        # the dense FFN: glm_tensors_from_synth's single expert, renamed
+        one = glm_tensors_from_synth(layer["ffn"], shape.dense(), l, attn_w=layer["attn"], router_dtype="F32",
+                                     norm_dtype=norm_dtype)
+        P = f"model.layers.{l}."
+        for name, v in one.items():
+            if name.startswith(P + "mlp.experts.0."):
+                out[name.replace("mlp.experts.0.", "mlp.")] = v
+            elif not name.startswith(P + "mlp.gate."):
+                out[name] = v
+    return out
+
+
+def torch_u16():
+    import torch
+    return torch.uint16 if hasattr(torch, "uint16") else torch.int16
+
+
+def write_model(directory, shape, weights: dict, shards: int = 1, tie_embeddings: bool = False) -> None:
+    """A model directory the engine's init_engine reads: config.json (HF
+    GLM-4.x keys) and the checkpoint (glm_model_tensors)."""
+    d = Path(directory)
+    d.mkdir(parents=True, exist_ok=True)
+    cfg = {
+        "architectures": ["Glm4MoeForCausalLM"],
+        "hidden_size": shape.hidden,
+        "num_hidden_layers": shape.num_layers,
+        "num_attention_heads": shape.num_q_heads,
+        "num_key_value_heads": shape.num_kv_heads,
+        "head_dim": shape.head_dim,
+        "partial_rotary_factor": shape.rotary_dim / shape.head_dim,
+        "vocab_size": shape.vocab_size,
+        "n_routed_experts": shape.num_experts,
+        "num_experts_per_tok": shape.top_k,
+        "moe_intermediate_size": shape.moe_intermediate,
+        "intermediate_size": shape.dense_intermediate,
+        "n_shared_experts": shape.num_shared,
+        "first_k_dense_replace": shape.first_dense,
+        "rope_theta": shape.rope_theta,
+        "rms_norm_eps": shape.eps,
+        "tie_word_embeddings": tie_embeddings,
+    }
+    (d / "config.json").write_text(json.dumps(cfg, indent=1))
+    tensors = glm_model_tensors(shape, weights)
+    if tie_embeddings:
+        del tensors["lm_head.weight"]
+    write_checkpoint(d, tensors, shards=shards)

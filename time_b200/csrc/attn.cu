@@ -49,12 +49,21 @@ inline moe_status_t launch_status() {
 
 // ---------------------------------------------------------------- RoPE + page write
 
+// Page-table row of row b: row_seq[b] when the rows are tokens of several
+// sequences (prefill chunks, slot-indexed batches), else b; -1 when outside
+// [0, num_seqs).
+__device__ __forceinline__ int seq_of_row(const int32_t* row_seq, int b, int num_seqs) {
+    const int s = row_seq ? row_seq[b] : b;
+    return (s >= 0 && s < num_seqs) ? s : -1;
+}
+
 // One 64-thread block per (token, head): heads 0..nq-1 are queries, the next
 // nkv keys (both rotated on their first `rot` dims, pairs i, i + rot/2), the
 // last nkv values (copied); k and v go to the token's page slot.
 __global__ void __launch_bounds__(64)
 rope_kv_write_kernel(const __nv_bfloat16* __restrict__ qkv, int nq, int nkv, int rot,
                      const float* __restrict__ inv_freq, const int32_t* __restrict__ positions,
+                     const int32_t* __restrict__ row_seq, int num_seqs,
                      const int32_t* __restrict__ page_table, int max_pages, int num_cache_pages,
                      __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ k_cache,
                      __nv_bfloat16* __restrict__ v_cache, int32_t* __restrict__ seq_lens_out,
@@ -62,12 +71,17 @@ rope_kv_write_kernel(const __nv_bfloat16* __restrict__ qkv, int nq, int nkv, int
     const int b = blockIdx.x, h = blockIdx.y;
     const int pos = positions[b];
     const int pidx = pos / kPage;
-    if (h == 0 && threadIdx.x == 0 && seq_lens_out) seq_lens_out[b] = pos >= 0 ? pos + 1 : 0;
+    const int seq = seq_of_row(row_seq, b, num_seqs);
+    if (h == 0 && threadIdx.x == 0 && seq_lens_out) seq_lens_out[b] = (pos >= 0 && seq >= 0) ? pos + 1 : 0;
+    if (seq < 0) {
+        if (h == 0 && threadIdx.x == 0 && error_word) atomicExch(error_word, 7);
+        return;
+    }
     if (pos < 0 || pidx >= max_pages) {
         if (h == 0 && threadIdx.x == 0 && error_word) atomicExch(error_word, 4);
         return;
     }
-    const int phys = page_table[static_cast<size_t>(b) * max_pages + pidx];
+    const int phys = page_table[static_cast<size_t>(seq) * max_pages + pidx];
     if (phys < 0 || phys >= num_cache_pages) {
         if (h == 0 && threadIdx.x == 0 && error_word) atomicExch(error_word, 6);
         return;
@@ -121,12 +135,13 @@ struct DecodeParams {
     const __nv_bfloat16* q;        // [B][nq][128]
     const __nv_bfloat16* k_cache;  // [pages][16][nkv][128]
     const __nv_bfloat16* v_cache;
-    const int32_t* page_table;     // [B][max_pages]
+    const int32_t* page_table;     // [num_seqs][max_pages]
+    const int32_t* row_seq;        // [B] page-table row of each row, or null (row b -> b)
     const int32_t* seq_lens;       // [B]
     float* part_o;                 // [B*nkv][max_splits][G][128]
     float* part_ml;                // [B*nkv][max_splits][G][2]  (max in log2 units, sum)
     int* error_word;
-    int nq, nkv, G, max_pages, num_cache_pages, split_tokens, max_splits;
+    int nq, nkv, G, max_pages, num_cache_pages, split_tokens, max_splits, num_seqs;
     float scale_log2;              // softmax scale * log2(e)
 };
 
@@ -150,6 +165,8 @@ decode_split_kernel(const DecodeParams p) {
     const int split = blockIdx.x;
     const int bk = blockIdx.y;                 // b * nkv + kv head
     const int b = bk / p.nkv, kvh = bk % p.nkv;
+    const int seq = seq_of_row(p.row_seq, b, p.num_seqs);
+    if (seq < 0) return;                       // recorded (7) by the page write; the merge writes zeros
     const int len_in = p.seq_lens[b];
     const int len = clamp_len(len_in, p.max_pages, p.split_tokens, p.max_splits);
     if (len != len_in && split == 0 && threadIdx.x == 0 && kvh == 0 && p.error_word) atomicExch(p.error_word, 5);
@@ -165,7 +182,7 @@ decode_split_kernel(const DecodeParams p) {
     const int page0 = t0 / kPage;
     const int npages = (t1 - 1) / kPage - page0 + 1;
     {
-        const int32_t* ptb = p.page_table + static_cast<size_t>(b) * p.max_pages + page0;
+        const int32_t* ptb = p.page_table + static_cast<size_t>(seq) * p.max_pages + page0;
         for (int i = threadIdx.x; i < npages; i += blockDim.x) {
             const int phys = ptb[i];
             // a page id outside the cache reads nothing (zeros) and records error 6
@@ -347,14 +364,14 @@ decode_split_kernel(const DecodeParams p) {
 // splits, normalise, write bf16 and optionally the e4m3 row + its scale.
 __global__ void __launch_bounds__(kD)
 decode_merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
-                    const int32_t* __restrict__ seq_lens, int nq, int nkv, int G, int max_pages, int split_tokens,
-                    int max_splits,
+                    const int32_t* __restrict__ seq_lens, const int32_t* __restrict__ row_seq, int num_seqs, int nq,
+                    int nkv, int G, int max_pages, int split_tokens, int max_splits,
                     __nv_bfloat16* __restrict__ out, uint8_t* __restrict__ out_q, float* __restrict__ out_s,
                     int out_ld) {
     const int b = blockIdx.x / nq, h = blockIdx.x % nq;
     const int kvh = h / G, r = h % G;
     const int d = threadIdx.x;
-    const int len = clamp_len(seq_lens[b], max_pages, split_tokens, max_splits);
+    const int len = seq_of_row(row_seq, b, num_seqs) < 0 ? 0 : clamp_len(seq_lens[b], max_pages, split_tokens, max_splits);
     const int ns = len > 0 ? (len + split_tokens - 1) / split_tokens : 0;
     const size_t bk = static_cast<size_t>(b) * nkv + kvh;
     float M = -INFINITY;
@@ -422,22 +439,32 @@ inline bool a16(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) ==
 
 extern "C" {
 
-moe_status_t attn_rope_kv_write(const void* qkv_bf16, int B, int nq, int nkv, int head_dim, int rot,
-                                const float* inv_freq, const int32_t* positions, const int32_t* page_table,
-                                int max_pages, int page_size, int num_cache_pages, void* q_out_bf16, void* k_cache,
-                                void* v_cache, int32_t* seq_lens_out, int* error_word, cwStream_t stream) {
+moe_status_t attn_rope_kv_write_rows(const void* qkv_bf16, int B, int nq, int nkv, int head_dim, int rot,
+                                     const float* inv_freq, const int32_t* positions, const int32_t* row_seq,
+                                     int num_seqs, const int32_t* page_table, int max_pages, int page_size,
+                                     int num_cache_pages, void* q_out_bf16, void* k_cache, void* v_cache,
+                                     int32_t* seq_lens_out, int* error_word, cwStream_t stream) {
     if (B < 0 || nq <= 0 || nkv <= 0 || nq % nkv || head_dim != kD || page_size != kPage) return MOE_ERR_INVALID_ARGUMENT;
-    if (num_cache_pages <= 0) return MOE_ERR_INVALID_ARGUMENT;
+    if (num_cache_pages <= 0 || num_seqs <= 0) return MOE_ERR_INVALID_ARGUMENT;
     if (rot < 0 || rot > kD || rot % 2 || max_pages <= 0) return MOE_ERR_INVALID_ARGUMENT;
     if (B == 0) return MOE_OK;
     if (!qkv_bf16 || (rot > 0 && !inv_freq) || !positions || !page_table || !q_out_bf16 || !k_cache || !v_cache)
         return MOE_ERR_INVALID_ARGUMENT;
     if (nq + 2 * nkv > 65535) return MOE_ERR_UNSUPPORTED;
     rope_kv_write_kernel<<<dim3(B, nq + 2 * nkv), 64, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const __nv_bfloat16*>(qkv_bf16), nq, nkv, rot, inv_freq, positions, page_table, max_pages,
-        num_cache_pages, static_cast<__nv_bfloat16*>(q_out_bf16), static_cast<__nv_bfloat16*>(k_cache),
+        static_cast<const __nv_bfloat16*>(qkv_bf16), nq, nkv, rot, inv_freq, positions, row_seq, num_seqs, page_table,
+        max_pages, num_cache_pages, static_cast<__nv_bfloat16*>(q_out_bf16), static_cast<__nv_bfloat16*>(k_cache),
         static_cast<__nv_bfloat16*>(v_cache), seq_lens_out, error_word);
     return launch_status();
+}
+
+moe_status_t attn_rope_kv_write(const void* qkv_bf16, int B, int nq, int nkv, int head_dim, int rot,
+                                const float* inv_freq, const int32_t* positions, const int32_t* page_table,
+                                int max_pages, int page_size, int num_cache_pages, void* q_out_bf16, void* k_cache,
+                                void* v_cache, int32_t* seq_lens_out, int* error_word, cwStream_t stream) {
+    return attn_rope_kv_write_rows(qkv_bf16, B, nq, nkv, head_dim, rot, inv_freq, positions, nullptr, B > 0 ? B : 1,
+                                   page_table, max_pages, page_size, num_cache_pages, q_out_bf16, k_cache, v_cache,
+                                   seq_lens_out, error_word, stream);
 }
 
 size_t attn_decode_workspace_bytes(int B, int nq, int max_splits) {
@@ -445,11 +472,13 @@ size_t attn_decode_workspace_bytes(int B, int nq, int max_splits) {
     return static_cast<size_t>(B) * nq * max_splits * (kD + 2) * sizeof(float);
 }
 
-moe_status_t attn_decode_paged(const void* q_bf16, const void* k_cache, const void* v_cache, int num_cache_pages,
-                               const int32_t* page_table, int max_pages, const int32_t* seq_lens, int B, int nq,
-                               int nkv, int head_dim, int page_size, float scale, int split_tokens, int max_splits,
-                               void* workspace, size_t workspace_bytes, void* out_bf16, void* out_q, float* out_s,
-                               int out_ld, int* error_word, cwStream_t stream) {
+moe_status_t attn_decode_paged_rows(const void* q_bf16, const void* k_cache, const void* v_cache,
+                                    int num_cache_pages, const int32_t* page_table, int max_pages,
+                                    const int32_t* row_seq, int num_seqs, const int32_t* seq_lens, int B, int nq,
+                                    int nkv, int head_dim, int page_size, float scale, int split_tokens,
+                                    int max_splits, void* workspace, size_t workspace_bytes, void* out_bf16,
+                                    void* out_q, float* out_s, int out_ld, int* error_word, cwStream_t stream) {
+    if (num_seqs <= 0) return MOE_ERR_INVALID_ARGUMENT;
     if (B < 0 || nq <= 0 || nkv <= 0 || nq % nkv || nq / nkv > kGPad || head_dim != kD || page_size != kPage)
         return MOE_ERR_INVALID_ARGUMENT;
     if (split_tokens <= 0 || split_tokens % kPage || split_tokens > kMaxSplitPages * kPage || max_splits <= 0 ||
@@ -470,6 +499,8 @@ moe_status_t attn_decode_paged(const void* q_bf16, const void* k_cache, const vo
     p.k_cache = static_cast<const __nv_bfloat16*>(k_cache);
     p.v_cache = static_cast<const __nv_bfloat16*>(v_cache);
     p.page_table = page_table;
+    p.row_seq = row_seq;
+    p.num_seqs = num_seqs;
     p.seq_lens = seq_lens;
     p.part_o = static_cast<float*>(workspace);
     p.part_ml = p.part_o + static_cast<size_t>(B) * nq * max_splits * kD;
@@ -486,11 +517,22 @@ moe_status_t attn_decode_paged(const void* q_bf16, const void* k_cache, const vo
     decode_split_kernel<<<dim3(max_splits, B * nkv), kWarps * 32, kDecodeSmem, st>>>(p);
     moe_status_t s = launch_status();
     if (s != MOE_OK) return s;
-    decode_merge_kernel<<<B * nq, kD, 0, st>>>(p.part_o, p.part_ml, seq_lens, nq, nkv, p.G, max_pages, split_tokens,
-                                              max_splits,
+    decode_merge_kernel<<<B * nq, kD, 0, st>>>(p.part_o, p.part_ml, seq_lens, row_seq, num_seqs, nq, nkv, p.G,
+                                              max_pages, split_tokens, max_splits,
                                               static_cast<__nv_bfloat16*>(out_bf16), static_cast<uint8_t*>(out_q),
                                               out_s, out_ld);
     return launch_status();
+}
+
+moe_status_t attn_decode_paged(const void* q_bf16, const void* k_cache, const void* v_cache, int num_cache_pages,
+                               const int32_t* page_table, int max_pages, const int32_t* seq_lens, int B, int nq,
+                               int nkv, int head_dim, int page_size, float scale, int split_tokens, int max_splits,
+                               void* workspace, size_t workspace_bytes, void* out_bf16, void* out_q, float* out_s,
+                               int out_ld, int* error_word, cwStream_t stream) {
+    return attn_decode_paged_rows(q_bf16, k_cache, v_cache, num_cache_pages, page_table, max_pages, nullptr,
+                                  B > 0 ? B : 1, seq_lens, B, nq, nkv, head_dim, page_size, scale, split_tokens,
+                                  max_splits, workspace, workspace_bytes, out_bf16, out_q, out_s, out_ld, error_word,
+                                  stream);
 }
 
 moe_status_t attn_tp_reduce_residual(const void* const* partials_dev, int tp, const void* residual_bf16, int T, int H,

@@ -255,8 +255,9 @@ moe_status_t gemm(const attn_block* L, int mode, int B, int K, int N, const void
     } while (0)
 
 // Steps 1-5: the rank's o_proj partial (bf16 [B][H]) into `partial`.
-moe_status_t run_partial(attn_block* L, const void* x, int B, const int32_t* positions, const int32_t* page_table,
-                         int num_cache_pages, void* k_cache, void* v_cache, void* partial, void* ws, cudaStream_t st) {
+moe_status_t run_partial(attn_block* L, const void* x, int B, const int32_t* positions, const int32_t* row_seq,
+                         int num_seqs, const int32_t* page_table, int num_cache_pages, void* k_cache, void* v_cache,
+                         void* partial, void* ws, cudaStream_t st) {
     const attn_block_config_t& c = L->cfg;
     const int H = c.hidden, nq = c.num_q_heads, nkv = c.num_kv_heads;
     ATT_TRY(moe_rmsnorm_quant(x, L->w.gamma, B, H, c.eps, at<float>(ws, L->off_rms), at<void>(ws, L->off_xq),
@@ -267,14 +268,15 @@ moe_status_t run_partial(attn_block* L, const void* x, int B, const int32_t* pos
     }
     ATT_TRY(gemm(L, CBW_GEMM_DOWN_BF16, B, H, L->nqkv, at<void>(ws, L->off_xq), at<float>(ws, L->off_xs), L->w.w_qkv,
                  L->w.s_qkv, ws, at<void>(ws, L->off_qkv), st));
-    ATT_TRY(attn_rope_kv_write(at<void>(ws, L->off_qkv), B, nq, nkv, kD, c.rotary_dim, L->inv_freq, positions,
-                               page_table, c.max_pages_per_seq, 16, num_cache_pages, at<void>(ws, L->off_q), k_cache,
-                               v_cache, at<int32_t>(ws, L->off_lens), L->error_word, st));
-    ATT_TRY(attn_decode_paged(at<void>(ws, L->off_q), k_cache, v_cache, num_cache_pages, page_table,
-                              c.max_pages_per_seq, at<int32_t>(ws, L->off_lens), B, nq, nkv, kD, 16,
-                              1.0f / std::sqrt(static_cast<float>(kD)), L->split_tokens, L->max_splits,
-                              at<void>(ws, L->off_dec), L->dec_bytes, at<void>(ws, L->off_out), at<void>(ws, L->off_aq),
-                              at<float>(ws, L->off_as), L->ld, L->error_word, st));
+    ATT_TRY(attn_rope_kv_write_rows(at<void>(ws, L->off_qkv), B, nq, nkv, kD, c.rotary_dim, L->inv_freq, positions,
+                                    row_seq, num_seqs, page_table, c.max_pages_per_seq, 16, num_cache_pages,
+                                    at<void>(ws, L->off_q), k_cache, v_cache, at<int32_t>(ws, L->off_lens),
+                                    L->error_word, st));
+    ATT_TRY(attn_decode_paged_rows(at<void>(ws, L->off_q), k_cache, v_cache, num_cache_pages, page_table,
+                                   c.max_pages_per_seq, row_seq, num_seqs, at<int32_t>(ws, L->off_lens), B, nq, nkv,
+                                   kD, 16, 1.0f / std::sqrt(static_cast<float>(kD)), L->split_tokens, L->max_splits,
+                                   at<void>(ws, L->off_dec), L->dec_bytes, at<void>(ws, L->off_out),
+                                   at<void>(ws, L->off_aq), at<float>(ws, L->off_as), L->ld, L->error_word, st));
     ATT_TRY(gemm(L, CBW_GEMM_DOWN_BF16, B, nq * kD, H, at<void>(ws, L->off_aq), at<float>(ws, L->off_as), L->w.w_o,
                  L->w.s_o, ws, partial, st));
     return MOE_OK;
@@ -361,22 +363,31 @@ moe_status_t attn_block_set_peer_buffers(attn_block_t* L, void* const* bufs, int
     return MOE_OK;
 }
 
-moe_status_t attn_block_decode_partial(attn_block_t* L, const void* x_bf16, int B, const int32_t* positions,
-                                       const int32_t* page_table, int num_cache_pages, void* k_cache, void* v_cache,
-                                       void* partial_bf16, void* workspace, size_t workspace_bytes, cwStream_t stream) {
-    if (!L || B < 0 || B > L->cfg.max_batch) return MOE_ERR_INVALID_ARGUMENT;
+moe_status_t attn_block_forward_partial(attn_block_t* L, const void* x_bf16, int B, const int32_t* positions,
+                                        const int32_t* row_seq, int num_seqs, const int32_t* page_table,
+                                        int num_cache_pages, void* k_cache, void* v_cache, void* partial_bf16,
+                                        void* workspace, size_t workspace_bytes, cwStream_t stream) {
+    if (!L || B < 0 || B > L->cfg.max_batch || num_seqs <= 0) return MOE_ERR_INVALID_ARGUMENT;
     if (B == 0) return MOE_OK;
     if (!x_bf16 || !positions || !page_table || !k_cache || !v_cache || !partial_bf16 || !workspace)
         return MOE_ERR_INVALID_ARGUMENT;
     if (workspace_bytes < L->bytes) return MOE_ERR_WORKSPACE;
-    return run_partial(L, x_bf16, B, positions, page_table, num_cache_pages, k_cache, v_cache, partial_bf16, workspace,
-                       static_cast<cudaStream_t>(stream));
+    return run_partial(L, x_bf16, B, positions, row_seq, num_seqs, page_table, num_cache_pages, k_cache, v_cache,
+                       partial_bf16, workspace, static_cast<cudaStream_t>(stream));
 }
 
-moe_status_t attn_block_decode(attn_block_t* L, const void* x_bf16, int B, const int32_t* positions,
-                               const int32_t* page_table, int num_cache_pages, void* k_cache, void* v_cache,
-                               void* out_bf16, void* workspace, size_t workspace_bytes, cwStream_t stream) {
-    if (!L || B < 0 || B > L->cfg.max_batch) return MOE_ERR_INVALID_ARGUMENT;
+moe_status_t attn_block_decode_partial(attn_block_t* L, const void* x_bf16, int B, const int32_t* positions,
+                                       const int32_t* page_table, int num_cache_pages, void* k_cache, void* v_cache,
+                                       void* partial_bf16, void* workspace, size_t workspace_bytes, cwStream_t stream) {
+    return attn_block_forward_partial(L, x_bf16, B, positions, nullptr, B > 0 ? B : 1, page_table, num_cache_pages,
+                                      k_cache, v_cache, partial_bf16, workspace, workspace_bytes, stream);
+}
+
+moe_status_t attn_block_forward(attn_block_t* L, const void* x_bf16, int B, const int32_t* positions,
+                                const int32_t* row_seq, int num_seqs, const int32_t* page_table, int num_cache_pages,
+                                void* k_cache, void* v_cache, void* out_bf16, void* workspace, size_t workspace_bytes,
+                                cwStream_t stream) {
+    if (!L || B < 0 || B > L->cfg.max_batch || num_seqs <= 0) return MOE_ERR_INVALID_ARGUMENT;
     if (!x_bf16 || !positions || !page_table || !k_cache || !v_cache || !out_bf16 || !workspace)
         return MOE_ERR_INVALID_ARGUMENT;
     if (workspace_bytes < L->bytes) return MOE_ERR_WORKSPACE;
@@ -387,8 +398,8 @@ moe_status_t attn_block_decode(attn_block_t* L, const void* x_bf16, int B, const
     if (L->cfg.tp_size == 1) {
         if (B == 0) return MOE_OK;
         void* part = at<void>(workspace, L->off_part);
-        ATT_TRY(run_partial(L, x_bf16, B, positions, page_table, num_cache_pages, k_cache, v_cache, part, workspace,
-                            st));
+        ATT_TRY(run_partial(L, x_bf16, B, positions, row_seq, num_seqs, page_table, num_cache_pages, k_cache, v_cache,
+                            part, workspace, st));
         residual_add_kernel<<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(part),
                                                     static_cast<const __nv_bfloat16*>(x_bf16), n,
                                                     static_cast<__nv_bfloat16*>(out_bf16));
@@ -399,8 +410,8 @@ moe_status_t attn_block_decode(attn_block_t* L, const void* x_bf16, int B, const
     tp_wait_done_kernel<<<1, 32, 0, st>>>(L->peers, L->epoch_dev, L->timeout_ns, L->error_word);
     ATT_TRY(launch_status());
     if (B > 0)
-        ATT_TRY(run_partial(L, x_bf16, B, positions, page_table, num_cache_pages, k_cache, v_cache, part, workspace,
-                            st));
+        ATT_TRY(run_partial(L, x_bf16, B, positions, row_seq, num_seqs, page_table, num_cache_pages, k_cache, v_cache,
+                            part, workspace, st));
     tp_signal_kernel<<<1, 32, 0, st>>>(L->peers, L->epoch_dev);
     ATT_TRY(launch_status());
     if (B > 0) {
@@ -413,6 +424,13 @@ moe_status_t attn_block_decode(attn_block_t* L, const void* x_bf16, int B, const
     return launch_status();
 }
 
+moe_status_t attn_block_decode(attn_block_t* L, const void* x_bf16, int B, const int32_t* positions,
+                               const int32_t* page_table, int num_cache_pages, void* k_cache, void* v_cache,
+                               void* out_bf16, void* workspace, size_t workspace_bytes, cwStream_t stream) {
+    return attn_block_forward(L, x_bf16, B, positions, nullptr, B > 0 ? B : 1, page_table, num_cache_pages, k_cache,
+                              v_cache, out_bf16, workspace, workspace_bytes, stream);
+}
+
 moe_status_t attn_block_check_error(attn_block_t* L, cwStream_t stream) {
     if (!L) return MOE_ERR_INVALID_ARGUMENT;
     int h = 0;
@@ -422,8 +440,8 @@ moe_status_t attn_block_check_error(attn_block_t* L, cwStream_t stream) {
         return MOE_ERR_CUDA;
     cudaMemsetAsync(L->error_word, 0, sizeof(int), st);
     if (h == 0) return MOE_OK;
-    // 1: a GEMM wait gave up, 3: a peer flag wait gave up; 4-6: positions,
-    // lengths or page ids outside the given tables
+    // 1: a GEMM wait gave up, 3: a peer flag wait gave up; 4-7: positions,
+    // lengths, page ids or sequence rows outside the given tables
     return (h == 1 || h == 3) ? MOE_ERR_DEVICE_TIMEOUT : MOE_ERR_INVALID_ARGUMENT;
 }
 

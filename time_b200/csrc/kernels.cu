@@ -16,8 +16,12 @@
 #include <cstdint>
 
 #include "kernels.h"
+#include "sampling.cuh"
 
 namespace {
+
+using tb::warp_argmax_first;
+using tb::warp_top_p;
 
 thread_local int g_last_error = 0;
 
@@ -319,24 +323,6 @@ __global__ void embedding_kernel(const T* __restrict__ table, const int64_t* __r
     for (int i = threadIdx.x; i < H; i += blockDim.x) o[i] = load_embed<T>(row + i);
 }
 
-// First index of the maximum, reference semantics (row[0] NaN -> 0; NaN never wins).
-__device__ __forceinline__ int warp_argmax_first(const float* row, int V, int lane) {
-    const float r0 = row[0];
-    if (isnan(r0)) return 0;
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
-    for (int i = lane; i < V; i += 32) {
-        const float v = row[i];
-        if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
-    }
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-    }
-    return (bi == 0x7fffffff) ? 0 : bi;
-}
-
 __global__ void argmax_kernel(const float* __restrict__ logits, int64_t* __restrict__ out, int V, int B) {
     const int b = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
@@ -345,47 +331,13 @@ __global__ void argmax_kernel(const float* __restrict__ logits, int64_t* __restr
     if (lane == 0) out[b] = i;
 }
 
-// csrc/kernels.cu:236-262: max, sum of exp((l - max)/T) in index order, then
-// the first index whose running sum reaches rand * top_p * sum.  The fp32
-// running sums are formed in index order exactly as the reference's loop;
-// the warp only parallelises the expf evaluations.
 __global__ void top_p_kernel(const float* __restrict__ logits, int64_t* __restrict__ out, float temperature,
                              float top_p, int V, int B, const uint64_t* __restrict__ seeds) {
     const int b = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (b >= B) return;
-    const float* row = logits + static_cast<size_t>(b) * V;
-    float m = row[0];
-    {
-        float lm = -INFINITY;
-        for (int i = lane; i < V; i += 32) lm = fmaxf(lm, row[i]);
-        for (int o = 16; o > 0; o >>= 1) lm = fmaxf(lm, __shfl_xor_sync(0xffffffffu, lm, o));
-        if (!isnan(m)) m = lm;
-    }
-    float sum = 0.0f;
-    for (int base = 0; base < V; base += 32) {
-        const int i = base + lane;
-        const float e = (i < V) ? expf((row[i] - m) / temperature) : 0.0f;
-        const int cnt = min(32, V - base);
-        for (int j = 0; j < cnt; ++j) sum += __shfl_sync(0xffffffffu, e, j);
-    }
-    const float threshold = top_p * sum;
-    const uint64_t seed = seeds[b];
-    const float rv = static_cast<float>(seed & 0xFFFFFFFFull) / 4294967296.0f;
-    const float target = rv * threshold;
-    float cum = 0.0f;
-    int selected = 0;
-    bool found = false;
-    for (int base = 0; base < V && !found; base += 32) {
-        const int i = base + lane;
-        const float e = (i < V) ? expf((row[i] - m) / temperature) : 0.0f;
-        const int cnt = min(32, V - base);
-        for (int j = 0; j < cnt; ++j) {
-            cum += __shfl_sync(0xffffffffu, e, j);
-            if (cum >= target) { selected = base + j; found = true; break; }
-        }
-    }
-    if (lane == 0) out[b] = selected;
+    const int i = warp_top_p(logits + static_cast<size_t>(b) * V, V, temperature, top_p, seeds[b], lane);
+    if (lane == 0) out[b] = i;
 }
 
 // Each distinct past token's logit is penalised once (the reference's

@@ -211,3 +211,79 @@ def attn_rank_slice(w: dict, shape: AttnShape, tp: int, rank: int) -> dict:
         "s_o": w["s_o"][:, qb].contiguous(),
     }
 
+
+
+# ---------------------------------------------------------------- whole model (serving)
+
+@dataclasses.dataclass(frozen=True)
+class ModelShape:
+    """A GLM-4.x decoder: `first_dense` dense-FFN layers, then MoE layers."""
+    hidden: int
+    num_layers: int
+    first_dense: int
+    num_q_heads: int
+    num_kv_heads: int
+    vocab_size: int
+    num_experts: int
+    top_k: int
+    moe_intermediate: int
+    num_shared: int
+    dense_intermediate: int
+    head_dim: int = 128
+    rotary_dim: int = 64
+    rope_theta: float = 1e6
+    eps: float = 1e-5
+
+    def attn(self) -> AttnShape:
+        return AttnShape(self.hidden, self.num_q_heads, self.num_kv_heads, self.head_dim, self.rotary_dim,
+                         self.rope_theta, self.eps)
+
+    def moe(self) -> MoEShape:
+        return MoEShape(self.hidden, self.num_experts, self.top_k, self.moe_intermediate, self.num_shared, self.eps)
+
+    def dense(self) -> MoEShape:
+        """The dense FFN as a one-expert MoE layer (weight 1.0, no shared expert)."""
+        return MoEShape(self.hidden, 1, 1, self.dense_intermediate, 0, self.eps)
+
+
+TINY_MODEL = ModelShape(hidden=256, num_layers=3, first_dense=1, num_q_heads=4, num_kv_heads=2, vocab_size=1000,
+                        num_experts=8, top_k=2, moe_intermediate=256, num_shared=1, dense_intermediate=512)
+# BASELINE config 5: 92 layers, the first 3 dense (I = 12288), vocabulary 151552
+GLM_MODEL = ModelShape(hidden=5120, num_layers=92, first_dense=3, num_q_heads=96, num_kv_heads=8,
+                       vocab_size=151552, num_experts=160, top_k=8, moe_intermediate=1536, num_shared=1,
+                       dense_intermediate=12288)
+
+
+def make_model_weights(shape: ModelShape, seed: int = 0, device="cpu", share_layers: bool = False) -> dict:
+    """Embedding bf16 [V][H] ~ N(0, 1), lm_head bf16 ~ N(0, 0.02), final-norm
+    and per-layer RMSNorm gammas 1 + 0.1 N(0, 1), and per layer the attention
+    (make_attn_weights) and FFN (make_moe_weights; the dense layers as one
+    expert) weights: layer l's projections from seed * 1000 + l + 1, its
+    gammas and FFN from a generator seeded seed * 1000 + 500 + l.  share_layers: one attention, one dense and one MoE weight set
+    reused by every layer (a whole-depth model in one GPU's memory for
+    timing; each layer still reads its full weights from HBM)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    H, V = shape.hidden, shape.vocab_size
+    out = {
+        "embed": torch.randn(V, H, generator=g, device=device, dtype=torch.float32).to(torch.bfloat16),
+        "lm_head": (torch.randn(V, H, generator=g, device=device, dtype=torch.float32) * 0.02).to(torch.bfloat16),
+        "final_norm": 1.0 + 0.1 * torch.randn(H, generator=g, device=device, dtype=torch.float32),
+    }
+    layers = []
+    cache = {}
+    for l in range(shape.num_layers):
+        dense = l < shape.first_dense
+        key = "dense" if dense else "moe"
+        if share_layers and key in cache:
+            layers.append(cache[key])
+            continue
+        lg = torch.Generator(device=device).manual_seed(seed * 1000 + 500 + l)
+        attn = make_attn_weights(shape.attn(), seed=seed * 1000 + l + 1, device=device)
+        attn["gamma"] = 1.0 + 0.1 * torch.randn(H, generator=lg, device=device, dtype=torch.float32)
+        ffn = make_moe_weights(shape.dense() if dense else shape.moe(), device=device, gen=lg)
+        ffn["gamma"] = 1.0 + 0.1 * torch.randn(H, generator=lg, device=device, dtype=torch.float32)
+        entry = {"attn": attn, "ffn": ffn, "dense": dense}
+        cache[key] = entry
+        layers.append(entry)
+    out["layers"] = layers
+    return out
