@@ -143,7 +143,9 @@ moe_status_t attn_block_create(const attn_block_config_t* cfg, const attn_block_
 moe_status_t attn_block_destroy(attn_block_t* block);
 /* Device workspace of one call (the caller's; one per stream). */
 size_t attn_block_workspace_bytes(const attn_block_t* block);
-/* Context split chosen for the decode kernel (tokens). */
+/* Context split of the decode kernel for a call of max_batch rows (tokens);
+ * a call with fewer rows may cut contexts finer (about two CTAs per SM at
+ * half the longest context, never more partials than the workspace holds). */
 int attn_block_split_tokens(const attn_block_t* block);
 
 /* tp_size > 1: each rank allocates attn_block_peer_bytes bytes that every rank

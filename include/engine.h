@@ -7,8 +7,14 @@
  * first seven functions below keep its names, argument order, return values
  * and error values, so the reference's NativeEngine loads this library
  * unchanged.  What differs, by design:
- *   - run_batch_decode_ext runs ONE forward over all unfinished requests
- *     (the reference loops run_decode_step per request, engine.t:1877-1903);
+ *   - run_batch_decode_ext runs the unfinished requests together (the
+ *     reference loops run_decode_step per request, engine.t:1877-1903), and
+ *     prefill_opaque admits a request whose prompt then runs with the next
+ *     decode step, batched with every other admitted prompt (the reference
+ *     runs each prompt at once, engine.t:1373-1410): a step's rows are every
+ *     position without K/V yet, request by request, in forwards of at most
+ *     prefill_chunk rows, the last forward ending with each request's newest
+ *     position -- the rows that are sampled;
  *   - layers are the B200 attention block (attn_block.h) and MoE layer
  *     (moe_layer.h) with bf16 activations, FP8 weights with 128x128 block
  *     scales and bf16 KV pages; the first `first_k_dense_replace` layers run
@@ -51,9 +57,10 @@ typedef struct glm_engine glm_engine_t;
  * short), with a line on stderr. */
 glm_engine_t* init_engine(const char* model_dir, int32_t max_batch, int32_t max_seq, int32_t num_gpus);
 
-/* Creates a request, runs its prompt (positions 0..seq_len-2) through every
- * layer and returns its state, or NULL (seq_len outside [1, max_seq], no free
- * request slot or KV pages, a device error). */
+/* Creates a request (a request slot, the KV pages of its prompt) and returns
+ * its state, or NULL (seq_len outside [1, max_seq], a token outside the
+ * vocabulary, no free request slot or KV pages).  The prompt's positions
+ * 0..seq_len-2 run through the layers with the next decode step. */
 void* prefill_opaque(glm_engine_t* engine, int64_t request_id, const int64_t* token_ids, int32_t seq_len,
                      float temperature, float top_p, float rep_penalty, int32_t max_tokens);
 
@@ -91,7 +98,7 @@ typedef struct {
     float rope_theta, rms_eps;
     int max_batch;           /* requests in flight (decode rows) */
     int max_seq;             /* tokens per request, prompt + generated */
-    int prefill_chunk;       /* rows per prefill forward; 0 = 256 */
+    int prefill_chunk;       /* rows per forward (admitted prompts are cut to it); 0 = 2048 */
     int num_cache_pages;     /* 16-token KV pages shared by all requests; 0 = max_batch * ceil(max_seq / 16) */
 } glm_engine_config_t;
 

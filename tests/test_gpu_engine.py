@@ -119,36 +119,35 @@ def test_attn_block_rows_prefill_and_slots(gpu):
     blk.close()
 
 
-def run_parity(eng, w_cpu, prompts, steps, shape, report):
-    """Prefill `prompts`, decode `steps` batched steps; compare every step's
-    logits with the oracle fed the same tokens and routing."""
+def run_parity(eng, w_cpu, prompts, steps, shape, report, rows_cap):
+    """Admit `prompts`, decode `steps` batched steps; compare every step's
+    logits with the oracle fed the same rows, tokens and routing.  A step's
+    rows (the engine's packing): every position without K/V yet, request by
+    request, then each request's newest position (the sampled rows); here
+    they fit one forward (rows_cap), so the captured routing covers them."""
     P = -(-96 // PS)
     ref = engine_ref(w_cpu, shape, P * len(prompts))
     tables = [np.arange(r * P, (r + 1) * P, dtype=np.int32) for r in range(len(prompts))]
-    states, toks = [], []
-    ties = [0, 0]
+    states, toks, kv = [], [], []
     for r, pr in enumerate(prompts):
         st = eng.prefill(100 + r, list(map(int, pr)), 0.0, 1.0, 1.0, 64)
         assert st is not None
         states.append(st)
         toks.append(list(map(int, pr)))
-        L = len(pr)
-        if L > 1:
-            rt = gpu_routing(eng, shape, L - 1)
-            own = []
-            ref.forward(pr[:-1], np.arange(L - 1), np.repeat(tables[r][None], L - 1, 0), routing=rt, own_routing=own)
-            t, b = near_tie_mismatches(rt, own, shape)
-            ties[0] += t
-            ties[1] += b
+        kv.append(0)
+    ties = [0, 0]
     worst = (0.0, 0.0)
     for step in range(steps):
+        rows = [(r, p) for r in range(len(toks)) for p in range(kv[r], len(toks[r]) - 1)]
+        rows += [(r, len(toks[r]) - 1) for r in range(len(toks))]
+        assert len(rows) <= rows_cap
         raw = eng.batch_decode_raw(states)
         R = len(states)
         lg = eng.copy_logits(R)
-        rt = gpu_routing(eng, shape, R)
+        rt = gpu_routing(eng, shape, len(rows))
         own = []
-        pos = [len(t) - 1 for t in toks]
-        lr = ref.forward([t[-1] for t in toks], pos, np.stack(tables), routing=rt, logits=True, own_routing=own)
+        lr = ref.forward([toks[r][p] for r, p in rows], [p for _, p in rows], np.stack([tables[r] for r, _ in rows]),
+                         routing=rt, logits=True, own_routing=own)[-R:]
         t, b = near_tie_mismatches(rt, own, shape)
         ties[0] += t
         ties[1] += b
@@ -156,6 +155,7 @@ def run_parity(eng, w_cpu, prompts, steps, shape, report):
         worst = (max(worst[0], mr), max(worst[1], mae))
         for i, (tok, done) in enumerate(raw):
             assert tok == int(np.argmax(lg[i])), (step, i)     # greedy: first maximum of the engine's logits
+            kv[i] = len(toks[i])
             toks[i].append(tok)
     report.update(max_rel=worst[0], mae=worst[1], routing_mismatch=ties[0], routing_mismatch_not_tie=ties[1])
     return states, toks
@@ -168,7 +168,7 @@ def test_engine_matches_oracle(gpu, model):
     rng = np.random.default_rng(7)
     prompts = [rng.integers(0, SHAPE.vocab_size, L) for L in (5, 17, 40)]
     rep = {}
-    run_parity(eng, w_cpu, prompts, 4, SHAPE, rep)
+    run_parity(eng, w_cpu, prompts, 4, SHAPE, rep, rows_cap=64)
     eng.check_error()
     print("engine vs oracle:", rep)
     assert rep["max_rel"] <= MAX_REL and rep["mae"] <= MAE, rep
@@ -202,7 +202,8 @@ def test_engine_batch_and_chunk_invariance(gpu, model):
     _, w_dev = model
     rng = np.random.default_rng(9)
     prompts = [list(map(int, rng.integers(0, SHAPE.vocab_size, L))) for L in (40, 12, 3)]
-    # A decoded alone (prefill in chunks of 8) vs in a batch of three (one 39-row prefill)
+    # A decoded alone (its prompt in forwards of at most 16 rows) vs in a batch
+    # of three (all prompts in one forward)
     e1 = EN.NativeEngine.from_weights(SHAPE, w_dev, max_batch=4, max_seq=96, prefill_chunk=8)
     e3 = EN.NativeEngine.from_weights(SHAPE, w_dev, max_batch=4, max_seq=96, prefill_chunk=64)
     s1 = e1.prefill(0, prompts[0], 0.0, 1.0, 1.0, 16)

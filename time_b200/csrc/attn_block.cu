@@ -254,6 +254,21 @@ moe_status_t gemm(const attn_block* L, int mode, int B, int K, int N, const void
         if (s_ != MOE_OK) return s_;        \
     } while (0)
 
+// Context split for a call of B rows: about two CTAs per SM at half the
+// longest context (256..4096 tokens), the same rule as at creation for
+// max_batch rows, then widened until the split partials of B rows fit the
+// workspace sized at creation.
+int split_for_rows(const attn_block* L, int B, int* max_splits) {
+    const attn_block_config_t& c = L->cfg;
+    const long long work = static_cast<long long>(B) * c.num_kv_heads * (c.max_context / 2 + 1);
+    int split = 256;
+    while (split < 4096 && work / split > 2 * 2 * 148) split *= 2;
+    const long long cap = static_cast<long long>(c.max_batch) * L->max_splits;
+    while (split < 8192 && static_cast<long long>(B) * ((c.max_context + split - 1) / split) > cap) split *= 2;
+    *max_splits = (c.max_context + split - 1) / split;
+    return split;
+}
+
 // Steps 1-5: the rank's o_proj partial (bf16 [B][H]) into `partial`.
 moe_status_t run_partial(attn_block* L, const void* x, int B, const int32_t* positions, const int32_t* row_seq,
                          int num_seqs, const int32_t* page_table, int num_cache_pages, void* k_cache, void* v_cache,
@@ -272,9 +287,11 @@ moe_status_t run_partial(attn_block* L, const void* x, int B, const int32_t* pos
                                     row_seq, num_seqs, page_table, c.max_pages_per_seq, 16, num_cache_pages,
                                     at<void>(ws, L->off_q), k_cache, v_cache, at<int32_t>(ws, L->off_lens),
                                     L->error_word, st));
+    int max_splits = 0;
+    const int split = split_for_rows(L, B, &max_splits);
     ATT_TRY(attn_decode_paged_rows(at<void>(ws, L->off_q), k_cache, v_cache, num_cache_pages, page_table,
                                    c.max_pages_per_seq, row_seq, num_seqs, at<int32_t>(ws, L->off_lens), B, nq, nkv,
-                                   kD, 16, 1.0f / std::sqrt(static_cast<float>(kD)), L->split_tokens, L->max_splits,
+                                   kD, 16, 1.0f / std::sqrt(static_cast<float>(kD)), split, max_splits,
                                    at<void>(ws, L->off_dec), L->dec_bytes, at<void>(ws, L->off_out),
                                    at<void>(ws, L->off_aq), at<float>(ws, L->off_as), L->ld, L->error_word, st));
     ATT_TRY(gemm(L, CBW_GEMM_DOWN_BF16, B, nq * kD, H, at<void>(ws, L->off_aq), at<float>(ws, L->off_as), L->w.w_o,

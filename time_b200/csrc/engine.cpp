@@ -7,23 +7,25 @@
 // state (create_request_state, engine.t:974-1030), the page allocator
 // (allocate_kv_pages / free_kv_pages, engine.t:793-856), prefill and decode
 // (run_prefill / run_decode_step, engine.t:1373-1512) and the opaque entry
-// points (engine.t:1833-1903).  Here a decode step is one forward over every
-// request in flight:
+// points (engine.t:1833-1903).  Here prefill_opaque only admits a request;
+// a decode step runs every request in flight together -- the positions of
+// admitted prompts that have no K/V yet, request by request, in forwards of
+// at most rows_cap rows, the last forward ending with each request's newest
+// position (the sampled rows).  One forward:
 //
-//   stage (pinned)   token, position, page-table row, seed, temperature, top_p
-//                    of every row -> one host-to-device copy
+//   stage (pinned)   token, position, page-table row of every row, and seed,
+//                    temperature, top_p of every sampled row -> one copy
 //   embed            bf16 rows
 //   per layer        attn_block_forward (RoPE + K/V page write + paged decode
 //                    attention + o_proj + residual), then the FFN: moe_layer_forward
 //                    (routed experts + shared expert + residual) or, for the
 //                    first dense layers, the same layer with one expert
-//   final norm       bf16 rows
-//   lm_head          cuBLAS bf16 GEMM, fp32 logits [rows][vocab]
+//   final norm       bf16, the sampled rows only
+//   lm_head          cuBLAS bf16 GEMM, fp32 logits [sampled rows][vocab]
 //   sample           one warp per row; the tokens come back in one copy
 //
-// A prefill is the same forward without the last three stages, over prompt
-// positions 0..L-2 in chunks of prefill_chunk rows (row_seq maps every row to
-// the request's page-table row, so the chunk attends causally).
+// row_seq maps every row to its request's page-table row, and every row's K/V
+// is written before any row attends, so prompt rows in one forward are causal.
 #include <cublas_v2.h>
 #include <cuda_runtime.h>
 
@@ -56,6 +58,7 @@ struct Request {
     int max_tokens = 0;
     float temperature = 1.0f, top_p = 1.0f, rep_penalty = 1.0f;
     std::vector<int32_t> pages;
+    int kv_len = 0;                // positions whose K/V are in the pages
     bool finished = false;
 };
 
@@ -169,7 +172,7 @@ struct Plan {
 
 Plan make_plan(const glm_engine_config_t& c) {
     Plan p{};
-    const int chunk = c.prefill_chunk > 0 ? c.prefill_chunk : 256;
+    const int chunk = c.prefill_chunk > 0 ? c.prefill_chunk : 2048;
     p.rows_cap = static_cast<int>(align_up(static_cast<size_t>(std::max(c.max_batch, chunk)), 16));
     p.max_pages_per_seq = (c.max_seq + kPage - 1) / kPage;
     p.num_pages = c.num_cache_pages > 0 ? c.num_cache_pages : c.max_batch * p.max_pages_per_seq;
@@ -218,7 +221,7 @@ moe_status_t create(const glm_engine_config_t* cfg, glm_engine** out) {
     glm_engine* E = new (std::nothrow) glm_engine();
     if (!E) return MOE_ERR_INVALID_ARGUMENT;
     E->cfg = *cfg;
-    if (E->cfg.prefill_chunk <= 0) E->cfg.prefill_chunk = 256;
+    if (E->cfg.prefill_chunk <= 0) E->cfg.prefill_chunk = 2048;
     const Plan p = make_plan(E->cfg);
     E->rows_cap = p.rows_cap;
     E->max_pages_per_seq = p.max_pages_per_seq;
@@ -358,8 +361,11 @@ void set_events(glm_engine* E, bool on) {
 }
 
 // One forward over R staged rows (already copied to the device).  With
-// `sample`: final norm, lm_head, sampler and the tokens copied back.
-moe_status_t forward(glm_engine* E, int R, bool sample) {
+// head > 0: rows [R - head, R) also go through the final norm, the lm_head
+// and the sampler (per-row parameters at stage indices 0..head-1), and the
+// tokens come back to tokens_host.
+moe_status_t forward(glm_engine* E, int R, int head) {
+    const bool sample = head > 0;
     const glm_engine_config_t& c = E->cfg;
     cudaStream_t st = E->stream;
     const int64_t* tokens = reinterpret_cast<const int64_t*>(E->stage_dev + E->stage.tokens);
@@ -392,21 +398,22 @@ moe_status_t forward(glm_engine* E, int R, bool sample) {
     if (!sample) return cudaStreamSynchronize(st) == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
     const size_t nl = E->layers.size();
     if (tm) cudaEventRecord(E->events[1 + 2 * nl], st);
-    ENG_CUDA(tb_engine::final_norm_rows(E->x0, E->final_norm, R, c.hidden, c.rms_eps, E->xn, st));
+    const void* head_x = static_cast<const uint8_t*>(E->x0) + static_cast<size_t>(R - head) * c.hidden * 2;
+    ENG_CUDA(tb_engine::final_norm_rows(head_x, E->final_norm, head, c.hidden, c.rms_eps, E->xn, st));
     // logits [R][V] (row-major) = xn [R][H] . lm_head [V][H]^T: column-major
     // C [V][R] = A^T B with A = lm_head as [H][V], B = xn as [H][R]
     const float one = 1.0f, zero = 0.0f;
-    if (cublasGemmEx(E->cublas, CUBLAS_OP_T, CUBLAS_OP_N, c.vocab_size, R, c.hidden, &one, E->lm_head, CUDA_R_16BF,
+    if (cublasGemmEx(E->cublas, CUBLAS_OP_T, CUBLAS_OP_N, c.vocab_size, head, c.hidden, &one, E->lm_head, CUDA_R_16BF,
                      c.hidden, E->xn, CUDA_R_16BF, c.hidden, &zero, E->logits, CUDA_R_32F, c.vocab_size,
                      CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT) != CUBLAS_STATUS_SUCCESS)
         return MOE_ERR_CUDA;
-    ENG_CUDA(tb_engine::sample_rows(E->logits, R, c.vocab_size,
+    ENG_CUDA(tb_engine::sample_rows(E->logits, head, c.vocab_size,
                                     reinterpret_cast<const float*>(E->stage_dev + E->stage.temp),
                                     reinterpret_cast<const float*>(E->stage_dev + E->stage.top_p),
                                     reinterpret_cast<const uint64_t*>(E->stage_dev + E->stage.seeds), E->tokens_out,
                                     st));
     if (tm) cudaEventRecord(E->events[2 + 2 * nl], st);
-    ENG_CUDA(cudaMemcpyAsync(E->tokens_host, E->tokens_out, static_cast<size_t>(R) * 8, cudaMemcpyDeviceToHost, st));
+    ENG_CUDA(cudaMemcpyAsync(E->tokens_host, E->tokens_out, static_cast<size_t>(head) * 8, cudaMemcpyDeviceToHost, st));
     ENG_CUDA(cudaStreamSynchronize(st));
     if (tm) {
         float ms = 0.0f, attn = 0.0f, ffn = 0.0f;
@@ -456,6 +463,8 @@ uint64_t reference_seed(int64_t request_id, int64_t past_len) {
     return s * 6364136223846793005ull + 1442695040888963407ull;
 }
 
+// Admits a request: checks, a request slot, KV pages for its prompt and its
+// page-table row.  Its prompt runs with the next decode step.
 Request* prefill(glm_engine* E, int64_t id, const int64_t* ids, int L, float temperature, float top_p,
                  float rep_penalty, int max_tokens) {
     if (L <= 0 || L > E->cfg.max_seq || !ids) return nullptr;
@@ -478,22 +487,7 @@ Request* prefill(glm_engine* E, int64_t id, const int64_t* ids, int L, float tem
         r->pages.push_back(E->free_pages.back());
         E->free_pages.pop_back();
     }
-    moe_status_t s = upload_pages(E, r, 0, need);
-    const int chunk = E->cfg.prefill_chunk;
-    for (int p0 = 0; s == MOE_OK && p0 < L - 1; p0 += chunk) {
-        const int R = std::min(chunk, L - 1 - p0);
-        int64_t* tok = reinterpret_cast<int64_t*>(E->stage_host + E->stage.tokens);
-        int32_t* pos = reinterpret_cast<int32_t*>(E->stage_host + E->stage.pos);
-        int32_t* rs = reinterpret_cast<int32_t*>(E->stage_host + E->stage.row_seq);
-        for (int i = 0; i < R; ++i) {
-            tok[i] = ids[p0 + i];
-            pos[i] = p0 + i;
-            rs[i] = r->slot;
-        }
-        s = upload_stage(E);
-        if (s == MOE_OK) s = forward(E, R, false);
-    }
-    if (s != MOE_OK) {
+    if (upload_pages(E, r, 0, need) != MOE_OK || cudaStreamSynchronize(E->stream) != cudaSuccess) {
         release(E, r);
         delete r;
         return nullptr;
@@ -526,31 +520,54 @@ int32_t batch_decode(glm_engine* E, void* const* states, int n, int64_t* out_tok
             E->free_pages.pop_back();
             if (upload_pages(E, r, pidx, pidx + 1) != MOE_OK) return -4;
         }
+        if (std::find(rows.begin(), rows.end(), r) != rows.end()) continue;   // a state passed twice
         row_of[i] = static_cast<int>(rows.size());
         rows.push_back(r);
-        if (static_cast<int>(rows.size()) > E->cfg.max_batch) return -4;   // cannot happen: one slot per request
     }
-    const int R = static_cast<int>(rows.size());
-    E->last_rows = R;
-    if (R == 0) return 0;
+    const int B = static_cast<int>(rows.size());
+    E->last_rows = B;
+    if (B == 0) return 0;
     int64_t* tok = reinterpret_cast<int64_t*>(E->stage_host + E->stage.tokens);
     uint64_t* seeds = reinterpret_cast<uint64_t*>(E->stage_host + E->stage.seeds);
     int32_t* pos = reinterpret_cast<int32_t*>(E->stage_host + E->stage.pos);
     int32_t* rs = reinterpret_cast<int32_t*>(E->stage_host + E->stage.row_seq);
     float* temp = reinterpret_cast<float*>(E->stage_host + E->stage.temp);
     float* topp = reinterpret_cast<float*>(E->stage_host + E->stage.top_p);
-    for (int b = 0; b < R; ++b) {
+    // Rows: every position whose K/V is not yet written (admitted prompts,
+    // chunked), request by request, in forwards of at most rows_cap rows;
+    // the last forward ends with each request's newest position, the rows
+    // that are sampled.
+    moe_status_t s = MOE_OK;
+    int fill = 0;
+    auto flush = [&](int head) {
+        if (s == MOE_OK) s = upload_stage(E);
+        if (s == MOE_OK) s = forward(E, fill, head);
+        fill = 0;
+    };
+    for (Request* r : rows) {
+        const int last = static_cast<int>(r->tokens.size()) - 1;
+        for (int p = r->kv_len; p < last && s == MOE_OK; ++p) {
+            tok[fill] = r->tokens[p];
+            pos[fill] = p;
+            rs[fill] = r->slot;
+            if (++fill == E->rows_cap) flush(0);
+        }
+    }
+    if (s == MOE_OK && fill + B > E->rows_cap) flush(0);
+    for (int b = 0; b < B && s == MOE_OK; ++b) {
         const Request* r = rows[b];
         const int64_t past_len = static_cast<int64_t>(r->tokens.size());
-        tok[b] = r->tokens.back();
-        pos[b] = static_cast<int32_t>(past_len - 1);
-        rs[b] = r->slot;
+        tok[fill + b] = r->tokens.back();
+        pos[fill + b] = static_cast<int32_t>(past_len - 1);
+        rs[fill + b] = r->slot;
         seeds[b] = reference_seed(r->id, past_len);
         temp[b] = r->temperature;
         topp[b] = r->top_p;
     }
-    moe_status_t s = upload_stage(E);
-    if (s == MOE_OK) s = forward(E, R, true);
+    if (s == MOE_OK) {
+        fill += B;
+        flush(B);
+    }
     if (s != MOE_OK) {
         for (Request* r : rows) r->finished = true;
         return -4;
@@ -559,6 +576,7 @@ int32_t batch_decode(glm_engine* E, void* const* states, int n, int64_t* out_tok
         if (row_of[i] < 0) continue;
         Request* r = rows[row_of[i]];
         const int64_t t = E->tokens_host[row_of[i]];
+        r->kv_len = static_cast<int>(r->tokens.size());
         r->tokens.push_back(t);
         r->generated += 1;
         if (r->generated >= r->max_tokens || static_cast<int>(r->tokens.size()) >= E->cfg.max_seq) r->finished = true;
@@ -593,6 +611,7 @@ bool upload_bf16_table(glm_engine* E, const st_model_t* M, const char* name, int
     void* d = nullptr;
     if (cudaMalloc(&d, n * 2) != cudaSuccess) return false;
     E->owned.push_back(d);
+    *out = d;
     if (t.dtype == ST_BF16) return cudaMemcpy(d, t.data, n * 2, cudaMemcpyHostToDevice) == cudaSuccess;
     if (t.dtype != ST_F16 && t.dtype != ST_F32) return false;
     std::vector<uint16_t> h(n);
@@ -611,7 +630,6 @@ bool upload_bf16_table(glm_engine* E, const st_model_t* M, const char* name, int
         }
         h[i] = f32_to_bf16_rne(v);
     }
-    *out = d;
     return cudaMemcpy(d, h.data(), n * 2, cudaMemcpyHostToDevice) == cudaSuccess;
 }
 
@@ -731,7 +749,10 @@ glm_engine* init_from_dir(const char* model_dir, int max_batch, int max_seq, int
         ok = ok && upload_owned(E, g.data(), H * 4, &fnorm);
     }
     if (!ok) std::fprintf(stderr, "init_engine: embedding, lm_head or final norm missing or malformed\n");
-    if (ok) ok = glm_engine_set_embedding(E, embed, static_cast<const float*>(fnorm), lm) == MOE_OK;
+    if (ok && glm_engine_set_embedding(E, embed, static_cast<const float*>(fnorm), lm) != MOE_OK) {
+        std::fprintf(stderr, "init_engine: embedding or lm_head not usable\n");
+        ok = false;
+    }
     st_attn_spec_t as{c.hidden, c.num_q_heads, c.num_kv_heads, c.head_dim, 1, 0};
     st_attn_sizes_t asz;
     ok = ok && st_attn_rank_sizes(&as, &asz) == MOE_OK;
@@ -754,7 +775,11 @@ glm_engine* init_from_dir(const char* model_dir, int max_batch, int max_seq, int
         ok = upload_owned(E, ag.b.data(), asz.gamma, &d0) && upload_owned(E, aqkv.b.data(), asz.w_qkv, &d1) &&
              upload_owned(E, asqkv.b.data(), asz.s_qkv, &d2) && upload_owned(E, ao.b.data(), asz.w_o, &d3) &&
              upload_owned(E, aso.b.data(), asz.s_o, &d4);
-        if (!ok) break;
+        if (!ok) {
+            std::fprintf(stderr, "init_engine: layer %d attention upload failed (%s)\n", l,
+                         cudaGetErrorString(cudaGetLastError()));
+            break;
+        }
         aw.gamma = static_cast<const float*>(d0);
         aw.w_qkv = d1;
         aw.s_qkv = static_cast<const float*>(d2);
@@ -799,7 +824,11 @@ glm_engine* init_from_dir(const char* model_dir, int max_batch, int max_seq, int
              (has_bias ? upload_owned(E, frb.b.data(), fs.router_bias, &e2) : true) &&
              upload_owned(E, fw13.b.data(), fs.w13, &e3) && upload_owned(E, fs13.b.data(), fs.s13, &e4) &&
              upload_owned(E, fw2.b.data(), fs.w2, &e5) && upload_owned(E, fs2.b.data(), fs.s2, &e6);
-        if (!ok) break;
+        if (!ok) {
+            std::fprintf(stderr, "init_engine: layer %d FFN upload failed (%s)\n", l,
+                         cudaGetErrorString(cudaGetLastError()));
+            break;
+        }
         moe_layer_weights_t fw{};
         fw.norm_gamma = static_cast<const float*>(e0);
         fw.router_w = static_cast<const float*>(e1);
@@ -814,9 +843,11 @@ glm_engine* init_from_dir(const char* model_dir, int max_batch, int max_seq, int
         }
     }
     st_close(M);
-    if (ok) ok = ensure_ready(E) == MOE_OK;
+    if (ok && ensure_ready(E) != MOE_OK) {
+        std::fprintf(stderr, "init_engine: workspace allocation failed\n");
+        ok = false;
+    }
     if (!ok) {
-        std::fprintf(stderr, "init_engine: failed (device memory or checkpoint)\n");
         destroy(E);
         return nullptr;
     }
@@ -1017,7 +1048,7 @@ moe_status_t glm_engine_stage_ms(glm_engine_t* E, float* out4) {
 size_t glm_engine_device_bytes(const glm_engine_config_t* cfg) {
     if (!cfg || !config_ok(*cfg)) return 0;
     glm_engine_config_t c = *cfg;
-    if (c.prefill_chunk <= 0) c.prefill_chunk = 256;
+    if (c.prefill_chunk <= 0) c.prefill_chunk = 2048;
     const Plan p = make_plan(c);
     return p.kv_bytes + 2 * p.act_bytes + static_cast<size_t>(c.max_batch) * c.hidden * 2 + p.logits_bytes +
            p.small_bytes;

@@ -6,6 +6,7 @@ hundred MB on the device, a handful of launches):
     python -m time_b200.profile_cases gemm   [--tokens 4096] [--experts 32] [--iters 3]
     python -m time_b200.profile_cases attention [--batch 64] [--ctx-min 1024] [--ctx-max 32768] [--iters 3]
     python -m time_b200.profile_cases attn_block [--batch 64] [--ctx-min 1024] [--ctx-max 32768] [--iters 3]
+    python -m time_b200.profile_cases serving [--batch 64] [--prompt 512] [--steps 10] [--layers 92]
 
 `router`: RMSNorm+quant (with the fp32 n rows), tiled router logits, top-k
 over T tokens of the GLM shape (hidden 5120, 160 experts; n is 84 MB at 4096
@@ -17,6 +18,15 @@ attention block (12 query heads over 1 KV head, head_dim 128, bf16 pages of
 [ctx-min, ctx-max] (seed 0); its bytes are the K and V pages it must read.
 `attn_block`: one TP rank's whole decode step of that block (rmsnorm, FP8
 QKV, RoPE + page write, decode, FP8 o_proj, residual) on this GPU.
+`serving`: the serving engine (engine.so) on the GLM-4.x shape of config 5
+(92 layers, the first 3 dense), one GPU: `batch` requests prefilled with
+`prompt` random tokens each, then batched greedy decode steps.  One weight set
+per layer kind is shared by all layers of that kind (the whole depth fits one
+GPU; each layer still streams its full weights from HBM, far more than L2);
+every layer has its own KV pages.  Reports prefill tokens/s (the first step,
+which runs every admitted prompt in forwards of up to 2048 rows), decode
+tokens/s (wall time of the synchronous engine calls) and the engine's
+per-stage device times of one decode step.
 Prints one line per stage with the mean CUDA-event time per launch.
 """
 from __future__ import annotations
@@ -226,9 +236,54 @@ def attn_block(batch: int, ctx_min: int, ctx_max: int, iters: int, tp: int = 8, 
             "achieved_gbs": (kv + wbytes) / (ms * 1e-3) / 1e9, "split_tokens": blk.split_tokens}
 
 
+def serving(batch: int, prompt: int, steps: int, layers: int, max_seq: int) -> dict:
+    import time
+
+    import numpy as np
+
+    from . import engine as EN
+    shape = dataclasses.replace(synth.GLM_MODEL, num_layers=layers)
+    dev = torch.device("cuda:0")
+    w = synth.make_model_weights(shape, seed=0, device=dev, share_layers=True)
+    torch.cuda.synchronize()
+    eng = EN.NativeEngine.from_weights(shape, w, max_batch=batch, max_seq=max_seq)
+    rng = np.random.default_rng(0)
+    prompts = [list(map(int, rng.integers(0, shape.vocab_size, prompt))) for _ in range(batch)]
+    states = [eng.prefill(i, p, 0.0, 1.0, 1.0, 1 << 20) for i, p in enumerate(prompts)]
+    assert all(s is not None for s in states)
+    # the first step runs every admitted prompt (positions 0..prompt-2 of all
+    # requests, in forwards of up to 2048 rows) and then one decode row each
+    t0 = time.perf_counter()
+    eng.batch_decode_raw(states)
+    prefill_s = time.perf_counter() - t0
+    for _ in range(3):
+        eng.batch_decode_raw(states)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        r = eng.batch_decode_raw(states)
+    dt = (time.perf_counter() - t0) / steps
+    assert r is not None and not any(d for _, d in r)
+    eng.set_timing(True)
+    eng.batch_decode_raw(states)
+    st = eng.stage_ms()
+    eng.check_error()
+    weights_gb = (sum(t.numel() * t.element_size() for t in w["layers"][0]["ffn"].values() if t is not None)
+                  + sum(t.numel() * t.element_size() for t in w["layers"][-1]["ffn"].values() if t is not None))
+    eng.shutdown()
+    return {"layers": layers, "batch": batch, "prompt": prompt, "max_seq": max_seq,
+            "prefill_tokens_per_s": batch * (prompt - 1) / prefill_s, "prefill_s": prefill_s,
+            "decode_ms_per_step": dt * 1e3, "decode_tokens_per_s": batch / dt,
+            "context_after": prompt + 4 + steps, "stage_ms_one_step": st,
+            "ffn_weight_sets_gb": weights_gb / 1e9}
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["router", "gemm", "attention", "attn_block"])
+    ap.add_argument("case", choices=["router", "gemm", "attention", "attn_block", "serving"])
+    ap.add_argument("--prompt", type=int, default=512)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--layers", type=int, default=92)
+    ap.add_argument("--max-seq", type=int, default=1024)
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--ctx-min", type=int, default=1024)
     ap.add_argument("--ctx-max", type=int, default=32768)
@@ -244,6 +299,8 @@ def main() -> int:
         res = attention(a.batch, a.ctx_min, a.ctx_max, a.split, a.iters, cpu_sample=a.cpu_sample)
     elif a.case == "attn_block":
         res = attn_block(a.batch, a.ctx_min, a.ctx_max, a.iters, use_graph=a.graph)
+    elif a.case == "serving":
+        res = serving(a.batch, a.prompt, a.steps, a.layers, a.max_seq)
     else:
         res = router(a.tokens, a.iters) if a.case == "router" else gemm(a.tokens, a.experts, a.iters)
     print(json.dumps({"case": a.case, "tokens": a.tokens, **res}), flush=True)
