@@ -122,12 +122,19 @@ moe_status_t glm_engine_set_layer(glm_engine_t* engine, int layer, const attn_bl
  * order of the states passed to it, finished ones skipped) into host memory. */
 moe_status_t glm_engine_copy_logits(glm_engine_t* engine, float* host_out, int rows);
 
-/* Routing capture, for checking the layers one by one: when on, every
- * forward (prefill chunk or decode step) keeps each MoE layer's top-k ids
- * and weights; glm_engine_copy_routing copies layer `layer`'s [rows][top_k]
- * of the last forward to host memory. */
+/* Test hooks, for checking the layers one by one.  Routing capture: when on,
+ * each MoE layer's top-k ids and weights of every row of a decode step (all
+ * its forwards, rows in the step's order) are kept; glm_engine_copy_routing
+ * copies layer `layer`'s first `rows` [rows][top_k] of the last step.  Capture
+ * synchronises after every forward. */
 moe_status_t glm_engine_set_capture(glm_engine_t* engine, int on);
 moe_status_t glm_engine_copy_routing(glm_engine_t* engine, int layer, int rows, int32_t* idx_host, float* w_host);
+/* A request's KV page ids (up to max_pages into out); returns the number of
+ * pages it holds, or -1 for an unknown state. */
+int glm_engine_request_pages(glm_engine_t* engine, const void* state, int32_t* out, int max_pages);
+/* Pages [page, page + npages) of layer `layer`'s K and V caches (bf16
+ * [npages][16][num_kv_heads][128]) into host memory. */
+moe_status_t glm_engine_copy_kv(glm_engine_t* engine, int layer, int page, int npages, void* k_host, void* v_host);
 
 /* Reads and clears every layer's device error word (synchronises). */
 moe_status_t glm_engine_check_error(glm_engine_t* engine);

@@ -198,26 +198,64 @@ def test_engine_from_checkpoint_bit_identical(gpu, model, tmp_path):
     b.shutdown()
 
 
-def test_engine_batch_and_chunk_invariance(gpu, model):
-    _, w_dev = model
+def test_engine_packings_match_oracle(gpu, model):
+    """Request A (40-token prompt) run three ways -- alone in one forward,
+    alone in forwards of at most 16 rows, and next to two other prompts in one
+    forward -- each compared with the oracle's run of A alone (fed the same
+    routing): the logits of its first sampled row, and every layer's K/V pages
+    of its 40 positions.  The three runs are also compared with one another."""
+    w_cpu, w_dev = model
     rng = np.random.default_rng(9)
     prompts = [list(map(int, rng.integers(0, SHAPE.vocab_size, L))) for L in (40, 12, 3)]
-    # A decoded alone (its prompt in forwards of at most 16 rows) vs in a batch
-    # of three (all prompts in one forward)
-    e1 = EN.NativeEngine.from_weights(SHAPE, w_dev, max_batch=4, max_seq=96, prefill_chunk=8)
-    e3 = EN.NativeEngine.from_weights(SHAPE, w_dev, max_batch=4, max_seq=96, prefill_chunk=64)
-    s1 = e1.prefill(0, prompts[0], 0.0, 1.0, 1.0, 16)
-    s3 = [e3.prefill(i, p, 0.0, 1.0, 1.0, 16) for i, p in enumerate(prompts)]
-    for _ in range(3):
-        t1 = e1.decode_step(s1)
-        r3 = e3.batch_decode_raw(s3)
-        l1, l3 = e1.copy_logits(1), e3.copy_logits(3)
-        mr, _ = O.max_rel_and_mae(l1[0], l3[0])
-        print("batch/chunk invariance max_rel", mr, "exact", np.array_equal(l1[0], l3[0]))
-        assert mr <= 1e-4, mr
-        assert t1[0] == r3[0][0]
-    e1.shutdown()
-    e3.shutdown()
+    A = prompts[0]
+    variants = {"alone_one_forward": (64, [A]), "alone_16_row_forwards": (8, [A]), "batched": (64, prompts)}
+    got = {}
+    for name, (chunk, ps) in variants.items():
+        eng = EN.NativeEngine.from_weights(SHAPE, w_dev, max_batch=4, max_seq=96, prefill_chunk=chunk)
+        eng.set_capture(True)
+        st = [eng.prefill(i, p, 0.0, 1.0, 1.0, 16) for i, p in enumerate(ps)]
+        eng.batch_decode_raw(st)
+        # the step's rows: prompts' positions 0..L-2 request by request, then the sampled rows
+        rows = [(i, q) for i, p in enumerate(ps) for q in range(len(p) - 1)] + [(i, len(p) - 1) for i, p in enumerate(ps)]
+        sel = [j for j, (i, _) in enumerate(rows) if i == 0]          # A's rows, positions 0..39
+        routing = []
+        for l in range(SHAPE.num_layers):
+            if l < SHAPE.first_dense:
+                routing.append(None)
+            else:
+                idx, w = eng.routing(l, len(rows), SHAPE.top_k)
+                routing.append((idx[sel], w[sel]))
+        pages = eng.request_pages(st[0])
+        kv = [eng.kv_pages(l, pages, SHAPE.num_kv_heads) for l in range(SHAPE.num_layers)]
+        got[name] = (eng.copy_logits(len(ps))[0], routing, kv)
+        eng.check_error()
+        eng.shutdown()
+    report = {}
+    for name, (lg, routing, kv) in got.items():
+        ref = engine_ref(w_cpu, SHAPE, 8)
+        table = np.arange(3, dtype=np.int32)[None]
+        lr = ref.forward(A, np.arange(40), np.repeat(table, 40, 0), routing=routing, logits=True)[-1]
+        mr, mae = O.max_rel_and_mae(lg, lr)
+        kvd = []
+        for l in range(SHAPE.num_layers):
+            k, v = kv[l]
+            kr = ref.k[l][:3].reshape(48, SHAPE.num_kv_heads, 128)[:40]
+            vr = ref.v[l][:3].reshape(48, SHAPE.num_kv_heads, 128)[:40]
+            kg = k.reshape(48, SHAPE.num_kv_heads, 128)[:40]
+            vg = v.reshape(48, SHAPE.num_kv_heads, 128)[:40]
+            kvd.append((float(np.abs(kg - kr).max() / np.abs(kr).max()), float(np.abs(vg - vr).max() / np.abs(vr).max())))
+        report[name] = {"logits_max_rel": mr, "logits_mae": mae, "kv_max_rel_per_layer": kvd}
+    names = list(got)
+    for a_, b_ in ((names[0], names[1]), (names[0], names[2])):
+        report[f"{a_}=={b_}"] = {"logits": bool(np.array_equal(got[a_][0], got[b_][0])),
+                                 "kv": [bool(np.array_equal(got[a_][2][l][0], got[b_][2][l][0])) and
+                                        bool(np.array_equal(got[a_][2][l][1], got[b_][2][l][1]))
+                                        for l in range(SHAPE.num_layers)]}
+    print("packings:", report)
+    for name in got:
+        r = report[name]
+        assert r["logits_max_rel"] <= MAX_REL and r["logits_mae"] <= MAE, (name, r)
+        assert all(k <= 2e-2 and v <= 2e-2 for k, v in r["kv_max_rel_per_layer"]), (name, r)
 
 
 def test_engine_request_semantics(gpu, model):

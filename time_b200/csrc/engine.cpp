@@ -138,6 +138,9 @@ struct glm_engine {
     int32_t* cap_idx = nullptr;
     float* cap_w = nullptr;
     int cap_rows = 0;
+    // ... gathered on the host over all forwards of the last step: [layer][row][top_k]
+    std::vector<std::vector<int32_t>> cap_step_idx;
+    std::vector<std::vector<float>> cap_step_w;
 };
 
 namespace {
@@ -395,6 +398,20 @@ moe_status_t forward(glm_engine* E, int R, int head) {
         }
     }
     E->cap_rows = R;
+    if (E->cap_idx) {   // keep this forward's routing with the step's (tests only: synchronises)
+        ENG_CUDA(cudaStreamSynchronize(st));
+        for (size_t l = 0; l < E->layers.size(); ++l) {
+            if (E->layers[l].dense) continue;
+            const size_t n = static_cast<size_t>(R) * c.top_k, off = l * static_cast<size_t>(E->rows_cap) * c.top_k;
+            std::vector<int32_t>& vi = E->cap_step_idx[l];
+            std::vector<float>& vw = E->cap_step_w[l];
+            const size_t o = vi.size();
+            vi.resize(o + n);
+            vw.resize(o + n);
+            ENG_CUDA(cudaMemcpy(vi.data() + o, E->cap_idx + off, n * 4, cudaMemcpyDeviceToHost));
+            ENG_CUDA(cudaMemcpy(vw.data() + o, E->cap_w + off, n * 4, cudaMemcpyDeviceToHost));
+        }
+    }
     if (!sample) return cudaStreamSynchronize(st) == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
     const size_t nl = E->layers.size();
     if (tm) cudaEventRecord(E->events[1 + 2 * nl], st);
@@ -526,6 +543,8 @@ int32_t batch_decode(glm_engine* E, void* const* states, int n, int64_t* out_tok
     }
     const int B = static_cast<int>(rows.size());
     E->last_rows = B;
+    for (auto& v : E->cap_step_idx) v.clear();
+    for (auto& v : E->cap_step_w) v.clear();
     if (B == 0) return 0;
     int64_t* tok = reinterpret_cast<int64_t*>(E->stage_host + E->stage.tokens);
     uint64_t* seeds = reinterpret_cast<uint64_t*>(E->stage_host + E->stage.seeds);
@@ -983,6 +1002,8 @@ moe_status_t glm_engine_set_capture(glm_engine_t* E, int on) {
         return MOE_OK;
     }
     if (E->cap_idx || E->cfg.first_dense == E->cfg.num_layers) return MOE_OK;
+    E->cap_step_idx.assign(E->cfg.num_layers, {});
+    E->cap_step_w.assign(E->cfg.num_layers, {});
     const size_t n = static_cast<size_t>(E->cfg.num_layers) * E->rows_cap * E->cfg.top_k;
     if (dev_alloc(&E->cap_idx, n * 4) != cudaSuccess || dev_alloc(&E->cap_w, n * 4) != cudaSuccess) {
         if (E->cap_idx) cudaFree(E->cap_idx);
@@ -996,13 +1017,36 @@ moe_status_t glm_engine_set_capture(glm_engine_t* E, int on) {
 moe_status_t glm_engine_copy_routing(glm_engine_t* E, int layer, int rows, int32_t* idx_host, float* w_host) {
     if (!E || !idx_host || !w_host || layer < 0 || rows < 0) return MOE_ERR_INVALID_ARGUMENT;
     std::lock_guard<std::mutex> g(E->mu);
-    if (!E->cap_idx || layer >= E->cfg.num_layers || E->layers[layer].dense || rows > E->cap_rows)
-        return MOE_ERR_INVALID_ARGUMENT;
-    cudaSetDevice(E->device);
+    if (!E->cap_idx || layer >= E->cfg.num_layers || E->layers[layer].dense) return MOE_ERR_INVALID_ARGUMENT;
     const size_t n = static_cast<size_t>(rows) * E->cfg.top_k;
-    const size_t off = static_cast<size_t>(layer) * E->rows_cap * E->cfg.top_k;
-    return cudaMemcpy(idx_host, E->cap_idx + off, n * 4, cudaMemcpyDeviceToHost) == cudaSuccess &&
-                   cudaMemcpy(w_host, E->cap_w + off, n * 4, cudaMemcpyDeviceToHost) == cudaSuccess
+    if (n > E->cap_step_idx[layer].size()) return MOE_ERR_INVALID_ARGUMENT;
+    std::memcpy(idx_host, E->cap_step_idx[layer].data(), n * 4);
+    std::memcpy(w_host, E->cap_step_w[layer].data(), n * 4);
+    return MOE_OK;
+}
+
+int glm_engine_request_pages(glm_engine_t* E, const void* state, int32_t* out, int max_pages) {
+    if (!E || !state) return -1;
+    std::lock_guard<std::mutex> g(E->mu);
+    Request* r = static_cast<Request*>(const_cast<void*>(state));
+    if (!E->requests.count(r)) return -1;
+    const int n = static_cast<int>(r->pages.size());
+    for (int i = 0; i < n && i < max_pages && out; ++i) out[i] = r->pages[i];
+    return n;
+}
+
+moe_status_t glm_engine_copy_kv(glm_engine_t* E, int layer, int page, int npages, void* k_host, void* v_host) {
+    if (!E || layer < 0 || layer >= E->cfg.num_layers || page < 0 || npages < 0 || page + npages > E->num_pages ||
+        !k_host || !v_host)
+        return MOE_ERR_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(E->mu);
+    cudaSetDevice(E->device);
+    const size_t pb = static_cast<size_t>(kPage) * E->cfg.num_kv_heads * kHeadDim * 2;
+    const Layer& L = E->layers[layer];
+    return cudaMemcpy(k_host, static_cast<const uint8_t*>(L.k_cache) + page * pb, npages * pb,
+                      cudaMemcpyDeviceToHost) == cudaSuccess &&
+                   cudaMemcpy(v_host, static_cast<const uint8_t*>(L.v_cache) + page * pb, npages * pb,
+                              cudaMemcpyDeviceToHost) == cudaSuccess
                ? MOE_OK
                : MOE_ERR_CUDA;
 }

@@ -81,6 +81,8 @@ def lib() -> ctypes.CDLL:
         e.glm_engine_check_error.argtypes = [c_void_p]
         e.glm_engine_set_capture.argtypes = [c_void_p, c_int]
         e.glm_engine_copy_routing.argtypes = [c_void_p, c_int, c_int, c_void_p, c_void_p]
+        e.glm_engine_request_pages.argtypes = [c_void_p, c_void_p, c_void_p, c_int]
+        e.glm_engine_copy_kv.argtypes = [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]
         e.glm_engine_set_timing.argtypes = [c_void_p, c_int]
         e.glm_engine_stage_ms.argtypes = [c_void_p, ctypes.POINTER(c_float)]
         e.glm_engine_device_bytes.argtypes = [ctypes.POINTER(EngineConfig)]
@@ -254,6 +256,26 @@ class NativeEngine:
         M.check("glm_engine_copy_routing",
                 self.lib.glm_engine_copy_routing(self.handle, layer, rows, idx.ctypes.data, w.ctypes.data))
         return idx, w
+
+    def request_pages(self, state) -> np.ndarray:
+        n = int(self.lib.glm_engine_request_pages(self.handle, state, None, 0))
+        assert n >= 0
+        out = np.empty(max(n, 1), np.int32)
+        self.lib.glm_engine_request_pages(self.handle, state, out.ctypes.data, n)
+        return out[:n]
+
+    def kv_pages(self, layer: int, pages, kv_heads: int) -> tuple[np.ndarray, np.ndarray]:
+        """K and V (fp32 copies of the bf16 pages) of the given page ids, [n][16][kv_heads][128]."""
+        import torch
+        ks, vs = [], []
+        for p in pages:
+            k = np.empty((16, kv_heads, 128), np.uint16)
+            v = np.empty((16, kv_heads, 128), np.uint16)
+            M.check("glm_engine_copy_kv", self.lib.glm_engine_copy_kv(self.handle, layer, int(p), 1, k.ctypes.data,
+                                                                      v.ctypes.data))
+            ks.append(torch.from_numpy(k.view(np.int16)).view(torch.bfloat16).float().numpy())
+            vs.append(torch.from_numpy(v.view(np.int16)).view(torch.bfloat16).float().numpy())
+        return np.stack(ks), np.stack(vs)
 
     def check_error(self) -> None:
         M.check("glm_engine_check_error", self.lib.glm_engine_check_error(self.handle))
