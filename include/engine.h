@@ -104,7 +104,9 @@ typedef struct {
 
 /* Creates an engine whose weights the caller provides (device memory that
  * must outlive the engine; several layers may share one weight set).  The KV
- * caches, activations and workspaces are allocated here. */
+ * caches, activations and workspaces are allocated here.  The first request
+ * waits for the device once, so the weights may still be in flight on any
+ * stream until then. */
 moe_status_t glm_engine_create(const glm_engine_config_t* cfg, glm_engine_t** out);
 
 /* embed bf16 [vocab][hidden], final_norm fp32 [hidden], lm_head bf16

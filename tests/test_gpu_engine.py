@@ -258,6 +258,27 @@ def test_engine_packings_match_oracle(gpu, model):
         assert all(k <= 2e-2 and v <= 2e-2 for k, v in r["kv_max_rel_per_layer"]), (name, r)
 
 
+def test_engine_two_engines_from_one_weight_dict(gpu, model):
+    """Two engines alive at once over the same weights dict (each makes its
+    own rank-layout attention copies and keeps them): request A alone in
+    16-row forwards and A next to two other prompts give bit-identical
+    logits at every step."""
+    _, w_dev = model
+    rng = np.random.default_rng(9)
+    prompts = [list(map(int, rng.integers(0, SHAPE.vocab_size, L))) for L in (40, 12, 3)]
+    e1 = EN.NativeEngine.from_weights(SHAPE, w_dev, max_batch=4, max_seq=96, prefill_chunk=8)
+    e3 = EN.NativeEngine.from_weights(SHAPE, w_dev, max_batch=4, max_seq=96, prefill_chunk=64)
+    s1 = e1.prefill(0, prompts[0], 0.0, 1.0, 1.0, 16)
+    s3 = [e3.prefill(i, p, 0.0, 1.0, 1.0, 16) for i, p in enumerate(prompts)]
+    for _ in range(3):
+        t1 = e1.decode_step(s1)
+        r3 = e3.batch_decode_raw(s3)
+        assert np.array_equal(e1.copy_logits(1)[0], e3.copy_logits(3)[0])
+        assert t1[0] == r3[0][0]
+    e1.shutdown()
+    e3.shutdown()
+
+
 def test_engine_request_semantics(gpu, model):
     _, w_dev = model
     # 3 KV pages in all: a 40-token prompt holds all three (positions 0..47)

@@ -332,6 +332,8 @@ moe_status_t set_layer(glm_engine* E, int l, const attn_block_weights_t* aw, con
 }
 
 // Every layer and the embedding are set: size and allocate the workspace.
+// The first call also waits for the whole device once, so that weights the
+// caller wrote on any stream are complete before the engine's stream reads them.
 moe_status_t ensure_ready(glm_engine* E) {
     if (E->ws) return MOE_OK;
     if (!E->embed || !E->final_norm || !E->lm_head) return MOE_ERR_INVALID_ARGUMENT;
@@ -341,6 +343,7 @@ moe_status_t ensure_ready(glm_engine* E) {
         need = std::max(need, attn_block_workspace_bytes(L.attn));
         need = std::max(need, moe_layer_workspace_bytes(L.ffn));
     }
+    ENG_CUDA(cudaDeviceSynchronize());
     ENG_CUDA(dev_alloc(&E->ws, need));
     E->ws_bytes = need;
     return MOE_OK;

@@ -206,8 +206,9 @@ class NativeEngine:
     def from_weights(cls, shape, weights: dict, max_batch: int, max_seq: int, prefill_chunk: int = 0,
                      num_cache_pages: int = 0) -> "NativeEngine":
         """An engine over device tensors (synth.make_model_weights on a CUDA
-        device; layers may share tensors).  The tensors are kept alive by the
-        returned object."""
+        device; layers may share tensors).  The tensors, and the rank-layout
+        copies of whole-model attention weights made here, are kept alive by
+        the returned object; `weights` is not modified."""
         self = cls(max_batch=max_batch, max_seq=max_seq)
         self.lib = lib()
         cfg = engine_config(shape, max_batch, max_seq, prefill_chunk, num_cache_pages)
@@ -216,17 +217,20 @@ class NativeEngine:
         self.handle = h.value
         self._loaded = True
         try:
-            self._keep = [weights]
+            # the engine reads these tensors for its whole life: keep them here
+            # (rank-layout copies made below included), never in the caller's dict
+            own = {}
+            self._keep = [weights, own]
             M.check("glm_engine_set_embedding",
                     self.lib.glm_engine_set_embedding(self.handle, M.ptr(weights["embed"]),
                                                       M.ptr(weights["final_norm"]), M.ptr(weights["lm_head"])))
             for l, layer in enumerate(weights["layers"]):
                 a = layer["attn"]
-                qkv = a.get("w_qkv")
-                if qkv is None:   # whole-model layout -> the tp 1 rank layout
+                if a.get("w_qkv") is None:   # whole-model layout -> the tp 1 rank layout (one copy per weight set)
                     from . import synth
-                    a = synth.attn_rank_slice(a, shape.attn(), 1, 0)
-                    layer["attn_rank"] = a
+                    if id(a) not in own:
+                        own[id(a)] = synth.attn_rank_slice(a, shape.attn(), 1, 0)
+                    a = own[id(a)]
                 aw = A.BlockWeights(M.ptr(a["gamma"]), M.ptr(a["w_qkv"]), M.ptr(a["s_qkv"]), M.ptr(a["w_o"]),
                                     M.ptr(a["s_o"]))
                 f = layer["ffn"]
