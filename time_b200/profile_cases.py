@@ -91,14 +91,21 @@ def router(tokens: int, iters: int) -> dict:
     return out
 
 
-def gemm(tokens: int, experts: int, iters: int) -> dict:
+def gemm(tokens: int, experts: int, iters: int, zipf: bool = True) -> dict:
     shape = dataclasses.replace(synth.GLM, num_experts=experts)
     dev = torch.device("cuda", 0)
-    w = synth.make_moe_weights(shape, seed=0, device=dev, zipf_bias=True)
+    w = synth.make_moe_weights(shape, seed=0, device=dev, zipf_bias=zipf)
     x = synth.make_x(shape, tokens, seed=1, device=dev)
     layer = M.MoELayer(shape, w, max_tokens=tokens)
     out = torch.empty_like(x)
     ms = _time(lambda: layer.forward(x, out), iters)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(M.NUM_STAGES + 1)]
+    layer.set_stage_events(ev)
+    layer.forward(x, out)
+    torch.cuda.synchronize()
+    layer.set_stage_events(None)
+    names = ["rmsnorm_quant", "router_topk", "permute", "gather", "gemm_gate_up", "gemm_down", "combine"]
+    stages = {n: ev[i].elapsed_time(ev[i + 1]) for i, n in enumerate(names)}
     layer.check_error()
     _, _, counts = layer.last_routing(tokens)
     layer.close()
@@ -108,9 +115,45 @@ def gemm(tokens: int, experts: int, iters: int) -> dict:
     touched = int((counts > 0).sum())
     w13 = 2 * I * H + (2 * I // 128) * (H // 128) * 4
     w2 = H * I + (H // 128) * (I // 128) * 4
-    return {"layer_forward_ms": ms, "rows": rows, "touched_groups": touched,
-            "gemm_gate_up_bytes": touched * w13 + rows * (H + H // 128 * 4) + rows * (I + I // 128 * 4),
-            "gemm_down_bytes": touched * w2 + rows * (I + I // 128 * 4) + rows * H * 2}
+    gu = touched * w13 + rows * (H + H // 128 * 4) + rows * (I + I // 128 * 4)
+    dn = touched * w2 + rows * (I + I // 128 * 4) + rows * H * 2
+    return {"layer_forward_ms": ms, "stage_ms": stages, "rows": rows, "touched_groups": touched,
+            "gemm_gate_up_bytes": gu, "gemm_down_bytes": dn,
+            "gate_up_gbs": gu / (stages["gemm_gate_up"] * 1e-3) / 1e9,
+            "down_gbs": dn / (stages["gemm_down"] * 1e-3) / 1e9}
+
+
+def proj(iters: int) -> dict:
+    """The attention block's projections at one GPU's GLM shapes (QKV: N =
+    (96 + 16) x 128, K = 5120; o_proj: N = 5120, K = 12288) for a few batch
+    sizes, on the split-K mma.sync kernel (fp8_gemm_small) and on the tcgen05
+    grouped GEMM with one group."""
+    from . import attn as A
+    dev = torch.device("cuda", 0)
+    k = A.lib()
+    out = {}
+    for name, N, K in (("qkv", 112 * 128, 5120), ("o_proj", 5120, 12288)):
+        wq = torch.randint(0, 120, (N, K), dtype=torch.uint8, device=dev)
+        ws = torch.rand(N // 128, K // 128, device=dev) * 1e-3
+        for T in (16, 64, 128, 256, 512):
+            ld = (T + 15) // 16 * 16
+            a = torch.randint(0, 120, (T, K), dtype=torch.uint8, device=dev)
+            asc = torch.rand(K // 128, ld, device=dev)
+            o = torch.empty(T, N, dtype=torch.bfloat16, device=dev)
+            wsb = int(k.fp8_gemm_small_workspace_bytes(T, N, K))
+            wsp = torch.empty(max(wsb, 16), dtype=torch.uint8, device=dev)
+
+            def small():
+                M.check("fp8_gemm_small", k.fp8_gemm_small(M.ptr(a), M.ptr(asc), ld, T, M.ptr(wq), M.ptr(ws), N, K,
+                                                           M.ptr(o), M.ptr(wsp), wsb, M.stream_ptr()))
+            cnt = torch.tensor([T], dtype=torch.int32, device=dev)
+            start = torch.tensor([0], dtype=torch.int32, device=dev)
+
+            def grouped():
+                M.grouped_gemm(M.GEMM_DOWN_BF16, a, asc, ld, wq, ws, cnt, start, o, None, 0, K, N, ld)
+            out[f"{name}_T{T}"] = {"small_us": _time(small, iters) * 1e3, "grouped_us": _time(grouped, iters) * 1e3,
+                                   "weight_mb": N * K / 1e6}
+    return out
 
 
 def attention(batch: int, ctx_min: int, ctx_max: int, split: int, iters: int, nq: int = 12, nkv: int = 1,
@@ -279,7 +322,8 @@ def serving(batch: int, prompt: int, steps: int, layers: int, max_seq: int) -> d
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["router", "gemm", "attention", "attn_block", "serving"])
+    ap.add_argument("case", choices=["router", "gemm", "attention", "attn_block", "serving", "proj"])
+    ap.add_argument("--no-zipf", action="store_true", help="gemm: uniform routing (no router bias)")
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--layers", type=int, default=92)
@@ -301,8 +345,10 @@ def main() -> int:
         res = attn_block(a.batch, a.ctx_min, a.ctx_max, a.iters, use_graph=a.graph)
     elif a.case == "serving":
         res = serving(a.batch, a.prompt, a.steps, a.layers, a.max_seq)
+    elif a.case == "proj":
+        res = proj(a.iters)
     else:
-        res = router(a.tokens, a.iters) if a.case == "router" else gemm(a.tokens, a.experts, a.iters)
+        res = router(a.tokens, a.iters) if a.case == "router" else gemm(a.tokens, a.experts, a.iters, not a.no_zipf)
     print(json.dumps({"case": a.case, "tokens": a.tokens, **res}), flush=True)
     return 0
 
