@@ -113,3 +113,23 @@ def test_block_glm_shape_tp8_emulated(gpu):
         blk.check_error()
         blk.close()
     check(A.tp_reduce_residual(parts, x), ref)
+
+
+@pytest.mark.parametrize("shape,ctx", [
+    # more than 64 rows: the projections run on the tcgen05 grouped GEMM
+    (synth.AttnShape(hidden=512, num_q_heads=4, num_kv_heads=1), list(np.random.default_rng(2).integers(0, 200, 96))),
+    # one GPU's GLM weights (QKV 14336 x 5120, o_proj 5120 x 12288) at a decode batch: grouped GEMM too
+    (synth.GLM_ATTN, [100, 517, 1000]),
+])
+def test_block_grouped_gemm_path(gpu, shape, ctx):
+    ctx = [int(c) for c in ctx]
+    B = len(ctx)
+    w_all, caches, pt, max_pages, x = setup_case(shape, 1, B, ctx, seed=B, dev=gpu)
+    ref = oracle_out(shape, 1, w_all, caches, pt, ctx, x)
+    blk = A.AttnBlock(shape, synth.attn_rank_slice(w_all, shape, 1, 0), max_batch=max(B, 4),
+                      max_pages_per_seq=max_pages, max_context=max_pages * PS)
+    out = blk.decode(x, torch.tensor(ctx, dtype=torch.int32, device=gpu), torch.from_numpy(pt).to(gpu), *caches[0])
+    torch.cuda.synchronize()
+    blk.check_error()
+    blk.close()
+    check(out, ref)

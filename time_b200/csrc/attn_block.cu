@@ -2,8 +2,10 @@
 // layer, one call per decode step (one new token per sequence), per TP rank:
 //
 //   rmsnorm + e4m3 1x128   moe_rmsnorm_quant
-//   QKV projection         fp8_gemm_small (split-K mma.sync; the tcgen05 grouped
-//                          GEMM with one group above 256 tokens), bf16 out
+//   QKV projection         bf16 out: the tcgen05 grouped GEMM with one group, or
+//                          for a small batch on a small weight (a TP rank's
+//                          slice) fp8_gemm_small (split-K mma.sync), which
+//                          spreads the few weight rows over every SM
 //   partial RoPE + pages   attn_rope_kv_write (also seq_lens = pos + 1)
 //   decode attention       attn_decode_paged (bf16 + e4m3 rows for o_proj)
 //   o_proj (row parallel)  the same, bf16 partial
@@ -22,6 +24,7 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstdlib>
@@ -40,10 +43,20 @@ using namespace tb;
 constexpr int kD = 128;
 constexpr int kMaxTp = 64;
 constexpr size_t kFlagBytes = 512;   // ready[kMaxTp] at 0, done[kMaxTp] at 256, partial after
-constexpr int kSmallGemmMaxT = 256;   // up to this batch the projections run on fp8_gemm_small
+constexpr int kSmallGemmMaxT = 64;    // batches up to this may run the projections on fp8_gemm_small
+constexpr long long kSmallGemmMaxW = 32ll << 20;   // ... when the weight has fewer bytes than this
 
 inline moe_status_t launch_status() {
     return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+}
+
+// Measured on B200 (one GPU's GLM shapes, bf16 out): QKV 14336 x 5120 at 16 /
+// 64 / 256 tokens 31 / 33 / 52 us grouped vs 59 / 58 / 181 us split-K;
+// o_proj 5120 x 12288 57 / 64 / 102 vs 64 / 65 / 216 us.  The split-K kernel
+// wins only where the grouped GEMM's 128-row tiles leave most SMs idle (a TP
+// rank's 1792 x 5120 or 5120 x 1536 at a decode batch).
+bool use_small_gemm(int B, int N, int K) {
+    return B <= kSmallGemmMaxT && static_cast<long long>(N) * K < kSmallGemmMaxW;
 }
 
 // out = bf16(residual + (0 + part)): the tp == 1 form of the rank-ordered sum
@@ -172,7 +185,7 @@ struct attn_block {
     attn_block_config_t cfg;
     attn_block_weights_t w;
     int nqkv;              // (nq + 2 nkv) * 128
-    int rows_pad;          // max_batch rounded up to 16 (the GEMM's token tiles)
+    int rows_pad;          // max_batch rounded up to 16, at least 32 (the GEMM's token tiles)
     int ld;                // scale-row stride (= rows_pad)
     int split_tokens, max_splits;
     float* inv_freq;       // device [rot / 2]
@@ -213,8 +226,10 @@ void plan(attn_block* L) {
     // split-K partials of the small-batch projections, for any B <= max_batch
     size_t g = 0;
     for (int t = 1; t <= c.max_batch && t <= kSmallGemmMaxT; ++t) {
-        const size_t a = fp8_gemm_small_workspace_bytes(t, L->nqkv, H);
-        const size_t b = fp8_gemm_small_workspace_bytes(t, H, c.num_q_heads * kD);
+        const size_t a = use_small_gemm(t, L->nqkv, H) ? fp8_gemm_small_workspace_bytes(t, L->nqkv, H) : 0;
+        const size_t b = use_small_gemm(t, H, c.num_q_heads * kD)
+                             ? fp8_gemm_small_workspace_bytes(t, H, c.num_q_heads * kD)
+                             : 0;
         g = a > g ? a : g;
         g = b > g ? b : g;
     }
@@ -225,7 +240,7 @@ void plan(attn_block* L) {
 
 moe_status_t gemm(const attn_block* L, int mode, int B, int K, int N, const void* a, const float* as, const void* w,
                   const float* ws, void* ws_base, void* out, cudaStream_t st) {
-    if (B <= kSmallGemmMaxT)
+    if (use_small_gemm(B, N, K))
         return fp8_gemm_small(a, as, L->ld, B, w, ws, N, K, out, at<void>(ws_base, L->off_gsplit), L->gsplit_bytes, st);
     cbwGroupedGemmArgs g;
     std::memset(&g, 0, sizeof(g));
@@ -277,7 +292,7 @@ moe_status_t run_partial(attn_block* L, const void* x, int B, const int32_t* pos
     const int H = c.hidden, nq = c.num_q_heads, nkv = c.num_kv_heads;
     ATT_TRY(moe_rmsnorm_quant(x, L->w.gamma, B, H, c.eps, at<float>(ws, L->off_rms), at<void>(ws, L->off_xq),
                               at<float>(ws, L->off_xs), L->ld, st));
-    if (B > kSmallGemmMaxT) {
+    if (!use_small_gemm(B, L->nqkv, H) || !use_small_gemm(B, H, nq * kD)) {
         set_group_kernel<<<1, 1, 0, st>>>(at<int32_t>(ws, L->off_group), B);
         ATT_TRY(launch_status());
     }
@@ -319,7 +334,9 @@ moe_status_t attn_block_create(const attn_block_config_t* cfg, const attn_block_
     L->cfg = c;
     L->w = *w;
     L->nqkv = (c.num_q_heads + 2 * c.num_kv_heads) * kD;
-    L->rows_pad = (c.max_batch + 15) / 16 * 16;
+    // rows of the GEMMs' activation tensors: a multiple of 16, at least the
+    // grouped GEMM's 32-row token box
+    L->rows_pad = std::max(32, (c.max_batch + 15) / 16 * 16);
     L->ld = L->rows_pad;   // the GEMM wants a scale stride of at least its row extent
     // splits: about two CTAs per SM for a full batch at half the longest context
     const long long work = static_cast<long long>(c.max_batch) * c.num_kv_heads * (c.max_context / 2 + 1);
