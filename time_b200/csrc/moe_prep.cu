@@ -328,24 +328,21 @@ router_topk_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict_
 // (tg = (lane & 3) + 4 * warp, eg = lane >> 2) owns tokens tg + 16 i and
 // experts eg + 8 j, so the 4 token rows and 8 expert rows a warp reads per
 // load sit in distinct banks (row pitch 68 floats: row r at bank 4r).  K in
-// chunks of 64 through an S-stage cp.async ring: 2 stages when the grid
-// fills the GPU, 6 for the few blocks of a small batch, whose time is the
-// latency of each chunk's load unless several chunks are in flight.  Each
-// chain still advances one fma per k in ascending k from +0.0f:
-// bit-identical logits.
+// chunks of 64 through a cp.async double buffer.  Each chain still advances
+// one fma per k in ascending k from +0.0f: bit-identical logits.
 constexpr int kR3Exp = 32, kR3KC = 64, kR3Ld = kR3KC + 4, kR3Threads = 128;
 
-template <int TI, int S>
-constexpr size_t r3_smem_bytes() { return S * static_cast<size_t>(16 * TI + kR3Exp) * kR3Ld * sizeof(float); }
+template <int TI>
+constexpr size_t r3_smem_bytes() { return 2 * static_cast<size_t>(16 * TI + kR3Exp) * kR3Ld * sizeof(float); }
 
-template <int TI, int S>
+template <int TI>
 __global__ void __launch_bounds__(kR3Threads, 4)
 router_logits_tile_kernel(const float* __restrict__ n, const float* __restrict__ W, const float* __restrict__ bias,
                           int T, int H, int E, float* __restrict__ logits) {
     constexpr int TT = 16 * TI;
     extern __shared__ __align__(16) float r3_smem[];
-    auto n_s = reinterpret_cast<float (*)[TT][kR3Ld]>(r3_smem);                          // [S][TT][68]
-    auto w_s = reinterpret_cast<float (*)[kR3Exp][kR3Ld]>(r3_smem + S * TT * kR3Ld);   // [S][32][68]
+    auto n_s = reinterpret_cast<float (*)[TT][kR3Ld]>(r3_smem);                          // [2][TT][68]
+    auto w_s = reinterpret_cast<float (*)[kR3Exp][kR3Ld]>(r3_smem + 2 * TT * kR3Ld);   // [2][32][68]
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int tg = (lane & 3) + 4 * warp, eg = lane >> 2;
     const int t0 = blockIdx.y * TT, e0 = blockIdx.x * kR3Exp;
@@ -372,34 +369,16 @@ router_logits_tile_kernel(const float* __restrict__ n, const float* __restrict__
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
     const int nchunks = H / kR3KC;
-    if constexpr (S > 2) {
-        // S - 1 chunks in flight ahead of the one computed; one commit group
-        // per chunk (empty past the end) keeps the wait count fixed
-#pragma unroll
-        for (int c = 0; c < S - 1; ++c) {
-            if (c < nchunks) load(c, c * kR3KC);
-            else cp_async_commit();
-        }
-    } else {
-        load(0, 0);
-    }
+    load(0, 0);
     for (int c = 0; c < nchunks; ++c) {
-        if constexpr (S > 2) {
-            cp_async_wait<S - 2>();
-            __syncthreads();   // chunk c landed for every thread; stage (c - 1) % S is free
-            if (c + S - 1 < nchunks) load((c + S - 1) % S, (c + S - 1) * kR3KC);
-            else cp_async_commit();
+        if (c + 1 < nchunks) {
+            load((c + 1) & 1, (c + 1) * kR3KC);
+            cp_async_wait<1>();
         } else {
-            // double buffer: the next chunk's load goes out before waiting for this one
-            if (c + 1 < nchunks) {
-                load((c + 1) & 1, (c + 1) * kR3KC);
-                cp_async_wait<1>();
-            } else {
-                cp_async_wait<0>();
-            }
-            __syncthreads();
+            cp_async_wait<0>();
         }
-        const int st = c % S;
+        __syncthreads();
+        const int st = c & 1;
 #pragma unroll 4
         for (int kk = 0; kk < kR3KC; kk += 4) {
             float4 a[TI], b[4];
@@ -417,9 +396,8 @@ router_logits_tile_kernel(const float* __restrict__ n, const float* __restrict__
                     acc[i][j] = __fmaf_rn(a[i].w, b[j].w, acc[i][j]);
                 }
         }
-        if constexpr (S == 2) __syncthreads();   // the double buffer's stage is reloaded next iteration
+        __syncthreads();
     }
-    cp_async_wait<0>();
 #pragma unroll
     for (int i = 0; i < TI; ++i)
 #pragma unroll
@@ -793,21 +771,19 @@ moe_status_t moe_router_logits(const float* n, const float* router_w, const floa
     const int ti = blocks_for(1) <= 148 ? 1 : (blocks_for(2) <= 148 ? 2 : (blocks_for(4) <= 148 ? 4 : 2));
     const dim3 grid(etiles, (T + 16 * ti - 1) / (16 * ti));
     if (grid.y > 65535) return MOE_ERR_UNSUPPORTED;
-    static bool attr4[kMaxDevices] = {}, attr1[kMaxDevices] = {};
-    if (smem_optin_once(router_logits_tile_kernel<4, 2>, static_cast<int>(r3_smem_bytes<4, 2>()), attr4) !=
-            cudaSuccess ||
-        smem_optin_once(router_logits_tile_kernel<1, 6>, static_cast<int>(r3_smem_bytes<1, 6>()), attr1) != cudaSuccess)
+    static bool attr[kMaxDevices] = {};
+    if (smem_optin_once(router_logits_tile_kernel<4>, static_cast<int>(r3_smem_bytes<4>()), attr) != cudaSuccess)
         return MOE_ERR_CUDA;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (ti == 4)
-        router_logits_tile_kernel<4, 2><<<grid, kR3Threads, r3_smem_bytes<4, 2>(), st>>>(n, router_w, router_bias, T,
-                                                                                         H, E, logits);
+        router_logits_tile_kernel<4><<<grid, kR3Threads, r3_smem_bytes<4>(), st>>>(n, router_w, router_bias, T, H, E,
+                                                                                   logits);
     else if (ti == 2)
-        router_logits_tile_kernel<2, 2><<<grid, kR3Threads, r3_smem_bytes<2, 2>(), st>>>(n, router_w, router_bias, T,
-                                                                                         H, E, logits);
+        router_logits_tile_kernel<2><<<grid, kR3Threads, r3_smem_bytes<2>(), st>>>(n, router_w, router_bias, T, H, E,
+                                                                                   logits);
     else
-        router_logits_tile_kernel<1, 6><<<grid, kR3Threads, r3_smem_bytes<1, 6>(), st>>>(n, router_w, router_bias, T,
-                                                                                         H, E, logits);
+        router_logits_tile_kernel<1><<<grid, kR3Threads, r3_smem_bytes<1>(), st>>>(n, router_w, router_bias, T, H, E,
+                                                                                   logits);
     return launch_status();
 }
 
