@@ -98,6 +98,10 @@ typedef void* cbwLtMatmulPreference_t;
  *   out_q[r][n] (e4m3) and out_scale[n/128][r] (fp32) -- the input format of
  *   the down projection.  Rows in [count, round_up(count,16)) are zeroed.
  * mode CBW_GEMM_DOWN_BF16: W[g] holds N rows; out[r][n] = bf16(acc).
+ * Either mode may be or-ed with CBW_GEMM_SMALL_TILES (tiles of at most 32
+ * rows and a deeper weight ring: the decode form) or CBW_GEMM_FULL_TILES;
+ * without either, small tiles are used when rows <= 32 * num_groups.  Both
+ * forms give the same result.
  *
  * Requirements: K % 128 == 0, N % 128 == 0, start[g] % 16 == 0, every
  * segment [start, start + round_up(count,16)) inside [0, rows), a_ld (the
@@ -107,7 +111,9 @@ typedef void* cbwLtMatmulPreference_t;
  */
 typedef enum {
     CBW_GEMM_GATED_SWIGLU = 0,
-    CBW_GEMM_DOWN_BF16 = 1
+    CBW_GEMM_DOWN_BF16 = 1,
+    CBW_GEMM_SMALL_TILES = 0x10,
+    CBW_GEMM_FULL_TILES = 0x20
 } cbwGemmMode_t;
 
 typedef struct {

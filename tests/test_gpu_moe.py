@@ -357,6 +357,55 @@ def test_grouped_gemm_gated_swiglu(gpu, oracle, counts, K, N):
         assert (hs_c[:, starts[gi] + counts[gi]:pad_end] == 0).all()
 
 
+@pytest.mark.parametrize("gated", [False, True])
+@pytest.mark.parametrize("counts", [[1, 0, 3, 16, 31, 32, 33, 70], [0, 5, 1000, 2], [64] * 12])
+def test_grouped_gemm_small_tiles(gpu, gated, counts):
+    """The decode form (CBW_GEMM_SMALL_TILES: tiles of at most 32 rows, a
+    deeper weight ring) and the full form on the same inputs: both within the
+    float64 reference's tolerance, padding rows zeroed; reports whether they
+    agree bit for bit."""
+    K, N = 640, 256
+    g = torch.Generator().manual_seed(31 + sum(counts) + gated)
+    starts, rows, A, A_s, a_ld, W, W_s = _make_groups(counts, K, 2 * N if gated else N, g)
+    cnt = torch.tensor(counts, dtype=torch.int32, device=gpu)
+    st = torch.tensor(starts, dtype=torch.int32, device=gpu)
+    ref = _gemm_ref(A, A_s, W, W_s, starts, counts, K)
+    lut = _lut()
+    outs = {}
+    for form in (M.GEMM_SMALL_TILES, M.GEMM_FULL_TILES):
+        err = torch.zeros(1, dtype=torch.int32, device=gpu)
+        if gated:
+            hq = torch.full((rows, N), 0x55, dtype=torch.uint8, device=gpu)
+            hs = torch.full((N // 128, a_ld), -1.0, device=gpu)
+            M.grouped_gemm(M.GEMM_GATED_SWIGLU | form, A.to(gpu), A_s.to(gpu), a_ld, W.to(gpu), W_s.to(gpu), cnt, st,
+                           hq, hs, a_ld, K, N, rows, error_word=err)
+            torch.cuda.synchronize()
+            outs[form] = (hq.cpu(), hs.cpu())
+        else:
+            out = torch.full((rows, N), float("nan"), dtype=torch.bfloat16, device=gpu)
+            M.grouped_gemm(M.GEMM_DOWN_BF16 | form, A.to(gpu), A_s.to(gpu), a_ld, W.to(gpu), W_s.to(gpu), cnt, st,
+                           out, None, 0, K, N, rows, error_word=err)
+            torch.cuda.synchronize()
+            outs[form] = (out.cpu(),)
+        assert err.item() == 0
+        for gi, r in ref.items():
+            s0, c = starts[gi], counts[gi]
+            if gated:
+                hq_c, hs_c = outs[form]
+                gte, up = r[:, :N].float(), r[:, N:]
+                h = (gte / (1 + torch.exp(-gte))).double() * up
+                deq = lut[hq_c[s0:s0 + c].long()] * hs_c[:, s0:s0 + c].T.double().repeat_interleave(128, 1)
+                assert (deq - h).abs().max() / h.abs().max() < 4e-2, (form, gi)
+                pad_end = s0 + (c + 15) // 16 * 16
+                assert (hq_c[s0 + c:pad_end] == 0).all() and (hs_c[:, s0 + c:pad_end] == 0).all()
+            else:
+                y = outs[form][0][s0:s0 + c].double()
+                assert torch.isfinite(y).all()
+                assert (y - r).abs().max() / r.abs().max() < 8e-3, (form, gi)
+    same = all(torch.equal(a_, b_) for a_, b_ in zip(outs[M.GEMM_SMALL_TILES], outs[M.GEMM_FULL_TILES]))
+    print(f"small vs full tiles ({'gated' if gated else 'down'}, counts {counts}): bit-identical {same}")
+
+
 # ---------------------------------------------------------------- full layer
 
 def _run_layer(shape, case, T, dev, routing=None):

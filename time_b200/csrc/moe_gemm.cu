@@ -67,21 +67,28 @@ constexpr int kTmemCols = 512;
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
 constexpr uint64_t kDrainTimeoutNs = 200000000ull;
 
-template <bool kGated>
+// kSmall: the decode form.  A tile holds at most 32 tokens, so an operand
+// stage shrinks to the weights plus 4 KB and the ring holds 5 (gated) or 9
+// (down) stages instead of 3 -- with a few tokens per expert the GEMM is a
+// weight stream, and the weight bytes in flight per SM set its rate.  The
+// promotion and epilogue keep the kNMax column layout (the warps whose
+// columns lie past the tile idle).
+template <bool kGated, bool kSmall = false>
 struct GemmCfg {
-    static constexpr int kNMax = kGated ? 128 : 256;       // tokens per tile
-    static constexpr int kStages = 3;                       // operand ring
+    static constexpr int kNMax = kGated ? 128 : 256;       // token columns of the promotion layout
+    static constexpr int kTileTok = kSmall ? 32 : kNMax;   // tokens per tile
+    static constexpr int kStages = kSmall ? (kGated ? 5 : 9) : 3;   // operand ring
     static constexpr int kSStages = 8;                      // token-scale ring
     static constexpr int kATiles = kGated ? 2 : 1;          // gate + up
     static constexpr int kABytes = kATiles * kTileM * kBlockK;
-    static constexpr int kBBytes = kNMax * kBlockK;
-    static constexpr int kStageBytes = kABytes + kBBytes;   // 48 KB either way
+    static constexpr int kBBytes = kTileTok * kBlockK;
+    static constexpr int kStageBytes = kABytes + kBBytes;   // 48 KB; small: 36 KB gated, 20 KB down
     static constexpr int kNumCombined = kGated ? 2 : 1;
     static constexpr int kScaleFloats = kNumCombined * kNMax;   // one scale-ring entry
     static constexpr int kRawSlot = kNumCombined - 1;       // where the bulk copy lands in an entry
     static constexpr int kBufCols = 256;                    // TMEM columns per partial buffer
     static constexpr int kColsPerWarp = kNMax / 4;          // 32 (gated) / 64 (down)
-    static constexpr int kOutStageBytes = kGated ? kNMax * 128 * 4 : kNMax * 128 * 2;
+    static constexpr int kOutStageBytes = kGated ? kTileTok * 128 * 4 : kTileTok * 128 * 2;
     // shared-memory carve-up (offsets from the 1024-aligned base)
     static constexpr int kOffStages = 0;
     static constexpr int kOffOut = kOffStages + kStages * kStageBytes;
@@ -94,6 +101,8 @@ struct GemmCfg {
     static constexpr int kOffMisc = kOffBars + kNumBars * 8;
     static constexpr int kSmemBytes = kOffMisc + 64 + 1024;  // + alignment slack
     static_assert(kOffBars % 8 == 0, "mbarrier alignment");
+    static_assert(kStageBytes % 1024 == 0, "128-byte-swizzled stages start on 1024-byte boundaries");
+    static_assert(kStages <= 32 && kSStages <= 32, "armed masks hold one bit per stage");
     static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
@@ -145,12 +154,12 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
     }
 }
 
-template <bool kGated>
+template <bool kGated, bool kSmall>
 __global__ void __launch_bounds__(kNumThreads, 1)
 grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
                         const __grid_constant__ CUtensorMap tmap_a,
                         const GemmParams p) {
-    using C = GemmCfg<kGated>;
+    using C = GemmCfg<kGated, kSmall>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -200,7 +209,7 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
     }
     if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
     if (warp == 2) {
-        // tiles per group: ceil(count / N_MAX) token chunks x (N / 128) row blocks
+        // tiles per group: ceil(count / tile tokens) token chunks x (N / 128) row blocks
         const int nbt = p.N / 128;
         int per_lane = (G + 31) / 32;
         int g0 = lane * per_lane;
@@ -209,7 +218,7 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
             int g = g0 + i;
             if (g < G) {
                 int cnt = p.count[g];
-                int ch = (cnt + C::kNMax - 1) / C::kNMax;
+                int ch = (cnt + C::kTileTok - 1) / C::kTileTok;
                 t_chunks[g] = ch;
                 t_start[g] = p.start[g];
                 counts_smem[g] = cnt;
@@ -248,7 +257,7 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
             uint32_t sarmed_mask = 0, sarmed_phase = 0;   // scale ring
             bool ok = true;
             for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
-                TileCoord tc = decode_tile(tile, t_prefix, t_chunks, t_start, counts_smem, G, C::kNMax);
+                TileCoord tc = decode_tile(tile, t_prefix, t_chunks, t_start, counts_smem, G, C::kTileTok);
                 const int b_loads = (tc.ntile + 31) >> 5;
                 const uint32_t bytes = C::kABytes + b_loads * 32 * kBlockK;
                 const int wrow = tc.g * p.w_rows + tc.nb * kTileM;
@@ -289,7 +298,7 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
             bool ok = true;
             bool issued = false;
             for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
-                TileCoord tc = decode_tile(tile, t_prefix, t_chunks, t_start, counts_smem, G, C::kNMax);
+                TileCoord tc = decode_tile(tile, t_prefix, t_chunks, t_start, counts_smem, G, C::kTileTok);
                 const uint32_t idesc = idesc_e4m3_f32(kTileM, tc.ntile);
                 for (int kb = 0; kb < KB; ++kb) {
                     if (!mbar_wait_bounded(&full_bar[s], phase, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
@@ -328,7 +337,7 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
         bool ok = true;
         const int wsb = p.w_rows / kTileM;
         for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
-            TileCoord tc = decode_tile(tile, t_prefix, t_chunks, t_start, counts_smem, G, C::kNMax);
+            TileCoord tc = decode_tile(tile, t_prefix, t_chunks, t_start, counts_smem, G, C::kTileTok);
             const float* wsg = p.w_scale + ((size_t)tc.g * wsb + tc.nb) * KB;
             const float* wsu = p.w_scale + ((size_t)tc.g * wsb + (p.N / kTileM) + tc.nb) * KB;
             for (int kb = 0; kb < KB; ++kb) {
@@ -376,7 +385,7 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
         };
 
         for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
-            TileCoord tc = decode_tile(tile, t_prefix, t_chunks, t_start, counts_smem, G, C::kNMax);
+            TileCoord tc = decode_tile(tile, t_prefix, t_chunks, t_start, counts_smem, G, C::kTileTok);
             bool live[kPieces];
 #pragma unroll
             for (int q = 0; q < kPieces; ++q) live[q] = (kGated ? col0 : col0 + 32 * q) < tc.ntile;
@@ -462,7 +471,8 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
                     const float g = (c & 1) ? acc2[c >> 1].y : acc2[c >> 1].x;
                     const float u = (c & 1) ? acc2[16 + (c >> 1)].y : acc2[16 + (c >> 1)].x;
                     const float h = (g / (1.0f + expf(-g))) * u;
-                    stage[(col0 + c) * 128 + row_in_tile] = h;
+                    // the small form's stage holds only the tile's columns
+                    if (!kSmall || col0 + c < tc.ntile) stage[(col0 + c) * 128 + row_in_tile] = h;
                 }
                 if (!group_sync()) { ok = false; break; }
                 uint8_t* outq = reinterpret_cast<uint8_t*>(p.out);
@@ -492,7 +502,7 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
 #pragma unroll
                 for (int c = 0; c < C::kColsPerWarp; ++c) {
                     const float v = (c & 1) ? acc2[c >> 1].y : acc2[c >> 1].x;
-                    stage[(col0 + c) * 128 + row_in_tile] = __float2bfloat16_rn(v);
+                    if (!kSmall || col0 + c < tc.ntile) stage[(col0 + c) * 128 + row_in_tile] = __float2bfloat16_rn(v);
                 }
                 if (!group_sync()) { ok = false; break; }
                 __nv_bfloat16* outy = reinterpret_cast<__nv_bfloat16*>(p.out);
@@ -546,9 +556,9 @@ bool encode_u8_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t co
     return r == CUDA_SUCCESS;
 }
 
-template <bool kGated>
+template <bool kGated, bool kSmall>
 cbwStatus_t launch_gemm(const cbwGroupedGemmArgs* a, int* error_word, cudaStream_t stream) {
-    using C = GemmCfg<kGated>;
+    using C = GemmCfg<kGated, kSmall>;
     const int w_rows = kGated ? 2 * a->N : a->N;
     CUtensorMap tw, ta;
     if (!encode_u8_2d(&tw, a->w, static_cast<uint64_t>(a->num_groups) * w_rows, a->K, kTileM)) return CBW_ERROR_INTERNAL;
@@ -566,7 +576,7 @@ cbwStatus_t launch_gemm(const cbwGroupedGemmArgs* a, int* error_word, cudaStream
         if (dev >= 0 && dev < kMaxDevices) sm_count[dev] = sms;
     }
     {
-        cudaError_t e = smem_optin_once(grouped_fp8_gemm_kernel<kGated>, C::kSmemBytes, attr_set);
+        cudaError_t e = smem_optin_once(grouped_fp8_gemm_kernel<kGated, kSmall>, C::kSmemBytes, attr_set);
         if (e != cudaSuccess) {
             std::fprintf(stderr, "cbwFp8BlockScaledGroupedGemm: shared memory opt-in (%d B) failed: %s\n",
                          C::kSmemBytes, cudaGetErrorString(e));
@@ -587,11 +597,11 @@ cbwStatus_t launch_gemm(const cbwGroupedGemmArgs* a, int* error_word, cudaStream
     p.N = a->N;
     p.w_rows = w_rows;
     p.error_word = error_word;
-    grouped_fp8_gemm_kernel<kGated><<<sms, kNumThreads, C::kSmemBytes, stream>>>(tw, ta, p);
+    grouped_fp8_gemm_kernel<kGated, kSmall><<<sms, kNumThreads, C::kSmemBytes, stream>>>(tw, ta, p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         cudaFuncAttributes fa;
-        cudaFuncGetAttributes(&fa, grouped_fp8_gemm_kernel<kGated>);
+        cudaFuncGetAttributes(&fa, grouped_fp8_gemm_kernel<kGated, kSmall>);
         std::fprintf(stderr,
                      "cbwFp8BlockScaledGroupedGemm: launch failed: %s (regs %d, max threads %d, smem %d B)\n",
                      cudaGetErrorString(e), fa.numRegs, fa.maxThreadsPerBlock, C::kSmemBytes);
@@ -613,10 +623,18 @@ extern "C" cbwStatus_t cbwFp8BlockScaledGroupedGemm(const cbwGroupedGemmArgs* ar
     if ((reinterpret_cast<uintptr_t>(a.a) | reinterpret_cast<uintptr_t>(a.w) |
          reinterpret_cast<uintptr_t>(a.a_scale) | reinterpret_cast<uintptr_t>(a.out)) & 15)
         return CBW_ERROR_INVALID_VALUE;
-    if (a.mode == CBW_GEMM_GATED_SWIGLU) {
+    const int base = a.mode & 0xF, tiles = a.mode & ~0xF;
+    if (tiles != 0 && tiles != CBW_GEMM_SMALL_TILES && tiles != CBW_GEMM_FULL_TILES) return CBW_ERROR_INVALID_VALUE;
+    // 32-token tiles when the padded rows average at most 32 per group (decode
+    // batches: a few tokens per expert), full tiles otherwise
+    const bool small = tiles == CBW_GEMM_SMALL_TILES ||
+                       (tiles == 0 && static_cast<long long>(a.rows) <= 32ll * a.num_groups);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (base == CBW_GEMM_GATED_SWIGLU) {
         if (!a.out_scale || a.out_ld < a.rows) return CBW_ERROR_INVALID_VALUE;
-        return launch_gemm<true>(&a, error_word, static_cast<cudaStream_t>(stream));
+        return small ? launch_gemm<true, true>(&a, error_word, st) : launch_gemm<true, false>(&a, error_word, st);
     }
-    if (a.mode == CBW_GEMM_DOWN_BF16) return launch_gemm<false>(&a, error_word, static_cast<cudaStream_t>(stream));
+    if (base == CBW_GEMM_DOWN_BF16)
+        return small ? launch_gemm<false, true>(&a, error_word, st) : launch_gemm<false, false>(&a, error_word, st);
     return CBW_ERROR_INVALID_VALUE;
 }

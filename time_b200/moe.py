@@ -50,6 +50,8 @@ STAGE_NAMES = ("rmsnorm_quant", "router_topk", "permute", "gather", "gemm_gate_u
 
 GEMM_GATED_SWIGLU = 0
 GEMM_DOWN_BF16 = 1
+GEMM_SMALL_TILES = 0x10   # or-ed into a mode: the decode form (tiles of <= 32 rows)
+GEMM_FULL_TILES = 0x20
 
 _bound = False
 
