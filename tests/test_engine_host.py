@@ -6,7 +6,8 @@ oracle.EngineRef):
   forward over the whole sequence, bit for bit) and to routing supplied back;
 - init_engine reads config.json and the checkpoint of a written model and
   gets as far as device allocation (no GPU here), refuses missing or malformed
-  model directories, and never crashes on them.
+  model directories, and never crashes on them;
+- the device memory plan the engine reports matches its documented layout.
 """
 import json
 import os
@@ -128,3 +129,24 @@ def test_model_writer_names(weights):
                                    for s in ("weight", "weight_scale_inv"))
     assert "model.layers.1.mlp.gate.weight" in t and "model.layers.1.mlp.shared_experts.up_proj.weight" in t
     assert t["model.embed_tokens.weight"][1].shape == (SHAPE.vocab_size, SHAPE.hidden)
+
+
+@pytest.mark.parametrize("max_batch,max_seq,chunk,pages", [(4, 64, 0, 0), (64, 1024, 256, 0), (3, 100, 8, 50)])
+def test_engine_device_bytes_plan(max_batch, max_seq, chunk, pages):
+    """glm_engine_device_bytes = the KV pool (per layer a K and a V cache of
+    [pages][16][nkv][128] bf16, 256-byte aligned), two [rows][hidden] bf16
+    activation buffers (rows = max(max_batch, chunk or 2048) rounded to 16), the
+    sampled rows' bf16 [max_batch][hidden], fp32 logits [max_batch][vocab], the
+    page table, per-row index/weight/token arrays, a router stand-in and the
+    staging block."""
+    from time_b200 import engine as EN
+    s = SHAPE
+    got = EN.device_bytes(s, max_batch, max_seq, chunk, pages)
+    rows = -(-max(max_batch, chunk or 2048) // 16) * 16
+    mpps = -(-max_seq // 16)
+    npages = pages or max_batch * mpps
+    kv_layer = -(-(npages * 16 * s.num_kv_heads * 128 * 2) // 256) * 256
+    stage = rows * (8 + 8 + 4 + 4 + 4 + 4)
+    want = (kv_layer * 2 * s.num_layers + 2 * rows * s.hidden * 2 + max_batch * s.hidden * 2 +
+            max_batch * s.vocab_size * 4 + max_batch * mpps * 4 + rows * (8 + 4 + 4) + s.hidden * 4 + stage)
+    assert got == want, (got, want)
