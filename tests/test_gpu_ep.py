@@ -130,9 +130,11 @@ def ep_emulated(shape, w_all, x, ep, routing=None, placement=None):
         hq = torch.empty(R, I, dtype=torch.uint8, device=dev)
         hs = torch.empty(I // 128, R, device=dev)
         y = torch.empty(R, H, dtype=torch.bfloat16, device=dev)
-        M.grouped_gemm(M.GEMM_GATED_SWIGLU, xp, xps, R, wr["w13"], wr["s13"], counts, start, hq, hs, R, H, I, R,
-                       error_word=err)
-        M.grouped_gemm(M.GEMM_DOWN_BF16, hq, hs, R, wr["w2"], wr["s2"], counts, start, y, None, 0, I, H, R,
+        # the layer's GEMM form: the decode form at <= 16 routed tokens per expert over all ranks
+        form = M.GEMM_SMALL_TILES if E > 1 and T * K <= 16 * E else M.GEMM_FULL_TILES
+        M.grouped_gemm(M.GEMM_GATED_SWIGLU | form, xp, xps, R, wr["w13"], wr["s13"], counts, start, hq, hs, R, H, I,
+                       R, error_word=err)
+        M.grouped_gemm(M.GEMM_DOWN_BF16 | form, hq, hs, R, wr["w2"], wr["s2"], counts, start, y, None, 0, I, H, R,
                        error_word=err)
         rtot = rk["plan"][5]
         ysend = torch.zeros(max(rtot, 1), H, dtype=torch.bfloat16, device=dev)

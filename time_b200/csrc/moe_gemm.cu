@@ -68,41 +68,54 @@ constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
 constexpr uint64_t kDrainTimeoutNs = 200000000ull;
 
 // kSmall: the decode form.  A tile holds at most 32 tokens, so an operand
-// stage shrinks to the weights plus 4 KB and the ring holds 5 (gated) or 9
+// stage shrinks to the weights plus 4 KB and the ring holds 4 (gated) or 9
 // (down) stages instead of 3 -- with a few tokens per expert the GEMM is a
-// weight stream, and the weight bytes in flight per SM set its rate.  The
-// promotion and epilogue keep the kNMax column layout (the warps whose
-// columns lie past the tile idle).
+// weight stream.  Its rate is then set by the per-K-block promotion chain
+// (TMEM loads, fold, release), so the four promotion column groups, which
+// all cover the tile's 32 columns here, share the K blocks: group j folds the
+// tile's K blocks kb = j (mod 4); TMEM holds eight 64-column partial buffers
+// (gate at +0, up at +32); at the end of a tile the groups' sums are added in
+// group order 0, 1, 2, 3 through shared memory.  The sum order differs from
+// the full form's, so one caller should use one form for comparable results.
 template <bool kGated, bool kSmall = false>
 struct GemmCfg {
     static constexpr int kNMax = kGated ? 128 : 256;       // token columns of the promotion layout
     static constexpr int kTileTok = kSmall ? 32 : kNMax;   // tokens per tile
-    static constexpr int kStages = kSmall ? (kGated ? 5 : 9) : 3;   // operand ring
+    static constexpr int kStages = kSmall ? (kGated ? 4 : 9) : 3;   // operand ring
     static constexpr int kSStages = 8;                      // token-scale ring
     static constexpr int kATiles = kGated ? 2 : 1;          // gate + up
     static constexpr int kABytes = kATiles * kTileM * kBlockK;
     static constexpr int kBBytes = kTileTok * kBlockK;
     static constexpr int kStageBytes = kABytes + kBBytes;   // 48 KB; small: 36 KB gated, 20 KB down
+    static constexpr int kTBufs = kSmall ? 8 : 2;           // TMEM partial buffers
+    static constexpr int kTBufColsSm = 64;                  // small form: columns per buffer
     static constexpr int kNumCombined = kGated ? 2 : 1;
     static constexpr int kScaleFloats = kNumCombined * kNMax;   // one scale-ring entry
     static constexpr int kRawSlot = kNumCombined - 1;       // where the bulk copy lands in an entry
-    static constexpr int kBufCols = 256;                    // TMEM columns per partial buffer
+    static constexpr int kBufCols = kSmall ? kTBufColsSm : 256;   // TMEM columns per partial buffer
+    static constexpr int kUpOff = kSmall ? 32 : 128;        // the up partial's columns within a buffer
+    static constexpr int kPromoGroups = kSmall ? 4 : 1;     // column groups sharing a tile's K blocks
     static constexpr int kColsPerWarp = kNMax / 4;          // 32 (gated) / 64 (down)
     static constexpr int kOutStageBytes = kGated ? kTileTok * 128 * 4 : kTileTok * 128 * 2;
+    // small form: the column groups' sums, [64 (gated) / 32 columns][128 rows] fp32
+    static constexpr int kRedBytes = kSmall ? (kGated ? 64 : 32) * 128 * 4 : 0;
     // shared-memory carve-up (offsets from the 1024-aligned base)
     static constexpr int kOffStages = 0;
     static constexpr int kOffOut = kOffStages + kStages * kStageBytes;
-    static constexpr int kOffScale = kOffOut + kOutStageBytes;
+    static constexpr int kOffRed = kOffOut + kOutStageBytes;
+    static constexpr int kOffScale = kOffRed + kRedBytes;
     static constexpr int kOffTables = kOffScale + kSStages * kScaleFloats * 4;
     static constexpr int kOffBars = kOffTables + (4 * kMaxGroups + 2) * 4;   // prefix, chunks, start, count
     // full/empty per operand stage; sfull/sempty/cready per scale entry;
     // tfull/tempty per TMEM buffer; one epilogue group barrier
-    static constexpr int kNumBars = 2 * kStages + 3 * kSStages + 4 + 1;
+    static constexpr int kNumBars = 2 * kStages + 3 * kSStages + 2 * kTBufs + 1;
     static constexpr int kOffMisc = kOffBars + kNumBars * 8;
     static constexpr int kSmemBytes = kOffMisc + 64 + 1024;  // + alignment slack
     static_assert(kOffBars % 8 == 0, "mbarrier alignment");
     static_assert(kStageBytes % 1024 == 0, "128-byte-swizzled stages start on 1024-byte boundaries");
     static_assert(kStages <= 32 && kSStages <= 32, "armed masks hold one bit per stage");
+    static_assert(kTBufs * kBufCols <= kTmemCols, "TMEM partial buffers");
+    static_assert(!kSmall || (kSStages == 8 && kTBufs == 8), "small form: ring positions from the K-block count");
     static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
@@ -176,8 +189,8 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
     uint64_t* sempty_bar = sfull_bar + C::kSStages;
     uint64_t* cready_bar = sempty_bar + C::kSStages;
     uint64_t* tfull_bar = cready_bar + C::kSStages;
-    uint64_t* tempty_bar = tfull_bar + 2;
-    uint64_t* epi_bar = tempty_bar + 2;
+    uint64_t* tempty_bar = tfull_bar + C::kTBufs;
+    uint64_t* epi_bar = tempty_bar + C::kTBufs;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffMisc);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kOffMisc + 8);
 
@@ -194,12 +207,12 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
         }
         for (int s = 0; s < C::kSStages; ++s) {
             mbar_init(&sfull_bar[s], 1);
-            mbar_init(&sempty_bar[s], kNumPromoWarps);
+            mbar_init(&sempty_bar[s], kNumPromoWarps / C::kPromoGroups);
             mbar_init(&cready_bar[s], 1);
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < C::kTBufs; ++b) {
             mbar_init(&tfull_bar[b], 1);
-            mbar_init(&tempty_bar[b], kNumPromoWarps);
+            mbar_init(&tempty_bar[b], kNumPromoWarps / C::kPromoGroups);
         }
         mbar_init(epi_bar, kNumPromoWarps);
         *abort_flag = 0;
@@ -312,20 +325,19 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
                         const uint64_t bdesc = umma_desc_sw128(b_addr + k * 32);
                         umma_f8(d, umma_desc_sw128(a_addr + k * 32), bdesc, idesc, k > 0 ? 1u : 0u);
                         if (kGated)
-                            umma_f8(d + 128, umma_desc_sw128(a_addr + kTileM * kBlockK + k * 32), bdesc, idesc,
+                            umma_f8(d + C::kUpOff, umma_desc_sw128(a_addr + kTileM * kBlockK + k * 32), bdesc, idesc,
                                     k > 0 ? 1u : 0u);
                     }
                     umma_commit(&empty_bar[s]);
                     umma_commit(&tfull_bar[b]);
                     issued = true;
                     if (++s == C::kStages) { s = 0; phase ^= 1; }
-                    b ^= 1;
-                    if (b == 0) tphase ^= 1;
+                    if (++b == C::kTBufs) { b = 0; tphase ^= 1; }
                 }
             }
             if (!ok && issued) {
                 // the last commit lands after every MMA this thread issued
-                int lb = b ^ 1;
+                int lb = (b + C::kTBufs - 1) % C::kTBufs;
                 uint32_t lph = (b == 0) ? (tphase ^ 1) : tphase;
                 mbar_drain(&tfull_bar[lb], lph);
             }
@@ -364,12 +376,13 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
         const int pw = warp - kFirstPromoWarp;        // 0..15
         const int quarter = warp & 3;                  // TMEM lane quarter this warp may access
         const int colgrp = pw >> 2;                    // 0..3
-        const int col0 = colgrp * C::kColsPerWarp;
+        const int col0 = kSmall ? 0 : colgrp * C::kColsPerWarp;   // small form: every group covers the tile
         const int row_in_tile = quarter * 32 + lane;   // weight row within the 128-row block
         const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
         int ss = 0, b = 0;
         uint32_t sphase = 0, tphase = 0, ephase = 0;
         bool ok = true;
+        int kbase = 0;   // small form: K blocks of this CTA's earlier tiles
 
         // 32-column pieces per K block: gated = gate cols [col0, +32) and the
         // matching up cols (TMEM +128); down = cols [col0, +32) and [col0+32, +32).
@@ -394,6 +407,17 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
             for (int i = 0; i < kAcc2; ++i) acc2[i] = make_float2(0.0f, 0.0f);
 
             for (int kb = 0; kb < KB; ++kb) {
+                if constexpr (kSmall) {
+                    // group kb % 4 owns K block kb of every tile (so a row's partial sums
+                    // never depend on where its tile ran); ring positions and parities
+                    // follow the CTA's K-block count, as the producer and MMA issue them
+                    if ((kb & 3) != colgrp) continue;
+                    const int g = kbase + kb;
+                    ss = g & 7;
+                    sphase = (g >> 3) & 1;
+                    b = g & 7;
+                    tphase = (g >> 3) & 1;
+                }
                 if (!mbar_wait_bounded(&cready_bar[ss], sphase, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
                 if (!mbar_wait_bounded(&tfull_bar[b], tphase, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
                 tc_fence_after();
@@ -403,7 +427,7 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
                 // chunk c+1 is in flight while chunk c is folded
                 auto ld_chunk = [&](int c, uint32_t (&pv)[16]) {
                     const int q = c >> 1, h = c & 1;
-                    const int tcol = kGated ? (q * 128 + col0) : (col0 + 32 * q);
+                    const int tcol = kGated ? (q * C::kUpOff + col0) : (col0 + 32 * q);
                     tmem_ld16(tbuf + tcol + 16 * h, pv);
                 };
                 auto fold_chunk = [&](int c, const uint32_t (&pv)[16]) {
@@ -454,11 +478,44 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
                     mbar_arrive(&tempty_bar[b]);
                     mbar_arrive(&sempty_bar[ss]);
                 }
-                if (++ss == C::kSStages) { ss = 0; sphase ^= 1; }
-                b ^= 1;
-                if (b == 0) tphase ^= 1;
+                if constexpr (!kSmall) {
+                    if (++ss == C::kSStages) { ss = 0; sphase ^= 1; }
+                    if (++b == C::kTBufs) { b = 0; tphase ^= 1; }
+                }
             }
             if (!ok || *abort_flag) { ok = false; break; }
+            if constexpr (kSmall) {
+                kbase += KB;
+                // the groups' sums, added in group order: red = acc0, += acc1, += acc2; group 3 keeps the total
+                float* red = reinterpret_cast<float*>(smem + C::kOffRed);   // [column][128 rows]
+                constexpr int kRedPairs = kGated ? 32 : 16;
+                // acc2[q * 16 + k] holds piece q's columns 2k, 2k + 1
+                auto red_col = [](int i) { return kGated ? (i >> 4) * 32 + 2 * (i & 15) : 2 * i; };
+                auto add_red = [&]() {
+#pragma unroll
+                    for (int i = 0; i < kRedPairs; ++i) {
+                        const int c = red_col(i);
+                        acc2[i].x += red[c * 128 + row_in_tile];
+                        acc2[i].y += red[(c + 1) * 128 + row_in_tile];
+                    }
+                };
+                auto store_red = [&]() {
+#pragma unroll
+                    for (int i = 0; i < kRedPairs; ++i) {
+                        const int c = red_col(i);
+                        red[c * 128 + row_in_tile] = acc2[i].x;
+                        red[(c + 1) * 128 + row_in_tile] = acc2[i].y;
+                    }
+                };
+                if (colgrp == 0) store_red();
+                if (!group_sync()) { ok = false; break; }
+                if (colgrp == 1) { add_red(); store_red(); }
+                if (!group_sync()) { ok = false; break; }
+                if (colgrp == 2) { add_red(); store_red(); }
+                if (!group_sync()) { ok = false; break; }
+                if (colgrp == 3) add_red();
+                if (!ok) break;
+            }
 
             // ---------------------------------------------------------- epilogue
             // acc2[i] holds columns 2i, 2i+1 of this warp's 64 accumulators:
@@ -471,8 +528,8 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
                     const float g = (c & 1) ? acc2[c >> 1].y : acc2[c >> 1].x;
                     const float u = (c & 1) ? acc2[16 + (c >> 1)].y : acc2[16 + (c >> 1)].x;
                     const float h = (g / (1.0f + expf(-g))) * u;
-                    // the small form's stage holds only the tile's columns
-                    if (!kSmall || col0 + c < tc.ntile) stage[(col0 + c) * 128 + row_in_tile] = h;
+                    // the small form's stage holds only the tile's columns, written by group 3 (the total)
+                    if (!kSmall || (colgrp == 3 && col0 + c < tc.ntile)) stage[(col0 + c) * 128 + row_in_tile] = h;
                 }
                 if (!group_sync()) { ok = false; break; }
                 uint8_t* outq = reinterpret_cast<uint8_t*>(p.out);
@@ -502,7 +559,8 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
 #pragma unroll
                 for (int c = 0; c < C::kColsPerWarp; ++c) {
                     const float v = (c & 1) ? acc2[c >> 1].y : acc2[c >> 1].x;
-                    if (!kSmall || col0 + c < tc.ntile) stage[(col0 + c) * 128 + row_in_tile] = __float2bfloat16_rn(v);
+                    if (!kSmall || (colgrp == 3 && col0 + c < tc.ntile))
+                        stage[(col0 + c) * 128 + row_in_tile] = __float2bfloat16_rn(v);
                 }
                 if (!group_sync()) { ok = false; break; }
                 __nv_bfloat16* outy = reinterpret_cast<__nv_bfloat16*>(p.out);

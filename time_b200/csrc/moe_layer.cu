@@ -149,7 +149,19 @@ moe_status_t cbw_to_moe(cbwStatus_t s) {
 
 moe_status_t nccl_to_moe(ncwResult_t r) { return r == NCW_SUCCESS ? MOE_OK : MOE_ERR_NCCL; }
 
-cbwGroupedGemmArgs gemm_args(const moe_layer* L, void* ws, bool down) {
+// The grouped GEMM's decode form (32-row tiles whose K blocks the promotion
+// groups share) when the call averages at most 16 routed tokens per expert
+// over all ranks (T x ep_size x top_k <= 16 x E): the same choice on every
+// rank of an expert-parallel call, so its rows match the one-GPU layer bit for
+// bit.  One expert (a dense FFN as one group) always takes the full form.
+int gemm_form(const moe_layer* L, int T) {
+    const moe_layer_config_t& c = L->cfg;
+    const bool small = c.num_experts > 1 &&
+                       static_cast<long long>(T) * c.ep_size * c.top_k <= 16ll * c.num_experts;
+    return small ? CBW_GEMM_SMALL_TILES : CBW_GEMM_FULL_TILES;
+}
+
+cbwGroupedGemmArgs gemm_args(const moe_layer* L, void* ws, bool down, int T) {
     const moe_layer_config_t& c = L->cfg;
     cbwGroupedGemmArgs g;
     std::memset(&g, 0, sizeof(g));
@@ -159,7 +171,7 @@ cbwGroupedGemmArgs gemm_args(const moe_layer* L, void* ws, bool down) {
     g.count = at<int32_t>(ws, L->off_counts);
     g.start = at<int32_t>(ws, L->off_start);
     if (!down) {
-        g.mode = CBW_GEMM_GATED_SWIGLU;
+        g.mode = CBW_GEMM_GATED_SWIGLU | gemm_form(L, T);
         g.K = c.hidden;
         g.N = c.intermediate;
         g.a = at<void>(ws, L->off_xp);
@@ -170,7 +182,7 @@ cbwGroupedGemmArgs gemm_args(const moe_layer* L, void* ws, bool down) {
         g.out_scale = at<float>(ws, L->off_hs);
         g.out_ld = L->rcap;
     } else {
-        g.mode = CBW_GEMM_DOWN_BF16;
+        g.mode = CBW_GEMM_DOWN_BF16 | gemm_form(L, T);
         g.K = c.intermediate;
         g.N = c.hidden;
         g.a = at<void>(ws, L->off_hq);
@@ -197,7 +209,7 @@ moe_status_t run_experts(moe_layer* L, const void* x, const int32_t* idx, const 
     mark(L, 3, st);
     MOE_TRY(moe_gather_rows_n(at<void>(ws, L->off_xq), at<float>(ws, L->off_xs), L->xs_ld, rowtok, total, L->rcap, H,
                               at<void>(ws, L->off_xp), at<float>(ws, L->off_xps), L->rcap, st));
-    cbwGroupedGemmArgs g1 = gemm_args(L, ws, false), g2 = gemm_args(L, ws, true);
+    cbwGroupedGemmArgs g1 = gemm_args(L, ws, false, T), g2 = gemm_args(L, ws, true, T);
     mark(L, 4, st);
     MOE_TRY(cbw_to_moe(cbwFp8BlockScaledGroupedGemm(&g1, L->error_word, st)));
     mark(L, 5, st);
@@ -256,7 +268,7 @@ moe_status_t run_experts_ep(moe_layer* L, const int32_t* idx, const float* wts, 
         MOE_TRY(moe_ep_gather(mine + P.lay.off_recv, at<void>(ws, L->off_xq), at<float>(ws, L->off_xs), L->xs_ld,
                               row_src, total, L->rcap, H, at<void>(ws, L->off_xp), at<float>(ws, L->off_xps), L->rcap,
                               st));
-        cbwGroupedGemmArgs g1 = gemm_args(L, ws, false), g2 = gemm_args(L, ws, true);
+        cbwGroupedGemmArgs g1 = gemm_args(L, ws, false, T), g2 = gemm_args(L, ws, true, T);
         mark(L, 4, st);
         MOE_TRY(cbw_to_moe(cbwFp8BlockScaledGroupedGemm(&g1, L->error_word, st)));
         mark(L, 5, st);
@@ -301,7 +313,7 @@ moe_status_t run_experts_ep(moe_layer* L, const int32_t* idx, const float* wts, 
                              L->error_word, st));
     MOE_TRY(moe_ep_gather(at<void>(ws, L->off_precv), at<void>(ws, L->off_xq), at<float>(ws, L->off_xs), L->xs_ld,
                           row_src, total, L->rcap, H, at<void>(ws, L->off_xp), at<float>(ws, L->off_xps), L->rcap, st));
-    cbwGroupedGemmArgs g1 = gemm_args(L, ws, false), g2 = gemm_args(L, ws, true);
+    cbwGroupedGemmArgs g1 = gemm_args(L, ws, false, T), g2 = gemm_args(L, ws, true, T);
     mark(L, 4, st);
     MOE_TRY(cbw_to_moe(cbwFp8BlockScaledGroupedGemm(&g1, L->error_word, st)));
     mark(L, 5, st);
