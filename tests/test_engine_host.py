@@ -150,3 +150,22 @@ def test_engine_device_bytes_plan(max_batch, max_seq, chunk, pages):
     want = (kv_layer * 2 * s.num_layers + 2 * rows * s.hidden * 2 + max_batch * s.hidden * 2 +
             max_batch * s.vocab_size * 4 + max_batch * mpps * 4 + rows * (8 + 4 + 4) + s.hidden * 4 + stage)
     assert got == want, (got, want)
+
+
+def test_native_engine_unloaded_behaviour(tmp_path):
+    """NativeEngine before a successful load behaves as the reference's
+    wrapper does (src/server/engine_wrapper.py:44-196): load() is False for a
+    missing library or a model that does not load, and every call reports
+    "nothing" instead of raising."""
+    from time_b200 import engine as EN
+    e = EN.NativeEngine(engine_path=str(tmp_path / "missing.so"), model_dir=str(tmp_path))
+    assert e.load() is False and not e.is_loaded()
+    e2 = EN.NativeEngine(model_dir=str(tmp_path / "no_model"))
+    assert e2.load() is False and not e2.is_loaded()
+    for eng in (e, e2):
+        assert eng.get_info() is None
+        assert eng.prefill(1, [1, 2, 3], 0.0, 1.0, 1.0, 4) is None
+        assert eng.decode_step(None) == (None, True)
+        assert eng.batch_decode([None, None]) == [(None, True), (None, True)]
+        eng.free_request(None)
+        eng.shutdown()
