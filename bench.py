@@ -1,22 +1,33 @@
 #!/usr/bin/env python
 """MoE-layer tokens/s on B200 (BASELINE.json metric) for the GLM-4.x-shape MoE
 FFN block: hidden 5120, 160 routed experts top-8 + 1 shared expert,
-intermediate 1536, 4096 tokens, zipf-skewed router.
+intermediate 1536, SwiGLU, FP8 e4m3 expert weights with 128x128 block scales.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload prefill|decode]
 
-One step = one forward of the MoE FFN block (RMSNorm -> router/top-k ->
-permute -> gate/up GEMM + SwiGLU -> down GEMM -> combine + residual) over the
-4096 tokens, inputs resident in HBM.  With N > 1 the 4096 tokens are split
-over N expert-parallel ranks (strong scaling: rank r owns 160/N experts and
-4096/N tokens, NCCL all-to-all dispatch/combine), and rank 0 prints one JSON
-line with the max-over-ranks time.
+prefill (default): one step = one forward of the MoE
+FFN block (RMSNorm -> router/top-k -> permute -> gate/up GEMM + SwiGLU ->
+down GEMM -> combine + residual) over 4096 tokens with the zipf-skewed router
+bias, inputs resident in HBM.
+decode: one step = 256 tokens whose routing comes from
+uniform random router logits (top-8 softmax of U(0,1) logits, supplied to
+the layer's routed forward); the per-expert token histogram is printed.
+
+With N > 1 the tokens are split over N expert-parallel ranks (strong
+scaling: rank r owns 160/N experts and T/N tokens).  The exchange is the
+layer's NVLink peer-memory exchange by default (own kernels: P2P stores with
+device-side flags, no host synchronisation), `--exchange nccl` for NCCL
+send/recv; rows travel as e4m3 + 1x128 scales, outputs return as bf16.
+Rank 0 prints one JSON line with the max-over-ranks time.
 
 `e2e` is the same metric through the public layer call with host buffers:
-pinned host x -> device, forward, device -> pinned host output, every step.
-`cpu_baseline` / `--impl reference` time the CPU restatement of the
-reference's path (the oracle, fp32 activations -- the reference has no CPU
-MoE path of its own that builds here) on the host cores on a bounded sample.
+pinned host x (and, for decode, the routing) -> device, forward, device ->
+pinned host output, every step.  `cpu_baseline` / `--impl reference` time
+the CPU restatement of the reference's path (the oracle, fp32 activations --
+the reference has no CPU MoE path of its own that builds here) on the host
+cores on a bounded sample; the same sample gives the `parity` key: the GPU
+output of those tokens against the oracle's fp32-activation result.
 """
 from __future__ import annotations
 
@@ -33,7 +44,9 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "MoE-layer tokens/sec at 1/2/4/8 B200 (EP); % of FP8/HBM/NVLink roofline"
 UNIT = "tokens/s"
-TOKENS = 4096
+TOKENS = {"prefill": 4096, "decode": 256}
+WORKLOAD = {"prefill": "glm4x_moe_ffn_prefill (BASELINE configs[1])",
+            "decode": "glm4x_moe_ffn_decode (BASELINE configs[2])"}
 
 
 def parse():
@@ -42,16 +55,34 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--tokens", type=int, default=TOKENS)
+    ap.add_argument("--workload", choices=["prefill", "decode"], default="prefill")
+    ap.add_argument("--tokens", type=int, default=None, help="global tokens per step (default 4096 prefill, 256 decode)")
     ap.add_argument("--experts", type=int, default=160,
                     help="routed experts (profiling captures of a smaller case only; the metric uses 160)")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
                     help="expert-parallel exchange for N > 1: NVLink peer memory (own kernels) or NCCL send/recv")
-    ap.add_argument("--placement", choices=["balanced", "contiguous"], default="balanced",
-                    help="expert placement for N > 1: load-balanced from a calibration batch, or contiguous slices")
+    ap.add_argument("--placement", choices=["balanced", "contiguous"], default=None,
+                    help="expert placement for N > 1: load-balanced from a calibration batch (prefill default), "
+                         "or contiguous slices (decode default: configs[2] names 160/EP experts per GPU)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    return ap.parse_args()
+    a = ap.parse_args()
+    if a.tokens is None:
+        a.tokens = TOKENS[a.workload]
+    if a.placement is None:
+        a.placement = "balanced" if a.workload == "prefill" else "contiguous"
+    return a
+
+
+def decode_routing(shape, T: int, device):
+    """configs[2] routing: router logits drawn U(0,1) [T][E] (seeded), the
+    top-k by value (equal values do not occur in practice among 160 uniform
+    fp32 draws) and softmax weights over the selected logits."""
+    import torch
+    from time_b200 import synth
+    logits = synth.uniform_routing(T, shape.num_experts, shape.top_k, seed=4, device=device)
+    top = torch.topk(logits, shape.top_k, dim=1)
+    return top.indices.to(torch.int32).contiguous(), torch.softmax(top.values, dim=1).contiguous()
 
 
 def load_peaks():
@@ -130,18 +161,27 @@ def cpu_threads() -> int:
         return os.cpu_count() or 1
 
 
-def cpu_baseline(shape, weights_cpu, x_cpu, budget_s: float, fixed_tokens: int | None = None):
+def cpu_baseline(shape, weights_cpu, x_cpu, budget_s: float, fixed_tokens: int | None = None, routing=None):
     """The oracle (fp32-activation "ref" mode, OpenMP over tokens, all host
-    threads) on a bounded sample of the workload's tokens; tokens/s."""
+    threads) on a bounded sample of the workload's tokens; tokens/s.  With
+    `routing` ((idx, w) host tensors of every token) the experts run on that
+    routing (the decode workload's supplied routing).  Also returns the
+    sample's output (bf16 bits) for the parity check."""
     import numpy as np
     from oracle import oracle as orc   # CPU-baseline leg: the checker timed as the reference's CPU path
     ow = orc.OracleWeights(shape, weights_cpu)
     xb = x_cpu.contiguous().view(__import__("torch").int16).numpy().view(np.uint16)
     th = cpu_threads()
+
+    def run(n):
+        if routing is None:
+            return orc.moe_ffn_forward(ow, xb[:n], mode=1, threads=th)[0]
+        return orc.moe_ffn_experts(ow, xb[:n], routing[0][:n].numpy(), routing[1][:n].numpy(), mode=1, threads=th)
+
     if fixed_tokens is None:
         n = min(th, xb.shape[0])
         t0 = time.perf_counter()
-        orc.moe_ffn_forward(ow, xb[:n], mode=1, threads=th)
+        run(n)
         dt = time.perf_counter() - t0
         n = int(max(n, min(xb.shape[0], n * budget_s / max(dt, 1e-3))))
         n = max(th, (n // th) * th)
@@ -149,11 +189,26 @@ def cpu_baseline(shape, weights_cpu, x_cpu, budget_s: float, fixed_tokens: int |
     else:
         n = fixed_tokens
     t0 = time.perf_counter()
-    orc.moe_ffn_forward(ow, xb[:n], mode=1, threads=th)
+    out = run(n)
     dt = time.perf_counter() - t0
+    what = "full layer" if routing is None else "experts + combine on the supplied routing"
     return {"value": n / dt, "unit": UNIT, "cores": th, "kind": "port",
-            "sample": f"{n} of {xb.shape[0]} tokens, full layer incl. all routed + shared experts, "
-                      f"oracle ref mode (fp32 activations), {dt:.1f} s"}, n, dt
+            "sample": f"{n} of {xb.shape[0]} tokens, {what} incl. all routed + shared experts, "
+                      f"oracle ref mode (fp32 activations), {dt:.1f} s"}, n, dt, out
+
+
+def parity_of(out_gpu, ref_bits, n: int):
+    """The north-star tolerance metrics of the GPU output's first n tokens
+    against the oracle's fp32-activation ("ref" mode) result."""
+    import numpy as np
+    from oracle import oracle as orc
+    y = out_gpu[:n].float().cpu().numpy()
+    mr, mae = orc.max_rel_and_mae(y, orc.bf16_bits_to_f32(ref_bits))
+    return {"tokens": n, "against": "oracle ref mode: fp32 activations, dequantised e4m3 weights, fp32 router",
+            "max_rel": mr, "mae": mae, "bar": {"max_rel": 1e-2, "mae": 2e-3},
+            "within_bar": bool(mr <= 1e-2 and mae <= 2e-3),
+            "note": "the layer computes with e4m3 activations (1x128 scales) as the north star specifies; "
+                    "3 mantissa bits give ~3.6% RMS relative rounding per activation, which this gap measures"}
 
 
 # ---------------------------------------------------------------- algorithmic work
@@ -197,22 +252,26 @@ def run_reference(args):
     if rank != 0:
         return 0
     shape = synth.GLM
+    decode = args.workload == "decode"
     torch.manual_seed(0)
-    w = synth.make_moe_weights(shape, seed=0, device="cpu", zipf_bias=True)
+    w = synth.make_moe_weights(shape, seed=0, device="cpu", zipf_bias=not decode)
     x = synth.make_x(shape, args.tokens, seed=1, device="cpu")
+    routing = decode_routing(shape, args.tokens, "cpu") if decode else None
     th = cpu_threads()
     # size one step to ~budget/steps seconds so the whole run stays within minutes
     per_step = max(2.0, min(20.0, 120.0 / max(1, args.steps + args.warmup)))
-    _, n, _ = cpu_baseline(shape, w, x, per_step)
+    _, n, _, _ = cpu_baseline(shape, w, x, per_step, routing=routing)
+    from oracle import oracle as orc
+    import numpy as np
+    ow = orc.OracleWeights(shape, w)
+    xb = x[:n].contiguous().view(torch.int16).numpy().view(np.uint16)
     times = []
     for i in range(args.warmup + args.steps):
-        t0 = time.perf_counter()
-        from oracle import oracle as orc
-        ow = orc.OracleWeights(shape, w) if i == 0 else ow
-        import numpy as np
-        xb = x[:n].contiguous().view(torch.int16).numpy().view(np.uint16)
         t1 = time.perf_counter()
-        orc.moe_ffn_forward(ow, xb, mode=1, threads=th)
+        if decode:
+            orc.moe_ffn_experts(ow, xb, routing[0][:n].numpy(), routing[1][:n].numpy(), mode=1, threads=th)
+        else:
+            orc.moe_ffn_forward(ow, xb, mode=1, threads=th)
         dt = time.perf_counter() - t1
         if i >= args.warmup:
             times.append(dt)
@@ -221,9 +280,11 @@ def run_reference(args):
     line = {"metric": METRIC, "impl": "reference", "value": value, "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "glm4x_moe_ffn_prefill", "tokens": args.tokens, "hidden": shape.hidden,
+            "config": {"workload": WORKLOAD[args.workload], "tokens": args.tokens, "hidden": shape.hidden,
                        "experts": shape.num_experts, "top_k": shape.top_k, "intermediate": shape.intermediate,
-                       "shared_experts": shape.num_shared, "router": "softmax top-k, zipf(1.1) bias",
+                       "shared_experts": shape.num_shared,
+                       "router": ("top-8 softmax of U(0,1) logits (supplied routing)" if decode
+                                  else "softmax top-k, zipf(1.1) bias"),
                        "sample_tokens_per_step": n},
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": th, "kind": "port",
                              "sample": f"{n} tokens per step of the {args.tokens}-token workload, oracle ref mode"},
@@ -252,6 +313,7 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
         comm = M.nccl_comm(rank, world)
 
+    decode = args.workload == "decode"
     shape = synth.GLM
     if args.experts != shape.num_experts:
         import dataclasses
@@ -259,7 +321,7 @@ def run_ours(args):
     if shape.num_experts % world:
         raise SystemExit(f"{shape.num_experts} experts do not split over {world} ranks")
     T = args.tokens
-    w_all = synth.make_moe_weights(shape, seed=0, device=dev, zipf_bias=True)
+    w_all = synth.make_moe_weights(shape, seed=0, device=dev, zipf_bias=not decode)
     placement = None
     if world > 1 and args.placement == "balanced":
         # per-expert load measured on a calibration batch (not the timed tokens), the same table on every rank
@@ -272,6 +334,13 @@ def run_ours(args):
     t0, t1 = synth.token_slice(T, world, rank)
     x = x_all[t0:t1].contiguous()
     del x_all
+    routing = None
+    hist = None
+    if decode:
+        idx_all, w_all_r = decode_routing(shape, T, dev)         # the same draw on every rank
+        hist = torch.bincount(idx_all.flatten().long(), minlength=shape.num_experts).tolist()
+        routing = (idx_all[t0:t1].contiguous(), w_all_r[t0:t1].contiguous())
+        del idx_all, w_all_r
     Tr = t1 - t0
     max_tokens = -(-T // world)
     out = torch.empty_like(x)
@@ -294,10 +363,12 @@ def run_ours(args):
         return float(t.item())
 
     for _ in range(max(3, args.warmup)):
-        layer.forward(x, out)
+        layer.forward(x, out, routing=routing)
     torch.cuda.synchronize()
     layer.check_error()
     idx, _, counts = layer.last_routing(Tr)
+    if decode:
+        idx = routing[0].cpu()
 
     # ---- device-resident timed region with per-stage events
     K = args.steps
@@ -309,7 +380,7 @@ def run_ours(args):
         start.record(stream)
         for i in range(K):
             layer.set_stage_events(stage_ev[i])
-            layer.forward(x, out)
+            layer.forward(x, out, routing=routing)
         end.record(stream)
         torch.cuda.synchronize()
     barrier()
@@ -330,23 +401,32 @@ def run_ours(args):
     x_host = x.cpu().pin_memory()
     out_host = torch.empty(x_host.shape, dtype=x_host.dtype).pin_memory()
     x_dev = torch.empty_like(x)
-    for _ in range(2):
+    r_host = r_dev = None
+    if decode:
+        r_host = tuple(t_.cpu().pin_memory() for t_ in routing)
+        r_dev = tuple(torch.empty_like(t_) for t_ in routing)
+
+    def e2e_step():
         x_dev.copy_(x_host, non_blocking=True)
-        layer.forward(x_dev, out)
+        if decode:
+            for d_, h_ in zip(r_dev, r_host):
+                d_.copy_(h_, non_blocking=True)
+        layer.forward(x_dev, out, routing=r_dev)
         out_host.copy_(out, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
     torch.cuda.synchronize()
     barrier()
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_start.record(stream)
     for _ in range(K):
-        x_dev.copy_(x_host, non_blocking=True)
-        layer.forward(x_dev, out)
-        out_host.copy_(out, non_blocking=True)
+        e2e_step()
     e_end.record(stream)
     torch.cuda.synchronize()
     barrier()
     e2e_ms = max_over_ranks(e_start.elapsed_time(e_end) / K)
-    h2d = x.numel() * x.element_size()
+    h2d = x.numel() * x.element_size() + (sum(t_.numel() * t_.element_size() for t_ in routing) if decode else 0)
     d2h = out.numel() * out.element_size()
 
     # ---- roofline of the dominant kernel (this rank) and of the layer
@@ -362,11 +442,15 @@ def run_ours(args):
     dom_s = stages[dom] / 1000.0
     achieved_gbs = dom_bytes / dom_s / 1e9
     roofline = {"kernel": dom, "bound": "hbm", "achieved": achieved_gbs, "peak": peaks["hbm_gbs"],
-                "unit": "GB/s", "frac": achieved_gbs / peaks["hbm_gbs"], "traffic": load_traffic(dom),
+                "unit": "GB/s", "frac": achieved_gbs / peaks["hbm_gbs"],
+                "traffic": load_traffic(dom) if not decode else None,
                 "peak_source": peaks["source"], "algorithmic_bytes": dom_bytes,
                 "tensor_tflops": dom_flops / dom_s / 1e12}
     lb, lf = work["layer"]
-    if world > 1:
+    if decode:
+        lb -= shape.num_experts * shape.hidden * 4                  # the router does not run: routing is supplied
+        lf -= 2.0 * Tr * shape.hidden * shape.num_experts
+    elif world > 1:
         lb += (shape.num_experts - G_local) * shape.hidden * 4      # router weights are replicated
         lf += 2.0 * Tr * shape.hidden * (shape.num_experts - G_local)
     idx_h = idx.flatten().tolist()
@@ -399,33 +483,44 @@ def run_ours(args):
                       "note": "per rank, max over ranks; fp8 peak = 2x measured bf16 (no fp8 measurement "
                               "in MEASURED_PEAKS.json); nvlink = measured peer copy per direction"}
 
-    cpu = None
+    cpu = parity = None
     if not args.no_cpu_baseline and world == 1:
         wc = {k_: (v.cpu() if isinstance(v, torch.Tensor) else v) for k_, v in w.items()}
-        cpu, _, _ = cpu_baseline(shape, wc, x.cpu(), args.cpu_seconds)
+        rc_ = tuple(t_.cpu() for t_ in routing) if decode else None
+        layer.forward(x, out, routing=routing)
+        torch.cuda.synchronize()
+        cpu, n_s, _, ref_bits = cpu_baseline(shape, wc, x.cpu(), args.cpu_seconds, routing=rc_)
+        parity = parity_of(out, ref_bits, n_s)
 
     # our kernels per forward: rmsnorm, router logits, top-k, 3 permutation kernels (count, scan,
-    # scatter), gather, 2 GEMMs, combine = 10; EP replaces gather/combine and adds (NCCL) row pack,
-    # receive plan, gather, output pack, split combine = 13 or (peer memory) counts, dispatch,
-    # 2 signal/waits, receive plan, gather, output send, split combine = 16; the expert placement
-    # adds its remap kernel.  NCCL's own kernels are not counted.
+    # scatter), gather, 2 GEMMs, combine = 10 (8 with supplied routing); EP replaces gather/combine
+    # and adds (NCCL) row pack, receive plan, gather, output pack, split combine = 13 or (peer memory)
+    # counts, dispatch, 2 signal/waits, receive plan, gather, output send, split combine = 16; the
+    # expert placement adds its remap kernel.  NCCL's own kernels are not counted.
     launches_per_step = 10 if world == 1 else ((13 if args.exchange == "nccl" else 16) + (1 if placement else 0))
+    if decode:
+        launches_per_step -= 2
+    dispatch = None
+    if world > 1:
+        dispatch = ("fp8 rows + 1x128 scales (5,280 B per row at H = 5120; BASELINE configs[2] names bf16 hidden "
+                    "states -- a deviation: the GEMM reads e4m3 rows, so sending them halves the bytes), combine "
+                    "bf16, " + ("NVLink peer-memory stores from own kernels, no host sync" if args.exchange == "peer"
+                                else "NCCL send/recv, one host sync"))
     line = {"metric": METRIC, "value": T * 1000.0 / ms_per_step, "unit": UNIT, "n_gpus": world,
             "steps": K, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "e4m3 x e4m3 -> f32 (bf16 in/out)",
             "data": "synthetic",
-            "config": {"workload": "glm4x_moe_ffn_prefill (BASELINE configs[1])", "tokens": T,
+            "config": {"workload": WORKLOAD[args.workload], "tokens": T,
                        "tokens_per_rank": max_tokens,
                        "hidden": shape.hidden, "experts": shape.num_experts, "top_k": shape.top_k,
                        "intermediate": shape.intermediate, "shared_experts": shape.num_shared,
-                       "router": "fp32 softmax top-k, zipf(1.1) bias", "parallelism": f"ep{world}",
+                       "router": ("top-8 softmax of U(0,1) logits (supplied to the routed forward)" if decode
+                                  else "fp32 softmax top-k in the reference's summation order, zipf(1.1) bias"),
+                       "parallelism": f"ep{world}",
                        "expert_placement": ((args.placement + (" (greedy by routed pairs of a separate 4096-token "
                                                                 "calibration batch)" if placement else ""))
                                             if world > 1 else None),
-                       "dispatch": (("fp8 rows + 1x128 scales, combine bf16, " +
-                                     ("NVLink peer-memory stores from own kernels, no host sync"
-                                      if args.exchange == "peer" else "NCCL send/recv, one host sync"))
-                                    if world > 1 else None),
+                       "dispatch": dispatch,
                        "l2": "inputs larger than L2: %.1f GB of expert weights streamed per step per rank"
                              % (sum(v.numel() for k_, v in w.items() if k_ in ("w13", "w2")) / 1e9)},
             "e2e": {"value": T * 1000.0 / e2e_ms, "unit": UNIT, "h2d_bytes_per_step": h2d,
@@ -436,7 +531,9 @@ def run_ours(args):
             "routed_rows_per_rank": {"max": rows_max, "mean": rows_mean},
             "expert_tokens_rank0": {"max": int(counts[:G_local].max()), "min": int(counts[:G_local].min()),
                                     "mean": float(counts[:G_local].float().mean())},
-            "gpu_launches": K * launches_per_step, "clocks": clocks, "cpu_baseline": cpu}
+            "gpu_launches": K * launches_per_step, "clocks": clocks, "cpu_baseline": cpu, "parity": parity}
+    if hist is not None:
+        line["expert_histogram"] = hist
     if rank == 0:
         print(json.dumps(line), flush=True)
     layer.close()

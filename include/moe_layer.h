@@ -150,6 +150,16 @@ moe_status_t moe_layer_set_peer_buffers(moe_layer_t* layer, void* const* peer_bu
  * moe_layer_destroy); NULL restores the contiguous placement. */
 moe_status_t moe_layer_set_expert_placement(moe_layer_t* layer, const int32_t* slot_of_expert);
 
+/* No counterpart in the reference.  Which form of the grouped GEMM the
+ * forward runs: CBW_GEMM_SMALL_TILES (the decode form), CBW_GEMM_FULL_TILES,
+ * or 0 for the default rule -- the decode form when the call averages at most
+ * 16 routed tokens per expert, counting max_tokens x ep_size tokens when
+ * ep_size > 1 (the same count on every rank) and the call's tokens on one
+ * GPU.  The two forms add a row's K blocks in different orders, so outputs
+ * differ in the last bits between them; an expert-parallel layer and a
+ * one-GPU layer give bit-identical outputs when they run the same form. */
+moe_status_t moe_layer_set_gemm_form(moe_layer_t* layer, int form);
+
 /* Reads and clears the device error word (synchronises `stream`). */
 moe_status_t moe_layer_check_error(moe_layer_t* layer, cwStream_t stream);
 

@@ -160,19 +160,18 @@ void orc_moe_gate_ref(const float* hidden, const float* w, float* logits,
                 tree256_dot(hidden + (size_t)t * hidden_dim, w + (size_t)e * hidden_dim, hidden_dim);
 }
 
-void orc_moe_gate_seq(const float* hidden, const float* w, const float* bias,
-                      float* logits, int hidden_dim, int num_experts, int tokens) {
+/* The MoE layer's router: the reference's logits (csrc/kernels.cu:412-435,
+ * the same tree256_dot) plus the new-build routing bias, added in fp32 after
+ * the tree (bias may be NULL). */
+void orc_moe_router_logits(const float* hidden, const float* w, const float* bias,
+                           float* logits, int hidden_dim, int num_experts, int tokens) {
 #pragma omp parallel for schedule(static)
-    for (int t = 0; t < tokens; ++t) {
-        const float* h = hidden + (size_t)t * hidden_dim;
+    for (int t = 0; t < tokens; ++t)
         for (int e = 0; e < num_experts; ++e) {
-            const float* we = w + (size_t)e * hidden_dim;
-            float s = 0.0f;
-            for (int i = 0; i < hidden_dim; ++i) s = fmaf(h[i], we[i], s);
+            float s = tree256_dot(hidden + (size_t)t * hidden_dim, w + (size_t)e * hidden_dim, hidden_dim);
             if (bias) s = s + bias[e];
             logits[(size_t)t * num_experts + e] = s;
         }
-    }
 }
 
 /* csrc/kernels.cu:437-471 */
@@ -388,7 +387,7 @@ void orc_moe_ffn_forward(const orc_moe_cfg* cfg, const orc_moe_weights* w,
     float* logits = (float*)malloc(sizeof(float) * (size_t)tokens * E);
     int32_t* idx = (int32_t*)malloc(sizeof(int32_t) * (size_t)tokens * K);
     float* wts = (float*)malloc(sizeof(float) * (size_t)tokens * K);
-    orc_moe_gate_seq(n, w->router_w, w->router_bias, logits, cfg->hidden, E, tokens);
+    orc_moe_router_logits(n, w->router_w, w->router_bias, logits, cfg->hidden, E, tokens);
     orc_moe_topk_ref(logits, idx, wts, E, K, tokens);
     ffn_experts_impl(cfg, w, x_bf16, n, idx, wts, out_bf16, tokens, mode, threads);
     if (idx_out) memcpy(idx_out, idx, sizeof(int32_t) * (size_t)tokens * K);

@@ -61,12 +61,11 @@ void orc_rms_ref(const float* x, float* rms, int hidden, int rows, float eps);
  * logits[t][e] = tree256(fma partials of hidden[t] . W[e]). */
 void orc_moe_gate_ref(const float* hidden, const float* w, float* logits,
                       int hidden_dim, int num_experts, int tokens);
-/* Router logits in the order the MoE path's router kernel uses: one fma chain
- * over i = 0..H-1 ascending from +0.0f, then + bias[e] (if bias != NULL).
- * The value is the same dot product as the reference's; only the fp32
- * summation order differs. */
-void orc_moe_gate_seq(const float* hidden, const float* w, const float* bias,
-                      float* logits, int hidden_dim, int num_experts, int tokens);
+/* The MoE layer's router logits: orc_moe_gate_ref's value for each (t, e)
+ * (the reference's 256-lane fma partials and pairwise tree) + bias[e] in fp32
+ * when bias != NULL. */
+void orc_moe_router_logits(const float* hidden, const float* w, const float* bias,
+                           float* logits, int hidden_dim, int num_experts, int tokens);
 
 /* Top-k, csrc/kernels.cu:437-471: insertion with strict '>' from -FLT_MAX, so
  * the lower expert index wins a tie and NaN is never selected (slot index
@@ -116,7 +115,7 @@ int orc_moe_permute(const int32_t* idx, int tokens, int top_k, int num_experts,
 void orc_quant_row_1x128(const float* v, int cols, uint8_t* q, float* s);
 
 /* MoE FFN block forward for `tokens` tokens:
- *   n = RMSNorm_ref(x) ; logits = gate_seq(n) (+bias) ; top-k (ref)
+ *   n = RMSNorm_ref(x) ; logits = gate_ref(n) (+bias) ; top-k (ref)
  *   routed/shared expert MLP y = W2 . (silu(W_gate . n) * (W_up . n))
  *   out = bf16( x + y_shared + sum_s w[t][s] * y[t][s] )
  * mode 0 ("q"): mirrors the rounding points of the B200 kernels: n quantised

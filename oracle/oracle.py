@@ -56,7 +56,7 @@ def lib():
         L.orc_rmsnorm_ref.argtypes = [f32p, f32p, f32p, ctypes.c_int, ctypes.c_int, ctypes.c_float]
         L.orc_rms_ref.argtypes = [f32p, f32p, ctypes.c_int, ctypes.c_int, ctypes.c_float]
         L.orc_moe_gate_ref.argtypes = [f32p, f32p, f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int]
-        L.orc_moe_gate_seq.argtypes = [f32p, f32p, f32p, f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+        L.orc_moe_router_logits.argtypes = [f32p, f32p, f32p, f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int]
         L.orc_moe_topk_ref.argtypes = [f32p, i32p, f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int]
         L.orc_moe_permute.restype = ctypes.c_int
         L.orc_moe_permute.argtypes = [i32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
@@ -142,22 +142,18 @@ def rms_ref(x: np.ndarray, eps: float) -> np.ndarray:
     return out
 
 
-def moe_gate_ref(h: np.ndarray, w: np.ndarray) -> np.ndarray:
+def moe_gate_ref(h: np.ndarray, w: np.ndarray, bias=None) -> np.ndarray:
+    """Router logits in the reference's order (csrc/kernels.cu:412-435); with
+    `bias`, the MoE layer's routing bias added to each logit after the tree."""
     h, w = _f32(h), _f32(w)
     T, H = h.shape
     E = w.shape[0]
     out = np.empty((T, E), np.float32)
-    lib().orc_moe_gate_ref(_p(h, f32p), _p(w, f32p), _p(out, f32p), H, E, T)
-    return out
-
-
-def moe_gate_seq(h: np.ndarray, w: np.ndarray, bias=None) -> np.ndarray:
-    h, w = _f32(h), _f32(w)
-    T, H = h.shape
-    E = w.shape[0]
-    out = np.empty((T, E), np.float32)
-    b = _f32(bias) if bias is not None else None
-    lib().orc_moe_gate_seq(_p(h, f32p), _p(w, f32p), _p(b, f32p) if b is not None else None, _p(out, f32p), H, E, T)
+    if bias is None:
+        lib().orc_moe_gate_ref(_p(h, f32p), _p(w, f32p), _p(out, f32p), H, E, T)
+    else:
+        b = _f32(bias)
+        lib().orc_moe_router_logits(_p(h, f32p), _p(w, f32p), _p(b, f32p), _p(out, f32p), H, E, T)
     return out
 
 

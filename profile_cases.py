@@ -1,12 +1,13 @@
-"""Small, self-contained launches of single stages of the MoE FFN block, for
+"""Profiling driver (a tool beside bench.py, not part of the package): small,
+self-contained launches of single stages of the MoE FFN block, for
 timing with CUDA events and for ncu captures that must stay small (a few
 hundred MB on the device, a handful of launches):
 
-    python -m time_b200.profile_cases router [--tokens 4096] [--iters 3]
-    python -m time_b200.profile_cases gemm   [--tokens 4096] [--experts 32] [--iters 3]
-    python -m time_b200.profile_cases attention [--batch 64] [--ctx-min 1024] [--ctx-max 32768] [--iters 3]
-    python -m time_b200.profile_cases attn_block [--batch 64] [--ctx-min 1024] [--ctx-max 32768] [--iters 3]
-    python -m time_b200.profile_cases serving [--batch 64] [--prompt 512] [--steps 10] [--layers 92]
+    python profile_cases.py router [--tokens 4096] [--iters 3]
+    python profile_cases.py gemm   [--tokens 4096] [--experts 32] [--iters 3]
+    python profile_cases.py attention [--batch 64] [--ctx-min 1024] [--ctx-max 32768] [--iters 3]
+    python profile_cases.py attn_block [--batch 64] [--ctx-min 1024] [--ctx-max 32768] [--iters 3]
+    python profile_cases.py serving [--batch 64] [--prompt 512] [--steps 10] [--layers 92]
 
 `router`: RMSNorm+quant (with the fp32 n rows), tiled router logits, top-k
 over T tokens of the GLM shape (hidden 5120, 160 experts; n is 84 MB at 4096
@@ -37,8 +38,13 @@ import json
 
 import torch
 
-from . import synth
-from . import moe as M
+import sys
+from pathlib import Path
+
+sys.path.insert(0, str(Path(__file__).resolve().parent))
+
+from time_b200 import synth          # noqa: E402
+from time_b200 import moe as M       # noqa: E402
 
 
 def _time(fn, iters: int) -> float:
@@ -128,7 +134,7 @@ def proj(iters: int) -> dict:
     (96 + 16) x 128, K = 5120; o_proj: N = 5120, K = 12288) for a few batch
     sizes, on the split-K mma.sync kernel (fp8_gemm_small) and on the tcgen05
     grouped GEMM with one group."""
-    from . import attn as A
+    from time_b200 import attn as A
     dev = torch.device("cuda", 0)
     k = A.lib()
     out = {}
@@ -159,7 +165,7 @@ def proj(iters: int) -> dict:
 def attention(batch: int, ctx_min: int, ctx_max: int, split: int, iters: int, nq: int = 12, nkv: int = 1,
               cpu_sample: int = 0) -> dict:
     import numpy as np
-    from . import attn as A
+    from time_b200 import attn as A
     dev = torch.device("cuda", 0)
     rng = np.random.default_rng(0)
     lens = rng.integers(ctx_min, ctx_max + 1, size=batch)
@@ -225,7 +231,7 @@ def attn_block(batch: int, ctx_min: int, ctx_max: int, iters: int, tp: int = 8, 
     weight slice, its own cache) with the rank-local residual add in place of
     the TP sum (tp_size 1 on this GPU)."""
     import numpy as np
-    from . import attn as A
+    from time_b200 import attn as A
     dev = torch.device("cuda", 0)
     shape = synth.GLM_ATTN
     rng = np.random.default_rng(0)
@@ -284,7 +290,7 @@ def serving(batch: int, prompt: int, steps: int, layers: int, max_seq: int) -> d
 
     import numpy as np
 
-    from . import engine as EN
+    from time_b200 import engine as EN
     shape = dataclasses.replace(synth.GLM_MODEL, num_layers=layers)
     dev = torch.device("cuda:0")
     w = synth.make_model_weights(shape, seed=0, device=dev, share_layers=True)

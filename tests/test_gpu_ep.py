@@ -130,8 +130,9 @@ def ep_emulated(shape, w_all, x, ep, routing=None, placement=None):
         hq = torch.empty(R, I, dtype=torch.uint8, device=dev)
         hs = torch.empty(I // 128, R, device=dev)
         y = torch.empty(R, H, dtype=torch.bfloat16, device=dev)
-        # the layer's GEMM form: the decode form at <= 16 routed tokens per expert over all ranks
-        form = M.GEMM_SMALL_TILES if E > 1 and T * K <= 16 * E else M.GEMM_FULL_TILES
+        # the GEMM form exactly as every rank's layer picks it: from max_tokens x ep_size (the
+        # same on every rank), not from the rank's own token count
+        form = M.GEMM_SMALL_TILES if E > 1 and Tmax * ep * K <= 16 * E else M.GEMM_FULL_TILES
         M.grouped_gemm(M.GEMM_GATED_SWIGLU | form, xp, xps, R, wr["w13"], wr["s13"], counts, start, hq, hs, R, H, I,
                        R, error_word=err)
         M.grouped_gemm(M.GEMM_DOWN_BF16 | form, hq, hs, R, wr["w2"], wr["s2"], counts, start, y, None, 0, I, H, R,
@@ -192,11 +193,15 @@ def test_ep_emulated_all_tokens_one_rank(gpu):
     assert counts[1][:2].tolist() == [T, T] and int(counts[0][:2].sum()) == 0
 
 
-def test_ep_emulated_glm_decode_uniform_logits(gpu):
+@pytest.mark.parametrize("T", [256, 319, 321])
+def test_ep_emulated_glm_decode_uniform_logits(gpu, T):
     """256 decode tokens, EP 8 over the GLM shape, routing
-    from uniform random logits (top-8 softmax of U(0,1) logits)."""
+    from uniform random logits (top-8 softmax of U(0,1) logits).  319 and 321
+    tokens split unevenly over the 8 ranks (40/39 and 41/40 tokens) right at
+    the decode-form threshold (16 routed tokens per expert = 320 tokens): the
+    ranks must all run the form the one-GPU layer runs."""
     shape = synth.GLM
-    T, ep = 256, 8
+    ep = 8
     w = synth.make_moe_weights(shape, seed=0, device=gpu)
     x = synth.make_x(shape, T, seed=2, device=gpu)
     logits = synth.uniform_routing(T, shape.num_experts, shape.top_k, seed=4, device=gpu)

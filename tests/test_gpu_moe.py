@@ -3,7 +3,9 @@ the C-ABI (include/moe_layer.h, cublas_wrappers.h) against the CPU oracle.
 
 Bars (from the north star):
   * integer/byte/index work bit-exact: RMSNorm rms, e4m3 activation bytes and
-    scales, router logits, top-k indices, the expert permutation;
+    scales, router logits in the reference's order (csrc/kernels.cu:412-435:
+    256 lane partials and a pairwise tree, pinned to the reference's own kernel
+    by tests/golden/ref_kernels.npz), top-k indices, the expert permutation;
   * bf16 layer outputs: max|y - y_oracle| / max|y_oracle| <= 1e-2 and
     mean|y - y_oracle| <= 2e-3 against the oracle in "q" mode (the oracle
     mirrors the kernels' e4m3 activation rounding points, accumulates in
@@ -84,15 +86,16 @@ def test_router_topk_bit_exact(gpu, oracle, T, H, E, K, bias):
                                         M.ptr(logits), M.ptr(idx), M.ptr(w), stream()))
     torch.cuda.synchronize()
     n = oracle.rmsnorm_ref(x.float().numpy(), gamma.numpy(), 1e-5)
-    lg = oracle.moe_gate_seq(n, W.numpy(), b.numpy() if b is not None else None)
-    assert np.array_equal(logits.cpu().numpy(), lg)
+    lg = oracle.moe_gate_ref(n, W.numpy(), b.numpy() if b is not None else None)
+    assert np.array_equal(logits.cpu().numpy().view(np.uint32), lg.view(np.uint32))
     oi, ow = oracle.moe_topk_ref(lg, K)
     assert np.array_equal(idx.cpu().numpy(), oi)
     assert np.allclose(w.cpu().numpy(), ow, rtol=2e-6, atol=1e-7)
 
 
 @pytest.mark.parametrize("T,H,E,K,bias", [(5, 256, 8, 2, False), (70, 512, 160, 8, True), (33, 256, 64, 16, False),
-                                          (300, 5120, 160, 8, True), (17, 384, 200, 4, True),
+                                          (300, 5120, 160, 8, True), (17, 384, 200, 4, True), (9, 128, 40, 3, True),
+                                          (45, 640, 100, 5, False), (64, 12288, 160, 8, True),
                                           (1000, 512, 160, 8, True), (512, 5120, 160, 8, True),
                                           (4096, 1024, 160, 8, True),
                                           (4096, 5120, 200, 8, False)])
@@ -127,7 +130,7 @@ def test_tiled_router_bit_exact(gpu, oracle, T, H, E, K, bias):
     torch.cuda.synchronize()
     nref = oracle.rmsnorm_ref(x.float().numpy(), gamma.numpy(), 1e-5)
     assert np.array_equal(n.cpu().numpy().view(np.uint32), nref.view(np.uint32))
-    lg = oracle.moe_gate_seq(nref, W.numpy(), b.numpy() if b is not None else None)
+    lg = oracle.moe_gate_ref(nref, W.numpy(), b.numpy() if b is not None else None)
     assert np.array_equal(logits.cpu().numpy().view(np.uint32), lg.view(np.uint32))
     assert np.array_equal(logits.cpu().numpy().view(np.uint32), logits2.cpu().numpy().view(np.uint32))
     oi, ow = oracle.moe_topk_ref(lg, K)
@@ -135,6 +138,55 @@ def test_tiled_router_bit_exact(gpu, oracle, T, H, E, K, bias):
     assert np.array_equal(idx.cpu().numpy(), idx2.cpu().numpy())
     assert np.array_equal(w.cpu().numpy().view(np.uint32), w2.cpu().numpy().view(np.uint32))
     assert np.allclose(w.cpu().numpy(), ow, rtol=2e-6, atol=1e-7)
+
+
+def _router_logits_gpu(k, n, W, b, gpu):
+    T, H = n.shape
+    E = W.shape[0]
+    nd, Wd = torch.from_numpy(np.ascontiguousarray(n)).to(gpu), torch.from_numpy(np.ascontiguousarray(W)).to(gpu)
+    bd = torch.from_numpy(b).to(gpu) if b is not None else None
+    logits = torch.empty(T, E, device=gpu)
+    M.check("router_logits", k.moe_router_logits(M.ptr(nd), M.ptr(Wd), M.ptr(bd), T, H, E, M.ptr(logits), stream()))
+    torch.cuda.synchronize()
+    return logits.cpu().numpy()
+
+
+@pytest.mark.parametrize("H,E", [(512, 64), (5120, 160)])
+def test_router_logits_match_reference_kernel_golden(gpu, H, E):
+    """The layer's router kernel on the inputs of the reference's own
+    kernel_moe_gate run (tests/golden/ref_kernels.npz): identical bits."""
+    from pathlib import Path
+    fix = Path(__file__).resolve().parent / "golden" / "ref_kernels.npz"
+    g = np.load(fix)
+    k = M.libs()["libkernels.so"]
+    got = _router_logits_gpu(k, g[f"gate_x_{H}_{E}"], g[f"gate_w_{H}_{E}"], None, gpu)
+    assert np.array_equal(got.view(np.uint32), g[f"gate_out_{H}_{E}"].view(np.uint32))
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2, 3, 4])
+def test_router_glm_shape_reference_order_every_token(gpu, oracle, seed):
+    """BASELINE configs[1] router: 4096 tokens x 5120 x 160 experts with the
+    zipf routing bias.  Every logit bit-identical to the reference-order
+    oracle, and every token's top-8 index list equal to the reference's top-k
+    of those logits."""
+    shape = synth.GLM
+    k = M.libs()["libkernels.so"]
+    T, H, E, K = 4096, shape.hidden, shape.num_experts, shape.top_k
+    w = synth.make_moe_weights(shape, seed=seed, device="cpu", zipf_bias=True, experts=False)
+    x = synth.make_x(shape, T, seed=seed + 1, device="cpu")
+    n = oracle.rmsnorm_ref(x.float().numpy(), w["gamma"].numpy(), shape.eps)
+    Wr, b = w["router_w"].numpy(), w["router_bias"].numpy()
+    got = _router_logits_gpu(k, n, Wr, b, gpu)
+    lg = oracle.moe_gate_ref(n, Wr, b)
+    assert np.array_equal(got.view(np.uint32), lg.view(np.uint32))
+    ld = torch.from_numpy(got).to(gpu)
+    idx = torch.empty(T, K, dtype=torch.int32, device=gpu)
+    wts = torch.empty(T, K, device=gpu)
+    M.check("topk_softmax", k.moe_topk_softmax(M.ptr(ld), T, E, K, M.ptr(idx), M.ptr(wts), stream()))
+    torch.cuda.synchronize()
+    oi, ow = oracle.moe_topk_ref(lg, K)
+    assert np.array_equal(idx.cpu().numpy(), oi)
+    assert np.allclose(wts.cpu().numpy(), ow, rtol=2e-6, atol=1e-7)
 
 
 @pytest.mark.parametrize("T,K,E,shared", [(1, 1, 4, 1), (37, 4, 9, 1), (4096, 8, 160, 1), (300, 2, 8, 0),
@@ -406,6 +458,65 @@ def test_grouped_gemm_small_tiles(gpu, gated, counts):
     print(f"small vs full tiles ({'gated' if gated else 'down'}, counts {counts}): bit-identical {same}")
 
 
+@pytest.mark.parametrize("gated", [False, True])
+def test_grouped_gemm_small_tiles_placement_independent(gpu, gated):
+    """The decode form's result for a row does not depend on where its tile
+    runs: the same expert groups, run (a) twice and (b) after two extra
+    leading groups that shift every tile to other CTAs and other positions in
+    each CTA's K-block sequence, give bit-identical outputs."""
+    K, N = 640, 256
+    Nw = 2 * N if gated else N
+    counts = [1, 7, 33, 64, 64, 20, 0, 31]
+    pre = [45, 200]
+    g = torch.Generator().manual_seed(77 + gated)
+    starts, rows, A, A_s, a_ld, W, W_s = _make_groups(counts, K, Nw, g)
+    p_starts, p_rows, pA, pA_s, p_ld, pW, pW_s = _make_groups(pre, K, Nw, g)
+    p_used = p_starts[-1] + (pre[-1] + 15) // 16 * 16          # rows the prefix groups occupy
+    A2 = torch.cat([pA[:p_used], A])
+    rows2 = A2.shape[0]
+    a_ld2 = (rows2 + 3) // 4 * 4
+    A_s2 = torch.zeros(K // 128, a_ld2)
+    A_s2[:, :p_used] = pA_s[:, :p_used]
+    A_s2[:, p_used:p_used + rows] = A_s[:, :rows]
+    W2, W_s2 = torch.cat([pW, W]), torch.cat([pW_s, W_s])
+    starts2 = p_starts + [p_used + s_ for s_ in starts]
+    counts2 = pre + counts
+
+    def run(A_, A_s_, ld_, W_, W_s_, starts_, counts_, rows_):
+        err = torch.zeros(1, dtype=torch.int32, device=gpu)
+        cnt = torch.tensor(counts_, dtype=torch.int32, device=gpu)
+        st = torch.tensor(starts_, dtype=torch.int32, device=gpu)
+        form = M.GEMM_SMALL_TILES
+        if gated:
+            hq = torch.zeros((rows_, N), dtype=torch.uint8, device=gpu)
+            hs = torch.zeros((N // 128, ld_), device=gpu)
+            M.grouped_gemm(M.GEMM_GATED_SWIGLU | form, A_.to(gpu), A_s_.to(gpu), ld_, W_.to(gpu), W_s_.to(gpu), cnt,
+                           st, hq, hs, ld_, K, N, rows_, error_word=err)
+            torch.cuda.synchronize()
+            assert err.item() == 0
+            return hq.cpu(), hs.cpu()
+        out = torch.zeros((rows_, N), dtype=torch.bfloat16, device=gpu)
+        M.grouped_gemm(M.GEMM_DOWN_BF16 | form, A_.to(gpu), A_s_.to(gpu), ld_, W_.to(gpu), W_s_.to(gpu), cnt, st,
+                       out, None, 0, K, N, rows_, error_word=err)
+        torch.cuda.synchronize()
+        assert err.item() == 0
+        return (out.cpu(),)
+
+    first = run(A, A_s, a_ld, W, W_s, starts, counts, rows)
+    again = run(A, A_s, a_ld, W, W_s, starts, counts, rows)
+    shifted = run(A2, A_s2, a_ld2, W2, W_s2, starts2, counts2, rows2)
+    for gi, c in enumerate(counts):
+        s0, s1 = starts[gi], starts2[len(pre) + gi]
+        if gated:
+            for a_, b_ in ((first, again), (first, shifted)):
+                off = 0 if b_ is again else s1 - s0
+                assert torch.equal(a_[0][s0:s0 + c], b_[0][s0 + off:s0 + off + c]), gi
+                assert torch.equal(a_[1][:, s0:s0 + c], b_[1][:, s0 + off:s0 + off + c]), gi
+        else:
+            assert torch.equal(first[0][s0:s0 + c].view(torch.int16), again[0][s0:s0 + c].view(torch.int16)), gi
+            assert torch.equal(first[0][s0:s0 + c].view(torch.int16), shifted[0][s1:s1 + c].view(torch.int16)), gi
+
+
 # ---------------------------------------------------------------- full layer
 
 def _run_layer(shape, case, T, dev, routing=None):
@@ -432,10 +543,13 @@ def test_layer_tiny_config(gpu, oracle, T):
     y = out.float().cpu().numpy().astype(np.float64)
     mr, mae = oracle.max_rel_and_mae(y, oracle.bf16_bits_to_f32(ref))
     assert mr <= MAX_REL and mae <= MAE, (mr, mae)
-    # the fp32-activation ("ref") result is reported, not gated: e4m3 activations cost a few percent
-    refm, *_ = oracle.moe_ffn_forward(ow, bits(case["x"]), mode=1)
-    mr1, _ = oracle.max_rel_and_mae(y, oracle.bf16_bits_to_f32(refm))
-    assert mr1 < 0.1
+    # against the reference's semantics (fp32 activations, oracle "ref" mode): at this
+    # configuration the e4m3 activations stay within the north-star bar as well
+    refm, ridx, *_ = oracle.moe_ffn_forward(ow, bits(case["x"]), mode=1)
+    assert np.array_equal(idx.cpu().numpy(), ridx)
+    mr1, mae1 = oracle.max_rel_and_mae(y, oracle.bf16_bits_to_f32(refm))
+    print(f"tiny T={T}: vs q mode {mr:.2e}/{mae:.2e}, vs ref mode (fp32 activations) {mr1:.2e}/{mae1:.2e}")
+    assert mr1 <= MAX_REL and mae1 <= MAE, (mr1, mae1)
 
 
 def test_layer_zipf_bias_and_routed_entry(gpu, oracle):
@@ -482,8 +596,17 @@ def test_layer_deterministic(gpu):
 def test_layer_glm_shape_sampled_tokens(gpu, oracle):
     """BASELINE configs[1] at full size (hidden 5120, 160 experts top-8 + shared,
     intermediate 1536, 4096 tokens, zipf-skewed router): the whole layer runs
-    on the GPU; the oracle recomputes 24 sampled tokens (tokens are independent
-    given the weights), and routing is checked bit-exact for all tokens."""
+    on the GPU; the oracle recomputes 256 sampled tokens (tokens are independent
+    given the weights), and routing is checked bit-exact for all tokens.
+
+    Against the oracle's e4m3-activation mirror ("q" mode) the outputs meet the
+    north-star bar.  Against the reference's semantics (fp32 activations, "ref"
+    mode) they do not: the e4m3 activations the north star specifies (1x128
+    scales, 3 mantissa bits) round each activation by up to 6.25 % (about
+    3.6 % RMS), and at this shape the MoE output differs from the
+    fp32-activation one by max-rel ~3e-2 and MAE ~4e-2 (measured on the CPU
+    oracle: q vs ref on 64 tokens, 3.2e-2 / 4.0e-2).  That gap is asserted to
+    stay at its measured size (bound 5e-2 / 5e-2), and printed."""
     shape = synth.GLM
     T = 4096
     w = synth.make_moe_weights(shape, seed=0, device=gpu, zipf_bias=True)
@@ -497,10 +620,10 @@ def test_layer_glm_shape_sampled_tokens(gpu, oracle):
     assert counts[shape.num_experts].item() == T
     xf = x.float().cpu().numpy()
     n = oracle.rmsnorm_ref(xf, w["gamma"].cpu().numpy(), shape.eps)
-    lg = oracle.moe_gate_seq(n, w["router_w"].cpu().numpy(), w["router_bias"].cpu().numpy())
+    lg = oracle.moe_gate_ref(n, w["router_w"].cpu().numpy(), w["router_bias"].cpu().numpy())
     oi, _ = oracle.moe_topk_ref(lg, shape.top_k)
     assert np.array_equal(idx.cpu().numpy(), oi)
-    sample = np.random.default_rng(0).choice(T, 24, replace=False)
+    sample = np.random.default_rng(0).choice(T, 256, replace=False)
     case = {k_: v for k_, v in w.items()}
     ow = oracle.OracleWeights(shape, case)
     xs = bits(x.cpu()[sample])
@@ -508,3 +631,8 @@ def test_layer_glm_shape_sampled_tokens(gpu, oracle):
     y = out.cpu()[sample].float().numpy()
     mr, mae = oracle.max_rel_and_mae(y, oracle.bf16_bits_to_f32(ref))
     assert mr <= MAX_REL and mae <= MAE, (mr, mae)
+    refm, *_ = oracle.moe_ffn_forward(ow, xs, mode=1)
+    mr1, mae1 = oracle.max_rel_and_mae(y, oracle.bf16_bits_to_f32(refm))
+    print(f"GLM 256 sampled tokens: vs q mode {mr:.2e}/{mae:.2e}, vs ref mode (fp32 activations) "
+          f"{mr1:.2e}/{mae1:.2e}")
+    assert mr1 <= 5e-2 and mae1 <= 5e-2, (mr1, mae1)

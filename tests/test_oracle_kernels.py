@@ -34,17 +34,42 @@ def test_rmsnorm_tree_order_is_not_sequential(oracle):
     assert np.allclose(rms, emu, rtol=3e-7)
 
 
-def test_gate_orders_agree(oracle):
+def _fma_f32(a: float, b: float, c: float) -> float:
+    """fp32 fma with one rounding: the exact a*b + c (as a fraction), rounded
+    to the nearest fp32 (ties to even)."""
+    from fractions import Fraction
+    exact = Fraction(a) * Fraction(b) + Fraction(c)
+    lo = np.float32(float(exact))              # within one fp32 ulp of exact
+    cands = [np.nextafter(lo, np.float32(-np.inf)), lo, np.nextafter(lo, np.float32(np.inf))]
+    best = min(cands, key=lambda v: (abs(Fraction(float(v)) - exact), int(np.array(v).view(np.uint32)) & 1))
+    return float(best)
+
+
+def test_router_logits_tree_restated_in_python(oracle):
+    """moe_gate_ref against a pure-Python restatement of kernel_moe_gate
+    (csrc/kernels.cu:412-435, blockDim 256): 256 fma chains, then the pairwise
+    tree with fp32 adds; and the bias is one fp32 add after the tree."""
     rng = np.random.default_rng(2)
-    h = rng.normal(0, 1, (9, 512)).astype(np.float32)
-    w = rng.normal(0, 0.02, (12, 512)).astype(np.float32)
-    ref = oracle.moe_gate_ref(h, w)
-    seq = oracle.moe_gate_seq(h, w)
-    exact = h.astype(np.float64) @ w.astype(np.float64).T
-    assert np.allclose(ref, exact, rtol=1e-5, atol=1e-6)
-    assert np.allclose(seq, exact, rtol=1e-5, atol=1e-6)
-    b = rng.normal(0, 1, 12).astype(np.float32)
-    assert np.array_equal(oracle.moe_gate_seq(h, w, b), (seq + b).astype(np.float32))
+    H = 640                                  # not a multiple of 256: chains of 3 and 2 steps
+    h = (rng.normal(0, 1, (3, H)) * np.exp(rng.normal(0, 2, (3, 1)))).astype(np.float32)
+    w = rng.normal(0, 0.02, (4, H)).astype(np.float32)
+    got = oracle.moe_gate_ref(h, w)
+    for t in range(3):
+        for e in range(4):
+            p = []
+            for lane in range(256):
+                acc = 0.0
+                for i in range(lane, H, 256):
+                    acc = _fma_f32(float(h[t, i]), float(w[e, i]), acc)
+                p.append(np.float32(acc))
+            stride = 128
+            while stride:
+                for lane in range(stride):
+                    p[lane] = np.float32(p[lane] + p[lane + stride])
+                stride //= 2
+            assert np.float32(p[0]).view(np.uint32) == got[t, e].view(np.uint32), (t, e)
+    b = rng.normal(0, 1, 4).astype(np.float32)
+    assert np.array_equal(oracle.moe_gate_ref(h, w, b).view(np.uint32), (got + b).astype(np.float32).view(np.uint32))
 
 
 def _topk_insertion_py(row, k):
@@ -137,7 +162,7 @@ def _numpy_moe(case, shape, mode):
     n32 = None
     from oracle import oracle as orc
     n32 = orc.rmsnorm_ref(case["x"].float().numpy(), case["gamma"].numpy(), shape.eps)
-    logits = orc.moe_gate_seq(n32, case["router_w"].numpy(),
+    logits = orc.moe_gate_ref(n32, case["router_w"].numpy(),
                               case["router_bias"].numpy() if case["router_bias"] is not None else None)
     idx, wts = orc.moe_topk_ref(logits, k)
     lut = np.arange(256, dtype=np.uint8).view(ml_dtypes.float8_e4m3fn).astype(np.float64)

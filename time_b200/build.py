@@ -102,6 +102,18 @@ def build(force: bool = False, verbose: bool = False) -> None:
             print(f"linked {name}")
 
 
+def reference_dir() -> Path | None:
+    """The reference checkout whose own kernels oracle/_ref/ is built from: the
+    REF_DIR environment variable, else a `reference` directory beside this
+    repository's directory; None when neither exists (the GPU box has no
+    reference sources and uses the prebuilt oracle/_ref/)."""
+    env = os.environ.get("REF_DIR")
+    if env:
+        return Path(env)
+    sibling = PKG.parent.parent / "reference"
+    return sibling if sibling.is_dir() else None
+
+
 def build_oracle(verbose: bool = False) -> None:
     """Build the CPU oracle (test infrastructure) and, when the reference
     sources are present, the reference's own kernels into oracle/_ref/."""
@@ -109,8 +121,8 @@ def build_oracle(verbose: bool = False) -> None:
     r = subprocess.run(["make", "-C", str(odir)], capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"oracle build failed:\n{r.stdout}\n{r.stderr}")
-    ref = Path(os.environ.get("REF_DIR", "/root/reference"))
-    if (ref / "csrc" / "kernels.cu").exists():
+    ref = reference_dir()
+    if ref is not None and (ref / "csrc" / "kernels.cu").exists():
         r = subprocess.run(["make", "-C", str(odir), "ref", f"REF_DIR={ref}"], capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"reference kernel build failed:\n{r.stdout}\n{r.stderr}")

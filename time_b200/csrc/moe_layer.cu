@@ -74,6 +74,7 @@ struct moe_layer {
     tbep::Peers peers;
     uint32_t epoch;
     size_t off_plan;
+    int gemm_form;        // 0 = by the rule in gemm_form(), else a CBW_GEMM_*_TILES flag
 };
 
 namespace {
@@ -150,14 +151,19 @@ moe_status_t cbw_to_moe(cbwStatus_t s) {
 moe_status_t nccl_to_moe(ncwResult_t r) { return r == NCW_SUCCESS ? MOE_OK : MOE_ERR_NCCL; }
 
 // The grouped GEMM's decode form (32-row tiles whose K blocks the promotion
-// groups share) when the call averages at most 16 routed tokens per expert
-// over all ranks (T x ep_size x top_k <= 16 x E): the same choice on every
-// rank of an expert-parallel call, so its rows match the one-GPU layer bit for
-// bit.  One expert (a dense FFN as one group) always takes the full form.
+// groups share) when a call averages at most 16 routed tokens per expert over
+// all ranks (tokens x top_k <= 16 x E).  The two forms add a row's K blocks in
+// different orders, so every rank of an expert-parallel call must make the
+// same choice: with ep_size > 1 the rule counts max_tokens x ep_size tokens
+// (max_tokens is the same on every rank), never the rank's own token count,
+// which differs between ranks when the tokens do not split evenly.  A single
+// GPU counts the call's tokens.  moe_layer_set_gemm_form overrides the rule.
+// One expert (a dense FFN as one group) always takes the full form.
 int gemm_form(const moe_layer* L, int T) {
+    if (L->gemm_form) return L->gemm_form;
     const moe_layer_config_t& c = L->cfg;
-    const bool small = c.num_experts > 1 &&
-                       static_cast<long long>(T) * c.ep_size * c.top_k <= 16ll * c.num_experts;
+    const long long tokens = c.ep_size > 1 ? static_cast<long long>(c.max_tokens) * c.ep_size : T;
+    const bool small = c.num_experts > 1 && tokens * c.top_k <= 16ll * c.num_experts;
     return small ? CBW_GEMM_SMALL_TILES : CBW_GEMM_FULL_TILES;
 }
 
@@ -458,6 +464,13 @@ moe_status_t moe_layer_set_stage_events(moe_layer_t* L, cwEvent_t* events) {
     L->timing = events != nullptr;
     for (int i = 0; i <= MOE_NUM_STAGES; ++i)
         L->stage_ev[i] = events ? static_cast<cudaEvent_t>(events[i]) : nullptr;
+    return MOE_OK;
+}
+
+moe_status_t moe_layer_set_gemm_form(moe_layer_t* L, int form) {
+    if (!L) return MOE_ERR_INVALID_ARGUMENT;
+    if (form != 0 && form != CBW_GEMM_SMALL_TILES && form != CBW_GEMM_FULL_TILES) return MOE_ERR_INVALID_ARGUMENT;
+    L->gemm_form = form;
     return MOE_OK;
 }
 

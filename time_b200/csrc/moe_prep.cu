@@ -2,8 +2,10 @@
 // RMSNorm + FP8 quantisation, fp32 router + top-k, stable expert permutation,
 // row gather and the weighted combine.  C-ABI entry points are declared in
 // include/moe_layer.h.
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
+#include <cooperative_groups.h>
 #include <cfloat>
 #include <cstdint>
 #include <mutex>
@@ -223,13 +225,45 @@ __device__ __forceinline__ void topk_row(const float* row, int E, int K, int lan
 }
 
 // ---------------------------------------------------------------- router
-// Block: 32 tokens x all experts (E <= 32*EPT).  256 threads: thread
-// (tg = tid & 7, eg = tid >> 3) owns tokens 4tg..4tg+3 and experts
-// eg*EPT..eg*EPT+EPT-1.  Logits accumulate with one fma per k in ascending k
-// from +0.0f -- the order the router's parity is defined in.
-constexpr int kRouterTok = 32;
-constexpr int kRouterKC = 32;
+// Router logits in the reference's order (csrc/kernels.cu:412-435, launched
+// with blockDim 256): for each (t, e) the 256 lane partials
+//   p[l] = fma chain over i = l, l + 256, l + 512, ... < H  (ascending i, from +0.0f)
+// are reduced by the pairwise tree p[l] += p[l + s] for s = 128, 64, ..., 1;
+// the routing bias, when given, is added to the tree's result.  The lane
+// index is split as l = 32m + 4q + r (m: bits 7..5, q: bits 4..2, r: bits
+// 1..0), so the tree's levels are, in order: m bit 2, 1, 0 (s = 128, 64, 32),
+// q bit 2, 1, 0 (s = 16, 8, 4), r bit 1, 0 (s = 2, 1).
 
+// One warp, one (t, e): lane owns l = lane + 32m; levels s = 128, 64, 32 are
+// lane-local, s = 16..1 shuffles (each add pairs the same operands as the
+// reference's tree).  Used by the one-call router below.
+__device__ __forceinline__ float warp_logit_ref_order(const float* __restrict__ a, const float* __restrict__ b,
+                                                      int H, int lane) {
+    float p[8];
+#pragma unroll
+    for (int m = 0; m < 8; ++m) p[m] = 0.0f;
+    for (int j = 0; j < H; j += 256) {
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+            const int i = j + 32 * m + lane;
+            if (i < H) p[m] = __fmaf_rn(a[i], b[i], p[m]);
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < 4; ++m) p[m] = __fadd_rn(p[m], p[m + 4]);
+#pragma unroll
+    for (int m = 0; m < 2; ++m) p[m] = __fadd_rn(p[m], p[m + 2]);
+    float s = __fadd_rn(p[0], p[1]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_down_sync(0xffffffffu, s, o));
+    return __shfl_sync(0xffffffffu, s, 0);
+}
+
+// One block per token: n = (x / rms) * gamma into shared memory (the same
+// fp32 operations as the RMSNorm kernels), one warp per expert logit in the
+// reference order, then the top-k of the row.  The one-call router
+// (moe_router_topk): a reference point for tests and small callers, not the
+// layer's throughput path.
 template <int EPT>
 __global__ void __launch_bounds__(256)
 router_topk_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ rms,
@@ -237,174 +271,226 @@ router_topk_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict_
                    const float* __restrict__ bias, int T, int H, int E, int K,
                    float* __restrict__ logits_out, int32_t* __restrict__ topk_idx,
                    float* __restrict__ topk_w) {
-    constexpr int EMAX = 32 * EPT;
-    // the K-loop tiles and the logits table are never live at the same time
-    struct Tiles {
-        float n[kRouterKC][kRouterTok];
-        float w[kRouterKC][EMAX + 4];
-    };
-    constexpr int kBytes = sizeof(Tiles) > sizeof(float) * kRouterTok * (EMAX + 1)
-                               ? sizeof(Tiles) : sizeof(float) * kRouterTok * (EMAX + 1);
-    __shared__ __align__(16) uint8_t buf[kBytes];
-    __shared__ float rms_s[kRouterTok];
-    auto& n_s = reinterpret_cast<Tiles*>(buf)->n;
-    auto& w_s = reinterpret_cast<Tiles*>(buf)->w;
-    auto lg_s = reinterpret_cast<float (*)[EMAX + 1]>(buf);
-
-    const int tid = threadIdx.x;
-    const int t0 = blockIdx.x * kRouterTok;
-    const int tg = tid & 7, eg = tid >> 3;
-    if (tid < kRouterTok) rms_s[tid] = (t0 + tid < T) ? rms[t0 + tid] : 1.0f;
-
-    float acc[4][EPT];
-#pragma unroll
-    for (int a = 0; a < 4; ++a)
-#pragma unroll
-        for (int e = 0; e < EPT; ++e) acc[a][e] = 0.0f;
-
-    for (int k0 = 0; k0 < H; k0 += kRouterKC) {
-        __syncthreads();
-        // n tile: 32 tokens x 32 k, transposed into n_s[k][t]
-        for (int i = tid; i < kRouterTok * kRouterKC; i += 256) {
-            const int t = i / kRouterKC, kk = i % kRouterKC;
-            float v = 0.0f;
-            if (t0 + t < T) {
-                const float xv = __bfloat162float(x[static_cast<size_t>(t0 + t) * H + k0 + kk]);
-                v = __fmul_rn(__fdiv_rn(xv, rms_s[t]), gamma[k0 + kk]);
-            }
-            n_s[kk][t] = v;
-        }
-        // W tile: E experts x 32 k, transposed into w_s[k][e]
-        for (int i = tid; i < EMAX * kRouterKC; i += 256) {
-            const int e = i / kRouterKC, kk = i % kRouterKC;
-            w_s[kk][e] = (e < E) ? W[static_cast<size_t>(e) * H + k0 + kk] : 0.0f;
-        }
-        __syncthreads();
-#pragma unroll 4
-        for (int kk = 0; kk < kRouterKC; ++kk) {
-            const float4 nv = *reinterpret_cast<const float4*>(&n_s[kk][tg * 4]);
-            float wv[EPT];
-#pragma unroll
-            for (int e = 0; e < EPT; ++e) wv[e] = w_s[kk][eg * EPT + e];
-#pragma unroll
-            for (int e = 0; e < EPT; ++e) {
-                acc[0][e] = __fmaf_rn(nv.x, wv[e], acc[0][e]);
-                acc[1][e] = __fmaf_rn(nv.y, wv[e], acc[1][e]);
-                acc[2][e] = __fmaf_rn(nv.z, wv[e], acc[2][e]);
-                acc[3][e] = __fmaf_rn(nv.w, wv[e], acc[3][e]);
-            }
-        }
+    extern __shared__ __align__(16) float rt_smem[];
+    float* n_s = rt_smem;          // [H]
+    float* lg_s = rt_smem + H;     // [E]
+    const int t = blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float r = rms[t];
+    for (int i = threadIdx.x; i < H; i += blockDim.x)
+        n_s[i] = __fmul_rn(__fdiv_rn(__bfloat162float(x[static_cast<size_t>(t) * H + i]), r), gamma[i]);
+    __syncthreads();
+    for (int e = warp; e < E; e += 8) {
+        float v = warp_logit_ref_order(n_s, W + static_cast<size_t>(e) * H, H, lane);
+        if (bias) v = __fadd_rn(v, bias[e]);
+        if (lane == 0) lg_s[e] = v;
     }
     __syncthreads();
-#pragma unroll
-    for (int a = 0; a < 4; ++a)
-#pragma unroll
-        for (int e = 0; e < EPT; ++e) {
-            const int ee = eg * EPT + e;
-            if (ee < E) lg_s[tg * 4 + a][ee] = bias ? __fadd_rn(acc[a][e], bias[ee]) : acc[a][e];
-        }
-    __syncthreads();
-
-    // top-k: one warp per token, 4 tokens per warp
-    const int warp = tid >> 5, lane = tid & 31;
-    for (int tl = warp; tl < kRouterTok; tl += 8) {
-        const int t = t0 + tl;
-        if (t >= T) break;
+    if (warp == 0) {
         if (logits_out)
-            for (int e = lane; e < E; e += 32) logits_out[static_cast<size_t>(t) * E + e] = lg_s[tl][e];
-        topk_row<EPT>(lg_s[tl], E, K, lane, topk_idx + static_cast<size_t>(t) * K, topk_w + static_cast<size_t>(t) * K);
+            for (int e = lane; e < E; e += 32) logits_out[static_cast<size_t>(t) * E + e] = lg_s[e];
+        topk_row<EPT>(lg_s, E, K, lane, topk_idx + static_cast<size_t>(t) * K, topk_w + static_cast<size_t>(t) * K);
     }
 }
 
 // ---------------------------------------------------------------- tiled router
-// logits[t][e] = (fma chain over k = 0..H-1 of n[t][k] * W[e][k], from +0.0f)
-// + bias[e]: the same per-(t, e) order as router_topk_kernel, laid out for
-// throughput instead of one block per 32 tokens.
-// Scalar-FMA form of the same chains (what moe_router_logits runs): thread
-// tile TI tokens x 4 experts, so one 16-byte load of a token row (four k
-// steps) and of an expert row feed 4*TI FMAs each -- about 1.1 instructions
-// per FMA, against ~2.4 for the packed form whose operand pairs cost register
-// moves.  Block: 128 threads, 16*TI tokens x 32 experts; thread
-// (tg = (lane & 3) + 4 * warp, eg = lane >> 2) owns tokens tg + 16 i and
-// experts eg + 8 j, so the 4 token rows and 8 expert rows a warp reads per
-// load sit in distinct banks (row pitch 68 floats: row r at bank 4r).  K in
-// chunks of 64 through a cp.async double buffer.  Each chain still advances
-// one fma per k in ascending k from +0.0f: bit-identical logits.
-constexpr int kR3Exp = 32, kR3KC = 64, kR3Ld = kR3KC + 4, kR3Threads = 128;
+// The layer's router.  A cluster of 4 CTAs computes one 32-token x 32-expert
+// tile; CTA k of the cluster takes the lanes with q in {2k, 2k + 1} (warps
+// 0-3: q = 2k, warps 4-7: q = 2k + 1), so every row it stages is one 32-byte
+// piece (l = 32m + 8k .. +7) per 256-element step j.  A thread owns 2 tokens
+// x 4 experts and, for its q, the four chains r = 0..3 of each pair: one
+// 16-byte shared-memory load per operand row feeds two fp32x2 FMAs per pair.
+// The chains of one m run over all j (ascending, across as many staged chunks
+// of <= 20 steps as H needs); the 8 m values are processed in the tree's
+// post-order 0, 4, 2, 6, 1, 5, 3, 7 and folded with a 3-deep stack, which
+// forms exactly the levels s = 128, 64, 32.  Each CTA then leaves its 2 x 4
+// sub-sums per pair in shared memory; after a cluster barrier CTA k reduces
+// the pairs [256k, 256k + 256) of the tile over the four CTAs (distributed
+// shared memory) with the levels s = 16, 8, 4, 2, 1, adds the bias and
+// writes the logit.  Operands go through a two-stage cp.async ring with a row
+// pitch of 32*jc + 16 bytes, which puts 8 consecutive rows in 8 distinct
+// 16-byte bank groups (conflict-free loads).
+constexpr int kRtTok = 32, kRtExp = 32, kRtRows = kRtTok + kRtExp;
+constexpr int kRtThreads = 256;
+constexpr int kRtMaxJc = 20;           // 256-element steps per staged chunk
+constexpr int kRtCluster = 4;
 
-template <int TI>
-constexpr size_t r3_smem_bytes() { return 2 * static_cast<size_t>(16 * TI + kR3Exp) * kR3Ld * sizeof(float); }
+__host__ __device__ constexpr int rt_pitch(int jc) { return 32 * jc + 16; }
+__host__ __device__ constexpr int rt_steps(int H, int m) { return H > 32 * m ? (H - 32 * m + 255) / 256 : 0; }
+inline size_t rt_smem_bytes(int jc) {
+    const size_t ring = 2 * static_cast<size_t>(kRtRows) * rt_pitch(jc);
+    const size_t red = static_cast<size_t>(kRtTok) * kRtExp * 8 * sizeof(float);
+    return ring > red ? ring : red;
+}
 
-template <int TI>
-__global__ void __launch_bounds__(kR3Threads, 4)
-router_logits_tile_kernel(const float* __restrict__ n, const float* __restrict__ W, const float* __restrict__ bias,
-                          int T, int H, int E, float* __restrict__ logits) {
-    constexpr int TT = 16 * TI;
-    extern __shared__ __align__(16) float r3_smem[];
-    auto n_s = reinterpret_cast<float (*)[TT][kR3Ld]>(r3_smem);                          // [2][TT][68]
-    auto w_s = reinterpret_cast<float (*)[kR3Exp][kR3Ld]>(r3_smem + 2 * TT * kR3Ld);   // [2][32][68]
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int tg = (lane & 3) + 4 * warp, eg = lane >> 2;
-    const int t0 = blockIdx.y * TT, e0 = blockIdx.x * kR3Exp;
+__device__ __forceinline__ float4 f4_add(float4 a, float4 b) {
+    return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
+}
 
-    auto load = [&](int stage, int k0) {
-        for (int c = tid; c < (TT + kR3Exp) * (kR3KC / 4); c += kR3Threads) {
-            const int row = c >> 4, q = c & 15;
-            if (row < TT) {
+__global__ void __cluster_dims__(kRtCluster, 1, 1) __launch_bounds__(kRtThreads, 1)
+router_logits_ref_kernel(const float* __restrict__ n, const float* __restrict__ W, const float* __restrict__ bias,
+                         int T, int H, int E, int jc, float* __restrict__ logits) {
+    namespace cg = cooperative_groups;
+    extern __shared__ __align__(16) uint8_t rt_ring[];
+    cg::cluster_group cluster = cg::this_cluster();
+    const int k = static_cast<int>(cluster.block_rank());
+    const int t0 = (blockIdx.x / kRtCluster) * kRtTok, e0 = blockIdx.y * kRtExp;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int h = warp >> 2;                       // q = 2k + h
+    const int wt = (warp >> 1) & 1, we = warp & 1;
+    const int tg = lane & 7, eg = lane >> 3;
+    const int pitch = rt_pitch(jc);
+    // rows: tokens 16wt + tg, +8; experts 16we + eg + 4i (i = 0..3)
+    const int tr0 = 16 * wt + tg;
+    const int er0 = kRtTok + 16 * we + eg;
+
+    // the stage list: m in the tree's post-order (order index mi -> m is the
+    // 3-bit reversal of mi: 0, 4, 2, 6, 1, 5, 3, 7), each m in chunks of <= jc
+    // steps; an m without steps (H < 256) keeps one empty stage so that its
+    // +0.0f chains are folded like the reference adds its empty partials
+    auto m_of = [](int mi) { return ((mi & 1) << 2) | (mi & 2) | (mi >> 2); };
+    auto chunks_of = [&](int m) { const int J = rt_steps(H, m); return J == 0 ? 1 : (J + jc - 1) / jc; };
+    int nstages = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) nstages += chunks_of(m_of(i));
+
+    // stage s -> (order index mi, first step j0, steps jn)
+    auto stage_at = [&](int s, int& mi, int& j0, int& jn) {
+        mi = 0;
+        int c = chunks_of(m_of(0));
+        while (s >= c) { s -= c; ++mi; c = chunks_of(m_of(mi)); }
+        j0 = s * jc;
+        const int J = rt_steps(H, m_of(mi));
+        jn = J - j0 < jc ? J - j0 : jc;
+    };
+    auto load_stage = [&](int s, int buf) {
+        int mi, j0, jn;
+        stage_at(s, mi, j0, jn);
+        const int m = m_of(mi);
+        uint8_t* base = rt_ring + static_cast<size_t>(buf) * kRtRows * pitch;
+        const int per_row = 2 * jn;
+        for (int c = tid; c < kRtRows * per_row; c += kRtThreads) {
+            const int row = c / per_row, rem = c - row * per_row;
+            const int j = rem >> 1, hh = rem & 1;
+            const float* src;
+            bool ok;
+            if (row < kRtTok) {
                 const int t = t0 + row;
-                const float* src = n + static_cast<size_t>(t < T ? t : 0) * H + k0 + q * 4;
-                cp_async16(&n_s[stage][row][q * 4], src, t < T ? 16u : 0u);
+                ok = t < T;
+                src = n + static_cast<size_t>(ok ? t : 0) * H;
             } else {
-                const int r = row - TT, e = e0 + r;
-                const float* src = W + static_cast<size_t>(e < E ? e : 0) * H + k0 + q * 4;
-                cp_async16(&w_s[stage][r][q * 4], src, e < E ? 16u : 0u);
+                const int e = e0 + row - kRtTok;
+                ok = e < E;
+                src = W + static_cast<size_t>(ok ? e : 0) * H;
             }
+            src += 256 * (j0 + j) + 32 * m + 8 * k + 4 * hh;
+            cp_async16(base + row * pitch + j * 32 + hh * 16, src, ok ? 16u : 0u);
         }
         cp_async_commit();
     };
 
-    float acc[TI][4];
+    float4 acc[2][4], s0[2][4], s1[2][4], s2[2][4];
+    const float4 z4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll
-    for (int i = 0; i < TI; ++i)
+    for (int a = 0; a < 2; ++a)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
-    const int nchunks = H / kR3KC;
-    load(0, 0);
-    for (int c = 0; c < nchunks; ++c) {
-        if (c + 1 < nchunks) {
-            load((c + 1) & 1, (c + 1) * kR3KC);
+        for (int b = 0; b < 4; ++b) { acc[a][b] = z4; s0[a][b] = z4; s1[a][b] = z4; s2[a][b] = z4; }
+
+    load_stage(0, 0);
+    for (int s = 0; s < nstages; ++s) {
+        if (s + 1 < nstages) {
+            load_stage(s + 1, (s + 1) & 1);
             cp_async_wait<1>();
         } else {
             cp_async_wait<0>();
         }
         __syncthreads();
-        const int st = c & 1;
-#pragma unroll 4
-        for (int kk = 0; kk < kR3KC; kk += 4) {
-            float4 a[TI], b[4];
+        int mi, j0, jn;
+        stage_at(s, mi, j0, jn);
+        const uint8_t* base = rt_ring + static_cast<size_t>(s & 1) * kRtRows * pitch + h * 16;
+        const uint8_t* pa0 = base + tr0 * pitch;
+        const uint8_t* pa1 = base + (tr0 + 8) * pitch;
+        const uint8_t* pb = base + er0 * pitch;
+#pragma unroll 2
+        for (int j = 0; j < jn; ++j) {
+            const float4 a0 = *reinterpret_cast<const float4*>(pa0 + j * 32);
+            const float4 a1 = *reinterpret_cast<const float4*>(pa1 + j * 32);
+            float4 b[4];
 #pragma unroll
-            for (int i = 0; i < TI; ++i) a[i] = *reinterpret_cast<const float4*>(&n_s[st][tg + 16 * i][kk]);
+            for (int i = 0; i < 4; ++i) b[i] = *reinterpret_cast<const float4*>(pb + 4 * i * pitch + j * 32);
 #pragma unroll
-            for (int j = 0; j < 4; ++j) b[j] = *reinterpret_cast<const float4*>(&w_s[st][eg + 8 * j][kk]);
+            for (int i = 0; i < 4; ++i) {
+                float2 lo = ffma2(make_float2(a0.x, a0.y), make_float2(b[i].x, b[i].y), make_float2(acc[0][i].x, acc[0][i].y));
+                float2 hi = ffma2(make_float2(a0.z, a0.w), make_float2(b[i].z, b[i].w), make_float2(acc[0][i].z, acc[0][i].w));
+                acc[0][i] = make_float4(lo.x, lo.y, hi.x, hi.y);
+                lo = ffma2(make_float2(a1.x, a1.y), make_float2(b[i].x, b[i].y), make_float2(acc[1][i].x, acc[1][i].y));
+                hi = ffma2(make_float2(a1.z, a1.w), make_float2(b[i].z, b[i].w), make_float2(acc[1][i].z, acc[1][i].w));
+                acc[1][i] = make_float4(lo.x, lo.y, hi.x, hi.y);
+            }
+        }
+        __syncthreads();    // the buffer is refilled by the next iteration's load
+        if (j0 + jn == rt_steps(H, m_of(mi))) {
+            // the m = m_of(mi) chains are complete: fold them into the tree
 #pragma unroll
-            for (int i = 0; i < TI; ++i)
+            for (int a = 0; a < 2; ++a)
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    acc[i][j] = __fmaf_rn(a[i].x, b[j].x, acc[i][j]);
-                    acc[i][j] = __fmaf_rn(a[i].y, b[j].y, acc[i][j]);
-                    acc[i][j] = __fmaf_rn(a[i].z, b[j].z, acc[i][j]);
-                    acc[i][j] = __fmaf_rn(a[i].w, b[j].w, acc[i][j]);
+                for (int b = 0; b < 4; ++b) {
+                    const float4 v = acc[a][b];
+                    switch (mi) {
+                        case 0: s0[a][b] = v; break;                                   // p0
+                        case 1: s0[a][b] = f4_add(s0[a][b], v); break;                 // p0 + p4
+                        case 2: s1[a][b] = v; break;                                   // p2
+                        case 3: s1[a][b] = f4_add(s1[a][b], v);                        // p2 + p6
+                                s0[a][b] = f4_add(s0[a][b], s1[a][b]); break;          // (p0+p4) + (p2+p6)
+                        case 4: s1[a][b] = v; break;                                   // p1
+                        case 5: s1[a][b] = f4_add(s1[a][b], v); break;                 // p1 + p5
+                        case 6: s2[a][b] = v; break;                                   // p3
+                        default: s2[a][b] = f4_add(s2[a][b], v);                       // p3 + p7
+                                 s1[a][b] = f4_add(s1[a][b], s2[a][b]);                // (p1+p5) + (p3+p7)
+                                 s0[a][b] = f4_add(s0[a][b], s1[a][b]); break;         // levels 128, 64, 32 done
+                    }
+                    acc[a][b] = z4;
                 }
         }
-        __syncthreads();
     }
+    // this CTA's sub-sums (q = 2k + h, r = 0..3) per pair: red[pair][h * 4 + r]
+    float* red = reinterpret_cast<float*>(rt_ring);
 #pragma unroll
-    for (int i = 0; i < TI; ++i)
+    for (int a = 0; a < 2; ++a)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int t = t0 + tg + 16 * i, e = e0 + eg + 8 * j;
-            if (t < T && e < E) logits[static_cast<size_t>(t) * E + e] = bias ? __fadd_rn(acc[i][j], bias[e]) : acc[i][j];
+        for (int b = 0; b < 4; ++b) {
+            const int tl = tr0 + 8 * a, el = 16 * we + eg + 4 * b;
+            *reinterpret_cast<float4*>(red + (tl * kRtExp + el) * 8 + h * 4) = s0[a][b];
         }
+    cluster.sync();
+    {
+        const int pair = k * (kRtTok * kRtExp / kRtCluster) + tid;   // 256 pairs per CTA
+        const int tl = pair / kRtExp, el = pair % kRtExp;
+        float sq[8][4];   // [q][r]
+#pragma unroll
+        for (int kk = 0; kk < kRtCluster; ++kk) {
+            const float* rr = cluster.map_shared_rank(red, kk) + pair * 8;
+            const float4 lo = *reinterpret_cast<const float4*>(rr);
+            const float4 hi = *reinterpret_cast<const float4*>(rr + 4);
+            sq[2 * kk][0] = lo.x; sq[2 * kk][1] = lo.y; sq[2 * kk][2] = lo.z; sq[2 * kk][3] = lo.w;
+            sq[2 * kk + 1][0] = hi.x; sq[2 * kk + 1][1] = hi.y; sq[2 * kk + 1][2] = hi.z; sq[2 * kk + 1][3] = hi.w;
+        }
+        float x4[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const float v0 = __fadd_rn(sq[0][r], sq[4][r]), v1 = __fadd_rn(sq[1][r], sq[5][r]);   // s = 16
+            const float v2 = __fadd_rn(sq[2][r], sq[6][r]), v3 = __fadd_rn(sq[3][r], sq[7][r]);
+            const float w0 = __fadd_rn(v0, v2), w1 = __fadd_rn(v1, v3);                            // s = 8
+            x4[r] = __fadd_rn(w0, w1);                                                             // s = 4
+        }
+        float v = __fadd_rn(__fadd_rn(x4[0], x4[2]), __fadd_rn(x4[1], x4[3]));                    // s = 2, 1
+        const int t = t0 + tl, e = e0 + el;
+        if (t < T && e < E) {
+            if (bias) v = __fadd_rn(v, bias[e]);
+            logits[static_cast<size_t>(t) * E + e] = v;
+        }
+    }
+    cluster.sync();   // no CTA leaves while the others still read its shared memory
 }
 
 // Top-k + softmax of the selected logits, one warp per token (8 tokens per
@@ -759,31 +845,17 @@ moe_status_t moe_router_logits(const float* n, const float* router_w, const floa
     if (T < 0 || H <= 0 || H % 128 || E <= 0 || E > 256) return MOE_ERR_INVALID_ARGUMENT;
     if (T == 0) return MOE_OK;
     if (!n || !router_w || !logits || !aligned16(n) || !aligned16(router_w)) return MOE_ERR_INVALID_ARGUMENT;
-    // tokens per thread: the smallest tile whose grid fits in one wave of 148
-    // SMs (a lone block is latency-bound, so a grid of <= 148 blocks finishes
-    // in about one block's time, and a smaller tile is a shorter block); when
-    // even 4 tokens per thread need more than one wave, 2 per thread (several
-    // resident blocks per SM).  Measured on B200, H = 5120, E = 160: T = 256 ->
-    // 1 (76 us), 512 -> 2 (84 us), 1024 -> 4 (123 us), 2048 / 4096 -> 2
-    // (170 / 274 us).
-    const int etiles = (E + kR3Exp - 1) / kR3Exp;
-    auto blocks_for = [&](int t) { return etiles * ((T + 16 * t - 1) / (16 * t)); };
-    const int ti = blocks_for(1) <= 148 ? 1 : (blocks_for(2) <= 148 ? 2 : (blocks_for(4) <= 148 ? 4 : 2));
-    const dim3 grid(etiles, (T + 16 * ti - 1) / (16 * ti));
-    if (grid.y > 65535) return MOE_ERR_UNSUPPORTED;
+    const long long tiles_t = (static_cast<long long>(T) + kRtTok - 1) / kRtTok;
+    if (tiles_t * kRtCluster > 0x7fffffffll) return MOE_ERR_UNSUPPORTED;
+    const int steps = rt_steps(H, 0);
+    const int jc = steps < kRtMaxJc ? steps : kRtMaxJc;
+    const size_t smem = rt_smem_bytes(jc);
     static bool attr[kMaxDevices] = {};
-    if (smem_optin_once(router_logits_tile_kernel<4>, static_cast<int>(r3_smem_bytes<4>()), attr) != cudaSuccess)
+    if (smem_optin_once(router_logits_ref_kernel, static_cast<int>(rt_smem_bytes(kRtMaxJc)), attr) != cudaSuccess)
         return MOE_ERR_CUDA;
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (ti == 4)
-        router_logits_tile_kernel<4><<<grid, kR3Threads, r3_smem_bytes<4>(), st>>>(n, router_w, router_bias, T, H, E,
-                                                                                   logits);
-    else if (ti == 2)
-        router_logits_tile_kernel<2><<<grid, kR3Threads, r3_smem_bytes<2>(), st>>>(n, router_w, router_bias, T, H, E,
-                                                                                   logits);
-    else
-        router_logits_tile_kernel<1><<<grid, kR3Threads, r3_smem_bytes<1>(), st>>>(n, router_w, router_bias, T, H, E,
-                                                                                   logits);
+    const dim3 grid(static_cast<unsigned>(tiles_t * kRtCluster), (E + kRtExp - 1) / kRtExp);
+    router_logits_ref_kernel<<<grid, kRtThreads, smem, static_cast<cudaStream_t>(stream)>>>(n, router_w, router_bias, T,
+                                                                                           H, E, jc, logits);
     return launch_status();
 }
 
@@ -814,15 +886,22 @@ moe_status_t moe_router_topk(const void* x_bf16, const float* rms, const float* 
                              int T, int H, int E, int k,
                              float* logits_out, int32_t* topk_idx, float* topk_w,
                              cwStream_t stream) {
-    if (T < 0 || H <= 0 || H % kRouterKC || E <= 0 || E > 256 || k <= 0 || k > 16 || k > E) return MOE_ERR_INVALID_ARGUMENT;
+    if (T < 0 || H <= 0 || H % 128 || E <= 0 || E > 256 || k <= 0 || k > 16 || k > E) return MOE_ERR_INVALID_ARGUMENT;
     if (T == 0) return MOE_OK;
     if (!x_bf16 || !rms || !gamma || !router_w || !topk_idx || !topk_w) return MOE_ERR_INVALID_ARGUMENT;
-    const int blocks = (T + kRouterTok - 1) / kRouterTok;
+    const size_t smem = static_cast<size_t>(H + E) * sizeof(float);
+    if (smem > 200 * 1024) return MOE_ERR_UNSUPPORTED;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x_bf16);
-    const int ept = (E + 31) / 32;
-#define TB_ROUTER(EPTV) router_topk_kernel<EPTV><<<blocks, 256, 0, s>>>(xb, rms, gamma, router_w, router_bias, T, H, E, k, logits_out, topk_idx, topk_w)
-    switch (ept) {
+    static bool attr[8][kMaxDevices] = {};
+#define TB_ROUTER(EPTV)                                                                                        \
+    do {                                                                                                       \
+        if (smem_optin_once(router_topk_kernel<EPTV>, 200 * 1024, attr[EPTV - 1]) != cudaSuccess)              \
+            return MOE_ERR_CUDA;                                                                               \
+        router_topk_kernel<EPTV><<<T, 256, smem, s>>>(xb, rms, gamma, router_w, router_bias, T, H, E, k,       \
+                                                      logits_out, topk_idx, topk_w);                           \
+    } while (0)
+    switch ((E + 31) / 32) {
         case 1: TB_ROUTER(1); break;
         case 2: TB_ROUTER(2); break;
         case 3: TB_ROUTER(3); break;
@@ -951,25 +1030,55 @@ static __device__ __align__(256) float g_router_logits_scratch[kNoAllocLogits];
 
 namespace {
 
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+
+// cuCtxGetCurrent through the runtime's driver entry-point query (this library
+// links only the runtime); null when the driver does not offer it.
+CtxGetCurrentFn ctx_get_current_fn() {
+    static CtxGetCurrentFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<CtxGetCurrentFn>(p);
+    });
+    return fn;
+}
+
 // The array's device address, looked up once per device with that device
-// current (host code cannot use the array's name as a device pointer).
+// current (host code cannot use the array's name as a device pointer).  The
+// cache entry remembers the context it was looked up in: after a
+// cudaDeviceReset the device gets a new primary context, the module is loaded
+// again, and the address is looked up again instead of reusing the old one.
 float* router_scratch_address(moe_status_t* status) {
     constexpr int kMaxDevices = 64;
     static std::mutex mu;
     static float* addr[kMaxDevices] = {};
+    static CUcontext ctx_of[kMaxDevices] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
         *status = MOE_ERR_CUDA;
         return nullptr;
     }
+    // make the device's primary context current before asking which it is
+    if (cudaFree(nullptr) != cudaSuccess) {
+        *status = MOE_ERR_CUDA;
+        return nullptr;
+    }
+    CUcontext ctx = nullptr;
+    CtxGetCurrentFn get = ctx_get_current_fn();
+    if (get && get(&ctx) != CUDA_SUCCESS) ctx = nullptr;
     std::lock_guard<std::mutex> lock(mu);
-    if (!addr[dev]) {
+    if (!addr[dev] || ctx_of[dev] != ctx) {
         void* p = nullptr;
         if (cudaGetSymbolAddress(&p, g_router_logits_scratch) != cudaSuccess || !p) {
             *status = MOE_ERR_CUDA;
             return nullptr;
         }
         addr[dev] = static_cast<float*>(p);
+        ctx_of[dev] = ctx;
     }
     *status = MOE_OK;
     return addr[dev];
@@ -980,9 +1089,12 @@ float* router_scratch_address(moe_status_t* status) {
 extern "C" moe_status_t moe_router_topk_noalloc(const float* n, const float* router_w, const float* router_bias,
                                                 int T, int H, int E, int k, int32_t* topk_idx, float* topk_w,
                                                 cwStream_t stream) {
-    if (T < 0 || E <= 0) return MOE_ERR_INVALID_ARGUMENT;
+    // every argument check of the two kernels comes first, so a refused call launches nothing
+    if (T < 0 || H <= 0 || H % 128 || E <= 0 || E > 256 || k <= 0 || k > 16 || k > E) return MOE_ERR_INVALID_ARGUMENT;
     if (static_cast<long long>(T) * E > kNoAllocLogits) return MOE_ERR_WORKSPACE;   // beyond the fixed array
     if (T == 0) return MOE_OK;
+    if (!n || !router_w || !topk_idx || !topk_w || !aligned16(n) || !aligned16(router_w))
+        return MOE_ERR_INVALID_ARGUMENT;
     moe_status_t st = MOE_OK;
     float* logits = router_scratch_address(&st);
     if (!logits) return st;

@@ -94,6 +94,7 @@ def libs():
         k.moe_permute_padded.argtypes = [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p,
                                          c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p]
         k.moe_layer_set_expert_placement.argtypes = [c_void_p, c_void_p]
+        k.moe_layer_set_gemm_form.argtypes = [c_void_p, c_int]
         k.moe_ep_remap_experts.argtypes = [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p]
         k.moe_layer_peer_bytes.argtypes = [c_void_p]
         k.moe_layer_peer_bytes.restype = c_size_t
@@ -269,6 +270,10 @@ class MoELayer:
         arr = np.ascontiguousarray(slot_of_expert, dtype=np.int32)
         check("moe_layer_set_expert_placement",
               self._k.moe_layer_set_expert_placement(self._h, arr.ctypes.data_as(c_void_p)))
+
+    def set_gemm_form(self, form: int):
+        """GEMM_SMALL_TILES, GEMM_FULL_TILES or 0 (the layer's rule)."""
+        check("moe_layer_set_gemm_form", self._k.moe_layer_set_gemm_form(self._h, form))
 
     def use_peer_memory(self, group=None):
         """Switch the expert-parallel exchange to NVLink peer memory: allocate

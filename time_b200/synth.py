@@ -49,8 +49,10 @@ def quantize_blocks(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
 
 
 def make_moe_weights(shape: MoEShape, seed: int = 0, device="cpu", zipf_bias: bool = False,
-                     gen: torch.Generator | None = None, skip_x: bool = True) -> dict:
-    """Router + expert weights (see module docstring for the draw order)."""
+                     gen: torch.Generator | None = None, skip_x: bool = True, experts: bool = True) -> dict:
+    """Router + expert weights (see module docstring for the draw order).
+    experts=False stops after the router (gamma, router_w, router_bias: the
+    same values as the full draw)."""
     g = gen or torch.Generator(device=device).manual_seed(seed)
     H, E, I, S = shape.hidden, shape.num_experts, shape.intermediate, shape.num_shared
     out = {"gamma": torch.ones(H, dtype=torch.float32, device=device)}
@@ -60,6 +62,8 @@ def make_moe_weights(shape: MoEShape, seed: int = 0, device="cpu", zipf_bias: bo
         out["router_bias"] = (-1.1 * torch.log(perm)).to(torch.float32)
     else:
         out["router_bias"] = None
+    if not experts:
+        return out
     G = E + S
     w13 = torch.empty(G, 2 * I, H, dtype=torch.uint8, device=device)
     s13 = torch.empty(G, 2 * I // 128, H // 128, dtype=torch.float32, device=device)
