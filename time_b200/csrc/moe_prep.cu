@@ -3,6 +3,7 @@
 // row gather and the weighted combine.  C-ABI entry points are declared in
 // include/moe_layer.h.
 #include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <cooperative_groups.h>
@@ -293,204 +294,239 @@ router_topk_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict_
     }
 }
 
+// One warp per logit in the reference order (hidden sizes that are odd
+// multiples of 128, where the tiled kernel's 256-element steps do not fit).
+__global__ void __launch_bounds__(256)
+router_logits_warp_kernel(const float* __restrict__ n, const float* __restrict__ W, const float* __restrict__ bias,
+                          int T, int H, int E, float* __restrict__ logits) {
+    const long long pair = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (pair >= static_cast<long long>(T) * E) return;
+    const int t = static_cast<int>(pair / E), e = static_cast<int>(pair % E);
+    float v = warp_logit_ref_order(n + static_cast<size_t>(t) * H, W + static_cast<size_t>(e) * H, H, lane);
+    if (bias) v = __fadd_rn(v, bias[e]);
+    if (lane == 0) logits[static_cast<size_t>(t) * E + e] = v;
+}
+
 // ---------------------------------------------------------------- tiled router
-// The layer's router.  A cluster of 4 CTAs computes one 32-token x 32-expert
-// tile; CTA k of the cluster takes the lanes with q in {2k, 2k + 1} (warps
-// 0-3: q = 2k, warps 4-7: q = 2k + 1), so every row it stages is one 32-byte
-// piece (l = 32m + 8k .. +7) per 256-element step j.  A thread owns 2 tokens
-// x 4 experts and, for its q, the four chains r = 0..3 of each pair: one
-// 16-byte shared-memory load per operand row feeds two fp32x2 FMAs per pair.
-// The chains of one m run over all j (ascending, across as many staged chunks
-// of <= 20 steps as H needs); the 8 m values are processed in the tree's
-// post-order 0, 4, 2, 6, 1, 5, 3, 7 and folded with a 3-deep stack, which
-// forms exactly the levels s = 128, 64, 32.  Each CTA then leaves its 2 x 4
-// sub-sums per pair in shared memory; after a cluster barrier CTA k reduces
-// the pairs [256k, 256k + 256) of the tile over the four CTAs (distributed
-// shared memory) with the levels s = 16, 8, 4, 2, 1, adds the bias and
-// writes the logit.  Operands go through a two-stage cp.async ring with a row
-// pitch of 32*jc + 16 bytes, which puts 8 consecutive rows in 8 distinct
-// 16-byte bank groups (conflict-free loads).
-constexpr int kRtTok = 32, kRtExp = 32, kRtRows = kRtTok + kRtExp;
+// The layer's router, persistent over 32-token x 32-expert tiles.  A cluster
+// of 4 CTAs owns a tile at a time; CTA k of the cluster takes the lanes with
+// q in {2k, 2k + 1}, so per 256-element step j it needs one 32-byte piece of
+// every row (l = 32m + 8k .. +7).  Thread 0 streams those pieces with 3-D TMA
+// loads -- box {8 floats, 32 rows, 20 steps} of n and of W, laid out in shared
+// memory as [step][row][32 bytes] -- through a 4-stage ring of mbarriers, one
+// stage per (m, chunk of <= 20 steps), continuing across the cluster's tiles.
+//
+// Lanes: a warp covers 8 tokens x 16 experts, both q of the CTA (lane bit 2);
+// a thread owns 2 tokens x 4 experts and, for its q, the four chains r = 0..3
+// of each pair as two fp32x2 registers.  A token load of the warp reads 128
+// contiguous bytes (4 rows x 2 q), the same in each 8-lane phase, so it is
+// conflict-free.  The chains of one m run over all j (ascending); the 8 m
+// values are processed in the tree's post-order 0, 4, 2, 6, 1, 5, 3, 7 and
+// folded with a 3-deep stack, which forms exactly the levels s = 128, 64, 32.
+// At the end of a tile each CTA leaves its 2 x 4 sub-sums per pair in shared
+// memory; after a cluster barrier CTA k reduces the pairs [256k, 256k + 256)
+// over the four CTAs (distributed shared memory) with the levels s = 16, 8, 4,
+// 2, 1, adds the bias and writes the logit.  Every mbarrier wait is bounded
+// (2 s); a CTA whose wait gives up writes NaN logits for its tiles (never
+// selected by the top-k) instead of hanging.
+constexpr int kRtTok = 32, kRtExp = 32;
 constexpr int kRtThreads = 256;
-constexpr int kRtMaxJc = 20;           // 256-element steps per staged chunk
+constexpr int kRtJc = 20;                                   // steps per stage
 constexpr int kRtCluster = 4;
+constexpr int kRtRing = 4;
+constexpr int kRtBoxBytes = kRtJc * 32 * 32;                // [20 steps][32 rows][32 bytes]
+constexpr int kRtStageBytes = 2 * kRtBoxBytes;              // n box, then W box
+constexpr int kRtRedBytes = kRtTok * kRtExp * 8 * 4;
+constexpr int kRtOffRed = kRtRing * kRtStageBytes;
+constexpr int kRtOffBars = kRtOffRed + kRtRedBytes;
+constexpr size_t kRtSmemBytes = kRtOffBars + kRtRing * 8 + 16 + 1024;   // + abort flag, alignment slack
+constexpr uint64_t kRtWaitNs = 2000000000ull;
 
-__host__ __device__ constexpr int rt_pitch(int jc) { return 32 * jc + 16; }
-__host__ __device__ constexpr int rt_steps(int H, int m) { return H > 32 * m ? (H - 32 * m + 255) / 256 : 0; }
-inline size_t rt_smem_bytes(int jc) {
-    const size_t ring = 2 * static_cast<size_t>(kRtRows) * rt_pitch(jc);
-    const size_t red = static_cast<size_t>(kRtTok) * kRtExp * 8 * sizeof(float);
-    return ring > red ? ring : red;
+using u64 = unsigned long long;
+__device__ __forceinline__ u64 ffma2_u(u64 a, u64 b, u64 c) {
+    u64 d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ u64 fadd2_u(u64 a, u64 b) {
+    u64 d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
 }
 
-__device__ __forceinline__ float4 f4_add(float4 a, float4 b) {
-    return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
-}
+struct RtParams {
+    const float* bias;
+    float* logits;
+    int T, E, J;          // J = H / 256 steps
+    int t_tiles, e_tiles;
+};
 
 __global__ void __cluster_dims__(kRtCluster, 1, 1) __launch_bounds__(kRtThreads, 1)
-router_logits_ref_kernel(const float* __restrict__ n, const float* __restrict__ W, const float* __restrict__ bias,
-                         int T, int H, int E, int jc, float* __restrict__ logits) {
+router_logits_ref_kernel(const __grid_constant__ CUtensorMap tmap_n, const __grid_constant__ CUtensorMap tmap_w,
+                         const RtParams p) {
     namespace cg = cooperative_groups;
-    extern __shared__ __align__(16) uint8_t rt_ring[];
+    extern __shared__ uint8_t rt_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(rt_raw) + 1023) & ~uintptr_t(1023));
+    float* red = reinterpret_cast<float*>(smem + kRtOffRed);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRtOffBars);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kRtOffBars + kRtRing * 8);
     cg::cluster_group cluster = cg::this_cluster();
     const int k = static_cast<int>(cluster.block_rank());
-    const int t0 = (blockIdx.x / kRtCluster) * kRtTok, e0 = blockIdx.y * kRtExp;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int h = warp >> 2;                       // q = 2k + h
-    const int wt = (warp >> 1) & 1, we = warp & 1;
-    const int tg = lane & 7, eg = lane >> 3;
-    const int pitch = rt_pitch(jc);
-    // rows: tokens 16wt + tg, +8; experts 16we + eg + 4i (i = 0..3)
-    const int tr0 = 16 * wt + tg;
-    const int er0 = kRtTok + 16 * we + eg;
+    const int wt = warp >> 1, we = warp & 1;
+    const int tg = lane & 3, h = (lane >> 2) & 1, eg = lane >> 3;
+    const int trow = 8 * wt + tg;                  // tokens trow, trow + 4
+    const int erow = 16 * we + eg;                 // experts erow + 4b, b = 0..3
 
-    // the stage list: m in the tree's post-order (order index mi -> m is the
-    // 3-bit reversal of mi: 0, 4, 2, 6, 1, 5, 3, 7), each m in chunks of <= jc
-    // steps; an m without steps (H < 256) keeps one empty stage so that its
-    // +0.0f chains are folded like the reference adds its empty partials
+    const int cid = blockIdx.x / kRtCluster, ncl = gridDim.x / kRtCluster;
+    const int tiles = p.t_tiles * p.e_tiles;
+    const int my_tiles = cid < tiles ? (tiles - cid + ncl - 1) / ncl : 0;
+    const int C = (p.J + kRtJc - 1) / kRtJc;       // chunks per m
+    const int S = 8 * C;                           // stages per tile
+    const long long g_total = static_cast<long long>(my_tiles) * S;
     auto m_of = [](int mi) { return ((mi & 1) << 2) | (mi & 2) | (mi >> 2); };
-    auto chunks_of = [&](int m) { const int J = rt_steps(H, m); return J == 0 ? 1 : (J + jc - 1) / jc; };
-    int nstages = 0;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) nstages += chunks_of(m_of(i));
 
-    // stage s -> (order index mi, first step j0, steps jn)
-    auto stage_at = [&](int s, int& mi, int& j0, int& jn) {
-        mi = 0;
-        int c = chunks_of(m_of(0));
-        while (s >= c) { s -= c; ++mi; c = chunks_of(m_of(mi)); }
-        j0 = s * jc;
-        const int J = rt_steps(H, m_of(mi));
-        jn = J - j0 < jc ? J - j0 : jc;
-    };
-    auto load_stage = [&](int s, int buf) {
-        int mi, j0, jn;
-        stage_at(s, mi, j0, jn);
-        const int m = m_of(mi);
-        uint8_t* base = rt_ring + static_cast<size_t>(buf) * kRtRows * pitch;
-        const int per_row = 2 * jn;
-        for (int c = tid; c < kRtRows * per_row; c += kRtThreads) {
-            const int row = c / per_row, rem = c - row * per_row;
-            const int j = rem >> 1, hh = rem & 1;
-            const float* src;
-            bool ok;
-            if (row < kRtTok) {
-                const int t = t0 + row;
-                ok = t < T;
-                src = n + static_cast<size_t>(ok ? t : 0) * H;
-            } else {
-                const int e = e0 + row - kRtTok;
-                ok = e < E;
-                src = W + static_cast<size_t>(ok ? e : 0) * H;
-            }
-            src += 256 * (j0 + j) + 32 * m + 8 * k + 4 * hh;
-            cp_async16(base + row * pitch + j * 32 + hh * 16, src, ok ? 16u : 0u);
-        }
-        cp_async_commit();
+    auto issue = [&](long long g) {                // thread 0 only
+        const int it = static_cast<int>(g / S), s = static_cast<int>(g % S);
+        const int tile = cid + it * ncl;
+        const int t0 = (tile / p.e_tiles) * kRtTok, e0 = (tile % p.e_tiles) * kRtExp;
+        const int m = m_of(s / C), j0 = (s % C) * kRtJc;
+        const int slot = static_cast<int>(g % kRtRing);
+        uint8_t* st = smem + slot * kRtStageBytes;
+        mbar_arrive_expect_tx(&full[slot], kRtStageBytes);
+        tma_load_3d(&tmap_n, &full[slot], st, 32 * m + 8 * k, t0, j0);
+        tma_load_3d(&tmap_w, &full[slot], st + kRtBoxBytes, 32 * m + 8 * k, e0, j0);
     };
 
-    float4 acc[2][4], s0[2][4], s1[2][4], s2[2][4];
-    const float4 z4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll
-    for (int a = 0; a < 2; ++a)
-#pragma unroll
-        for (int b = 0; b < 4; ++b) { acc[a][b] = z4; s0[a][b] = z4; s1[a][b] = z4; s2[a][b] = z4; }
+    if (tid == 0) {
+        for (int i = 0; i < kRtRing; ++i) mbar_init(&full[i], 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+        prefetch_tmap(&tmap_n);
+        prefetch_tmap(&tmap_w);
+    }
+    __syncthreads();
+    if (tid == 0)
+        for (long long g = 0; g < g_total && g < kRtRing; ++g) issue(g);
 
-    load_stage(0, 0);
-    for (int s = 0; s < nstages; ++s) {
-        if (s + 1 < nstages) {
-            load_stage(s + 1, (s + 1) & 1);
-            cp_async_wait<1>();
-        } else {
-            cp_async_wait<0>();
-        }
-        __syncthreads();
-        int mi, j0, jn;
-        stage_at(s, mi, j0, jn);
-        const uint8_t* base = rt_ring + static_cast<size_t>(s & 1) * kRtRows * pitch + h * 16;
-        const uint8_t* pa0 = base + tr0 * pitch;
-        const uint8_t* pa1 = base + (tr0 + 8) * pitch;
-        const uint8_t* pb = base + er0 * pitch;
-#pragma unroll 2
-        for (int j = 0; j < jn; ++j) {
-            const float4 a0 = *reinterpret_cast<const float4*>(pa0 + j * 32);
-            const float4 a1 = *reinterpret_cast<const float4*>(pa1 + j * 32);
-            float4 b[4];
+    bool ok = true;
+    for (int it = 0; it < my_tiles; ++it) {
+        const int tile = cid + it * ncl;
+        const int t0 = (tile / p.e_tiles) * kRtTok, e0 = (tile % p.e_tiles) * kRtExp;
+        u64 acc[2][4][2], s0[2][4][2], s1[2][4][2], s2[2][4][2];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) b[i] = *reinterpret_cast<const float4*>(pb + 4 * i * pitch + j * 32);
+        for (int a = 0; a < 2; ++a)
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                float2 lo = ffma2(make_float2(a0.x, a0.y), make_float2(b[i].x, b[i].y), make_float2(acc[0][i].x, acc[0][i].y));
-                float2 hi = ffma2(make_float2(a0.z, a0.w), make_float2(b[i].z, b[i].w), make_float2(acc[0][i].z, acc[0][i].w));
-                acc[0][i] = make_float4(lo.x, lo.y, hi.x, hi.y);
-                lo = ffma2(make_float2(a1.x, a1.y), make_float2(b[i].x, b[i].y), make_float2(acc[1][i].x, acc[1][i].y));
-                hi = ffma2(make_float2(a1.z, a1.w), make_float2(b[i].z, b[i].w), make_float2(acc[1][i].z, acc[1][i].w));
-                acc[1][i] = make_float4(lo.x, lo.y, hi.x, hi.y);
-            }
-        }
-        __syncthreads();    // the buffer is refilled by the next iteration's load
-        if (j0 + jn == rt_steps(H, m_of(mi))) {
-            // the m = m_of(mi) chains are complete: fold them into the tree
+            for (int b = 0; b < 4; ++b)
 #pragma unroll
-            for (int a = 0; a < 2; ++a)
+                for (int c = 0; c < 2; ++c) { acc[a][b][c] = 0; s0[a][b][c] = 0; s1[a][b][c] = 0; s2[a][b][c] = 0; }
+        for (int s = 0; s < S; ++s) {
+            const long long g = static_cast<long long>(it) * S + s;
+            const int slot = static_cast<int>(g % kRtRing);
+            if (ok && !mbar_wait_bounded(&full[slot], static_cast<uint32_t>((g / kRtRing) & 1), abort_flag, kRtWaitNs))
+                ok = false;
+            const int mi = s / C, j0 = (s % C) * kRtJc;
+            const int jn = p.J - j0 < kRtJc ? p.J - j0 : kRtJc;
+            if (ok) {
+                const uint8_t* nb = smem + slot * kRtStageBytes + h * 16;
+                const uint8_t* pa = nb + trow * 32;
+                const uint8_t* pb = nb + kRtBoxBytes + erow * 32;
+#pragma unroll 4
+                for (int j = 0; j < jn; ++j) {
+                    const ulonglong2 a0 = *reinterpret_cast<const ulonglong2*>(pa + j * 1024);
+                    const ulonglong2 a1 = *reinterpret_cast<const ulonglong2*>(pa + j * 1024 + 4 * 32);
+                    ulonglong2 bv[4];
 #pragma unroll
-                for (int b = 0; b < 4; ++b) {
-                    const float4 v = acc[a][b];
-                    switch (mi) {
-                        case 0: s0[a][b] = v; break;                                   // p0
-                        case 1: s0[a][b] = f4_add(s0[a][b], v); break;                 // p0 + p4
-                        case 2: s1[a][b] = v; break;                                   // p2
-                        case 3: s1[a][b] = f4_add(s1[a][b], v);                        // p2 + p6
-                                s0[a][b] = f4_add(s0[a][b], s1[a][b]); break;          // (p0+p4) + (p2+p6)
-                        case 4: s1[a][b] = v; break;                                   // p1
-                        case 5: s1[a][b] = f4_add(s1[a][b], v); break;                 // p1 + p5
-                        case 6: s2[a][b] = v; break;                                   // p3
-                        default: s2[a][b] = f4_add(s2[a][b], v);                       // p3 + p7
-                                 s1[a][b] = f4_add(s1[a][b], s2[a][b]);                // (p1+p5) + (p3+p7)
-                                 s0[a][b] = f4_add(s0[a][b], s1[a][b]); break;         // levels 128, 64, 32 done
+                    for (int i = 0; i < 4; ++i) bv[i] = *reinterpret_cast<const ulonglong2*>(pb + j * 1024 + 4 * i * 32);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        acc[0][i][0] = ffma2_u(a0.x, bv[i].x, acc[0][i][0]);
+                        acc[0][i][1] = ffma2_u(a0.y, bv[i].y, acc[0][i][1]);
+                        acc[1][i][0] = ffma2_u(a1.x, bv[i].x, acc[1][i][0]);
+                        acc[1][i][1] = ffma2_u(a1.y, bv[i].y, acc[1][i][1]);
                     }
-                    acc[a][b] = z4;
                 }
+            }
+            __syncthreads();            // every warp is done with the slot
+            if (tid == 0 && g + kRtRing < g_total && !*abort_flag) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                issue(g + kRtRing);
+            }
+            if (j0 + jn == p.J) {
+                // the m = m_of(mi) chains are complete: fold them into the tree
+#pragma unroll
+                for (int a = 0; a < 2; ++a)
+#pragma unroll
+                    for (int b = 0; b < 4; ++b)
+#pragma unroll
+                        for (int c = 0; c < 2; ++c) {
+                            const u64 v = acc[a][b][c];
+                            switch (mi) {
+                                case 0: s0[a][b][c] = v; break;                                       // p0
+                                case 1: s0[a][b][c] = fadd2_u(s0[a][b][c], v); break;                 // p0 + p4
+                                case 2: s1[a][b][c] = v; break;                                       // p2
+                                case 3: s1[a][b][c] = fadd2_u(s1[a][b][c], v);                        // p2 + p6
+                                        s0[a][b][c] = fadd2_u(s0[a][b][c], s1[a][b][c]); break;       // (p0+p4)+(p2+p6)
+                                case 4: s1[a][b][c] = v; break;                                       // p1
+                                case 5: s1[a][b][c] = fadd2_u(s1[a][b][c], v); break;                 // p1 + p5
+                                case 6: s2[a][b][c] = v; break;                                       // p3
+                                default: s2[a][b][c] = fadd2_u(s2[a][b][c], v);                       // p3 + p7
+                                         s1[a][b][c] = fadd2_u(s1[a][b][c], s2[a][b][c]);             // (p1+p5)+(p3+p7)
+                                         s0[a][b][c] = fadd2_u(s0[a][b][c], s1[a][b][c]); break;      // s = 128, 64, 32
+                            }
+                            acc[a][b][c] = 0;
+                        }
+            }
+        }
+        // this CTA's sub-sums (q = 2k + h, r = 0..3) per pair: red[pair][h * 4 + r]
+#pragma unroll
+        for (int a = 0; a < 2; ++a)
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                const int tl = trow + 4 * a, el = erow + 4 * b;
+                *reinterpret_cast<ulonglong2*>(red + (tl * kRtExp + el) * 8 + h * 4) =
+                    make_ulonglong2(s0[a][b][0], s0[a][b][1]);
+            }
+        cluster.sync();
+        {
+            const int pair = k * (kRtTok * kRtExp / kRtCluster) + tid;   // 256 pairs per CTA
+            const int tl = pair / kRtExp, el = pair % kRtExp;
+            float sq[8][4];   // [q][r]
+#pragma unroll
+            for (int kk = 0; kk < kRtCluster; ++kk) {
+                const float* rr = cluster.map_shared_rank(red, kk) + pair * 8;
+                const float4 lo = *reinterpret_cast<const float4*>(rr);
+                const float4 hi = *reinterpret_cast<const float4*>(rr + 4);
+                sq[2 * kk][0] = lo.x; sq[2 * kk][1] = lo.y; sq[2 * kk][2] = lo.z; sq[2 * kk][3] = lo.w;
+                sq[2 * kk + 1][0] = hi.x; sq[2 * kk + 1][1] = hi.y; sq[2 * kk + 1][2] = hi.z; sq[2 * kk + 1][3] = hi.w;
+            }
+            float x4[4];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const float v0 = __fadd_rn(sq[0][r], sq[4][r]), v1 = __fadd_rn(sq[1][r], sq[5][r]);   // s = 16
+                const float v2 = __fadd_rn(sq[2][r], sq[6][r]), v3 = __fadd_rn(sq[3][r], sq[7][r]);
+                const float w0 = __fadd_rn(v0, v2), w1 = __fadd_rn(v1, v3);                            // s = 8
+                x4[r] = __fadd_rn(w0, w1);                                                             // s = 4
+            }
+            float v = __fadd_rn(__fadd_rn(x4[0], x4[2]), __fadd_rn(x4[1], x4[3]));                    // s = 2, 1
+            const int t = t0 + tl, e = e0 + el;
+            if (t < p.T && e < p.E) {
+                if (p.bias) v = __fadd_rn(v, p.bias[e]);
+                p.logits[static_cast<size_t>(t) * p.E + e] = *abort_flag ? __int_as_float(0x7fc00000) : v;
+            }
+        }
+        cluster.sync();   // the next tile's sub-sums overwrite what the other CTAs just read
+    }
+    // a CTA that gave up lets the copies it issued land before it exits
+    if (tid == 0 && *abort_flag) {
+        for (long long g = g_total - kRtRing; g < g_total; ++g) {
+            if (g < 0) continue;
+            const uint64_t t1 = globaltimer_ns();
+            while (!mbar_try_wait(&full[g % kRtRing], static_cast<uint32_t>((g / kRtRing) & 1)))
+                if (globaltimer_ns() - t1 > 200000000ull) break;
         }
     }
-    // this CTA's sub-sums (q = 2k + h, r = 0..3) per pair: red[pair][h * 4 + r]
-    float* red = reinterpret_cast<float*>(rt_ring);
-#pragma unroll
-    for (int a = 0; a < 2; ++a)
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-            const int tl = tr0 + 8 * a, el = 16 * we + eg + 4 * b;
-            *reinterpret_cast<float4*>(red + (tl * kRtExp + el) * 8 + h * 4) = s0[a][b];
-        }
-    cluster.sync();
-    {
-        const int pair = k * (kRtTok * kRtExp / kRtCluster) + tid;   // 256 pairs per CTA
-        const int tl = pair / kRtExp, el = pair % kRtExp;
-        float sq[8][4];   // [q][r]
-#pragma unroll
-        for (int kk = 0; kk < kRtCluster; ++kk) {
-            const float* rr = cluster.map_shared_rank(red, kk) + pair * 8;
-            const float4 lo = *reinterpret_cast<const float4*>(rr);
-            const float4 hi = *reinterpret_cast<const float4*>(rr + 4);
-            sq[2 * kk][0] = lo.x; sq[2 * kk][1] = lo.y; sq[2 * kk][2] = lo.z; sq[2 * kk][3] = lo.w;
-            sq[2 * kk + 1][0] = hi.x; sq[2 * kk + 1][1] = hi.y; sq[2 * kk + 1][2] = hi.z; sq[2 * kk + 1][3] = hi.w;
-        }
-        float x4[4];
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            const float v0 = __fadd_rn(sq[0][r], sq[4][r]), v1 = __fadd_rn(sq[1][r], sq[5][r]);   // s = 16
-            const float v2 = __fadd_rn(sq[2][r], sq[6][r]), v3 = __fadd_rn(sq[3][r], sq[7][r]);
-            const float w0 = __fadd_rn(v0, v2), w1 = __fadd_rn(v1, v3);                            // s = 8
-            x4[r] = __fadd_rn(w0, w1);                                                             // s = 4
-        }
-        float v = __fadd_rn(__fadd_rn(x4[0], x4[2]), __fadd_rn(x4[1], x4[3]));                    // s = 2, 1
-        const int t = t0 + tl, e = e0 + el;
-        if (t < T && e < E) {
-            if (bias) v = __fadd_rn(v, bias[e]);
-            logits[static_cast<size_t>(t) * E + e] = v;
-        }
-    }
-    cluster.sync();   // no CTA leaves while the others still read its shared memory
 }
 
 // Top-k + softmax of the selected logits, one warp per token (8 tokens per
@@ -810,6 +846,35 @@ inline moe_status_t launch_status() {
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+PFN_cuTensorMapEncodeTiled_v12000 rt_encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess && q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    });
+    return fn;
+}
+
+// The router's view of an fp32 [rows][H] matrix (H % 256 == 0) as a 3-D
+// tensor {256 lanes l, rows, H/256 steps j} -- element (l, row, j) is
+// m[row][256 j + l] -- with box {8, 32, 20}: a TMA load lands as
+// [step][row][8 floats] in shared memory.  Rows past the end read as zero.
+bool encode_rt_map(CUtensorMap* map, const float* base, int rows, int H) {
+    auto fn = rt_encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {256, static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(H / 256)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(H) * 4, 1024};
+    cuuint32_t box[3] = {8, kRtTok, kRtJc};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace
 
 extern "C" {
@@ -845,17 +910,52 @@ moe_status_t moe_router_logits(const float* n, const float* router_w, const floa
     if (T < 0 || H <= 0 || H % 128 || E <= 0 || E > 256) return MOE_ERR_INVALID_ARGUMENT;
     if (T == 0) return MOE_OK;
     if (!n || !router_w || !logits || !aligned16(n) || !aligned16(router_w)) return MOE_ERR_INVALID_ARGUMENT;
-    const long long tiles_t = (static_cast<long long>(T) + kRtTok - 1) / kRtTok;
-    if (tiles_t * kRtCluster > 0x7fffffffll) return MOE_ERR_UNSUPPORTED;
-    const int steps = rt_steps(H, 0);
-    const int jc = steps < kRtMaxJc ? steps : kRtMaxJc;
-    const size_t smem = rt_smem_bytes(jc);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (H % 256) {
+        // a hidden size that is an odd multiple of 128 (only small test shapes): one warp per logit
+        const long long warps = static_cast<long long>(T) * E;
+        if ((warps + 7) / 8 > 0x7fffffffll) return MOE_ERR_UNSUPPORTED;
+        router_logits_warp_kernel<<<static_cast<unsigned>((warps + 7) / 8), 256, 0, st>>>(n, router_w, router_bias,
+                                                                                          T, H, E, logits);
+        return launch_status();
+    }
+    CUtensorMap tn, tw;
+    if (!encode_rt_map(&tn, n, T, H) || !encode_rt_map(&tw, router_w, E, H)) return MOE_ERR_CUDA;
     static bool attr[kMaxDevices] = {};
-    if (smem_optin_once(router_logits_ref_kernel, static_cast<int>(rt_smem_bytes(kRtMaxJc)), attr) != cudaSuccess)
+    static int max_clusters[kMaxDevices] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return MOE_ERR_CUDA;
+    if (smem_optin_once(router_logits_ref_kernel, static_cast<int>(kRtSmemBytes), attr) != cudaSuccess)
         return MOE_ERR_CUDA;
-    const dim3 grid(static_cast<unsigned>(tiles_t * kRtCluster), (E + kRtExp - 1) / kRtExp);
-    router_logits_ref_kernel<<<grid, kRtThreads, smem, static_cast<cudaStream_t>(stream)>>>(n, router_w, router_bias, T,
-                                                                                           H, E, jc, logits);
+    RtParams prm;
+    prm.bias = router_bias;
+    prm.logits = logits;
+    prm.T = T;
+    prm.E = E;
+    prm.J = H / 256;
+    prm.t_tiles = (T + kRtTok - 1) / kRtTok;
+    prm.e_tiles = (E + kRtExp - 1) / kRtExp;
+    const long long tiles = static_cast<long long>(prm.t_tiles) * prm.e_tiles;
+    if (tiles > 0x7fffffffll / kRtCluster) return MOE_ERR_UNSUPPORTED;
+    int ncl = dev >= 0 && dev < kMaxDevices ? max_clusters[dev] : 0;
+    if (ncl <= 0) {
+        // as many clusters as can be resident at once (one CTA per SM)
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(kRtCluster * 512);
+        cfg.blockDim = dim3(kRtThreads);
+        cfg.dynamicSmemBytes = kRtSmemBytes;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = kRtCluster;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        if (cudaOccupancyMaxActiveClusters(&ncl, router_logits_ref_kernel, &cfg) != cudaSuccess || ncl <= 0) ncl = 32;
+        if (dev >= 0 && dev < kMaxDevices) max_clusters[dev] = ncl;
+    }
+    const int grid = kRtCluster * static_cast<int>(tiles < ncl ? tiles : ncl);
+    router_logits_ref_kernel<<<grid, kRtThreads, kRtSmemBytes, st>>>(tn, tw, prm);
     return launch_status();
 }
 

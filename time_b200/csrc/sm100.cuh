@@ -94,6 +94,15 @@ __device__ __forceinline__ void tma_load_2d(const void* tmap, uint64_t* bar, voi
         :: "r"(smem_u32(dst)), "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar)) : "memory");
 }
 
+// 3-D tiled load (coordinates innermost first).
+__device__ __forceinline__ void tma_load_3d(const void* tmap, uint64_t* bar, void* dst,
+                                            int32_t x, int32_t y, int32_t z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];"
+        :: "r"(smem_u32(dst)), "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)) : "memory");
+}
+
 // Untiled bulk copy global -> shared (both 16-byte aligned, bytes % 16 == 0).
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile(
