@@ -100,8 +100,14 @@ typedef void* cbwLtMatmulPreference_t;
  * mode CBW_GEMM_DOWN_BF16: W[g] holds N rows; out[r][n] = bf16(acc).
  * Either mode may be or-ed with CBW_GEMM_SMALL_TILES (tiles of at most 32
  * rows and a deeper weight ring: the decode form) or CBW_GEMM_FULL_TILES;
- * without either, small tiles are used when rows <= 32 * num_groups.  Both
- * forms give the same result.
+ * without either, small tiles are used when rows <= 32 * num_groups.  The
+ * full form has two variants with bit-identical results: one SM per tile, and
+ * pairs of SMs (tcgen05 cta_group::2, 256 weight rows x up to 128 rows per
+ * instruction; needs K % 256 == 0 and, for the down mode, N % 256 == 0).  By
+ * default the gated mode runs on one SM and the down mode on pairs;
+ * CBW_GEMM_ONE_SM_TILES or CBW_GEMM_PAIR_TILES (instead of FULL) picks one.
+ * The decode form adds a row's K blocks in a different order from the full
+ * form, so its results differ from the full form's in the last bits.
  *
  * Requirements: K % 128 == 0, N % 128 == 0, start[g] % 16 == 0, every
  * segment [start, start + round_up(count,16)) inside [0, rows), a_ld (the
@@ -113,7 +119,9 @@ typedef enum {
     CBW_GEMM_GATED_SWIGLU = 0,
     CBW_GEMM_DOWN_BF16 = 1,
     CBW_GEMM_SMALL_TILES = 0x10,
-    CBW_GEMM_FULL_TILES = 0x20
+    CBW_GEMM_FULL_TILES = 0x20,
+    CBW_GEMM_ONE_SM_TILES = 0x40,
+    CBW_GEMM_PAIR_TILES = 0x80
 } cbwGemmMode_t;
 
 typedef struct {

@@ -459,6 +459,62 @@ def test_grouped_gemm_small_tiles(gpu, gated, counts):
 
 
 @pytest.mark.parametrize("gated", [False, True])
+@pytest.mark.parametrize("counts,K", [([16], 256), ([1, 0, 130, 255, 300, 17], 512), ([128] * 9 + [7], 768),
+                                      ([1000, 3, 129], 1536)])
+def test_grouped_gemm_pair_matches_one_sm(gpu, gated, counts, K):
+    """The full form on CTA pairs (tcgen05 cta_group::2) against the same form
+    on one SM per tile: identical bits, and both within the float64
+    reference's tolerance."""
+    N = 256
+    g = torch.Generator().manual_seed(101 + sum(counts) + gated)
+    starts, rows, A, A_s, a_ld, W, W_s = _make_groups(counts, K, 2 * N if gated else N, g)
+    cnt = torch.tensor(counts, dtype=torch.int32, device=gpu)
+    st = torch.tensor(starts, dtype=torch.int32, device=gpu)
+    outs = {}
+    for form in (M.GEMM_PAIR_TILES, M.GEMM_ONE_SM_TILES):
+        err = torch.zeros(1, dtype=torch.int32, device=gpu)
+        if gated:
+            hq = torch.full((rows, N), 0x55, dtype=torch.uint8, device=gpu)
+            hs = torch.full((N // 128, a_ld), -1.0, device=gpu)
+            M.grouped_gemm(M.GEMM_GATED_SWIGLU | form, A.to(gpu), A_s.to(gpu), a_ld, W.to(gpu), W_s.to(gpu), cnt, st,
+                           hq, hs, a_ld, K, N, rows, error_word=err)
+            torch.cuda.synchronize()
+            outs[form] = (hq.cpu(), hs.cpu())
+        else:
+            out = torch.full((rows, N), float("nan"), dtype=torch.bfloat16, device=gpu)
+            M.grouped_gemm(M.GEMM_DOWN_BF16 | form, A.to(gpu), A_s.to(gpu), a_ld, W.to(gpu), W_s.to(gpu), cnt, st,
+                           out, None, 0, K, N, rows, error_word=err)
+            torch.cuda.synchronize()
+            outs[form] = (out.cpu(),)
+        assert err.item() == 0, form
+    ref = _gemm_ref(A, A_s, W, W_s, starts, counts, K)
+    lut = _lut()
+    for gi, r in ref.items():
+        s0, c = starts[gi], counts[gi]
+        for form in outs:
+            if gated:
+                hq_c, hs_c = outs[form]
+                gte, up = r[:, :N].float(), r[:, N:]
+                h = (gte / (1 + torch.exp(-gte))).double() * up
+                deq = lut[hq_c[s0:s0 + c].long()] * hs_c[:, s0:s0 + c].T.double().repeat_interleave(128, 1)
+                assert (deq - h).abs().max() / h.abs().max() < 4e-2, (form, gi)
+                pad_end = s0 + (c + 15) // 16 * 16
+                assert (hq_c[s0 + c:pad_end] == 0).all() and (hs_c[:, s0 + c:pad_end] == 0).all()
+            else:
+                y = outs[form][0][s0:s0 + c].double()
+                assert torch.isfinite(y).all()
+                assert (y - r).abs().max() / r.abs().max() < 8e-3, (form, gi)
+        if gated:
+            a_, b_ = outs[M.GEMM_PAIR_TILES], outs[M.GEMM_ONE_SM_TILES]
+            assert torch.equal(a_[0][s0:s0 + c], b_[0][s0:s0 + c]), gi
+            assert torch.equal(a_[1][:, s0:s0 + c], b_[1][:, s0:s0 + c]), gi
+        else:
+            a_ = outs[M.GEMM_PAIR_TILES][0][s0:s0 + c].view(torch.int16)
+            b_ = outs[M.GEMM_ONE_SM_TILES][0][s0:s0 + c].view(torch.int16)
+            assert torch.equal(a_, b_), gi
+
+
+@pytest.mark.parametrize("gated", [False, True])
 def test_grouped_gemm_small_tiles_placement_independent(gpu, gated):
     """The decode form's result for a row does not depend on where its tile
     runs: the same expert groups, run (a) twice and (b) after two extra

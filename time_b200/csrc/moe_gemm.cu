@@ -39,6 +39,8 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 
+#include <cooperative_groups.h>
+
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -171,6 +173,8 @@ template <bool kGated, bool kSmall>
 __global__ void __launch_bounds__(kNumThreads, 1)
 grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
                         const __grid_constant__ CUtensorMap tmap_a,
+                        const __grid_constant__ CUtensorMap tmap_a64,
+                        const __grid_constant__ CUtensorMap tmap_a128,
                         const GemmParams p) {
     using C = GemmCfg<kGated, kSmall>;
     extern __shared__ uint8_t smem_raw[];
@@ -219,6 +223,8 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
         fence_mbar_init();
         prefetch_tmap(&tmap_w);
         prefetch_tmap(&tmap_a);
+        prefetch_tmap(&tmap_a64);
+        prefetch_tmap(&tmap_a128);
     }
     if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
     if (warp == 2) {
@@ -271,17 +277,24 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
             bool ok = true;
             for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
                 TileCoord tc = decode_tile(tile, t_prefix, t_chunks, t_start, counts_smem, G, C::kTileTok);
-                const int b_loads = (tc.ntile + 31) >> 5;
-                const uint32_t bytes = C::kABytes + b_loads * 32 * kBlockK;
+                // token rows in as few loads as the box sizes allow (each TMA instruction
+                // costs the SM's copy engine far more than its bytes): one box of 32, 64 or
+                // 128 rows, or 128-row boxes for down tiles of more than 128 rows
+                const int box = tc.ntile <= 32 ? 32 : (tc.ntile <= 64 ? 64 : 128);
+                const int b_loads = (tc.ntile + box - 1) / box;
+                const CUtensorMap* tmap_b = box == 32 ? &tmap_a : (box == 64 ? &tmap_a64 : &tmap_a128);
+                const uint32_t bytes = C::kABytes + b_loads * box * kBlockK;
                 const int wrow = tc.g * p.w_rows + tc.nb * kTileM;
                 for (int kb = 0; kb < KB; ++kb) {
                     if (!mbar_wait_bounded(&empty_bar[s], phase ^ 1, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
                     uint8_t* st = smem + C::kOffStages + s * C::kStageBytes;
                     mbar_arrive_expect_tx(&full_bar[s], bytes);
-                    tma_load_2d(&tmap_w, &full_bar[s], st, kb * kBlockK, wrow);
-                    if (kGated) tma_load_2d(&tmap_w, &full_bar[s], st + kTileM * kBlockK, kb * kBlockK, wrow + p.N);
+                    if (kGated)   // gate and up rows in one load: {K, rows, gate/up}
+                        tma_load_3d(&tmap_w, &full_bar[s], st, kb * kBlockK, wrow, 0);
+                    else
+                        tma_load_2d(&tmap_w, &full_bar[s], st, kb * kBlockK, wrow);
                     for (int r = 0; r < b_loads; ++r)
-                        tma_load_2d(&tmap_a, &full_bar[s], st + C::kABytes + r * 32 * kBlockK, kb * kBlockK, tc.row0 + 32 * r);
+                        tma_load_2d(tmap_b, &full_bar[s], st + C::kABytes + r * box * kBlockK, kb * kBlockK, tc.row0 + box * r);
                     armed_mask |= 1u << s;
                     armed_phase = (armed_phase & ~(1u << s)) | (phase << s);
                     if (++s == C::kStages) { s = 0; phase ^= 1; }
@@ -583,6 +596,506 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
     if (threadIdx.x == 0 && *abort_flag && p.error_word) atomicExch(p.error_word, 1);
 }
 
+// ------------------------------------------------------------------ full form on CTA pairs
+// The full form (tiles of up to 128 tokens) runs on CTA pairs: a cluster of two
+// CTAs on two SMs issues tcgen05.mma with cta_group::2, M = 256 weight rows x
+// N <= 128 tokens per instruction, from the even CTA.  Each CTA stages its own
+// 128 weight rows and half of the tile's token rows (the MMA reads both CTAs'
+// shared memory) and receives its 128 rows of the product in its own TMEM.
+//   gated: the pair covers output columns [128 nb, 128 nb + 128) of h; CTA r
+//          holds gate rows 128 nb + 64 r + [0, 64) in TMEM lanes 0-63 and the
+//          matching up rows in lanes 64-127, so SwiGLU stays inside the CTA.
+//          The 1x128 requantisation needs the token's amax over both CTAs'
+//          64 columns: the two CTAs swap their partial amax through
+//          distributed shared memory once per tile.
+//   down:  CTA r holds output rows 256 nb + 128 r + [0, 128).
+// Per K block each CTA promotes 128 lanes x N columns (16 warps x one 32-column
+// TMEM load), half of what one SM promotes in the one-SM form for the same
+// MMA work, and its operand stage is 24 KB instead of 48 KB, so the ring is
+// six stages deep.  Hand-offs: the even CTA's producer arms the stage's full
+// barrier with both CTAs' bytes and both CTAs' TMA loads complete on it; the
+// MMA commits release the operand stage and publish the TMEM buffer in both
+// CTAs (multicast commit); both CTAs' promotion warps release a TMEM buffer
+// on the even CTA's barrier.  Every wait is bounded as in the one-SM form.
+constexpr int kPairTok = 128;                               // tokens per tile (UMMA N)
+constexpr int kPairKbPerStage = 2;                          // K blocks per TMA load (one instruction each)
+constexpr int kPairStages = 3;
+constexpr int kPairSStages = 4;
+constexpr int kPairTBufs = 4;                               // 4 x 128 TMEM columns
+constexpr int kPairABytes = kTileM * kBlockK;               // this CTA's 128 weight rows, one K block
+constexpr int kPairBRows = kPairTok / 2;                    // this CTA's half of the tokens
+constexpr int kPairBBytes = kPairBRows * kBlockK;
+constexpr int kPairStageABytes = kPairKbPerStage * kPairABytes;   // [kb][128 rows][128 B]
+constexpr int kPairStageBytes = kPairStageABytes + kPairKbPerStage * kPairBBytes;   // 48 KB
+constexpr int kPairEpiBytes = kPairTok * 128 * 2;           // 32 KB: gated [128 tok][64] fp32, down [128][128] bf16
+// scale ring entry: raw token scales [kb][128] (TMA), then the folded [kb][gate, up][128]
+constexpr int kPairScaleRaw = kPairKbPerStage * kPairTok;
+constexpr int kPairScaleFloats = kPairScaleRaw + kPairKbPerStage * 2 * kPairTok;
+constexpr int kPairOffStages = 0;
+constexpr int kPairOffEpi = kPairOffStages + kPairStages * kPairStageBytes;
+constexpr int kPairOffScale = kPairOffEpi + kPairEpiBytes;
+constexpr int kPairOffAmax = kPairOffScale + kPairSStages * kPairScaleFloats * 4;   // own[128], peer[2][128]
+constexpr int kPairOffTables = kPairOffAmax + 3 * kPairTok * 4;
+constexpr int kPairOffBars = kPairOffTables + (4 * kMaxGroups + 2) * 4;
+constexpr int kPairNumBars = 2 * kPairStages + 3 * kPairSStages + 2 * kPairTBufs + 1 + 2;
+constexpr int kPairOffMisc = kPairOffBars + kPairNumBars * 8;
+constexpr int kPairSmemBytes = kPairOffMisc + 64 + 1024;
+static_assert(kPairOffBars % 8 == 0, "mbarrier alignment");
+static_assert(kPairStageBytes % 1024 == 0 && kPairStageABytes % 1024 == 0, "swizzled tiles on 1024-byte boundaries");
+static_assert((kPairScaleFloats * 4) % 128 == 0, "scale entries 128-byte aligned");
+static_assert(kPairTBufs * kPairTok <= kTmemCols, "TMEM buffers");
+static_assert(kPairSmemBytes <= 227 * 1024, "shared memory budget");
+
+struct PairParams {
+    GemmParams g;
+    int I;     // gated: intermediate size (up rows start at I within a group)
+};
+
+__device__ __forceinline__ void tma_load_3d_pair(const void* tmap, uint32_t bar_cluster, void* dst,
+                                                 int32_t x, int32_t y, int32_t z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];"
+        :: "r"(smem_u32(dst)), "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(bar_cluster) : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_3d(const void* tmap, int32_t x, int32_t y, int32_t z) {
+    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global [%0, {%1, %2, %3}];"
+                 :: "l"(tmap), "r"(x), "r"(y), "r"(z) : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_4d(const void* tmap, int32_t x, int32_t y, int32_t z, int32_t w) {
+    asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global [%0, {%1, %2, %3, %4}];"
+                 :: "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
+}
+constexpr int kPairPrefetch = 4;     // stages of weights fetched into L2 ahead of the ring
+
+__device__ __forceinline__ void tma_load_4d_pair(const void* tmap, uint32_t bar_cluster, void* dst,
+                                                 int32_t x, int32_t y, int32_t z, int32_t w) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5}], [%6];"
+        :: "r"(smem_u32(dst)), "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(w), "r"(bar_cluster) : "memory");
+}
+
+template <bool kGated>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kNumThreads, 1)
+grouped_fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_a,
+                             const __grid_constant__ CUtensorMap tmap_s, const PairParams pp) {
+    const GemmParams& p = pp.g;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+
+    float* scale_ring = reinterpret_cast<float*>(smem + kPairOffScale);
+    float* amax_own = reinterpret_cast<float*>(smem + kPairOffAmax);
+    float* amax_peer = amax_own + kPairTok;                                  // [2][128], written by the peer
+    int* t_prefix = reinterpret_cast<int*>(smem + kPairOffTables);
+    int* t_chunks = t_prefix + (kMaxGroups + 1);
+    int* t_start = t_chunks + kMaxGroups;
+    int* counts_smem = t_start + kMaxGroups;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kPairOffBars);
+    uint64_t* full_bar = bars;                              // used in the even CTA
+    uint64_t* empty_bar = full_bar + kPairStages;
+    uint64_t* sfull_bar = empty_bar + kPairStages;
+    uint64_t* sempty_bar = sfull_bar + kPairSStages;
+    uint64_t* cready_bar = sempty_bar + kPairSStages;
+    uint64_t* tfull_bar = cready_bar + kPairSStages;
+    uint64_t* tempty_bar = tfull_bar + kPairTBufs;          // used in the even CTA
+    uint64_t* epi_bar = tempty_bar + kPairTBufs;
+    uint64_t* xbar = epi_bar + 1;                           // [2]: the peer's amax has landed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kPairOffMisc);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kPairOffMisc + 8);
+
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    const uint32_t rank = cluster.block_rank();             // 0: issues the MMAs
+    const uint32_t peer = rank ^ 1u;
+    const int cid = blockIdx.x >> 1, ncl = gridDim.x >> 1;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int G = p.G;
+    const int KB = p.K / kBlockK;
+    const int KS = KB / kPairKbPerStage;                   // stages per tile
+
+    // ---------------------------------------------------------------- setup
+    if (warp == 0 && lane == 0) {
+        for (int s = 0; s < kPairStages; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1);
+        }
+        for (int s = 0; s < kPairSStages; ++s) {
+            mbar_init(&sfull_bar[s], 1);
+            mbar_init(&sempty_bar[s], kNumPromoWarps);
+            mbar_init(&cready_bar[s], 1);
+        }
+        for (int b = 0; b < kPairTBufs; ++b) {
+            mbar_init(&tfull_bar[b], 1);
+            mbar_init(&tempty_bar[b], 2 * kNumPromoWarps);
+        }
+        mbar_init(epi_bar, kNumPromoWarps);
+        mbar_init(&xbar[0], kNumPromoWarps);
+        mbar_init(&xbar[1], kNumPromoWarps);
+        *abort_flag = 0;
+        fence_mbar_init();
+        prefetch_tmap(&tmap_w);
+        prefetch_tmap(&tmap_a);
+        prefetch_tmap(&tmap_s);
+    }
+    if (warp == 1) tmem_alloc_pair(tmem_slot, kTmemCols);
+    if (warp == 2) {
+        const int nbt = kGated ? p.N / 128 : p.N / 256;     // pair row blocks per group
+        int per_lane = (G + 31) / 32;
+        int g0 = lane * per_lane;
+        int local = 0;
+        for (int i = 0; i < per_lane; ++i) {
+            int g = g0 + i;
+            if (g < G) {
+                int cnt = p.count[g];
+                int ch = (cnt + kPairTok - 1) / kPairTok;
+                t_chunks[g] = ch;
+                t_start[g] = p.start[g];
+                counts_smem[g] = cnt;
+                local += ch * nbt;
+            }
+        }
+        int incl = local;
+        for (int o = 1; o < 32; o <<= 1) {
+            int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        int run = incl - local;
+        for (int i = 0; i < per_lane; ++i) {
+            int g = g0 + i;
+            if (g < G) {
+                t_prefix[g] = run;
+                run += t_chunks[g] * nbt;
+            }
+        }
+        if (lane == 31) t_prefix[G] = incl;
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster.sync();          // both CTAs' barriers are initialised before any cross-CTA traffic
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int total_tiles = t_prefix[G];
+    const uint16_t both = 0x3;
+
+    if (warp < kFirstPromoWarp) {
+      asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" :: "n"(kRoleRegs));
+      if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer (both CTAs)
+        // per stage (two K blocks): one load of this CTA's weight rows, one of its
+        // token rows, one of the tile's raw token scales
+        if (lane == 0) {
+            int s = 0, ss = 0;
+            uint32_t phase = 0, sphase = 0;
+            uint32_t sarmed_mask = 0, sarmed_phase = 0;
+            uint32_t full_leader[kPairStages];
+            for (int i = 0; i < kPairStages; ++i) full_leader[i] = mapa_u32(smem_u32(&full_bar[i]), 0);
+            bool ok = true;
+            bool issued = false;
+            // weights arrive from HBM: fetch them into L2 kPairPrefetch stages ahead of
+            // the ring (no shared memory), so the ring's loads mostly hit L2
+            int pf_tile = cid, pf_ks = 0;
+            auto pf_row = [&](int tile) {
+                TileCoord t2 = decode_tile(tile, t_prefix, t_chunks, t_start, counts_smem, G, kPairTok);
+                return kGated ? t2.g * p.w_rows + t2.nb * 128 + 64 * static_cast<int>(rank)
+                              : t2.g * p.w_rows + t2.nb * 256 + 128 * static_cast<int>(rank);
+            };
+            int pf_wrow = pf_tile < total_tiles ? pf_row(pf_tile) : 0;
+            auto prefetch_next = [&]() {
+                if (pf_tile >= total_tiles) return;
+                if (kGated) tma_prefetch_4d(&tmap_w, 0, pf_wrow, 0, pf_ks * kPairKbPerStage);
+                else tma_prefetch_3d(&tmap_w, 0, pf_wrow, pf_ks * kPairKbPerStage);
+                if (++pf_ks == KS) {
+                    pf_ks = 0;
+                    pf_tile += ncl;
+                    if (pf_tile < total_tiles) pf_wrow = pf_row(pf_tile);
+                }
+            };
+            for (int i = 0; i < kPairPrefetch; ++i) prefetch_next();
+            for (int tile = cid; tile < total_tiles && ok; tile += ncl) {
+                TileCoord tc = decode_tile(tile, t_prefix, t_chunks, t_start, counts_smem, G, kPairTok);
+                const int half = tc.ntile >> 1;
+                const int wrow = kGated ? tc.g * p.w_rows + tc.nb * 128 + 64 * static_cast<int>(rank)
+                                        : tc.g * p.w_rows + tc.nb * 256 + 128 * static_cast<int>(rank);
+                for (int ks = 0; ks < KS; ++ks) {
+                    const int kb0 = ks * kPairKbPerStage;
+                    prefetch_next();
+                    if (!mbar_wait_bounded(&empty_bar[s], phase ^ 1, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
+                    uint8_t* st = smem + kPairOffStages + s * kPairStageBytes;
+                    if (rank == 0) mbar_arrive_expect_tx(&full_bar[s], 2 * kPairStageBytes);
+                    if (kGated)   // {128 B, 64 rows, gate/up, 2 K blocks}
+                        tma_load_4d_pair(&tmap_w, full_leader[s], st, 0, wrow, 0, kb0);
+                    else          // {128 B, 128 rows, 2 K blocks}
+                        tma_load_3d_pair(&tmap_w, full_leader[s], st, 0, wrow, kb0);
+                    tma_load_3d_pair(&tmap_a, full_leader[s], st + kPairStageABytes, 0,
+                                     tc.row0 + static_cast<int>(rank) * half, kb0);
+                    issued = true;
+                    if (++s == kPairStages) { s = 0; phase ^= 1; }
+
+                    if (!mbar_wait_bounded(&sempty_bar[ss], sphase ^ 1, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&sfull_bar[ss], kPairScaleRaw * 4);
+                    tma_load_2d(&tmap_s, &sfull_bar[ss], scale_ring + ss * kPairScaleFloats, tc.row0, kb0);
+                    sarmed_mask |= 1u << ss;
+                    sarmed_phase = (sarmed_phase & ~(1u << ss)) | (sphase << ss);
+                    if (++ss == kPairSStages) { ss = 0; sphase ^= 1; }
+                }
+            }
+            if (!ok) {
+                // this CTA's operand copies complete on the even CTA's barrier: give
+                // them time to land before the CTA can leave (they take microseconds)
+                if (issued) {
+                    const uint64_t t0 = globaltimer_ns();
+                    while (globaltimer_ns() - t0 < 20000000ull) { }
+                }
+                for (int i = 0; i < kPairSStages; ++i)
+                    if (sarmed_mask & (1u << i)) mbar_drain(&sfull_bar[i], (sarmed_phase >> i) & 1u);
+            }
+        }
+      } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer (even CTA)
+        if (rank == 0 && lane == 0) {
+            int s = 0, b = 0;
+            uint32_t phase = 0, tphase = 0;
+            bool ok = true;
+            bool issued = false;
+            for (int tile = cid; tile < total_tiles && ok; tile += ncl) {
+                TileCoord tc = decode_tile(tile, t_prefix, t_chunks, t_start, counts_smem, G, kPairTok);
+                const uint32_t idesc = idesc_e4m3_f32(2 * kTileM, tc.ntile);
+                for (int ks = 0; ks < KS && ok; ++ks) {
+                    if (!mbar_wait_bounded(&full_bar[s], phase, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
+                    const uint32_t st_addr = smem_u32(smem + kPairOffStages + s * kPairStageBytes);
+                    for (int h = 0; h < kPairKbPerStage; ++h) {
+                        if (!mbar_wait_bounded(&tempty_bar[b], tphase ^ 1, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
+                        tc_fence_after();
+                        const uint32_t a_addr = st_addr + h * kPairABytes;
+                        const uint32_t b_addr = st_addr + kPairStageABytes + h * kPairBBytes;
+                        const uint32_t d = tmem_base + b * kPairTok;
+#pragma unroll
+                        for (int k = 0; k < kBlockK / 32; ++k)
+                            umma_f8_pair(d, umma_desc_sw128(a_addr + k * 32), umma_desc_sw128(b_addr + k * 32), idesc,
+                                         k > 0 ? 1u : 0u);
+                        umma_commit_pair(&tfull_bar[b], both);
+                        issued = true;
+                        if (++b == kPairTBufs) { b = 0; tphase ^= 1; }
+                    }
+                    if (!ok) break;
+                    umma_commit_pair(&empty_bar[s], both);
+                    if (++s == kPairStages) { s = 0; phase ^= 1; }
+                }
+            }
+            if (!ok && issued) {
+                int lb = (b + kPairTBufs - 1) % kPairTBufs;
+                uint32_t lph = (b == 0) ? (tphase ^ 1) : tphase;
+                mbar_drain(&tfull_bar[lb], lph);
+            }
+        }
+      } else if (warp == 2) {
+        // ------------------------------------------------------------ scale folding (both CTAs)
+        // c[kb][gate|up][n] = raw[kb][n] * w_scale (this CTA's weight block(s)), per stage
+        int ss = 0;
+        uint32_t sphase = 0;
+        bool ok = true;
+        const int wsb = p.w_rows / kTileM;                 // scale blocks per group
+        for (int tile = cid; tile < total_tiles && ok; tile += ncl) {
+            TileCoord tc = decode_tile(tile, t_prefix, t_chunks, t_start, counts_smem, G, kPairTok);
+            // gated: gate block nb, up block I/128 + nb; down: block 2 nb + rank
+            const int blk0 = kGated ? tc.nb : 2 * tc.nb + static_cast<int>(rank);
+            const float* wsg = p.w_scale + ((size_t)tc.g * wsb + blk0) * KB;
+            const float* wsu = p.w_scale + ((size_t)tc.g * wsb + (pp.I / kTileM) + tc.nb) * KB;
+            for (int ks = 0; ks < KS; ++ks) {
+                float sg[kPairKbPerStage], su[kPairKbPerStage];
+#pragma unroll
+                for (int h = 0; h < kPairKbPerStage; ++h) {
+                    sg[h] = __ldg(wsg + ks * kPairKbPerStage + h);
+                    su[h] = kGated ? __ldg(wsu + ks * kPairKbPerStage + h) : 0.0f;
+                }
+                if (!mbar_wait_bounded(&sfull_bar[ss], sphase, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
+                float* e = scale_ring + ss * kPairScaleFloats;
+#pragma unroll
+                for (int h = 0; h < kPairKbPerStage; ++h) {
+                    float* f = e + kPairScaleRaw + h * 2 * kPairTok;
+                    for (int c = lane; c < tc.ntile; c += 32) {
+                        const float a = e[h * kPairTok + c];
+                        f[c] = a * sg[h];
+                        if (kGated) f[kPairTok + c] = a * su[h];
+                    }
+                }
+                // the raw scales are overwritten by the next TMA load into this entry
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&cready_bar[ss]);
+                if (++ss == kPairSStages) { ss = 0; sphase ^= 1; }
+            }
+        }
+      }
+    } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" :: "n"(kPromoRegs));
+        // ------------------------------------------------------------ promotion + epilogue (both CTAs)
+        const int pw = warp - kFirstPromoWarp;        // 0..15
+        const int quarter = warp & 3;                  // TMEM lane quarter
+        const int colgrp = pw >> 2;                    // token columns [32 colgrp, +32)
+        const int lane_row = quarter * 32 + lane;      // TMEM lane = this CTA's weight row
+        const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+        const uint32_t tempty_leader0 = mapa_u32(smem_u32(&tempty_bar[0]), 0);
+        const uint32_t xbar_peer0 = mapa_u32(smem_u32(&xbar[0]), peer);
+        float* amax_peer_remote = cluster.map_shared_rank(amax_peer, peer);   // the peer's copy of amax_peer
+        int ss = 0, b = 0;
+        uint32_t sphase = 0, tphase = 0, ephase = 0;
+        uint32_t xphase[2] = {0, 0};
+        bool ok = true;
+        int it = 0;
+        auto group_sync = [&]() -> bool {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(epi_bar);
+            const bool r = mbar_wait_bounded(epi_bar, ephase, abort_flag, kWaitTimeoutNs);
+            ephase ^= 1;
+            return r;
+        };
+
+        for (int tile = cid; tile < total_tiles && ok; tile += ncl, ++it) {
+            TileCoord tc = decode_tile(tile, t_prefix, t_chunks, t_start, counts_smem, G, kPairTok);
+            const bool live = colgrp * 32 < tc.ntile;
+            float2 acc2[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) acc2[i] = make_float2(0.0f, 0.0f);
+            // gated: lanes 0-63 hold gate rows, 64-127 up rows (their own scale vector)
+            const int cofs = (kGated && quarter >= 2 ? kPairTok : 0) + colgrp * 32;
+            for (int kb = 0; kb < KB; ++kb) {
+                const int h = kb % kPairKbPerStage;
+                if (h == 0 && !mbar_wait_bounded(&cready_bar[ss], sphase, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
+                if (!mbar_wait_bounded(&tfull_bar[b], tphase, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
+                tc_fence_after();
+                if (live) {
+                    uint32_t v[32];
+                    tmem_ld32(lane_addr + b * kPairTok + colgrp * 32, v);
+                    const float* cs = scale_ring + ss * kPairScaleFloats + kPairScaleRaw + h * 2 * kPairTok + cofs;
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4) {
+                        const float4 c4 = *reinterpret_cast<const float4*>(cs + j);
+                        acc2[j / 2] = ffma2(make_float2(__uint_as_float(v[j]), __uint_as_float(v[j + 1])),
+                                            make_float2(c4.x, c4.y), acc2[j / 2]);
+                        acc2[j / 2 + 1] = ffma2(make_float2(__uint_as_float(v[j + 2]), __uint_as_float(v[j + 3])),
+                                                make_float2(c4.z, c4.w), acc2[j / 2 + 1]);
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive_cluster(tempty_leader0 + b * 8);
+                    if (h == kPairKbPerStage - 1) mbar_arrive(&sempty_bar[ss]);
+                }
+                if (h == kPairKbPerStage - 1 && ++ss == kPairSStages) { ss = 0; sphase ^= 1; }
+                if (++b == kPairTBufs) { b = 0; tphase ^= 1; }
+            }
+            if (!ok || *abort_flag) { ok = false; break; }
+
+            // ---------------------------------------------------------- epilogue
+            // acc2[i] holds token columns 32 colgrp + 2i, + 1 of this lane's row
+            if (kGated) {
+                float* hbuf = reinterpret_cast<float*>(smem + kPairOffEpi);   // [128 tokens][64 rows]
+                if (quarter >= 2 && live) {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        hbuf[(colgrp * 32 + 2 * i) * 64 + lane_row - 64] = acc2[i].x;
+                        hbuf[(colgrp * 32 + 2 * i + 1) * 64 + lane_row - 64] = acc2[i].y;
+                    }
+                }
+                if (!group_sync()) { ok = false; break; }
+                if (quarter < 2 && live) {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+#pragma unroll
+                        for (int h2 = 0; h2 < 2; ++h2) {
+                            const int c = colgrp * 32 + 2 * i + h2;
+                            const float g = h2 ? acc2[i].y : acc2[i].x;
+                            const float u = hbuf[c * 64 + lane_row];
+                            hbuf[c * 64 + lane_row] = (g / (1.0f + expf(-g))) * u;
+                        }
+                    }
+                }
+                if (!group_sync()) { ok = false; break; }
+                // per token: amax over this CTA's 64 columns; swap with the peer
+                const int par = it & 1;
+                for (int c = pw; c < kPairTok; c += kNumPromoWarps) {
+                    float a = 0.0f;
+                    if (c < tc.nrows) a = fmaxf(fabsf(hbuf[c * 64 + lane]), fabsf(hbuf[c * 64 + lane + 32]));
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+                    if (lane == 0) {
+                        amax_own[c] = a;
+                        amax_peer_remote[par * kPairTok + c] = a;
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive_release_cluster(xbar_peer0 + par * 8);
+                {
+                    // the peer's 16 warps have written their amax into amax_peer[par]
+                    bool got = mbar_try_wait_cluster(&xbar[par], xphase[par]);
+                    const uint64_t t0 = globaltimer_ns();
+                    while (!got) {
+                        if (*abort_flag) break;
+                        if (globaltimer_ns() - t0 > kWaitTimeoutNs) { *abort_flag = 1; break; }
+                        got = mbar_try_wait_cluster(&xbar[par], xphase[par]);
+                    }
+                    xphase[par] ^= 1;
+                    if (!got) { ok = false; break; }
+                }
+                uint8_t* outq = reinterpret_cast<uint8_t*>(p.out);
+                const int col0 = tc.nb * 128 + 64 * static_cast<int>(rank);
+                for (int c = pw; c < tc.ntile; c += kNumPromoWarps) {
+                    const size_t row = static_cast<size_t>(tc.row0 + c);
+                    uint8_t q0 = 0, q1 = 0;
+                    float scale = 0.0f;
+                    if (c < tc.nrows) {
+                        const float amax = fmaxf(amax_own[c], amax_peer[par * kPairTok + c]);
+                        if (amax > 0.0f) {
+                            const float inv = 448.0f / amax;
+                            const uint16_t q = cvt_e4m3x2(hbuf[c * 64 + lane] * inv, hbuf[c * 64 + lane + 32] * inv);
+                            q0 = static_cast<uint8_t>(q & 0xFF);
+                            q1 = static_cast<uint8_t>(q >> 8);
+                            scale = amax / 448.0f;
+                        }
+                    }
+                    outq[row * p.N + col0 + lane] = q0;
+                    outq[row * p.N + col0 + 32 + lane] = q1;
+                    if (rank == 0 && lane == 0) p.out_scale[(size_t)tc.nb * p.out_ld + row] = scale;
+                }
+                if (!group_sync()) { ok = false; break; }
+            } else {
+                __nv_bfloat16* stage = reinterpret_cast<__nv_bfloat16*>(smem + kPairOffEpi);   // [128 tok][128]
+                if (live) {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        stage[(colgrp * 32 + 2 * i) * 128 + lane_row] = __float2bfloat16_rn(acc2[i].x);
+                        stage[(colgrp * 32 + 2 * i + 1) * 128 + lane_row] = __float2bfloat16_rn(acc2[i].y);
+                    }
+                }
+                if (!group_sync()) { ok = false; break; }
+                __nv_bfloat16* outy = reinterpret_cast<__nv_bfloat16*>(p.out);
+                const int col0 = tc.nb * 256 + 128 * static_cast<int>(rank);
+                for (int c = pw; c < tc.nrows; c += kNumPromoWarps) {
+                    const uint2 v = *reinterpret_cast<const uint2*>(stage + c * 128 + lane * 4);
+                    *reinterpret_cast<uint2*>(outy + static_cast<size_t>(tc.row0 + c) * p.N + col0 + lane * 4) = v;
+                }
+                if (!group_sync()) { ok = false; break; }
+            }
+        }
+    }
+
+    // ---------------------------------------------------------------- teardown
+    tc_fence_before();
+    __syncthreads();
+    cluster.sync();          // the even CTA's MMAs into this CTA's TMEM and all cross-CTA arrivals are done
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, kTmemCols);
+    }
+    if (threadIdx.x == 0 && *abort_flag && p.error_word) atomicExch(p.error_word, 1);
+}
+
 // ------------------------------------------------------------------ host side
 
 PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
@@ -614,13 +1127,35 @@ bool encode_u8_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t co
     return r == CUDA_SUCCESS;
 }
 
+// Gate and up weight rows of a group as one 3-D tensor {K, rows, gate/up}
+// (the up row of gate row r is r + N): box {128, 128, 2}, 128-byte swizzle.
+bool encode_gate_up_3d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t K, uint64_t N) {
+    auto fn = get_encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {K, rows, 2};
+    cuuint64_t strides[2] = {K, N * K};
+    cuuint32_t box[3] = {128, kTileM, 2};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <bool kGated, bool kSmall>
 cbwStatus_t launch_gemm(const cbwGroupedGemmArgs* a, int* error_word, cudaStream_t stream) {
     using C = GemmCfg<kGated, kSmall>;
     const int w_rows = kGated ? 2 * a->N : a->N;
-    CUtensorMap tw, ta;
-    if (!encode_u8_2d(&tw, a->w, static_cast<uint64_t>(a->num_groups) * w_rows, a->K, kTileM)) return CBW_ERROR_INTERNAL;
-    if (!encode_u8_2d(&ta, a->a, static_cast<uint64_t>(a->rows), a->K, 32)) return CBW_ERROR_INTERNAL;
+    CUtensorMap tw, ta, ta64, ta128;
+    if (kGated) {
+        if (!encode_gate_up_3d(&tw, a->w, static_cast<uint64_t>(a->num_groups) * w_rows, a->K, a->N))
+            return CBW_ERROR_INTERNAL;
+    } else if (!encode_u8_2d(&tw, a->w, static_cast<uint64_t>(a->num_groups) * w_rows, a->K, kTileM)) {
+        return CBW_ERROR_INTERNAL;
+    }
+    if (!encode_u8_2d(&ta, a->a, static_cast<uint64_t>(a->rows), a->K, 32) ||
+        !encode_u8_2d(&ta64, a->a, static_cast<uint64_t>(a->rows), a->K, 64) ||
+        !encode_u8_2d(&ta128, a->a, static_cast<uint64_t>(a->rows), a->K, 128))
+        return CBW_ERROR_INTERNAL;
 
     static int sm_count[kMaxDevices] = {};
     static bool attr_set[kMaxDevices] = {};
@@ -655,7 +1190,7 @@ cbwStatus_t launch_gemm(const cbwGroupedGemmArgs* a, int* error_word, cudaStream
     p.N = a->N;
     p.w_rows = w_rows;
     p.error_word = error_word;
-    grouped_fp8_gemm_kernel<kGated, kSmall><<<sms, kNumThreads, C::kSmemBytes, stream>>>(tw, ta, p);
+    grouped_fp8_gemm_kernel<kGated, kSmall><<<sms, kNumThreads, C::kSmemBytes, stream>>>(tw, ta, ta64, ta128, p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         cudaFuncAttributes fa;
@@ -663,6 +1198,105 @@ cbwStatus_t launch_gemm(const cbwGroupedGemmArgs* a, int* error_word, cudaStream
         std::fprintf(stderr,
                      "cbwFp8BlockScaledGroupedGemm: launch failed: %s (regs %d, max threads %d, smem %d B)\n",
                      cudaGetErrorString(e), fa.numRegs, fa.maxThreadsPerBlock, C::kSmemBytes);
+        return CBW_ERROR_EXECUTION_FAILED;
+    }
+    return CBW_SUCCESS;
+}
+
+// Tensor maps of the pair form: every load moves two K blocks.
+//   weights, gated: {128 B, rows, gate/up (I rows apart), K blocks} box {128, 64, 2, 2}
+//   weights, down:  {128 B, rows, K blocks} box {128, 128, 2}
+//   tokens:         {128 B, rows, K blocks} box {128, 64, 2}
+//   token scales:   fp32 {a_ld, K blocks} box {128, 2}
+bool encode_pair_maps(const cbwGroupedGemmArgs* a, bool gated, CUtensorMap* tw, CUtensorMap* ta, CUtensorMap* ts) {
+    auto fn = get_encode_fn();
+    if (!fn) return false;
+    const cuuint64_t K = static_cast<cuuint64_t>(a->K), KB = K / 128;
+    const cuuint64_t wrows = static_cast<cuuint64_t>(a->num_groups) * (gated ? 2 * a->N : a->N);
+    cuuint32_t es[4] = {1, 1, 1, 1};
+    CUresult r;
+    if (gated) {
+        cuuint64_t dims[4] = {128, wrows, 2, KB};
+        cuuint64_t str[3] = {K, static_cast<cuuint64_t>(a->N) * K, 128};
+        cuuint32_t box[4] = {128, 64, 2, static_cast<cuuint32_t>(kPairKbPerStage)};
+        r = fn(tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(a->w), dims, str, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    } else {
+        cuuint64_t dims[3] = {128, wrows, KB};
+        cuuint64_t str[2] = {K, 128};
+        cuuint32_t box[3] = {128, 128, static_cast<cuuint32_t>(kPairKbPerStage)};
+        r = fn(tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(a->w), dims, str, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    }
+    if (r != CUDA_SUCCESS) return false;
+    {
+        cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(a->rows), KB};
+        cuuint64_t str[2] = {K, 128};
+        cuuint32_t box[3] = {128, static_cast<cuuint32_t>(kPairBRows), static_cast<cuuint32_t>(kPairKbPerStage)};
+        if (fn(ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(a->a), dims, str, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return false;
+    }
+    {
+        cuuint64_t dims[2] = {static_cast<cuuint64_t>(a->a_ld), KB};
+        cuuint64_t str[1] = {static_cast<cuuint64_t>(a->a_ld) * 4};
+        cuuint32_t box[2] = {static_cast<cuuint32_t>(kPairTok), static_cast<cuuint32_t>(kPairKbPerStage)};
+        if (fn(ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(a->a_scale), dims, str, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return false;
+    }
+    return true;
+}
+
+template <bool kGated>
+cbwStatus_t launch_gemm_pair(const cbwGroupedGemmArgs* a, int* error_word, cudaStream_t stream) {
+    const int w_rows = kGated ? 2 * a->N : a->N;
+    CUtensorMap tw, ta, ts;
+    if (!encode_pair_maps(a, kGated, &tw, &ta, &ts)) return CBW_ERROR_INTERNAL;
+    static int sm_count[kMaxDevices] = {};
+    static bool attr_set[kMaxDevices] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int sms = 0;
+    if (dev >= 0 && dev < kMaxDevices && sm_count[dev] > 0) {
+        sms = sm_count[dev];
+    } else {
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (dev >= 0 && dev < kMaxDevices) sm_count[dev] = sms;
+    }
+    {
+        cudaError_t e = smem_optin_once(grouped_fp8_gemm_pair_kernel<kGated>, kPairSmemBytes, attr_set);
+        if (e != cudaSuccess) {
+            std::fprintf(stderr, "cbwFp8BlockScaledGroupedGemm: shared memory opt-in (%d B) failed: %s\n",
+                         kPairSmemBytes, cudaGetErrorString(e));
+            return CBW_ERROR_EXECUTION_FAILED;
+        }
+    }
+    PairParams pp;
+    GemmParams& p = pp.g;
+    p.a_scale = a->a_scale;
+    p.a_ld = a->a_ld;
+    p.w_scale = a->w_scale;
+    p.count = a->count;
+    p.start = a->start;
+    p.out = a->out;
+    p.out_scale = a->out_scale;
+    p.out_ld = a->out_ld;
+    p.G = a->num_groups;
+    p.K = a->K;
+    p.N = a->N;
+    p.w_rows = w_rows;
+    p.error_word = error_word;
+    pp.I = a->N;
+    const int grid = (sms / 2) * 2;
+    grouped_fp8_gemm_pair_kernel<kGated><<<grid, kNumThreads, kPairSmemBytes, stream>>>(tw, ta, ts, pp);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        std::fprintf(stderr, "cbwFp8BlockScaledGroupedGemm: pair launch failed: %s\n", cudaGetErrorString(e));
         return CBW_ERROR_EXECUTION_FAILED;
     }
     return CBW_SUCCESS;
@@ -682,17 +1316,32 @@ extern "C" cbwStatus_t cbwFp8BlockScaledGroupedGemm(const cbwGroupedGemmArgs* ar
          reinterpret_cast<uintptr_t>(a.a_scale) | reinterpret_cast<uintptr_t>(a.out)) & 15)
         return CBW_ERROR_INVALID_VALUE;
     const int base = a.mode & 0xF, tiles = a.mode & ~0xF;
-    if (tiles != 0 && tiles != CBW_GEMM_SMALL_TILES && tiles != CBW_GEMM_FULL_TILES) return CBW_ERROR_INVALID_VALUE;
+    if (tiles != 0 && tiles != CBW_GEMM_SMALL_TILES && tiles != CBW_GEMM_FULL_TILES && tiles != CBW_GEMM_ONE_SM_TILES &&
+        tiles != CBW_GEMM_PAIR_TILES)
+        return CBW_ERROR_INVALID_VALUE;
     // 32-token tiles when the padded rows average at most 32 per group (decode
     // batches: a few tokens per expert), full tiles otherwise
     const bool small = tiles == CBW_GEMM_SMALL_TILES ||
                        (tiles == 0 && static_cast<long long>(a.rows) <= 32ll * a.num_groups);
+    if ((tiles == CBW_GEMM_ONE_SM_TILES || tiles == CBW_GEMM_PAIR_TILES) && small) return CBW_ERROR_INVALID_VALUE;
+    const bool pair_ok = a.K % (kPairKbPerStage * kBlockK) == 0 && (base == CBW_GEMM_GATED_SWIGLU || a.N % 256 == 0);
+    if (tiles == CBW_GEMM_PAIR_TILES && !pair_ok) return CBW_ERROR_INVALID_VALUE;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // The full form's default: the gated projection on one SM per tile, the down
+    // projection on CTA pairs (measured faster at the GLM shape, 4096 tokens:
+    // gate/up 1.27 ms one-SM vs 1.87 ms paired -- the paired tile's cross-CTA amax
+    // exchange and SwiGLU staging cost more than its halved MMA count saves;
+    // down 0.84 ms one-SM vs 0.79 ms paired).
+    const bool pair = tiles == CBW_GEMM_PAIR_TILES ||
+                      (tiles != CBW_GEMM_ONE_SM_TILES && base == CBW_GEMM_DOWN_BF16 && pair_ok);
     if (base == CBW_GEMM_GATED_SWIGLU) {
         if (!a.out_scale || a.out_ld < a.rows) return CBW_ERROR_INVALID_VALUE;
-        return small ? launch_gemm<true, true>(&a, error_word, st) : launch_gemm<true, false>(&a, error_word, st);
+        if (small) return launch_gemm<true, true>(&a, error_word, st);
+        return pair ? launch_gemm_pair<true>(&a, error_word, st) : launch_gemm<true, false>(&a, error_word, st);
     }
-    if (base == CBW_GEMM_DOWN_BF16)
-        return small ? launch_gemm<false, true>(&a, error_word, st) : launch_gemm<false, false>(&a, error_word, st);
+    if (base == CBW_GEMM_DOWN_BF16) {
+        if (small) return launch_gemm<false, true>(&a, error_word, st);
+        return pair ? launch_gemm_pair<false>(&a, error_word, st) : launch_gemm<false, false>(&a, error_word, st);
+    }
     return CBW_ERROR_INVALID_VALUE;
 }

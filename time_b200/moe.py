@@ -52,6 +52,8 @@ GEMM_GATED_SWIGLU = 0
 GEMM_DOWN_BF16 = 1
 GEMM_SMALL_TILES = 0x10   # or-ed into a mode: the decode form (tiles of <= 32 rows)
 GEMM_FULL_TILES = 0x20
+GEMM_ONE_SM_TILES = 0x40  # the full form on one SM per tile
+GEMM_PAIR_TILES = 0x80    # the full form on pairs of SMs (tcgen05 cta_group::2)
 
 _bound = False
 
