@@ -182,11 +182,32 @@ moe_status_t moe_rmsnorm_quant_n(const void* x_bf16, const float* gamma, int T, 
                                  float* rms_out, float* n_out, void* xq_out, float* xs_out,
                                  int xs_ld, cwStream_t stream);
 
-/* Router logits from the stored n: logits[t][e] = fma-chain over
- * i = 0..H-1 of n[t][i]*W[e][i] from +0.0f (+ bias[e]) -- bit-identical to
- * the logits moe_router_topk computes; H a multiple of 128, E <= 256. */
+/* Router logits from the stored n in the reference's summation order
+ * (csrc/kernels.cu:412-435 with blockDim 256): for each (t, e) the 256 lane
+ * partials p[l] = fma-chain over i = l, l+256, ... of n[t][i]*W[e][i] from
+ * +0.0f, reduced by the pairwise tree p[l] += p[l+s], s = 128..1, then
+ * + bias[e] -- bit-identical to the reference's kernel_moe_gate and to the
+ * logits moe_router_topk computes; H a multiple of 128, E <= 256. */
 moe_status_t moe_router_logits(const float* n, const float* router_w, const float* router_bias,
                                int T, int H, int E, float* logits, cwStream_t stream);
+
+/* No counterpart in the reference.  The "router column order" of a [rows][H]
+ * fp32 matrix (H a multiple of 256, J = H/256): element i = 256j + 32m + 4q + r
+ * (r = 2*r_hi + r_lo) of a row is stored at column
+ *     r_lo*128J + m*16J + 16j + 8*r_hi + q,
+ * which groups the lanes of the reference's reduction so that the layer's
+ * router streams long contiguous runs and splits the lanes over a CTA pair
+ * at the last tree level.  moe_router_columns writes src in that order to
+ * dst (no aliasing); moe_rmsnorm_quant_rc is moe_rmsnorm_quant_n with n
+ * (required) written in that order; moe_router_logits_rc takes n and W in
+ * that order and returns exactly the logits of moe_router_logits on the
+ * plain matrices (E <= 256). */
+moe_status_t moe_router_columns(const float* src, float* dst, int rows, int H, cwStream_t stream);
+moe_status_t moe_rmsnorm_quant_rc(const void* x_bf16, const float* gamma, int T, int H, float eps,
+                                  float* rms_out, float* n_rc_out, void* xq_out, float* xs_out,
+                                  int xs_ld, cwStream_t stream);
+moe_status_t moe_router_logits_rc(const float* n_rc, const float* w_rc, const float* router_bias,
+                                  int T, int H, int E, float* logits, cwStream_t stream);
 
 /* Top-k + weights of given logits [T][E] with the same rule as
  * moe_router_topk. */
@@ -214,8 +235,8 @@ moe_status_t moe_router_topk_noalloc(const float* n, const float* router_w,
                                      const float* router_bias, int T, int H, int E, int k,
                                      int32_t* topk_idx, float* topk_w, cwStream_t stream);
 
-/* Router: logits[t][e] = fma-chain over i = 0..H-1 of n[t][i]*W[e][i]
- * (+ bias[e]), n recomputed from x, rms, gamma exactly as above; then the
+/* Router: the logits of moe_router_logits (reference summation order),
+ * n recomputed from x, rms, gamma exactly as above; then the
  * reference's top-k (strict '>' from -FLT_MAX: lower index wins ties, NaN
  * never chosen; csrc/kernels.cu:437-471) and weights exp(v)/sum exp(v) over
  * the selected slots (max-subtracted when the top logit exceeds 80).

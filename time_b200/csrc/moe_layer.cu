@@ -59,6 +59,7 @@ struct moe_layer {
     bool timing;
     // workspace layout (byte offsets)
     size_t off_bcounts, bcounts_bytes;
+    size_t off_wrc = 0;   // router weight in the router column order (H % 256 == 0)
     size_t off_rms, off_n, off_logits, off_xq, off_xs, off_idx, off_w, off_counts, off_start, off_total, off_pos, off_rowtok,
         off_xp, off_xps, off_hq, off_hs, off_y, bytes;
     int xs_ld, rcap;
@@ -100,6 +101,7 @@ void plan_workspace(moe_layer* L) {
     L->off_bcounts = take(L->bcounts_bytes);
     L->off_n = take(T * H * 4);
     L->off_logits = take(T * static_cast<size_t>(c.num_experts) * 4);
+    if (H % 256 == 0) L->off_wrc = take(static_cast<size_t>(c.num_experts) * H * 4);
     L->off_xq = take(T * H);
     L->off_xs = take((H / 128) * L->xs_ld * 4);
     L->off_idx = take(T * K * 4);
@@ -439,12 +441,26 @@ moe_status_t moe_layer_forward(moe_layer_t* L, const void* x, void* out, int T, 
     float* n = at<float>(ws, L->off_n);
     float* logits = at<float>(ws, L->off_logits);
     mark(L, 0, st);
-    MOE_TRY(moe_rmsnorm_quant_n(x, L->w.norm_gamma, T, c.hidden, c.rms_eps, rms, n, at<void>(ws, L->off_xq),
-                                at<float>(ws, L->off_xs), L->xs_ld, stream));
+    // hidden sizes that are multiples of 256 (every real model) take the
+    // column-ordered router: n is written in that order by the RMSNorm and
+    // the router weight is reordered into the workspace (E x H floats)
+    const bool rc = c.hidden % 256 == 0;
+    if (rc)
+        MOE_TRY(moe_rmsnorm_quant_rc(x, L->w.norm_gamma, T, c.hidden, c.rms_eps, rms, n, at<void>(ws, L->off_xq),
+                                     at<float>(ws, L->off_xs), L->xs_ld, stream));
+    else
+        MOE_TRY(moe_rmsnorm_quant_n(x, L->w.norm_gamma, T, c.hidden, c.rms_eps, rms, n, at<void>(ws, L->off_xq),
+                                    at<float>(ws, L->off_xs), L->xs_ld, stream));
     int32_t* idx = at<int32_t>(ws, L->off_idx);
     float* wts = at<float>(ws, L->off_w);
     mark(L, 1, st);
-    MOE_TRY(moe_router_logits(n, L->w.router_w, L->w.router_bias, T, c.hidden, c.num_experts, logits, stream));
+    if (rc) {
+        float* wrc = at<float>(ws, L->off_wrc);
+        MOE_TRY(moe_router_columns(L->w.router_w, wrc, c.num_experts, c.hidden, stream));
+        MOE_TRY(moe_router_logits_rc(n, wrc, L->w.router_bias, T, c.hidden, c.num_experts, logits, stream));
+    } else {
+        MOE_TRY(moe_router_logits(n, L->w.router_w, L->w.router_bias, T, c.hidden, c.num_experts, logits, stream));
+    }
     MOE_TRY(moe_topk_softmax(logits, T, c.num_experts, c.top_k, idx, wts, stream));
     return run_experts_any(L, x, idx, wts, out, T, ws, st);
 }

@@ -21,6 +21,31 @@ using namespace tb;
 __device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
 
+// Router column order of a row of H = 256 J floats (H % 256 == 0): element
+// i = 256j + 32m + 4q + r (r = 2 r_hi + r_lo) is stored at column
+//   r_lo * 128J + m * 16J + 16j + 8 r_hi + q,
+// so that for fixed (r_lo, m) the 16 lanes (r_hi, q) of all J steps of the
+// router's reduction (csrc/kernels.cu:412-435 with blockDim 256) form one
+// contiguous run of 16J floats.
+__host__ __device__ __forceinline__ int router_col(int i, int J) {
+    const int r = i & 3, q = (i >> 2) & 7, m = (i >> 5) & 7, j = i >> 8;
+    return (r & 1) * 128 * J + m * 16 * J + 16 * j + 8 * (r >> 1) + q;
+}
+
+// n[c .. c+3] of one row (c % 4 == 0), in the plain or the router column order.
+template <bool kRc>
+__device__ __forceinline__ void store_n(float* row, int c, int H, float v0, float v1, float v2, float v3) {
+    if constexpr (kRc) {
+        const int J = H >> 8;
+        row[router_col(c, J)] = v0;
+        row[router_col(c + 1, J)] = v1;
+        row[router_col(c + 2, J)] = v2;
+        row[router_col(c + 3, J)] = v3;
+    } else {
+        *reinterpret_cast<float4*>(row + c) = make_float4(v0, v1, v2, v3);
+    }
+}
+
 // ---------------------------------------------------------------- RMSNorm
 // Sum of squares of one row in the reference's order
 // (csrc/kernels.cu:67-79 with blockDim 256): the 256 partials
@@ -54,6 +79,7 @@ __device__ __forceinline__ float rowsumsq_ref_order(const __nv_bfloat16* x, int 
 
 // One warp per token: rms, n = (x/rms)*gamma (stored in fp32 when n_out is
 // given, for the router), 1x128 e4m3 quantisation of n.
+template <bool kRc>
 __global__ void __launch_bounds__(256)
 rmsnorm_quant_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ gamma, int T, int H,
                      float eps, float* __restrict__ rms_out, float* __restrict__ n_out, uint8_t* __restrict__ xq,
@@ -74,7 +100,7 @@ rmsnorm_quant_kernel(const __nv_bfloat16* __restrict__ x, const float* __restric
         float v1 = __fmul_rn(__fdiv_rn(bf16_hi(raw.x), rms), g.y);
         float v2 = __fmul_rn(__fdiv_rn(bf16_lo(raw.y), rms), g.z);
         float v3 = __fmul_rn(__fdiv_rn(bf16_hi(raw.y), rms), g.w);
-        if (n_out) *reinterpret_cast<float4*>(n_out + static_cast<size_t>(warp) * H + c) = make_float4(v0, v1, v2, v3);
+        if (n_out) store_n<kRc>(n_out + static_cast<size_t>(warp) * H, c, H, v0, v1, v2, v3);
         float amax = fmaxf(fmaxf(fabsf(v0), fabsf(v1)), fmaxf(fabsf(v2), fabsf(v3)));
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
@@ -99,6 +125,7 @@ constexpr int kRmsRowMax = 16384;   // bf16 elements of the row staged in shared
 // its lane, the eight partials meet in shared memory, and warp 0 applies the
 // same add tree and shuffle-down reduction; the 1x128 blocks are then split
 // over the eight warps.
+template <bool kRc>
 __global__ void __launch_bounds__(256)
 rmsnorm_quant_block_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ gamma, int T, int H,
                            float eps, float* __restrict__ rms_out, float* __restrict__ n_out,
@@ -150,7 +177,7 @@ rmsnorm_quant_block_kernel(const __nv_bfloat16* __restrict__ x, const float* __r
         float v1 = __fmul_rn(__fdiv_rn(bf16_hi(raw.x), rms), g.y);
         float v2 = __fmul_rn(__fdiv_rn(bf16_lo(raw.y), rms), g.z);
         float v3 = __fmul_rn(__fdiv_rn(bf16_hi(raw.y), rms), g.w);
-        if (n_out) *reinterpret_cast<float4*>(n_out + static_cast<size_t>(t) * H + c) = make_float4(v0, v1, v2, v3);
+        if (n_out) store_n<kRc>(n_out + static_cast<size_t>(t) * H, c, H, v0, v1, v2, v3);
         float amax = fmaxf(fmaxf(fabsf(v0), fabsf(v1)), fmaxf(fabsf(v2), fabsf(v3)));
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
@@ -309,51 +336,48 @@ router_logits_warp_kernel(const float* __restrict__ n, const float* __restrict__
 }
 
 // ---------------------------------------------------------------- tiled router
-// The layer's router, persistent over 32-token x 32-expert tiles.  A cluster
+// The layer's router, persistent over 64-token x 32-expert tiles.  A cluster
 // of 4 CTAs owns a tile at a time; CTA k of the cluster takes the lanes with
-// q in {2k, 2k + 1}, so per 256-element step j it needs one 32-byte piece of
-// every row (l = 32m + 8k .. +7).  Thread 0 streams those pieces with 3-D TMA
-// loads -- box {8 floats, 32 rows, 20 steps} of n and of W, laid out in shared
-// memory as [step][row][32 bytes] -- through a 4-stage ring of mbarriers, one
-// stage per (m, chunk of <= 20 steps), continuing across the cluster's tiles.
+// l % 32 in [8k, 8k + 8) (q in {2k, 2k + 1}), so per 256-element step j it
+// needs one 32-byte piece of every row (l = 32m + 8k .. +7).  Thread 0
+// streams those pieces with 3-D TMA loads -- box {8 floats, 64 token rows,
+// 10 steps} of n and {8 floats, 32 expert rows, 10 steps} of W, laid out in
+// shared memory as [step][row][32 bytes] -- through a 4-stage ring of full and
+// empty mbarriers, one stage per (m, chunk of <= 10 steps), continuing across
+// the cluster's tiles.
 //
-// Lanes: a warp covers 8 tokens x 16 experts, both q of the CTA (lane bit 2);
-// a thread owns 2 tokens x 4 experts and, for its q, the four chains r = 0..3
-// of each pair as two fp32x2 registers.  A token load of the warp reads 128
-// contiguous bytes (4 rows x 2 q), the same in each 8-lane phase, so it is
-// conflict-free.  The chains of one m run over all j (ascending); the 8 m
-// values are processed in the tree's post-order 0, 4, 2, 6, 1, 5, 3, 7 and
-// folded with a 3-deep stack, which forms exactly the levels s = 128, 64, 32.
-// At the end of a tile each CTA leaves its 2 x 4 sub-sums per pair in shared
-// memory; after a cluster barrier CTA k reduces the pairs [256k, 256k + 256)
-// over the four CTAs (distributed shared memory) with the levels s = 16, 8, 4,
-// 2, 1, adds the bias and writes the logit.  Every mbarrier wait is bounded
-// (2 s); a CTA whose wait gives up writes NaN logits for its tiles (never
-// selected by the top-k) instead of hanging.
-constexpr int kRtTok = 32, kRtExp = 32;
+// A thread owns one lane (l % 32 = 8k + lane % 8) of 8 tokens x 8 experts:
+// 64 fma chains, with each one-word shared load feeding 8 fmas (16 loads per
+// 64 fmas, which keeps the shared-memory pipe below the fma rate).  Within a
+// warp the four 8-lane groups read two adjacent token rows and two adjacent
+// expert rows, so every load is one conflict-free wavefront.  The chains of
+// one m run over all j (ascending); the 8 m values are processed in the
+// tree's post-order 0, 4, 2, 6, 1, 5, 3, 7 and folded with a 3-deep stack,
+// which forms exactly the levels s = 128, 64, 32.  The stack lives in tensor
+// memory (3 x 64 columns of the thread's TMEM lane), so the registers hold
+// only the live chains.  At the end of a tile each CTA leaves its per-lane
+// sums in shared memory; after a cluster barrier CTA k reduces the pairs
+// [512k, 512k + 512) over the four CTAs (distributed shared memory) with the
+// levels s = 16, 8, 4, 2, 1, adds the bias and writes the logit.  Every
+// mbarrier wait is bounded (2 s); a CTA whose wait gives up writes NaN logits
+// for its tiles (never selected by the top-k) instead of hanging.
+constexpr int kRtTok = 64, kRtExp = 32;
 constexpr int kRtThreads = 256;
-constexpr int kRtJc = 20;                                   // steps per stage
+constexpr int kRtJc = 10;                                   // steps per stage
 constexpr int kRtCluster = 4;
 constexpr int kRtRing = 4;
-constexpr int kRtBoxBytes = kRtJc * 32 * 32;                // [20 steps][32 rows][32 bytes]
-constexpr int kRtStageBytes = 2 * kRtBoxBytes;              // n box, then W box
-constexpr int kRtRedBytes = kRtTok * kRtExp * 8 * 4;
+constexpr int kRtNBox = kRtJc * kRtTok * 32;                // [10 steps][64 rows][32 bytes]
+constexpr int kRtWBox = kRtJc * kRtExp * 32;                // [10 steps][32 rows][32 bytes]
+constexpr int kRtStageBytes = kRtNBox + kRtWBox;
+constexpr int kRtRedRow = kRtExp * 8 + 16;                  // floats per token row (padding: conflict-free stores)
+constexpr int kRtRedBytes = kRtTok * kRtRedRow * 4;
 constexpr int kRtOffRed = kRtRing * kRtStageBytes;
 constexpr int kRtOffBars = kRtOffRed + kRtRedBytes;
-constexpr size_t kRtSmemBytes = kRtOffBars + kRtRing * 8 + 16 + 1024;   // + abort flag, alignment slack
+constexpr size_t kRtSmemBytes = kRtOffBars + 2 * kRtRing * 8 + 16 + 1024;   // + abort flag, TMEM slot, slack
+constexpr uint32_t kRtTmemCols = 512;                       // 2 warps per TMEM lane quarter x 192 columns
 constexpr uint64_t kRtWaitNs = 2000000000ull;
-
-using u64 = unsigned long long;
-__device__ __forceinline__ u64 ffma2_u(u64 a, u64 b, u64 c) {
-    u64 d;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-    return d;
-}
-__device__ __forceinline__ u64 fadd2_u(u64 a, u64 b) {
-    u64 d;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
+static_assert(kRtStageBytes % 1024 == 0 && kRtNBox % 1024 == 0, "TMA destinations stay 1 KB aligned");
+static_assert(kRtSmemBytes <= 232448, "router shared memory");
 
 struct RtParams {
     const float* bias;
@@ -366,18 +390,21 @@ __global__ void __cluster_dims__(kRtCluster, 1, 1) __launch_bounds__(kRtThreads,
 router_logits_ref_kernel(const __grid_constant__ CUtensorMap tmap_n, const __grid_constant__ CUtensorMap tmap_w,
                          const RtParams p) {
     namespace cg = cooperative_groups;
-    extern __shared__ uint8_t rt_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(rt_raw) + 1023) & ~uintptr_t(1023));
+    extern __shared__ __align__(16) uint8_t rt_raw[];
+    // 1 KB aligned by pointer arithmetic on the shared array itself, so the
+    // compiler keeps every access below in the shared state space
+    uint8_t* smem = rt_raw + ((1024u - (smem_u32(rt_raw) & 1023u)) & 1023u);
     float* red = reinterpret_cast<float*>(smem + kRtOffRed);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRtOffBars);
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kRtOffBars + kRtRing * 8);
+    uint64_t* empty = full + kRtRing;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kRtRing);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(empty + kRtRing) + 1;
     cg::cluster_group cluster = cg::this_cluster();
     const int k = static_cast<int>(cluster.block_rank());
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int wt = warp >> 1, we = warp & 1;
-    const int tg = lane & 3, h = (lane >> 2) & 1, eg = lane >> 3;
-    const int trow = 8 * wt + tg;                  // tokens trow, trow + 4
-    const int erow = 16 * we + eg;                 // experts erow + 4b, b = 0..3
+    const int grp = lane >> 3, ln = lane & 7;
+    const int tsel = 2 * (warp & 3) + (grp & 1);   // tokens tsel + 8x, x = 0..7
+    const int esel = 2 * (warp >> 2) + (grp >> 1); // experts esel + 4y, y = 0..7
 
     const int cid = blockIdx.x / kRtCluster, ncl = gridDim.x / kRtCluster;
     const int tiles = p.t_tiles * p.e_tiles;
@@ -396,31 +423,65 @@ router_logits_ref_kernel(const __grid_constant__ CUtensorMap tmap_n, const __gri
         uint8_t* st = smem + slot * kRtStageBytes;
         mbar_arrive_expect_tx(&full[slot], kRtStageBytes);
         tma_load_3d(&tmap_n, &full[slot], st, 32 * m + 8 * k, t0, j0);
-        tma_load_3d(&tmap_w, &full[slot], st + kRtBoxBytes, 32 * m + 8 * k, e0, j0);
+        tma_load_3d(&tmap_w, &full[slot], st + kRtNBox, 32 * m + 8 * k, e0, j0);
     };
 
     if (tid == 0) {
-        for (int i = 0; i < kRtRing; ++i) mbar_init(&full[i], 1);
+        for (int i = 0; i < kRtRing; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], kRtThreads / 32);
+        }
         *abort_flag = 0;
         fence_mbar_init();
         prefetch_tmap(&tmap_n);
         prefetch_tmap(&tmap_w);
     }
+    __syncwarp();
+    if (warp == 0) tmem_alloc(tmem_slot, kRtTmemCols);
+    tc_fence_before();
     __syncthreads();
+    tc_fence_after();
+    // this thread's stack: its TMEM lane (warp % 4 selects the lane quarter),
+    // columns [256 * (warp / 4), + 192): slot s at + 64 s
+    const uint32_t tstack = *tmem_slot + ((32u * static_cast<uint32_t>(warp & 3)) << 16) +
+                            256u * static_cast<uint32_t>(warp >> 2);
+    long long issued = 0;                          // thread 0: stages issued so far
     if (tid == 0)
-        for (long long g = 0; g < g_total && g < kRtRing; ++g) issue(g);
+        for (; issued < g_total && issued < kRtRing - 1; ++issued) issue(issued);
+
+    float acc[8][8];
+    auto st_slot = [&](int s) {                    // stack[s] = acc
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+            uint32_t r[32];
+#pragma unroll
+            for (int q = 0; q < 32; ++q) r[q] = __float_as_uint(acc[4 * c + q / 8][q % 8]);
+            tmem_st32(tstack + 64u * s + 32u * c, r);
+        }
+    };
+    auto add_slot = [&](int s) {                   // acc = stack[s] + acc
+        uint32_t r0[32], r1[32];
+        tmem_wait_st();                            // this thread's earlier stores have landed
+
+        tmem_ld32(tstack + 64u * s, r0);
+        tmem_ld32(tstack + 64u * s + 32u, r1);
+        tmem_wait_ld();
+#pragma unroll
+        for (int q = 0; q < 32; ++q) {
+            asm volatile("" : "+r"(r0[q]), "+r"(r1[q]));     // uses stay after the wait
+            acc[q / 8][q % 8] = __fadd_rn(__uint_as_float(r0[q]), acc[q / 8][q % 8]);
+            acc[4 + q / 8][q % 8] = __fadd_rn(__uint_as_float(r1[q]), acc[4 + q / 8][q % 8]);
+        }
+    };
 
     bool ok = true;
     for (int it = 0; it < my_tiles; ++it) {
         const int tile = cid + it * ncl;
         const int t0 = (tile / p.e_tiles) * kRtTok, e0 = (tile % p.e_tiles) * kRtExp;
-        u64 acc[2][4][2], s0[2][4][2], s1[2][4][2], s2[2][4][2];
 #pragma unroll
-        for (int a = 0; a < 2; ++a)
+        for (int x = 0; x < 8; ++x)
 #pragma unroll
-            for (int b = 0; b < 4; ++b)
-#pragma unroll
-                for (int c = 0; c < 2; ++c) { acc[a][b][c] = 0; s0[a][b][c] = 0; s1[a][b][c] = 0; s2[a][b][c] = 0; }
+            for (int y = 0; y < 8; ++y) acc[x][y] = 0.0f;
         for (int s = 0; s < S; ++s) {
             const long long g = static_cast<long long>(it) * S + s;
             const int slot = static_cast<int>(g % kRtRing);
@@ -429,75 +490,75 @@ router_logits_ref_kernel(const __grid_constant__ CUtensorMap tmap_n, const __gri
             const int mi = s / C, j0 = (s % C) * kRtJc;
             const int jn = p.J - j0 < kRtJc ? p.J - j0 : kRtJc;
             if (ok) {
-                const uint8_t* nb = smem + slot * kRtStageBytes + h * 16;
-                const uint8_t* pa = nb + trow * 32;
-                const uint8_t* pb = nb + kRtBoxBytes + erow * 32;
-#pragma unroll 4
-                for (int j = 0; j < jn; ++j) {
-                    const ulonglong2 a0 = *reinterpret_cast<const ulonglong2*>(pa + j * 1024);
-                    const ulonglong2 a1 = *reinterpret_cast<const ulonglong2*>(pa + j * 1024 + 4 * 32);
-                    ulonglong2 bv[4];
+                const float* nb = reinterpret_cast<const float*>(smem + slot * kRtStageBytes) + tsel * 8 + ln;
+                const float* wb = reinterpret_cast<const float*>(smem + slot * kRtStageBytes + kRtNBox) + esel * 8 + ln;
+                auto step = [&](int j) {
+                    float a[8], b[8];
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) bv[i] = *reinterpret_cast<const ulonglong2*>(pb + j * 1024 + 4 * i * 32);
+                    for (int x = 0; x < 8; ++x) a[x] = nb[j * (kRtTok * 8) + x * 64];
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        acc[0][i][0] = ffma2_u(a0.x, bv[i].x, acc[0][i][0]);
-                        acc[0][i][1] = ffma2_u(a0.y, bv[i].y, acc[0][i][1]);
-                        acc[1][i][0] = ffma2_u(a1.x, bv[i].x, acc[1][i][0]);
-                        acc[1][i][1] = ffma2_u(a1.y, bv[i].y, acc[1][i][1]);
-                    }
+                    for (int y = 0; y < 8; ++y) b[y] = wb[j * (kRtExp * 8) + y * 32];
+#pragma unroll
+                    for (int x = 0; x < 8; ++x)
+#pragma unroll
+                        for (int y = 0; y < 8; ++y) acc[x][y] = __fmaf_rn(a[x], b[y], acc[x][y]);
+                };
+                if (jn == kRtJc) {
+#pragma unroll
+                    for (int j = 0; j < kRtJc; ++j) step(j);       // constant offsets, loads run ahead
+                } else {
+                    for (int j = 0; j < jn; ++j) step(j);
                 }
             }
-            __syncthreads();            // every warp is done with the slot
-            if (tid == 0 && g + kRtRing < g_total && !*abort_flag) {
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                issue(g + kRtRing);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (tid == 0 && issued < g_total && !*abort_flag) {
+                // the slot of stage `issued` was last read as stage issued - kRtRing
+                const long long prev = issued - kRtRing;
+                if (prev < 0 || mbar_wait_bounded(&empty[issued % kRtRing], static_cast<uint32_t>((prev / kRtRing) & 1),
+                                                  abort_flag, kRtWaitNs)) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    issue(issued);
+                    ++issued;
+                }
             }
             if (j0 + jn == p.J) {
                 // the m = m_of(mi) chains are complete: fold them into the tree
+                __syncwarp();
+                switch (mi) {
+                    case 0: st_slot(0); break;                                  // p0
+                    case 1: add_slot(0); st_slot(0); break;                     // p0 + p4
+                    case 2: st_slot(1); break;                                  // p2
+                    case 3: add_slot(1); add_slot(0); st_slot(0); break;        // (p0+p4) + (p2+p6)
+                    case 4: st_slot(1); break;                                  // p1
+                    case 5: add_slot(1); st_slot(1); break;                     // p1 + p5
+                    case 6: st_slot(2); break;                                  // p3
+                    default: add_slot(2); add_slot(1); add_slot(0); break;      // s = 128, 64, 32 complete
+                }
+                if (mi != 7) {
 #pragma unroll
-                for (int a = 0; a < 2; ++a)
+                    for (int x = 0; x < 8; ++x)
 #pragma unroll
-                    for (int b = 0; b < 4; ++b)
-#pragma unroll
-                        for (int c = 0; c < 2; ++c) {
-                            const u64 v = acc[a][b][c];
-                            switch (mi) {
-                                case 0: s0[a][b][c] = v; break;                                       // p0
-                                case 1: s0[a][b][c] = fadd2_u(s0[a][b][c], v); break;                 // p0 + p4
-                                case 2: s1[a][b][c] = v; break;                                       // p2
-                                case 3: s1[a][b][c] = fadd2_u(s1[a][b][c], v);                        // p2 + p6
-                                        s0[a][b][c] = fadd2_u(s0[a][b][c], s1[a][b][c]); break;       // (p0+p4)+(p2+p6)
-                                case 4: s1[a][b][c] = v; break;                                       // p1
-                                case 5: s1[a][b][c] = fadd2_u(s1[a][b][c], v); break;                 // p1 + p5
-                                case 6: s2[a][b][c] = v; break;                                       // p3
-                                default: s2[a][b][c] = fadd2_u(s2[a][b][c], v);                       // p3 + p7
-                                         s1[a][b][c] = fadd2_u(s1[a][b][c], s2[a][b][c]);             // (p1+p5)+(p3+p7)
-                                         s0[a][b][c] = fadd2_u(s0[a][b][c], s1[a][b][c]); break;      // s = 128, 64, 32
-                            }
-                            acc[a][b][c] = 0;
-                        }
+                        for (int y = 0; y < 8; ++y) acc[x][y] = 0.0f;
+                }
             }
         }
-        // this CTA's sub-sums (q = 2k + h, r = 0..3) per pair: red[pair][h * 4 + r]
+        // this CTA's sums (q = 2k + ln / 4, r = ln % 4) per pair: red[token][expert][ln]
 #pragma unroll
-        for (int a = 0; a < 2; ++a)
+        for (int x = 0; x < 8; ++x)
 #pragma unroll
-            for (int b = 0; b < 4; ++b) {
-                const int tl = trow + 4 * a, el = erow + 4 * b;
-                *reinterpret_cast<ulonglong2*>(red + (tl * kRtExp + el) * 8 + h * 4) =
-                    make_ulonglong2(s0[a][b][0], s0[a][b][1]);
-            }
+            for (int y = 0; y < 8; ++y) red[(tsel + 8 * x) * kRtRedRow + (esel + 4 * y) * 8 + ln] = acc[x][y];
         cluster.sync();
-        {
-            const int pair = k * (kRtTok * kRtExp / kRtCluster) + tid;   // 256 pairs per CTA
+#pragma unroll
+        for (int pp = 0; pp < 2; ++pp) {
+            const int pair = k * (kRtTok * kRtExp / kRtCluster) + pp * kRtThreads + tid;
             const int tl = pair / kRtExp, el = pair % kRtExp;
             float sq[8][4];   // [q][r]
 #pragma unroll
             for (int kk = 0; kk < kRtCluster; ++kk) {
-                const float* rr = cluster.map_shared_rank(red, kk) + pair * 8;
-                const float4 lo = *reinterpret_cast<const float4*>(rr);
-                const float4 hi = *reinterpret_cast<const float4*>(rr + 4);
+                const uint32_t rr = mapa_u32(smem_u32(red + tl * kRtRedRow + el * 8), static_cast<uint32_t>(kk));
+                const float4 lo = ld_dsmem_f4(rr);
+                const float4 hi = ld_dsmem_f4(rr + 16);
                 sq[2 * kk][0] = lo.x; sq[2 * kk][1] = lo.y; sq[2 * kk][2] = lo.z; sq[2 * kk][3] = lo.w;
                 sq[2 * kk + 1][0] = hi.x; sq[2 * kk + 1][1] = hi.y; sq[2 * kk + 1][2] = hi.z; sq[2 * kk + 1][3] = hi.w;
             }
@@ -516,17 +577,338 @@ router_logits_ref_kernel(const __grid_constant__ CUtensorMap tmap_n, const __gri
                 p.logits[static_cast<size_t>(t) * p.E + e] = *abort_flag ? __int_as_float(0x7fc00000) : v;
             }
         }
-        cluster.sync();   // the next tile's sub-sums overwrite what the other CTAs just read
+        cluster.sync();   // the next tile's sums overwrite what the other CTAs just read
     }
     // a CTA that gave up lets the copies it issued land before it exits
     if (tid == 0 && *abort_flag) {
-        for (long long g = g_total - kRtRing; g < g_total; ++g) {
+        for (long long g = issued - kRtRing; g < issued; ++g) {
             if (g < 0) continue;
             const uint64_t t1 = globaltimer_ns();
             while (!mbar_try_wait(&full[g % kRtRing], static_cast<uint32_t>((g / kRtRing) & 1)))
                 if (globaltimer_ns() - t1 > 200000000ull) break;
         }
     }
+    tmem_wait_st();
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(*tmem_slot, kRtTmemCols);
+    }
+}
+
+// ---------------------------------------------------------------- router, column-ordered inputs
+// The layer's router reads n and W in the router column order (router_col
+// above): the RMSNorm kernels write n in that order and
+// router_columns_kernel reorders W once per forward.
+//
+// Persistent over 32-token x 32-expert tiles.  A cluster of 2 CTAs owns a
+// tile at a time; CTA k takes the lanes with r_lo = k, whose tree level
+// (s = 1) is the last one, so everything before it stays inside the CTA.
+// Thread 0 streams, per (m, chunk of <= 7 steps), one 2-D TMA box of n
+// {112 floats, 32 rows} and one of W through a 6-stage ring of full and
+// empty mbarriers.  A thread owns one lane l' = 8 r_hi + q of 8 tokens x 8
+// experts (64 fma chains; the two 16-lane halves of a warp share the token
+// rows and read adjacent expert rows, 112 floats apart, so every load is one
+// conflict-free wavefront).  The m chains run in the tree's post-order with
+// the 3-deep stack of levels s = 128, 64, 32 in tensor memory.  At the end of
+// a tile the levels s = 16, 8, 4 (q bits) and s = 2 (r_hi) are formed by
+// recursive-halving shuffles inside each 16-lane group, one value per
+// (token, expert) goes to a double-buffered exchange array, and after one
+// cluster barrier CTA k adds the two CTAs' values (s = 1) for the pairs
+// [512k, 512k + 512), adds the bias and writes the logits.  Every mbarrier
+// wait is bounded (2 s); a CTA whose wait gives up writes NaN logits.
+constexpr int kRcTok = 32, kRcExp = 32;
+constexpr int kRcThreads = 256;
+constexpr int kRcJc = 7;                                    // steps per stage (odd: see the bank note above)
+constexpr int kRcCluster = 2;
+constexpr int kRcRing = 6;
+constexpr int kRcRow = 16 * kRcJc;                          // floats per row per stage
+constexpr int kRcNBox = kRcTok * kRcRow * 4;
+constexpr int kRcWBox = kRcExp * kRcRow * 4;
+constexpr int kRcStageBytes = kRcNBox + kRcWBox;
+constexpr int kRcXch = kRcTok * kRcExp;                     // floats per exchange buffer
+constexpr int kRcOffXch = kRcRing * kRcStageBytes;
+constexpr int kRcOffBars = kRcOffXch + 2 * kRcXch * 4;
+constexpr size_t kRcSmemBytes = kRcOffBars + 2 * kRcRing * 8 + 16 + 1024;
+constexpr uint32_t kRcTmemCols = 512;                       // 2 warps per TMEM lane quarter x 192 columns
+static_assert(kRcStageBytes % 1024 == 0 && kRcNBox % 1024 == 0, "TMA destinations stay 1 KB aligned");
+static_assert(kRcSmemBytes <= 232448, "router shared memory");
+
+__global__ void __cluster_dims__(kRcCluster, 1, 1) __launch_bounds__(kRcThreads, 1)
+router_logits_rc_kernel(const __grid_constant__ CUtensorMap tmap_n, const __grid_constant__ CUtensorMap tmap_w,
+                        const RtParams p) {
+    extern __shared__ __align__(16) uint8_t rc_raw[];
+    uint8_t* smem = rc_raw + ((1024u - (smem_u32(rc_raw) & 1023u)) & 1023u);
+    float* xch = reinterpret_cast<float*>(smem + kRcOffXch);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRcOffBars);
+    uint64_t* empty = full + kRcRing;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kRcRing);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(empty + kRcRing) + 1;
+    uint32_t k;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(k));
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int ln = lane & 15;                      // l' = 8 r_hi + q
+    const int tsel = warp & 3;                     // tokens tsel + 4x, x = 0..7
+    const int esel = 2 * (warp >> 2) + (lane >> 4);// experts esel + 4y, y = 0..7
+    const int J = p.J;
+
+    const int cid = blockIdx.x / kRcCluster, ncl = gridDim.x / kRcCluster;
+    const int tiles = p.t_tiles * p.e_tiles;
+    const int my_tiles = cid < tiles ? (tiles - cid + ncl - 1) / ncl : 0;
+    const int C = (J + kRcJc - 1) / kRcJc;         // chunks per m
+    const int S = 8 * C;                           // stages per tile
+    const int g_total = my_tiles * S;
+    auto m_of = [](int mi) { return ((mi & 1) << 2) | (mi & 2) | (mi >> 2); };
+
+    int iss_tile = 0, iss_s = 0;                   // thread 0: the next stage to issue, as (tile, stage)
+    auto issue = [&](int g) {                      // thread 0 only; g = iss_tile * S + iss_s
+        const int tile = cid + iss_tile * ncl;
+        const int t0 = (tile / p.e_tiles) * kRcTok, e0 = (tile % p.e_tiles) * kRcExp;
+        const int mi = iss_s / C, j0 = (iss_s - mi * C) * kRcJc;
+        const int x = static_cast<int>(k) * 128 * J + m_of(mi) * 16 * J + 16 * j0;
+        const int slot = g % kRcRing;
+        uint8_t* st = smem + slot * kRcStageBytes;
+        mbar_arrive_expect_tx(&full[slot], kRcStageBytes);
+        tma_load_2d(&tmap_n, &full[slot], st, x, t0);
+        tma_load_2d(&tmap_w, &full[slot], st + kRcNBox, x, e0);
+        if (++iss_s == S) { iss_s = 0; ++iss_tile; }
+    };
+
+    if (tid == 0) {
+        for (int i = 0; i < kRcRing; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], kRcThreads / 32);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+        prefetch_tmap(&tmap_n);
+        prefetch_tmap(&tmap_w);
+    }
+    __syncwarp();
+    if (warp == 0) tmem_alloc(tmem_slot, kRcTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    // this thread's stack: its TMEM lane (warp % 4 selects the lane quarter),
+    // columns [256 * (warp / 4), + 192): slot s at + 64 s
+    const uint32_t tstack = *tmem_slot + ((32u * static_cast<uint32_t>(warp & 3)) << 16) +
+                            256u * static_cast<uint32_t>(warp >> 2);
+    int issued = 0;                                // thread 0: stages issued so far
+    if (tid == 0)
+        for (; issued < g_total && issued < kRcRing - 1; ++issued) issue(issued);
+
+    float acc[8][8];
+    auto st_slot = [&](int s) {                    // stack[s] = acc
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+            uint32_t r[32];
+#pragma unroll
+            for (int q = 0; q < 32; ++q) r[q] = __float_as_uint(acc[4 * c + q / 8][q % 8]);
+            tmem_st32(tstack + 64u * s + 32u * c, r);
+        }
+    };
+    auto add_slot = [&](int s) {                   // acc = stack[s] + acc
+        uint32_t r0[32], r1[32];
+        tmem_wait_st();                            // this thread's earlier stores have landed
+        tmem_ld32(tstack + 64u * s, r0);
+        tmem_ld32(tstack + 64u * s + 32u, r1);
+        tmem_wait_ld();
+#pragma unroll
+        for (int q = 0; q < 32; ++q) {
+            asm volatile("" : "+r"(r0[q]), "+r"(r1[q]));     // uses stay after the wait
+            acc[q / 8][q % 8] = __fadd_rn(__uint_as_float(r0[q]), acc[q / 8][q % 8]);
+            acc[4 + q / 8][q % 8] = __fadd_rn(__uint_as_float(r1[q]), acc[4 + q / 8][q % 8]);
+        }
+    };
+
+    bool ok = true;
+    for (int it = 0; it < my_tiles; ++it) {
+        const int tile = cid + it * ncl;
+        const int t0 = (tile / p.e_tiles) * kRcTok, e0 = (tile % p.e_tiles) * kRcExp;
+#pragma unroll
+        for (int x = 0; x < 8; ++x)
+#pragma unroll
+            for (int y = 0; y < 8; ++y) acc[x][y] = 0.0f;
+        int mi = 0, ci = 0;                        // stage s = mi * C + ci
+        for (int s = 0; s < S; ++s) {
+            const int g = it * S + s;
+            const int slot = g % kRcRing;
+            if (ok && !mbar_wait_bounded(&full[slot], static_cast<uint32_t>((g / kRcRing) & 1), abort_flag, kRtWaitNs))
+                ok = false;
+            const int j0 = ci * kRcJc;
+            const int jn = J - j0 < kRcJc ? J - j0 : kRcJc;
+            if (ok) {
+                const float* nb = reinterpret_cast<const float*>(smem + slot * kRcStageBytes) + tsel * kRcRow + ln;
+                const float* wb = reinterpret_cast<const float*>(smem + slot * kRcStageBytes + kRcNBox) +
+                                  esel * kRcRow + ln;
+                auto step = [&](int j) {
+                    float a[8], b[8];
+#pragma unroll
+                    for (int x = 0; x < 8; ++x) a[x] = nb[x * 4 * kRcRow + 16 * j];
+#pragma unroll
+                    for (int y = 0; y < 8; ++y) b[y] = wb[y * 4 * kRcRow + 16 * j];
+                    // two experts per packed fma (each lane an IEEE fma, RN): the
+                    // same operations as the scalar chains, half the instructions
+#pragma unroll
+                    for (int x = 0; x < 8; ++x) {
+                        const float2 ad = make_float2(a[x], a[x]);
+#pragma unroll
+                        for (int y = 0; y < 8; y += 2) {
+                            const float2 c = __ffma2_rn(ad, make_float2(b[y], b[y + 1]),
+                                                        make_float2(acc[x][y], acc[x][y + 1]));
+                            acc[x][y] = c.x;
+                            acc[x][y + 1] = c.y;
+                        }
+                    }
+                };
+#pragma unroll
+                for (int j = 0; j < kRcJc; ++j)            // constant offsets, loads run ahead
+                    if (j < jn) step(j);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (tid == 0 && issued < g_total && !*abort_flag) {
+                // the slot of stage `issued` was last read as stage issued - kRcRing
+                const int prev = issued - kRcRing;
+                if (prev < 0 || mbar_wait_bounded(&empty[issued % kRcRing], static_cast<uint32_t>((prev / kRcRing) & 1),
+                                                  abort_flag, kRtWaitNs)) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    issue(issued);
+                    ++issued;
+                }
+            }
+            if (++ci == C) {
+                // the m = m_of(mi) chains are complete: fold them into the tree
+                __syncwarp();
+                switch (mi) {
+                    case 0: st_slot(0); break;                                  // p0
+                    case 1: add_slot(0); st_slot(0); break;                     // p0 + p4
+                    case 2: st_slot(1); break;                                  // p2
+                    case 3: add_slot(1); add_slot(0); st_slot(0); break;        // (p0+p4) + (p2+p6)
+                    case 4: st_slot(1); break;                                  // p1
+                    case 5: add_slot(1); st_slot(1); break;                     // p1 + p5
+                    case 6: st_slot(2); break;                                  // p3
+                    default: add_slot(2); add_slot(1); add_slot(0); break;      // s = 128, 64, 32 complete
+                }
+                if (mi != 7) {
+#pragma unroll
+                    for (int x = 0; x < 8; ++x)
+#pragma unroll
+                        for (int y = 0; y < 8; ++y) acc[x][y] = 0.0f;
+                }
+                ci = 0;
+                ++mi;
+            }
+        }
+        // levels s = 16, 8, 4 (lane bits 2, 1, 0: q) and s = 2 (lane bit 3:
+        // r_hi) by recursive halving: at each level a lane keeps the half of
+        // its pairs selected by its lane bit and adds the partner's values
+        // for that half.  Afterwards lane l' holds pairs 8 q + 4 r_hi + i.
+        float v[64];
+#pragma unroll
+        for (int x = 0; x < 8; ++x)
+#pragma unroll
+            for (int y = 0; y < 8; ++y) v[x * 8 + y] = acc[x][y];
+        {
+            const bool hi = (lane >> 2) & 1;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const float send = hi ? v[i] : v[32 + i], keep = hi ? v[32 + i] : v[i];
+                v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 4));
+            }
+        }
+        {
+            const bool hi = (lane >> 1) & 1;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const float send = hi ? v[i] : v[16 + i], keep = hi ? v[16 + i] : v[i];
+                v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 2));
+            }
+        }
+        {
+            const bool hi = lane & 1;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float send = hi ? v[i] : v[8 + i], keep = hi ? v[8 + i] : v[i];
+                v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 1));
+            }
+        }
+        {
+            const bool hi = (lane >> 3) & 1;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float send = hi ? v[i] : v[4 + i], keep = hi ? v[4 + i] : v[i];
+                v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 8));
+            }
+        }
+        // this CTA's value (r_lo = k) per pair: xch[buf][tl][el ^ 2 (tl / 4)]
+        // (the XOR spreads a warp's stores over the banks, keeps el pairs adjacent)
+        float* xb = xch + (it & 1) * kRcXch;
+        {
+            const int q = ln & 7, rh = ln >> 3;
+            const int tl = tsel + 4 * q;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int el = esel + 4 * (4 * rh + i);
+                xb[tl * kRcExp + (el ^ (2 * q))] = v[i];
+            }
+        }
+        asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+        {
+            const int pair = static_cast<int>(k) * (kRcXch / kRcCluster) + 2 * tid;   // two adjacent experts
+            const int tl = pair / kRcExp, el = pair % kRcExp;
+            const uint32_t a = smem_u32(xb + tl * kRcExp + (el ^ (2 * ((tl >> 2) & 7))));
+            float2 c0, c1;
+            asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(c0.x), "=f"(c0.y) : "r"(mapa_u32(a, 0)) : "memory");
+            asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(c1.x), "=f"(c1.y) : "r"(mapa_u32(a, 1)) : "memory");
+            const int t = t0 + tl;
+            const bool bad = *abort_flag != 0;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int e = e0 + el + h;
+                if (t < p.T && e < p.E) {
+                    float val = __fadd_rn(h ? c0.y : c0.x, h ? c1.y : c1.x);                   // s = 1
+                    if (p.bias) val = __fadd_rn(val, p.bias[e]);
+                    p.logits[static_cast<size_t>(t) * p.E + e] = bad ? __int_as_float(0x7fc00000) : val;
+                }
+            }
+        }
+    }
+    // the peer may still read this CTA's exchange array
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    // a CTA that gave up lets the copies it issued land before it exits
+    if (tid == 0 && *abort_flag) {
+        for (int g = issued - kRcRing; g < issued; ++g) {
+            if (g < 0) continue;
+            const uint64_t t1 = globaltimer_ns();
+            while (!mbar_try_wait(&full[g % kRcRing], static_cast<uint32_t>((g / kRcRing) & 1)))
+                if (globaltimer_ns() - t1 > 200000000ull) break;
+        }
+    }
+    tmem_wait_st();
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(*tmem_slot, kRcTmemCols);
+    }
+}
+
+// W (or any [rows][H] matrix) into the router column order.
+__global__ void __launch_bounds__(256)
+router_columns_kernel(const float* __restrict__ src, float* __restrict__ dst, int rows, int H) {
+    const long long i4 = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;   // 4 elements each
+    const int per_row = H / 4;
+    if (i4 >= static_cast<long long>(rows) * per_row) return;
+    const int row = static_cast<int>(i4 / per_row), c = static_cast<int>(i4 % per_row) * 4;
+    const float4 v = *reinterpret_cast<const float4*>(src + static_cast<size_t>(row) * H + c);
+    float* d = dst + static_cast<size_t>(row) * H;
+    const int J = H / 256;
+    d[router_col(c, J)] = v.x;
+    d[router_col(c + 1, J)] = v.y;
+    d[router_col(c + 2, J)] = v.z;
+    d[router_col(c + 3, J)] = v.w;
 }
 
 // Top-k + softmax of the selected logits, one warp per token (8 tokens per
@@ -861,20 +1243,60 @@ PFN_cuTensorMapEncodeTiled_v12000 rt_encode_fn() {
 
 // The router's view of an fp32 [rows][H] matrix (H % 256 == 0) as a 3-D
 // tensor {256 lanes l, rows, H/256 steps j} -- element (l, row, j) is
-// m[row][256 j + l] -- with box {8, 32, 20}: a TMA load lands as
-// [step][row][8 floats] in shared memory.  Rows past the end read as zero.
-bool encode_rt_map(CUtensorMap* map, const float* base, int rows, int H) {
+// m[row][256 j + l] -- with box {8, box_rows, 10}: a TMA load lands as
+// [step][row][8 floats] in shared memory.  Rows and steps past the end read
+// as zero.
+bool encode_rt_map(CUtensorMap* map, const float* base, int rows, int H, int box_rows) {
     auto fn = rt_encode_fn();
     if (!fn) return false;
     cuuint64_t dims[3] = {256, static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(H / 256)};
     cuuint64_t strides[2] = {static_cast<cuuint64_t>(H) * 4, 1024};
-    cuuint32_t box[3] = {8, kRtTok, kRtJc};
+    cuuint32_t box[3] = {8, static_cast<cuuint32_t>(box_rows), kRtJc};
     cuuint32_t estr[3] = {1, 1, 1};
     return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// The router-column-ordered [rows][H] fp32 matrix as a 2-D tensor with box
+// {112 floats, 32 rows}: one (r_lo, m, 7-step chunk) piece of 32 rows per load.
+bool encode_rc_map(CUtensorMap* map, const float* base, int rows, int H) {
+    auto fn = rt_encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(H) * 4};
+    cuuint32_t box[2] = {kRcRow, kRcTok};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+
+namespace {
+template <bool kRc>
+moe_status_t rmsnorm_quant_launch(const void* x_bf16, const float* gamma, int T, int H, float eps,
+                                  float* rms_out, float* n_out, void* xq_out, float* xs_out, int xs_ld,
+                                  cwStream_t stream) {
+    if (T < 0 || H <= 0 || H % 128 || xs_ld < T) return MOE_ERR_INVALID_ARGUMENT;
+    if (kRc && (H % 256 || !n_out)) return MOE_ERR_INVALID_ARGUMENT;
+    if (T == 0) return MOE_OK;
+    if (!x_bf16 || !gamma || !xq_out || !xs_out) return MOE_ERR_INVALID_ARGUMENT;
+    if (!aligned16(x_bf16) || !aligned16(gamma) || !aligned16(xq_out)) return MOE_ERR_INVALID_ARGUMENT;
+    const int blocks = (T + 7) / 8;
+    if (n_out && !aligned16(n_out)) return MOE_ERR_INVALID_ARGUMENT;
+    if (T <= kRmsBlockPerTokenMaxT && H <= kRmsRowMax)
+        rmsnorm_quant_block_kernel<kRc><<<T, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+            static_cast<const __nv_bfloat16*>(x_bf16), gamma, T, H, eps, rms_out, n_out,
+            static_cast<uint8_t*>(xq_out), xs_out, xs_ld);
+    else
+        rmsnorm_quant_kernel<kRc><<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+            static_cast<const __nv_bfloat16*>(x_bf16), gamma, T, H, eps, rms_out, n_out,
+            static_cast<uint8_t*>(xq_out), xs_out, xs_ld);
+    return launch_status();
+}
 }  // namespace
 
 extern "C" {
@@ -882,27 +1304,76 @@ extern "C" {
 moe_status_t moe_rmsnorm_quant_n(const void* x_bf16, const float* gamma, int T, int H, float eps,
                                  float* rms_out, float* n_out, void* xq_out, float* xs_out, int xs_ld,
                                  cwStream_t stream) {
-    if (T < 0 || H <= 0 || H % 128 || xs_ld < T) return MOE_ERR_INVALID_ARGUMENT;
-    if (T == 0) return MOE_OK;
-    if (!x_bf16 || !gamma || !xq_out || !xs_out) return MOE_ERR_INVALID_ARGUMENT;
-    if (!aligned16(x_bf16) || !aligned16(gamma) || !aligned16(xq_out)) return MOE_ERR_INVALID_ARGUMENT;
-    const int blocks = (T + 7) / 8;
-    if (n_out && !aligned16(n_out)) return MOE_ERR_INVALID_ARGUMENT;
-    if (T <= kRmsBlockPerTokenMaxT && H <= kRmsRowMax)
-        rmsnorm_quant_block_kernel<<<T, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-            static_cast<const __nv_bfloat16*>(x_bf16), gamma, T, H, eps, rms_out, n_out,
-            static_cast<uint8_t*>(xq_out), xs_out, xs_ld);
-    else
-        rmsnorm_quant_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-            static_cast<const __nv_bfloat16*>(x_bf16), gamma, T, H, eps, rms_out, n_out,
-            static_cast<uint8_t*>(xq_out), xs_out, xs_ld);
-    return launch_status();
+    return rmsnorm_quant_launch<false>(x_bf16, gamma, T, H, eps, rms_out, n_out, xq_out, xs_out, xs_ld, stream);
+}
+
+moe_status_t moe_rmsnorm_quant_rc(const void* x_bf16, const float* gamma, int T, int H, float eps,
+                                  float* rms_out, float* n_rc_out, void* xq_out, float* xs_out, int xs_ld,
+                                  cwStream_t stream) {
+    return rmsnorm_quant_launch<true>(x_bf16, gamma, T, H, eps, rms_out, n_rc_out, xq_out, xs_out, xs_ld, stream);
 }
 
 moe_status_t moe_rmsnorm_quant(const void* x_bf16, const float* gamma, int T, int H, float eps,
                                float* rms_out, void* xq_out, float* xs_out, int xs_ld,
                                cwStream_t stream) {
     return moe_rmsnorm_quant_n(x_bf16, gamma, T, H, eps, rms_out, nullptr, xq_out, xs_out, xs_ld, stream);
+}
+
+moe_status_t moe_router_columns(const float* src, float* dst, int rows, int H, cwStream_t stream) {
+    if (rows < 0 || H <= 0 || H % 256) return MOE_ERR_INVALID_ARGUMENT;
+    if (rows == 0) return MOE_OK;
+    if (!src || !dst || src == dst || !aligned16(src) || !aligned16(dst)) return MOE_ERR_INVALID_ARGUMENT;
+    const long long n4 = static_cast<long long>(rows) * (H / 4);
+    if ((n4 + 255) / 256 > 0x7fffffffll) return MOE_ERR_UNSUPPORTED;
+    router_columns_kernel<<<static_cast<unsigned>((n4 + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        src, dst, rows, H);
+    return launch_status();
+}
+
+moe_status_t moe_router_logits_rc(const float* n_rc, const float* w_rc, const float* router_bias, int T, int H,
+                                  int E, float* logits, cwStream_t stream) {
+    if (T < 0 || H <= 0 || H % 256 || E <= 0 || E > 256) return MOE_ERR_INVALID_ARGUMENT;
+    if (T == 0) return MOE_OK;
+    if (!n_rc || !w_rc || !logits || !aligned16(n_rc) || !aligned16(w_rc)) return MOE_ERR_INVALID_ARGUMENT;
+    CUtensorMap tn, tw;
+    if (!encode_rc_map(&tn, n_rc, T, H) || !encode_rc_map(&tw, w_rc, E, H)) return MOE_ERR_CUDA;
+    static bool attr[kMaxDevices] = {};
+    static int max_clusters[kMaxDevices] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return MOE_ERR_CUDA;
+    if (smem_optin_once(router_logits_rc_kernel, static_cast<int>(kRcSmemBytes), attr) != cudaSuccess)
+        return MOE_ERR_CUDA;
+    RtParams prm;
+    prm.bias = router_bias;
+    prm.logits = logits;
+    prm.T = T;
+    prm.E = E;
+    prm.J = H / 256;
+    prm.t_tiles = (T + kRcTok - 1) / kRcTok;
+    prm.e_tiles = (E + kRcExp - 1) / kRcExp;
+    const long long tiles = static_cast<long long>(prm.t_tiles) * prm.e_tiles;
+    const long long stages = tiles * 8 * ((prm.J + kRcJc - 1) / kRcJc);
+    if (tiles > 0x7fffffffll / kRcCluster || stages > 0x7fffffffll) return MOE_ERR_UNSUPPORTED;
+    int ncl = dev >= 0 && dev < kMaxDevices ? max_clusters[dev] : 0;
+    if (ncl <= 0) {
+        // as many clusters as can be resident at once (one CTA per SM)
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(kRcCluster * 512);
+        cfg.blockDim = dim3(kRcThreads);
+        cfg.dynamicSmemBytes = kRcSmemBytes;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = kRcCluster;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        if (cudaOccupancyMaxActiveClusters(&ncl, router_logits_rc_kernel, &cfg) != cudaSuccess || ncl <= 0) ncl = 64;
+        if (dev >= 0 && dev < kMaxDevices) max_clusters[dev] = ncl;
+    }
+    const int grid = kRcCluster * static_cast<int>(tiles < ncl ? tiles : ncl);
+    router_logits_rc_kernel<<<grid, kRcThreads, kRcSmemBytes, static_cast<cudaStream_t>(stream)>>>(tn, tw, prm);
+    return launch_status();
 }
 
 moe_status_t moe_router_logits(const float* n, const float* router_w, const float* router_bias, int T, int H,
@@ -920,7 +1391,7 @@ moe_status_t moe_router_logits(const float* n, const float* router_w, const floa
         return launch_status();
     }
     CUtensorMap tn, tw;
-    if (!encode_rt_map(&tn, n, T, H) || !encode_rt_map(&tw, router_w, E, H)) return MOE_ERR_CUDA;
+    if (!encode_rt_map(&tn, n, T, H, kRtTok) || !encode_rt_map(&tw, router_w, E, H, kRtExp)) return MOE_ERR_CUDA;
     static bool attr[kMaxDevices] = {};
     static int max_clusters[kMaxDevices] = {};
     int dev = 0;

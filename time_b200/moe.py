@@ -88,6 +88,10 @@ def libs():
         k.moe_rmsnorm_quant_n.argtypes = [c_void_p, c_void_p, c_int, c_int, c_float, c_void_p, c_void_p, c_void_p,
                                           c_void_p, c_int, c_void_p]
         k.moe_router_logits.argtypes = [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]
+        k.moe_router_logits_rc.argtypes = [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]
+        k.moe_router_columns.argtypes = [c_void_p, c_void_p, c_int, c_int, c_void_p]
+        k.moe_rmsnorm_quant_rc.argtypes = [c_void_p, c_void_p, c_int, c_int, c_float, c_void_p, c_void_p, c_void_p,
+                                           c_void_p, c_int, c_void_p]
         k.moe_topk_softmax.argtypes = [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]
         k.moe_router_topk_noalloc.argtypes = [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p,
                                               c_void_p, c_void_p]
