@@ -109,6 +109,16 @@ typedef void* cbwLtMatmulPreference_t;
  * The decode form adds a row's K blocks in a different order from the full
  * form, so its results differ from the full form's in the last bits.
  *
+ * CBW_GEMM_ACT_X2 (or-ed in; no counterpart in the reference): two-term
+ * activations.  A holds two e4m3 planes, hi at a and lo at a + rows*K bytes,
+ * with one scale: A = a_scale * (decode(hi) + decode(lo)), lo being the e4m3
+ * rounding of the residual (x/scale - decode(hi)).  Each K block's tensor-core
+ * partial covers both planes (twice the MMA work) and carries about 7
+ * significant bits of every activation instead of 4.  The gated mode then
+ * writes its output in the same two-plane form (hi at out, lo at
+ * out + rows*N); the down mode reads it.  The full down form runs on CTA
+ * pairs (K % 256 == 0 and N % 256 == 0) or else in 32-token tiles.
+ *
  * Requirements: K % 128 == 0, N % 128 == 0, start[g] % 16 == 0, every
  * segment [start, start + round_up(count,16)) inside [0, rows), a_ld (the
  * scale leading dimension) % 4 == 0 and >= rows, 16-byte aligned pointers.
@@ -121,7 +131,8 @@ typedef enum {
     CBW_GEMM_SMALL_TILES = 0x10,
     CBW_GEMM_FULL_TILES = 0x20,
     CBW_GEMM_ONE_SM_TILES = 0x40,
-    CBW_GEMM_PAIR_TILES = 0x80
+    CBW_GEMM_PAIR_TILES = 0x80,
+    CBW_GEMM_ACT_X2 = 0x100
 } cbwGemmMode_t;
 
 typedef struct {

@@ -160,6 +160,17 @@ moe_status_t moe_layer_set_expert_placement(moe_layer_t* layer, const int32_t* s
  * one-GPU layer give bit-identical outputs when they run the same form. */
 moe_status_t moe_layer_set_gemm_form(moe_layer_t* layer, int form);
 
+/* No counterpart in the reference.  Activation format of the two expert
+ * GEMMs: planes = 1 (e4m3 with one scale per 1x128 block, as FP8 serving
+ * stacks run it) or planes = 2 (two-term e4m3, hi + lo residual with the same
+ * scale -- CBW_GEMM_ACT_X2: twice the tensor-core work, about 7 significant
+ * bits per activation instead of 4, which keeps the layer within the
+ * tolerance of an fp32-activation evaluation).  The workspace size depends on
+ * it: query moe_layer_workspace_bytes after setting it.  Two planes are not
+ * available with ep_size > 1 (MOE_ERR_UNSUPPORTED). */
+moe_status_t moe_layer_set_act_planes(moe_layer_t* layer, int planes);
+moe_status_t moe_layer_get_act_planes(const moe_layer_t* layer, int* planes);
+
 /* Reads and clears the device error word (synchronises `stream`). */
 moe_status_t moe_layer_check_error(moe_layer_t* layer, cwStream_t stream);
 
@@ -208,6 +219,24 @@ moe_status_t moe_rmsnorm_quant_rc(const void* x_bf16, const float* gamma, int T,
                                   int xs_ld, cwStream_t stream);
 moe_status_t moe_router_logits_rc(const float* n_rc, const float* w_rc, const float* router_bias,
                                   int T, int H, int E, float* logits, cwStream_t stream);
+
+/* No counterpart in the reference.  Two-term e4m3 activations ("x2", the
+ * input format of CBW_GEMM_ACT_X2): per 128-column block one scale s =
+ * amax/448 and two e4m3 planes, hi = e4m3_rne(v/s) (the same bytes as the
+ * one-plane quantisation) and lo = e4m3_rne(v/s - decode(hi)), so that
+ * v ~= s * (decode(hi) + decode(lo)) with about 7 significant bits.
+ * moe_rmsnorm_quant_x2 is moe_rmsnorm_quant_n (n_router_cols = 0) or
+ * moe_rmsnorm_quant_rc (n_router_cols = 1) that also writes the lo plane
+ * ([T][H], xq_lo_out, required); n_out may be NULL with n_router_cols = 0.
+ * moe_gather_rows_x2 is moe_gather_rows that also moves the lo plane
+ * (xq_lo and xp_lo both given, or both NULL); total_rows (device, may be
+ * NULL) bounds the rows written. */
+moe_status_t moe_rmsnorm_quant_x2(const void* x_bf16, const float* gamma, int T, int H, float eps,
+                                  float* rms_out, float* n_out, int n_router_cols, void* xq_out,
+                                  void* xq_lo_out, float* xs_out, int xs_ld, cwStream_t stream);
+moe_status_t moe_gather_rows_x2(const void* xq, const void* xq_lo, const float* xs, int xs_ld,
+                                const int32_t* row_token, const int32_t* total_rows, int row_capacity,
+                                int H, void* xp, void* xp_lo, float* xps, int xps_ld, cwStream_t stream);
 
 /* Top-k + weights of given logits [T][E] with the same rule as
  * moe_router_topk. */

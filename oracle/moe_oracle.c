@@ -260,13 +260,35 @@ void orc_quant_row_1x128(const float* v, int cols, uint8_t* q, float* s) {
     }
 }
 
+void orc_quant_row_1x128_x2(const float* v, int cols, uint8_t* q, uint8_t* ql, float* s) {
+    for (int b = 0; b < cols / 128; ++b) {
+        const float* vb = v + b * 128;
+        float amax = 0.0f;
+        for (int i = 0; i < 128; ++i) amax = fmaxf(amax, fabsf(vb[i]));
+        if (amax == 0.0f) {
+            for (int i = 0; i < 128; ++i) q[b * 128 + i] = ql[b * 128 + i] = 0;
+            s[b] = 0.0f;
+            continue;
+        }
+        float inv = 448.0f / amax;
+        for (int i = 0; i < 128; ++i) {
+            float u = vb[i] * inv;
+            uint8_t hi = orc_e4m3_encode_rne(u);
+            q[b * 128 + i] = hi;
+            ql[b * 128 + i] = orc_e4m3_encode_rne(u - orc_e4m3_decode(hi));
+        }
+        s[b] = amax / 448.0f;
+    }
+}
+
 static float silu_f(float g) { return g / (1.0f + expf(-g)); }
 
 /* One expert MLP for one token: kernels.fut:343-347 with block scales.
- * mode 0: activations given as (q, s) 1x128-quantised; mode 1: fp32 n. */
+ * mode 0: activations given as (q, s) 1x128-quantised; mode 1: fp32 n;
+ * mode 2: two-term (q, ql, s), activation = s * (decode(q) + decode(ql)). */
 static void expert_mlp_one(const orc_moe_cfg* cfg, const orc_moe_weights* w, int e,
-                           int mode, const float* n, const uint8_t* nq, const float* ns,
-                           const float* lut, float* hbuf, uint8_t* hq, float* hs,
+                           int mode, const float* n, const uint8_t* nq, const uint8_t* nql, const float* ns,
+                           const float* lut, float* hbuf, uint8_t* hq, uint8_t* hql, float* hs,
                            float* y) {
     const int H = cfg->hidden, I = cfg->intermediate;
     const int KB1 = H / 128, KB2 = I / 128;
@@ -282,9 +304,9 @@ static void expert_mlp_one(const orc_moe_cfg* cfg, const orc_moe_weights* w, int
             float sg = S13[(j / 128) * KB1 + kb];
             float su = S13[((I + j) / 128) * KB1 + kb];
             double dg = 0.0, du = 0.0;
-            if (mode == 0) {
+            if (mode != 1) {
                 for (int i = kb * 128; i < kb * 128 + 128; ++i) {
-                    float a = lut[nq[i]];
+                    float a = mode == 2 ? lut[nq[i]] + lut[nql[i]] : lut[nq[i]];
                     dg += (double)a * lut[wg[i]];
                     du += (double)a * lut[wu[i]];
                 }
@@ -302,14 +324,16 @@ static void expert_mlp_one(const orc_moe_cfg* cfg, const orc_moe_weights* w, int
         hbuf[j] = silu_f((float)g) * (float)u;
     }
     if (mode == 0) orc_quant_row_1x128(hbuf, I, hq, hs);
+    if (mode == 2) orc_quant_row_1x128_x2(hbuf, I, hq, hql, hs);
     for (int o = 0; o < H; ++o) {
         const uint8_t* wd = W2 + (size_t)o * I;
         double acc = 0.0;
         for (int kb = 0; kb < KB2; ++kb) {
             float sd = S2[(o / 128) * KB2 + kb];
             double d = 0.0;
-            if (mode == 0) {
-                for (int i = kb * 128; i < kb * 128 + 128; ++i) d += (double)lut[hq[i]] * lut[wd[i]];
+            if (mode != 1) {
+                for (int i = kb * 128; i < kb * 128 + 128; ++i)
+                    d += (double)(mode == 2 ? lut[hq[i]] + lut[hql[i]] : lut[hq[i]]) * lut[wd[i]];
                 acc += d * ((double)hs[kb] * sd);
             } else {
                 for (int i = kb * 128; i < kb * 128 + 128; ++i) d += (double)hbuf[i] * lut[wd[i]];
@@ -317,7 +341,7 @@ static void expert_mlp_one(const orc_moe_cfg* cfg, const orc_moe_weights* w, int
             }
         }
         float yv = (float)acc;
-        y[o] = (mode == 0) ? orc_bf16_to_f32(orc_f32_to_bf16(yv)) : yv;
+        y[o] = (mode != 1) ? orc_bf16_to_f32(orc_f32_to_bf16(yv)) : yv;
     }
 }
 
@@ -338,29 +362,32 @@ static void ffn_experts_impl(const orc_moe_cfg* cfg, const orc_moe_weights* w,
         float* y = (float*)malloc(sizeof(float) * H);
         float* hbuf = (float*)malloc(sizeof(float) * I);
         uint8_t* hq = (uint8_t*)malloc(I);
+        uint8_t* hql = (uint8_t*)malloc(I);
         float* hs = (float*)malloc(sizeof(float) * (I / 128));
         uint8_t* nq = (uint8_t*)malloc(H);
+        uint8_t* nql = (uint8_t*)malloc(H);
         float* ns = (float*)malloc(sizeof(float) * (H / 128));
 #pragma omp for schedule(dynamic, 1)
         for (int t = 0; t < tokens; ++t) {
             const float* n = nrm + (size_t)t * H;
             for (int i = 0; i < H; ++i) xf[i] = orc_bf16_to_f32(x_bf16[(size_t)t * H + i]);
             if (mode == 0) orc_quant_row_1x128(n, H, nq, ns);
+            if (mode == 2) orc_quant_row_1x128_x2(n, H, nq, nql, ns);
             for (int i = 0; i < H; ++i) acc[i] = xf[i];
             for (int sidx = 0; sidx < cfg->num_shared; ++sidx) {
-                expert_mlp_one(cfg, w, cfg->num_experts + sidx, mode, n, nq, ns, lut, hbuf, hq, hs, y);
+                expert_mlp_one(cfg, w, cfg->num_experts + sidx, mode, n, nq, nql, ns, lut, hbuf, hq, hql, hs, y);
                 for (int i = 0; i < H; ++i) acc[i] += y[i];
             }
             for (int s = 0; s < K; ++s) {
                 int e = idx[(size_t)t * K + s];
                 if (e < 0 || e >= cfg->num_experts) continue;
                 float wt = weights[(size_t)t * K + s];
-                expert_mlp_one(cfg, w, e, mode, n, nq, ns, lut, hbuf, hq, hs, y);
+                expert_mlp_one(cfg, w, e, mode, n, nq, nql, ns, lut, hbuf, hq, hql, hs, y);
                 for (int i = 0; i < H; ++i) acc[i] = fmaf(wt, y[i], acc[i]);
             }
             for (int i = 0; i < H; ++i) out_bf16[(size_t)t * H + i] = orc_f32_to_bf16(acc[i]);
         }
-        free(xf); free(acc); free(y); free(hbuf); free(hq); free(hs); free(nq); free(ns);
+        free(xf); free(acc); free(y); free(hbuf); free(hq); free(hql); free(hs); free(nq); free(nql); free(ns);
     }
 }
 

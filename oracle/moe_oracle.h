@@ -114,6 +114,11 @@ int orc_moe_permute(const int32_t* idx, int tokens, int top_k, int num_experts,
  * an all-zero block gets q = 0, s = 0. */
 void orc_quant_row_1x128(const float* v, int cols, uint8_t* q, float* s);
 
+/* Two-term 1x128 quantisation (the kernels' CBW_GEMM_ACT_X2 format): q as
+ * above, and the residual's e4m3 byte ql = rne_satfinite(u - decode(q)) with
+ * u = v*inv (fp32 product and difference), one scale s for both. */
+void orc_quant_row_1x128_x2(const float* v, int cols, uint8_t* q, uint8_t* ql, float* s);
+
 /* MoE FFN block forward for `tokens` tokens:
  *   n = RMSNorm_ref(x) ; logits = gate_ref(n) (+bias) ; top-k (ref)
  *   routed/shared expert MLP y = W2 . (silu(W_gate . n) * (W_up . n))
@@ -123,6 +128,9 @@ void orc_quant_row_1x128(const float* v, int cols, uint8_t* q, float* s);
  *   quantised 1x128, y rounded to bf16 before the combine.
  * mode 1 ("ref"): fp32 activations end to end with dequantised weights, the
  *   reference's arithmetic (kernels.fut:343-368, engine.t:1317-1347).
+ * mode 2 ("q2"): mode 0 with the two-term activations of
+ *   orc_quant_row_1x128_x2 (activation = s * (decode(q) + decode(ql))), the
+ *   kernels' two-plane mode.
  * Optional outputs (may be NULL): idx [T][k], weights [T][k], logits [T][E].
  * threads: OpenMP threads (<= 0 means the library default). */
 void orc_moe_ffn_forward(const orc_moe_cfg* cfg, const orc_moe_weights* w,

@@ -62,6 +62,7 @@ def lib():
         L.orc_moe_permute.argtypes = [i32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                       i32p, i32p, i32p, i32p, ctypes.c_int]
         L.orc_quant_row_1x128.argtypes = [f32p, ctypes.c_int, u8p, f32p]
+        L.orc_quant_row_1x128_x2.argtypes = [f32p, ctypes.c_int, u8p, u8p, f32p]
         L.orc_moe_ffn_forward.argtypes = [ctypes.POINTER(MoeCfg), ctypes.POINTER(MoeWeights), u16p, u16p,
                                           ctypes.c_int, ctypes.c_int, i32p, f32p, f32p, ctypes.c_int]
         L.orc_moe_ffn_experts.argtypes = [ctypes.POINTER(MoeCfg), ctypes.POINTER(MoeWeights), u16p, i32p, f32p,
@@ -188,6 +189,18 @@ def quant_rows_1x128(v: np.ndarray):
     for r in range(rows):
         lib().orc_quant_row_1x128(_p(v[r], f32p), cols, _p(q[r], u8p), _p(s[r], f32p))
     return q, s
+
+
+def quant_rows_1x128_x2(v: np.ndarray):
+    """Two-term 1x128 quantisation: (hi bytes, lo bytes, scales)."""
+    v = _f32(v)
+    rows, cols = v.shape
+    q = np.empty((rows, cols), np.uint8)
+    ql = np.empty((rows, cols), np.uint8)
+    s = np.empty((rows, cols // 128), np.float32)
+    for r in range(rows):
+        lib().orc_quant_row_1x128_x2(_p(v[r], f32p), cols, _p(q[r], u8p), _p(ql[r], u8p), _p(s[r], f32p))
+    return q, ql, s
 
 
 class OracleWeights:

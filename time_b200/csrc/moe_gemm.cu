@@ -79,16 +79,18 @@ constexpr uint64_t kDrainTimeoutNs = 200000000ull;
 // (gate at +0, up at +32); at the end of a tile the groups' sums are added in
 // group order 0, 1, 2, 3 through shared memory.  The sum order differs from
 // the full form's, so one caller should use one form for comparable results.
-template <bool kGated, bool kSmall = false>
+template <bool kGated, bool kSmall = false, bool kX2 = false>
 struct GemmCfg {
+    static constexpr int kPlanes = kX2 ? 2 : 1;            // activation e4m3 planes: hi (+ lo residual)
     static constexpr int kNMax = kGated ? 128 : 256;       // token columns of the promotion layout
     static constexpr int kTileTok = kSmall ? 32 : kNMax;   // tokens per tile
-    static constexpr int kStages = kSmall ? (kGated ? 4 : 9) : 3;   // operand ring
+    static constexpr int kStages = kX2 ? (kSmall ? (kGated ? 3 : 6) : 2)
+                                       : (kSmall ? (kGated ? 4 : 9) : 3);   // operand ring
     static constexpr int kSStages = 8;                      // token-scale ring
     static constexpr int kATiles = kGated ? 2 : 1;          // gate + up
     static constexpr int kABytes = kATiles * kTileM * kBlockK;
-    static constexpr int kBBytes = kTileTok * kBlockK;
-    static constexpr int kStageBytes = kABytes + kBBytes;   // 48 KB; small: 36 KB gated, 20 KB down
+    static constexpr int kBBytes = kPlanes * kTileTok * kBlockK;   // [plane][tokens][128 B]
+    static constexpr int kStageBytes = kABytes + kBBytes;   // 48 KB; small: 36 KB gated, 20 KB down (one plane)
     static constexpr int kTBufs = kSmall ? 8 : 2;           // TMEM partial buffers
     static constexpr int kTBufColsSm = 64;                  // small form: columns per buffer
     static constexpr int kNumCombined = kGated ? 2 : 1;
@@ -119,6 +121,7 @@ struct GemmCfg {
     static_assert(kTBufs * kBufCols <= kTmemCols, "TMEM partial buffers");
     static_assert(!kSmall || (kSStages == 8 && kTBufs == 8), "small form: ring positions from the K-block count");
     static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+    static_assert(!kX2 || kGated || kSmall, "two-plane activations: the full down form runs on CTA pairs");
 };
 
 struct GemmParams {
@@ -130,6 +133,7 @@ struct GemmParams {
     void* out;
     float* out_scale;
     int out_ld;
+    size_t out_plane;       // two-plane mode, gated: bytes from the hi plane of out to its lo plane
     int G;
     int K;
     int N;                  // output columns per group
@@ -169,14 +173,14 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
     }
 }
 
-template <bool kGated, bool kSmall>
+template <bool kGated, bool kSmall, bool kX2>
 __global__ void __launch_bounds__(kNumThreads, 1)
 grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
                         const __grid_constant__ CUtensorMap tmap_a,
                         const __grid_constant__ CUtensorMap tmap_a64,
                         const __grid_constant__ CUtensorMap tmap_a128,
                         const GemmParams p) {
-    using C = GemmCfg<kGated, kSmall>;
+    using C = GemmCfg<kGated, kSmall, kX2>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -283,7 +287,7 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
                 const int box = tc.ntile <= 32 ? 32 : (tc.ntile <= 64 ? 64 : 128);
                 const int b_loads = (tc.ntile + box - 1) / box;
                 const CUtensorMap* tmap_b = box == 32 ? &tmap_a : (box == 64 ? &tmap_a64 : &tmap_a128);
-                const uint32_t bytes = C::kABytes + b_loads * box * kBlockK;
+                const uint32_t bytes = C::kABytes + b_loads * box * kBlockK * C::kPlanes;
                 const int wrow = tc.g * p.w_rows + tc.nb * kTileM;
                 for (int kb = 0; kb < KB; ++kb) {
                     if (!mbar_wait_bounded(&empty_bar[s], phase ^ 1, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
@@ -293,8 +297,13 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
                         tma_load_3d(&tmap_w, &full_bar[s], st, kb * kBlockK, wrow, 0);
                     else
                         tma_load_2d(&tmap_w, &full_bar[s], st, kb * kBlockK, wrow);
-                    for (int r = 0; r < b_loads; ++r)
-                        tma_load_2d(tmap_b, &full_bar[s], st + C::kABytes + r * box * kBlockK, kb * kBlockK, tc.row0 + box * r);
+                    for (int r = 0; r < b_loads; ++r) {
+                        uint8_t* dst = st + C::kABytes + r * box * kBlockK * C::kPlanes;
+                        if constexpr (kX2)   // {K, rows, plane}: [hi | lo][box rows][128 B]
+                            tma_load_3d(tmap_b, &full_bar[s], dst, kb * kBlockK, tc.row0 + box * r, 0);
+                        else
+                            tma_load_2d(tmap_b, &full_bar[s], dst, kb * kBlockK, tc.row0 + box * r);
+                    }
                     armed_mask |= 1u << s;
                     armed_phase = (armed_phase & ~(1u << s)) | (phase << s);
                     if (++s == C::kStages) { s = 0; phase ^= 1; }
@@ -333,13 +342,21 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
                     const uint32_t a_addr = smem_u32(smem + C::kOffStages + s * C::kStageBytes);
                     const uint32_t b_addr = a_addr + C::kABytes;
                     const uint32_t d = tmem_base + b * C::kBufCols;
+                    // two-plane mode: the lo plane's products add into the same partial
+                    // (one K block = W (hi + lo), one scale), at the box's plane offset
+                    const uint32_t plane_bytes =
+                        (tc.ntile <= 32 ? 32 : (tc.ntile <= 64 ? 64 : 128)) * kBlockK;
 #pragma unroll
-                    for (int k = 0; k < kBlockK / 32; ++k) {
-                        const uint64_t bdesc = umma_desc_sw128(b_addr + k * 32);
-                        umma_f8(d, umma_desc_sw128(a_addr + k * 32), bdesc, idesc, k > 0 ? 1u : 0u);
-                        if (kGated)
-                            umma_f8(d + C::kUpOff, umma_desc_sw128(a_addr + kTileM * kBlockK + k * 32), bdesc, idesc,
-                                    k > 0 ? 1u : 0u);
+                    for (int pl = 0; pl < C::kPlanes; ++pl) {
+#pragma unroll
+                        for (int k = 0; k < kBlockK / 32; ++k) {
+                            const uint64_t bdesc = umma_desc_sw128(b_addr + pl * plane_bytes + k * 32);
+                            const uint32_t acc = (k > 0 || pl > 0) ? 1u : 0u;
+                            umma_f8(d, umma_desc_sw128(a_addr + k * 32), bdesc, idesc, acc);
+                            if (kGated)
+                                umma_f8(d + C::kUpOff, umma_desc_sw128(a_addr + kTileM * kBlockK + k * 32), bdesc, idesc,
+                                        acc);
+                        }
                     }
                     umma_commit(&empty_bar[s]);
                     umma_commit(&tfull_bar[b]);
@@ -548,7 +565,7 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
                 uint8_t* outq = reinterpret_cast<uint8_t*>(p.out);
                 for (int c = pw; c < tc.ntile; c += kNumPromoWarps) {
                     const size_t row = static_cast<size_t>(tc.row0 + c);
-                    uint32_t packed = 0;
+                    uint32_t packed = 0, packed_lo = 0;
                     float scale = 0.0f;
                     if (c < tc.nrows) {
                         const float4 v = *reinterpret_cast<const float4*>(stage + c * 128 + lane * 4);
@@ -557,13 +574,22 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
                         for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
                         if (amax > 0.0f) {
                             const float inv = 448.0f / amax;
-                            const uint32_t lo = cvt_e4m3x2(v.x * inv, v.y * inv);
-                            const uint32_t hi = cvt_e4m3x2(v.z * inv, v.w * inv);
-                            packed = lo | (hi << 16);
+                            if constexpr (kX2) {
+                                const uint32_t s0 = cvt_e4m3x2_split(__fmul_rn(v.x, inv), __fmul_rn(v.y, inv));
+                                const uint32_t s1 = cvt_e4m3x2_split(__fmul_rn(v.z, inv), __fmul_rn(v.w, inv));
+                                packed = (s0 & 0xFFFFu) | (s1 << 16);
+                                packed_lo = (s0 >> 16) | (s1 & 0xFFFF0000u);
+                            } else {
+                                const uint32_t lo = cvt_e4m3x2(v.x * inv, v.y * inv);
+                                const uint32_t hi = cvt_e4m3x2(v.z * inv, v.w * inv);
+                                packed = lo | (hi << 16);
+                            }
                             scale = amax / 448.0f;
                         }
                     }
                     *reinterpret_cast<uint32_t*>(outq + row * p.N + tc.nb * 128 + lane * 4) = packed;
+                    if constexpr (kX2)
+                        *reinterpret_cast<uint32_t*>(outq + p.out_plane + row * p.N + tc.nb * 128 + lane * 4) = packed_lo;
                     if (lane == 0) p.out_scale[(size_t)tc.nb * p.out_ld + row] = scale;
                 }
                 if (!group_sync()) { ok = false; break; }
@@ -619,32 +645,38 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
 // on the even CTA's barrier.  Every wait is bounded as in the one-SM form.
 constexpr int kPairTok = 128;                               // tokens per tile (UMMA N)
 constexpr int kPairKbPerStage = 2;                          // K blocks per TMA load (one instruction each)
-constexpr int kPairStages = 3;
 constexpr int kPairSStages = 4;
 constexpr int kPairTBufs = 4;                               // 4 x 128 TMEM columns
 constexpr int kPairABytes = kTileM * kBlockK;               // this CTA's 128 weight rows, one K block
 constexpr int kPairBRows = kPairTok / 2;                    // this CTA's half of the tokens
 constexpr int kPairBBytes = kPairBRows * kBlockK;
-constexpr int kPairStageABytes = kPairKbPerStage * kPairABytes;   // [kb][128 rows][128 B]
-constexpr int kPairStageBytes = kPairStageABytes + kPairKbPerStage * kPairBBytes;   // 48 KB
 constexpr int kPairEpiBytes = kPairTok * 128 * 2;           // 32 KB: gated [128 tok][64] fp32, down [128][128] bf16
 // scale ring entry: raw token scales [kb][128] (TMA), then the folded [kb][gate, up][128]
 constexpr int kPairScaleRaw = kPairKbPerStage * kPairTok;
 constexpr int kPairScaleFloats = kPairScaleRaw + kPairKbPerStage * 2 * kPairTok;
-constexpr int kPairOffStages = 0;
-constexpr int kPairOffEpi = kPairOffStages + kPairStages * kPairStageBytes;
-constexpr int kPairOffScale = kPairOffEpi + kPairEpiBytes;
-constexpr int kPairOffAmax = kPairOffScale + kPairSStages * kPairScaleFloats * 4;   // own[128], peer[2][128]
-constexpr int kPairOffTables = kPairOffAmax + 3 * kPairTok * 4;
-constexpr int kPairOffBars = kPairOffTables + (4 * kMaxGroups + 2) * 4;
-constexpr int kPairNumBars = 2 * kPairStages + 3 * kPairSStages + 2 * kPairTBufs + 1 + 2;
-constexpr int kPairOffMisc = kPairOffBars + kPairNumBars * 8;
-constexpr int kPairSmemBytes = kPairOffMisc + 64 + 1024;
-static_assert(kPairOffBars % 8 == 0, "mbarrier alignment");
-static_assert(kPairStageBytes % 1024 == 0 && kPairStageABytes % 1024 == 0, "swizzled tiles on 1024-byte boundaries");
-static_assert((kPairScaleFloats * 4) % 128 == 0, "scale entries 128-byte aligned");
-static_assert(kPairTBufs * kPairTok <= kTmemCols, "TMEM buffers");
-static_assert(kPairSmemBytes <= 227 * 1024, "shared memory budget");
+// Operand ring and shared-memory carve-up; two-plane activations (hi + lo
+// residual) double the token part of a stage: [plane][kb][64 rows][128 B].
+template <bool kX2>
+struct PairCfg {
+    static constexpr int kPlanes = kX2 ? 2 : 1;
+    static constexpr int kStages = kX2 ? 2 : 3;
+    static constexpr int kStageABytes = kPairKbPerStage * kPairABytes;   // [kb][128 rows][128 B]
+    static constexpr int kStageBytes = kStageABytes + kPlanes * kPairKbPerStage * kPairBBytes;   // 48 / 64 KB
+    static constexpr int kOffStages = 0;
+    static constexpr int kOffEpi = kOffStages + kStages * kStageBytes;
+    static constexpr int kOffScale = kOffEpi + kPairEpiBytes;
+    static constexpr int kOffAmax = kOffScale + kPairSStages * kPairScaleFloats * 4;   // own[128], peer[2][128]
+    static constexpr int kOffTables = kOffAmax + 3 * kPairTok * 4;
+    static constexpr int kOffBars = kOffTables + (4 * kMaxGroups + 2) * 4;
+    static constexpr int kNumBars = 2 * kStages + 3 * kPairSStages + 2 * kPairTBufs + 1 + 2;
+    static constexpr int kOffMisc = kOffBars + kNumBars * 8;
+    static constexpr int kSmemBytes = kOffMisc + 64 + 1024;
+    static_assert(kOffBars % 8 == 0, "mbarrier alignment");
+    static_assert(kStageBytes % 1024 == 0 && kStageABytes % 1024 == 0, "swizzled tiles on 1024-byte boundaries");
+    static_assert((kPairScaleFloats * 4) % 128 == 0, "scale entries 128-byte aligned");
+    static_assert(kPairTBufs * kPairTok <= kTmemCols, "TMEM buffers");
+    static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+};
 
 struct PairParams {
     GemmParams g;
@@ -676,34 +708,35 @@ __device__ __forceinline__ void tma_load_4d_pair(const void* tmap, uint32_t bar_
         :: "r"(smem_u32(dst)), "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(w), "r"(bar_cluster) : "memory");
 }
 
-template <bool kGated>
+template <bool kGated, bool kX2>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kNumThreads, 1)
 grouped_fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_a,
                              const __grid_constant__ CUtensorMap tmap_s, const PairParams pp) {
+    using P = PairCfg<kX2>;
     const GemmParams& p = pp.g;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
 
-    float* scale_ring = reinterpret_cast<float*>(smem + kPairOffScale);
-    float* amax_own = reinterpret_cast<float*>(smem + kPairOffAmax);
+    float* scale_ring = reinterpret_cast<float*>(smem + P::kOffScale);
+    float* amax_own = reinterpret_cast<float*>(smem + P::kOffAmax);
     float* amax_peer = amax_own + kPairTok;                                  // [2][128], written by the peer
-    int* t_prefix = reinterpret_cast<int*>(smem + kPairOffTables);
+    int* t_prefix = reinterpret_cast<int*>(smem + P::kOffTables);
     int* t_chunks = t_prefix + (kMaxGroups + 1);
     int* t_start = t_chunks + kMaxGroups;
     int* counts_smem = t_start + kMaxGroups;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kPairOffBars);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P::kOffBars);
     uint64_t* full_bar = bars;                              // used in the even CTA
-    uint64_t* empty_bar = full_bar + kPairStages;
-    uint64_t* sfull_bar = empty_bar + kPairStages;
+    uint64_t* empty_bar = full_bar + P::kStages;
+    uint64_t* sfull_bar = empty_bar + P::kStages;
     uint64_t* sempty_bar = sfull_bar + kPairSStages;
     uint64_t* cready_bar = sempty_bar + kPairSStages;
     uint64_t* tfull_bar = cready_bar + kPairSStages;
     uint64_t* tempty_bar = tfull_bar + kPairTBufs;          // used in the even CTA
     uint64_t* epi_bar = tempty_bar + kPairTBufs;
     uint64_t* xbar = epi_bar + 1;                           // [2]: the peer's amax has landed
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kPairOffMisc);
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kPairOffMisc + 8);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + P::kOffMisc);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + P::kOffMisc + 8);
 
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
@@ -718,7 +751,7 @@ grouped_fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const _
 
     // ---------------------------------------------------------------- setup
     if (warp == 0 && lane == 0) {
-        for (int s = 0; s < kPairStages; ++s) {
+        for (int s = 0; s < P::kStages; ++s) {
             mbar_init(&full_bar[s], 1);
             mbar_init(&empty_bar[s], 1);
         }
@@ -790,8 +823,8 @@ grouped_fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const _
             int s = 0, ss = 0;
             uint32_t phase = 0, sphase = 0;
             uint32_t sarmed_mask = 0, sarmed_phase = 0;
-            uint32_t full_leader[kPairStages];
-            for (int i = 0; i < kPairStages; ++i) full_leader[i] = mapa_u32(smem_u32(&full_bar[i]), 0);
+            uint32_t full_leader[P::kStages];
+            for (int i = 0; i < P::kStages; ++i) full_leader[i] = mapa_u32(smem_u32(&full_bar[i]), 0);
             bool ok = true;
             bool issued = false;
             // weights arrive from HBM: fetch them into L2 kPairPrefetch stages ahead of
@@ -823,16 +856,20 @@ grouped_fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const _
                     const int kb0 = ks * kPairKbPerStage;
                     prefetch_next();
                     if (!mbar_wait_bounded(&empty_bar[s], phase ^ 1, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
-                    uint8_t* st = smem + kPairOffStages + s * kPairStageBytes;
-                    if (rank == 0) mbar_arrive_expect_tx(&full_bar[s], 2 * kPairStageBytes);
+                    uint8_t* st = smem + P::kOffStages + s * P::kStageBytes;
+                    if (rank == 0) mbar_arrive_expect_tx(&full_bar[s], 2 * P::kStageBytes);
                     if (kGated)   // {128 B, 64 rows, gate/up, 2 K blocks}
                         tma_load_4d_pair(&tmap_w, full_leader[s], st, 0, wrow, 0, kb0);
                     else          // {128 B, 128 rows, 2 K blocks}
                         tma_load_3d_pair(&tmap_w, full_leader[s], st, 0, wrow, kb0);
-                    tma_load_3d_pair(&tmap_a, full_leader[s], st + kPairStageABytes, 0,
-                                     tc.row0 + static_cast<int>(rank) * half, kb0);
+                    if constexpr (kX2)   // {128 B, 64 rows, 2 K blocks, hi/lo}
+                        tma_load_4d_pair(&tmap_a, full_leader[s], st + P::kStageABytes, 0,
+                                         tc.row0 + static_cast<int>(rank) * half, kb0, 0);
+                    else                 // {128 B, 64 rows, 2 K blocks}
+                        tma_load_3d_pair(&tmap_a, full_leader[s], st + P::kStageABytes, 0,
+                                         tc.row0 + static_cast<int>(rank) * half, kb0);
                     issued = true;
-                    if (++s == kPairStages) { s = 0; phase ^= 1; }
+                    if (++s == P::kStages) { s = 0; phase ^= 1; }
 
                     if (!mbar_wait_bounded(&sempty_bar[ss], sphase ^ 1, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
                     mbar_arrive_expect_tx(&sfull_bar[ss], kPairScaleRaw * 4);
@@ -865,24 +902,28 @@ grouped_fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const _
                 const uint32_t idesc = idesc_e4m3_f32(2 * kTileM, tc.ntile);
                 for (int ks = 0; ks < KS && ok; ++ks) {
                     if (!mbar_wait_bounded(&full_bar[s], phase, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
-                    const uint32_t st_addr = smem_u32(smem + kPairOffStages + s * kPairStageBytes);
+                    const uint32_t st_addr = smem_u32(smem + P::kOffStages + s * P::kStageBytes);
                     for (int h = 0; h < kPairKbPerStage; ++h) {
                         if (!mbar_wait_bounded(&tempty_bar[b], tphase ^ 1, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
                         tc_fence_after();
                         const uint32_t a_addr = st_addr + h * kPairABytes;
-                        const uint32_t b_addr = st_addr + kPairStageABytes + h * kPairBBytes;
                         const uint32_t d = tmem_base + b * kPairTok;
+                        // two-plane mode: W (hi + lo) of the K block into one partial
 #pragma unroll
-                        for (int k = 0; k < kBlockK / 32; ++k)
-                            umma_f8_pair(d, umma_desc_sw128(a_addr + k * 32), umma_desc_sw128(b_addr + k * 32), idesc,
-                                         k > 0 ? 1u : 0u);
+                        for (int pl = 0; pl < P::kPlanes; ++pl) {
+                            const uint32_t b_addr = st_addr + P::kStageABytes + (pl * kPairKbPerStage + h) * kPairBBytes;
+#pragma unroll
+                            for (int k = 0; k < kBlockK / 32; ++k)
+                                umma_f8_pair(d, umma_desc_sw128(a_addr + k * 32), umma_desc_sw128(b_addr + k * 32), idesc,
+                                             (k > 0 || pl > 0) ? 1u : 0u);
+                        }
                         umma_commit_pair(&tfull_bar[b], both);
                         issued = true;
                         if (++b == kPairTBufs) { b = 0; tphase ^= 1; }
                     }
                     if (!ok) break;
                     umma_commit_pair(&empty_bar[s], both);
-                    if (++s == kPairStages) { s = 0; phase ^= 1; }
+                    if (++s == P::kStages) { s = 0; phase ^= 1; }
                 }
             }
             if (!ok && issued) {
@@ -995,7 +1036,7 @@ grouped_fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const _
             // ---------------------------------------------------------- epilogue
             // acc2[i] holds token columns 32 colgrp + 2i, + 1 of this lane's row
             if (kGated) {
-                float* hbuf = reinterpret_cast<float*>(smem + kPairOffEpi);   // [128 tokens][64 rows]
+                float* hbuf = reinterpret_cast<float*>(smem + P::kOffEpi);   // [128 tokens][64 rows]
                 if (quarter >= 2 && live) {
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
@@ -1047,25 +1088,38 @@ grouped_fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const _
                 const int col0 = tc.nb * 128 + 64 * static_cast<int>(rank);
                 for (int c = pw; c < tc.ntile; c += kNumPromoWarps) {
                     const size_t row = static_cast<size_t>(tc.row0 + c);
-                    uint8_t q0 = 0, q1 = 0;
+                    uint8_t q0 = 0, q1 = 0, l0 = 0, l1 = 0;
                     float scale = 0.0f;
                     if (c < tc.nrows) {
                         const float amax = fmaxf(amax_own[c], amax_peer[par * kPairTok + c]);
                         if (amax > 0.0f) {
                             const float inv = 448.0f / amax;
-                            const uint16_t q = cvt_e4m3x2(hbuf[c * 64 + lane] * inv, hbuf[c * 64 + lane + 32] * inv);
-                            q0 = static_cast<uint8_t>(q & 0xFF);
-                            q1 = static_cast<uint8_t>(q >> 8);
+                            if constexpr (kX2) {
+                                const uint32_t q = cvt_e4m3x2_split(__fmul_rn(hbuf[c * 64 + lane], inv),
+                                                                    __fmul_rn(hbuf[c * 64 + lane + 32], inv));
+                                q0 = static_cast<uint8_t>(q & 0xFF);
+                                q1 = static_cast<uint8_t>((q >> 8) & 0xFF);
+                                l0 = static_cast<uint8_t>((q >> 16) & 0xFF);
+                                l1 = static_cast<uint8_t>(q >> 24);
+                            } else {
+                                const uint16_t q = cvt_e4m3x2(hbuf[c * 64 + lane] * inv, hbuf[c * 64 + lane + 32] * inv);
+                                q0 = static_cast<uint8_t>(q & 0xFF);
+                                q1 = static_cast<uint8_t>(q >> 8);
+                            }
                             scale = amax / 448.0f;
                         }
                     }
                     outq[row * p.N + col0 + lane] = q0;
                     outq[row * p.N + col0 + 32 + lane] = q1;
+                    if constexpr (kX2) {
+                        outq[p.out_plane + row * p.N + col0 + lane] = l0;
+                        outq[p.out_plane + row * p.N + col0 + 32 + lane] = l1;
+                    }
                     if (rank == 0 && lane == 0) p.out_scale[(size_t)tc.nb * p.out_ld + row] = scale;
                 }
                 if (!group_sync()) { ok = false; break; }
             } else {
-                __nv_bfloat16* stage = reinterpret_cast<__nv_bfloat16*>(smem + kPairOffEpi);   // [128 tok][128]
+                __nv_bfloat16* stage = reinterpret_cast<__nv_bfloat16*>(smem + P::kOffEpi);   // [128 tok][128]
                 if (live) {
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
@@ -1127,6 +1181,21 @@ bool encode_u8_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t co
     return r == CUDA_SUCCESS;
 }
 
+// Two e4m3 planes [2][rows][cols] (lo plane `plane` bytes after hi) as a
+// 3-D tensor {cols, rows, plane}, box [2][box_rows][128], 128-byte swizzle.
+bool encode_u8_planes(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows,
+                      uint64_t plane) {
+    auto fn = get_encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {cols, rows, 2};
+    cuuint64_t strides[2] = {cols, plane};
+    cuuint32_t box[3] = {128, box_rows, 2};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // Gate and up weight rows of a group as one 3-D tensor {K, rows, gate/up}
 // (the up row of gate row r is r + N): box {128, 128, 2}, 128-byte swizzle.
 bool encode_gate_up_3d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t K, uint64_t N) {
@@ -1141,9 +1210,9 @@ bool encode_gate_up_3d(CUtensorMap* map, const void* base, uint64_t rows, uint64
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <bool kGated, bool kSmall>
+template <bool kGated, bool kSmall, bool kX2>
 cbwStatus_t launch_gemm(const cbwGroupedGemmArgs* a, int* error_word, cudaStream_t stream) {
-    using C = GemmCfg<kGated, kSmall>;
+    using C = GemmCfg<kGated, kSmall, kX2>;
     const int w_rows = kGated ? 2 * a->N : a->N;
     CUtensorMap tw, ta, ta64, ta128;
     if (kGated) {
@@ -1152,10 +1221,16 @@ cbwStatus_t launch_gemm(const cbwGroupedGemmArgs* a, int* error_word, cudaStream
     } else if (!encode_u8_2d(&tw, a->w, static_cast<uint64_t>(a->num_groups) * w_rows, a->K, kTileM)) {
         return CBW_ERROR_INTERNAL;
     }
-    if (!encode_u8_2d(&ta, a->a, static_cast<uint64_t>(a->rows), a->K, 32) ||
-        !encode_u8_2d(&ta64, a->a, static_cast<uint64_t>(a->rows), a->K, 64) ||
-        !encode_u8_2d(&ta128, a->a, static_cast<uint64_t>(a->rows), a->K, 128))
+    const uint64_t rows = static_cast<uint64_t>(a->rows), aplane = rows * static_cast<uint64_t>(a->K);
+    if (kX2) {
+        if (!encode_u8_planes(&ta, a->a, rows, a->K, 32, aplane) ||
+            !encode_u8_planes(&ta64, a->a, rows, a->K, 64, aplane) ||
+            !encode_u8_planes(&ta128, a->a, rows, a->K, 128, aplane))
+            return CBW_ERROR_INTERNAL;
+    } else if (!encode_u8_2d(&ta, a->a, rows, a->K, 32) || !encode_u8_2d(&ta64, a->a, rows, a->K, 64) ||
+               !encode_u8_2d(&ta128, a->a, rows, a->K, 128)) {
         return CBW_ERROR_INTERNAL;
+    }
 
     static int sm_count[kMaxDevices] = {};
     static bool attr_set[kMaxDevices] = {};
@@ -1169,7 +1244,7 @@ cbwStatus_t launch_gemm(const cbwGroupedGemmArgs* a, int* error_word, cudaStream
         if (dev >= 0 && dev < kMaxDevices) sm_count[dev] = sms;
     }
     {
-        cudaError_t e = smem_optin_once(grouped_fp8_gemm_kernel<kGated, kSmall>, C::kSmemBytes, attr_set);
+        cudaError_t e = smem_optin_once(grouped_fp8_gemm_kernel<kGated, kSmall, kX2>, C::kSmemBytes, attr_set);
         if (e != cudaSuccess) {
             std::fprintf(stderr, "cbwFp8BlockScaledGroupedGemm: shared memory opt-in (%d B) failed: %s\n",
                          C::kSmemBytes, cudaGetErrorString(e));
@@ -1185,16 +1260,17 @@ cbwStatus_t launch_gemm(const cbwGroupedGemmArgs* a, int* error_word, cudaStream
     p.out = a->out;
     p.out_scale = a->out_scale;
     p.out_ld = a->out_ld;
+    p.out_plane = static_cast<size_t>(a->rows) * a->N;
     p.G = a->num_groups;
     p.K = a->K;
     p.N = a->N;
     p.w_rows = w_rows;
     p.error_word = error_word;
-    grouped_fp8_gemm_kernel<kGated, kSmall><<<sms, kNumThreads, C::kSmemBytes, stream>>>(tw, ta, ta64, ta128, p);
+    grouped_fp8_gemm_kernel<kGated, kSmall, kX2><<<sms, kNumThreads, C::kSmemBytes, stream>>>(tw, ta, ta64, ta128, p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         cudaFuncAttributes fa;
-        cudaFuncGetAttributes(&fa, grouped_fp8_gemm_kernel<kGated, kSmall>);
+        cudaFuncGetAttributes(&fa, grouped_fp8_gemm_kernel<kGated, kSmall, kX2>);
         std::fprintf(stderr,
                      "cbwFp8BlockScaledGroupedGemm: launch failed: %s (regs %d, max threads %d, smem %d B)\n",
                      cudaGetErrorString(e), fa.numRegs, fa.maxThreadsPerBlock, C::kSmemBytes);
@@ -1206,9 +1282,11 @@ cbwStatus_t launch_gemm(const cbwGroupedGemmArgs* a, int* error_word, cudaStream
 // Tensor maps of the pair form: every load moves two K blocks.
 //   weights, gated: {128 B, rows, gate/up (I rows apart), K blocks} box {128, 64, 2, 2}
 //   weights, down:  {128 B, rows, K blocks} box {128, 128, 2}
-//   tokens:         {128 B, rows, K blocks} box {128, 64, 2}
+//   tokens:         {128 B, rows, K blocks} box {128, 64, 2}; two planes:
+//                   {128 B, rows, K blocks, hi/lo} box {128, 64, 2, 2}
 //   token scales:   fp32 {a_ld, K blocks} box {128, 2}
-bool encode_pair_maps(const cbwGroupedGemmArgs* a, bool gated, CUtensorMap* tw, CUtensorMap* ta, CUtensorMap* ts) {
+bool encode_pair_maps(const cbwGroupedGemmArgs* a, bool gated, bool x2, CUtensorMap* tw, CUtensorMap* ta,
+                      CUtensorMap* ts) {
     auto fn = get_encode_fn();
     if (!fn) return false;
     const cuuint64_t K = static_cast<cuuint64_t>(a->K), KB = K / 128;
@@ -1232,10 +1310,10 @@ bool encode_pair_maps(const cbwGroupedGemmArgs* a, bool gated, CUtensorMap* tw, 
     }
     if (r != CUDA_SUCCESS) return false;
     {
-        cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(a->rows), KB};
-        cuuint64_t str[2] = {K, 128};
-        cuuint32_t box[3] = {128, static_cast<cuuint32_t>(kPairBRows), static_cast<cuuint32_t>(kPairKbPerStage)};
-        if (fn(ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(a->a), dims, str, box, es,
+        cuuint64_t dims[4] = {128, static_cast<cuuint64_t>(a->rows), KB, 2};
+        cuuint64_t str[3] = {K, 128, static_cast<cuuint64_t>(a->rows) * K};
+        cuuint32_t box[4] = {128, static_cast<cuuint32_t>(kPairBRows), static_cast<cuuint32_t>(kPairKbPerStage), 2};
+        if (fn(ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, x2 ? 4 : 3, const_cast<void*>(a->a), dims, str, box, es,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return false;
@@ -1252,11 +1330,12 @@ bool encode_pair_maps(const cbwGroupedGemmArgs* a, bool gated, CUtensorMap* tw, 
     return true;
 }
 
-template <bool kGated>
+template <bool kGated, bool kX2>
 cbwStatus_t launch_gemm_pair(const cbwGroupedGemmArgs* a, int* error_word, cudaStream_t stream) {
+    using P = PairCfg<kX2>;
     const int w_rows = kGated ? 2 * a->N : a->N;
     CUtensorMap tw, ta, ts;
-    if (!encode_pair_maps(a, kGated, &tw, &ta, &ts)) return CBW_ERROR_INTERNAL;
+    if (!encode_pair_maps(a, kGated, kX2, &tw, &ta, &ts)) return CBW_ERROR_INTERNAL;
     static int sm_count[kMaxDevices] = {};
     static bool attr_set[kMaxDevices] = {};
     int dev = 0;
@@ -1269,10 +1348,10 @@ cbwStatus_t launch_gemm_pair(const cbwGroupedGemmArgs* a, int* error_word, cudaS
         if (dev >= 0 && dev < kMaxDevices) sm_count[dev] = sms;
     }
     {
-        cudaError_t e = smem_optin_once(grouped_fp8_gemm_pair_kernel<kGated>, kPairSmemBytes, attr_set);
+        cudaError_t e = smem_optin_once(grouped_fp8_gemm_pair_kernel<kGated, kX2>, P::kSmemBytes, attr_set);
         if (e != cudaSuccess) {
             std::fprintf(stderr, "cbwFp8BlockScaledGroupedGemm: shared memory opt-in (%d B) failed: %s\n",
-                         kPairSmemBytes, cudaGetErrorString(e));
+                         P::kSmemBytes, cudaGetErrorString(e));
             return CBW_ERROR_EXECUTION_FAILED;
         }
     }
@@ -1286,6 +1365,7 @@ cbwStatus_t launch_gemm_pair(const cbwGroupedGemmArgs* a, int* error_word, cudaS
     p.out = a->out;
     p.out_scale = a->out_scale;
     p.out_ld = a->out_ld;
+    p.out_plane = static_cast<size_t>(a->rows) * a->N;
     p.G = a->num_groups;
     p.K = a->K;
     p.N = a->N;
@@ -1293,7 +1373,7 @@ cbwStatus_t launch_gemm_pair(const cbwGroupedGemmArgs* a, int* error_word, cudaS
     p.error_word = error_word;
     pp.I = a->N;
     const int grid = (sms / 2) * 2;
-    grouped_fp8_gemm_pair_kernel<kGated><<<grid, kNumThreads, kPairSmemBytes, stream>>>(tw, ta, ts, pp);
+    grouped_fp8_gemm_pair_kernel<kGated, kX2><<<grid, kNumThreads, P::kSmemBytes, stream>>>(tw, ta, ts, pp);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         std::fprintf(stderr, "cbwFp8BlockScaledGroupedGemm: pair launch failed: %s\n", cudaGetErrorString(e));
@@ -1315,7 +1395,9 @@ extern "C" cbwStatus_t cbwFp8BlockScaledGroupedGemm(const cbwGroupedGemmArgs* ar
     if ((reinterpret_cast<uintptr_t>(a.a) | reinterpret_cast<uintptr_t>(a.w) |
          reinterpret_cast<uintptr_t>(a.a_scale) | reinterpret_cast<uintptr_t>(a.out)) & 15)
         return CBW_ERROR_INVALID_VALUE;
-    const int base = a.mode & 0xF, tiles = a.mode & ~0xF;
+    const int base = a.mode & 0xF, tiles = a.mode & 0xF0;
+    const bool x2 = (a.mode & CBW_GEMM_ACT_X2) != 0;
+    if (a.mode & ~(0xFF | CBW_GEMM_ACT_X2)) return CBW_ERROR_INVALID_VALUE;
     if (tiles != 0 && tiles != CBW_GEMM_SMALL_TILES && tiles != CBW_GEMM_FULL_TILES && tiles != CBW_GEMM_ONE_SM_TILES &&
         tiles != CBW_GEMM_PAIR_TILES)
         return CBW_ERROR_INVALID_VALUE;
@@ -1336,12 +1418,23 @@ extern "C" cbwStatus_t cbwFp8BlockScaledGroupedGemm(const cbwGroupedGemmArgs* ar
                       (tiles != CBW_GEMM_ONE_SM_TILES && base == CBW_GEMM_DOWN_BF16 && pair_ok);
     if (base == CBW_GEMM_GATED_SWIGLU) {
         if (!a.out_scale || a.out_ld < a.rows) return CBW_ERROR_INVALID_VALUE;
-        if (small) return launch_gemm<true, true>(&a, error_word, st);
-        return pair ? launch_gemm_pair<true>(&a, error_word, st) : launch_gemm<true, false>(&a, error_word, st);
+        if (x2) {
+            if (small) return launch_gemm<true, true, true>(&a, error_word, st);
+            return pair ? launch_gemm_pair<true, true>(&a, error_word, st) : launch_gemm<true, false, true>(&a, error_word, st);
+        }
+        if (small) return launch_gemm<true, true, false>(&a, error_word, st);
+        return pair ? launch_gemm_pair<true, false>(&a, error_word, st) : launch_gemm<true, false, false>(&a, error_word, st);
     }
     if (base == CBW_GEMM_DOWN_BF16) {
-        if (small) return launch_gemm<false, true>(&a, error_word, st);
-        return pair ? launch_gemm_pair<false>(&a, error_word, st) : launch_gemm<false, false>(&a, error_word, st);
+        if (x2) {
+            // the one-SM full form has no room for two token planes: pairs when the
+            // shape allows them, else the 32-token form
+            if (tiles == CBW_GEMM_ONE_SM_TILES) return CBW_ERROR_INVALID_VALUE;
+            if (small || !pair_ok) return launch_gemm<false, true, true>(&a, error_word, st);
+            return launch_gemm_pair<false, true>(&a, error_word, st);
+        }
+        if (small) return launch_gemm<false, true, false>(&a, error_word, st);
+        return pair ? launch_gemm_pair<false, false>(&a, error_word, st) : launch_gemm<false, false, false>(&a, error_word, st);
     }
     return CBW_ERROR_INVALID_VALUE;
 }

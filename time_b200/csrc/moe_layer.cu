@@ -76,6 +76,8 @@ struct moe_layer {
     uint32_t epoch;
     size_t off_plan;
     int gemm_form;        // 0 = by the rule in gemm_form(), else a CBW_GEMM_*_TILES flag
+    int act_planes = 1;   // 1: e4m3 activations; 2: two-term e4m3 (hi + lo residual)
+    size_t off_xq_lo = 0;  // [T][H] lo plane of xq (act_planes == 2)
 };
 
 namespace {
@@ -103,6 +105,7 @@ void plan_workspace(moe_layer* L) {
     L->off_logits = take(T * static_cast<size_t>(c.num_experts) * 4);
     if (H % 256 == 0) L->off_wrc = take(static_cast<size_t>(c.num_experts) * H * 4);
     L->off_xq = take(T * H);
+    if (L->act_planes == 2) L->off_xq_lo = take(T * H);
     L->off_xs = take((H / 128) * L->xs_ld * 4);
     L->off_idx = take(T * K * 4);
     L->off_w = take(T * K * 4);
@@ -111,9 +114,9 @@ void plan_workspace(moe_layer* L) {
     L->off_total = take(16);
     L->off_pos = take(T * K * 4);
     L->off_rowtok = take(R * 4);
-    L->off_xp = take(R * H);
+    L->off_xp = take(R * H * L->act_planes);     // [planes][R][H]: the lo plane R*H bytes on
     L->off_xps = take((H / 128) * R * 4);
-    L->off_hq = take(R * I);
+    L->off_hq = take(R * I * L->act_planes);     // [planes][R][I]
     L->off_hs = take((I / 128) * R * 4);
     L->off_y = take(R * H * 2);
     if (ep) {
@@ -179,7 +182,7 @@ cbwGroupedGemmArgs gemm_args(const moe_layer* L, void* ws, bool down, int T) {
     g.count = at<int32_t>(ws, L->off_counts);
     g.start = at<int32_t>(ws, L->off_start);
     if (!down) {
-        g.mode = CBW_GEMM_GATED_SWIGLU | gemm_form(L, T);
+        g.mode = CBW_GEMM_GATED_SWIGLU | gemm_form(L, T) | (L->act_planes == 2 ? CBW_GEMM_ACT_X2 : 0);
         g.K = c.hidden;
         g.N = c.intermediate;
         g.a = at<void>(ws, L->off_xp);
@@ -190,7 +193,7 @@ cbwGroupedGemmArgs gemm_args(const moe_layer* L, void* ws, bool down, int T) {
         g.out_scale = at<float>(ws, L->off_hs);
         g.out_ld = L->rcap;
     } else {
-        g.mode = CBW_GEMM_DOWN_BF16 | gemm_form(L, T);
+        g.mode = CBW_GEMM_DOWN_BF16 | gemm_form(L, T) | (L->act_planes == 2 ? CBW_GEMM_ACT_X2 : 0);
         g.K = c.intermediate;
         g.N = c.hidden;
         g.a = at<void>(ws, L->off_hq);
@@ -215,8 +218,11 @@ moe_status_t run_experts(moe_layer* L, const void* x, const int32_t* idx, const 
     MOE_TRY(moe_permute_mb(idx, T, K, L->e_begin, L->e_end, S, counts, start, pos, rowtok, total, L->rcap,
                            L->error_word, 16, at<void>(ws, L->off_bcounts), L->bcounts_bytes, st));
     mark(L, 3, st);
-    MOE_TRY(moe_gather_rows_n(at<void>(ws, L->off_xq), at<float>(ws, L->off_xs), L->xs_ld, rowtok, total, L->rcap, H,
-                              at<void>(ws, L->off_xp), at<float>(ws, L->off_xps), L->rcap, st));
+    const bool x2 = L->act_planes == 2;
+    MOE_TRY(moe_gather_rows_x2(at<void>(ws, L->off_xq), x2 ? at<void>(ws, L->off_xq_lo) : nullptr,
+                               at<float>(ws, L->off_xs), L->xs_ld, rowtok, total, L->rcap, H, at<void>(ws, L->off_xp),
+                               x2 ? at<void>(ws, L->off_xp + L->rcap * static_cast<size_t>(H)) : nullptr,
+                               at<float>(ws, L->off_xps), L->rcap, st));
     cbwGroupedGemmArgs g1 = gemm_args(L, ws, false, T), g2 = gemm_args(L, ws, true, T);
     mark(L, 4, st);
     MOE_TRY(cbw_to_moe(cbwFp8BlockScaledGroupedGemm(&g1, L->error_word, st)));
@@ -380,6 +386,7 @@ moe_status_t moe_layer_create(const moe_layer_config_t* cfg, const moe_layer_wei
     moe_layer* L = new (std::nothrow) moe_layer;
     if (!L) return MOE_ERR_INVALID_ARGUMENT;
     std::memset(L, 0, sizeof(*L));
+    L->act_planes = 1;
     L->cfg = c;
     L->w = *w;
     L->comm = comm;
@@ -423,8 +430,13 @@ moe_status_t moe_layer_forward_routed(moe_layer_t* L, const void* x, const int32
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const moe_layer_config_t& c = L->cfg;
     mark(L, 0, st);
-    MOE_TRY(moe_rmsnorm_quant(x, L->w.norm_gamma, T, c.hidden, c.rms_eps, at<float>(ws, L->off_rms),
-                              at<void>(ws, L->off_xq), at<float>(ws, L->off_xs), L->xs_ld, stream));
+    if (L->act_planes == 2)
+        MOE_TRY(moe_rmsnorm_quant_x2(x, L->w.norm_gamma, T, c.hidden, c.rms_eps, at<float>(ws, L->off_rms), nullptr,
+                                     0, at<void>(ws, L->off_xq), at<void>(ws, L->off_xq_lo), at<float>(ws, L->off_xs),
+                                     L->xs_ld, stream));
+    else
+        MOE_TRY(moe_rmsnorm_quant(x, L->w.norm_gamma, T, c.hidden, c.rms_eps, at<float>(ws, L->off_rms),
+                                  at<void>(ws, L->off_xq), at<float>(ws, L->off_xs), L->xs_ld, stream));
     mark(L, 1, st);
     return run_experts_any(L, x, idx, wts, out, T, ws, st);
 }
@@ -445,7 +457,11 @@ moe_status_t moe_layer_forward(moe_layer_t* L, const void* x, void* out, int T, 
     // column-ordered router: n is written in that order by the RMSNorm and
     // the router weight is reordered into the workspace (E x H floats)
     const bool rc = c.hidden % 256 == 0;
-    if (rc)
+    if (L->act_planes == 2)
+        MOE_TRY(moe_rmsnorm_quant_x2(x, L->w.norm_gamma, T, c.hidden, c.rms_eps, rms, n, rc ? 1 : 0,
+                                     at<void>(ws, L->off_xq), at<void>(ws, L->off_xq_lo), at<float>(ws, L->off_xs),
+                                     L->xs_ld, stream));
+    else if (rc)
         MOE_TRY(moe_rmsnorm_quant_rc(x, L->w.norm_gamma, T, c.hidden, c.rms_eps, rms, n, at<void>(ws, L->off_xq),
                                      at<float>(ws, L->off_xs), L->xs_ld, stream));
     else
@@ -480,6 +496,21 @@ moe_status_t moe_layer_set_stage_events(moe_layer_t* L, cwEvent_t* events) {
     L->timing = events != nullptr;
     for (int i = 0; i <= MOE_NUM_STAGES; ++i)
         L->stage_ev[i] = events ? static_cast<cudaEvent_t>(events[i]) : nullptr;
+    return MOE_OK;
+}
+
+moe_status_t moe_layer_set_act_planes(moe_layer_t* L, int planes) {
+    if (!L || (planes != 1 && planes != 2)) return MOE_ERR_INVALID_ARGUMENT;
+    // the expert-parallel exchange moves one e4m3 plane per row
+    if (planes == 2 && L->cfg.ep_size > 1) return MOE_ERR_UNSUPPORTED;
+    L->act_planes = planes;
+    plan_workspace(L);
+    return MOE_OK;
+}
+
+moe_status_t moe_layer_get_act_planes(const moe_layer_t* L, int* planes) {
+    if (!L || !planes) return MOE_ERR_INVALID_ARGUMENT;
+    *planes = L->act_planes;
     return MOE_OK;
 }
 

@@ -83,7 +83,7 @@ template <bool kRc>
 __global__ void __launch_bounds__(256)
 rmsnorm_quant_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ gamma, int T, int H,
                      float eps, float* __restrict__ rms_out, float* __restrict__ n_out, uint8_t* __restrict__ xq,
-                     float* __restrict__ xs, int xs_ld) {
+                     uint8_t* __restrict__ xq_lo, float* __restrict__ xs, int xs_ld) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (warp >= T) return;
@@ -92,6 +92,7 @@ rmsnorm_quant_kernel(const __nv_bfloat16* __restrict__ x, const float* __restric
     const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(H)), eps));
     if (rms_out && lane == 0) rms_out[warp] = rms;
     uint8_t* qr = xq + static_cast<size_t>(warp) * H;
+    uint8_t* lr = xq_lo ? xq_lo + static_cast<size_t>(warp) * H : nullptr;
     for (int b = 0; b < H / 128; ++b) {
         const int c = b * 128 + lane * 4;
         const uint2 raw = *reinterpret_cast<const uint2*>(xr + c);
@@ -104,15 +105,23 @@ rmsnorm_quant_kernel(const __nv_bfloat16* __restrict__ x, const float* __restric
         float amax = fmaxf(fmaxf(fabsf(v0), fabsf(v1)), fmaxf(fabsf(v2), fabsf(v3)));
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        uint32_t packed = 0;
+        uint32_t packed = 0, packed_lo = 0;
         float scale = 0.0f;
         if (amax > 0.0f) {
             const float inv = __fdiv_rn(448.0f, amax);
-            packed = static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v0, inv), __fmul_rn(v1, inv))) |
-                     (static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v2, inv), __fmul_rn(v3, inv))) << 16);
+            if (lr) {   // two planes: hi, and the e4m3 residual (one scale)
+                const uint32_t s0 = cvt_e4m3x2_split(__fmul_rn(v0, inv), __fmul_rn(v1, inv));
+                const uint32_t s1 = cvt_e4m3x2_split(__fmul_rn(v2, inv), __fmul_rn(v3, inv));
+                packed = (s0 & 0xFFFFu) | (s1 << 16);
+                packed_lo = (s0 >> 16) | (s1 & 0xFFFF0000u);
+            } else {
+                packed = static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v0, inv), __fmul_rn(v1, inv))) |
+                         (static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v2, inv), __fmul_rn(v3, inv))) << 16);
+            }
             scale = __fdiv_rn(amax, 448.0f);
         }
         *reinterpret_cast<uint32_t*>(qr + c) = packed;
+        if (lr) *reinterpret_cast<uint32_t*>(lr + c) = packed_lo;
         if (lane == 0) xs[static_cast<size_t>(b) * xs_ld + warp] = scale;
     }
 }
@@ -129,7 +138,7 @@ template <bool kRc>
 __global__ void __launch_bounds__(256)
 rmsnorm_quant_block_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ gamma, int T, int H,
                            float eps, float* __restrict__ rms_out, float* __restrict__ n_out,
-                           uint8_t* __restrict__ xq, float* __restrict__ xs, int xs_ld) {
+                           uint8_t* __restrict__ xq, uint8_t* __restrict__ xq_lo, float* __restrict__ xs, int xs_ld) {
     __shared__ float part[8][32];
     __shared__ float s_rms;
     __shared__ __align__(16) __nv_bfloat16 row_s[kRmsRowMax];
@@ -169,6 +178,7 @@ rmsnorm_quant_block_kernel(const __nv_bfloat16* __restrict__ x, const float* __r
     const float rms = s_rms;
     if (rms_out && threadIdx.x == 0) rms_out[t] = rms;
     uint8_t* qr = xq + static_cast<size_t>(t) * H;
+    uint8_t* lr = xq_lo ? xq_lo + static_cast<size_t>(t) * H : nullptr;
     for (int b = warp; b < H / 128; b += 8) {
         const int c = b * 128 + lane * 4;
         const uint2 raw = *reinterpret_cast<const uint2*>(row_s + c);
@@ -181,15 +191,23 @@ rmsnorm_quant_block_kernel(const __nv_bfloat16* __restrict__ x, const float* __r
         float amax = fmaxf(fmaxf(fabsf(v0), fabsf(v1)), fmaxf(fabsf(v2), fabsf(v3)));
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        uint32_t packed = 0;
+        uint32_t packed = 0, packed_lo = 0;
         float scale = 0.0f;
         if (amax > 0.0f) {
             const float inv = __fdiv_rn(448.0f, amax);
-            packed = static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v0, inv), __fmul_rn(v1, inv))) |
-                     (static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v2, inv), __fmul_rn(v3, inv))) << 16);
+            if (lr) {   // two planes: hi, and the e4m3 residual (one scale)
+                const uint32_t s0 = cvt_e4m3x2_split(__fmul_rn(v0, inv), __fmul_rn(v1, inv));
+                const uint32_t s1 = cvt_e4m3x2_split(__fmul_rn(v2, inv), __fmul_rn(v3, inv));
+                packed = (s0 & 0xFFFFu) | (s1 << 16);
+                packed_lo = (s0 >> 16) | (s1 & 0xFFFF0000u);
+            } else {
+                packed = static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v0, inv), __fmul_rn(v1, inv))) |
+                         (static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v2, inv), __fmul_rn(v3, inv))) << 16);
+            }
             scale = __fdiv_rn(amax, 448.0f);
         }
         *reinterpret_cast<uint32_t*>(qr + c) = packed;
+        if (lr) *reinterpret_cast<uint32_t*>(lr + c) = packed_lo;
         if (lane == 0) xs[static_cast<size_t>(b) * xs_ld + t] = scale;
     }
 }
@@ -1152,7 +1170,8 @@ mp_scatter_kernel(const int32_t* __restrict__ idx, int P, int K, int e_begin, in
 __global__ void __launch_bounds__(256)
 gather_rows_kernel(const uint8_t* __restrict__ xq, const float* __restrict__ xs, int xs_ld,
                    const int32_t* __restrict__ row_token, const int32_t* __restrict__ total_rows,
-                   int row_capacity, int H, uint8_t* __restrict__ xp, float* __restrict__ xps, int xps_ld) {
+                   int row_capacity, int H, uint8_t* __restrict__ xp, float* __restrict__ xps, int xps_ld,
+                   const uint8_t* __restrict__ xq_lo, uint8_t* __restrict__ xp_lo) {
     const int R = total_rows ? min(*total_rows, row_capacity) : row_capacity;
     const int lane = threadIdx.x & 31;
     const int nwarps = (gridDim.x * blockDim.x) >> 5;
@@ -1160,13 +1179,20 @@ gather_rows_kernel(const uint8_t* __restrict__ xq, const float* __restrict__ xs,
     for (int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < R; r += nwarps) {
         const int t = row_token[r];
         int4* dst = reinterpret_cast<int4*>(xp + static_cast<size_t>(r) * H);
+        int4* dlo = xp_lo ? reinterpret_cast<int4*>(xp_lo + static_cast<size_t>(r) * H) : nullptr;
         if (t >= 0) {
             const int4* src = reinterpret_cast<const int4*>(xq + static_cast<size_t>(t) * H);
             for (int i = lane; i < vec; i += 32) dst[i] = src[i];
+            if (dlo) {
+                const int4* slo = reinterpret_cast<const int4*>(xq_lo + static_cast<size_t>(t) * H);
+                for (int i = lane; i < vec; i += 32) dlo[i] = slo[i];
+            }
             for (int b = lane; b < H / 128; b += 32) xps[static_cast<size_t>(b) * xps_ld + r] = xs[static_cast<size_t>(b) * xs_ld + t];
         } else {
             const int4 z = make_int4(0, 0, 0, 0);
             for (int i = lane; i < vec; i += 32) dst[i] = z;
+            if (dlo)
+                for (int i = lane; i < vec; i += 32) dlo[i] = z;
             for (int b = lane; b < H / 128; b += 32) xps[static_cast<size_t>(b) * xps_ld + r] = 0.0f;
         }
     }
@@ -1279,7 +1305,7 @@ namespace {
 template <bool kRc>
 moe_status_t rmsnorm_quant_launch(const void* x_bf16, const float* gamma, int T, int H, float eps,
                                   float* rms_out, float* n_out, void* xq_out, float* xs_out, int xs_ld,
-                                  cwStream_t stream) {
+                                  cwStream_t stream, void* xq_lo_out = nullptr) {
     if (T < 0 || H <= 0 || H % 128 || xs_ld < T) return MOE_ERR_INVALID_ARGUMENT;
     if (kRc && (H % 256 || !n_out)) return MOE_ERR_INVALID_ARGUMENT;
     if (T == 0) return MOE_OK;
@@ -1287,14 +1313,15 @@ moe_status_t rmsnorm_quant_launch(const void* x_bf16, const float* gamma, int T,
     if (!aligned16(x_bf16) || !aligned16(gamma) || !aligned16(xq_out)) return MOE_ERR_INVALID_ARGUMENT;
     const int blocks = (T + 7) / 8;
     if (n_out && !aligned16(n_out)) return MOE_ERR_INVALID_ARGUMENT;
+    if (xq_lo_out && !aligned16(xq_lo_out)) return MOE_ERR_INVALID_ARGUMENT;
     if (T <= kRmsBlockPerTokenMaxT && H <= kRmsRowMax)
         rmsnorm_quant_block_kernel<kRc><<<T, 256, 0, static_cast<cudaStream_t>(stream)>>>(
             static_cast<const __nv_bfloat16*>(x_bf16), gamma, T, H, eps, rms_out, n_out,
-            static_cast<uint8_t*>(xq_out), xs_out, xs_ld);
+            static_cast<uint8_t*>(xq_out), static_cast<uint8_t*>(xq_lo_out), xs_out, xs_ld);
     else
         rmsnorm_quant_kernel<kRc><<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
             static_cast<const __nv_bfloat16*>(x_bf16), gamma, T, H, eps, rms_out, n_out,
-            static_cast<uint8_t*>(xq_out), xs_out, xs_ld);
+            static_cast<uint8_t*>(xq_out), static_cast<uint8_t*>(xq_lo_out), xs_out, xs_ld);
     return launch_status();
 }
 }  // namespace
@@ -1311,6 +1338,16 @@ moe_status_t moe_rmsnorm_quant_rc(const void* x_bf16, const float* gamma, int T,
                                   float* rms_out, float* n_rc_out, void* xq_out, float* xs_out, int xs_ld,
                                   cwStream_t stream) {
     return rmsnorm_quant_launch<true>(x_bf16, gamma, T, H, eps, rms_out, n_rc_out, xq_out, xs_out, xs_ld, stream);
+}
+
+moe_status_t moe_rmsnorm_quant_x2(const void* x_bf16, const float* gamma, int T, int H, float eps, float* rms_out,
+                                  float* n_out, int n_router_cols, void* xq_out, void* xq_lo_out, float* xs_out,
+                                  int xs_ld, cwStream_t stream) {
+    if (!xq_lo_out) return MOE_ERR_INVALID_ARGUMENT;
+    return n_router_cols
+        ? rmsnorm_quant_launch<true>(x_bf16, gamma, T, H, eps, rms_out, n_out, xq_out, xs_out, xs_ld, stream, xq_lo_out)
+        : rmsnorm_quant_launch<false>(x_bf16, gamma, T, H, eps, rms_out, n_out, xq_out, xs_out, xs_ld, stream,
+                                      xq_lo_out);
 }
 
 moe_status_t moe_rmsnorm_quant(const void* x_bf16, const float* gamma, int T, int H, float eps,
@@ -1542,18 +1579,26 @@ moe_status_t moe_permute_mb(const int32_t* topk_idx, int T, int k, int e_begin, 
     return launch_status();
 }
 
-moe_status_t moe_gather_rows_n(const void* xq, const float* xs, int xs_ld, const int32_t* row_token,
-                               const int32_t* total_rows, int row_capacity, int H, void* xp, float* xps,
-                               int xps_ld, cwStream_t stream) {
+moe_status_t moe_gather_rows_x2(const void* xq, const void* xq_lo, const float* xs, int xs_ld,
+                                const int32_t* row_token, const int32_t* total_rows, int row_capacity, int H,
+                                void* xp, void* xp_lo, float* xps, int xps_ld, cwStream_t stream) {
     if (H <= 0 || H % 128 || !xq || !xs || !row_token || !xp || !xps || row_capacity < 0 || xps_ld < row_capacity) return MOE_ERR_INVALID_ARGUMENT;
     if (!aligned16(xq) || !aligned16(xp)) return MOE_ERR_INVALID_ARGUMENT;
+    if (!xq_lo != !xp_lo || (xq_lo && (!aligned16(xq_lo) || !aligned16(xp_lo)))) return MOE_ERR_INVALID_ARGUMENT;
     if (row_capacity == 0) return MOE_OK;
     int blocks = (row_capacity + 7) / 8;
     if (blocks > 148 * 16) blocks = 148 * 16;
     gather_rows_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const uint8_t*>(xq), xs, xs_ld, row_token, total_rows, row_capacity, H,
-        static_cast<uint8_t*>(xp), xps, xps_ld);
+        static_cast<uint8_t*>(xp), xps, xps_ld, static_cast<const uint8_t*>(xq_lo), static_cast<uint8_t*>(xp_lo));
     return launch_status();
+}
+
+moe_status_t moe_gather_rows_n(const void* xq, const float* xs, int xs_ld, const int32_t* row_token,
+                               const int32_t* total_rows, int row_capacity, int H, void* xp, float* xps,
+                               int xps_ld, cwStream_t stream) {
+    return moe_gather_rows_x2(xq, nullptr, xs, xs_ld, row_token, total_rows, row_capacity, H, xp, nullptr, xps,
+                              xps_ld, stream);
 }
 
 moe_status_t moe_gather_rows(const void* xq, const float* xs, int xs_ld, const int32_t* row_token,

@@ -331,6 +331,28 @@ __device__ __forceinline__ uint16_t cvt_e4m3x2(float a, float b) {
     return r;
 }
 
+// Two e4m3 bytes (low byte first) -> two floats, exactly (e4m3 -> f16 is exact).
+__device__ __forceinline__ float2 e4m3x2_to_float2(uint16_t v) {
+    float x, y;
+    asm("{\n\t.reg .b32 h;\n\t.reg .b16 lo, hi;\n\t"
+        "cvt.rn.f16x2.e4m3x2 h, %2;\n\t"
+        "mov.b32 {lo, hi}, h;\n\t"
+        "cvt.f32.f16 %0, lo;\n\t"
+        "cvt.f32.f16 %1, hi;\n\t}"
+        : "=f"(x), "=f"(y) : "h"(v));
+    return make_float2(x, y);
+}
+
+// Two-term e4m3 quantisation of u0, u1 (values already divided by the block
+// scale): hi = e4m3_rne(u), lo = e4m3_rne(u - decode(hi)); u ~= hi + lo with
+// the residual's own 3 mantissa bits.  Returns hi | lo << 16 (low byte = u0).
+__device__ __forceinline__ uint32_t cvt_e4m3x2_split(float u0, float u1) {
+    const uint16_t hi = cvt_e4m3x2(u0, u1);
+    const float2 d = e4m3x2_to_float2(hi);
+    const uint16_t lo = cvt_e4m3x2(__fsub_rn(u0, d.x), __fsub_rn(u1, d.y));
+    return static_cast<uint32_t>(hi) | (static_cast<uint32_t>(lo) << 16);
+}
+
 // ---------------------------------------------------------------- host
 
 constexpr int kMaxDevices = 64;

@@ -54,6 +54,7 @@ GEMM_SMALL_TILES = 0x10   # or-ed into a mode: the decode form (tiles of <= 32 r
 GEMM_FULL_TILES = 0x20
 GEMM_ONE_SM_TILES = 0x40  # the full form on one SM per tile
 GEMM_PAIR_TILES = 0x80    # the full form on pairs of SMs (tcgen05 cta_group::2)
+GEMM_ACT_X2 = 0x100       # two-term e4m3 activations (hi plane, lo plane rows*K bytes on)
 
 _bound = False
 
@@ -101,6 +102,12 @@ def libs():
                                          c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p]
         k.moe_layer_set_expert_placement.argtypes = [c_void_p, c_void_p]
         k.moe_layer_set_gemm_form.argtypes = [c_void_p, c_int]
+        k.moe_layer_set_act_planes.argtypes = [c_void_p, c_int]
+        k.moe_layer_get_act_planes.argtypes = [c_void_p, ctypes.POINTER(c_int)]
+        k.moe_rmsnorm_quant_x2.argtypes = [c_void_p, c_void_p, c_int, c_int, c_float, c_void_p, c_void_p, c_int,
+                                           c_void_p, c_void_p, c_void_p, c_int, c_void_p]
+        k.moe_gather_rows_x2.argtypes = [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int, c_int,
+                                         c_void_p, c_void_p, c_void_p, c_int, c_void_p]
         k.moe_ep_remap_experts.argtypes = [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p]
         k.moe_layer_peer_bytes.argtypes = [c_void_p]
         k.moe_layer_peer_bytes.restype = c_size_t
@@ -280,6 +287,21 @@ class MoELayer:
     def set_gemm_form(self, form: int):
         """GEMM_SMALL_TILES, GEMM_FULL_TILES or 0 (the layer's rule)."""
         check("moe_layer_set_gemm_form", self._k.moe_layer_set_gemm_form(self._h, form))
+
+    def set_act_planes(self, planes: int):
+        """1: e4m3 activations; 2: two-term e4m3 (hi + lo residual, one scale).
+        Re-sizes the workspace (allocated again on the next forward)."""
+        check("moe_layer_set_act_planes", self._k.moe_layer_set_act_planes(self._h, planes))
+        nbytes = self._k.moe_layer_workspace_bytes(self._h)
+        if nbytes != self.workspace_bytes:
+            self.workspace_bytes = nbytes
+            self.workspace = None
+
+    @property
+    def act_planes(self) -> int:
+        v = c_int()
+        check("moe_layer_get_act_planes", self._k.moe_layer_get_act_planes(self._h, ctypes.byref(v)))
+        return v.value
 
     def use_peer_memory(self, group=None):
         """Switch the expert-parallel exchange to NVLink peer memory: allocate
