@@ -220,16 +220,19 @@ def parity_of(out_gpu, ref_bits, n: int, act_planes: int = 1):
 
 # ---------------------------------------------------------------- algorithmic work
 
-def algorithmic(shape, counts, T):
-    """Bytes / FLOPs the layer must move or do, from the actual routing."""
+def algorithmic(shape, counts, T, planes: int = 1):
+    """Bytes / FLOPs the layer must move or do, from the actual routing.  With
+    two-term activations (planes = 2) each e4m3 activation row is read or
+    written twice (hi and lo planes); the FLOPs are the layer's arithmetic
+    (the tensor cores do `planes` times the MMA work of it)."""
     H, I, E, S, k = shape.hidden, shape.intermediate, shape.num_experts, shape.num_shared, shape.top_k
     counts = [int(c) for c in counts]
     touched = [c > 0 for c in counts]
     rows = sum(counts)
     w13 = 2 * I * H + (2 * I // 128) * (H // 128) * 4
     w2 = H * I + (H // 128) * (I // 128) * 4
-    g1_bytes = sum(w13 for t in touched if t) + rows * (H + H // 128 * 4) + rows * (I + I // 128 * 4)
-    g2_bytes = sum(w2 for t in touched if t) + rows * (I + I // 128 * 4) + rows * H * 2
+    g1_bytes = sum(w13 for t in touched if t) + rows * (planes * H + H // 128 * 4) + rows * (planes * I + I // 128 * 4)
+    g2_bytes = sum(w2 for t in touched if t) + rows * (planes * I + I // 128 * 4) + rows * H * 2
     g1_flops = 2.0 * rows * H * 2 * I
     g2_flops = 2.0 * rows * I * H
     layer_bytes = sum(w13 + w2 for t in touched if t) + T * H * 2 * 2 + E * H * 4
@@ -238,12 +241,14 @@ def algorithmic(shape, counts, T):
             "layer": (layer_bytes, layer_flops), "rows": rows}
 
 
-def load_traffic(kernel: str):
+def load_traffic(kernel: str, planes: int = 1):
+    """ncu DRAM bytes per full launch of `kernel` (profiles/traffic.json; keys
+    with a "_x2" suffix for two-term activations), or None."""
     p = ROOT / "profiles" / "traffic.json"
     if not p.exists():
         return None
     try:
-        return json.loads(p.read_text()).get(kernel)
+        return json.loads(p.read_text()).get(kernel + ("_x2" if planes == 2 else ""))
     except Exception:
         return None
 
@@ -474,14 +479,14 @@ def run_ours(args):
     if world > 1:
         import dataclasses
         local_shape = dataclasses.replace(shape, num_experts=G_local)
-    work = algorithmic(local_shape, counts.tolist(), Tr)
+    work = algorithmic(local_shape, counts.tolist(), Tr, act_planes)
     dom = max(("gemm_gate_up", "gemm_down"), key=lambda n: stages[n])
     dom_bytes, dom_flops = work[dom]
     dom_s = stages[dom] / 1000.0
     achieved_gbs = dom_bytes / dom_s / 1e9
     roofline = {"kernel": dom, "bound": "hbm", "achieved": achieved_gbs, "peak": peaks["hbm_gbs"],
                 "unit": "GB/s", "frac": achieved_gbs / peaks["hbm_gbs"],
-                "traffic": load_traffic(dom) if not decode else None,
+                "traffic": load_traffic(dom, act_planes) if not decode else None,
                 "peak_source": peaks["source"], "algorithmic_bytes": dom_bytes,
                 "tensor_tflops": dom_flops / dom_s / 1e12}
     lb, lf = work["layer"]

@@ -3,16 +3,19 @@ self-contained launches of single stages of the MoE FFN block, for
 timing with CUDA events and for ncu captures that must stay small (a few
 hundred MB on the device, a handful of launches):
 
-    python profile_cases.py router [--tokens 4096] [--iters 3]
-    python profile_cases.py gemm   [--tokens 4096] [--experts 32] [--iters 3]
+    python profile_cases.py router [--tokens 4096] [--iters 3] [--plain]
+    python profile_cases.py gemm   [--tokens 4096] [--experts 32] [--iters 3] [--act-planes 1|2]
     python profile_cases.py attention [--batch 64] [--ctx-min 1024] [--ctx-max 32768] [--iters 3]
     python profile_cases.py attn_block [--batch 64] [--ctx-min 1024] [--ctx-max 32768] [--iters 3]
     python profile_cases.py serving [--batch 64] [--prompt 512] [--steps 10] [--layers 92]
 
-`router`: RMSNorm+quant (with the fp32 n rows), tiled router logits, top-k
+`router`: RMSNorm+quant (with the fp32 n rows), the router logits, top-k
 over T tokens of the GLM shape (hidden 5120, 160 experts; n is 84 MB at 4096
-tokens, larger than L2).  `gemm`: the layer forward on a reduced expert count
-(weights 23.6 MB per expert) -- the grouped GEMMs are its top kernels.
+tokens, larger than L2) -- the layer's column-ordered path (n written in the
+router column order, W reordered, `router_logits_rc_kernel`), or with
+`--plain` the plain-layout `moe_router_logits`.  `gemm`: the layer forward on
+a reduced expert count (weights 23.6 MB per expert) with one or two
+activation planes -- the grouped GEMMs are its top kernels.
 `attention`: paged decode attention at the per-rank shape of the TP=8
 attention block (12 query heads over 1 KV head, head_dim 128, bf16 pages of
 16 tokens), one new token per sequence with contexts drawn uniformly from
@@ -59,7 +62,7 @@ def _time(fn, iters: int) -> float:
     return a.elapsed_time(b) / iters
 
 
-def router(tokens: int, iters: int) -> dict:
+def router(tokens: int, iters: int, plain: bool = False) -> dict:
     k = M.libs()["libkernels.so"]
     shape = synth.GLM
     dev = torch.device("cuda", 0)
@@ -79,12 +82,20 @@ def router(tokens: int, iters: int) -> dict:
     w = torch.empty(T, K, device=dev)
     s = torch.cuda.current_stream().cuda_stream
 
+    wrc = torch.empty_like(W)
+    norm_fn = k.moe_rmsnorm_quant_n if plain else k.moe_rmsnorm_quant_rc
+
     def norm():
-        M.check("rmsnorm_n", k.moe_rmsnorm_quant_n(M.ptr(x), M.ptr(gamma), T, H, shape.eps, M.ptr(rms), M.ptr(n),
-                                                   M.ptr(xq), M.ptr(xs), ld, s))
+        M.check("rmsnorm", norm_fn(M.ptr(x), M.ptr(gamma), T, H, shape.eps, M.ptr(rms), M.ptr(n),
+                                   M.ptr(xq), M.ptr(xs), ld, s))
 
     def logit():
-        M.check("router_logits", k.moe_router_logits(M.ptr(n), M.ptr(W), M.ptr(bias), T, H, E, M.ptr(logits), s))
+        if plain:
+            M.check("router_logits", k.moe_router_logits(M.ptr(n), M.ptr(W), M.ptr(bias), T, H, E, M.ptr(logits), s))
+        else:
+            M.check("router_columns", k.moe_router_columns(M.ptr(W), M.ptr(wrc), E, H, s))
+            M.check("router_logits_rc", k.moe_router_logits_rc(M.ptr(n), M.ptr(wrc), M.ptr(bias), T, H, E,
+                                                                 M.ptr(logits), s))
 
     def topk():
         M.check("topk", k.moe_topk_softmax(M.ptr(logits), T, E, K, M.ptr(idx), M.ptr(w), s))
@@ -97,12 +108,14 @@ def router(tokens: int, iters: int) -> dict:
     return out
 
 
-def gemm(tokens: int, experts: int, iters: int, zipf: bool = True) -> dict:
+def gemm(tokens: int, experts: int, iters: int, zipf: bool = True, planes: int = 1) -> dict:
     shape = dataclasses.replace(synth.GLM, num_experts=experts)
     dev = torch.device("cuda", 0)
     w = synth.make_moe_weights(shape, seed=0, device=dev, zipf_bias=zipf)
     x = synth.make_x(shape, tokens, seed=1, device=dev)
     layer = M.MoELayer(shape, w, max_tokens=tokens)
+    if planes == 2:
+        layer.set_act_planes(2)
     out = torch.empty_like(x)
     ms = _time(lambda: layer.forward(x, out), iters)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(M.NUM_STAGES + 1)]
@@ -121,9 +134,9 @@ def gemm(tokens: int, experts: int, iters: int, zipf: bool = True) -> dict:
     touched = int((counts > 0).sum())
     w13 = 2 * I * H + (2 * I // 128) * (H // 128) * 4
     w2 = H * I + (H // 128) * (I // 128) * 4
-    gu = touched * w13 + rows * (H + H // 128 * 4) + rows * (I + I // 128 * 4)
-    dn = touched * w2 + rows * (I + I // 128 * 4) + rows * H * 2
-    return {"layer_forward_ms": ms, "stage_ms": stages, "rows": rows, "touched_groups": touched,
+    gu = touched * w13 + rows * (planes * H + H // 128 * 4) + rows * (planes * I + I // 128 * 4)
+    dn = touched * w2 + rows * (planes * I + I // 128 * 4) + rows * H * 2
+    return {"layer_forward_ms": ms, "stage_ms": stages, "rows": rows, "touched_groups": touched, "act_planes": planes,
             "gemm_gate_up_bytes": gu, "gemm_down_bytes": dn,
             "gate_up_gbs": gu / (stages["gemm_gate_up"] * 1e-3) / 1e9,
             "down_gbs": dn / (stages["gemm_down"] * 1e-3) / 1e9}
@@ -343,6 +356,8 @@ def main() -> int:
     ap.add_argument("--tokens", type=int, default=4096)
     ap.add_argument("--experts", type=int, default=32)
     ap.add_argument("--iters", type=int, default=3)
+    ap.add_argument("--plain", action="store_true", help="router: the plain-layout router")
+    ap.add_argument("--act-planes", type=int, choices=[1, 2], default=1, help="gemm: activation planes")
     a = ap.parse_args()
     torch.cuda.set_device(0)
     if a.case == "attention":
@@ -354,7 +369,8 @@ def main() -> int:
     elif a.case == "proj":
         res = proj(a.iters)
     else:
-        res = router(a.tokens, a.iters) if a.case == "router" else gemm(a.tokens, a.experts, a.iters, not a.no_zipf)
+        res = (router(a.tokens, a.iters, a.plain) if a.case == "router"
+               else gemm(a.tokens, a.experts, a.iters, not a.no_zipf, a.act_planes))
     print(json.dumps({"case": a.case, "tokens": a.tokens, **res}), flush=True)
     return 0
 
