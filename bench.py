@@ -14,11 +14,17 @@ decode: one step = 256 tokens whose routing comes from
 uniform random router logits (top-8 softmax of U(0,1) logits, supplied to
 the layer's routed forward); the per-expert token histogram is printed.
 
+Activations are two-term e4m3 by default (hi plane + e4m3 residual plane, one
+1x128 scale: the format that keeps the layer within the north-star tolerance
+of the fp32-activation result); `--act-planes 1` runs one e4m3 plane, and on
+one GPU the line also reports the one-plane time of the same layer.
+
 With N > 1 the tokens are split over N expert-parallel ranks (strong
 scaling: rank r owns 160/N experts and T/N tokens).  The exchange is the
 layer's NVLink peer-memory exchange by default (own kernels: P2P stores with
 device-side flags, no host synchronisation), `--exchange nccl` for NCCL
-send/recv; rows travel as e4m3 + 1x128 scales, outputs return as bf16.
+send/recv; rows travel as e4m3 (both planes) + 1x128 scales, outputs return
+as bf16.
 Rank 0 prints one JSON line with the max-over-ranks time.
 
 `e2e` is the same metric through the public layer call with host buffers:
@@ -58,9 +64,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["prefill", "decode"], default="prefill")
-    ap.add_argument("--act-planes", type=int, choices=[1, 2], default=None,
-                    help="expert-GEMM activations: 1 = e4m3, 2 = two-term e4m3 (hi + lo residual); "
-                         "default 2 on one GPU, 1 with expert parallelism (the exchange moves one plane)")
+    ap.add_argument("--act-planes", type=int, choices=[1, 2], default=2,
+                    help="expert-GEMM activations: 1 = e4m3, 2 = two-term e4m3 (hi + lo residual, the format "
+                         "within the north-star tolerance of the fp32-activation result)")
     ap.add_argument("--tokens", type=int, default=None, help="global tokens per step (default 4096 prefill, 256 decode)")
     ap.add_argument("--experts", type=int, default=160,
                     help="routed experts (profiling captures of a smaller case only; the metric uses 160)")
@@ -357,7 +363,7 @@ def run_ours(args):
     max_tokens = -(-T // world)
     out = torch.empty_like(x)
     layer = M.MoELayer(shape, w, max_tokens=max_tokens, ep_size=world, ep_rank=rank, comm=comm)
-    act_planes = args.act_planes or (2 if world == 1 else 1)
+    act_planes = args.act_planes
     if act_planes == 2:
         layer.set_act_planes(2)
     if placement is not None:

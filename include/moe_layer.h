@@ -157,7 +157,11 @@ moe_status_t moe_layer_set_expert_placement(moe_layer_t* layer, const int32_t* s
  * ep_size > 1 (the same count on every rank) and the call's tokens on one
  * GPU.  The two forms add a row's K blocks in different orders, so outputs
  * differ in the last bits between them; an expert-parallel layer and a
- * one-GPU layer give bit-identical outputs when they run the same form. */
+ * one-GPU layer give bit-identical outputs when they run the same form.
+ * CBW_GEMM_ONE_SM_TILES or CBW_GEMM_PAIR_TILES force that variant of the full
+ * form on both GEMMs (bit-identical to each other; a GEMM whose shape or
+ * activation format has no such variant fails the forward with
+ * MOE_ERR_INVALID_ARGUMENT). */
 moe_status_t moe_layer_set_gemm_form(moe_layer_t* layer, int form);
 
 /* No counterpart in the reference.  Activation format of the two expert
@@ -166,8 +170,10 @@ moe_status_t moe_layer_set_gemm_form(moe_layer_t* layer, int form);
  * scale -- CBW_GEMM_ACT_X2: twice the tensor-core work, about 7 significant
  * bits per activation instead of 4, which keeps the layer within the
  * tolerance of an fp32-activation evaluation).  The workspace size depends on
- * it: query moe_layer_workspace_bytes after setting it.  Two planes are not
- * available with ep_size > 1 (MOE_ERR_UNSUPPORTED). */
+ * it: query moe_layer_workspace_bytes after setting it.  With expert
+ * parallelism the dispatched rows carry both planes (moe_ep_row_bytes(H) + H
+ * bytes), so set it before moe_layer_peer_bytes / moe_layer_set_peer_buffers
+ * (changing it afterwards returns MOE_ERR_INVALID_ARGUMENT). */
 moe_status_t moe_layer_set_act_planes(moe_layer_t* layer, int planes);
 moe_status_t moe_layer_get_act_planes(const moe_layer_t* layer, int* planes);
 
@@ -373,6 +379,19 @@ moe_status_t moe_ep_recv_plan(const int32_t* recv_counts, int ep_size, int exper
 moe_status_t moe_ep_gather(const void* packed, const void* xq, const float* xs, int xs_ld,
                            const int32_t* row_src, const int32_t* total_rows, int row_capacity,
                            int H, void* xp, float* xps, int xps_ld, cwStream_t stream);
+
+/* No counterpart in the reference.  moe_ep_pack_rows / moe_ep_gather for
+ * two-term activations: a packed row is the hi plane's H bytes, the lo
+ * plane's H bytes, then the scales (moe_ep_row_bytes(H) + H bytes); xq_lo /
+ * xp_lo are the lo planes ([T][H] / [rows][H]; for the gather both given or
+ * both NULL, NULL meaning one plane). */
+moe_status_t moe_ep_pack_rows_x2(const void* xq, const void* xq_lo, const float* xs, int xs_ld,
+                                 const int32_t* row_token, const int32_t* num_rows, int row_capacity,
+                                 int H, void* packed, cwStream_t stream);
+moe_status_t moe_ep_gather_x2(const void* packed, const void* xq, const void* xq_lo, const float* xs,
+                              int xs_ld, const int32_t* row_src, const int32_t* total_rows,
+                              int row_capacity, int H, void* xp, void* xp_lo, float* xps, int xps_ld,
+                              cwStream_t stream);
 
 /* vidx[p] = slot_of_expert[topk_idx[p]] for 0 <= topk_idx[p] < E, else -1
  * (num_pairs = T * k; device arrays). */

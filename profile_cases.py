@@ -108,7 +108,7 @@ def router(tokens: int, iters: int, plain: bool = False) -> dict:
     return out
 
 
-def gemm(tokens: int, experts: int, iters: int, zipf: bool = True, planes: int = 1) -> dict:
+def gemm(tokens: int, experts: int, iters: int, zipf: bool = True, planes: int = 1, form: int = 0) -> dict:
     shape = dataclasses.replace(synth.GLM, num_experts=experts)
     dev = torch.device("cuda", 0)
     w = synth.make_moe_weights(shape, seed=0, device=dev, zipf_bias=zipf)
@@ -116,6 +116,8 @@ def gemm(tokens: int, experts: int, iters: int, zipf: bool = True, planes: int =
     layer = M.MoELayer(shape, w, max_tokens=tokens)
     if planes == 2:
         layer.set_act_planes(2)
+    if form:
+        layer.set_gemm_form(form)
     out = torch.empty_like(x)
     ms = _time(lambda: layer.forward(x, out), iters)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(M.NUM_STAGES + 1)]
@@ -358,6 +360,8 @@ def main() -> int:
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--plain", action="store_true", help="router: the plain-layout router")
     ap.add_argument("--act-planes", type=int, choices=[1, 2], default=1, help="gemm: activation planes")
+    ap.add_argument("--gemm-form", choices=["rule", "one_sm", "pair", "small"], default="rule",
+                    help="gemm: force a grouped-GEMM form on both GEMMs")
     a = ap.parse_args()
     torch.cuda.set_device(0)
     if a.case == "attention":
@@ -370,7 +374,9 @@ def main() -> int:
         res = proj(a.iters)
     else:
         res = (router(a.tokens, a.iters, a.plain) if a.case == "router"
-               else gemm(a.tokens, a.experts, a.iters, not a.no_zipf, a.act_planes))
+               else gemm(a.tokens, a.experts, a.iters, not a.no_zipf, a.act_planes,
+                         {"rule": 0, "one_sm": M.GEMM_ONE_SM_TILES, "pair": M.GEMM_PAIR_TILES,
+                          "small": M.GEMM_SMALL_TILES}[a.gemm_form]))
     print(json.dumps({"case": a.case, "tokens": a.tokens, **res}), flush=True)
     return 0
 

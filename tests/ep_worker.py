@@ -31,6 +31,7 @@ def main() -> int:
     ap.add_argument("--repeats", type=int, default=2)
     ap.add_argument("--exchange", choices=["nccl", "peer"], default="nccl")
     ap.add_argument("--placement", choices=["contiguous", "balanced"], default="contiguous")
+    ap.add_argument("--act-planes", type=int, choices=[1, 2], default=1)
     a = ap.parse_args()
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -56,6 +57,8 @@ def main() -> int:
         placement = synth.balanced_placement(load.cpu().tolist(), world)
     w = synth.expert_slice(w_all, shape, world, rank, slot_of_expert=placement)
     layer = M.MoELayer(shape, w, max_tokens=-(-T // world), ep_size=world, ep_rank=rank, comm=comm)
+    if a.act_planes == 2:
+        layer.set_act_planes(2)      # before the peer buffers: packed rows carry both planes
     if placement is not None:
         layer.set_expert_placement(placement)
     if a.exchange == "peer":
@@ -79,6 +82,8 @@ def main() -> int:
         full = torch.cat([got[r][: synth.token_slice(T, world, r)[1] - synth.token_slice(T, world, r)[0]]
                           for r in range(world)])
         ref_layer = M.MoELayer(shape, w_all, max_tokens=T)
+        if a.act_planes == 2:
+            ref_layer.set_act_planes(2)
         ref = ref_layer.forward(x_all, routing=routing)
         torch.cuda.synchronize()
         ref_layer.close()

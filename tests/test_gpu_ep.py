@@ -28,8 +28,10 @@ def st():
     return torch.cuda.current_stream().cuda_stream
 
 
-def single_gpu(shape, w, x):
+def single_gpu(shape, w, x, planes=1):
     layer = M.MoELayer(shape, w, max_tokens=x.shape[0])
+    if planes == 2:
+        layer.set_act_planes(2)
     out = layer.forward(x)
     torch.cuda.synchronize()
     layer.check_error()
@@ -38,7 +40,7 @@ def single_gpu(shape, w, x):
     return out, idx
 
 
-def ep_emulated(shape, w_all, x, ep, routing=None, placement=None):
+def ep_emulated(shape, w_all, x, ep, routing=None, placement=None, planes=1):
     """The EP forward of every rank, with host-planned device copies for the
     two exchanges.  `placement`: expert -> slot permutation (the send order
     then sorts by slot, as moe_layer_set_expert_placement makes the layer do).
@@ -48,7 +50,8 @@ def ep_emulated(shape, w_all, x, ep, routing=None, placement=None):
     T, H, I, E, K, S = x.shape[0], shape.hidden, shape.intermediate, shape.num_experts, shape.top_k, shape.num_shared
     epr = E // ep
     Tmax = -(-T // ep)
-    rb = k.moe_ep_row_bytes(H)
+    rb = k.moe_ep_row_bytes(H) + (H if planes == 2 else 0)
+    x2 = planes == 2
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     slot_of = None if placement is None else torch.tensor(placement, dtype=torch.int32, device=dev)
     ranks = []
@@ -60,9 +63,15 @@ def ep_emulated(shape, w_all, x, ep, routing=None, placement=None):
         ld = (Tmax + 3) // 4 * 4
         rms = torch.empty(max(Tr, 1), device=dev)
         xq = torch.zeros(max(Tr, 1), H, dtype=torch.uint8, device=dev)
+        xql = torch.zeros(max(Tr, 1), H, dtype=torch.uint8, device=dev) if x2 else None
         xs = torch.zeros(H // 128, ld, device=dev)
-        M.check("rmsnorm", k.moe_rmsnorm_quant(M.ptr(xr), M.ptr(w_all["gamma"]), Tr, H, shape.eps, M.ptr(rms),
-                                               M.ptr(xq), M.ptr(xs), ld, st()))
+        if x2:
+            M.check("rmsnorm_x2", k.moe_rmsnorm_quant_x2(M.ptr(xr), M.ptr(w_all["gamma"]), Tr, H, shape.eps,
+                                                         M.ptr(rms), None, 0, M.ptr(xq), M.ptr(xql), M.ptr(xs), ld,
+                                                         st()))
+        else:
+            M.check("rmsnorm", k.moe_rmsnorm_quant(M.ptr(xr), M.ptr(w_all["gamma"]), Tr, H, shape.eps, M.ptr(rms),
+                                                   M.ptr(xq), M.ptr(xs), ld, st()))
         if routing is None:
             idx = torch.empty(max(Tr, 1), K, dtype=torch.int32, device=dev)
             wts = torch.empty(max(Tr, 1), K, device=dev)
@@ -86,10 +95,10 @@ def ep_emulated(shape, w_all, x, ep, routing=None, placement=None):
                                                        M.ptr(spos), M.ptr(stok), M.ptr(stotal), P, M.ptr(err), 1,
                                                        st()))
         psend = torch.zeros(max(P, 1), rb, dtype=torch.uint8, device=dev)
-        M.check("pack_rows", k.moe_ep_pack_rows(M.ptr(xq), M.ptr(xs), ld, M.ptr(stok), M.ptr(stotal), P, H,
-                                                M.ptr(psend), st()))
-        ranks.append(dict(t0=t0, Tr=Tr, x=xr, xq=xq, xs=xs, ld=ld, idx=idx, wts=wts, ecounts=ecounts, spos=spos,
-                          psend=psend))
+        M.check("pack_rows", k.moe_ep_pack_rows_x2(M.ptr(xq), M.ptr(xql), M.ptr(xs), ld, M.ptr(stok),
+                                                   M.ptr(stotal), P, H, M.ptr(psend), st()))
+        ranks.append(dict(t0=t0, Tr=Tr, x=xr, xq=xq, xql=xql, xs=xs, ld=ld, idx=idx, wts=wts, ecounts=ecounts,
+                          spos=spos, psend=psend))
     torch.cuda.synchronize()
     assert int(err.item()) == 0
     # ---- counts exchange + host plan
@@ -123,16 +132,19 @@ def ep_emulated(shape, w_all, x, ep, routing=None, placement=None):
         M.check("recv_plan", k.moe_ep_recv_plan(M.ptr(rk["recv_counts"]), ep, epr, rk["Tr"], S, M.ptr(counts),
                                                 M.ptr(start), M.ptr(total), M.ptr(row_src), M.ptr(recv_dst), R,
                                                 recv_cap, M.ptr(err), st()))
-        xp = torch.empty(R, H, dtype=torch.uint8, device=dev)
+        xp = torch.empty(planes, R, H, dtype=torch.uint8, device=dev)
         xps = torch.empty(H // 128, R, device=dev)
-        M.check("ep_gather", k.moe_ep_gather(M.ptr(rk["precv"]), M.ptr(rk["xq"]), M.ptr(rk["xs"]), rk["ld"],
-                                             M.ptr(row_src), M.ptr(total), R, H, M.ptr(xp), M.ptr(xps), R, st()))
-        hq = torch.empty(R, I, dtype=torch.uint8, device=dev)
+        M.check("ep_gather", k.moe_ep_gather_x2(M.ptr(rk["precv"]), M.ptr(rk["xq"]), M.ptr(rk["xql"]), M.ptr(rk["xs"]),
+                                                rk["ld"], M.ptr(row_src), M.ptr(total), R, H, M.ptr(xp[0]),
+                                                M.ptr(xp[1]) if x2 else None, M.ptr(xps), R, st()))
+        hq = torch.empty(planes, R, I, dtype=torch.uint8, device=dev)
         hs = torch.empty(I // 128, R, device=dev)
         y = torch.empty(R, H, dtype=torch.bfloat16, device=dev)
         # the GEMM form exactly as every rank's layer picks it: from max_tokens x ep_size (the
         # same on every rank), not from the rank's own token count
         form = M.GEMM_SMALL_TILES if E > 1 and Tmax * ep * K <= 16 * E else M.GEMM_FULL_TILES
+        if x2:
+            form |= M.GEMM_ACT_X2
         M.grouped_gemm(M.GEMM_GATED_SWIGLU | form, xp, xps, R, wr["w13"], wr["s13"], counts, start, hq, hs, R, H, I,
                        R, error_word=err)
         M.grouped_gemm(M.GEMM_DOWN_BF16 | form, hq, hs, R, wr["w2"], wr["s2"], counts, start, y, None, 0, I, H, R,
@@ -171,6 +183,38 @@ def test_ep_emulated_tiny_bit_identical(gpu, ep, T):
     x = w.pop("x")
     ref, _ = single_gpu(shape, w, x)
     out, _ = ep_emulated(shape, w, x, ep)
+    assert np.array_equal(bits(out), bits(ref))
+
+
+@pytest.mark.parametrize("ep,T", [(2, 64), (4, 37), (8, 50)])
+def test_ep_emulated_two_planes_bit_identical(gpu, ep, T):
+    """Two-term activations over expert parallelism: packed rows carry the hi
+    and lo planes; the output is bit-identical to the one-GPU two-plane layer."""
+    shape = synth.TINY
+    case = synth.make_case(shape, T, seed=5)
+    w = {k_: (v.to(gpu) if isinstance(v, torch.Tensor) else v) for k_, v in case.items()}
+    x = w.pop("x")
+    ref, _ = single_gpu(shape, w, x, planes=2)
+    out, _ = ep_emulated(shape, w, x, ep, planes=2)
+    assert np.array_equal(bits(out), bits(ref))
+
+
+def test_ep_emulated_two_planes_glm_decode(gpu):
+    """configs[2] decode shape (256 tokens, uniform routing) at EP 8 with
+    two-term activations: bit-identical to one GPU."""
+    shape = synth.GLM
+    T = 256
+    w = synth.make_moe_weights(shape, seed=0, device=gpu, zipf_bias=False)
+    x = synth.make_x(shape, T, seed=1, device=gpu)
+    logits = synth.uniform_routing(T, shape.num_experts, shape.top_k, seed=4, device=gpu)
+    top = torch.topk(logits, shape.top_k, dim=1)
+    routing = (top.indices.to(torch.int32).contiguous(), torch.softmax(top.values, dim=1).contiguous())
+    layer = M.MoELayer(shape, w, max_tokens=T)
+    layer.set_act_planes(2)
+    ref = layer.forward(x, routing=routing).clone()
+    torch.cuda.synchronize()
+    layer.close()
+    out, _ = ep_emulated(shape, w, x, 8, routing=routing, planes=2)
     assert np.array_equal(bits(out), bits(ref))
 
 

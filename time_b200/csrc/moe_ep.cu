@@ -28,7 +28,8 @@
 //      order, where the combine adds them exactly as on one GPU.
 //
 // Packed row (moe_ep_row_bytes(H) bytes, a multiple of 16): H e4m3 bytes, then
-// H/128 fp32 scales, then zero padding.
+// H/128 fp32 scales, then zero padding.  Two-term activations add the lo
+// plane's H bytes after the hi plane's (moe_ep_row_bytes(H) + H bytes).
 //
 // Peer-memory exchange (moe_layer_set_peer_buffers): the same protocol with no
 // NCCL and no host synchronisation.  Every rank owns a symmetric buffer that
@@ -78,19 +79,24 @@ __global__ void ep_remap_kernel(const int32_t* __restrict__ idx, int P, int E, c
 __global__ void __launch_bounds__(256)
 ep_pack_rows_kernel(const uint8_t* __restrict__ xq, const float* __restrict__ xs, int xs_ld,
                     const int32_t* __restrict__ row_token, const int32_t* __restrict__ num_rows, int row_capacity,
-                    int H, uint8_t* __restrict__ packed, size_t row_bytes) {
+                    int H, uint8_t* __restrict__ packed, size_t row_bytes, const uint8_t* __restrict__ xq_lo) {
     const int R = min(*num_rows, row_capacity);
     const int lane = threadIdx.x & 31;
     const int nwarps = (gridDim.x * blockDim.x) >> 5;
     const int vec = H / 16;
     const int nblk = H / 128;
-    const int nscale_padded = (nblk * 4 + 15) / 16 * 4;   // row_bytes == H + 4 * nscale_padded
+    const int nscale_padded = (nblk * 4 + 15) / 16 * 4;   // row_bytes == planes * H + 4 * nscale_padded
+    const int planes = xq_lo ? 2 : 1;
     for (int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < R; r += nwarps) {
         const int t = row_token[r];
         uint8_t* dst = packed + static_cast<size_t>(r) * row_bytes;
         const int4* src = reinterpret_cast<const int4*>(xq + static_cast<size_t>(t) * H);
         for (int i = lane; i < vec; i += 32) reinterpret_cast<int4*>(dst)[i] = src[i];
-        float* ds = reinterpret_cast<float*>(dst + H);
+        if (xq_lo) {
+            const int4* slo = reinterpret_cast<const int4*>(xq_lo + static_cast<size_t>(t) * H);
+            for (int i = lane; i < vec; i += 32) reinterpret_cast<int4*>(dst + H)[i] = slo[i];
+        }
+        float* ds = reinterpret_cast<float*>(dst + static_cast<size_t>(planes) * H);
         for (int b = lane; b < nblk; b += 32) ds[b] = xs[static_cast<size_t>(b) * xs_ld + t];
         // zero the padding after the scales so the transferred bytes are defined
         for (int b = nblk + lane; b < nscale_padded; b += 32) ds[b] = 0.0f;
@@ -168,28 +174,38 @@ __global__ void __launch_bounds__(256)
 ep_gather_kernel(const uint8_t* __restrict__ packed, size_t row_bytes, const uint8_t* __restrict__ xq,
                  const float* __restrict__ xs, int xs_ld, const int32_t* __restrict__ row_src,
                  const int32_t* __restrict__ total_rows, int row_capacity, int H, uint8_t* __restrict__ xp,
-                 float* __restrict__ xps, int xps_ld) {
+                 float* __restrict__ xps, int xps_ld, const uint8_t* __restrict__ xq_lo, uint8_t* __restrict__ xp_lo) {
     const int R = min(*total_rows, row_capacity);
     const int lane = threadIdx.x & 31;
     const int nwarps = (gridDim.x * blockDim.x) >> 5;
     const int vec = H / 16;
     const int nblk = H / 128;
+    const int planes = xp_lo ? 2 : 1;
     for (int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < R; r += nwarps) {
         const int v = row_src[r];
         int4* dst = reinterpret_cast<int4*>(xp + static_cast<size_t>(r) * H);
+        int4* dlo = xp_lo ? reinterpret_cast<int4*>(xp_lo + static_cast<size_t>(r) * H) : nullptr;
         if (v >= 0) {
             const uint8_t* src = packed + static_cast<size_t>(v) * row_bytes;
             for (int i = lane; i < vec; i += 32) dst[i] = reinterpret_cast<const int4*>(src)[i];
-            const float* ss = reinterpret_cast<const float*>(src + H);
+            if (dlo)
+                for (int i = lane; i < vec; i += 32) dlo[i] = reinterpret_cast<const int4*>(src + H)[i];
+            const float* ss = reinterpret_cast<const float*>(src + static_cast<size_t>(planes) * H);
             for (int b = lane; b < nblk; b += 32) xps[static_cast<size_t>(b) * xps_ld + r] = ss[b];
         } else if (v <= -2) {
             const int t = -v - 2;
             const int4* src = reinterpret_cast<const int4*>(xq + static_cast<size_t>(t) * H);
             for (int i = lane; i < vec; i += 32) dst[i] = src[i];
+            if (dlo) {
+                const int4* slo = reinterpret_cast<const int4*>(xq_lo + static_cast<size_t>(t) * H);
+                for (int i = lane; i < vec; i += 32) dlo[i] = slo[i];
+            }
             for (int b = lane; b < nblk; b += 32) xps[static_cast<size_t>(b) * xps_ld + r] = xs[static_cast<size_t>(b) * xs_ld + t];
         } else {
             const int4 z = make_int4(0, 0, 0, 0);
             for (int i = lane; i < vec; i += 32) dst[i] = z;
+            if (dlo)
+                for (int i = lane; i < vec; i += 32) dlo[i] = z;
             for (int b = lane; b < nblk; b += 32) xps[static_cast<size_t>(b) * xps_ld + r] = 0.0f;
         }
     }
@@ -313,7 +329,7 @@ ep_counts_kernel(const EpPeers P, const int32_t* __restrict__ ecounts, uint32_t 
 __global__ void __launch_bounds__(256)
 ep_dispatch_kernel(const EpPeers P, const uint8_t* __restrict__ xq, const float* __restrict__ xs, int xs_ld,
                    const int32_t* __restrict__ stok, const int32_t* __restrict__ plan, int H, size_t row_bytes,
-                   int recv_cap) {
+                   int recv_cap, const uint8_t* __restrict__ xq_lo) {
     __shared__ int s_soff[kMaxEpRanks], s_roff[kMaxEpRanks];
     for (int d = threadIdx.x; d < P.ep; d += blockDim.x) {
         s_soff[d] = plan[6 * d + kPlanSoff];
@@ -334,7 +350,11 @@ ep_dispatch_kernel(const EpPeers P, const uint8_t* __restrict__ xq, const float*
         const int t = stok[r];
         const int4* src = reinterpret_cast<const int4*>(xq + static_cast<size_t>(t) * H);
         for (int i = lane; i < vec; i += 32) reinterpret_cast<int4*>(dst)[i] = src[i];
-        float* ds = reinterpret_cast<float*>(dst + H);
+        if (xq_lo) {
+            const int4* slo = reinterpret_cast<const int4*>(xq_lo + static_cast<size_t>(t) * H);
+            for (int i = lane; i < vec; i += 32) reinterpret_cast<int4*>(dst + H)[i] = slo[i];
+        }
+        float* ds = reinterpret_cast<float*>(dst + static_cast<size_t>(xq_lo ? 2 : 1) * H);
         for (int b = lane; b < nscale_padded; b += 32) ds[b] = (b < nblk) ? xs[static_cast<size_t>(b) * xs_ld + t] : 0.0f;
     }
     __threadfence_system();
@@ -426,16 +446,23 @@ moe_status_t moe_ep_remap_experts(const int32_t* topk_idx, int num_pairs, int E,
     return launch_status();
 }
 
-moe_status_t moe_ep_pack_rows(const void* xq, const float* xs, int xs_ld, const int32_t* row_token,
-                              const int32_t* num_rows, int row_capacity, int H, void* packed, cwStream_t stream) {
-    const size_t rb = moe_ep_row_bytes(H);
-    if (!rb || !xq || !xs || !row_token || !num_rows || !packed || row_capacity < 0) return MOE_ERR_INVALID_ARGUMENT;
-    if (!aligned16(xq) || !aligned16(packed)) return MOE_ERR_INVALID_ARGUMENT;
+moe_status_t moe_ep_pack_rows_x2(const void* xq, const void* xq_lo, const float* xs, int xs_ld,
+                                 const int32_t* row_token, const int32_t* num_rows, int row_capacity, int H,
+                                 void* packed, cwStream_t stream) {
+    const size_t rb = moe_ep_row_bytes(H) + (xq_lo ? static_cast<size_t>(H) : 0);
+    if (H <= 0 || H % 128 || !xq || !xs || !row_token || !num_rows || !packed || row_capacity < 0)
+        return MOE_ERR_INVALID_ARGUMENT;
+    if (!aligned16(xq) || !aligned16(packed) || (xq_lo && !aligned16(xq_lo))) return MOE_ERR_INVALID_ARGUMENT;
     if (row_capacity == 0) return MOE_OK;
     ep_pack_rows_kernel<<<grid_for_rows(row_capacity), 256, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const uint8_t*>(xq), xs, xs_ld, row_token, num_rows, row_capacity, H,
-        static_cast<uint8_t*>(packed), rb);
+        static_cast<uint8_t*>(packed), rb, static_cast<const uint8_t*>(xq_lo));
     return launch_status();
+}
+
+moe_status_t moe_ep_pack_rows(const void* xq, const float* xs, int xs_ld, const int32_t* row_token,
+                              const int32_t* num_rows, int row_capacity, int H, void* packed, cwStream_t stream) {
+    return moe_ep_pack_rows_x2(xq, nullptr, xs, xs_ld, row_token, num_rows, row_capacity, H, packed, stream);
 }
 
 moe_status_t moe_ep_recv_plan(const int32_t* recv_counts, int ep_size, int experts_per_rank, int T_local,
@@ -454,19 +481,29 @@ moe_status_t moe_ep_recv_plan(const int32_t* recv_counts, int ep_size, int exper
     return launch_status();
 }
 
-moe_status_t moe_ep_gather(const void* packed, const void* xq, const float* xs, int xs_ld, const int32_t* row_src,
-                           const int32_t* total_rows, int row_capacity, int H, void* xp, float* xps, int xps_ld,
-                           cwStream_t stream) {
-    const size_t rb = moe_ep_row_bytes(H);
-    if (!rb || !packed || !xq || !xs || !row_src || !total_rows || !xp || !xps || row_capacity < 0 ||
+moe_status_t moe_ep_gather_x2(const void* packed, const void* xq, const void* xq_lo, const float* xs, int xs_ld,
+                              const int32_t* row_src, const int32_t* total_rows, int row_capacity, int H, void* xp,
+                              void* xp_lo, float* xps, int xps_ld, cwStream_t stream) {
+    const size_t rb = moe_ep_row_bytes(H) + (xp_lo ? static_cast<size_t>(H) : 0);
+    if (H <= 0 || H % 128 || !packed || !xq || !xs || !row_src || !total_rows || !xp || !xps || row_capacity < 0 ||
         xps_ld < row_capacity)
         return MOE_ERR_INVALID_ARGUMENT;
-    if (!aligned16(packed) || !aligned16(xq) || !aligned16(xp)) return MOE_ERR_INVALID_ARGUMENT;
+    if (!xq_lo != !xp_lo) return MOE_ERR_INVALID_ARGUMENT;
+    if (!aligned16(packed) || !aligned16(xq) || !aligned16(xp) || (xp_lo && (!aligned16(xp_lo) || !aligned16(xq_lo))))
+        return MOE_ERR_INVALID_ARGUMENT;
     if (row_capacity == 0) return MOE_OK;
     ep_gather_kernel<<<grid_for_rows(row_capacity), 256, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const uint8_t*>(packed), rb, static_cast<const uint8_t*>(xq), xs, xs_ld, row_src, total_rows,
-        row_capacity, H, static_cast<uint8_t*>(xp), xps, xps_ld);
+        row_capacity, H, static_cast<uint8_t*>(xp), xps, xps_ld, static_cast<const uint8_t*>(xq_lo),
+        static_cast<uint8_t*>(xp_lo));
     return launch_status();
+}
+
+moe_status_t moe_ep_gather(const void* packed, const void* xq, const float* xs, int xs_ld, const int32_t* row_src,
+                           const int32_t* total_rows, int row_capacity, int H, void* xp, float* xps, int xps_ld,
+                           cwStream_t stream) {
+    return moe_ep_gather_x2(packed, xq, nullptr, xs, xs_ld, row_src, total_rows, row_capacity, H, xp, nullptr, xps,
+                            xps_ld, stream);
 }
 
 moe_status_t moe_ep_pack_y(const void* y_bf16, const int32_t* recv_dst, int n, int H, void* ysend_bf16,
@@ -527,11 +564,13 @@ moe_status_t counts(const Peers& P, const int32_t* ecounts, uint32_t epoch, int3
     return launch_status();
 }
 
-moe_status_t dispatch(const Peers& P, const void* xq, const float* xs, int xs_ld, const int32_t* stok,
-                      const int32_t* plan, int H, size_t row_bytes, int recv_cap, int max_rows, cudaStream_t st) {
+moe_status_t dispatch(const Peers& P, const void* xq, const void* xq_lo, const float* xs, int xs_ld,
+                      const int32_t* stok, const int32_t* plan, int H, size_t row_bytes, int recv_cap, int max_rows,
+                      cudaStream_t st) {
     if (max_rows <= 0) return MOE_OK;
     ep_dispatch_kernel<<<grid_for_rows(max_rows), 256, 0, st>>>(to_dev(P), static_cast<const uint8_t*>(xq), xs,
-                                                                 xs_ld, stok, plan, H, row_bytes, recv_cap);
+                                                                 xs_ld, stok, plan, H, row_bytes, recv_cap,
+                                                                 static_cast<const uint8_t*>(xq_lo));
     return launch_status();
 }
 

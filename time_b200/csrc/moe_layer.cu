@@ -94,7 +94,7 @@ void plan_workspace(moe_layer* L) {
     L->recv_cap = ep ? static_cast<int>(static_cast<size_t>(c.ep_size) * T * std::min(K, epr)) : 0;
     const size_t routed_rows = ep ? static_cast<size_t>(L->recv_cap) : T * K;
     L->rcap = static_cast<int>(align_up(routed_rows + static_cast<size_t>(c.num_shared) * T + 16 * static_cast<size_t>(L->groups), 16));
-    L->row_bytes = moe_ep_row_bytes(c.hidden);
+    L->row_bytes = moe_ep_row_bytes(c.hidden) + (L->act_planes == 2 ? static_cast<size_t>(c.hidden) : 0);
     const size_t R = L->rcap;
     size_t o = 0;
     auto take = [&o](size_t bytes) { size_t at = o; o = align_up(o + bytes, 256); return at; };
@@ -274,14 +274,17 @@ moe_status_t run_experts_ep(moe_layer* L, const int32_t* idx, const float* wts, 
                                    T * K, L->error_word, 1, at<void>(ws, L->off_bcounts), L->bcounts_bytes, st));
         MOE_TRY(tbep::counts(P, ecounts, epoch, plan, rcounts, L->error_word, st));
         mark(L, 3, st);
-        MOE_TRY(tbep::dispatch(P, at<void>(ws, L->off_xq), at<float>(ws, L->off_xs), L->xs_ld, stok, plan, H, rb,
-                               L->recv_cap, T * K, st));
+        const bool x2 = L->act_planes == 2;
+        void* xq_lo = x2 ? at<void>(ws, L->off_xq_lo) : nullptr;
+        void* xp_lo = x2 ? at<void>(ws, L->off_xp + L->rcap * static_cast<size_t>(H)) : nullptr;
+        MOE_TRY(tbep::dispatch(P, at<void>(ws, L->off_xq), xq_lo, at<float>(ws, L->off_xs), L->xs_ld, stok, plan, H,
+                               rb, L->recv_cap, T * K, st));
         MOE_TRY(tbep::signal_wait(P, tbep::kDispatch, epoch, L->error_word, st));
         MOE_TRY(moe_ep_recv_plan(rcounts, ep, epr, T, S, counts, start, total, row_src, recv_dst, L->rcap, L->recv_cap,
                                  L->error_word, st));
-        MOE_TRY(moe_ep_gather(mine + P.lay.off_recv, at<void>(ws, L->off_xq), at<float>(ws, L->off_xs), L->xs_ld,
-                              row_src, total, L->rcap, H, at<void>(ws, L->off_xp), at<float>(ws, L->off_xps), L->rcap,
-                              st));
+        MOE_TRY(moe_ep_gather_x2(mine + P.lay.off_recv, at<void>(ws, L->off_xq), xq_lo, at<float>(ws, L->off_xs),
+                                 L->xs_ld, row_src, total, L->rcap, H, at<void>(ws, L->off_xp), xp_lo,
+                                 at<float>(ws, L->off_xps), L->rcap, st));
         cbwGroupedGemmArgs g1 = gemm_args(L, ws, false, T), g2 = gemm_args(L, ws, true, T);
         mark(L, 4, st);
         MOE_TRY(cbw_to_moe(cbwFp8BlockScaledGroupedGemm(&g1, L->error_word, st)));
@@ -296,11 +299,14 @@ moe_status_t run_experts_ep(moe_layer* L, const int32_t* idx, const float* wts, 
         return MOE_OK;
     }
 
+    const bool x2 = L->act_planes == 2;
+    void* xq_lo = x2 ? at<void>(ws, L->off_xq_lo) : nullptr;
+    void* xp_lo = x2 ? at<void>(ws, L->off_xp + L->rcap * static_cast<size_t>(H)) : nullptr;
     mark(L, 2, st);
     MOE_TRY(moe_permute_mb(sort_ids, T, K, 0, E, 0, ecounts, at<int32_t>(ws, L->off_estart), spos, stok, stotal,
                                T * K, L->error_word, 1, at<void>(ws, L->off_bcounts), L->bcounts_bytes, st));
-    MOE_TRY(moe_ep_pack_rows(at<void>(ws, L->off_xq), at<float>(ws, L->off_xs), L->xs_ld, stok, stotal, T * K, H,
-                             at<void>(ws, L->off_psend), st));
+    MOE_TRY(moe_ep_pack_rows_x2(at<void>(ws, L->off_xq), xq_lo, at<float>(ws, L->off_xs), L->xs_ld, stok, stotal,
+                                T * K, H, at<void>(ws, L->off_psend), st));
     std::vector<size_t> cc(ep, static_cast<size_t>(epr)), co(ep);
     for (int p = 0; p < ep; ++p) co[p] = static_cast<size_t>(p) * epr;
     MOE_TRY(nccl_to_moe(ncwAllToAllv(ecounts, cc.data(), co.data(), rcounts, cc.data(), co.data(), NCW_INT32,
@@ -325,8 +331,9 @@ moe_status_t run_experts_ep(moe_layer* L, const int32_t* idx, const float* wts, 
     }
     MOE_TRY(moe_ep_recv_plan(rcounts, ep, epr, T, S, counts, start, total, row_src, recv_dst, L->rcap, L->recv_cap,
                              L->error_word, st));
-    MOE_TRY(moe_ep_gather(at<void>(ws, L->off_precv), at<void>(ws, L->off_xq), at<float>(ws, L->off_xs), L->xs_ld,
-                          row_src, total, L->rcap, H, at<void>(ws, L->off_xp), at<float>(ws, L->off_xps), L->rcap, st));
+    MOE_TRY(moe_ep_gather_x2(at<void>(ws, L->off_precv), at<void>(ws, L->off_xq), xq_lo, at<float>(ws, L->off_xs),
+                             L->xs_ld, row_src, total, L->rcap, H, at<void>(ws, L->off_xp), xp_lo,
+                             at<float>(ws, L->off_xps), L->rcap, st));
     cbwGroupedGemmArgs g1 = gemm_args(L, ws, false, T), g2 = gemm_args(L, ws, true, T);
     mark(L, 4, st);
     MOE_TRY(cbw_to_moe(cbwFp8BlockScaledGroupedGemm(&g1, L->error_word, st)));
@@ -501,8 +508,9 @@ moe_status_t moe_layer_set_stage_events(moe_layer_t* L, cwEvent_t* events) {
 
 moe_status_t moe_layer_set_act_planes(moe_layer_t* L, int planes) {
     if (!L || (planes != 1 && planes != 2)) return MOE_ERR_INVALID_ARGUMENT;
-    // the expert-parallel exchange moves one e4m3 plane per row
-    if (planes == 2 && L->cfg.ep_size > 1) return MOE_ERR_UNSUPPORTED;
+    // the exchange's packed rows and the peer buffers are sized for the format:
+    // choose it before the peer buffers are set
+    if (L->peer_mode && planes != L->act_planes) return MOE_ERR_INVALID_ARGUMENT;
     L->act_planes = planes;
     plan_workspace(L);
     return MOE_OK;
@@ -516,7 +524,9 @@ moe_status_t moe_layer_get_act_planes(const moe_layer_t* L, int* planes) {
 
 moe_status_t moe_layer_set_gemm_form(moe_layer_t* L, int form) {
     if (!L) return MOE_ERR_INVALID_ARGUMENT;
-    if (form != 0 && form != CBW_GEMM_SMALL_TILES && form != CBW_GEMM_FULL_TILES) return MOE_ERR_INVALID_ARGUMENT;
+    if (form != 0 && form != CBW_GEMM_SMALL_TILES && form != CBW_GEMM_FULL_TILES && form != CBW_GEMM_ONE_SM_TILES &&
+        form != CBW_GEMM_PAIR_TILES)
+        return MOE_ERR_INVALID_ARGUMENT;
     L->gemm_form = form;
     return MOE_OK;
 }

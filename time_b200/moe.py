@@ -103,6 +103,10 @@ def libs():
         k.moe_layer_set_expert_placement.argtypes = [c_void_p, c_void_p]
         k.moe_layer_set_gemm_form.argtypes = [c_void_p, c_int]
         k.moe_layer_set_act_planes.argtypes = [c_void_p, c_int]
+        k.moe_ep_pack_rows_x2.argtypes = [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int, c_int,
+                                          c_void_p, c_void_p]
+        k.moe_ep_gather_x2.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int,
+                                       c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p]
         k.moe_layer_get_act_planes.argtypes = [c_void_p, ctypes.POINTER(c_int)]
         k.moe_rmsnorm_quant_x2.argtypes = [c_void_p, c_void_p, c_int, c_int, c_float, c_void_p, c_void_p, c_int,
                                            c_void_p, c_void_p, c_void_p, c_int, c_void_p]
