@@ -11,9 +11,12 @@ package's drop-in launch_* kernels (tests/test_gpu_legacy.py) to the
 reference itself.  Inputs are stored beside the outputs, so the tests never
 need the reference or this script.  Kernels covered (reference
 csrc/kernels.h:12-31): fp8_dequantize, f32_to_fp8, rms_norm, moe_gate,
-moe_topk, swiglu, moe_combine, add_residual, argmax, rope; and into
+moe_topk, swiglu, moe_combine, add_residual, argmax, rope; into
 tests/golden/ref_attn.npz paged_attention_decode and update_kv_cache
-(`--only attn` writes just that file).
+(`--only attn` writes just that file); and into tests/golden/ref_legacy.npz
+softmax, gelu, embedding_lookup (e4m3 / fp16 / fp32 tables), top_p_sampling
+(sampling and argmax paths), apply_rep_penalty, paged_attention_prefill,
+moe_dispatch and copy_hidden (`--only legacy`).
 """
 from __future__ import annotations
 
@@ -44,6 +47,15 @@ def load_ref():
                                                   c_int, c_int, c_int, c_int, c_float, c_void_p]
     lib.launch_update_kv_cache.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                                            c_int, c_int, c_void_p]
+    lib.launch_softmax.argtypes = [c_void_p, c_int, c_int, c_void_p]
+    lib.launch_gelu.argtypes = [c_void_p, c_size_t, c_void_p]
+    lib.launch_embedding_lookup.argtypes = [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]
+    lib.launch_top_p_sampling.argtypes = [c_void_p, c_void_p, c_float, c_float, c_int, c_int, c_void_p, c_void_p]
+    lib.launch_apply_rep_penalty.argtypes = [c_void_p, c_void_p, c_int, c_int, c_float, c_void_p]
+    lib.launch_paged_attention_prefill.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
+                                                   c_int, c_int, c_int, c_float, c_void_p]
+    lib.launch_moe_dispatch.argtypes = [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]
+    lib.launch_copy_hidden.argtypes = [c_void_p, c_void_p, c_size_t, c_void_p]
     return lib
 
 
@@ -102,13 +114,101 @@ def attn_goldens(lib, out_path: str) -> None:
     print(f"wrote {out_path}: {len(g)} arrays")
 
 
+def legacy_goldens(lib, out_path: str) -> None:
+    """tests/golden/ref_legacy.npz: the remaining drop-in kernels.  Inputs stay
+    inside what the reference's kernels handle: token ids and past tokens
+    within the vocabulary (out-of-range past tokens are skipped by the
+    reference's own bounds check), no duplicate past tokens (the reference's
+    in-place penalty races on duplicates), prefill chunks of at most 1024
+    positions (its score buffer) whose every query has a positive score
+    (k correlated with q: the reference's float max through an integer
+    atomicMax is exact only then)."""
+    rng = np.random.default_rng(20261203)
+    st = None
+    g = {}
+    # softmax (in place), rows of varied scale and length
+    for B, L in ((4, 1000), (3, 77), (2, 5000)):
+        x = (rng.standard_normal((B, L)) * np.array([[1.0], [10.0], [0.1], [3.0]][:B])).astype(np.float32)
+        t = dev(x)
+        lib.launch_softmax(t.data_ptr(), B, L, st)
+        g[f"softmax_in_{L}"], g[f"softmax_out_{L}"] = x, host(t)
+    # gelu (in place)
+    x = (4 * rng.standard_normal(5000)).astype(np.float32)
+    t = dev(x)
+    lib.launch_gelu(t.data_ptr(), x.size, st)
+    g["gelu_in"], g["gelu_out"] = x, host(t)
+    # embedding lookup: e4m3, fp16 and fp32 tables
+    V, H, T = 50, 384, 9
+    ids = rng.integers(0, V, T).astype(np.int64)
+    ids[0], ids[1] = 0, V - 1
+    tabs = {1: rng.integers(0, 256, (V, H)).astype(np.uint8),
+            2: rng.standard_normal((V, H)).astype(np.float16),
+            0: rng.standard_normal((V, H)).astype(np.float32)}
+    g["embed_ids"] = ids
+    for dt, tab in tabs.items():
+        o = torch.empty(T, H, device="cuda")
+        lib.launch_embedding_lookup(dev(tab).data_ptr(), dev(ids).data_ptr(), o.data_ptr(), H, T, dt, st)
+        g[f"embed_tab_{dt}"], g[f"embed_out_{dt}"] = tab, host(o)
+    # top-p sampling: the sampling path (temperature 0.7, top_p 0.9 and 1.0) and
+    # the argmax path (temperature < 0.01)
+    B, Vv = 6, 3000
+    lg = (2 * rng.standard_normal((B, Vv))).astype(np.float32)
+    lg[3, 123] = 15.0
+    seeds = rng.integers(0, 2 ** 63, B, dtype=np.int64).astype(np.uint64)
+    g["topp_logits"], g["topp_seeds"] = lg, seeds
+    for name, temp, tp in (("a", 0.7, 0.9), ("b", 1.3, 1.0), ("c", 0.001, 0.9)):
+        o = torch.empty(B, dtype=torch.int64, device="cuda")
+        lib.launch_top_p_sampling(dev(lg).data_ptr(), o.data_ptr(), temp, tp, Vv, B, dev(seeds).data_ptr(), st)
+        g[f"topp_out_{name}"] = host(o)
+        g[f"topp_args_{name}"] = np.array([temp, tp], np.float32)
+    # repetition penalty (in place): positive and negative logits, ids out of range skipped
+    Vv = 1000
+    lg = rng.standard_normal(Vv).astype(np.float32)
+    past = np.concatenate([rng.choice(Vv, 300, replace=False), [-1, Vv, Vv + 7]]).astype(np.int64)
+    t = dev(lg)
+    lib.launch_apply_rep_penalty(t.data_ptr(), dev(past).data_ptr(), past.size, Vv, 1.3, st)
+    g["rep_logits"], g["rep_past"], g["rep_out"] = lg, past, host(t)
+    # paged attention prefill: causal attention over the chunk, [seq][heads][d]
+    for ci, (S_, NH, D) in enumerate(((37, 4, 64), (300, 2, 128))):
+        q = rng.standard_normal((S_, NH, D)).astype(np.float32)
+        k = (q + 0.3 * rng.standard_normal((S_, NH, D))).astype(np.float32)
+        v = rng.standard_normal((S_, NH, D)).astype(np.float32)
+        pt = np.arange(4, dtype=np.int32)
+        o = torch.zeros(S_, NH, D, device="cuda")
+        scale = float(1.0 / np.sqrt(D))
+        lib.launch_paged_attention_prefill(dev(q).data_ptr(), dev(k).data_ptr(), dev(v).data_ptr(), o.data_ptr(),
+                                           dev(pt).data_ptr(), 4, 16, NH, D, S_, scale, st)
+        for name, val in (("q", q), ("k", k), ("v", v), ("out", host(o))):
+            g[f"prefill{ci}_{name}"] = val
+        g[f"prefill{ci}_scale"] = np.array([scale], np.float32)
+    # moe_dispatch: every token replicated top_k times
+    T, K, H = 7, 3, 200
+    x = rng.standard_normal((T, H)).astype(np.float32)
+    idx = rng.integers(0, 8, (T, K)).astype(np.int32)
+    o = torch.full((T, K, H), float("nan"), device="cuda")
+    lib.launch_moe_dispatch(dev(x).data_ptr(), o.data_ptr(), dev(idx).data_ptr(), H, K, T, st)
+    g["dispatch_in"], g["dispatch_idx"], g["dispatch_out"] = x, idx, host(o)
+    # copy_hidden
+    x = rng.standard_normal(3001).astype(np.float32)
+    o = torch.full((3001,), float("nan"), device="cuda")
+    lib.launch_copy_hidden(dev(x).data_ptr(), o.data_ptr(), 3001, st)
+    g["copy_in"], g["copy_out"] = x, host(o)
+    np.savez_compressed(out_path, **g)
+    print(f"wrote {out_path}: {len(g)} arrays")
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", default=str(ROOT / "tests" / "golden" / "ref_kernels.npz"))
     ap.add_argument("--attn-out", default=str(ROOT / "tests" / "golden" / "ref_attn.npz"))
-    ap.add_argument("--only", choices=["all", "kernels", "attn"], default="all")
+    ap.add_argument("--legacy-out", default=str(ROOT / "tests" / "golden" / "ref_legacy.npz"))
+    ap.add_argument("--only", choices=["all", "kernels", "attn", "legacy"], default="all")
     a = ap.parse_args()
     lib = load_ref()
+    if a.only in ("all", "legacy"):
+        legacy_goldens(lib, a.legacy_out)
+    if a.only == "legacy":
+        return 0
     if a.only in ("all", "attn"):
         attn_goldens(lib, a.attn_out)
     if a.only == "attn":
