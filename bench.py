@@ -3,7 +3,7 @@
 FFN block: hidden 5120, 160 routed experts top-8 + 1 shared expert,
 intermediate 1536, SwiGLU, FP8 e4m3 expert weights with 128x128 block scales.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|reference_gpu]
                     [--workload prefill|decode]
 
 prefill (default): one step = one forward of the MoE
@@ -62,7 +62,9 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "reference_gpu"], default="ours",
+                    help="reference: the reference's CPU path (oracle port); reference_gpu: the reference's own "
+                         "GPU kernels + cuBLAS SGEMM in its MoE call order (the GPU component baseline)")
     ap.add_argument("--workload", choices=["prefill", "decode"], default="prefill")
     ap.add_argument("--act-planes", type=int, choices=[1, 2], default=2,
                     help="expert-GEMM activations: 1 = e4m3, 2 = two-term e4m3 (hi + lo residual, the format "
@@ -307,6 +309,162 @@ def run_reference(args):
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": th, "kind": "port",
                              "sample": f"{n} tokens per step of the {args.tokens}-token workload, oracle ref mode"},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_reference_gpu(args):
+    """--impl reference_gpu: the reference's own GPU components, the "beat this"
+    number.  The reference's csrc/kernels.cu and csrc/cublas_wrappers.cu, built
+    unmodified for sm_100 into oracle/_ref/, driven with ctypes in the call
+    order of its MoE branch (src/terra/engine.t:1317-1347): launch_rms_norm ->
+    launch_moe_gate (fp32 router) -> launch_moe_topk -> per expert:
+    launch_fp8_dequantize + cbwSgemm (gate), the same for up, launch_swiglu,
+    launch_fp8_dequantize + cbwSgemm (down) -> launch_moe_combine ->
+    launch_add_residual (shared expert, residual).  The reference runs each of
+    its top_k slots with the layer's single expert weight (its MoE path never
+    indexes an expert); here each routed expert's own e4m3 weights are
+    substituted and its rows gathered, so the FLOPs and weight bytes are the
+    layer's.  Glue that the reference has no kernel for runs in torch inside
+    the timed region: the zipf router bias add, the per-expert row order and
+    counts (one host read per step, as a host loop over experts needs), the
+    row gather and the scatter back to slot order.  The reference's dequantise
+    has no block scales, so this arm is timed, not compared.  One GPU,
+    rank 0 only; prefill only."""
+    import ctypes
+    import torch
+    from time_b200 import synth
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    base = {"metric": METRIC, "impl": "reference_gpu"}
+    libk = ROOT / "oracle" / "_ref" / "libref_kernels.so"
+    libc = ROOT / "oracle" / "_ref" / "libref_cublas.so"
+    if args.workload != "prefill" or not (libk.exists() and libc.exists()):
+        why = ("prefill only" if args.workload != "prefill"
+               else "oracle/_ref/ lacks the reference's kernels or cuBLAS wrapper (build() needs the reference sources)")
+        print(json.dumps({**base, "unavailable": why}), flush=True)
+        return 0
+    K = ctypes.CDLL(str(libk))
+    C = ctypes.CDLL(str(libc))
+    vp, i32, sz, f32 = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t, ctypes.c_float
+    K.launch_rms_norm.argtypes = [vp, vp, vp, i32, i32, f32, vp]
+    K.launch_moe_gate.argtypes = [vp, vp, vp, i32, i32, i32, i32, vp]
+    K.launch_moe_topk.argtypes = [vp, vp, vp, i32, i32, i32, vp]
+    K.launch_fp8_dequantize.argtypes = [vp, vp, sz, vp]
+    K.launch_swiglu.argtypes = [vp, vp, vp, sz, vp]
+    K.launch_moe_combine.argtypes = [vp, vp, vp, i32, i32, i32, vp]
+    K.launch_add_residual.argtypes = [vp, vp, sz, vp]
+    for f in (K.launch_rms_norm, K.launch_moe_gate, K.launch_moe_topk, K.launch_fp8_dequantize,
+              K.launch_swiglu, K.launch_moe_combine, K.launch_add_residual):
+        f.restype = None
+    C.cbwCreate.argtypes = [ctypes.POINTER(vp)]
+    C.cbwSetStream.argtypes = [vp, vp]
+    C.cbwDestroy.argtypes = [vp]
+    C.cbwSgemm.argtypes = [vp, i32, i32, i32, i32, i32, ctypes.POINTER(f32), vp, i32, vp, i32,
+                           ctypes.POINTER(f32), vp, i32]
+    for f in (C.cbwCreate, C.cbwSetStream, C.cbwDestroy, C.cbwSgemm):
+        f.restype = i32
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    shape = synth.GLM
+    H, E, k, I, S, T = (shape.hidden, shape.num_experts, shape.top_k, shape.intermediate,
+                        shape.num_shared, args.tokens)
+    w = synth.make_moe_weights(shape, seed=0, device=dev, zipf_bias=True)
+    x = synth.make_x(shape, T, seed=1, device=dev).float()        # the reference's hidden state is fp32
+    gamma, router_w, bias = w["gamma"], w["router_w"].contiguous(), w["router_bias"]
+    w13, w2 = w["w13"], w["w2"]                                    # [G][2I][H], [G][H][I] e4m3 bytes
+    f = dict(dtype=torch.float32, device=dev)
+    norm_out = torch.empty(T, H, **f)
+    logits = torch.empty(T, E, **f)
+    idx = torch.empty(T, k, dtype=torch.int32, device=dev)
+    ew = torch.empty(T, k, **f)
+    mlp = torch.empty(I * H, **f)                                   # handle.mlp_buffer: one dequantised matrix
+    ein = torch.empty(T * k, H, **f)
+    gate_o = torch.empty(T * k, I, **f)
+    up_o = torch.empty(T * k, I, **f)
+    eout = torch.empty(T * k, H, **f)
+    slots = torch.empty(T * k, H, **f)                              # combine's [t][slot][H] layout
+    sh_gate = torch.empty(T, I, **f)
+    sh_up = torch.empty(T, I, **f)
+    sh_out = torch.empty(T, H, **f)
+    out = torch.empty(T, H, **f)
+    stream = torch.cuda.current_stream(dev)
+    st = vp(stream.cuda_stream)
+    h = vp()
+    if C.cbwCreate(ctypes.byref(h)) != 0 or C.cbwSetStream(h, st) != 0:
+        raise RuntimeError("cbwCreate / cbwSetStream failed")
+    one, zero = f32(1.0), f32(0.0)
+    launches = [0]
+
+    def P(t, off=0):
+        return vp(t.data_ptr() + off)
+
+    def sgemm(m, n, kk, A, lda, B, ldb, Cm, ldc):
+        # engine.t:1328-1345: cbwSgemm(handle, N, N, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc)
+        if C.cbwSgemm(h, 0, 0, m, n, kk, ctypes.byref(one), A, lda, B, ldb, ctypes.byref(zero), Cm, ldc) != 0:
+            raise RuntimeError("cbwSgemm failed")
+        launches[0] += 1
+
+    def expert(g, rows, n, x_in, go, uo, yo):
+        """One expert's MLP over n rows, engine.t:1326-1345 (gate, up, swiglu, down)."""
+        K.launch_fp8_dequantize(P(w13[g]), P(mlp), I * H, st)
+        sgemm(I, n, H, P(mlp), I, P(x_in, rows * H * 4), H, P(go, rows * I * 4), I)
+        K.launch_fp8_dequantize(P(w13[g], I * H), P(mlp), I * H, st)
+        sgemm(I, n, H, P(mlp), I, P(x_in, rows * H * 4), H, P(uo, rows * I * 4), I)
+        K.launch_swiglu(P(go, rows * I * 4), P(uo, rows * I * 4), P(go, rows * I * 4), n * I, st)
+        K.launch_fp8_dequantize(P(w2[g]), P(mlp), H * I, st)
+        sgemm(H, n, I, P(mlp), H, P(go, rows * I * 4), I, P(yo, rows * H * 4), H)
+        launches[0] += 4
+
+    def step():
+        K.launch_rms_norm(P(x), P(gamma), P(norm_out), H, T, shape.eps, st)
+        K.launch_moe_gate(P(norm_out), P(router_w), P(logits), H, E, T, 0, st)
+        logits.add_(bias)                                           # the benchmark's zipf skew (glue)
+        K.launch_moe_topk(P(logits), P(idx), P(ew), E, k, T, st)
+        flat = idx.view(-1).long()
+        order = torch.argsort(flat, stable=True)                    # slot positions t*k+j, expert-major
+        counts = torch.bincount(flat, minlength=E).tolist()         # host loop bounds
+        torch.index_select(norm_out, 0, order // k, out=ein)
+        row = 0
+        for e in range(E):
+            n = counts[e]
+            if n:
+                expert(e, row, n, ein, gate_o, up_o, eout)
+            row += n
+        slots.index_copy_(0, order, eout)
+        K.launch_moe_combine(P(slots), P(ew), P(out), H, k, T, st)
+        for s in range(S):
+            expert(E + s, 0, T, norm_out, sh_gate, sh_up, sh_out)
+            K.launch_add_residual(P(out), P(sh_out), T * H, st)
+        K.launch_add_residual(P(out), P(x), T * H, st)
+        launches[0] += 5 + S
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    launches[0] = 0
+    times = []
+    with ClockSampler(0) as clk:
+        for _ in range(args.steps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            step()
+            b.record(stream)
+            b.synchronize()
+            times.append(a.elapsed_time(b))
+    C.cbwDestroy(h)
+    ms = sum(times) / len(times)
+    line = {**base, "value": T / (ms / 1000.0), "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+            "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD["prefill"], "tokens": T, "hidden": H, "experts": E, "top_k": k,
+                       "intermediate": I, "shared_experts": S, "router": "softmax top-k, zipf(1.1) bias",
+                       "path": "reference csrc/kernels.cu + cuBLAS SGEMM (cbwSgemm), engine.t:1317-1347 order, "
+                               "per-expert weights substituted", "l2": "weights (1.3 GB e4m3) exceed L2"},
+            "reference_launches_per_step": launches[0] // max(1, args.steps),
+            "clocks": clk.summary()}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -628,6 +786,8 @@ def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.impl == "reference_gpu":
+        return run_reference_gpu(args)
     return run_ours(args)
 
 
