@@ -101,11 +101,15 @@ typedef void* cbwLtMatmulPreference_t;
  * Either mode may be or-ed with CBW_GEMM_SMALL_TILES (tiles of at most 32
  * rows and a deeper weight ring: the decode form) or CBW_GEMM_FULL_TILES;
  * without either, small tiles are used when rows <= 32 * num_groups.  The
- * full form has two variants with bit-identical results: one SM per tile, and
- * pairs of SMs (tcgen05 cta_group::2, 256 weight rows x up to 128 rows per
- * instruction; needs K % 256 == 0 and, for the down mode, N % 256 == 0).  By
- * default the gated mode runs on one SM and the down mode on pairs;
- * CBW_GEMM_ONE_SM_TILES or CBW_GEMM_PAIR_TILES (instead of FULL) picks one.
+ * full form has three variants with bit-identical results: token-major tiles
+ * (128 rows x 256 weight rows per instruction -- the gate and up rows of 128
+ * output columns, or 256 down rows; the down mode needs N % 256 == 0), one SM
+ * per tile (128 weight rows x up to 128 rows), and pairs of SMs (tcgen05
+ * cta_group::2, 256 weight rows x up to 128 rows; needs K % 256 == 0 and,
+ * for the down mode, N % 256 == 0).  By default both modes run token-major;
+ * a down projection with N % 256 != 0 runs on one SM (one plane) or in
+ * 32-token tiles (two planes).  CBW_GEMM_TOKEN_TILES, CBW_GEMM_ONE_SM_TILES or
+ * CBW_GEMM_PAIR_TILES (instead of FULL) picks one.
  * The decode form adds a row's K blocks in a different order from the full
  * form, so its results differ from the full form's in the last bits.
  *
@@ -116,8 +120,8 @@ typedef void* cbwLtMatmulPreference_t;
  * partial covers both planes (twice the MMA work) and carries about 7
  * significant bits of every activation instead of 4.  The gated mode then
  * writes its output in the same two-plane form (hi at out, lo at
- * out + rows*N); the down mode reads it.  The full down form runs on CTA
- * pairs (K % 256 == 0 and N % 256 == 0) or else in 32-token tiles.
+ * out + rows*N); the down mode reads it.  The full down form runs token-major
+ * or on CTA pairs (both need N % 256 == 0) or else in 32-token tiles.
  *
  * Requirements: K % 128 == 0, N % 128 == 0, start[g] % 16 == 0, every
  * segment [start, start + round_up(count,16)) inside [0, rows), a_ld (the
@@ -132,6 +136,7 @@ typedef enum {
     CBW_GEMM_FULL_TILES = 0x20,
     CBW_GEMM_ONE_SM_TILES = 0x40,
     CBW_GEMM_PAIR_TILES = 0x80,
+    CBW_GEMM_TOKEN_TILES = 0x30,
     CBW_GEMM_ACT_X2 = 0x100
 } cbwGemmMode_t;
 

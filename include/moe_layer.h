@@ -158,10 +158,10 @@ moe_status_t moe_layer_set_expert_placement(moe_layer_t* layer, const int32_t* s
  * GPU.  The two forms add a row's K blocks in different orders, so outputs
  * differ in the last bits between them; an expert-parallel layer and a
  * one-GPU layer give bit-identical outputs when they run the same form.
- * CBW_GEMM_ONE_SM_TILES or CBW_GEMM_PAIR_TILES force that variant of the full
- * form on both GEMMs (bit-identical to each other; a GEMM whose shape or
- * activation format has no such variant fails the forward with
- * MOE_ERR_INVALID_ARGUMENT). */
+ * CBW_GEMM_ONE_SM_TILES, CBW_GEMM_PAIR_TILES or CBW_GEMM_TOKEN_TILES force
+ * that variant of the full form on both GEMMs (bit-identical to one another;
+ * a GEMM whose shape or activation format has no such variant fails the
+ * forward with MOE_ERR_INVALID_ARGUMENT). */
 moe_status_t moe_layer_set_gemm_form(moe_layer_t* layer, int form);
 
 /* No counterpart in the reference.  Activation format of the two expert

@@ -131,10 +131,11 @@ def _ref_x2(A2, A_s, W, W_s, starts, counts):
     return out
 
 
-FORMS = [("small", M.GEMM_SMALL_TILES), ("one_sm", M.GEMM_ONE_SM_TILES), ("pair", M.GEMM_PAIR_TILES)]
+FORMS = [("small", M.GEMM_SMALL_TILES), ("one_sm", M.GEMM_ONE_SM_TILES), ("pair", M.GEMM_PAIR_TILES),
+         ("token", M.GEMM_TOKEN_TILES)]
 
 
-@pytest.mark.parametrize("form", [f for f in FORMS if f[0] != "one_sm"], ids=["small", "pair"])
+@pytest.mark.parametrize("form", [f for f in FORMS if f[0] != "one_sm"], ids=["small", "pair", "token"])
 @pytest.mark.parametrize("counts,K,N", [([16], 256, 256), ([1, 0, 130, 255, 300], 512, 256), ([40, 257], 1536, 512)])
 def test_grouped_gemm_down_x2(gpu, form, counts, K, N):
     g = torch.Generator().manual_seed(11 + sum(counts))
@@ -199,6 +200,45 @@ def test_grouped_gemm_gated_x2(gpu, form, counts, K, N):
         assert (lo_v.abs() <= hi_v.abs() * 2.0 ** -4 + 2.0 ** -9).all()
         pad_end = starts[gi] + (counts[gi] + 15) // 16 * 16
         assert (hq_c[:, starts[gi] + counts[gi]:pad_end] == 0).all()
+
+
+@pytest.mark.parametrize("counts,K", [([16], 256), ([3, 0, 128, 129, 260, 1], 512), ([1000, 45], 1536)])
+def test_grouped_gemm_x2_token_major_bit_identical(gpu, counts, K):
+    """Two-plane token-major tiles give the bits of the other full forms: the
+    gated output (both planes and the scales) equal to the one-SM form's, the
+    down output equal to the CTA-pair form's."""
+    N = 256
+    g = torch.Generator().manual_seed(29 + sum(counts))
+    cnt = torch.tensor(counts, dtype=torch.int32, device=gpu)
+    starts, rows, A2, A_s, a_ld, W, W_s = _groups_x2(counts, K, 2 * N, g)
+    st = torch.tensor(starts, dtype=torch.int32, device=gpu)
+    gated = {}
+    for form in (M.GEMM_ONE_SM_TILES, M.GEMM_TOKEN_TILES):
+        hq = torch.full((2, rows, N), 0x55, dtype=torch.uint8, device=gpu)
+        hs = torch.full((N // 128, a_ld), -1.0, device=gpu)
+        err = torch.zeros(1, dtype=torch.int32, device=gpu)
+        M.grouped_gemm(M.GEMM_GATED_SWIGLU | form | M.GEMM_ACT_X2, A2.contiguous().to(gpu), A_s.to(gpu), a_ld,
+                       W.to(gpu), W_s.to(gpu), cnt, st, hq, hs, a_ld, K, N, rows, error_word=err)
+        torch.cuda.synchronize()
+        assert err.item() == 0
+        gated[form] = (hq.cpu(), hs.cpu())
+    _, _, _, _, _, Wd, Wd_s = _groups_x2(counts, K, N, g)
+    down = {}
+    for form in (M.GEMM_PAIR_TILES, M.GEMM_TOKEN_TILES):
+        out = torch.full((rows, N), float("nan"), dtype=torch.bfloat16, device=gpu)
+        err = torch.zeros(1, dtype=torch.int32, device=gpu)
+        M.grouped_gemm(M.GEMM_DOWN_BF16 | form | M.GEMM_ACT_X2, A2.contiguous().to(gpu), A_s.to(gpu), a_ld,
+                       Wd.to(gpu), Wd_s.to(gpu), cnt, st, out, None, 0, K, N, rows, error_word=err)
+        torch.cuda.synchronize()
+        assert err.item() == 0
+        down[form] = out.cpu()
+    for s0, c in zip(starts, counts):
+        pad = (c + 15) // 16 * 16
+        a_, b_ = gated[M.GEMM_TOKEN_TILES], gated[M.GEMM_ONE_SM_TILES]
+        assert torch.equal(a_[0][:, s0:s0 + pad], b_[0][:, s0:s0 + pad])
+        assert torch.equal(a_[1][:, s0:s0 + pad], b_[1][:, s0:s0 + pad])
+        assert torch.equal(down[M.GEMM_TOKEN_TILES][s0:s0 + c].view(torch.int16),
+                           down[M.GEMM_PAIR_TILES][s0:s0 + c].view(torch.int16))
 
 
 def _layer_x2(shape, w, x, T, routing=None):

@@ -462,8 +462,9 @@ def test_grouped_gemm_small_tiles(gpu, gated, counts):
 @pytest.mark.parametrize("counts,K", [([16], 256), ([1, 0, 130, 255, 300, 17], 512), ([128] * 9 + [7], 768),
                                       ([1000, 3, 129], 1536)])
 def test_grouped_gemm_pair_matches_one_sm(gpu, gated, counts, K):
-    """The full form on CTA pairs (tcgen05 cta_group::2) against the same form
-    on one SM per tile: identical bits, and both within the float64
+    """The full form on CTA pairs (tcgen05 cta_group::2) and in token-major
+    tiles (128 token rows x 256 weight rows per instruction) against the same
+    form on one SM per tile: identical bits, and all within the float64
     reference's tolerance."""
     N = 256
     g = torch.Generator().manual_seed(101 + sum(counts) + gated)
@@ -471,7 +472,7 @@ def test_grouped_gemm_pair_matches_one_sm(gpu, gated, counts, K):
     cnt = torch.tensor(counts, dtype=torch.int32, device=gpu)
     st = torch.tensor(starts, dtype=torch.int32, device=gpu)
     outs = {}
-    for form in (M.GEMM_PAIR_TILES, M.GEMM_ONE_SM_TILES):
+    for form in (M.GEMM_PAIR_TILES, M.GEMM_ONE_SM_TILES, M.GEMM_TOKEN_TILES):
         err = torch.zeros(1, dtype=torch.int32, device=gpu)
         if gated:
             hq = torch.full((rows, N), 0x55, dtype=torch.uint8, device=gpu)
@@ -504,14 +505,15 @@ def test_grouped_gemm_pair_matches_one_sm(gpu, gated, counts, K):
                 y = outs[form][0][s0:s0 + c].double()
                 assert torch.isfinite(y).all()
                 assert (y - r).abs().max() / r.abs().max() < 8e-3, (form, gi)
-        if gated:
-            a_, b_ = outs[M.GEMM_PAIR_TILES], outs[M.GEMM_ONE_SM_TILES]
-            assert torch.equal(a_[0][s0:s0 + c], b_[0][s0:s0 + c]), gi
-            assert torch.equal(a_[1][:, s0:s0 + c], b_[1][:, s0:s0 + c]), gi
-        else:
-            a_ = outs[M.GEMM_PAIR_TILES][0][s0:s0 + c].view(torch.int16)
-            b_ = outs[M.GEMM_ONE_SM_TILES][0][s0:s0 + c].view(torch.int16)
-            assert torch.equal(a_, b_), gi
+        for other in (M.GEMM_PAIR_TILES, M.GEMM_TOKEN_TILES):
+            if gated:
+                a_, b_ = outs[other], outs[M.GEMM_ONE_SM_TILES]
+                assert torch.equal(a_[0][s0:s0 + c], b_[0][s0:s0 + c]), (other, gi)
+                assert torch.equal(a_[1][:, s0:s0 + c], b_[1][:, s0:s0 + c]), (other, gi)
+            else:
+                a_ = outs[other][0][s0:s0 + c].view(torch.int16)
+                b_ = outs[M.GEMM_ONE_SM_TILES][0][s0:s0 + c].view(torch.int16)
+                assert torch.equal(a_, b_), (other, gi)
 
 
 @pytest.mark.parametrize("gated", [False, True])

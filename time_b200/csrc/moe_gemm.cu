@@ -622,6 +622,422 @@ grouped_fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
     if (threadIdx.x == 0 && *abort_flag && p.error_word) atomicExch(p.error_word, 1);
 }
 
+// ------------------------------------------------------------------ token-major full form
+// The default full form.  The roles of the one-SM form are kept, but the UMMA
+// operands are not swapped: M = 128 token rows of one expert (TMEM lanes) and
+// N = 256 weight rows -- the tile's 128 gate rows and their 128 up rows
+// (gated), or two 128-row blocks of W_down (down) -- so one tcgen05.mma is
+// 128 x 256 x 32.  An N = 128 or N = 64 instruction costs the tensor core about
+// as long as an N = 256 one (a fixed per-instruction floor, measured: 64 % and
+// 32 % of the fp8 peak against 96 % for N = 256 at M = 128), so the gated K
+// block issues 4 instructions per plane instead of 8, and the padding of a
+// ragged token chunk to 128 rows costs less than the instruction count saved.
+// A thread of the promotion warps owns one token row, so its per-K-block scale
+// is a scalar (token scale x weight-block scale, folded once per CTA by the
+// scale warp) and the fused epilogue stores each thread's 32 (gated, e4m3) or
+// 64 (down, bf16) output columns straight from registers: the 1x128 amax of a
+// token is the max over the four column-group warps of its lane quarter,
+// exchanged through 2 KB of shared memory.  Without the transposing stage the
+// operand ring holds four 48 KB stages (one plane) or three 64 KB stages (two
+// planes).  The products, their K order and every rounding step are those of
+// the one-SM form, so both give bit-identical outputs.
+template <bool kGated, bool kX2>
+struct TmCfg {
+    static constexpr int kPlanes = kX2 ? 2 : 1;
+    static constexpr int kTok = 128;                          // token rows per tile (UMMA M)
+    static constexpr int kWRows = 256;                        // weight rows per tile (UMMA N)
+    static constexpr int kWBytes = kWRows * kBlockK;          // 32 KB
+    static constexpr int kABytes = kPlanes * kTok * kBlockK;  // 16 / 32 KB: [plane][rows][128 B]
+    static constexpr int kStageBytes = kWBytes + kABytes;
+    static constexpr int kStages = kX2 ? 3 : 4;
+    static constexpr int kSStages = 8;
+    static constexpr int kScaleFloats = 2 * kTok;             // folded [first weight block][second] per token
+    static constexpr int kTBufs = 2;                          // 2 x 256 TMEM columns
+    static constexpr int kBufCols = 256;
+    static constexpr int kOffStages = 0;
+    static constexpr int kOffScale = kOffStages + kStages * kStageBytes;
+    static constexpr int kOffAmax = kOffScale + kSStages * kScaleFloats * 4;   // [tile parity][4 groups][128] fp32
+    static constexpr int kOffTables = kOffAmax + 2 * 4 * kTok * 4;
+    static constexpr int kOffBars = kOffTables + (4 * kMaxGroups + 2) * 4;
+    static constexpr int kNumBars = 2 * kStages + 3 * kSStages + 2 * kTBufs + 1;
+    static constexpr int kOffMisc = kOffBars + kNumBars * 8;
+    static constexpr int kSmemBytes = kOffMisc + 64 + 1024;
+    static_assert(kOffBars % 8 == 0, "mbarrier alignment");
+    static_assert(kStageBytes % 1024 == 0 && kWBytes % 1024 == 0, "128-byte-swizzled tiles on 1024-byte boundaries");
+    static_assert(kTBufs * kBufCols <= kTmemCols, "TMEM partial buffers");
+    static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+};
+
+template <bool kGated, bool kX2>
+__global__ void __launch_bounds__(kNumThreads, 1)
+grouped_fp8_gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w,
+                           const __grid_constant__ CUtensorMap tmap_a,
+                           const __grid_constant__ CUtensorMap tmap_a64,
+                           const __grid_constant__ CUtensorMap tmap_a128,
+                           const GemmParams p) {
+    using C = TmCfg<kGated, kX2>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+
+    float* scale_ring = reinterpret_cast<float*>(smem + C::kOffScale);
+    float* amax_x = reinterpret_cast<float*>(smem + C::kOffAmax);
+    int* t_prefix = reinterpret_cast<int*>(smem + C::kOffTables);
+    int* t_chunks = t_prefix + (kMaxGroups + 1);
+    int* t_start = t_chunks + kMaxGroups;
+    int* counts_smem = t_start + kMaxGroups;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBars);
+    uint64_t* full_bar = bars;
+    uint64_t* empty_bar = bars + C::kStages;
+    uint64_t* sfull_bar = bars + 2 * C::kStages;
+    uint64_t* sempty_bar = sfull_bar + C::kSStages;
+    uint64_t* cready_bar = sempty_bar + C::kSStages;
+    uint64_t* tfull_bar = cready_bar + C::kSStages;
+    uint64_t* tempty_bar = tfull_bar + C::kTBufs;
+    uint64_t* epi_bar = tempty_bar + C::kTBufs;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffMisc);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kOffMisc + 8);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int G = p.G;
+    const int KB = p.K / kBlockK;
+    const int nbt = kGated ? p.N / kTileM : p.N / C::kWRows;   // output column blocks per group
+
+    // ---------------------------------------------------------------- setup
+    if (warp == 0 && lane == 0) {
+        for (int s = 0; s < C::kStages; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1);
+        }
+        for (int s = 0; s < C::kSStages; ++s) {
+            mbar_init(&sfull_bar[s], 1);
+            mbar_init(&sempty_bar[s], kNumPromoWarps);
+            mbar_init(&cready_bar[s], 1);
+        }
+        for (int b = 0; b < C::kTBufs; ++b) {
+            mbar_init(&tfull_bar[b], 1);
+            mbar_init(&tempty_bar[b], kNumPromoWarps);
+        }
+        mbar_init(epi_bar, kNumPromoWarps);
+        *abort_flag = 0;
+        fence_mbar_init();
+        prefetch_tmap(&tmap_w);
+        prefetch_tmap(&tmap_a);
+        prefetch_tmap(&tmap_a64);
+        prefetch_tmap(&tmap_a128);
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+    if (warp == 2) {
+        // tiles per group: ceil(count / 128) token chunks x nbt column blocks
+        int per_lane = (G + 31) / 32;
+        int g0 = lane * per_lane;
+        int local = 0;
+        for (int i = 0; i < per_lane; ++i) {
+            int g = g0 + i;
+            if (g < G) {
+                int cnt = p.count[g];
+                int ch = (cnt + C::kTok - 1) / C::kTok;
+                t_chunks[g] = ch;
+                t_start[g] = p.start[g];
+                counts_smem[g] = cnt;
+                local += ch * nbt;
+            }
+        }
+        int incl = local;
+        for (int o = 1; o < 32; o <<= 1) {
+            int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        int run = incl - local;
+        for (int i = 0; i < per_lane; ++i) {
+            int g = g0 + i;
+            if (g < G) {
+                t_prefix[g] = run;
+                run += t_chunks[g] * nbt;
+            }
+        }
+        if (lane == 31) t_prefix[G] = incl;
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int total_tiles = t_prefix[G];
+
+    if (warp < kFirstPromoWarp) {
+      asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" :: "n"(kRoleRegs));
+      if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            int s = 0, ss = 0;
+            uint32_t phase = 0, sphase = 0;
+            uint32_t armed_mask = 0, armed_phase = 0;
+            uint32_t sarmed_mask = 0, sarmed_phase = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+                TileCoord tc = decode_tile(tile, t_prefix, t_chunks, t_start, counts_smem, G, C::kTok);
+                // one token box of 32, 64 or 128 rows (the MMA reads 128 rows; rows past
+                // the chunk hold stale bytes whose output rows are never stored)
+                const int box = tc.ntile <= 32 ? 32 : (tc.ntile <= 64 ? 64 : 128);
+                const CUtensorMap* tmap_b = box == 32 ? &tmap_a : (box == 64 ? &tmap_a64 : &tmap_a128);
+                const uint32_t bytes = C::kWBytes + box * kBlockK * C::kPlanes;
+                const int wrow = tc.g * p.w_rows + tc.nb * (kGated ? kTileM : C::kWRows);
+                for (int kb = 0; kb < KB; ++kb) {
+                    if (!mbar_wait_bounded(&empty_bar[s], phase ^ 1, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
+                    uint8_t* st = smem + C::kOffStages + s * C::kStageBytes;
+                    mbar_arrive_expect_tx(&full_bar[s], bytes);
+                    if (kGated)   // {K, rows, gate/up}: [128 gate rows][128 up rows]
+                        tma_load_3d(&tmap_w, &full_bar[s], st, kb * kBlockK, wrow, 0);
+                    else          // 256 rows
+                        tma_load_2d(&tmap_w, &full_bar[s], st, kb * kBlockK, wrow);
+                    if constexpr (kX2)   // {K, rows, plane}: [hi | lo][box rows][128 B]
+                        tma_load_3d(tmap_b, &full_bar[s], st + C::kWBytes, kb * kBlockK, tc.row0, 0);
+                    else
+                        tma_load_2d(tmap_b, &full_bar[s], st + C::kWBytes, kb * kBlockK, tc.row0);
+                    armed_mask |= 1u << s;
+                    armed_phase = (armed_phase & ~(1u << s)) | (phase << s);
+                    if (++s == C::kStages) { s = 0; phase ^= 1; }
+
+                    if (!mbar_wait_bounded(&sempty_bar[ss], sphase ^ 1, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&sfull_bar[ss], tc.ntile * 4);
+                    bulk_load(scale_ring + ss * C::kScaleFloats + C::kTok,
+                              p.a_scale + (size_t)kb * p.a_ld + tc.row0, tc.ntile * 4, &sfull_bar[ss]);
+                    sarmed_mask |= 1u << ss;
+                    sarmed_phase = (sarmed_phase & ~(1u << ss)) | (sphase << ss);
+                    if (++ss == C::kSStages) { ss = 0; sphase ^= 1; }
+                }
+            }
+            if (!ok) {
+                for (int i = 0; i < C::kStages; ++i)
+                    if (armed_mask & (1u << i)) mbar_drain(&full_bar[i], (armed_phase >> i) & 1u);
+                for (int i = 0; i < C::kSStages; ++i)
+                    if (sarmed_mask & (1u << i)) mbar_drain(&sfull_bar[i], (sarmed_phase >> i) & 1u);
+            }
+        }
+      } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            int s = 0, b = 0;
+            uint32_t phase = 0, tphase = 0;
+            bool ok = true;
+            bool issued = false;
+            const uint32_t idesc = idesc_e4m3_f32(C::kTok, C::kWRows);
+            for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+                TileCoord tc = decode_tile(tile, t_prefix, t_chunks, t_start, counts_smem, G, C::kTok);
+                const uint32_t plane_bytes = (tc.ntile <= 32 ? 32 : (tc.ntile <= 64 ? 64 : 128)) * kBlockK;
+                for (int kb = 0; kb < KB; ++kb) {
+                    if (!mbar_wait_bounded(&full_bar[s], phase, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
+                    if (!mbar_wait_bounded(&tempty_bar[b], tphase ^ 1, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t w_addr = smem_u32(smem + C::kOffStages + s * C::kStageBytes);
+                    const uint32_t a_addr = w_addr + C::kWBytes;
+                    const uint32_t d = tmem_base + b * C::kBufCols;
+#pragma unroll
+                    for (int pl = 0; pl < C::kPlanes; ++pl) {
+#pragma unroll
+                        for (int k = 0; k < kBlockK / 32; ++k)
+                            umma_f8(d, umma_desc_sw128(a_addr + pl * plane_bytes + k * 32),
+                                    umma_desc_sw128(w_addr + k * 32), idesc, (k > 0 || pl > 0) ? 1u : 0u);
+                    }
+                    umma_commit(&empty_bar[s]);
+                    umma_commit(&tfull_bar[b]);
+                    issued = true;
+                    if (++s == C::kStages) { s = 0; phase ^= 1; }
+                    if (++b == C::kTBufs) { b = 0; tphase ^= 1; }
+                }
+            }
+            if (!ok && issued) {
+                int lb = (b + C::kTBufs - 1) % C::kTBufs;
+                uint32_t lph = (b == 0) ? (tphase ^ 1) : tphase;
+                mbar_drain(&tfull_bar[lb], lph);
+            }
+        }
+      } else if (warp == 2) {
+        // ------------------------------------------------------------ scale folding
+        // entry [0, 128): token scale x the scale of the tile's first weight block
+        // (gate / W_down rows 256 nb..), [128, 256): x the second (up / rows 256 nb + 128..);
+        // the bulk copy lands the raw token scales in the second half
+        int ss = 0;
+        uint32_t sphase = 0;
+        bool ok = true;
+        const int wsb = p.w_rows / kTileM;
+        for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+            TileCoord tc = decode_tile(tile, t_prefix, t_chunks, t_start, counts_smem, G, C::kTok);
+            const int blk0 = kGated ? tc.nb : 2 * tc.nb;
+            const int blk1 = kGated ? p.N / kTileM + tc.nb : 2 * tc.nb + 1;
+            const float* ws0 = p.w_scale + ((size_t)tc.g * wsb + blk0) * KB;
+            const float* ws1 = p.w_scale + ((size_t)tc.g * wsb + blk1) * KB;
+            for (int kb = 0; kb < KB; ++kb) {
+                const float s0 = __ldg(ws0 + kb);
+                const float s1 = __ldg(ws1 + kb);
+                if (!mbar_wait_bounded(&sfull_bar[ss], sphase, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
+                float* e = scale_ring + ss * C::kScaleFloats;
+                for (int c = lane; c < tc.ntile; c += 32) {
+                    const float a = e[C::kTok + c];
+                    e[c] = a * s0;
+                    e[C::kTok + c] = a * s1;
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&cready_bar[ss]);
+                if (++ss == C::kSStages) { ss = 0; sphase ^= 1; }
+            }
+        }
+      }
+    } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" :: "n"(kPromoRegs));
+        // ------------------------------------------------------------ promotion + epilogue
+        const int pw = warp - kFirstPromoWarp;        // 0..15
+        const int quarter = warp & 3;                  // TMEM lane quarter this warp may access
+        const int colgrp = pw >> 2;                    // 0..3
+        const int r = quarter * 32 + lane;             // token row within the tile
+        const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+        int ss = 0, b = 0;
+        uint32_t sphase = 0, tphase = 0, ephase = 0;
+        bool ok = true;
+        int parity = 0;
+        auto group_sync = [&]() -> bool {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(epi_bar);
+            const bool res = mbar_wait_bounded(epi_bar, ephase, abort_flag, kWaitTimeoutNs);
+            ephase ^= 1;
+            return res;
+        };
+        // TMEM column of 16-column chunk c (0..3) and the acc2 pairs it feeds (8c..8c+7):
+        // gated: chunks 0, 1 = gate columns 32 colgrp + [0, 32), 2, 3 = the up columns
+        // (TMEM + 128); down: columns 64 colgrp + 16 c
+        auto tcol = [&](int c) { return kGated ? (c >> 1) * 128 + colgrp * 32 + (c & 1) * 16 : colgrp * 64 + c * 16; };
+
+        for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+            TileCoord tc = decode_tile(tile, t_prefix, t_chunks, t_start, counts_smem, G, C::kTok);
+            float2 acc2[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc2[i] = make_float2(0.0f, 0.0f);
+
+            for (int kb = 0; kb < KB; ++kb) {
+                if (!mbar_wait_bounded(&cready_bar[ss], sphase, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
+                if (!mbar_wait_bounded(&tfull_bar[b], tphase, abort_flag, kWaitTimeoutNs)) { ok = false; break; }
+                tc_fence_after();
+                const float* e = scale_ring + ss * C::kScaleFloats;
+                const float c_lo = kGated ? e[r] : e[(colgrp >> 1) * C::kTok + r];
+                const float c_hi = kGated ? e[C::kTok + r] : c_lo;
+                const uint32_t tbuf = lane_addr + b * C::kBufCols;
+                auto fold = [&](int c, const uint32_t (&pv)[16]) {
+                    const float cs = (kGated && c >= 2) ? c_hi : c_lo;
+                    const float2 c2 = make_float2(cs, cs);
+#pragma unroll
+                    for (int j = 0; j < 16; j += 2) {
+                        float2& a = acc2[8 * c + j / 2];
+                        a = ffma2(make_float2(__uint_as_float(pv[j]), __uint_as_float(pv[j + 1])), c2, a);
+                    }
+                };
+                uint32_t pa[16], pb[16];
+                tmem_ld16(tbuf + tcol(0), pa);
+                tmem_wait_ld();
+                tmem_ld16(tbuf + tcol(1), pb);
+                fold(0, pa);
+                tmem_wait_ld();
+                tmem_ld16(tbuf + tcol(2), pa);
+                fold(1, pb);
+                tmem_wait_ld();
+                tmem_ld16(tbuf + tcol(3), pb);
+                fold(2, pa);
+                tmem_wait_ld();
+                fold(3, pb);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&tempty_bar[b]);
+                    mbar_arrive(&sempty_bar[ss]);
+                }
+                if (++ss == C::kSStages) { ss = 0; sphase ^= 1; }
+                if (++b == C::kTBufs) { b = 0; tphase ^= 1; }
+            }
+            if (!ok || *abort_flag) { ok = false; break; }
+
+            // ---------------------------------------------------------- epilogue
+            // gated: rows [nrows, ntile) of the chunk are stored as zeros (the down
+            // projection reads whole 16-row groups); down: rows < nrows only
+            const bool row_live = r < tc.nrows;
+            const size_t row = static_cast<size_t>(tc.row0 + r);
+            if (kGated) {
+                // acc2[0..15]: gate columns 32 colgrp + 2i, +1; acc2[16..31]: the up columns
+                float amax = 0.0f;
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const float g0 = acc2[i].x, g1 = acc2[i].y;
+                    const float u0 = acc2[16 + i].x, u1 = acc2[16 + i].y;
+                    const float h0 = (g0 / (1.0f + expf(-g0))) * u0;
+                    const float h1 = (g1 / (1.0f + expf(-g1))) * u1;
+                    acc2[i] = make_float2(h0, h1);
+                    amax = fmaxf(amax, fmaxf(fabsf(h0), fabsf(h1)));
+                }
+                float* ax = amax_x + parity * 4 * C::kTok;
+                ax[colgrp * C::kTok + r] = amax;
+                if (!group_sync()) { ok = false; break; }
+                amax = fmaxf(fmaxf(ax[r], ax[C::kTok + r]), fmaxf(ax[2 * C::kTok + r], ax[3 * C::kTok + r]));
+                parity ^= 1;
+                if (r < tc.ntile) {
+                    uint32_t hi[8], lo[8];
+#pragma unroll
+                    for (int w = 0; w < 8; ++w) { hi[w] = 0u; lo[w] = 0u; }
+                    float scale = 0.0f;
+                    if (row_live && amax > 0.0f) {
+                        const float inv = 448.0f / amax;
+#pragma unroll
+                        for (int w = 0; w < 8; ++w) {
+                            const float2 v0 = acc2[2 * w], v1 = acc2[2 * w + 1];
+                            if constexpr (kX2) {
+                                const uint32_t s0 = cvt_e4m3x2_split(__fmul_rn(v0.x, inv), __fmul_rn(v0.y, inv));
+                                const uint32_t s1 = cvt_e4m3x2_split(__fmul_rn(v1.x, inv), __fmul_rn(v1.y, inv));
+                                hi[w] = (s0 & 0xFFFFu) | (s1 << 16);
+                                lo[w] = (s0 >> 16) | (s1 & 0xFFFF0000u);
+                            } else {
+                                const uint32_t q0 = cvt_e4m3x2(v0.x * inv, v0.y * inv);
+                                const uint32_t q1 = cvt_e4m3x2(v1.x * inv, v1.y * inv);
+                                hi[w] = q0 | (q1 << 16);
+                            }
+                        }
+                        scale = amax / 448.0f;
+                    }
+                    uint8_t* outq = reinterpret_cast<uint8_t*>(p.out) + row * p.N + tc.nb * 128 + colgrp * 32;
+                    uint4* o = reinterpret_cast<uint4*>(outq);
+                    o[0] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                    o[1] = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+                    if constexpr (kX2) {
+                        uint4* ol = reinterpret_cast<uint4*>(outq + p.out_plane);
+                        ol[0] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                        ol[1] = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+                    }
+                    if (colgrp == 0) p.out_scale[(size_t)tc.nb * p.out_ld + row] = scale;
+                }
+            } else if (row_live) {
+                // acc2[i]: columns 64 colgrp + 2i, +1 of the tile's 256
+                uint32_t w[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const __nv_bfloat162 h2 = __floats2bfloat162_rn(acc2[i].x, acc2[i].y);
+                    w[i] = *reinterpret_cast<const uint32_t*>(&h2);
+                }
+                uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + row * p.N +
+                                                    tc.nb * C::kWRows + colgrp * 64);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) o[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+            }
+        }
+    }
+
+    // ---------------------------------------------------------------- teardown
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kTmemCols);
+    }
+    if (threadIdx.x == 0 && *abort_flag && p.error_word) atomicExch(p.error_word, 1);
+}
+
 // ------------------------------------------------------------------ full form on CTA pairs
 // The full form (tiles of up to 128 tokens) runs on CTA pairs: a cluster of two
 // CTAs on two SMs issues tcgen05.mma with cta_group::2, M = 256 weight rows x
@@ -1279,6 +1695,70 @@ cbwStatus_t launch_gemm(const cbwGroupedGemmArgs* a, int* error_word, cudaStream
     return CBW_SUCCESS;
 }
 
+template <bool kGated, bool kX2>
+cbwStatus_t launch_gemm_tm(const cbwGroupedGemmArgs* a, int* error_word, cudaStream_t stream) {
+    using C = TmCfg<kGated, kX2>;
+    const int w_rows = kGated ? 2 * a->N : a->N;
+    CUtensorMap tw, ta, ta64, ta128;
+    if (kGated) {
+        if (!encode_gate_up_3d(&tw, a->w, static_cast<uint64_t>(a->num_groups) * w_rows, a->K, a->N))
+            return CBW_ERROR_INTERNAL;
+    } else if (!encode_u8_2d(&tw, a->w, static_cast<uint64_t>(a->num_groups) * w_rows, a->K, C::kWRows)) {
+        return CBW_ERROR_INTERNAL;
+    }
+    const uint64_t rows = static_cast<uint64_t>(a->rows), aplane = rows * static_cast<uint64_t>(a->K);
+    if (kX2) {
+        if (!encode_u8_planes(&ta, a->a, rows, a->K, 32, aplane) ||
+            !encode_u8_planes(&ta64, a->a, rows, a->K, 64, aplane) ||
+            !encode_u8_planes(&ta128, a->a, rows, a->K, 128, aplane))
+            return CBW_ERROR_INTERNAL;
+    } else if (!encode_u8_2d(&ta, a->a, rows, a->K, 32) || !encode_u8_2d(&ta64, a->a, rows, a->K, 64) ||
+               !encode_u8_2d(&ta128, a->a, rows, a->K, 128)) {
+        return CBW_ERROR_INTERNAL;
+    }
+    static int sm_count[kMaxDevices] = {};
+    static bool attr_set[kMaxDevices] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int sms = 0;
+    if (dev >= 0 && dev < kMaxDevices && sm_count[dev] > 0) {
+        sms = sm_count[dev];
+    } else {
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (dev >= 0 && dev < kMaxDevices) sm_count[dev] = sms;
+    }
+    {
+        cudaError_t e = smem_optin_once(grouped_fp8_gemm_tm_kernel<kGated, kX2>, C::kSmemBytes, attr_set);
+        if (e != cudaSuccess) {
+            std::fprintf(stderr, "cbwFp8BlockScaledGroupedGemm: shared memory opt-in (%d B) failed: %s\n",
+                         C::kSmemBytes, cudaGetErrorString(e));
+            return CBW_ERROR_EXECUTION_FAILED;
+        }
+    }
+    GemmParams p;
+    p.a_scale = a->a_scale;
+    p.a_ld = a->a_ld;
+    p.w_scale = a->w_scale;
+    p.count = a->count;
+    p.start = a->start;
+    p.out = a->out;
+    p.out_scale = a->out_scale;
+    p.out_ld = a->out_ld;
+    p.out_plane = static_cast<size_t>(a->rows) * a->N;
+    p.G = a->num_groups;
+    p.K = a->K;
+    p.N = a->N;
+    p.w_rows = w_rows;
+    p.error_word = error_word;
+    grouped_fp8_gemm_tm_kernel<kGated, kX2><<<sms, kNumThreads, C::kSmemBytes, stream>>>(tw, ta, ta64, ta128, p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        std::fprintf(stderr, "cbwFp8BlockScaledGroupedGemm: token-major launch failed: %s\n", cudaGetErrorString(e));
+        return CBW_ERROR_EXECUTION_FAILED;
+    }
+    return CBW_SUCCESS;
+}
+
 // Tensor maps of the pair form: every load moves two K blocks.
 //   weights, gated: {128 B, rows, gate/up (I rows apart), K blocks} box {128, 64, 2, 2}
 //   weights, down:  {128 B, rows, K blocks} box {128, 128, 2}
@@ -1399,41 +1879,48 @@ extern "C" cbwStatus_t cbwFp8BlockScaledGroupedGemm(const cbwGroupedGemmArgs* ar
     const bool x2 = (a.mode & CBW_GEMM_ACT_X2) != 0;
     if (a.mode & ~(0xFF | CBW_GEMM_ACT_X2)) return CBW_ERROR_INVALID_VALUE;
     if (tiles != 0 && tiles != CBW_GEMM_SMALL_TILES && tiles != CBW_GEMM_FULL_TILES && tiles != CBW_GEMM_ONE_SM_TILES &&
-        tiles != CBW_GEMM_PAIR_TILES)
+        tiles != CBW_GEMM_PAIR_TILES && tiles != CBW_GEMM_TOKEN_TILES)
         return CBW_ERROR_INVALID_VALUE;
     // 32-token tiles when the padded rows average at most 32 per group (decode
     // batches: a few tokens per expert), full tiles otherwise
     const bool small = tiles == CBW_GEMM_SMALL_TILES ||
                        (tiles == 0 && static_cast<long long>(a.rows) <= 32ll * a.num_groups);
-    if ((tiles == CBW_GEMM_ONE_SM_TILES || tiles == CBW_GEMM_PAIR_TILES) && small) return CBW_ERROR_INVALID_VALUE;
+    if ((tiles == CBW_GEMM_ONE_SM_TILES || tiles == CBW_GEMM_PAIR_TILES || tiles == CBW_GEMM_TOKEN_TILES) && small)
+        return CBW_ERROR_INVALID_VALUE;
     const bool pair_ok = a.K % (kPairKbPerStage * kBlockK) == 0 && (base == CBW_GEMM_GATED_SWIGLU || a.N % 256 == 0);
     if (tiles == CBW_GEMM_PAIR_TILES && !pair_ok) return CBW_ERROR_INVALID_VALUE;
+    // token-major tiles: 256 weight rows per tile (gate + up, or two W_down blocks)
+    const bool tm_ok = base == CBW_GEMM_GATED_SWIGLU || a.N % 256 == 0;
+    if (tiles == CBW_GEMM_TOKEN_TILES && !tm_ok) return CBW_ERROR_INVALID_VALUE;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    // The full form's default: the gated projection on one SM per tile, the down
-    // projection on CTA pairs (measured faster at the GLM shape, 4096 tokens:
-    // gate/up 1.27 ms one-SM vs 1.87 ms paired -- the paired tile's cross-CTA amax
-    // exchange and SwiGLU staging cost more than its halved MMA count saves;
-    // down 0.84 ms one-SM vs 0.79 ms paired).
-    const bool pair = tiles == CBW_GEMM_PAIR_TILES ||
-                      (tiles != CBW_GEMM_ONE_SM_TILES && base == CBW_GEMM_DOWN_BF16 && pair_ok);
+    // The full form's default is token-major (GLM shape, 4096 tokens, one plane:
+    // gate/up 1.27 ms one-SM, 1.87 ms paired; down 0.84 ms one-SM, 0.79 ms paired,
+    // before the token-major form); the one-SM and pair forms stay selectable.
+    const bool tm = !small && (tiles == CBW_GEMM_TOKEN_TILES || ((tiles == 0 || tiles == CBW_GEMM_FULL_TILES) && tm_ok));
+    const bool pair = !tm && (tiles == CBW_GEMM_PAIR_TILES ||
+                              (tiles != CBW_GEMM_ONE_SM_TILES && base == CBW_GEMM_DOWN_BF16 && pair_ok));
     if (base == CBW_GEMM_GATED_SWIGLU) {
         if (!a.out_scale || a.out_ld < a.rows) return CBW_ERROR_INVALID_VALUE;
         if (x2) {
             if (small) return launch_gemm<true, true, true>(&a, error_word, st);
+            if (tm) return launch_gemm_tm<true, true>(&a, error_word, st);
             return pair ? launch_gemm_pair<true, true>(&a, error_word, st) : launch_gemm<true, false, true>(&a, error_word, st);
         }
         if (small) return launch_gemm<true, true, false>(&a, error_word, st);
+        if (tm) return launch_gemm_tm<true, false>(&a, error_word, st);
         return pair ? launch_gemm_pair<true, false>(&a, error_word, st) : launch_gemm<true, false, false>(&a, error_word, st);
     }
     if (base == CBW_GEMM_DOWN_BF16) {
         if (x2) {
-            // the one-SM full form has no room for two token planes: pairs when the
-            // shape allows them, else the 32-token form
+            // the one-SM full form has no room for two token planes: token-major or
+            // pairs when the shape allows them, else the 32-token form
             if (tiles == CBW_GEMM_ONE_SM_TILES) return CBW_ERROR_INVALID_VALUE;
+            if (tm) return launch_gemm_tm<false, true>(&a, error_word, st);
             if (small || !pair_ok) return launch_gemm<false, true, true>(&a, error_word, st);
             return launch_gemm_pair<false, true>(&a, error_word, st);
         }
         if (small) return launch_gemm<false, true, false>(&a, error_word, st);
+        if (tm) return launch_gemm_tm<false, false>(&a, error_word, st);
         return pair ? launch_gemm_pair<false, false>(&a, error_word, st) : launch_gemm<false, false, false>(&a, error_word, st);
     }
     return CBW_ERROR_INVALID_VALUE;

@@ -525,7 +525,7 @@ moe_status_t moe_layer_get_act_planes(const moe_layer_t* L, int* planes) {
 moe_status_t moe_layer_set_gemm_form(moe_layer_t* L, int form) {
     if (!L) return MOE_ERR_INVALID_ARGUMENT;
     if (form != 0 && form != CBW_GEMM_SMALL_TILES && form != CBW_GEMM_FULL_TILES && form != CBW_GEMM_ONE_SM_TILES &&
-        form != CBW_GEMM_PAIR_TILES)
+        form != CBW_GEMM_PAIR_TILES && form != CBW_GEMM_TOKEN_TILES)
         return MOE_ERR_INVALID_ARGUMENT;
     L->gemm_form = form;
     return MOE_OK;

@@ -54,6 +54,7 @@ GEMM_SMALL_TILES = 0x10   # or-ed into a mode: the decode form (tiles of <= 32 r
 GEMM_FULL_TILES = 0x20
 GEMM_ONE_SM_TILES = 0x40  # the full form on one SM per tile
 GEMM_PAIR_TILES = 0x80    # the full form on pairs of SMs (tcgen05 cta_group::2)
+GEMM_TOKEN_TILES = 0x30   # the full form with 128 token rows x 256 weight rows per instruction
 GEMM_ACT_X2 = 0x100       # two-term e4m3 activations (hi plane, lo plane rows*K bytes on)
 
 _bound = False
