@@ -83,6 +83,22 @@ moe_status_t attn_decode_paged_rows(const void* q_bf16, const void* k_cache, con
                                     int max_splits, void* workspace, size_t workspace_bytes, void* out_bf16,
                                     void* out_q, float* out_s, int out_ld, int* error_word, cwStream_t stream);
 
+/* attn_decode_paged_rows with prefill rows first: rows [0, num_prefill_rows)
+ * -- prompt positions, normally runs of consecutive positions of one
+ * sequence (prefill chunks) -- are attended by a prefill kernel that stages
+ * each K/V page once for a block of 16 rows and all their query heads, each
+ * row over positions 0..positions[r] of its sequence with one online softmax
+ * over the pages in order, so a row's bits do not depend on the other rows of
+ * the call; rows [num_prefill_rows, B) (decode steps) by the split decode
+ * kernel.  Same arguments, outputs and checks as attn_decode_paged_rows;
+ * a row gets different last bits from the two kernels. */
+moe_status_t attn_paged_rows(const void* q_bf16, const void* k_cache, const void* v_cache, int num_cache_pages,
+                             const int32_t* page_table, int max_pages, const int32_t* row_seq, int num_seqs,
+                             const int32_t* seq_lens, int B, int num_prefill_rows, int nq, int nkv, int head_dim,
+                             int page_size, float scale, int split_tokens, int max_splits, void* workspace,
+                             size_t workspace_bytes, void* out_bf16, void* out_q, float* out_s, int out_ld,
+                             int* error_word, cwStream_t stream);
+
 /* out[t][i] = bf16(residual[t][i] + sum_{r < tp} partial_r[t][i]), the ranks
  * summed in fp32 in order 0..tp-1 so every rank gets the same bits.
  * partials_dev: device array of tp pointers (this GPU's buffers, or peer
@@ -189,6 +205,21 @@ moe_status_t attn_block_forward_partial(attn_block_t* block, const void* x_bf16,
                                         const int32_t* row_seq, int num_seqs, const int32_t* page_table,
                                         int num_cache_pages, void* k_cache, void* v_cache, void* partial_bf16,
                                         void* workspace, size_t workspace_bytes, cwStream_t stream);
+
+/* attn_block_forward with prompt rows first: rows [0, prefill_rows) are
+ * positions of prompts (prefill chunks) and are attended by the prefill
+ * kernel of attn_paged_rows, whose per-row result does not depend on how the
+ * prompts are packed into calls; rows [prefill_rows, R) by split decode.
+ * attn_block_forward is this call with prefill_rows = 0. */
+moe_status_t attn_block_prefill(attn_block_t* block, const void* x_bf16, int R, const int32_t* positions,
+                                const int32_t* row_seq, int num_seqs, int prefill_rows, const int32_t* page_table,
+                                int num_cache_pages, void* k_cache, void* v_cache, void* out_bf16, void* workspace,
+                                size_t workspace_bytes, cwStream_t stream);
+moe_status_t attn_block_prefill_partial(attn_block_t* block, const void* x_bf16, int R, const int32_t* positions,
+                                        const int32_t* row_seq, int num_seqs, int prefill_rows,
+                                        const int32_t* page_table, int num_cache_pages, void* k_cache, void* v_cache,
+                                        void* partial_bf16, void* workspace, size_t workspace_bytes,
+                                        cwStream_t stream);
 
 /* Reads and clears the device error word (synchronises `stream`):
  * MOE_ERR_DEVICE_TIMEOUT for a wait that gave up, MOE_ERR_INVALID_ARGUMENT for

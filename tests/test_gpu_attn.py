@@ -214,3 +214,134 @@ def test_small_gemm_matches_oracle(gpu, T, N, K):
     ref = O.gemm_fp8_block(aq, asc, wq.numpy(), ws.numpy())
     got = out.float().cpu().numpy()
     assert np.all(np.abs(got - ref) <= np.abs(ref) * 2 ** -7 + 1e-6), np.abs(got - ref).max()
+
+
+def _rows_case(rng, runs, nkv, gpu):
+    """runs: list of (first position, count) per sequence: the rows are each
+    sequence's positions in order, sequences one after the other.  Returns the
+    cache, page table, row arrays and the per-row (sequence, length)."""
+    lens = [p0 + n for p0, n in runs]
+    max_pages = max(-(-L // PS) for L in lens) + 1
+    num_pages = sum(-(-L // PS) for L in lens) + 3
+    kc, vc = make_cache(rng, num_pages, nkv, gpu)
+    pt = page_tables(rng, lens, num_pages, max_pages)
+    row_seq, row_len = [], []
+    for s, (p0, n) in enumerate(runs):
+        for i in range(n):
+            row_seq.append(s)
+            row_len.append(p0 + i + 1)
+    return kc, vc, pt, np.array(row_seq, dtype=np.int32), np.array(row_len, dtype=np.int32)
+
+
+@pytest.mark.parametrize("nq,nkv,runs,decode_rows", [
+    (12, 1, [(0, 40), (10, 23), (0, 1), (5, 2), (600, 3), (99, 1)], 1),
+    (8, 2, [(0, 300), (1000, 17), (31, 1)], 1),
+    (16, 1, [(0, 16), (16, 16), (0, 33)], 0),
+    (4, 4, [(3, 5), (0, 1), (7, 1)], 2),
+])
+def test_paged_rows_prefill_matches_oracle(gpu, nq, nkv, runs, decode_rows):
+    """attn_paged_rows: the prompt rows (all but the last `decode_rows`) go
+    through the prefill kernel (K/V pages staged once per 16-row block, runs
+    taken one after the other, single rows too), the rest through split
+    decode; every row against the float64 oracle over its own causal prefix,
+    against the all-decode path within the same bar, and its e4m3 row within
+    e4m3 precision of its bf16 row.  The decode rows are bit-identical to the
+    all-decode call."""
+    rng = np.random.default_rng(nq * 100 + nkv + len(runs))
+    kc, vc, pt, row_seq, row_len = _rows_case(rng, runs, nkv, gpu)
+    B = len(row_seq)
+    P = B - decode_rows
+    q = torch.from_numpy(rng.standard_normal((B, nq, D)).astype(np.float32)).to(torch.bfloat16).to(gpu)
+    scale = 1.0 / np.sqrt(D)
+    args = (q, kc, vc, torch.from_numpy(pt).to(gpu), torch.from_numpy(row_seq).to(gpu),
+            torch.from_numpy(row_len).to(gpu), nq, nkv, scale)
+    err = torch.zeros(1, dtype=torch.int32, device=gpu)
+    out, oq, os_ = A.paged_rows(*args, split_tokens=256, prefill_rows=P, quant=True, error_word=err)
+    dec, _, _ = A.paged_rows(*args, split_tokens=256)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    kf, vf, qf = bf16_np(kc), bf16_np(vc), bf16_np(q)
+    got, gdec = bf16_np(out), bf16_np(dec)
+    for r in range(B):
+        ref = O.attn_decode_paged(qf[r], kf, vf, pt[row_seq[r]], int(row_len[r]), scale)
+        check_close(got[r], ref)
+        check_close(gdec[r], ref)
+    assert np.array_equal(got[P:], gdec[P:])
+    lut = np.array([O.e4m3_decode(i) for i in range(256)], dtype=np.float32)
+    deq = lut[oq.cpu().numpy()].reshape(B, nq, D) * os_.cpu().numpy()[:, :B].T[:, :, None]
+    amax = np.abs(got).max(axis=2, keepdims=True)
+    assert np.all(np.abs(deq - got) <= amax / 16 + 1e-6)
+
+
+def test_paged_rows_prefill_packing_invariant(gpu):
+    """A prompt row's prefill result does not depend on the rows around it:
+    the same 37-position prompt alone in one call, in calls of 5 rows, and
+    after rows of another prompt give bit-identical rows."""
+    rng = np.random.default_rng(37)
+    kc, vc, pt, row_seq, row_len = _rows_case(rng, [(0, 37), (0, 9)], 1, gpu)
+    nq, scale = 12, 1.0 / np.sqrt(D)
+    q = torch.from_numpy(rng.standard_normal((len(row_seq), nq, D)).astype(np.float32)).to(torch.bfloat16).to(gpu)
+    ptd = torch.from_numpy(pt).to(gpu)
+
+    def run(rows):
+        idx = torch.tensor(rows, dtype=torch.int64)
+        out, _, _ = A.paged_rows(q[idx.to(gpu)].contiguous(), kc, vc, ptd, torch.from_numpy(row_seq[rows]).to(gpu),
+                                 torch.from_numpy(row_len[rows]).to(gpu), nq, 1, scale, split_tokens=256,
+                                 prefill_rows=len(rows))
+        return bf16_np(out)
+    alone = run(list(range(37)))
+    pieces = np.concatenate([run(list(range(i, min(i + 5, 37)))) for i in range(0, 37, 5)])
+    after = run(list(range(37, 46)) + list(range(37)))[9:]
+    torch.cuda.synchronize()
+    assert np.array_equal(alone, pieces)
+    assert np.array_equal(alone, after)
+
+
+def test_paged_rows_prefill_long_prompt_sampled(gpu):
+    """A 2048-token prompt as prefill rows (GLM rank shape: 12 query heads, 1
+    KV head) followed by a decode row; sampled rows against the oracle."""
+    rng = np.random.default_rng(2048)
+    kc, vc, pt, row_seq, row_len = _rows_case(rng, [(0, 2048), (4000, 1)], 1, gpu)
+    B, nq = len(row_seq), 12
+    q = torch.from_numpy(rng.standard_normal((B, nq, D)).astype(np.float32)).to(torch.bfloat16).to(gpu)
+    scale = 1.0 / np.sqrt(D)
+    out, _, _ = A.paged_rows(q, kc, vc, torch.from_numpy(pt).to(gpu), torch.from_numpy(row_seq).to(gpu),
+                             torch.from_numpy(row_len).to(gpu), nq, 1, scale, split_tokens=512, prefill_rows=2048)
+    torch.cuda.synchronize()
+    kf, vf, qf = bf16_np(kc), bf16_np(vc), bf16_np(q)
+    got = bf16_np(out)
+    for r in (0, 1, 15, 16, 17, 1000, 2047, 2048):
+        check_close(got[r], O.attn_decode_paged(qf[r], kf, vf, pt[row_seq[r]], int(row_len[r]), scale))
+
+
+def test_paged_rows_prefill_bounds_recorded(gpu):
+    """A prompt longer than its page table is cut there with error 5, and a
+    page id outside the cache reads as zeros with error 6, in the prefill
+    kernel as in the decode kernel; a row of a sequence outside the table
+    gets zeros."""
+    rng = np.random.default_rng(5)
+    kc, vc, pt, row_seq, row_len = _rows_case(rng, [(0, 20)], 1, gpu)
+    B, nq = len(row_seq), 4
+    q = torch.from_numpy(rng.standard_normal((B, nq, D)).astype(np.float32)).to(torch.bfloat16).to(gpu)
+    short = pt[:, :1].copy()                      # one page: positions 16.. are outside the table
+    err = torch.zeros(1, dtype=torch.int32, device=gpu)
+    A.paged_rows(q, kc, vc, torch.from_numpy(short).to(gpu), torch.from_numpy(row_seq).to(gpu),
+                 torch.from_numpy(row_len).to(gpu), nq, 1, 1.0 / np.sqrt(D), split_tokens=16, prefill_rows=B,
+                 error_word=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 5
+    bad = pt.copy()
+    bad[0, 1] = kc.shape[0] + 7
+    err.zero_()
+    A.paged_rows(q, kc, vc, torch.from_numpy(bad).to(gpu), torch.from_numpy(row_seq).to(gpu),
+                 torch.from_numpy(row_len).to(gpu), nq, 1, 1.0 / np.sqrt(D), split_tokens=256, prefill_rows=B,
+                 error_word=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 6
+    rs = row_seq.copy()
+    rs[3] = 9                                     # outside the one-row page table
+    out, _, _ = A.paged_rows(q, kc, vc, torch.from_numpy(pt).to(gpu), torch.from_numpy(rs).to(gpu),
+                             torch.from_numpy(row_len).to(gpu), nq, 1, 1.0 / np.sqrt(D), split_tokens=256,
+                             prefill_rows=B)
+    torch.cuda.synchronize()
+    assert (out[3].float() == 0).all()

@@ -44,6 +44,11 @@ def lib():
         k.attn_decode_paged.argtypes = [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_int,
                                         c_int, c_int, c_int, c_float, c_int, c_int, c_void_p, c_size_t, c_void_p,
                                         c_void_p, c_void_p, c_int, c_void_p, c_void_p]
+        rows_args = [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_int,
+                     c_int, c_int, c_int, c_float, c_int, c_int, c_void_p, c_size_t, c_void_p, c_void_p, c_void_p,
+                     c_int, c_void_p, c_void_p]
+        k.attn_decode_paged_rows.argtypes = rows_args
+        k.attn_paged_rows.argtypes = rows_args[:10] + [c_int] + rows_args[10:]
         k.attn_tp_reduce_residual.argtypes = [c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p]
         k.attn_block_create.argtypes = [ctypes.POINTER(BlockConfig), ctypes.POINTER(BlockWeights),
                                         ctypes.POINTER(c_void_p)]
@@ -114,6 +119,38 @@ def decode_paged(q, k_cache, v_cache, page_table, seq_lens, nq: int, nkv: int, s
         M.ptr(q), M.ptr(k_cache), M.ptr(v_cache), k_cache.shape[0], M.ptr(page_table), max_pages, M.ptr(seq_lens), B,
         nq, nkv, HEAD_DIM, PAGE, scale, split_tokens, max_splits, M.ptr(workspace), workspace.numel(), M.ptr(out),
         M.ptr(out_q), M.ptr(out_s), ld, M.ptr(error_word), M.stream_ptr(stream)))
+    return out, out_q, out_s
+
+
+def paged_rows(q, k_cache, v_cache, page_table, row_seq, seq_lens, nq: int, nkv: int, scale: float,
+               split_tokens: int = 2048, max_splits: int | None = None, prefill_rows: int | None = None,
+               quant: bool = False, error_word=None, stream=None):
+    """Attention over rows of several sequences (row r: page-table row row_seq[r], seq_lens[r] =
+    position + 1).  prefill_rows=P: attn_paged_rows (rows [0, P) through the prefill kernel, the rest
+    through split decode); None: attn_decode_paged_rows (split decode for all).
+    Returns (out bf16 [B][nq][128], out_q or None, out_s or None)."""
+    import torch
+    B = q.shape[0]
+    num_seqs, max_pages = page_table.shape
+    if max_splits is None:
+        max_splits = -(-max_pages * PAGE // split_tokens)
+    k = lib()
+    need = k.attn_decode_workspace_bytes(B, nq, max_splits)
+    workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=q.device)
+    out = torch.empty(B, nq, HEAD_DIM, dtype=torch.bfloat16, device=q.device)
+    out_q = out_s = None
+    ld = (B + 3) // 4 * 4
+    if quant:
+        out_q = torch.empty(B, nq * HEAD_DIM, dtype=torch.uint8, device=q.device)
+        out_s = torch.empty(nq, ld, dtype=torch.float32, device=q.device)
+    head = (M.ptr(q), M.ptr(k_cache), M.ptr(v_cache), k_cache.shape[0], M.ptr(page_table), max_pages,
+            M.ptr(row_seq), num_seqs, M.ptr(seq_lens), B)
+    tail = (nq, nkv, HEAD_DIM, PAGE, scale, split_tokens, max_splits, M.ptr(workspace), workspace.numel(),
+            M.ptr(out), M.ptr(out_q), M.ptr(out_s), ld, M.ptr(error_word), M.stream_ptr(stream))
+    if prefill_rows is None:
+        M.check("attn_decode_paged_rows", k.attn_decode_paged_rows(*head, *tail))
+    else:
+        M.check("attn_paged_rows", k.attn_paged_rows(*head, prefill_rows, *tail))
     return out, out_q, out_s
 
 

@@ -142,8 +142,16 @@ struct DecodeParams {
     float* part_ml;                // [B*nkv][max_splits][G][2]  (max in log2 units, sum)
     int* error_word;
     int nq, nkv, G, max_pages, num_cache_pages, split_tokens, max_splits, num_seqs;
+    int first_row;                 // rows below it belong to the prefill kernel
     float scale_log2;              // softmax scale * log2(e)
 };
+
+// Row b continues row a: the same sequence, one position later (seq_lens
+// holds position + 1, 0 for a row the page write skipped).
+__device__ __forceinline__ bool row_follows(const int32_t* row_seq, const int32_t* lens, int num_seqs, int a, int b) {
+    const int sa = seq_of_row(row_seq, a, num_seqs), sb = seq_of_row(row_seq, b, num_seqs);
+    return sa >= 0 && sa == sb && lens[a] > 0 && lens[b] == lens[a] + 1;
+}
 
 // Tokens attended for sequence b: its length, cut to what the page table and
 // the split partials can hold (a longer one records error 5).
@@ -167,6 +175,7 @@ decode_split_kernel(const DecodeParams p) {
     const int b = bk / p.nkv, kvh = bk % p.nkv;
     const int seq = seq_of_row(p.row_seq, b, p.num_seqs);
     if (seq < 0) return;                       // recorded (7) by the page write; the merge writes zeros
+    if (b < p.first_row) return;               // a prefill row
     const int len_in = p.seq_lens[b];
     const int len = clamp_len(len_in, p.max_pages, p.split_tokens, p.max_splits);
     if (len != len_in && split == 0 && threadIdx.x == 0 && kvh == 0 && p.error_word) atomicExch(p.error_word, 5);
@@ -367,8 +376,9 @@ decode_merge_kernel(const float* __restrict__ part_o, const float* __restrict__ 
                     const int32_t* __restrict__ seq_lens, const int32_t* __restrict__ row_seq, int num_seqs, int nq,
                     int nkv, int G, int max_pages, int split_tokens, int max_splits,
                     __nv_bfloat16* __restrict__ out, uint8_t* __restrict__ out_q, float* __restrict__ out_s,
-                    int out_ld) {
+                    int out_ld, int first_row) {
     const int b = blockIdx.x / nq, h = blockIdx.x % nq;
+    if (b < first_row) return;                 // a prefill row
     const int kvh = h / G, r = h % G;
     const int d = threadIdx.x;
     const int len = seq_of_row(row_seq, b, num_seqs) < 0 ? 0 : clamp_len(seq_lens[b], max_pages, split_tokens, max_splits);
@@ -400,6 +410,234 @@ decode_merge_kernel(const float* __restrict__ part_o, const float* __restrict__ 
         }
         out_q[static_cast<size_t>(b) * nq * kD + h * kD + d] = qv;
         if (d == 0) out_s[static_cast<size_t>(h) * out_ld + b] = amax > 0.0f ? amax / 448.0f : 0.0f;
+    }
+}
+
+// ---------------------------------------------------------------- prefill rows
+//
+// The first rows of a call (prompt positions of prefill chunks) are attended
+// by one CTA per (16-row block, kv head): a block's runs of consecutive
+// positions of one sequence are taken one after the other, each run's
+// (position, query head) rows -- up to 16 x 16 -- being the M rows of 16-row
+// mma.sync tiles, one warp each, while every 16-token K/V page of the
+// sequence up to the run's last position is staged once in shared memory for
+// all of them (the decode kernel streams the prefix again for every row).
+// Each row keeps one fp32 online softmax over the pages in order 0, 1, ...
+// with the causal limit of its own position, and a page past that limit
+// leaves it unchanged, so a row's result does not depend on which rows share
+// its block or its call: prompts give the same bits whichever way they are
+// packed into forwards.  The remaining rows (decode steps) stay with the split
+// decode kernel.
+constexpr int kPfRows = 16;                  // positions per CTA block
+constexpr int kPfWarps = 16;                 // one 16-row tile of (position, head) rows each
+constexpr int kPfNst = 4;                    // K/V pages in flight
+constexpr size_t kPfSmem = (static_cast<size_t>(kPfRows) * kGPad * kRowPad + kPfNst * 2 * kPage * kRowPad) * 2;
+static_assert(kPfWarps * 32 == 2 * kPage * (kD / 8), "one 16-byte chunk of a page per thread");
+
+struct PrefillParams {
+    const __nv_bfloat16* q;        // [B][nq][128]
+    const __nv_bfloat16* k_cache;  // [pages][16][nkv][128]
+    const __nv_bfloat16* v_cache;
+    const int32_t* page_table;     // [num_seqs][max_pages]
+    const int32_t* row_seq;        // [B]
+    const int32_t* seq_lens;       // [B]: position + 1
+    __nv_bfloat16* out;            // [B][nq][128]
+    uint8_t* out_q;                // [B][nq * 128] e4m3 or null
+    float* out_s;                  // [nq][out_ld]
+    int* error_word;
+    int B;                         // prefill rows: [0, B) of the call
+    int nq, nkv, G, max_pages, num_cache_pages, num_seqs, out_ld;
+    float scale_log2;
+};
+
+__global__ void __launch_bounds__(kPfWarps * 32, 1)
+prefill_rows_kernel(const PrefillParams p) {
+    extern __shared__ __align__(128) __nv_bfloat16 sm[];
+    __nv_bfloat16* q_s = sm;                                   // [256][kRowPad]
+    __nv_bfloat16* ring = sm + kPfRows * kGPad * kRowPad;      // [kPfNst][K 16 | V 16][kRowPad]
+    const int blk0 = blockIdx.x * kPfRows, kvh = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, tq = lane & 3;
+    const int rend = min(blk0 + kPfRows, p.B);
+    const int cap = p.max_pages * kPage;
+    const size_t row_stride = static_cast<size_t>(p.nkv) * kD;
+    int r = blk0;
+    while (r < rend) {
+        if (seq_of_row(p.row_seq, r, p.num_seqs) < 0 || p.seq_lens[r] <= 0) {
+            // a row the page write skipped (error 7 recorded there): zeros, as the decode merge writes
+            for (int c = threadIdx.x; c < p.G * kD; c += blockDim.x) {
+                const int head = kvh * p.G + c / kD, d = c % kD;
+                p.out[(static_cast<size_t>(r) * p.nq + head) * kD + d] = __float2bfloat16_rn(0.0f);
+                if (p.out_q) {
+                    p.out_q[static_cast<size_t>(r) * p.nq * kD + head * kD + d] = 0;
+                    if (d == 0) p.out_s[static_cast<size_t>(head) * p.out_ld + r] = 0.0f;
+                }
+            }
+            ++r;
+            continue;
+        }
+        int n = 1;
+        while (r + n < rend && row_follows(p.row_seq, p.seq_lens, p.num_seqs, r + n - 1, r + n)) ++n;
+        const int seq = seq_of_row(p.row_seq, r, p.num_seqs);
+        const int last_in = p.seq_lens[r + n - 1];
+        if (last_in > cap && threadIdx.x == 0 && kvh == 0 && p.error_word) atomicExch(p.error_word, 5);
+        const int npages = (min(last_in, cap) + kPage - 1) / kPage;
+        const int rows = n * p.G;                              // (position, head) rows, position-major
+        const int ntiles = (rows + 15) / 16;
+        __syncthreads();                                       // the previous run's shared memory is free
+        for (int c = threadIdx.x; c < kPfRows * kGPad * (kD / 8); c += blockDim.x) {
+            const int i = c / (kD / 8), q8 = c % (kD / 8);
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (i < rows)
+                v = *reinterpret_cast<const uint4*>(
+                    p.q + (static_cast<size_t>(r + i / p.G) * p.nq + kvh * p.G + i % p.G) * kD + q8 * 8);
+            *reinterpret_cast<uint4*>(q_s + i * kRowPad + q8 * 8) = v;
+        }
+        // tokens each of this thread's two rows attends (padding rows: token 0 only, never stored)
+        int len_r[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int i = warp * 16 + g + 8 * h;
+            len_r[h] = i < rows ? min(p.seq_lens[r + i / p.G], cap) : 1;
+        }
+        auto load_page = [&](int pg, int stage) {
+            int phys = p.page_table[static_cast<size_t>(seq) * p.max_pages + pg];
+            const bool ok = phys >= 0 && phys < p.num_cache_pages;
+            if (!ok && threadIdx.x == 0 && p.error_word) atomicExch(p.error_word, 6);
+            phys = ok ? phys : 0;
+            const int t = threadIdx.x, which = t >> 8, rr = (t >> 4) & 15, q8 = t & 15;
+            const __nv_bfloat16* src =
+                (which ? p.v_cache : p.k_cache) + (static_cast<size_t>(phys) * kPage + rr) * row_stride + kvh * kD + q8 * 8;
+            cp_async16(ring + (static_cast<size_t>(stage) * 2 * kPage + which * kPage + rr) * kRowPad + q8 * 8, src,
+                       ok ? 16u : 0u);
+        };
+#pragma unroll
+        for (int st = 0; st < kPfNst - 1; ++st) {
+            if (st < npages) load_page(st, st);
+            cp_async_commit();
+        }
+        __syncthreads();                                       // q_s written
+        uint32_t qa[kD / 16][4];
+        {
+            const int mi = lane >> 3, rr = (lane & 7) + 8 * (mi & 1);
+#pragma unroll
+            for (int ks = 0; ks < kD / 16; ++ks)
+                ldsm_x4(smem_u32(q_s + (warp * 16 + rr) * kRowPad + ks * 16 + 8 * (mi >> 1)), qa[ks][0], qa[ks][1],
+                        qa[ks][2], qa[ks][3]);
+        }
+        float o[kD / 8][4];
+#pragma unroll
+        for (int i = 0; i < kD / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
+        float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.0f, 0.0f};
+        const bool active = warp < ntiles;
+        for (int i = 0; i < npages; ++i) {
+            cp_async_wait<kPfNst - 2>();
+            __syncthreads();                                   // page i landed; page i - 1's stage is free
+            if (i + kPfNst - 1 < npages) load_page(i + kPfNst - 1, (i + kPfNst - 1) % kPfNst);
+            cp_async_commit();
+            if (!active) continue;
+            const __nv_bfloat16* ks_ = ring + (i % kPfNst) * 2 * kPage * kRowPad;
+            const __nv_bfloat16* vs_ = ks_ + kPage * kRowPad;
+            float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+            {
+                const int mi = lane >> 3, rr = (lane & 7) + 8 * (mi >> 1), cofs = 8 * (mi & 1);
+#pragma unroll
+                for (int ks = 0; ks < kD / 16; ++ks) {
+                    uint32_t b0, b1, b2, b3;
+                    ldsm_x4(smem_u32(ks_ + rr * kRowPad + ks * 16 + cofs), b0, b1, b2, b3);
+                    mma_bf16(s0, qa[ks], b0, b1);
+                    mma_bf16(s1, qa[ks], b2, b3);
+                }
+            }
+            const int tok = i * kPage;
+            const int c0 = 2 * tq;
+            float sv[2][4];
+            sv[0][0] = s0[0]; sv[0][1] = s0[1]; sv[0][2] = s1[0]; sv[0][3] = s1[1];
+            sv[1][0] = s0[2]; sv[1][1] = s0[3]; sv[1][2] = s1[2]; sv[1][3] = s1[3];
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int t = tok + c0 + (j & 1) + 8 * (j >> 1);
+                    sv[h][j] = t < len_r[h] ? sv[h][j] * p.scale_log2 : -INFINITY;
+                }
+            float alpha[2];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                float mx = fmaxf(fmaxf(sv[h][0], sv[h][1]), fmaxf(sv[h][2], sv[h][3]));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+                // finite: page 0 holds token 0, which every row attends
+                const float mn = fmaxf(m_r[h], mx);
+                alpha[h] = exp2f(m_r[h] - mn);
+                m_r[h] = mn;
+                float rs = 0.0f;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    sv[h][j] = exp2f(sv[h][j] - mn);
+                    rs += sv[h][j];
+                }
+                l_r[h] = l_r[h] * alpha[h] + rs;
+            }
+            if (alpha[0] != 1.0f || alpha[1] != 1.0f) {
+#pragma unroll
+                for (int nd = 0; nd < kD / 8; ++nd) {
+                    o[nd][0] *= alpha[0]; o[nd][1] *= alpha[0];
+                    o[nd][2] *= alpha[1]; o[nd][3] *= alpha[1];
+                }
+            }
+            uint32_t pa[4];
+            pa[0] = pack_bf16(sv[0][0], sv[0][1]);
+            pa[1] = pack_bf16(sv[1][0], sv[1][1]);
+            pa[2] = pack_bf16(sv[0][2], sv[0][3]);
+            pa[3] = pack_bf16(sv[1][2], sv[1][3]);
+            {
+                const int mi = lane >> 3, rr = (lane & 7) + 8 * (mi & 1), cofs = 8 * (mi >> 1);
+#pragma unroll
+                for (int nd = 0; nd < kD / 8; nd += 2) {
+                    uint32_t b0, b1, b2, b3;
+                    ldsm_x4_t(smem_u32(vs_ + rr * kRowPad + nd * 8 + cofs), b0, b1, b2, b3);
+                    mma_bf16(o[nd], pa, b0, b1);
+                    mma_bf16(o[nd + 1], pa, b2, b3);
+                }
+            }
+        }
+        cp_async_wait<0>();
+        if (active) {
+            // normalise; bf16 rows and the e4m3 1x128 quantisation of each (position, head) row
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                float l = l_r[h];
+                l += __shfl_xor_sync(0xffffffffu, l, 1);
+                l += __shfl_xor_sync(0xffffffffu, l, 2);
+                float amax = 0.0f;
+#pragma unroll
+                for (int nd = 0; nd < kD / 8; ++nd) {
+                    o[nd][2 * h] = o[nd][2 * h] / l;
+                    o[nd][2 * h + 1] = o[nd][2 * h + 1] / l;
+                    amax = fmaxf(amax, fmaxf(fabsf(o[nd][2 * h]), fabsf(o[nd][2 * h + 1])));
+                }
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+                const int i = warp * 16 + g + 8 * h;
+                if (i >= rows) continue;
+                const size_t row = static_cast<size_t>(r + i / p.G);
+                const int head = kvh * p.G + i % p.G;
+                __nv_bfloat16* orow = p.out + (row * p.nq + head) * kD;
+                const float inv = amax > 0.0f ? 448.0f / amax : 0.0f;
+#pragma unroll
+                for (int nd = 0; nd < kD / 8; ++nd) {
+                    const int col = nd * 8 + 2 * tq;
+                    *reinterpret_cast<uint32_t*>(orow + col) = pack_bf16(o[nd][2 * h], o[nd][2 * h + 1]);
+                    if (p.out_q) {
+                        const uint16_t qv = amax > 0.0f ? cvt_e4m3x2(o[nd][2 * h] * inv, o[nd][2 * h + 1] * inv) : 0;
+                        *reinterpret_cast<uint16_t*>(p.out_q + row * p.nq * kD + head * kD + col) = qv;
+                    }
+                }
+                if (p.out_q && tq == 0) p.out_s[static_cast<size_t>(head) * p.out_ld + row] = amax > 0.0f ? amax / 448.0f : 0.0f;
+            }
+        }
+        r += n;
     }
 }
 
@@ -472,12 +710,17 @@ size_t attn_decode_workspace_bytes(int B, int nq, int max_splits) {
     return static_cast<size_t>(B) * nq * max_splits * (kD + 2) * sizeof(float);
 }
 
-moe_status_t attn_decode_paged_rows(const void* q_bf16, const void* k_cache, const void* v_cache,
-                                    int num_cache_pages, const int32_t* page_table, int max_pages,
-                                    const int32_t* row_seq, int num_seqs, const int32_t* seq_lens, int B, int nq,
-                                    int nkv, int head_dim, int page_size, float scale, int split_tokens,
-                                    int max_splits, void* workspace, size_t workspace_bytes, void* out_bf16,
-                                    void* out_q, float* out_s, int out_ld, int* error_word, cwStream_t stream) {
+}  // extern "C"
+
+namespace {
+
+// Split decode over the rows of a call; rows below first_row are left to the
+// prefill kernel.
+moe_status_t decode_rows(const void* q_bf16, const void* k_cache, const void* v_cache, int num_cache_pages,
+                         const int32_t* page_table, int max_pages, const int32_t* row_seq, int num_seqs,
+                         const int32_t* seq_lens, int B, int nq, int nkv, int head_dim, int page_size, float scale,
+                         int split_tokens, int max_splits, void* workspace, size_t workspace_bytes, void* out_bf16,
+                         void* out_q, float* out_s, int out_ld, int* error_word, cudaStream_t st, int first_row) {
     if (num_seqs <= 0) return MOE_ERR_INVALID_ARGUMENT;
     if (B < 0 || nq <= 0 || nkv <= 0 || nq % nkv || nq / nkv > kGPad || head_dim != kD || page_size != kPage)
         return MOE_ERR_INVALID_ARGUMENT;
@@ -513,14 +756,68 @@ moe_status_t attn_decode_paged_rows(const void* q_bf16, const void* k_cache, con
     p.split_tokens = split_tokens;
     p.max_splits = max_splits;
     p.scale_log2 = scale * kLog2e;
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    p.first_row = first_row;
+    if (first_row >= B) return MOE_OK;
     decode_split_kernel<<<dim3(max_splits, B * nkv), kWarps * 32, kDecodeSmem, st>>>(p);
     moe_status_t s = launch_status();
     if (s != MOE_OK) return s;
     decode_merge_kernel<<<B * nq, kD, 0, st>>>(p.part_o, p.part_ml, seq_lens, row_seq, num_seqs, nq, nkv, p.G,
                                               max_pages, split_tokens, max_splits,
                                               static_cast<__nv_bfloat16*>(out_bf16), static_cast<uint8_t*>(out_q),
-                                              out_s, out_ld);
+                                              out_s, out_ld, first_row);
+    return launch_status();
+}
+
+}  // namespace
+
+extern "C" {
+
+moe_status_t attn_decode_paged_rows(const void* q_bf16, const void* k_cache, const void* v_cache,
+                                    int num_cache_pages, const int32_t* page_table, int max_pages,
+                                    const int32_t* row_seq, int num_seqs, const int32_t* seq_lens, int B, int nq,
+                                    int nkv, int head_dim, int page_size, float scale, int split_tokens,
+                                    int max_splits, void* workspace, size_t workspace_bytes, void* out_bf16,
+                                    void* out_q, float* out_s, int out_ld, int* error_word, cwStream_t stream) {
+    return decode_rows(q_bf16, k_cache, v_cache, num_cache_pages, page_table, max_pages, row_seq, num_seqs, seq_lens,
+                       B, nq, nkv, head_dim, page_size, scale, split_tokens, max_splits, workspace, workspace_bytes,
+                       out_bf16, out_q, out_s, out_ld, error_word, static_cast<cudaStream_t>(stream), 0);
+}
+
+moe_status_t attn_paged_rows(const void* q_bf16, const void* k_cache, const void* v_cache, int num_cache_pages,
+                             const int32_t* page_table, int max_pages, const int32_t* row_seq, int num_seqs,
+                             const int32_t* seq_lens, int B, int num_prefill_rows, int nq, int nkv, int head_dim,
+                             int page_size, float scale, int split_tokens, int max_splits, void* workspace,
+                             size_t workspace_bytes, void* out_bf16, void* out_q, float* out_s, int out_ld,
+                             int* error_word, cwStream_t stream) {
+    if (num_prefill_rows < 0 || num_prefill_rows > B) return MOE_ERR_INVALID_ARGUMENT;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    moe_status_t s = decode_rows(q_bf16, k_cache, v_cache, num_cache_pages, page_table, max_pages, row_seq, num_seqs,
+                                 seq_lens, B, nq, nkv, head_dim, page_size, scale, split_tokens, max_splits, workspace,
+                                 workspace_bytes, out_bf16, out_q, out_s, out_ld, error_word, st, num_prefill_rows);
+    if (s != MOE_OK || num_prefill_rows == 0) return s;
+    static bool attr[kMaxDevices] = {};
+    if (smem_optin_once(prefill_rows_kernel, static_cast<int>(kPfSmem), attr) != cudaSuccess) return MOE_ERR_CUDA;
+    PrefillParams p;
+    p.q = static_cast<const __nv_bfloat16*>(q_bf16);
+    p.k_cache = static_cast<const __nv_bfloat16*>(k_cache);
+    p.v_cache = static_cast<const __nv_bfloat16*>(v_cache);
+    p.page_table = page_table;
+    p.row_seq = row_seq;
+    p.seq_lens = seq_lens;
+    p.out = static_cast<__nv_bfloat16*>(out_bf16);
+    p.out_q = static_cast<uint8_t*>(out_q);
+    p.out_s = out_s;
+    p.error_word = error_word;
+    p.B = num_prefill_rows;
+    p.nq = nq;
+    p.nkv = nkv;
+    p.G = nq / nkv;
+    p.max_pages = max_pages;
+    p.num_cache_pages = num_cache_pages;
+    p.num_seqs = num_seqs;
+    p.out_ld = out_ld;
+    p.scale_log2 = scale * kLog2e;
+    prefill_rows_kernel<<<dim3((num_prefill_rows + kPfRows - 1) / kPfRows, nkv), kPfWarps * 32, kPfSmem, st>>>(p);
     return launch_status();
 }
 

@@ -286,8 +286,8 @@ int split_for_rows(const attn_block* L, int B, int* max_splits) {
 
 // Steps 1-5: the rank's o_proj partial (bf16 [B][H]) into `partial`.
 moe_status_t run_partial(attn_block* L, const void* x, int B, const int32_t* positions, const int32_t* row_seq,
-                         int num_seqs, const int32_t* page_table, int num_cache_pages, void* k_cache, void* v_cache,
-                         void* partial, void* ws, cudaStream_t st) {
+                         int num_seqs, int prefill_rows, const int32_t* page_table, int num_cache_pages, void* k_cache,
+                         void* v_cache, void* partial, void* ws, cudaStream_t st) {
     const attn_block_config_t& c = L->cfg;
     const int H = c.hidden, nq = c.num_q_heads, nkv = c.num_kv_heads;
     ATT_TRY(moe_rmsnorm_quant(x, L->w.gamma, B, H, c.eps, at<float>(ws, L->off_rms), at<void>(ws, L->off_xq),
@@ -304,8 +304,9 @@ moe_status_t run_partial(attn_block* L, const void* x, int B, const int32_t* pos
                                     L->error_word, st));
     int max_splits = 0;
     const int split = split_for_rows(L, B, &max_splits);
-    ATT_TRY(attn_decode_paged_rows(at<void>(ws, L->off_q), k_cache, v_cache, num_cache_pages, page_table,
-                                   c.max_pages_per_seq, row_seq, num_seqs, at<int32_t>(ws, L->off_lens), B, nq, nkv,
+    ATT_TRY(attn_paged_rows(at<void>(ws, L->off_q), k_cache, v_cache, num_cache_pages, page_table,
+                                   c.max_pages_per_seq, row_seq, num_seqs, at<int32_t>(ws, L->off_lens), B,
+                                   prefill_rows, nq, nkv,
                                    kD, 16, 1.0f / std::sqrt(static_cast<float>(kD)), split, max_splits,
                                    at<void>(ws, L->off_dec), L->dec_bytes, at<void>(ws, L->off_out),
                                    at<void>(ws, L->off_aq), at<float>(ws, L->off_as), L->ld, L->error_word, st));
@@ -397,17 +398,27 @@ moe_status_t attn_block_set_peer_buffers(attn_block_t* L, void* const* bufs, int
     return MOE_OK;
 }
 
-moe_status_t attn_block_forward_partial(attn_block_t* L, const void* x_bf16, int B, const int32_t* positions,
-                                        const int32_t* row_seq, int num_seqs, const int32_t* page_table,
-                                        int num_cache_pages, void* k_cache, void* v_cache, void* partial_bf16,
-                                        void* workspace, size_t workspace_bytes, cwStream_t stream) {
+moe_status_t attn_block_prefill_partial(attn_block_t* L, const void* x_bf16, int B, const int32_t* positions,
+                                        const int32_t* row_seq, int num_seqs, int prefill_rows,
+                                        const int32_t* page_table, int num_cache_pages, void* k_cache, void* v_cache,
+                                        void* partial_bf16, void* workspace, size_t workspace_bytes,
+                                        cwStream_t stream) {
     if (!L || B < 0 || B > L->cfg.max_batch || num_seqs <= 0) return MOE_ERR_INVALID_ARGUMENT;
+    if (prefill_rows < 0 || prefill_rows > B) return MOE_ERR_INVALID_ARGUMENT;
     if (B == 0) return MOE_OK;
     if (!x_bf16 || !positions || !page_table || !k_cache || !v_cache || !partial_bf16 || !workspace)
         return MOE_ERR_INVALID_ARGUMENT;
     if (workspace_bytes < L->bytes) return MOE_ERR_WORKSPACE;
-    return run_partial(L, x_bf16, B, positions, row_seq, num_seqs, page_table, num_cache_pages, k_cache, v_cache,
-                       partial_bf16, workspace, static_cast<cudaStream_t>(stream));
+    return run_partial(L, x_bf16, B, positions, row_seq, num_seqs, prefill_rows, page_table, num_cache_pages, k_cache,
+                       v_cache, partial_bf16, workspace, static_cast<cudaStream_t>(stream));
+}
+
+moe_status_t attn_block_forward_partial(attn_block_t* L, const void* x_bf16, int B, const int32_t* positions,
+                                        const int32_t* row_seq, int num_seqs, const int32_t* page_table,
+                                        int num_cache_pages, void* k_cache, void* v_cache, void* partial_bf16,
+                                        void* workspace, size_t workspace_bytes, cwStream_t stream) {
+    return attn_block_prefill_partial(L, x_bf16, B, positions, row_seq, num_seqs, 0, page_table, num_cache_pages,
+                                      k_cache, v_cache, partial_bf16, workspace, workspace_bytes, stream);
 }
 
 moe_status_t attn_block_decode_partial(attn_block_t* L, const void* x_bf16, int B, const int32_t* positions,
@@ -417,11 +428,12 @@ moe_status_t attn_block_decode_partial(attn_block_t* L, const void* x_bf16, int 
                                       k_cache, v_cache, partial_bf16, workspace, workspace_bytes, stream);
 }
 
-moe_status_t attn_block_forward(attn_block_t* L, const void* x_bf16, int B, const int32_t* positions,
-                                const int32_t* row_seq, int num_seqs, const int32_t* page_table, int num_cache_pages,
-                                void* k_cache, void* v_cache, void* out_bf16, void* workspace, size_t workspace_bytes,
-                                cwStream_t stream) {
+moe_status_t attn_block_prefill(attn_block_t* L, const void* x_bf16, int B, const int32_t* positions,
+                                const int32_t* row_seq, int num_seqs, int prefill_rows, const int32_t* page_table,
+                                int num_cache_pages, void* k_cache, void* v_cache, void* out_bf16, void* workspace,
+                                size_t workspace_bytes, cwStream_t stream) {
     if (!L || B < 0 || B > L->cfg.max_batch || num_seqs <= 0) return MOE_ERR_INVALID_ARGUMENT;
+    if (prefill_rows < 0 || prefill_rows > B) return MOE_ERR_INVALID_ARGUMENT;
     if (!x_bf16 || !positions || !page_table || !k_cache || !v_cache || !out_bf16 || !workspace)
         return MOE_ERR_INVALID_ARGUMENT;
     if (workspace_bytes < L->bytes) return MOE_ERR_WORKSPACE;
@@ -432,8 +444,8 @@ moe_status_t attn_block_forward(attn_block_t* L, const void* x_bf16, int B, cons
     if (L->cfg.tp_size == 1) {
         if (B == 0) return MOE_OK;
         void* part = at<void>(workspace, L->off_part);
-        ATT_TRY(run_partial(L, x_bf16, B, positions, row_seq, num_seqs, page_table, num_cache_pages, k_cache, v_cache,
-                            part, workspace, st));
+        ATT_TRY(run_partial(L, x_bf16, B, positions, row_seq, num_seqs, prefill_rows, page_table, num_cache_pages,
+                            k_cache, v_cache, part, workspace, st));
         residual_add_kernel<<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(part),
                                                     static_cast<const __nv_bfloat16*>(x_bf16), n,
                                                     static_cast<__nv_bfloat16*>(out_bf16));
@@ -444,8 +456,8 @@ moe_status_t attn_block_forward(attn_block_t* L, const void* x_bf16, int B, cons
     tp_wait_done_kernel<<<1, 32, 0, st>>>(L->peers, L->epoch_dev, L->timeout_ns, L->error_word);
     ATT_TRY(launch_status());
     if (B > 0)
-        ATT_TRY(run_partial(L, x_bf16, B, positions, row_seq, num_seqs, page_table, num_cache_pages, k_cache, v_cache,
-                            part, workspace, st));
+        ATT_TRY(run_partial(L, x_bf16, B, positions, row_seq, num_seqs, prefill_rows, page_table, num_cache_pages,
+                            k_cache, v_cache, part, workspace, st));
     tp_signal_kernel<<<1, 32, 0, st>>>(L->peers, L->epoch_dev);
     ATT_TRY(launch_status());
     if (B > 0) {
@@ -456,6 +468,14 @@ moe_status_t attn_block_forward(attn_block_t* L, const void* x_bf16, int B, cons
     }
     tp_done_kernel<<<1, 32, 0, st>>>(L->peers, L->epoch_dev);
     return launch_status();
+}
+
+moe_status_t attn_block_forward(attn_block_t* L, const void* x_bf16, int B, const int32_t* positions,
+                                const int32_t* row_seq, int num_seqs, const int32_t* page_table, int num_cache_pages,
+                                void* k_cache, void* v_cache, void* out_bf16, void* workspace, size_t workspace_bytes,
+                                cwStream_t stream) {
+    return attn_block_prefill(L, x_bf16, B, positions, row_seq, num_seqs, 0, page_table, num_cache_pages, k_cache,
+                              v_cache, out_bf16, workspace, workspace_bytes, stream);
 }
 
 moe_status_t attn_block_decode(attn_block_t* L, const void* x_bf16, int B, const int32_t* positions,

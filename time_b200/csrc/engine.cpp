@@ -16,8 +16,9 @@
 //   stage (pinned)   token, position, page-table row of every row, and seed,
 //                    temperature, top_p of every sampled row -> one copy
 //   embed            bf16 rows
-//   per layer        attn_block_forward (RoPE + K/V page write + paged decode
-//                    attention + o_proj + residual), then the FFN: moe_layer_forward
+//   per layer        attn_block_prefill (RoPE + K/V page write; prompt rows
+//                    through the prefill attention kernel, sampled rows through
+//                    split decode; o_proj + residual), then the FFN: moe_layer_forward
 //                    (routed experts + shared expert + residual) or, for the
 //                    first dense layers, the same layer with one expert
 //   final norm       bf16, the sampled rows only
@@ -383,7 +384,8 @@ moe_status_t forward(glm_engine* E, int R, int head) {
     for (size_t l = 0; l < E->layers.size(); ++l) {
         Layer& L = E->layers[l];
         if (tm) cudaEventRecord(E->events[1 + 2 * l], st);
-        ENG_TRY(attn_block_forward(L.attn, E->x0, R, pos, row_seq, c.max_batch, E->page_table, E->num_pages,
+        // rows [0, R - head) are prompt positions (the prefill kernel), the last `head` the sampled rows
+        ENG_TRY(attn_block_prefill(L.attn, E->x0, R, pos, row_seq, c.max_batch, R - head, E->page_table, E->num_pages,
                                    L.k_cache, L.v_cache, E->x1, E->ws, E->ws_bytes, st));
         if (tm) cudaEventRecord(E->events[2 + 2 * l], st);
         if (L.dense)
