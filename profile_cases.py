@@ -8,6 +8,7 @@ hundred MB on the device, a handful of launches):
     python profile_cases.py attention [--batch 64] [--ctx-min 1024] [--ctx-max 32768] [--iters 3]
     python profile_cases.py attn_block [--batch 64] [--ctx-min 1024] [--ctx-max 32768] [--iters 3]
     python profile_cases.py serving [--batch 64] [--prompt 512] [--steps 10] [--layers 92]
+    python profile_cases.py prefill [--prompts 1] [--prompt 2048] [--iters 3]
 
 `router`: RMSNorm+quant (with the fp32 n rows), the router logits, top-k
 over T tokens of the GLM shape (hidden 5120, 160 experts; n is 84 MB at 4096
@@ -31,6 +32,9 @@ every layer has its own KV pages.  Reports prefill tokens/s (the first step,
 which runs every admitted prompt in forwards of up to 2048 rows), decode
 tokens/s (wall time of the synchronous engine calls) and the engine's
 per-stage device times of one decode step.
+`prefill`: attention of prompt rows at that rank shape -- `prompts` prompts
+of `prompt` positions in one call -- through the prefill kernel of
+attn_paged_rows and, for comparison, through split decode.
 Prints one line per stage with the mean CUDA-event time per launch.
 """
 from __future__ import annotations
@@ -216,6 +220,42 @@ def attention(batch: int, ctx_min: int, ctx_max: int, split: int, iters: int, nq
     return out
 
 
+def prefill(prompts: int, prompt_len: int, iters: int, nq: int = 12, nkv: int = 1) -> dict:
+    """Attention of prefill rows (config-5 rank shape: 12 query heads, 1 KV
+    head): `prompts` prompts of `prompt_len` positions, all rows in one call,
+    through attn_paged_rows's prefill kernel and, for comparison, through the
+    split decode kernel (every row streams its own prefix)."""
+    import numpy as np
+    from time_b200 import attn as A
+    dev = torch.device("cuda", 0)
+    rng = np.random.default_rng(0)
+    pages = (prompt_len + A.PAGE - 1) // A.PAGE
+    num_pages = prompts * pages
+    pt = rng.permutation(num_pages).astype(np.int32).reshape(prompts, pages)
+    g = torch.Generator(device=dev).manual_seed(1)
+    kc = torch.randn(num_pages, A.PAGE, nkv, A.HEAD_DIM, generator=g, device=dev).to(torch.bfloat16)
+    vc = torch.randn(num_pages, A.PAGE, nkv, A.HEAD_DIM, generator=g, device=dev).to(torch.bfloat16)
+    R = prompts * prompt_len
+    q = torch.randn(R, nq, A.HEAD_DIM, generator=g, device=dev).to(torch.bfloat16)
+    row_seq = torch.arange(prompts, dtype=torch.int32, device=dev).repeat_interleave(prompt_len)
+    lens = (torch.arange(prompt_len, dtype=torch.int32, device=dev) + 1).repeat(prompts)
+    pt_d = torch.from_numpy(pt).to(dev)
+    scale = 1.0 / 128 ** 0.5
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    args = (q, kc, vc, pt_d, row_seq, lens, nq, nkv, scale)
+    t_pf = _time(lambda: A.paged_rows(*args, split_tokens=512, prefill_rows=R, quant=True, error_word=err), iters)
+    t_dec = _time(lambda: A.paged_rows(*args, split_tokens=512, quant=True, error_word=err), iters)
+    assert int(err.item()) == 0
+    # causal work: sum over rows of (position + 1) keys, 2 matmuls of 128 x heads
+    keys = prompts * prompt_len * (prompt_len + 1) // 2
+    flops = 2.0 * 2.0 * keys * nq * A.HEAD_DIM
+    kv_unique = num_pages * A.PAGE * nkv * A.HEAD_DIM * 2 * 2
+    return {"rows": R, "prompts": prompts, "prompt_len": prompt_len, "prefill_kernel_ms": t_pf,
+            "split_decode_ms": t_dec, "speedup": t_dec / t_pf, "attention_flop": flops,
+            "prefill_tflops": flops / (t_pf * 1e-3) / 1e12, "kv_bytes_unique": kv_unique,
+            "kv_bytes_decode_path": keys * nkv * A.HEAD_DIM * 2 * 2}
+
+
 def _attention_cpu(q, kc, vc, pt, lens, n_seq: int, scale: float) -> dict:
     """The CPU restatement of the reference's decode attention (the oracle,
     one thread, float64) on the first n_seq sequences, scaled to the batch by
@@ -343,7 +383,8 @@ def serving(batch: int, prompt: int, steps: int, layers: int, max_seq: int) -> d
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["router", "gemm", "attention", "attn_block", "serving", "proj"])
+    ap.add_argument("case", choices=["router", "gemm", "attention", "attn_block", "serving", "proj", "prefill"])
+    ap.add_argument("--prompts", type=int, default=1, help="prefill: prompts in the call")
     ap.add_argument("--no-zipf", action="store_true", help="gemm: uniform routing (no router bias)")
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--steps", type=int, default=10)
@@ -372,6 +413,8 @@ def main() -> int:
         res = serving(a.batch, a.prompt, a.steps, a.layers, a.max_seq)
     elif a.case == "proj":
         res = proj(a.iters)
+    elif a.case == "prefill":
+        res = prefill(a.prompts, a.prompt, a.iters)
     else:
         res = (router(a.tokens, a.iters, a.plain) if a.case == "router"
                else gemm(a.tokens, a.experts, a.iters, not a.no_zipf, a.act_planes,
