@@ -100,13 +100,27 @@ typedef struct {
     int max_seq;             /* tokens per request, prompt + generated */
     int prefill_chunk;       /* rows per forward (admitted prompts are cut to it); 0 = 2048 */
     int num_cache_pages;     /* 16-token KV pages shared by all requests; 0 = max_batch * ceil(max_seq / 16) */
+    int num_gpus;            /* GPUs of this process, from the current device on; 0 or 1 = one */
 } glm_engine_config_t;
 
 /* Creates an engine whose weights the caller provides (device memory that
  * must outlive the engine; several layers may share one weight set).  The KV
  * caches, activations and workspaces are allocated here.  The first request
  * waits for the device once, so the weights may still be in flight on any
- * stream until then. */
+ * stream until then.
+ *
+ * num_gpus = N > 1: one process drives devices d .. d + N - 1 (d = the
+ * current device; peer access is enabled between them).  Rank r holds query
+ * heads [r nq/N, (r+1) nq/N) and KV heads [r nkv/N, (r+1) nkv/N) of every
+ * attention layer (tensor parallel, the o_proj partials summed over the
+ * ranks in rank order), routed experts [r E/N, (r+1) E/N) of every MoE layer
+ * and the shared expert (expert parallel over NVLink peer memory), and the
+ * dense FFNs whole.  Each forward runs every layer's attention on all rows on
+ * every rank; the FFN of rows [r R/N, (r+1) R/N) runs on rank r and the rows
+ * are gathered to every rank (peer stores) before the next layer.  Rank 0
+ * holds the requests and computes the final norm, the lm_head and the
+ * sampling.  Weights come per rank (glm_engine_set_layer_rank,
+ * glm_engine_set_embedding_rank) on that rank's device. */
 moe_status_t glm_engine_create(const glm_engine_config_t* cfg, glm_engine_t** out);
 
 /* embed bf16 [vocab][hidden], final_norm fp32 [hidden], lm_head bf16
@@ -119,6 +133,18 @@ moe_status_t glm_engine_set_embedding(glm_engine_t* engine, const void* embed_bf
  * one expert (w13 [2 I][H], w2 [H][I], router fields ignored). */
 moe_status_t glm_engine_set_layer(glm_engine_t* engine, int layer, const attn_block_weights_t* attn,
                                   const moe_layer_weights_t* ffn);
+
+/* num_gpus > 1: rank `rank`'s weights, on that rank's device.  Attention in
+ * the rank's tp layout (w_qkv rows: its query heads, then its KV heads' k and
+ * v rows; w_o columns of its query heads), the MoE layer's local experts then
+ * the shared expert (router fields whole), a dense FFN whole.  The embedding
+ * table on every rank; final_norm and lm_head are read on rank 0 only (NULL
+ * elsewhere).  With one GPU these equal glm_engine_set_layer /
+ * glm_engine_set_embedding for rank 0. */
+moe_status_t glm_engine_set_layer_rank(glm_engine_t* engine, int rank, int layer, const attn_block_weights_t* attn,
+                                       const moe_layer_weights_t* ffn);
+moe_status_t glm_engine_set_embedding_rank(glm_engine_t* engine, int rank, const void* embed_bf16,
+                                           const float* final_norm, const void* lm_head_bf16);
 
 /* fp32 logits [rows][vocab] of the last decode step's rows (rows in the
  * order of the states passed to it, finished ones skipped) into host memory. */

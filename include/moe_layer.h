@@ -80,7 +80,9 @@ typedef struct moe_layer moe_layer_t;
 /* Validates the shapes and allocates the handle's small state (device error
  * word; with ep_size > 1 a pinned host buffer for the exchanged counts).
  * `comm` is an ncwComm_t over the ep_size ranks, rank ep_rank being this
- * process (NULL when ep_size == 1).  Weight pointers must stay valid.  With
+ * process (NULL when ep_size == 1, or when the peer-memory exchange is used:
+ * a forward with ep_size > 1 and neither a communicator nor peer buffers
+ * returns MOE_ERR_INVALID_ARGUMENT).  Weight pointers must stay valid.  With
  * ep_size > 1 every rank must call the forward with the same max_tokens and
  * may pass at most max_tokens tokens. */
 moe_status_t moe_layer_create(const moe_layer_config_t* cfg, const moe_layer_weights_t* w,

@@ -7,7 +7,7 @@ hundred MB on the device, a handful of launches):
     python profile_cases.py gemm   [--tokens 4096] [--experts 32] [--iters 3] [--act-planes 1|2]
     python profile_cases.py attention [--batch 64] [--ctx-min 1024] [--ctx-max 32768] [--iters 3]
     python profile_cases.py attn_block [--batch 64] [--ctx-min 1024] [--ctx-max 32768] [--iters 3]
-    python profile_cases.py serving [--batch 64] [--prompt 512] [--steps 10] [--layers 92]
+    python profile_cases.py serving [--batch 64] [--prompt 512] [--steps 10] [--layers 92] [--gpus 1]
     python profile_cases.py prefill [--prompts 1] [--prompt 2048] [--iters 3]
 
 `router`: RMSNorm+quant (with the fp32 n rows), the router logits, top-k
@@ -340,7 +340,7 @@ def attn_block(batch: int, ctx_min: int, ctx_max: int, iters: int, tp: int = 8, 
             "achieved_gbs": (kv + wbytes) / (ms * 1e-3) / 1e9, "split_tokens": blk.split_tokens}
 
 
-def serving(batch: int, prompt: int, steps: int, layers: int, max_seq: int) -> dict:
+def serving(batch: int, prompt: int, steps: int, layers: int, max_seq: int, gpus: int = 1) -> dict:
     import time
 
     import numpy as np
@@ -350,7 +350,7 @@ def serving(batch: int, prompt: int, steps: int, layers: int, max_seq: int) -> d
     dev = torch.device("cuda:0")
     w = synth.make_model_weights(shape, seed=0, device=dev, share_layers=True)
     torch.cuda.synchronize()
-    eng = EN.NativeEngine.from_weights(shape, w, max_batch=batch, max_seq=max_seq)
+    eng = EN.NativeEngine.from_weights(shape, w, max_batch=batch, max_seq=max_seq, num_gpus=gpus)
     rng = np.random.default_rng(0)
     prompts = [list(map(int, rng.integers(0, shape.vocab_size, prompt))) for _ in range(batch)]
     states = [eng.prefill(i, p, 0.0, 1.0, 1.0, 1 << 20) for i, p in enumerate(prompts)]
@@ -374,7 +374,7 @@ def serving(batch: int, prompt: int, steps: int, layers: int, max_seq: int) -> d
     weights_gb = (sum(t.numel() * t.element_size() for t in w["layers"][0]["ffn"].values() if t is not None)
                   + sum(t.numel() * t.element_size() for t in w["layers"][-1]["ffn"].values() if t is not None))
     eng.shutdown()
-    return {"layers": layers, "batch": batch, "prompt": prompt, "max_seq": max_seq,
+    return {"layers": layers, "gpus": gpus, "batch": batch, "prompt": prompt, "max_seq": max_seq,
             "prefill_tokens_per_s": batch * (prompt - 1) / prefill_s, "prefill_s": prefill_s,
             "decode_ms_per_step": dt * 1e3, "decode_tokens_per_s": batch / dt,
             "context_after": prompt + 4 + steps, "stage_ms_one_step": st,
@@ -385,6 +385,7 @@ def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("case", choices=["router", "gemm", "attention", "attn_block", "serving", "proj", "prefill"])
     ap.add_argument("--prompts", type=int, default=1, help="prefill: prompts in the call")
+    ap.add_argument("--gpus", type=int, default=1, help="serving: GPUs of the engine (one process)")
     ap.add_argument("--no-zipf", action="store_true", help="gemm: uniform routing (no router bias)")
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--steps", type=int, default=10)
@@ -410,7 +411,7 @@ def main() -> int:
     elif a.case == "attn_block":
         res = attn_block(a.batch, a.ctx_min, a.ctx_max, a.iters, use_graph=a.graph)
     elif a.case == "serving":
-        res = serving(a.batch, a.prompt, a.steps, a.layers, a.max_seq)
+        res = serving(a.batch, a.prompt, a.steps, a.layers, a.max_seq, a.gpus)
     elif a.case == "proj":
         res = proj(a.iters)
     elif a.case == "prefill":

@@ -38,6 +38,7 @@
 #include <mutex>
 #include <new>
 #include <string>
+#include <thread>
 #include <unordered_set>
 #include <vector>
 
@@ -142,6 +143,18 @@ struct glm_engine {
     // ... gathered on the host over all forwards of the last step: [layer][row][top_k]
     std::vector<std::vector<int32_t>> cap_step_idx;
     std::vector<std::vector<float>> cap_step_w;
+    // several GPUs (cfg.num_gpus > 1): this object is rank `rank` of `world`,
+    // one per device; rank 0 holds the requests, the host buffers and the
+    // head, and owns the other ranks' objects (ranks[0] == rank 0 itself)
+    int rank = 0, world = 1;
+    std::vector<glm_engine*> ranks;
+    glm_engine* root = nullptr;
+    void* x2 = nullptr;              // the other residual-stream buffer: layers alternate x0 / x2
+    uint32_t* gather_flags = nullptr;   // [kMaxGatherRanks] epochs raised by every rank
+    uint32_t* gather_epoch = nullptr;   // this rank's all-gather epoch (device)
+    unsigned int* gather_done = nullptr;
+    std::vector<void*> peer_bufs;    // attention / FFN peer buffers this rank allocated
+    moe_status_t thread_status = MOE_OK;
 };
 
 namespace {
@@ -180,7 +193,9 @@ Plan make_plan(const glm_engine_config_t& c) {
     p.rows_cap = static_cast<int>(align_up(static_cast<size_t>(std::max(c.max_batch, chunk)), 16));
     p.max_pages_per_seq = (c.max_seq + kPage - 1) / kPage;
     p.num_pages = c.num_cache_pages > 0 ? c.num_cache_pages : c.max_batch * p.max_pages_per_seq;
-    p.kv_layer_bytes = align_up(static_cast<size_t>(p.num_pages) * kPage * c.num_kv_heads * kHeadDim * 2, 256);
+    const int world = c.num_gpus > 1 ? c.num_gpus : 1;
+    p.kv_layer_bytes =
+        align_up(static_cast<size_t>(p.num_pages) * kPage * (c.num_kv_heads / world) * kHeadDim * 2, 256);
     p.kv_bytes = p.kv_layer_bytes * 2 * c.num_layers;
     p.act_bytes = static_cast<size_t>(p.rows_cap) * c.hidden * 2;
     p.logits_bytes = static_cast<size_t>(c.max_batch) * c.vocab_size * 4;
@@ -197,7 +212,7 @@ cudaError_t dev_alloc(T** p, size_t bytes) {
     return e;
 }
 
-void destroy(glm_engine* E) {
+void destroy_one(glm_engine* E) {
     if (!E) return;
     if (E->stream) cudaStreamSynchronize(E->stream);
     for (Request* r : E->requests) delete r;
@@ -208,9 +223,11 @@ void destroy(glm_engine* E) {
     }
     for (void* p : E->owned) cudaFree(p);
     void* dev[] = {E->kv, E->x0, E->x1, E->xn, E->logits, E->tokens_out, E->ws, E->page_table, E->dense_idx,
-                   E->dense_w, E->dummy_router, E->error_word, E->stage_dev, E->cap_idx, E->cap_w};
+                   E->dense_w, E->dummy_router, E->error_word, E->stage_dev, E->cap_idx, E->cap_w, E->x2,
+                   E->gather_flags, E->gather_epoch, E->gather_done};
     for (void* p : dev)
         if (p) cudaFree(p);
+    for (void* p : E->peer_bufs) cudaFree(p);
     void* host[] = {E->page_table_host, E->stage_host, E->tokens_host};
     for (void* p : host)
         if (p) cudaFreeHost(p);
@@ -220,11 +237,26 @@ void destroy(glm_engine* E) {
     delete E;
 }
 
-moe_status_t create(const glm_engine_config_t* cfg, glm_engine** out) {
+// Every rank (each on its own device), then rank 0.
+void destroy(glm_engine* E) {
+    if (!E) return;
+    for (size_t r = 1; r < E->ranks.size(); ++r) {
+        cudaSetDevice(E->ranks[r]->device);
+        destroy_one(E->ranks[r]);
+    }
+    cudaSetDevice(E->device);
+    destroy_one(E);
+}
+
+// One rank's device state on the current device.
+moe_status_t create_one(const glm_engine_config_t* cfg, int rank, int world, glm_engine** out) {
     if (!cfg || !out || !config_ok(*cfg)) return MOE_ERR_INVALID_ARGUMENT;
     glm_engine* E = new (std::nothrow) glm_engine();
     if (!E) return MOE_ERR_INVALID_ARGUMENT;
     E->cfg = *cfg;
+    E->rank = rank;
+    E->world = world;
+    E->root = E;
     if (E->cfg.prefill_chunk <= 0) E->cfg.prefill_chunk = 2048;
     const Plan p = make_plan(E->cfg);
     E->rows_cap = p.rows_cap;
@@ -252,7 +284,14 @@ moe_status_t create(const glm_engine_config_t* cfg, glm_engine** out) {
                             static_cast<size_t>(cfg->max_batch) * p.max_pages_per_seq * 4, 0) == cudaSuccess &&
               cudaHostAlloc(reinterpret_cast<void**>(&E->stage_host), E->stage.bytes, 0) == cudaSuccess &&
               cudaHostAlloc(reinterpret_cast<void**>(&E->tokens_host), static_cast<size_t>(p.rows_cap) * 8, 0) ==
-                  cudaSuccess;
+                  cudaSuccess &&
+              (world == 1 || (dev_alloc(&E->x2, p.act_bytes) == cudaSuccess &&
+                              dev_alloc(&E->gather_flags, tb_engine::kMaxGatherRanks * 4) == cudaSuccess &&
+                              dev_alloc(&E->gather_epoch, 4) == cudaSuccess &&
+                              dev_alloc(&E->gather_done, 4) == cudaSuccess &&
+                              cudaMemset(E->gather_flags, 0, tb_engine::kMaxGatherRanks * 4) == cudaSuccess &&
+                              cudaMemset(E->gather_epoch, 0, 4) == cudaSuccess &&
+                              cudaMemset(E->gather_done, 0, 4) == cudaSuccess));
     if (ok) {
         // K/V pages are zero until written (a page id is never read before
         // its slot is written, but the pool starts clean); the dense layers'
@@ -283,15 +322,70 @@ moe_status_t create(const glm_engine_config_t* cfg, glm_engine** out) {
     return MOE_OK;
 }
 
-moe_status_t set_layer(glm_engine* E, int l, const attn_block_weights_t* aw, const moe_layer_weights_t* fw) {
+// The engine: one rank, or cfg->num_gpus ranks on the devices from the
+// current one on, with peer access between every pair.
+moe_status_t create(const glm_engine_config_t* cfg, glm_engine** out) {
+    if (!cfg || !out) return MOE_ERR_INVALID_ARGUMENT;
+    const int N = cfg->num_gpus > 1 ? cfg->num_gpus : 1;
+    if (N == 1) return create_one(cfg, 0, 1, out);
+    const glm_engine_config_t& c = *cfg;
+    if (N > tb_engine::kMaxGatherRanks || c.num_q_heads % N || c.num_kv_heads % N ||
+        (c.first_dense < c.num_layers && c.num_experts % N))
+        return MOE_ERR_INVALID_ARGUMENT;
+    int dev0 = 0, count = 0;
+    if (cudaGetDevice(&dev0) != cudaSuccess || cudaGetDeviceCount(&count) != cudaSuccess) return MOE_ERR_CUDA;
+    if (dev0 + N > count) return MOE_ERR_INVALID_ARGUMENT;
+    for (int a = 0; a < N; ++a) {
+        if (cudaSetDevice(dev0 + a) != cudaSuccess) return MOE_ERR_CUDA;
+        for (int b = 0; b < N; ++b) {
+            if (a == b) continue;
+            int can = 0;
+            if (cudaDeviceCanAccessPeer(&can, dev0 + a, dev0 + b) != cudaSuccess || !can) {
+                cudaSetDevice(dev0);
+                return MOE_ERR_UNSUPPORTED;
+            }
+            const cudaError_t e = cudaDeviceEnablePeerAccess(dev0 + b, 0);
+            if (e == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();
+            else if (e != cudaSuccess) {
+                cudaSetDevice(dev0);
+                return MOE_ERR_CUDA;
+            }
+        }
+    }
+    std::vector<glm_engine*> ranks(N, nullptr);
+    moe_status_t st = MOE_OK;
+    for (int r = 0; r < N && st == MOE_OK; ++r) {
+        if (cudaSetDevice(dev0 + r) != cudaSuccess) st = MOE_ERR_CUDA;
+        else st = create_one(cfg, r, N, &ranks[r]);
+    }
+    cudaSetDevice(dev0);
+    if (st != MOE_OK) {
+        for (int r = N - 1; r >= 0; --r)
+            if (ranks[r]) {
+                cudaSetDevice(dev0 + r);
+                destroy_one(ranks[r]);
+            }
+        cudaSetDevice(dev0);
+        return st;
+    }
+    for (glm_engine* R : ranks) R->root = ranks[0];
+    ranks[0]->ranks = ranks;
+    *out = ranks[0];
+    return MOE_OK;
+}
+
+// Layer l of one rank (the rank's device current): attention with the
+// rank's heads (tp = world), the FFN for the rank's slice of the rows (EP =
+// world for a MoE layer, the whole dense FFN).
+moe_status_t set_layer_one(glm_engine* E, int l, const attn_block_weights_t* aw, const moe_layer_weights_t* fw) {
     if (!E || l < 0 || l >= E->cfg.num_layers || !aw || !fw) return MOE_ERR_INVALID_ARGUMENT;
     const glm_engine_config_t& c = E->cfg;
     Layer& L = E->layers[l];
     if (L.attn || L.ffn) return MOE_ERR_INVALID_ARGUMENT;   // once per layer
     attn_block_config_t ac{};
     ac.hidden = c.hidden;
-    ac.num_q_heads = c.num_q_heads;
-    ac.num_kv_heads = c.num_kv_heads;
+    ac.num_q_heads = c.num_q_heads / E->world;
+    ac.num_kv_heads = c.num_kv_heads / E->world;
     ac.head_dim = c.head_dim;
     ac.rotary_dim = c.rotary_dim;
     ac.rope_theta = c.rope_theta;
@@ -299,15 +393,15 @@ moe_status_t set_layer(glm_engine* E, int l, const attn_block_weights_t* aw, con
     ac.max_batch = E->rows_cap;
     ac.max_pages_per_seq = E->max_pages_per_seq;
     ac.max_context = E->max_pages_per_seq * kPage;
-    ac.tp_size = 1;
-    ac.tp_rank = 0;
+    ac.tp_size = E->world;
+    ac.tp_rank = E->rank;
     ENG_TRY(attn_block_create(&ac, aw, &L.attn));
     moe_layer_config_t mc{};
     mc.hidden = c.hidden;
     mc.rms_eps = c.rms_eps;
-    mc.max_tokens = E->rows_cap;
-    mc.ep_size = 1;
-    mc.ep_rank = 0;
+    mc.max_tokens = (E->rows_cap + E->world - 1) / E->world;   // this rank's slice of a forward's rows
+    mc.ep_size = L.dense ? 1 : E->world;
+    mc.ep_rank = L.dense ? 0 : E->rank;
     moe_layer_weights_t w = *fw;
     if (L.dense) {
         mc.num_experts = 1;
@@ -332,12 +426,58 @@ moe_status_t set_layer(glm_engine* E, int l, const attn_block_weights_t* aw, con
     return MOE_OK;
 }
 
+// Layer l is set on every rank: one zero-filled peer buffer per rank for its
+// attention sum and its expert exchange, every rank given all of them.
+moe_status_t setup_layer_peers(glm_engine* root, int l) {
+    const int N = root->world;
+    std::vector<void*> ab(N, nullptr), fb(N, nullptr);
+    const size_t abytes = attn_block_peer_bytes(root->layers[l].attn);
+    const size_t fbytes = moe_layer_peer_bytes(root->layers[l].ffn);
+    moe_status_t st = MOE_OK;
+    for (int r = 0; r < N && st == MOE_OK; ++r) {
+        glm_engine* R = root->ranks[r];
+        if (cudaSetDevice(R->device) != cudaSuccess) st = MOE_ERR_CUDA;
+        if (st == MOE_OK && abytes) {
+            if (dev_alloc(&ab[r], abytes) != cudaSuccess || cudaMemset(ab[r], 0, abytes) != cudaSuccess) st = MOE_ERR_CUDA;
+            if (ab[r]) R->peer_bufs.push_back(ab[r]);
+        }
+        if (st == MOE_OK && fbytes) {
+            if (dev_alloc(&fb[r], fbytes) != cudaSuccess || cudaMemset(fb[r], 0, fbytes) != cudaSuccess) st = MOE_ERR_CUDA;
+            if (fb[r]) R->peer_bufs.push_back(fb[r]);
+        }
+        if (st == MOE_OK && cudaDeviceSynchronize() != cudaSuccess) st = MOE_ERR_CUDA;
+    }
+    for (int r = 0; r < N && st == MOE_OK; ++r) {
+        glm_engine* R = root->ranks[r];
+        cudaSetDevice(R->device);
+        if (abytes) st = attn_block_set_peer_buffers(R->layers[l].attn, ab.data(), N);
+        if (st == MOE_OK && fbytes) st = moe_layer_set_peer_buffers(R->layers[l].ffn, fb.data(), N);
+    }
+    cudaSetDevice(root->device);
+    return st;
+}
+
+// Rank `rank`'s layer l; once every rank has it, the peer buffers.
+moe_status_t set_layer(glm_engine* E, int rank, int l, const attn_block_weights_t* aw, const moe_layer_weights_t* fw) {
+    if (!E || rank < 0 || rank >= E->world || l < 0 || l >= E->cfg.num_layers) return MOE_ERR_INVALID_ARGUMENT;
+    glm_engine* R = E->world > 1 ? E->ranks[rank] : E;
+    if (cudaSetDevice(R->device) != cudaSuccess) return MOE_ERR_CUDA;
+    moe_status_t st = set_layer_one(R, l, aw, fw);
+    if (st == MOE_OK && E->world > 1) {
+        bool all = true;
+        for (glm_engine* P : E->ranks) all = all && P->layers[l].attn && P->layers[l].ffn;
+        if (all) st = setup_layer_peers(E, l);
+    }
+    cudaSetDevice(E->device);
+    return st;
+}
+
 // Every layer and the embedding are set: size and allocate the workspace.
 // The first call also waits for the whole device once, so that weights the
 // caller wrote on any stream are complete before the engine's stream reads them.
-moe_status_t ensure_ready(glm_engine* E) {
+moe_status_t ensure_ready_one(glm_engine* E) {
     if (E->ws) return MOE_OK;
-    if (!E->embed || !E->final_norm || !E->lm_head) return MOE_ERR_INVALID_ARGUMENT;
+    if (!E->embed || (E->rank == 0 && (!E->final_norm || !E->lm_head))) return MOE_ERR_INVALID_ARGUMENT;
     size_t need = 0;
     for (const Layer& L : E->layers) {
         if (!L.attn || !L.ffn) return MOE_ERR_INVALID_ARGUMENT;
@@ -348,6 +488,18 @@ moe_status_t ensure_ready(glm_engine* E) {
     ENG_CUDA(dev_alloc(&E->ws, need));
     E->ws_bytes = need;
     return MOE_OK;
+}
+
+moe_status_t ensure_ready(glm_engine* E) {
+    if (E->world == 1) return ensure_ready_one(E);
+    moe_status_t st = MOE_OK;
+    for (glm_engine* R : E->ranks) {
+        if (st != MOE_OK) break;
+        if (cudaSetDevice(R->device) != cudaSuccess) st = MOE_ERR_CUDA;
+        else st = ensure_ready_one(R);
+    }
+    cudaSetDevice(E->device);
+    return st;
 }
 
 void set_events(glm_engine* E, bool on) {
@@ -371,7 +523,7 @@ void set_events(glm_engine* E, bool on) {
 // head > 0: rows [R - head, R) also go through the final norm, the lm_head
 // and the sampler (per-row parameters at stage indices 0..head-1), and the
 // tokens come back to tokens_host.
-moe_status_t forward(glm_engine* E, int R, int head) {
+moe_status_t forward_one(glm_engine* E, int R, int head) {
     const bool sample = head > 0;
     const glm_engine_config_t& c = E->cfg;
     cudaStream_t st = E->stream;
@@ -455,7 +607,109 @@ moe_status_t forward(glm_engine* E, int R, int head) {
     return MOE_OK;
 }
 
+// Rank P's part of a forward over R staged rows (several GPUs): the
+// attention of every layer on all rows (tensor parallel), the FFN on the
+// rank's rows [lo, hi), then those rows stored into every rank's buffer
+// before the next layer; the layers alternate between x0 and x2 so that a
+// rank that is ahead never overwrites rows another rank still reads.  Rank 0
+// then runs the head on the sampled rows.
+moe_status_t forward_rank(glm_engine* P, int R, int head) {
+    glm_engine* E = P->root;
+    const glm_engine_config_t& c = P->cfg;
+    ENG_CUDA(cudaSetDevice(P->device));
+    cudaStream_t st = P->stream;
+    const bool sample = head > 0;
+    const bool tm = P->rank == 0 && E->timing && sample;
+    ENG_CUDA(cudaMemcpyAsync(P->stage_dev, E->stage_host, E->stage.bytes, cudaMemcpyHostToDevice, st));
+    const int64_t* tokens = reinterpret_cast<const int64_t*>(P->stage_dev + P->stage.tokens);
+    const int32_t* pos = reinterpret_cast<const int32_t*>(P->stage_dev + P->stage.pos);
+    const int32_t* row_seq = reinterpret_cast<const int32_t*>(P->stage_dev + P->stage.row_seq);
+    if (tm) cudaEventRecord(E->events[0], st);
+    ENG_CUDA(tb_engine::embed_rows(P->embed, tokens, R, c.vocab_size, c.hidden, P->x0, P->error_word, st));
+    tb_engine::GatherSet G{};
+    G.world = P->world;
+    G.me = P->rank;
+    for (int r = 0; r < P->world; ++r) G.flags[r] = E->ranks[r]->gather_flags;
+    const int lo = static_cast<int>(static_cast<long long>(R) * P->rank / P->world);
+    const int hi = static_cast<int>(static_cast<long long>(R) * (P->rank + 1) / P->world);
+    const size_t row_bytes = static_cast<size_t>(c.hidden) * 2;
+    const size_t nl = P->layers.size();
+    void* xfinal = P->x0;
+    for (size_t l = 0; l < nl; ++l) {
+        Layer& L = P->layers[l];
+        void* xin = (l & 1) ? P->x2 : P->x0;
+        void* xout = (l & 1) ? P->x0 : P->x2;
+        if (tm) cudaEventRecord(E->events[1 + 2 * l], st);
+        ENG_TRY(attn_block_prefill(L.attn, xin, R, pos, row_seq, c.max_batch, R - head, P->page_table, P->num_pages,
+                                   L.k_cache, L.v_cache, P->x1, P->ws, P->ws_bytes, st));
+        if (tm) cudaEventRecord(E->events[2 + 2 * l], st);
+        const void* fin = static_cast<const uint8_t*>(P->x1) + lo * row_bytes;
+        void* fout = static_cast<uint8_t*>(xout) + lo * row_bytes;
+        if (L.dense)
+            ENG_TRY(moe_layer_forward_routed(L.ffn, fin, P->dense_idx, P->dense_w, fout, hi - lo, P->ws, P->ws_bytes,
+                                             st));
+        else
+            ENG_TRY(moe_layer_forward(L.ffn, fin, fout, hi - lo, P->ws, P->ws_bytes, st));
+        for (int r = 0; r < P->world; ++r) G.x[r] = (l & 1) ? E->ranks[r]->x0 : E->ranks[r]->x2;
+        ENG_CUDA(tb_engine::rows_allgather(G, xout, lo, hi - lo, c.hidden, P->gather_epoch, P->gather_done,
+                                           20000000000ull, P->error_word, st));
+        xfinal = xout;
+    }
+    if (P->rank != 0 || !sample) return cudaStreamSynchronize(st) == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+    if (tm) cudaEventRecord(E->events[1 + 2 * nl], st);
+    const void* head_x = static_cast<const uint8_t*>(xfinal) + static_cast<size_t>(R - head) * row_bytes;
+    ENG_CUDA(tb_engine::final_norm_rows(head_x, P->final_norm, head, c.hidden, c.rms_eps, P->xn, st));
+    const float one = 1.0f, zero = 0.0f;
+    if (cublasGemmEx(P->cublas, CUBLAS_OP_T, CUBLAS_OP_N, c.vocab_size, head, c.hidden, &one, P->lm_head, CUDA_R_16BF,
+                     c.hidden, P->xn, CUDA_R_16BF, c.hidden, &zero, P->logits, CUDA_R_32F, c.vocab_size,
+                     CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT) != CUBLAS_STATUS_SUCCESS)
+        return MOE_ERR_CUDA;
+    ENG_CUDA(tb_engine::sample_rows(P->logits, head, c.vocab_size,
+                                    reinterpret_cast<const float*>(P->stage_dev + P->stage.temp),
+                                    reinterpret_cast<const float*>(P->stage_dev + P->stage.top_p),
+                                    reinterpret_cast<const uint64_t*>(P->stage_dev + P->stage.seeds), P->tokens_out,
+                                    st));
+    if (tm) cudaEventRecord(E->events[2 + 2 * nl], st);
+    ENG_CUDA(cudaMemcpyAsync(E->tokens_host, P->tokens_out, static_cast<size_t>(head) * 8, cudaMemcpyDeviceToHost, st));
+    ENG_CUDA(cudaStreamSynchronize(st));
+    if (tm) {
+        float ms = 0.0f, attn = 0.0f, ffn = 0.0f;
+        cudaEventElapsedTime(&ms, E->events[0], E->events[1]);
+        E->stage_ms[0] = ms;
+        for (size_t l = 0; l < nl; ++l) {
+            cudaEventElapsedTime(&ms, E->events[1 + 2 * l], E->events[2 + 2 * l]);
+            attn += ms;
+            cudaEventElapsedTime(&ms, E->events[2 + 2 * l], E->events[3 + 2 * l]);
+            ffn += ms;
+        }
+        E->stage_ms[1] = attn;
+        E->stage_ms[2] = ffn;
+        cudaEventElapsedTime(&ms, E->events[1 + 2 * nl], E->events[2 + 2 * nl]);
+        E->stage_ms[3] = ms;
+    }
+    return MOE_OK;
+}
+
+// One forward: on one GPU, or every rank on its own host thread.
+moe_status_t forward(glm_engine* E, int R, int head) {
+    if (E->world == 1) return forward_one(E, R, head);
+    std::vector<std::thread> th;
+    th.reserve(E->world - 1);
+    for (int r = 1; r < E->world; ++r) {
+        glm_engine* P = E->ranks[r];
+        th.emplace_back([P, R, head]() { P->thread_status = forward_rank(P, R, head); });
+    }
+    const moe_status_t s0 = forward_rank(E, R, head);
+    for (std::thread& t : th) t.join();
+    cudaSetDevice(E->device);
+    if (s0 != MOE_OK) return s0;
+    for (int r = 1; r < E->world; ++r)
+        if (E->ranks[r]->thread_status != MOE_OK) return E->ranks[r]->thread_status;
+    return MOE_OK;
+}
+
 moe_status_t upload_stage(glm_engine* E) {
+    if (E->world > 1) return MOE_OK;   // every rank copies the stage itself (forward_rank)
     return cudaMemcpyAsync(E->stage_dev, E->stage_host, E->stage.bytes, cudaMemcpyHostToDevice, E->stream) ==
                    cudaSuccess
                ? MOE_OK
@@ -467,10 +721,20 @@ moe_status_t upload_pages(glm_engine* E, const Request* r, int i0, int i1) {
     if (i1 <= i0) return MOE_OK;
     const size_t off = static_cast<size_t>(r->slot) * E->max_pages_per_seq + i0;
     for (int i = i0; i < i1; ++i) E->page_table_host[off + (i - i0)] = r->pages[i];
-    return cudaMemcpyAsync(E->page_table + off, E->page_table_host + off, static_cast<size_t>(i1 - i0) * 4,
-                           cudaMemcpyHostToDevice, E->stream) == cudaSuccess
-               ? MOE_OK
-               : MOE_ERR_CUDA;
+    if (E->world == 1)
+        return cudaMemcpyAsync(E->page_table + off, E->page_table_host + off, static_cast<size_t>(i1 - i0) * 4,
+                               cudaMemcpyHostToDevice, E->stream) == cudaSuccess
+                   ? MOE_OK
+                   : MOE_ERR_CUDA;
+    // every rank holds the page table; the copies finish before the next forward reads it
+    bool ok = true;
+    for (glm_engine* P : E->ranks) {
+        ok = ok && cudaSetDevice(P->device) == cudaSuccess &&
+             cudaMemcpyAsync(P->page_table + off, E->page_table_host + off, static_cast<size_t>(i1 - i0) * 4,
+                             cudaMemcpyHostToDevice, P->stream) == cudaSuccess;
+    }
+    cudaSetDevice(E->device);
+    return ok ? MOE_OK : MOE_ERR_CUDA;
 }
 
 void release(glm_engine* E, Request* r) {
@@ -721,6 +985,90 @@ bool read_config(const std::string& dir, int max_batch, int max_seq, glm_engine_
     return true;
 }
 
+// One layer's attention (the rank's heads) and FFN (the rank's experts, or
+// the whole dense FFN) from the checkpoint into the rank's device memory.
+bool load_layer_rank(glm_engine* E, glm_engine* R, const st_model_t* M, int l, int rank) {
+    const glm_engine_config_t& c = E->cfg;
+    const std::string prefix = "model.layers." + std::to_string(l) + ".";
+    if (cudaSetDevice(R->device) != cudaSuccess) return false;
+    st_attn_spec_t as{c.hidden, c.num_q_heads, c.num_kv_heads, c.head_dim, E->world, rank};
+    st_attn_sizes_t asz;
+    if (st_attn_rank_sizes(&as, &asz) != MOE_OK) return false;
+    HostBuf ag, aqkv, asqkv, ao, aso;
+    ag.b.resize(asz.gamma);
+    aqkv.b.resize(asz.w_qkv);
+    asqkv.b.resize(asz.s_qkv);
+    ao.b.resize(asz.w_o);
+    aso.b.resize(asz.s_o);
+    if (st_attn_rank_host(M, prefix.c_str(), &as, ag.as<float>(), aqkv.as<uint8_t>(), asqkv.as<float>(),
+                          ao.as<uint8_t>(), aso.as<float>()) != MOE_OK) {
+        std::fprintf(stderr, "init_engine: layer %d attention tensors missing or malformed\n", l);
+        return false;
+    }
+    void *d0, *d1, *d2, *d3, *d4;
+    if (!(upload_owned(R, ag.b.data(), asz.gamma, &d0) && upload_owned(R, aqkv.b.data(), asz.w_qkv, &d1) &&
+          upload_owned(R, asqkv.b.data(), asz.s_qkv, &d2) && upload_owned(R, ao.b.data(), asz.w_o, &d3) &&
+          upload_owned(R, aso.b.data(), asz.s_o, &d4))) {
+        std::fprintf(stderr, "init_engine: layer %d attention upload failed (%s)\n", l,
+                     cudaGetErrorString(cudaGetLastError()));
+        return false;
+    }
+    attn_block_weights_t aw{};
+    aw.gamma = static_cast<const float*>(d0);
+    aw.w_qkv = d1;
+    aw.s_qkv = static_cast<const float*>(d2);
+    aw.w_o = d3;
+    aw.s_o = static_cast<const float*>(d4);
+    st_moe_sizes_t fs;
+    HostBuf fg, frw, frb, fw13, fs13, fw2, fs2;
+    int has_bias = 0;
+    moe_status_t s;
+    const bool dense = l < c.first_dense;
+    st_moe_spec_t ms{c.hidden, c.num_experts, c.moe_intermediate, c.num_shared, E->world, rank, nullptr};
+    s = dense ? st_dense_ffn_sizes(c.hidden, c.dense_intermediate, &fs) : st_moe_layer_sizes(&ms, &fs);
+    if (s == MOE_OK) {
+        fg.b.resize(fs.gamma);
+        frw.b.resize(fs.router_w);
+        frb.b.resize(fs.router_bias);
+        fw13.b.resize(fs.w13);
+        fs13.b.resize(fs.s13);
+        fw2.b.resize(fs.w2);
+        fs2.b.resize(fs.s2);
+        if (dense)
+            s = st_dense_ffn_host(M, prefix.c_str(), c.hidden, c.dense_intermediate, fg.as<float>(), fw13.as<uint8_t>(),
+                                  fs13.as<float>(), fw2.as<uint8_t>(), fs2.as<float>());
+        else
+            s = st_moe_layer_host(M, prefix.c_str(), &ms, fg.as<float>(), frw.as<float>(), frb.as<float>(), &has_bias,
+                                  fw13.as<uint8_t>(), fs13.as<float>(), fw2.as<uint8_t>(), fs2.as<float>());
+    }
+    if (s != MOE_OK) {
+        std::fprintf(stderr, "init_engine: layer %d FFN tensors missing or malformed\n", l);
+        return false;
+    }
+    void *e0, *e1 = nullptr, *e2 = nullptr, *e3, *e4, *e5, *e6;
+    if (!(upload_owned(R, fg.b.data(), fs.gamma, &e0) && upload_owned(R, frw.b.data(), fs.router_w, &e1) &&
+          (has_bias ? upload_owned(R, frb.b.data(), fs.router_bias, &e2) : true) &&
+          upload_owned(R, fw13.b.data(), fs.w13, &e3) && upload_owned(R, fs13.b.data(), fs.s13, &e4) &&
+          upload_owned(R, fw2.b.data(), fs.w2, &e5) && upload_owned(R, fs2.b.data(), fs.s2, &e6))) {
+        std::fprintf(stderr, "init_engine: layer %d FFN upload failed (%s)\n", l,
+                     cudaGetErrorString(cudaGetLastError()));
+        return false;
+    }
+    moe_layer_weights_t fw{};
+    fw.norm_gamma = static_cast<const float*>(e0);
+    fw.router_w = static_cast<const float*>(e1);
+    fw.router_bias = has_bias ? static_cast<const float*>(e2) : nullptr;
+    fw.w13 = e3;
+    fw.s13 = static_cast<const float*>(e4);
+    fw.w2 = e5;
+    fw.s2 = static_cast<const float*>(e6);
+    if (set_layer(E, rank, l, &aw, &fw) != MOE_OK) {
+        std::fprintf(stderr, "init_engine: layer %d rejected by the layer kernels\n", l);
+        return false;
+    }
+    return true;
+}
+
 glm_engine* init_from_dir(const char* model_dir, int max_batch, int max_seq, int num_gpus) {
     if (!model_dir || max_batch <= 0 || max_seq <= 0) return nullptr;
     const std::string dir(model_dir);
@@ -734,6 +1082,7 @@ glm_engine* init_from_dir(const char* model_dir, int max_batch, int max_seq, int
         std::fprintf(stderr, "init_engine: unsupported model shape in %s/config.json\n", model_dir);
         return nullptr;
     }
+    c.num_gpus = num_gpus > 1 ? num_gpus : 1;
     st_model_t* M = nullptr;
     if (st_open(model_dir, &M) != MOE_OK) {
         std::fprintf(stderr, "init_engine: cannot open the safetensors checkpoint in %s\n", model_dir);
@@ -742,131 +1091,49 @@ glm_engine* init_from_dir(const char* model_dir, int max_batch, int max_seq, int
     glm_engine* E = nullptr;
     if (create(&c, &E) != MOE_OK) {
         st_close(M);
-        std::fprintf(stderr, "init_engine: device allocation failed\n");
+        std::fprintf(stderr, "init_engine: device allocation failed (or %d GPUs with peer access not available)\n",
+                     c.num_gpus);
         return nullptr;
     }
     E->num_gpus_requested = num_gpus;
     E->num_tensors = st_num_tensors(M);
     bool ok = true;
     const int64_t H = c.hidden, V = c.vocab_size;
-    void *embed = nullptr, *lm = nullptr, *fnorm = nullptr;
-    ok = upload_bf16_table(E, M, "model.embed_tokens.weight", V, H, &embed);
-    if (ok) {
-        st_tensor_t t;
-        if (st_get(M, "lm_head.weight", &t) == MOE_OK) ok = upload_bf16_table(E, M, "lm_head.weight", V, H, &lm);
-        else if (tied) lm = embed;
-        else ok = false;
-    }
-    if (ok) {
-        st_tensor_t t;
-        std::vector<float> g(H);
-        ok = st_get(M, "model.norm.weight", &t) == MOE_OK && t.ndim == 1 && t.shape[0] == H;
-        if (ok && t.dtype == ST_F32) std::memcpy(g.data(), t.data, H * 4);
-        else if (ok && t.dtype == ST_BF16)
-            for (int64_t i = 0; i < H; ++i) {
-                uint16_t x;
-                std::memcpy(&x, static_cast<const uint8_t*>(t.data) + 2 * i, 2);
-                const uint32_t u = static_cast<uint32_t>(x) << 16;
-                std::memcpy(&g[i], &u, 4);
-            }
-        else ok = false;
-        ok = ok && upload_owned(E, g.data(), H * 4, &fnorm);
-    }
-    if (!ok) std::fprintf(stderr, "init_engine: embedding, lm_head or final norm missing or malformed\n");
-    if (ok && glm_engine_set_embedding(E, embed, static_cast<const float*>(fnorm), lm) != MOE_OK) {
-        std::fprintf(stderr, "init_engine: embedding or lm_head not usable\n");
-        ok = false;
-    }
-    st_attn_spec_t as{c.hidden, c.num_q_heads, c.num_kv_heads, c.head_dim, 1, 0};
-    st_attn_sizes_t asz;
-    ok = ok && st_attn_rank_sizes(&as, &asz) == MOE_OK;
-    for (int l = 0; ok && l < c.num_layers; ++l) {
-        const std::string prefix = "model.layers." + std::to_string(l) + ".";
-        HostBuf ag, aqkv, asqkv, ao, aso;
-        ag.b.resize(asz.gamma);
-        aqkv.b.resize(asz.w_qkv);
-        asqkv.b.resize(asz.s_qkv);
-        ao.b.resize(asz.w_o);
-        aso.b.resize(asz.s_o);
-        if (st_attn_rank_host(M, prefix.c_str(), &as, ag.as<float>(), aqkv.as<uint8_t>(), asqkv.as<float>(),
-                              ao.as<uint8_t>(), aso.as<float>()) != MOE_OK) {
-            std::fprintf(stderr, "init_engine: layer %d attention tensors missing or malformed\n", l);
-            ok = false;
-            break;
+    for (int rank = 0; ok && rank < E->world; ++rank) {
+        glm_engine* R = E->world > 1 ? E->ranks[rank] : E;
+        ok = cudaSetDevice(R->device) == cudaSuccess;
+        void *embed = nullptr, *lm = nullptr, *fnorm = nullptr;
+        ok = ok && upload_bf16_table(R, M, "model.embed_tokens.weight", V, H, &embed);
+        if (ok && rank == 0) {
+            st_tensor_t t;
+            if (st_get(M, "lm_head.weight", &t) == MOE_OK) ok = upload_bf16_table(R, M, "lm_head.weight", V, H, &lm);
+            else if (tied) lm = embed;
+            else ok = false;
+            std::vector<float> g(H);
+            ok = ok && st_get(M, "model.norm.weight", &t) == MOE_OK && t.ndim == 1 && t.shape[0] == H;
+            if (ok && t.dtype == ST_F32) std::memcpy(g.data(), t.data, H * 4);
+            else if (ok && t.dtype == ST_BF16)
+                for (int64_t i = 0; i < H; ++i) {
+                    uint16_t x;
+                    std::memcpy(&x, static_cast<const uint8_t*>(t.data) + 2 * i, 2);
+                    const uint32_t u = static_cast<uint32_t>(x) << 16;
+                    std::memcpy(&g[i], &u, 4);
+                }
+            else ok = false;
+            ok = ok && upload_owned(R, g.data(), H * 4, &fnorm);
         }
-        attn_block_weights_t aw{};
-        void *d0, *d1, *d2, *d3, *d4;
-        ok = upload_owned(E, ag.b.data(), asz.gamma, &d0) && upload_owned(E, aqkv.b.data(), asz.w_qkv, &d1) &&
-             upload_owned(E, asqkv.b.data(), asz.s_qkv, &d2) && upload_owned(E, ao.b.data(), asz.w_o, &d3) &&
-             upload_owned(E, aso.b.data(), asz.s_o, &d4);
-        if (!ok) {
-            std::fprintf(stderr, "init_engine: layer %d attention upload failed (%s)\n", l,
-                         cudaGetErrorString(cudaGetLastError()));
-            break;
-        }
-        aw.gamma = static_cast<const float*>(d0);
-        aw.w_qkv = d1;
-        aw.s_qkv = static_cast<const float*>(d2);
-        aw.w_o = d3;
-        aw.s_o = static_cast<const float*>(d4);
-        st_moe_sizes_t fs;
-        HostBuf fg, frw, frb, fw13, fs13, fw2, fs2;
-        int has_bias = 0;
-        moe_status_t s;
-        const bool dense = l < c.first_dense;
-        if (dense) {
-            s = st_dense_ffn_sizes(c.hidden, c.dense_intermediate, &fs);
-        } else {
-            st_moe_spec_t ms{c.hidden, c.num_experts, c.moe_intermediate, c.num_shared, 1, 0, nullptr};
-            s = st_moe_layer_sizes(&ms, &fs);
-        }
-        if (s == MOE_OK) {
-            fg.b.resize(fs.gamma);
-            frw.b.resize(fs.router_w);
-            frb.b.resize(fs.router_bias);
-            fw13.b.resize(fs.w13);
-            fs13.b.resize(fs.s13);
-            fw2.b.resize(fs.w2);
-            fs2.b.resize(fs.s2);
-            if (dense) {
-                s = st_dense_ffn_host(M, prefix.c_str(), c.hidden, c.dense_intermediate, fg.as<float>(),
-                                      fw13.as<uint8_t>(), fs13.as<float>(), fw2.as<uint8_t>(), fs2.as<float>());
-            } else {
-                st_moe_spec_t ms{c.hidden, c.num_experts, c.moe_intermediate, c.num_shared, 1, 0, nullptr};
-                s = st_moe_layer_host(M, prefix.c_str(), &ms, fg.as<float>(), frw.as<float>(), frb.as<float>(),
-                                      &has_bias, fw13.as<uint8_t>(), fs13.as<float>(), fw2.as<uint8_t>(),
-                                      fs2.as<float>());
-            }
-        }
-        if (s != MOE_OK) {
-            std::fprintf(stderr, "init_engine: layer %d FFN tensors missing or malformed\n", l);
-            ok = false;
-            break;
-        }
-        void *e0, *e1 = nullptr, *e2 = nullptr, *e3, *e4, *e5, *e6;
-        ok = upload_owned(E, fg.b.data(), fs.gamma, &e0) && upload_owned(E, frw.b.data(), fs.router_w, &e1) &&
-             (has_bias ? upload_owned(E, frb.b.data(), fs.router_bias, &e2) : true) &&
-             upload_owned(E, fw13.b.data(), fs.w13, &e3) && upload_owned(E, fs13.b.data(), fs.s13, &e4) &&
-             upload_owned(E, fw2.b.data(), fs.w2, &e5) && upload_owned(E, fs2.b.data(), fs.s2, &e6);
-        if (!ok) {
-            std::fprintf(stderr, "init_engine: layer %d FFN upload failed (%s)\n", l,
-                         cudaGetErrorString(cudaGetLastError()));
-            break;
-        }
-        moe_layer_weights_t fw{};
-        fw.norm_gamma = static_cast<const float*>(e0);
-        fw.router_w = static_cast<const float*>(e1);
-        fw.router_bias = has_bias ? static_cast<const float*>(e2) : nullptr;
-        fw.w13 = e3;
-        fw.s13 = static_cast<const float*>(e4);
-        fw.w2 = e5;
-        fw.s2 = static_cast<const float*>(e6);
-        if (set_layer(E, l, &aw, &fw) != MOE_OK) {
-            std::fprintf(stderr, "init_engine: layer %d rejected by the layer kernels\n", l);
-            ok = false;
+        if (!ok) std::fprintf(stderr, "init_engine: embedding, lm_head or final norm missing or malformed\n");
+        if (ok) {
+            R->embed = embed;
+            R->final_norm = static_cast<const float*>(fnorm);
+            R->lm_head = lm;
         }
     }
+    for (int l = 0; ok && l < c.num_layers; ++l)
+        for (int rank = 0; ok && rank < E->world; ++rank)
+            ok = load_layer_rank(E, E->world > 1 ? E->ranks[rank] : E, M, l, rank);
     st_close(M);
+    cudaSetDevice(E->device);
     if (ok && ensure_ready(E) != MOE_OK) {
         std::fprintf(stderr, "init_engine: workspace allocation failed\n");
         ok = false;
@@ -939,7 +1206,7 @@ int64_t get_engine_info(glm_engine_t* E, int32_t info_type) {
         case 3: return c.vocab_size;
         case 4: return c.num_experts;
         case 5: return c.top_k;
-        case 6: return 1;
+        case 6: return E->world;
         case 7: return c.max_batch;
         case 8: return c.max_seq;
         case 9: return E->num_pages - static_cast<int64_t>(E->free_pages.size());
@@ -978,10 +1245,31 @@ moe_status_t glm_engine_set_embedding(glm_engine_t* E, const void* embed_bf16, c
 
 moe_status_t glm_engine_set_layer(glm_engine_t* E, int layer, const attn_block_weights_t* attn,
                                   const moe_layer_weights_t* ffn) {
-    if (!E) return MOE_ERR_INVALID_ARGUMENT;
+    if (!E || E->world > 1) return MOE_ERR_INVALID_ARGUMENT;
     std::lock_guard<std::mutex> g(E->mu);
     cudaSetDevice(E->device);
-    return set_layer(E, layer, attn, ffn);
+    return set_layer(E, 0, layer, attn, ffn);
+}
+
+moe_status_t glm_engine_set_layer_rank(glm_engine_t* E, int rank, int layer, const attn_block_weights_t* attn,
+                                       const moe_layer_weights_t* ffn) {
+    if (!E) return MOE_ERR_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(E->mu);
+    return set_layer(E, rank, layer, attn, ffn);
+}
+
+moe_status_t glm_engine_set_embedding_rank(glm_engine_t* E, int rank, const void* embed_bf16, const float* final_norm,
+                                           const void* lm_head_bf16) {
+    if (!E || rank < 0 || rank >= E->world || !embed_bf16 || (reinterpret_cast<uintptr_t>(embed_bf16) & 15))
+        return MOE_ERR_INVALID_ARGUMENT;
+    if (rank == 0 && (!final_norm || !lm_head_bf16 || (reinterpret_cast<uintptr_t>(lm_head_bf16) & 15)))
+        return MOE_ERR_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(E->mu);
+    glm_engine* P = E->world > 1 ? E->ranks[rank] : E;
+    P->embed = embed_bf16;
+    P->final_norm = final_norm;
+    P->lm_head = lm_head_bf16;
+    return MOE_OK;
 }
 
 moe_status_t glm_engine_copy_logits(glm_engine_t* E, float* host_out, int rows) {
@@ -997,6 +1285,7 @@ moe_status_t glm_engine_copy_logits(glm_engine_t* E, float* host_out, int rows) 
 
 moe_status_t glm_engine_set_capture(glm_engine_t* E, int on) {
     if (!E) return MOE_ERR_INVALID_ARGUMENT;
+    if (E->world > 1) return on ? MOE_ERR_UNSUPPORTED : MOE_OK;   // routing is spread over the ranks
     std::lock_guard<std::mutex> g(E->mu);
     cudaSetDevice(E->device);
     if (!on) {
@@ -1044,6 +1333,7 @@ moe_status_t glm_engine_copy_kv(glm_engine_t* E, int layer, int page, int npages
     if (!E || layer < 0 || layer >= E->cfg.num_layers || page < 0 || npages < 0 || page + npages > E->num_pages ||
         !k_host || !v_host)
         return MOE_ERR_INVALID_ARGUMENT;
+    if (E->world > 1) return MOE_ERR_UNSUPPORTED;   // each rank holds its own KV heads
     std::lock_guard<std::mutex> g(E->mu);
     cudaSetDevice(E->device);
     const size_t pb = static_cast<size_t>(kPage) * E->cfg.num_kv_heads * kHeadDim * 2;
@@ -1056,9 +1346,7 @@ moe_status_t glm_engine_copy_kv(glm_engine_t* E, int layer, int page, int npages
                : MOE_ERR_CUDA;
 }
 
-moe_status_t glm_engine_check_error(glm_engine_t* E) {
-    if (!E) return MOE_ERR_INVALID_ARGUMENT;
-    std::lock_guard<std::mutex> g(E->mu);
+static moe_status_t check_error_one(glm_engine* E) {
     cudaSetDevice(E->device);
     moe_status_t worst = MOE_OK;
     for (Layer& L : E->layers) {
@@ -1075,8 +1363,21 @@ moe_status_t glm_engine_check_error(glm_engine_t* E) {
     if (cudaMemcpy(&h, E->error_word, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return MOE_ERR_CUDA;
     if (h) {
         cudaMemset(E->error_word, 0, 4);
-        if (worst == MOE_OK) worst = MOE_ERR_INVALID_ARGUMENT;   // a token id outside the vocabulary
+        // 3: a rows all-gather wait gave up (another rank stopped); else a token id outside the vocabulary
+        if (worst == MOE_OK) worst = h == 3 ? MOE_ERR_DEVICE_TIMEOUT : MOE_ERR_INVALID_ARGUMENT;
     }
+    return worst;
+}
+
+moe_status_t glm_engine_check_error(glm_engine_t* E) {
+    if (!E) return MOE_ERR_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(E->mu);
+    moe_status_t worst = check_error_one(E);
+    for (int r = 1; r < E->world; ++r) {
+        const moe_status_t s = check_error_one(E->ranks[r]);
+        if (s != MOE_OK && worst == MOE_OK) worst = s;
+    }
+    cudaSetDevice(E->device);
     return worst;
 }
 

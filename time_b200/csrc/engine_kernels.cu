@@ -5,6 +5,10 @@
 //   batched sampler    one warp per row: greedy or top-p with the row's own
 //                      temperature, top_p and seed (sampling.cuh, the rules of
 //                      the legacy launch_top_p_sampling)
+//   rows all-gather    several GPUs of one process: each rank stores its slice
+//                      of rows into every rank's buffer (peer stores), the last
+//                      block raises the rank's flag on every rank, and a wait
+//                      kernel holds the stream until every rank's flag is up
 //
 // The reference engine embeds into fp32 (launch_embedding_lookup,
 // src/terra/engine.t:1387) and samples one request per launch
@@ -69,6 +73,64 @@ sample_kernel(const float* __restrict__ logits, int V, int R, const float* __res
 
 inline cudaError_t last() { return cudaGetLastError(); }
 
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint64_t gtimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// This rank's rows [off16, off16 + n16) (16-byte units) into every other
+// rank's buffer; the last block to finish (all its puts fenced) raises
+// flags[r][me] = ++epoch on every rank r.
+__global__ void __launch_bounds__(256)
+rows_allgather_kernel(const tb_engine::GatherSet G, const uint4* __restrict__ src, size_t off16, size_t n16,
+                      uint32_t* __restrict__ epoch, unsigned int* __restrict__ done_blocks) {
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n16;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const uint4 v = src[off16 + i];
+        for (int r = 0; r < G.world; ++r)
+            if (r != G.me) static_cast<uint4*>(G.x[r])[off16 + i] = v;
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned int prev = atomicAdd(done_blocks, 1u);
+        if (prev == gridDim.x - 1) {
+            *done_blocks = 0;
+            const uint32_t e = *epoch + 1u;
+            *epoch = e;
+            __threadfence_system();
+            for (int r = 0; r < G.world; ++r) st_release_sys(G.flags[r] + G.me, e);
+        }
+    }
+}
+
+// Until every rank's flag in this rank's array reaches this rank's epoch
+// (bounded: error word 3 after timeout_ns).
+__global__ void rows_allgather_wait_kernel(const tb_engine::GatherSet G, const uint32_t* __restrict__ epoch,
+                                           unsigned long long timeout_ns, int* __restrict__ error_word) {
+    if (threadIdx.x != 0) return;
+    const uint32_t e = *epoch;
+    const uint64_t t0 = gtimer_ns();
+    for (int s = 0; s < G.world; ++s) {
+        while (ld_acquire_sys(G.flags[G.me] + s) < e) {
+            if (gtimer_ns() - t0 > timeout_ns) {
+                if (error_word) atomicExch(error_word, 3);
+                return;
+            }
+            __nanosleep(100);
+        }
+    }
+}
+
 }  // namespace
 
 namespace tb_engine {
@@ -92,6 +154,18 @@ cudaError_t sample_rows(const float* logits, int R, int V, const float* temperat
                         const uint64_t* seeds, int64_t* out, cudaStream_t st) {
     if (R <= 0) return cudaSuccess;
     sample_kernel<<<(R + 3) / 4, 128, 0, st>>>(logits, V, R, temperature, top_p, seeds, out);
+    return last();
+}
+
+cudaError_t rows_allgather(const GatherSet& G, const void* src, size_t row0, size_t rows, size_t H, uint32_t* epoch,
+                           unsigned int* done_blocks, unsigned long long timeout_ns, int* error_word,
+                           cudaStream_t st) {
+    if (G.world < 1 || G.world > kMaxGatherRanks || G.me < 0 || G.me >= G.world || H % 8) return cudaErrorInvalidValue;
+    const size_t off16 = row0 * H / 8, n16 = rows * H / 8;
+    const int blocks = static_cast<int>(n16 == 0 ? 1 : (n16 + 255) / 256 < 1184 ? (n16 + 255) / 256 : 1184);
+    rows_allgather_kernel<<<blocks, 256, 0, st>>>(G, static_cast<const uint4*>(src), off16, n16, epoch, done_blocks);
+    if (last() != cudaSuccess) return cudaErrorLaunchFailure;
+    rows_allgather_wait_kernel<<<1, 32, 0, st>>>(G, epoch, timeout_ns, error_word);
     return last();
 }
 

@@ -16,4 +16,21 @@ cudaError_t final_norm_rows(const void* x, const float* gamma, int R, int H, flo
 cudaError_t sample_rows(const float* logits, int R, int V, const float* temperature, const float* top_p,
                         const uint64_t* seeds, int64_t* out, cudaStream_t st);
 
+// Several GPUs of one process: every rank's row buffer and flag array
+// ([kMaxGatherRanks] uint32, zeroed at creation), as device pointers.
+constexpr int kMaxGatherRanks = 8;
+struct GatherSet {
+    void* x[kMaxGatherRanks];
+    uint32_t* flags[kMaxGatherRanks];
+    int world, me;
+};
+// Rows [row0, row0 + rows) of bf16 [*][H] src (this rank's buffer G.x[G.me])
+// into every rank's buffer at the same rows, then wait until every rank has
+// put its rows (each rank passes its own slice; every rank calls it once per
+// gather, in the same order).  epoch / done_blocks: this rank's device
+// counters (zeroed at creation).  A wait past timeout_ns sets *error_word = 3.
+cudaError_t rows_allgather(const GatherSet& G, const void* src, size_t row0, size_t rows, size_t H, uint32_t* epoch,
+                           unsigned int* done_blocks, unsigned long long timeout_ns, int* error_word,
+                           cudaStream_t st);
+
 }  // namespace tb_engine

@@ -387,7 +387,8 @@ moe_status_t moe_layer_create(const moe_layer_config_t* cfg, const moe_layer_wei
         return MOE_ERR_INVALID_ARGUMENT;
     if (c.num_shared < 0 || c.num_shared > 1 || c.max_tokens <= 0) return MOE_ERR_INVALID_ARGUMENT;
     if (c.ep_size <= 0 || c.ep_rank < 0 || c.ep_rank >= c.ep_size || c.num_experts % c.ep_size) return MOE_ERR_INVALID_ARGUMENT;
-    if (c.ep_size > 1 && !comm) return MOE_ERR_INVALID_ARGUMENT;
+    // ep_size > 1 without a communicator: the peer-memory exchange only (its
+    // buffers must be set before the first forward)
     if (c.ep_size > 1 && c.num_experts > 1024) return MOE_ERR_UNSUPPORTED;
     if (!w->norm_gamma || !w->router_w || !w->w13 || !w->s13 || !w->w2 || !w->s2) return MOE_ERR_INVALID_ARGUMENT;
     moe_layer* L = new (std::nothrow) moe_layer;
@@ -431,6 +432,7 @@ size_t moe_layer_workspace_bytes(const moe_layer_t* L) { return L ? L->bytes : 0
 moe_status_t moe_layer_forward_routed(moe_layer_t* L, const void* x, const int32_t* idx, const float* wts, void* out,
                                       int T, void* ws, size_t ws_bytes, cwStream_t stream) {
     if (!L || !ws || (T > 0 && (!x || !out || !idx || !wts))) return MOE_ERR_INVALID_ARGUMENT;
+    if (L->cfg.ep_size > 1 && !L->peer_mode && !L->comm) return MOE_ERR_INVALID_ARGUMENT;
     if (T < 0 || T > L->cfg.max_tokens) return MOE_ERR_INVALID_ARGUMENT;
     if (ws_bytes < L->bytes) return MOE_ERR_WORKSPACE;
     if (T == 0 && L->cfg.ep_size == 1) return MOE_OK;
@@ -451,6 +453,7 @@ moe_status_t moe_layer_forward_routed(moe_layer_t* L, const void* x, const int32
 moe_status_t moe_layer_forward(moe_layer_t* L, const void* x, void* out, int T, void* ws, size_t ws_bytes,
                                cwStream_t stream) {
     if (!L || !ws || (T > 0 && (!x || !out))) return MOE_ERR_INVALID_ARGUMENT;
+    if (L->cfg.ep_size > 1 && !L->peer_mode && !L->comm) return MOE_ERR_INVALID_ARGUMENT;
     if (T < 0 || T > L->cfg.max_tokens) return MOE_ERR_INVALID_ARGUMENT;
     if (ws_bytes < L->bytes) return MOE_ERR_WORKSPACE;
     if (T == 0 && L->cfg.ep_size == 1) return MOE_OK;

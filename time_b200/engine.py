@@ -29,7 +29,7 @@ class EngineConfig(ctypes.Structure):
                 ("num_kv_heads", c_int), ("head_dim", c_int), ("rotary_dim", c_int), ("vocab_size", c_int),
                 ("num_experts", c_int), ("top_k", c_int), ("moe_intermediate", c_int), ("num_shared", c_int),
                 ("dense_intermediate", c_int), ("rope_theta", c_float), ("rms_eps", c_float), ("max_batch", c_int),
-                ("max_seq", c_int), ("prefill_chunk", c_int), ("num_cache_pages", c_int)]
+                ("max_seq", c_int), ("prefill_chunk", c_int), ("num_cache_pages", c_int), ("num_gpus", c_int)]
 
 
 @dataclasses.dataclass
@@ -77,6 +77,9 @@ def lib() -> ctypes.CDLL:
         e.glm_engine_set_embedding.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p]
         e.glm_engine_set_layer.argtypes = [c_void_p, c_int, ctypes.POINTER(A.BlockWeights),
                                            ctypes.POINTER(M.LayerWeights)]
+        e.glm_engine_set_layer_rank.argtypes = [c_void_p, c_int, c_int, ctypes.POINTER(A.BlockWeights),
+                                                ctypes.POINTER(M.LayerWeights)]
+        e.glm_engine_set_embedding_rank.argtypes = [c_void_p, c_int, c_void_p, c_void_p, c_void_p]
         e.glm_engine_copy_logits.argtypes = [c_void_p, c_void_p, c_int]
         e.glm_engine_check_error.argtypes = [c_void_p]
         e.glm_engine_set_capture.argtypes = [c_void_p, c_int]
@@ -92,12 +95,12 @@ def lib() -> ctypes.CDLL:
 
 
 def engine_config(shape, max_batch: int, max_seq: int, prefill_chunk: int = 0,
-                  num_cache_pages: int = 0) -> EngineConfig:
+                  num_cache_pages: int = 0, num_gpus: int = 1) -> EngineConfig:
     """EngineConfig of a synth.ModelShape."""
     return EngineConfig(shape.hidden, shape.num_layers, shape.first_dense, shape.num_q_heads, shape.num_kv_heads,
                         shape.head_dim, shape.rotary_dim, shape.vocab_size, shape.num_experts, shape.top_k,
                         shape.moe_intermediate, shape.num_shared, shape.dense_intermediate, shape.rope_theta,
-                        shape.eps, max_batch, max_seq, prefill_chunk, num_cache_pages)
+                        shape.eps, max_batch, max_seq, prefill_chunk, num_cache_pages, num_gpus)
 
 
 def device_bytes(shape, max_batch: int, max_seq: int, prefill_chunk: int = 0, num_cache_pages: int = 0) -> int:
@@ -204,11 +207,16 @@ class NativeEngine:
 
     @classmethod
     def from_weights(cls, shape, weights: dict, max_batch: int, max_seq: int, prefill_chunk: int = 0,
-                     num_cache_pages: int = 0) -> "NativeEngine":
+                     num_cache_pages: int = 0, num_gpus: int = 1) -> "NativeEngine":
         """An engine over device tensors (synth.make_model_weights on a CUDA
         device; layers may share tensors).  The tensors, and the rank-layout
         copies of whole-model attention weights made here, are kept alive by
-        the returned object; `weights` is not modified."""
+        the returned object; `weights` is not modified.  num_gpus > 1: the
+        engine spans the devices from the current one on; each rank's slices
+        (its heads, its experts) are copied to its device here."""
+        if num_gpus > 1:
+            return cls._from_weights_ranks(shape, weights, max_batch, max_seq, prefill_chunk, num_cache_pages,
+                                           num_gpus)
         self = cls(max_batch=max_batch, max_seq=max_seq)
         self.lib = lib()
         cfg = engine_config(shape, max_batch, max_seq, prefill_chunk, num_cache_pages)
@@ -238,6 +246,62 @@ class NativeEngine:
                                     M.ptr(f["w13"]), M.ptr(f["s13"]), M.ptr(f["w2"]), M.ptr(f["s2"]))
                 M.check("glm_engine_set_layer",
                         self.lib.glm_engine_set_layer(self.handle, l, ctypes.byref(aw), ctypes.byref(fw)))
+        except Exception:
+            self.shutdown()
+            raise
+        return self
+
+    @classmethod
+    def _from_weights_ranks(cls, shape, weights: dict, max_batch: int, max_seq: int, prefill_chunk: int,
+                            num_cache_pages: int, n: int) -> "NativeEngine":
+        import torch
+        from . import synth
+        self = cls(max_batch=max_batch, max_seq=max_seq, num_gpus=n)
+        self.lib = lib()
+        dev0 = torch.cuda.current_device()
+        cfg = engine_config(shape, max_batch, max_seq, prefill_chunk, num_cache_pages, n)
+        h = c_void_p()
+        M.check("glm_engine_create", self.lib.glm_engine_create(ctypes.byref(cfg), ctypes.byref(h)))
+        self.handle = h.value
+        self._loaded = True
+        try:
+            own = {}                    # (id of a weight set, rank) -> that rank's copy
+            self._keep = [weights, own]
+
+            def on(t, r):
+                return None if t is None else t.to(torch.device("cuda", dev0 + r)).contiguous()
+
+            for r in range(n):
+                key = ("embed", r)
+                own[key] = {"embed": on(weights["embed"], r)}
+                if r == 0:
+                    own[key]["final_norm"] = on(weights["final_norm"], 0)
+                    own[key]["lm_head"] = on(weights["lm_head"], 0)
+                e = own[key]
+                M.check("glm_engine_set_embedding_rank",
+                        self.lib.glm_engine_set_embedding_rank(self.handle, r, M.ptr(e["embed"]),
+                                                               M.ptr(e.get("final_norm")), M.ptr(e.get("lm_head"))))
+            for l, layer in enumerate(weights["layers"]):
+                a, f = layer["attn"], layer["ffn"]
+                dense = l < shape.first_dense
+                for r in range(n):
+                    if (id(a), r) not in own:
+                        src = a if a.get("w_qkv") is None else None
+                        if src is None:
+                            raise ValueError("several GPUs need whole-model attention weights (w_q/w_k/w_v/w_o)")
+                        own[(id(a), r)] = {k: on(v, r) for k, v in synth.attn_rank_slice(a, shape.attn(), n, r).items()}
+                    if (id(f), r) not in own:
+                        sl = f if dense else synth.expert_slice(f, shape.moe(), n, r)
+                        own[(id(f), r)] = {k: on(v, r) for k, v in sl.items()}
+                    ar, fr = own[(id(a), r)], own[(id(f), r)]
+                    aw = A.BlockWeights(M.ptr(ar["gamma"]), M.ptr(ar["w_qkv"]), M.ptr(ar["s_qkv"]), M.ptr(ar["w_o"]),
+                                        M.ptr(ar["s_o"]))
+                    fw = M.LayerWeights(M.ptr(fr["gamma"]), M.ptr(fr["router_w"]), M.ptr(fr.get("router_bias")),
+                                        M.ptr(fr["w13"]), M.ptr(fr["s13"]), M.ptr(fr["w2"]), M.ptr(fr["s2"]))
+                    M.check("glm_engine_set_layer_rank",
+                            self.lib.glm_engine_set_layer_rank(self.handle, r, l, ctypes.byref(aw),
+                                                               ctypes.byref(fw)))
+            torch.cuda.set_device(dev0)
         except Exception:
             self.shutdown()
             raise
