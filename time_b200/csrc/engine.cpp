@@ -43,6 +43,7 @@
 #include <vector>
 
 #include "engine.h"
+#include "cublas_wrappers.h"
 #include "engine_kernels.h"
 #include "json_lite.h"
 #include "st_loader.h"
@@ -635,6 +636,11 @@ moe_status_t forward_rank(glm_engine* P, int R, int head) {
     const size_t row_bytes = static_cast<size_t>(c.hidden) * 2;
     const size_t nl = P->layers.size();
     void* xfinal = P->x0;
+    // the grouped-GEMM form from the forward's rows, which every rank knows (the
+    // one-GPU rule on R): all ranks of an expert-parallel layer take the same one
+    const int form = c.num_experts > 1 && static_cast<long long>(R) * c.top_k <= 16ll * c.num_experts
+                         ? CBW_GEMM_SMALL_TILES
+                         : CBW_GEMM_FULL_TILES;
     for (size_t l = 0; l < nl; ++l) {
         Layer& L = P->layers[l];
         void* xin = (l & 1) ? P->x2 : P->x0;
@@ -648,8 +654,10 @@ moe_status_t forward_rank(glm_engine* P, int R, int head) {
         if (L.dense)
             ENG_TRY(moe_layer_forward_routed(L.ffn, fin, P->dense_idx, P->dense_w, fout, hi - lo, P->ws, P->ws_bytes,
                                              st));
-        else
+        else {
+            ENG_TRY(moe_layer_set_gemm_form(L.ffn, form));
             ENG_TRY(moe_layer_forward(L.ffn, fin, fout, hi - lo, P->ws, P->ws_bytes, st));
+        }
         for (int r = 0; r < P->world; ++r) G.x[r] = (l & 1) ? E->ranks[r]->x0 : E->ranks[r]->x2;
         ENG_CUDA(tb_engine::rows_allgather(G, xout, lo, hi - lo, c.hidden, P->gather_epoch, P->gather_done,
                                            20000000000ull, P->error_word, st));
