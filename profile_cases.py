@@ -402,7 +402,7 @@ def main() -> int:
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--plain", action="store_true", help="router: the plain-layout router")
     ap.add_argument("--act-planes", type=int, choices=[1, 2], default=1, help="gemm: activation planes")
-    ap.add_argument("--gemm-form", choices=["rule", "one_sm", "pair", "small"], default="rule",
+    ap.add_argument("--gemm-form", choices=["rule", "one_sm", "pair", "small", "token"], default="rule",
                     help="gemm: force a grouped-GEMM form on both GEMMs")
     a = ap.parse_args()
     torch.cuda.set_device(0)
@@ -420,7 +420,7 @@ def main() -> int:
         res = (router(a.tokens, a.iters, a.plain) if a.case == "router"
                else gemm(a.tokens, a.experts, a.iters, not a.no_zipf, a.act_planes,
                          {"rule": 0, "one_sm": M.GEMM_ONE_SM_TILES, "pair": M.GEMM_PAIR_TILES,
-                          "small": M.GEMM_SMALL_TILES}[a.gemm_form]))
+                          "small": M.GEMM_SMALL_TILES, "token": M.GEMM_TOKEN_TILES}[a.gemm_form]))
     print(json.dumps({"case": a.case, "tokens": a.tokens, **res}), flush=True)
     return 0
 

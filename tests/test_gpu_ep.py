@@ -142,12 +142,16 @@ def ep_emulated(shape, w_all, x, ep, routing=None, placement=None, planes=1):
         y = torch.empty(R, H, dtype=torch.bfloat16, device=dev)
         # the GEMM form exactly as every rank's layer picks it: from max_tokens x ep_size (the
         # same on every rank), not from the rank's own token count
-        form = M.GEMM_SMALL_TILES if E > 1 and Tmax * ep * K <= 16 * E else M.GEMM_FULL_TILES
+        # (the down projection takes token-major tiles at decode sizes when H % 256 == 0)
+        small = E > 1 and Tmax * ep * K <= 16 * E
+        form = M.GEMM_SMALL_TILES if small else M.GEMM_FULL_TILES
+        dform = M.GEMM_TOKEN_TILES if small and H % 256 == 0 else form
         if x2:
             form |= M.GEMM_ACT_X2
+            dform |= M.GEMM_ACT_X2
         M.grouped_gemm(M.GEMM_GATED_SWIGLU | form, xp, xps, R, wr["w13"], wr["s13"], counts, start, hq, hs, R, H, I,
                        R, error_word=err)
-        M.grouped_gemm(M.GEMM_DOWN_BF16 | form, hq, hs, R, wr["w2"], wr["s2"], counts, start, y, None, 0, I, H, R,
+        M.grouped_gemm(M.GEMM_DOWN_BF16 | dform, hq, hs, R, wr["w2"], wr["s2"], counts, start, y, None, 0, I, H, R,
                        error_word=err)
         rtot = rk["plan"][5]
         ysend = torch.zeros(max(rtot, 1), H, dtype=torch.bfloat16, device=dev)
