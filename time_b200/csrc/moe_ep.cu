@@ -293,32 +293,59 @@ ep_counts_kernel(const EpPeers P, const int32_t* __restrict__ ecounts, uint32_t 
         for (int i = tid; i < P.ep * P.epr; i += blockDim.x) rcounts[i] = 0;
         return;
     }
+    // every source's counts and this rank's own into shared memory, then one
+    // warp per destination rank sums its plan entries in parallel (the sums
+    // are integers: the order does not matter)
+    extern __shared__ int sh_counts[];
+    const int EE = P.E, ep = P.ep, epr = P.epr, me = P.me;
+    int* stab = sh_counts;              // [ep][E]
+    int* mine_c = sh_counts + ep * EE;  // [E]
     const int32_t* tab = reinterpret_cast<const int32_t*>(P.base[P.me] + P.off_table);   // [ep][E], all sources
-    for (int i = tid; i < P.ep * P.epr; i += blockDim.x) {
-        const int s = i / P.epr, j = i % P.epr;
-        rcounts[i] = tab[static_cast<size_t>(s) * P.E + P.me * P.epr + j];
+    for (int i = tid; i < ep * EE; i += blockDim.x) stab[i] = tab[i];
+    for (int i = tid; i < EE; i += blockDim.x) mine_c[i] = ecounts[i];
+    __syncthreads();
+    for (int i = tid; i < ep * epr; i += blockDim.x) {
+        const int s = i / epr, j = i % epr;
+        rcounts[i] = stab[s * EE + me * epr + j];
     }
+    __shared__ int v_sn[kMaxEpRanks], v_rn[kMaxEpRanks], v_before[kMaxEpRanks], v_ys[kMaxEpRanks];
+    const int warp = tid >> 5, lane = tid & 31, nwarps = blockDim.x >> 5;
+    for (int d = warp; d < ep; d += nwarps) {
+        int sn = 0, rn = 0, before = 0, ys = 0;
+        for (int j = lane; j < epr; j += 32) {
+            sn += mine_c[d * epr + j];                   // my rows for d
+            rn += stab[d * EE + me * epr + j];           // d's rows for me
+        }
+        for (int i = lane; i < me * epr; i += 32) {
+            before += stab[(i / epr) * EE + d * epr + i % epr];   // earlier sources' rows for d
+            ys += stab[d * EE + i];                                // d's rows before mine
+        }
+        for (int o = 16; o > 0; o >>= 1) {
+            sn += __shfl_xor_sync(0xffffffffu, sn, o);
+            rn += __shfl_xor_sync(0xffffffffu, rn, o);
+            before += __shfl_xor_sync(0xffffffffu, before, o);
+            ys += __shfl_xor_sync(0xffffffffu, ys, o);
+        }
+        if (lane == 0) {
+            v_sn[d] = sn;
+            v_rn[d] = rn;
+            v_before[d] = before;
+            v_ys[d] = ys;
+        }
+    }
+    __syncthreads();
     if (tid == 0) {
-        const int ep = P.ep, epr = P.epr, me = P.me;
         int32_t* pl = plan;
         int so = 0, ro = 0;
         for (int d = 0; d < ep; ++d) {
-            int sn = 0, rn = 0, before = 0, ys = 0;
-            for (int j = 0; j < epr; ++j) {
-                sn += ecounts[d * epr + j];                                  // my rows for d
-                rn += tab[static_cast<size_t>(d) * P.E + me * epr + j];     // d's rows for me
-            }
-            for (int s = 0; s < me; ++s)                                      // earlier sources' rows for d
-                for (int j = 0; j < epr; ++j) before += tab[static_cast<size_t>(s) * P.E + d * epr + j];
-            for (int e = 0; e < me * epr; ++e) ys += tab[static_cast<size_t>(d) * P.E + e];   // d's rows before mine
             pl[6 * d + kPlanSoff] = so;
-            pl[6 * d + kPlanSrows] = sn;
-            pl[6 * d + kPlanRoffIn] = before;
+            pl[6 * d + kPlanSrows] = v_sn[d];
+            pl[6 * d + kPlanRoffIn] = v_before[d];
             pl[6 * d + kPlanRecvOff] = ro;
-            pl[6 * d + kPlanRrows] = rn;
-            pl[6 * d + kPlanYsoff] = ys;
-            so += sn;
-            ro += rn;
+            pl[6 * d + kPlanRrows] = v_rn[d];
+            pl[6 * d + kPlanYsoff] = v_ys[d];
+            so += v_sn[d];
+            ro += v_rn[d];
         }
         pl[6 * ep] = so;       // stot
         pl[6 * ep + 1] = ro;   // rtot
@@ -560,7 +587,13 @@ Layout layout(int ep, int E, int recv_cap, size_t row_bytes, size_t y_rows, int 
 
 moe_status_t counts(const Peers& P, const int32_t* ecounts, uint32_t epoch, int32_t* plan, int32_t* rcounts,
                     int* error_word, cudaStream_t st) {
-    ep_counts_kernel<<<1, 256, 0, st>>>(to_dev(P), ecounts, epoch, plan, rcounts, error_word);
+    // the counts of every source and this rank's own, staged in shared memory
+    // (the opt-in is to the largest size once per device, so any layer fits)
+    const size_t smem = (static_cast<size_t>(P.ep) + 1) * P.E * sizeof(int);
+    if (smem > 227 * 1024) return MOE_ERR_UNSUPPORTED;
+    static bool attr[kMaxDevices] = {};
+    if (smem > 48 * 1024 && smem_optin_once(ep_counts_kernel, 227 * 1024, attr) != cudaSuccess) return MOE_ERR_CUDA;
+    ep_counts_kernel<<<1, 256, smem, st>>>(to_dev(P), ecounts, epoch, plan, rcounts, error_word);
     return launch_status();
 }
 
