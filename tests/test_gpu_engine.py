@@ -339,3 +339,32 @@ def test_engine_top_p_sampling(gpu, model):
             assert lo <= target * (1 + 1e-4) and cum[tok] >= target * (1 - 1e-4), (i, tok)
             past[i] += 1
     eng.shutdown()
+
+
+def test_engine_decode_graphs_bit_identical(gpu, model, monkeypatch):
+    """Pure decode steps replay a CUDA graph of the whole forward (captured
+    the second time a row count occurs): logits and tokens of six steps equal
+    the eager engine's (TIME_B200_ENGINE_GRAPHS=0), including after a request
+    finishes and the row count changes."""
+    _, w_dev = model
+    rng = np.random.default_rng(12)
+    prompts = [list(map(int, rng.integers(0, SHAPE.vocab_size, L))) for L in (7, 19, 33)]
+
+    def run(graphs):
+        monkeypatch.setenv("TIME_B200_ENGINE_GRAPHS", "1" if graphs else "0")
+        eng = EN.NativeEngine.from_weights(SHAPE, w_dev, max_batch=4, max_seq=96, prefill_chunk=64)
+        st = [eng.prefill(i, p, 0.0, 1.0, 1.0, 4 if i == 1 else 16) for i, p in enumerate(prompts)]
+        out = []
+        finished = [False] * len(st)
+        for _ in range(6):
+            rows = finished.count(False)          # rows of this step: the requests not finished before it
+            r = eng.batch_decode_raw(st)
+            out.append(([t for t, _ in r], eng.copy_logits(rows)))
+            finished = [f or d for f, (_, d) in zip(finished, r)]
+        eng.check_error()
+        eng.shutdown()
+        return out
+    a, b = run(True), run(False)
+    for (ta, la), (tb, lb) in zip(a, b):
+        assert ta == tb
+        assert np.array_equal(la, lb)

@@ -33,8 +33,10 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <new>
 #include <string>
@@ -156,6 +158,12 @@ struct glm_engine {
     unsigned int* gather_done = nullptr;
     std::vector<void*> peer_bufs;    // attention / FFN peer buffers this rank allocated
     moe_status_t thread_status = MOE_OK;
+    // one GPU: a pure decode step of R rows replays a CUDA graph of the whole
+    // forward (stage copy, 92 layers, head, token copy), captured the second
+    // time R occurs; off with TIME_B200_ENGINE_GRAPHS=0, timing or routing capture
+    bool graphs_ok = true;
+    std::map<int, cudaGraphExec_t> graph_exec;
+    std::map<int, int> graph_seen;
 };
 
 namespace {
@@ -216,6 +224,8 @@ cudaError_t dev_alloc(T** p, size_t bytes) {
 void destroy_one(glm_engine* E) {
     if (!E) return;
     if (E->stream) cudaStreamSynchronize(E->stream);
+    for (auto& kv : E->graph_exec) cudaGraphExecDestroy(kv.second);
+    E->graph_exec.clear();
     for (Request* r : E->requests) delete r;
     E->requests.clear();
     for (Layer& L : E->layers) {
@@ -258,6 +268,10 @@ moe_status_t create_one(const glm_engine_config_t* cfg, int rank, int world, glm
     E->rank = rank;
     E->world = world;
     E->root = E;
+    {
+        const char* g = std::getenv("TIME_B200_ENGINE_GRAPHS");
+        E->graphs_ok = !(g && g[0] == '0');
+    }
     if (E->cfg.prefill_chunk <= 0) E->cfg.prefill_chunk = 2048;
     const Plan p = make_plan(E->cfg);
     E->rows_cap = p.rows_cap;
@@ -524,7 +538,7 @@ void set_events(glm_engine* E, bool on) {
 // head > 0: rows [R - head, R) also go through the final norm, the lm_head
 // and the sampler (per-row parameters at stage indices 0..head-1), and the
 // tokens come back to tokens_host.
-moe_status_t forward_one(glm_engine* E, int R, int head) {
+moe_status_t forward_one(glm_engine* E, int R, int head, bool sync = true) {
     const bool sample = head > 0;
     const glm_engine_config_t& c = E->cfg;
     cudaStream_t st = E->stream;
@@ -589,6 +603,7 @@ moe_status_t forward_one(glm_engine* E, int R, int head) {
                                     st));
     if (tm) cudaEventRecord(E->events[2 + 2 * nl], st);
     ENG_CUDA(cudaMemcpyAsync(E->tokens_host, E->tokens_out, static_cast<size_t>(head) * 8, cudaMemcpyDeviceToHost, st));
+    if (!sync) return MOE_OK;   // being captured into a graph
     ENG_CUDA(cudaStreamSynchronize(st));
     if (tm) {
         float ms = 0.0f, attn = 0.0f, ffn = 0.0f;
@@ -699,8 +714,49 @@ moe_status_t forward_rank(glm_engine* P, int R, int head) {
 }
 
 // One forward: on one GPU, or every rank on its own host thread.
+// A pure decode step of R rows on one GPU from a CUDA graph of the whole
+// forward: the first time R occurs it runs eagerly (every lazy setup --
+// shared-memory opt-ins, library handles -- happens outside the capture), the
+// second time it is captured (stage copy from the pinned staging buffer
+// included, so every replay reads the step's own rows), then replayed.  A
+// capture that fails leaves the engine eager for good.
+moe_status_t forward_graph(glm_engine* E, int R) {
+    auto it = E->graph_exec.find(R);
+    if (it == E->graph_exec.end()) {
+        if (++E->graph_seen[R] < 2) return forward_one(E, R, R);
+        cudaStream_t st = E->stream;
+        if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+            cudaGetLastError();
+            E->graphs_ok = false;
+            return forward_one(E, R, R);
+        }
+        moe_status_t s = cudaMemcpyAsync(E->stage_dev, E->stage_host, E->stage.bytes, cudaMemcpyHostToDevice, st) ==
+                                 cudaSuccess
+                             ? MOE_OK
+                             : MOE_ERR_CUDA;
+        if (s == MOE_OK) s = forward_one(E, R, R, false);
+        cudaGraph_t g = nullptr;
+        const cudaError_t e = cudaStreamEndCapture(st, &g);
+        cudaGraphExec_t x = nullptr;
+        if (s != MOE_OK || e != cudaSuccess || !g || cudaGraphInstantiate(&x, g, 0) != cudaSuccess) {
+            if (g) cudaGraphDestroy(g);
+            cudaGetLastError();
+            E->graphs_ok = false;
+            return forward_one(E, R, R);
+        }
+        cudaGraphDestroy(g);
+        it = E->graph_exec.emplace(R, x).first;
+    }
+    ENG_CUDA(cudaGraphLaunch(it->second, E->stream));
+    ENG_CUDA(cudaStreamSynchronize(E->stream));
+    return MOE_OK;
+}
+
 moe_status_t forward(glm_engine* E, int R, int head) {
-    if (E->world == 1) return forward_one(E, R, head);
+    if (E->world == 1) {
+        if (head == R && head > 0 && E->graphs_ok && !E->timing && !E->cap_idx) return forward_graph(E, R);
+        return forward_one(E, R, head);
+    }
     std::vector<std::thread> th;
     th.reserve(E->world - 1);
     for (int r = 1; r < E->world; ++r) {
