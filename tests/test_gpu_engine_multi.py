@@ -115,3 +115,21 @@ def test_engine_two_gpus_from_checkpoint(model, tmp_path):
     assert ta == tb
     for s in range(3):
         assert np.array_equal(la[s], lb[s])
+
+
+def test_engine_two_gpus_decode_graphs(model, monkeypatch):
+    """Decode steps replayed from per-rank CUDA graphs (the exchanges keep
+    their epochs on the device) give the eager engine's logits and tokens."""
+    _, w_dev = model
+    rng = np.random.default_rng(13)
+    prompts = [rng.integers(0, SHAPE.vocab_size, L) for L in (6, 23, 11)]
+    out = {}
+    for graphs in ("1", "0"):
+        monkeypatch.setenv("TIME_B200_ENGINE_GRAPHS", graphs)
+        eng = EN.NativeEngine.from_weights(SHAPE, w_dev, max_batch=4, max_seq=96, prefill_chunk=64, num_gpus=2)
+        out[graphs] = run(eng, prompts, 6)
+        eng.shutdown()
+    (lg, tg), (le, te) = out["1"], out["0"]
+    assert tg == te
+    for a, b in zip(lg, le):
+        assert np.array_equal(a, b)

@@ -629,7 +629,7 @@ moe_status_t forward_one(glm_engine* E, int R, int head, bool sync = true) {
 // before the next layer; the layers alternate between x0 and x2 so that a
 // rank that is ahead never overwrites rows another rank still reads.  Rank 0
 // then runs the head on the sampled rows.
-moe_status_t forward_rank(glm_engine* P, int R, int head) {
+moe_status_t forward_rank(glm_engine* P, int R, int head, bool sync = true) {
     glm_engine* E = P->root;
     const glm_engine_config_t& c = P->cfg;
     ENG_CUDA(cudaSetDevice(P->device));
@@ -678,7 +678,10 @@ moe_status_t forward_rank(glm_engine* P, int R, int head) {
                                            20000000000ull, P->error_word, st));
         xfinal = xout;
     }
-    if (P->rank != 0 || !sample) return cudaStreamSynchronize(st) == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+    if (P->rank != 0 || !sample) {
+        if (!sync) return MOE_OK;
+        return cudaStreamSynchronize(st) == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+    }
     if (tm) cudaEventRecord(E->events[1 + 2 * nl], st);
     const void* head_x = static_cast<const uint8_t*>(xfinal) + static_cast<size_t>(R - head) * row_bytes;
     ENG_CUDA(tb_engine::final_norm_rows(head_x, P->final_norm, head, c.hidden, c.rms_eps, P->xn, st));
@@ -694,6 +697,7 @@ moe_status_t forward_rank(glm_engine* P, int R, int head) {
                                     st));
     if (tm) cudaEventRecord(E->events[2 + 2 * nl], st);
     ENG_CUDA(cudaMemcpyAsync(E->tokens_host, P->tokens_out, static_cast<size_t>(head) * 8, cudaMemcpyDeviceToHost, st));
+    if (!sync) return MOE_OK;   // being captured into a graph
     ENG_CUDA(cudaStreamSynchronize(st));
     if (tm) {
         float ms = 0.0f, attn = 0.0f, ffn = 0.0f;
@@ -710,6 +714,40 @@ moe_status_t forward_rank(glm_engine* P, int R, int head) {
         cudaEventElapsedTime(&ms, E->events[1 + 2 * nl], E->events[2 + 2 * nl]);
         E->stage_ms[3] = ms;
     }
+    return MOE_OK;
+}
+
+// Rank P's pure decode step of R rows from a CUDA graph of its part of the
+// forward, as forward_graph on one GPU (every rank sees the same sequence of
+// row counts, so all ranks replay, capture or run eagerly in the same step;
+// the exchanges keep their epochs on the device, so a replay pairs up with
+// the other ranks' eager or replayed kernels).
+moe_status_t forward_rank_graph(glm_engine* P, int R) {
+    ENG_CUDA(cudaSetDevice(P->device));
+    auto it = P->graph_exec.find(R);
+    if (it == P->graph_exec.end()) {
+        if (++P->graph_seen[R] < 2 || !P->graphs_ok) return forward_rank(P, R, R);
+        cudaStream_t st = P->stream;
+        if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+            cudaGetLastError();
+            P->graphs_ok = false;
+            return forward_rank(P, R, R);
+        }
+        const moe_status_t s = forward_rank(P, R, R, false);
+        cudaGraph_t g = nullptr;
+        const cudaError_t e = cudaStreamEndCapture(st, &g);
+        cudaGraphExec_t x = nullptr;
+        if (s != MOE_OK || e != cudaSuccess || !g || cudaGraphInstantiate(&x, g, 0) != cudaSuccess) {
+            if (g) cudaGraphDestroy(g);
+            cudaGetLastError();
+            P->graphs_ok = false;
+            return forward_rank(P, R, R);
+        }
+        cudaGraphDestroy(g);
+        it = P->graph_exec.emplace(R, x).first;
+    }
+    ENG_CUDA(cudaGraphLaunch(it->second, P->stream));
+    ENG_CUDA(cudaStreamSynchronize(P->stream));
     return MOE_OK;
 }
 
@@ -757,13 +795,16 @@ moe_status_t forward(glm_engine* E, int R, int head) {
         if (head == R && head > 0 && E->graphs_ok && !E->timing && !E->cap_idx) return forward_graph(E, R);
         return forward_one(E, R, head);
     }
+    const bool graph = head == R && head > 0 && E->graphs_ok && !E->timing;
     std::vector<std::thread> th;
     th.reserve(E->world - 1);
     for (int r = 1; r < E->world; ++r) {
         glm_engine* P = E->ranks[r];
-        th.emplace_back([P, R, head]() { P->thread_status = forward_rank(P, R, head); });
+        th.emplace_back([P, R, head, graph]() {
+            P->thread_status = graph ? forward_rank_graph(P, R) : forward_rank(P, R, head);
+        });
     }
-    const moe_status_t s0 = forward_rank(E, R, head);
+    const moe_status_t s0 = graph ? forward_rank_graph(E, R) : forward_rank(E, R, head);
     for (std::thread& t : th) t.join();
     cudaSetDevice(E->device);
     if (s0 != MOE_OK) return s0;

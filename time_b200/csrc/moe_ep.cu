@@ -38,7 +38,7 @@
 //   table [ep][E] i32            every rank's per-expert send counts
 //   recv  [recv_cap][rb]         packed rows dispatched to this rank
 //   yrecv [T*k][H] bf16          expert outputs returned to this rank
-// Per forward (epoch e = 1, 2, ...): ep_counts_kernel writes this rank's
+// Per forward (epoch e = 1, 2, ..., counted on the device): ep_counts_kernel writes this rank's
 // counts into every table and raises flags[0][me] = e on every rank, waits for
 // all ranks' flags, then derives the whole exchange plan on the device;
 // ep_dispatch_kernel packs each sent row straight into its destination's recv
@@ -273,7 +273,8 @@ __device__ bool signal_and_wait(const EpPeers& P, int phase, uint32_t epoch) {
 
 // Single block: counts into every table, barrier, then the exchange plan.
 __global__ void __launch_bounds__(256)
-ep_counts_kernel(const EpPeers P, const int32_t* __restrict__ ecounts, uint32_t epoch, int32_t* __restrict__ plan,
+ep_counts_kernel(const EpPeers P, const int32_t* __restrict__ ecounts, uint32_t* __restrict__ epoch_dev,
+                 int32_t* __restrict__ plan,
                  int32_t* __restrict__ rcounts, int* __restrict__ error_word) {
     const int tid = threadIdx.x;
     for (int d = 0; d < P.ep; ++d) {
@@ -283,7 +284,12 @@ ep_counts_kernel(const EpPeers P, const int32_t* __restrict__ ecounts, uint32_t 
     __threadfence_system();
     __syncthreads();
     __shared__ int ok;
-    if (tid == 0) ok = signal_and_wait(P, kFlagCounts, epoch) ? 1 : 0;
+    if (tid == 0) {
+        // the forward's epoch lives on the device (a captured graph replays with the next one)
+        const uint32_t epoch = *epoch_dev + 1u;
+        *epoch_dev = epoch;
+        ok = signal_and_wait(P, kFlagCounts, epoch) ? 1 : 0;
+    }
     __syncthreads();
     if (!ok) {
         if (tid == 0) {
@@ -414,8 +420,9 @@ ep_combine_send_kernel(const EpPeers P, const uint8_t* __restrict__ y, const int
     __threadfence_system();
 }
 
-__global__ void ep_signal_wait_kernel(const EpPeers P, int phase, uint32_t epoch, int* __restrict__ error_word) {
-    if (threadIdx.x == 0 && !signal_and_wait(P, phase, epoch) && error_word) atomicExch(error_word, 3);
+__global__ void ep_signal_wait_kernel(const EpPeers P, int phase, const uint32_t* __restrict__ epoch_dev,
+                                      int* __restrict__ error_word) {
+    if (threadIdx.x == 0 && !signal_and_wait(P, phase, *epoch_dev) && error_word) atomicExch(error_word, 3);
 }
 
 inline int grid_for_rows(int rows) {
@@ -585,7 +592,7 @@ Layout layout(int ep, int E, int recv_cap, size_t row_bytes, size_t y_rows, int 
     return L;
 }
 
-moe_status_t counts(const Peers& P, const int32_t* ecounts, uint32_t epoch, int32_t* plan, int32_t* rcounts,
+moe_status_t counts(const Peers& P, const int32_t* ecounts, uint32_t* epoch_dev, int32_t* plan, int32_t* rcounts,
                     int* error_word, cudaStream_t st) {
     // the counts of every source and this rank's own, staged in shared memory
     // (the opt-in is to the largest size once per device, so any layer fits)
@@ -593,7 +600,7 @@ moe_status_t counts(const Peers& P, const int32_t* ecounts, uint32_t epoch, int3
     if (smem > 227 * 1024) return MOE_ERR_UNSUPPORTED;
     static bool attr[kMaxDevices] = {};
     if (smem > 48 * 1024 && smem_optin_once(ep_counts_kernel, 227 * 1024, attr) != cudaSuccess) return MOE_ERR_CUDA;
-    ep_counts_kernel<<<1, 256, smem, st>>>(to_dev(P), ecounts, epoch, plan, rcounts, error_word);
+    ep_counts_kernel<<<1, 256, smem, st>>>(to_dev(P), ecounts, epoch_dev, plan, rcounts, error_word);
     return launch_status();
 }
 
@@ -607,8 +614,8 @@ moe_status_t dispatch(const Peers& P, const void* xq, const void* xq_lo, const f
     return launch_status();
 }
 
-moe_status_t signal_wait(const Peers& P, int phase, uint32_t epoch, int* error_word, cudaStream_t st) {
-    ep_signal_wait_kernel<<<1, 32, 0, st>>>(to_dev(P), phase, epoch, error_word);
+moe_status_t signal_wait(const Peers& P, int phase, const uint32_t* epoch_dev, int* error_word, cudaStream_t st) {
+    ep_signal_wait_kernel<<<1, 32, 0, st>>>(to_dev(P), phase, epoch_dev, error_word);
     return launch_status();
 }
 

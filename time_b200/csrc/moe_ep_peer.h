@@ -31,12 +31,13 @@ struct Peers {
 // plan (device int32): 6 per rank + stot + rtot
 inline int plan_ints(int ep) { return 6 * ep + 2; }
 
-moe_status_t counts(const Peers& P, const int32_t* ecounts, uint32_t epoch, int32_t* plan, int32_t* rcounts,
+// epoch_dev: this rank's forward counter on the device (counts() increments it)
+moe_status_t counts(const Peers& P, const int32_t* ecounts, uint32_t* epoch_dev, int32_t* plan, int32_t* rcounts,
                     int* error_word, cudaStream_t st);
 moe_status_t dispatch(const Peers& P, const void* xq, const void* xq_lo, const float* xs, int xs_ld,
                       const int32_t* stok, const int32_t* plan, int H, size_t row_bytes, int recv_cap, int max_rows,
                       cudaStream_t st);
-moe_status_t signal_wait(const Peers& P, int phase, uint32_t epoch, int* error_word, cudaStream_t st);
+moe_status_t signal_wait(const Peers& P, int phase, const uint32_t* epoch_dev, int* error_word, cudaStream_t st);
 moe_status_t combine_send(const Peers& P, const void* y_bf16, const int32_t* recv_dst, const int32_t* plan,
                           int H, int y_cap, int y_rows, int max_rows, cudaStream_t st);
 

@@ -73,7 +73,7 @@ struct moe_layer {
     bool peer_mode;
     int32_t* slot_of_expert;   // device [E] or NULL (contiguous placement)
     tbep::Peers peers;
-    uint32_t epoch;
+    uint32_t* epoch_dev;   // peer exchange: the forward counter, on the device
     size_t off_plan;
     int gemm_form;        // 0 = by the rule in gemm_form(), else a CBW_GEMM_*_TILES flag
     int act_planes = 1;   // 1: e4m3 activations; 2: two-term e4m3 (hi + lo residual)
@@ -273,7 +273,7 @@ moe_status_t run_experts_ep(moe_layer* L, const int32_t* idx, const float* wts, 
         const tbep::Peers& P = L->peers;
         uint8_t* mine = static_cast<uint8_t*>(P.base[c.ep_rank]);
         int32_t* plan = at<int32_t>(ws, L->off_plan);
-        const uint32_t epoch = ++L->epoch;
+        uint32_t* epoch = L->epoch_dev;   // advanced on the device by the counts exchange
         const int y_cap = c.max_tokens * K;
         mark(L, 2, st);
         MOE_TRY(moe_permute_mb(sort_ids, T, K, 0, E, 0, ecounts, at<int32_t>(ws, L->off_estart), spos, stok, stotal,
@@ -428,6 +428,7 @@ moe_status_t moe_layer_destroy(moe_layer_t* L) {
     if (!L) return MOE_OK;
     if (L->slot_of_expert) cudaFree(L->slot_of_expert);
     if (L->h_counts) cudaFreeHost(L->h_counts);
+    if (L->epoch_dev) cudaFree(L->epoch_dev);
     cudaFree(L->error_word);
     delete L;
     return MOE_OK;
@@ -588,7 +589,11 @@ moe_status_t moe_layer_set_peer_buffers(moe_layer_t* L, void* const* peer_bufs, 
                                 static_cast<size_t>(c.max_tokens) * c.top_k, c.hidden);
     const int ms = L->sync_timeout_ms < 20000 ? L->sync_timeout_ms : 20000;   // device waits: at most 20 s
     L->peers.timeout_ns = static_cast<unsigned long long>(ms) * 1000000ull;
-    L->epoch = 0;
+    if (!L->epoch_dev && cudaMalloc(&L->epoch_dev, sizeof(uint32_t)) != cudaSuccess) {
+        L->epoch_dev = nullptr;
+        return MOE_ERR_CUDA;
+    }
+    if (cudaMemset(L->epoch_dev, 0, sizeof(uint32_t)) != cudaSuccess) return MOE_ERR_CUDA;
     L->peer_mode = true;
     return MOE_OK;
 }
