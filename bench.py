@@ -552,10 +552,23 @@ def run_ours(args):
     # ---- device-resident timed region with per-stage events
     K = args.steps
     stage_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(M.NUM_STAGES + 1)] for _ in range(K)]
+    for evs in stage_ev:            # create the CUDA events outside the timed loop
+        for e in evs:
+            e.record(stream)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    torch.cuda.synchronize()
+    gate = torch.zeros(1, device=dev)
+
+    def device_gate():
+        # the timed region starts when every GPU has left one tiny all-reduce
+        # queued on the stream, so a rank whose host starts late (NVML start-up
+        # of the clock sampler, Python) does not charge its delay to the others
+        if world > 1:
+            dist.all_reduce(gate)
+
     with ClockSampler(local) as clk:
+        barrier()
+        torch.cuda.synchronize()
+        device_gate()
         start.record(stream)
         for i in range(K):
             layer.set_stage_events(stage_ev[i])
@@ -622,6 +635,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     barrier()
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    device_gate()
     e_start.record(stream)
     s_in.wait_event(e_start)
     for i in range(K):
