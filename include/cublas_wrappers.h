@@ -161,6 +161,18 @@ typedef struct {
 cbwStatus_t cbwFp8BlockScaledGroupedGemm(const cbwGroupedGemmArgs* args, int* error_word,
                                          cwStream_t stream);
 
+/* Extension (no reference counterpart): the down projection with one output
+ * address per row, the expert-parallel return fused into the GEMM.
+ * row_out: device array [rows] of bf16 row addresses (N * 2 bytes each,
+ * 16-byte aligned), nullptr for rows that go to args->out as usual; an
+ * address may lie in another GPU's memory (peer mapping).  Every storing
+ * thread fences at system scope before the grid ends, so a flag raised by the
+ * next launch on the stream orders all rows before it.  Only the token-major
+ * down form takes row addresses: CBW_ERROR_NOT_SUPPORTED (nothing launched)
+ * when the mode or the shape selects another form. */
+cbwStatus_t cbwFp8BlockScaledGroupedGemmRowOut(const cbwGroupedGemmArgs* args, void* const* row_out,
+                                               int* error_word, cwStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

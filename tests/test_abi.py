@@ -29,7 +29,7 @@ HEADER_LIB = {
 # the reference's exported symbol counts per header
 REFERENCE_COUNTS = {"kernels.h": ("launch_", 20), "cublas_wrappers.h": ("cbw", 17),
                     "nccl_wrappers.h": ("ncw", 15), "cuda_wrappers.h": ("cw", 22)}
-REFERENCE_NEW = {"cublas_wrappers.h": {"cbwFp8BlockScaledGroupedGemm"},
+REFERENCE_NEW = {"cublas_wrappers.h": {"cbwFp8BlockScaledGroupedGemm", "cbwFp8BlockScaledGroupedGemmRowOut"},
                  "nccl_wrappers.h": {"ncwAllToAllv", "ncwCommInitRankTimeout", "ncwCommGetAsyncError",
                                      "ncwCommAbort", "ncwStreamSynchronizeTimeout"}}
 

@@ -30,8 +30,8 @@ def free_port() -> int:
     return port
 
 
-def launch(nproc: int, *args: str) -> subprocess.CompletedProcess:
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0", TIME_B200_EP_TIMEOUT_MS="60000")
+def launch(nproc: int, *args: str, extra_env=None) -> subprocess.CompletedProcess:
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", TIME_B200_EP_TIMEOUT_MS="60000", **(extra_env or {}))
     for _ in range(3):
         cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
                f"--nproc-per-node={nproc}", "--master-addr", "127.0.0.1", "--master-port", str(free_port()),
@@ -54,6 +54,21 @@ def test_ep_bit_identical(gpu, args, exchange):
         pytest.skip("needs >= 2 GPUs")
     nproc = 8 if n >= 8 else (4 if n >= 4 else 2)
     r = launch(nproc, *args, "--exchange", exchange)
+    assert r.returncode == 0 and "EP_OK" in r.stdout, (r.stdout[-3000:], r.stderr[-3000:])
+
+
+@pytest.mark.parametrize("fused", ["1", "0"])
+@pytest.mark.parametrize("args", [("--shape", "glm", "--tokens", "4096", "--act-planes", "2"),
+                                  ("--shape", "glm", "--tokens", "64", "--repeats", "3")])
+def test_ep_peer_return_forms_bit_identical(gpu, args, fused):
+    """The peer exchange's two return paths: the down GEMM storing each
+    output row into its owner's buffer (default at hidden % 256 == 0) and the
+    separate copy kernel after the GEMM."""
+    n = n_gpus()
+    if n < 2:
+        pytest.skip("needs >= 2 GPUs")
+    nproc = 8 if n >= 8 else (4 if n >= 4 else 2)
+    r = launch(nproc, *args, "--exchange", "peer", extra_env={"TIME_B200_EP_FUSED_RETURN": fused})
     assert r.returncode == 0 and "EP_OK" in r.stdout, (r.stdout[-3000:], r.stderr[-3000:])
 
 

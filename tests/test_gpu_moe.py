@@ -516,6 +516,61 @@ def test_grouped_gemm_pair_matches_one_sm(gpu, gated, counts, K):
                 assert torch.equal(a_, b_), (other, gi)
 
 
+@pytest.mark.parametrize("x2", [False, True])
+@pytest.mark.parametrize("counts,K", [([16], 256), ([1, 0, 130, 255, 300, 17], 512), ([1000, 3, 129], 1536)])
+def test_grouped_gemm_row_out_scatters_rows(gpu, counts, K, x2):
+    """cbwFp8BlockScaledGroupedGemmRowOut (the down projection storing rows at
+    per-row addresses, the expert-parallel return): every row with an address
+    lands there with the bits the token-major form writes to out, rows without
+    one go to out, and no other byte of either buffer changes."""
+    N = 512
+    g = torch.Generator().manual_seed(303 + sum(counts) + x2)
+    starts, rows, A, A_s, a_ld, W, W_s = _make_groups(counts, K, N, g)
+    A2 = torch.cat([A, torch.randint(0, 256, A.shape, generator=g, dtype=torch.uint8) & 0x77]) if x2 else A
+    mode = M.GEMM_DOWN_BF16 | M.GEMM_TOKEN_TILES | (M.GEMM_ACT_X2 if x2 else 0)
+    cnt = torch.tensor(counts, dtype=torch.int32, device=gpu)
+    st = torch.tensor(starts, dtype=torch.int32, device=gpu)
+    args = (A2.to(gpu), A_s.to(gpu), a_ld, W.to(gpu), W_s.to(gpu), cnt, st)
+    err = torch.zeros(1, dtype=torch.int32, device=gpu)
+    ref = torch.full((rows, N), float("nan"), dtype=torch.bfloat16, device=gpu)
+    M.grouped_gemm(mode, *args, ref, None, 0, K, N, rows, error_word=err)
+    # every other live row goes to a second buffer at a shuffled position
+    live = [s0 + i for s0, c in zip(starts, counts) for i in range(c)]
+    far = torch.full((rows + 7, N), -3.0, dtype=torch.bfloat16, device=gpu)
+    perm = torch.randperm(rows + 7, generator=g).tolist()
+    addr = torch.zeros(rows, dtype=torch.int64)
+    sent = {}
+    for j, r in enumerate(live):
+        if j % 2 == 0:
+            sent[r] = perm[j]
+            addr[r] = far.data_ptr() + perm[j] * N * 2
+    out = torch.full((rows, N), -5.0, dtype=torch.bfloat16, device=gpu)
+    M.grouped_gemm(mode, *args, out, None, 0, K, N, rows, error_word=err, row_out=addr.to(gpu))
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    ref_c, out_c, far_c = ref.cpu().view(torch.int16), out.cpu().view(torch.int16), far.cpu().view(torch.int16)
+    untouched_out = torch.full((N,), -5.0, dtype=torch.bfloat16).view(torch.int16)
+    untouched_far = torch.full((N,), -3.0, dtype=torch.bfloat16).view(torch.int16)
+    for r in live:
+        if r in sent:
+            assert torch.equal(far_c[sent[r]], ref_c[r]), r
+            assert torch.equal(out_c[r], untouched_out), r
+        else:
+            assert torch.equal(out_c[r], ref_c[r]), r
+    targets = set(sent.values())
+    for q in range(rows + 7):
+        if q not in targets:
+            assert torch.equal(far_c[q], untouched_far), q
+    liveset = set(live)
+    for r in range(rows):
+        if r not in liveset:
+            assert torch.equal(out_c[r], untouched_out), r
+    # a form that takes no row addresses is refused, nothing launched
+    with pytest.raises(M.MoEError):
+        M.grouped_gemm(M.GEMM_DOWN_BF16 | M.GEMM_ONE_SM_TILES, A.to(gpu), A_s.to(gpu), a_ld, W.to(gpu), W_s.to(gpu),
+                       cnt, st, out, None, 0, K, N, rows, error_word=err, row_out=addr.to(gpu))
+
+
 @pytest.mark.parametrize("gated", [False, True])
 def test_grouped_gemm_small_tiles_placement_independent(gpu, gated):
     """The decode form's result for a row does not depend on where its tile

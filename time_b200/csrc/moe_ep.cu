@@ -420,6 +420,34 @@ ep_combine_send_kernel(const EpPeers P, const uint8_t* __restrict__ y, const int
     __threadfence_system();
 }
 
+// Thread per GEMM row: the address its down-projection output goes to when the
+// GEMM returns rows itself -- a received row's place in its token owner's
+// yrecv (the row ep_combine_send_kernel would copy there), nullptr for this
+// rank's shared-expert and padding rows, which stay in the local y.
+__global__ void __launch_bounds__(256)
+ep_return_rows_kernel(const EpPeers P, const int32_t* __restrict__ row_src, const int32_t* __restrict__ total_rows,
+                      const int32_t* __restrict__ plan, size_t row_bytes, int ycap, int row_capacity,
+                      void** __restrict__ row_out) {
+    __shared__ int s_roff[kMaxEpRanks], s_ys[kMaxEpRanks];
+    for (int d = threadIdx.x; d < P.ep; d += blockDim.x) {
+        s_roff[d] = plan[6 * d + kPlanRecvOff];
+        s_ys[d] = plan[6 * d + kPlanYsoff];
+    }
+    __syncthreads();
+    const int R = min(*total_rows, row_capacity);
+    for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < R; r += gridDim.x * blockDim.x) {
+        const int sb = row_src[r];
+        void* dst = nullptr;
+        if (sb >= 0) {
+            int s = P.ep - 1;
+            while (s > 0 && s_roff[s] > sb) --s;
+            const int dest = s_ys[s] + (sb - s_roff[s]);
+            if (dest >= 0 && dest < ycap) dst = P.base[s] + P.off_yrecv + static_cast<size_t>(dest) * row_bytes;
+        }
+        row_out[r] = dst;
+    }
+}
+
 __global__ void ep_signal_wait_kernel(const EpPeers P, int phase, const uint32_t* __restrict__ epoch_dev,
                                       int* __restrict__ error_word) {
     if (threadIdx.x == 0 && !signal_and_wait(P, phase, *epoch_dev) && error_word) atomicExch(error_word, 3);
@@ -616,6 +644,16 @@ moe_status_t dispatch(const Peers& P, const void* xq, const void* xq_lo, const f
 
 moe_status_t signal_wait(const Peers& P, int phase, const uint32_t* epoch_dev, int* error_word, cudaStream_t st) {
     ep_signal_wait_kernel<<<1, 32, 0, st>>>(to_dev(P), phase, epoch_dev, error_word);
+    return launch_status();
+}
+
+moe_status_t return_rows(const Peers& P, const int32_t* row_src, const int32_t* total_rows, const int32_t* plan,
+                         int H, int y_cap, int row_capacity, void** row_out, cudaStream_t st) {
+    if (row_capacity <= 0) return MOE_OK;
+    int blocks = (row_capacity + 255) / 256;
+    if (blocks > 148 * 4) blocks = 148 * 4;
+    ep_return_rows_kernel<<<blocks, 256, 0, st>>>(to_dev(P), row_src, total_rows, plan, static_cast<size_t>(H) * 2,
+                                                  y_cap, row_capacity, row_out);
     return launch_status();
 }
 

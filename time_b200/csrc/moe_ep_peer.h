@@ -38,6 +38,11 @@ moe_status_t dispatch(const Peers& P, const void* xq, const void* xq_lo, const f
                       const int32_t* stok, const int32_t* plan, int H, size_t row_bytes, int recv_cap, int max_rows,
                       cudaStream_t st);
 moe_status_t signal_wait(const Peers& P, int phase, const uint32_t* epoch_dev, int* error_word, cudaStream_t st);
+// row_out[r] (r < *total_rows): where GEMM row r's down-projection output
+// belongs -- a received row's slot in its owner's yrecv, nullptr for rows that
+// stay local -- for cbwFp8BlockScaledGroupedGemmRowOut (replaces combine_send)
+moe_status_t return_rows(const Peers& P, const int32_t* row_src, const int32_t* total_rows, const int32_t* plan,
+                         int H, int y_cap, int row_capacity, void** row_out, cudaStream_t st);
 moe_status_t combine_send(const Peers& P, const void* y_bf16, const int32_t* recv_dst, const int32_t* plan,
                           int H, int y_cap, int y_rows, int max_rows, cudaStream_t st);
 

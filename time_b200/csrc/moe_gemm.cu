@@ -139,6 +139,10 @@ struct GemmParams {
     int N;                  // output columns per group
     int w_rows;             // weight rows per group (2N gated, N down)
     int* error_word;
+    // token-major down form only: [rows] address of each output row (nullptr:
+    // the row goes to out), e.g. the token owner's return buffer in another
+    // GPU's memory; every epilogue thread fences at system scope at its end
+    void* const* row_out = nullptr;
 };
 
 struct TileCoord {
@@ -1020,8 +1024,12 @@ grouped_fp8_gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w,
                     const __nv_bfloat162 h2 = __floats2bfloat162_rn(acc2[i].x, acc2[i].y);
                     w[i] = *reinterpret_cast<const uint32_t*>(&h2);
                 }
-                uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + row * p.N +
-                                                    tc.nb * C::kWRows + colgrp * 64);
+                __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(p.out) + row * p.N;
+                if (p.row_out) {
+                    void* dst = p.row_out[row];
+                    if (dst) orow = static_cast<__nv_bfloat16*>(dst);
+                }
+                uint4* o = reinterpret_cast<uint4*>(orow + tc.nb * C::kWRows + colgrp * 64);
 #pragma unroll
                 for (int i = 0; i < 8; ++i) o[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
             }
@@ -1029,6 +1037,9 @@ grouped_fp8_gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w,
     }
 
     // ---------------------------------------------------------------- teardown
+    // rows stored to other GPUs are visible system-wide before the grid ends,
+    // so a flag raised by the next launch on the stream orders them
+    if (!kGated && p.row_out) __threadfence_system();
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
@@ -1696,7 +1707,8 @@ cbwStatus_t launch_gemm(const cbwGroupedGemmArgs* a, int* error_word, cudaStream
 }
 
 template <bool kGated, bool kX2>
-cbwStatus_t launch_gemm_tm(const cbwGroupedGemmArgs* a, int* error_word, cudaStream_t stream) {
+cbwStatus_t launch_gemm_tm(const cbwGroupedGemmArgs* a, int* error_word, cudaStream_t stream,
+                           void* const* row_out = nullptr) {
     using C = TmCfg<kGated, kX2>;
     const int w_rows = kGated ? 2 * a->N : a->N;
     CUtensorMap tw, ta, ta64, ta128;
@@ -1750,6 +1762,7 @@ cbwStatus_t launch_gemm_tm(const cbwGroupedGemmArgs* a, int* error_word, cudaStr
     p.N = a->N;
     p.w_rows = w_rows;
     p.error_word = error_word;
+    p.row_out = kGated ? nullptr : row_out;
     grouped_fp8_gemm_tm_kernel<kGated, kX2><<<sms, kNumThreads, C::kSmemBytes, stream>>>(tw, ta, ta64, ta128, p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
@@ -1864,8 +1877,11 @@ cbwStatus_t launch_gemm_pair(const cbwGroupedGemmArgs* a, int* error_word, cudaS
 
 }  // namespace
 
-extern "C" cbwStatus_t cbwFp8BlockScaledGroupedGemm(const cbwGroupedGemmArgs* args, int* error_word,
-                                                    cwStream_t stream) {
+namespace {
+
+// row_out != nullptr: the token-major down form with per-row output addresses
+// (CBW_ERROR_NOT_SUPPORTED, nothing launched, when another form would run)
+cbwStatus_t grouped_gemm(const cbwGroupedGemmArgs* args, void* const* row_out, int* error_word, cwStream_t stream) {
     if (!args) return CBW_ERROR_INVALID_VALUE;
     const cbwGroupedGemmArgs& a = *args;
     if (a.num_groups <= 0 || a.num_groups > kMaxGroups) return CBW_ERROR_INVALID_VALUE;
@@ -1899,6 +1915,11 @@ extern "C" cbwStatus_t cbwFp8BlockScaledGroupedGemm(const cbwGroupedGemmArgs* ar
     const bool tm = !small && (tiles == CBW_GEMM_TOKEN_TILES || ((tiles == 0 || tiles == CBW_GEMM_FULL_TILES) && tm_ok));
     const bool pair = !tm && (tiles == CBW_GEMM_PAIR_TILES ||
                               (tiles != CBW_GEMM_ONE_SM_TILES && base == CBW_GEMM_DOWN_BF16 && pair_ok));
+    if (row_out) {
+        if (base != CBW_GEMM_DOWN_BF16 || !tm) return CBW_ERROR_NOT_SUPPORTED;
+        return x2 ? launch_gemm_tm<false, true>(&a, error_word, st, row_out)
+                  : launch_gemm_tm<false, false>(&a, error_word, st, row_out);
+    }
     if (base == CBW_GEMM_GATED_SWIGLU) {
         if (!a.out_scale || a.out_ld < a.rows) return CBW_ERROR_INVALID_VALUE;
         if (x2) {
@@ -1924,4 +1945,17 @@ extern "C" cbwStatus_t cbwFp8BlockScaledGroupedGemm(const cbwGroupedGemmArgs* ar
         return pair ? launch_gemm_pair<false, false>(&a, error_word, st) : launch_gemm<false, false, false>(&a, error_word, st);
     }
     return CBW_ERROR_INVALID_VALUE;
+}
+
+}  // namespace
+
+extern "C" cbwStatus_t cbwFp8BlockScaledGroupedGemm(const cbwGroupedGemmArgs* args, int* error_word,
+                                                    cwStream_t stream) {
+    return grouped_gemm(args, nullptr, error_word, stream);
+}
+
+extern "C" cbwStatus_t cbwFp8BlockScaledGroupedGemmRowOut(const cbwGroupedGemmArgs* args, void* const* row_out,
+                                                          int* error_word, cwStream_t stream) {
+    if (!row_out || (reinterpret_cast<uintptr_t>(row_out) & 7)) return CBW_ERROR_INVALID_VALUE;
+    return grouped_gemm(args, row_out, error_word, stream);
 }

@@ -31,6 +31,8 @@
 //   psend  [T*k][rb] / precv [recv_cap][rb]      packed rows (rb bytes each)
 //   row_src [R_cap], recv_dst [recv_cap]          received row <-> GEMM row
 //   ysend  [recv_cap][H] bf16 / yrecv [T*k][H] bf16  combine exchange
+//   row_out [R_cap] pointers        peer exchange: each GEMM row's output
+//                                  address (the owner's yrecv slot or local y)
 // and R_cap = recv_cap + S*T + 16*G (rounded to 16).
 #include <cuda_runtime.h>
 
@@ -75,6 +77,11 @@ struct moe_layer {
     tbep::Peers peers;
     uint32_t* epoch_dev;   // peer exchange: the forward counter, on the device
     size_t off_plan;
+    // peer exchange: the down GEMM stores each received row's output straight
+    // into its token owner's return buffer (TIME_B200_EP_FUSED_RETURN=0: a
+    // separate copy kernel after the GEMM)
+    bool fused_return = true;
+    size_t off_rowout = 0;   // [rcap] output row addresses of the down GEMM
     int gemm_form;        // 0 = by the rule in gemm_form(), else a CBW_GEMM_*_TILES flag
     int act_planes = 1;   // 1: e4m3 activations; 2: two-term e4m3 (hi + lo residual)
     size_t off_xq_lo = 0;  // [T][H] lo plane of xq (act_planes == 2)
@@ -132,6 +139,7 @@ void plan_workspace(moe_layer* L) {
         L->off_yrecv = take(T * K * H * 2);
         L->off_plan = take(tbep::plan_ints(c.ep_size) * 4);
         L->off_vidx = take(T * K * 4);
+        L->off_rowout = take(R * sizeof(void*));
     }
     L->bytes = o;
 }
@@ -176,6 +184,13 @@ int gemm_form(const moe_layer* L, int T, bool down = false) {
     const bool small = c.num_experts > 1 && tokens * c.top_k <= 16ll * c.num_experts;
     if (small && down && c.hidden % 256 == 0) return CBW_GEMM_TOKEN_TILES;
     return small ? CBW_GEMM_SMALL_TILES : CBW_GEMM_FULL_TILES;
+}
+
+// True when the down projection runs the token-major form, the one form that
+// takes per-row output addresses (cbwFp8BlockScaledGroupedGemmRowOut).
+bool down_token_major(const moe_layer* L, int T) {
+    const int f = gemm_form(L, T, true);
+    return L->cfg.hidden % 256 == 0 && (f == CBW_GEMM_TOKEN_TILES || f == CBW_GEMM_FULL_TILES);
 }
 
 cbwGroupedGemmArgs gemm_args(const moe_layer* L, void* ws, bool down, int T) {
@@ -291,13 +306,23 @@ moe_status_t run_experts_ep(moe_layer* L, const int32_t* idx, const float* wts, 
         MOE_TRY(moe_ep_gather_x2(mine + P.lay.off_recv, at<void>(ws, L->off_xq), xq_lo, at<float>(ws, L->off_xs),
                                  L->xs_ld, row_src, total, L->rcap, H, at<void>(ws, L->off_xp), xp_lo,
                                  at<float>(ws, L->off_xps), L->rcap, st));
+        // fused return: every received row's output address in its owner's
+        // return buffer, for the down GEMM's epilogue
+        const bool fused = L->fused_return && down_token_major(L, T);
+        void** row_out = at<void*>(ws, L->off_rowout);
+        if (fused) MOE_TRY(tbep::return_rows(P, row_src, total, plan, H, y_cap, L->rcap, row_out, st));
         cbwGroupedGemmArgs g1 = gemm_args(L, ws, false, T), g2 = gemm_args(L, ws, true, T);
         mark(L, 4, st);
         MOE_TRY(cbw_to_moe(cbwFp8BlockScaledGroupedGemm(&g1, L->error_word, st)));
         mark(L, 5, st);
-        MOE_TRY(cbw_to_moe(cbwFp8BlockScaledGroupedGemm(&g2, L->error_word, st)));
+        if (fused) {
+            MOE_TRY(cbw_to_moe(cbwFp8BlockScaledGroupedGemmRowOut(&g2, row_out, L->error_word, st)));
+        } else {
+            MOE_TRY(cbw_to_moe(cbwFp8BlockScaledGroupedGemm(&g2, L->error_word, st)));
+        }
         mark(L, 6, st);
-        MOE_TRY(tbep::combine_send(P, at<void>(ws, L->off_y), recv_dst, plan, H, y_cap, L->rcap, L->recv_cap, st));
+        if (!fused)
+            MOE_TRY(tbep::combine_send(P, at<void>(ws, L->off_y), recv_dst, plan, H, y_cap, L->rcap, L->recv_cap, st));
         MOE_TRY(tbep::signal_wait(P, tbep::kCombine, epoch, L->error_word, st));
         MOE_TRY(moe_combine_split(x, mine + P.lay.off_yrecv, spos, wts, at<void>(ws, L->off_y), start + epr, S, T, K,
                                   H, out, st));
@@ -594,6 +619,10 @@ moe_status_t moe_layer_set_peer_buffers(moe_layer_t* L, void* const* peer_bufs, 
         return MOE_ERR_CUDA;
     }
     if (cudaMemset(L->epoch_dev, 0, sizeof(uint32_t)) != cudaSuccess) return MOE_ERR_CUDA;
+    {
+        const char* f = std::getenv("TIME_B200_EP_FUSED_RETURN");
+        L->fused_return = !(f && f[0] == '0');
+    }
     L->peer_mode = true;
     return MOE_OK;
 }

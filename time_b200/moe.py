@@ -136,6 +136,8 @@ def libs():
         k.kernels_last_error.restype = c_int
         b = L["libcublaswrap.so"]
         b.cbwFp8BlockScaledGroupedGemm.argtypes = [ctypes.POINTER(GroupedGemmArgs), c_void_p, c_void_p]
+        b.cbwFp8BlockScaledGroupedGemmRowOut.argtypes = [ctypes.POINTER(GroupedGemmArgs), c_void_p, c_void_p,
+                                                         c_void_p]
         n = L["libncclwrap.so"]
         n.ncwGetUniqueId.argtypes = [ctypes.POINTER(UniqueId)]
         n.ncwCommInitRank.argtypes = [ctypes.POINTER(c_void_p), c_int, UniqueId, c_int]
@@ -364,12 +366,21 @@ class MoELayer:
 
 
 def grouped_gemm(mode: int, a, a_scale, a_ld: int, w, w_scale, count, start, out, out_scale, out_ld: int,
-                 K: int, N: int, rows: int, error_word=None, stream=None):
+                 K: int, N: int, rows: int, error_word=None, stream=None, row_out=None):
+    """cbwFp8BlockScaledGroupedGemm; with row_out (an int64 device tensor of
+    [rows] output row addresses, 0 for rows that go to out) the down
+    projection's cbwFp8BlockScaledGroupedGemmRowOut."""
     L = libs()
     args = GroupedGemmArgs(mode, count.numel(), K, N, rows, ptr(a), ptr(a_scale), a_ld, ptr(w), ptr(w_scale),
                            ptr(count), ptr(start), ptr(out), ptr(out_scale), out_ld)
-    rc = L["libcublaswrap.so"].cbwFp8BlockScaledGroupedGemm(ctypes.byref(args), ptr(error_word), stream_ptr(stream))
-    check("cbwFp8BlockScaledGroupedGemm", rc)
+    b = L["libcublaswrap.so"]
+    if row_out is None:
+        check("cbwFp8BlockScaledGroupedGemm", b.cbwFp8BlockScaledGroupedGemm(ctypes.byref(args), ptr(error_word),
+                                                                            stream_ptr(stream)))
+    else:
+        check("cbwFp8BlockScaledGroupedGemmRowOut",
+              b.cbwFp8BlockScaledGroupedGemmRowOut(ctypes.byref(args), ptr(row_out), ptr(error_word),
+                                                   stream_ptr(stream)))
 
 
 def router_load(shape, weights, x) -> "torch.Tensor":
