@@ -61,9 +61,9 @@ def test_ep_bit_identical(gpu, args, exchange):
 @pytest.mark.parametrize("args", [("--shape", "glm", "--tokens", "4096", "--act-planes", "2"),
                                   ("--shape", "glm", "--tokens", "64", "--repeats", "3")])
 def test_ep_peer_return_forms_bit_identical(gpu, args, fused):
-    """The peer exchange's two return paths: the down GEMM storing each
-    output row into its owner's buffer (default at hidden % 256 == 0) and the
-    separate copy kernel after the GEMM."""
+    """The peer exchange's two return paths: the copy kernel after the GEMM
+    (default) and the down GEMM storing each output row into its owner's
+    buffer (TIME_B200_EP_FUSED_RETURN=1, token-major down form)."""
     n = n_gpus()
     if n < 2:
         pytest.skip("needs >= 2 GPUs")

@@ -43,8 +43,11 @@
 // all ranks' flags, then derives the whole exchange plan on the device;
 // ep_dispatch_kernel packs each sent row straight into its destination's recv
 // buffer; ep_signal_wait_kernel raises flags[1][me] and waits for every
-// source; after the GEMMs ep_combine_send_kernel writes each expert output row
-// into its token owner's yrecv, and flags[2] closes the step.  Writers fence
+// source; each expert output row then goes into its token owner's yrecv --
+// copied there by ep_combine_send_kernel after the GEMM, or (optional,
+// token-major down form) stored there by the down GEMM's own epilogue, which
+// ep_return_rows_kernel gives every row's address -- and flags[2] closes the
+// step.  Writers fence
 // (system scope) before a release store of the flag; waiters acquire.  Every
 // wait is a bounded spin of one thread (error word 3 on timeout).
 #include <cuda_runtime.h>

@@ -77,10 +77,13 @@ struct moe_layer {
     tbep::Peers peers;
     uint32_t* epoch_dev;   // peer exchange: the forward counter, on the device
     size_t off_plan;
-    // peer exchange: the down GEMM stores each received row's output straight
-    // into its token owner's return buffer (TIME_B200_EP_FUSED_RETURN=0: a
-    // separate copy kernel after the GEMM)
-    bool fused_return = true;
+    // peer exchange, TIME_B200_EP_FUSED_RETURN=1: the down GEMM stores each
+    // received row's output straight into its token owner's return buffer
+    // instead of a copy kernel after the GEMM.  Off by default: at EP 2 (GLM
+    // shape, 4096 tokens) the epilogue's stores over NVLink hold the GEMM's
+    // TMEM buffers and the down GEMM takes 0.72 ms against 0.41 ms + a
+    // 0.14 ms copy.
+    bool fused_return = false;
     size_t off_rowout = 0;   // [rcap] output row addresses of the down GEMM
     int gemm_form;        // 0 = by the rule in gemm_form(), else a CBW_GEMM_*_TILES flag
     int act_planes = 1;   // 1: e4m3 activations; 2: two-term e4m3 (hi + lo residual)
@@ -621,7 +624,7 @@ moe_status_t moe_layer_set_peer_buffers(moe_layer_t* L, void* const* peer_bufs, 
     if (cudaMemset(L->epoch_dev, 0, sizeof(uint32_t)) != cudaSuccess) return MOE_ERR_CUDA;
     {
         const char* f = std::getenv("TIME_B200_EP_FUSED_RETURN");
-        L->fused_return = !(f && f[0] == '0');
+        L->fused_return = f && f[0] == '1';
     }
     L->peer_mode = true;
     return MOE_OK;
