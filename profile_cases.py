@@ -181,8 +181,7 @@ def proj(iters: int) -> dict:
     return out
 
 
-def attention(batch: int, ctx_min: int, ctx_max: int, split: int, iters: int, nq: int = 12, nkv: int = 1,
-              cpu_sample: int = 0) -> dict:
+def attention(batch: int, ctx_min: int, ctx_max: int, split: int, iters: int, nq: int = 12, nkv: int = 1) -> dict:
     import numpy as np
     from time_b200 import attn as A
     dev = torch.device("cuda", 0)
@@ -215,8 +214,6 @@ def attention(batch: int, ctx_min: int, ctx_max: int, split: int, iters: int, nq
     out = {"decode_ms": ms, "kv_bytes": kv_bytes, "algorithmic_bytes": kv_bytes + io_bytes,
            "achieved_gbs": (kv_bytes + io_bytes) / (ms * 1e-3) / 1e9, "context_tokens": int(lens.sum()),
            "split_tokens": split, "max_splits": max_splits}
-    if cpu_sample > 0:
-        out["cpu_baseline"] = _attention_cpu(q, kc, vc, pt, lens, cpu_sample, 1.0 / 128 ** 0.5)
     return out
 
 
@@ -254,31 +251,6 @@ def prefill(prompts: int, prompt_len: int, iters: int, nq: int = 12, nkv: int = 
             "split_decode_ms": t_dec, "speedup": t_dec / t_pf, "attention_flop": flops,
             "prefill_tflops": flops / (t_pf * 1e-3) / 1e12, "kv_bytes_unique": kv_unique,
             "kv_bytes_decode_path": keys * nkv * A.HEAD_DIM * 2 * 2}
-
-
-def _attention_cpu(q, kc, vc, pt, lens, n_seq: int, scale: float) -> dict:
-    """The CPU restatement of the reference's decode attention (the oracle,
-    one thread, float64) on the first n_seq sequences, scaled to the batch by
-    context tokens.  The reference engine has no CPU attention of its own."""
-    import time
-    import numpy as np
-    from oracle import oracle as O
-    qf = q.float().cpu().numpy()
-    tok = 0
-    t_cpu = 0.0
-    for b in range(min(n_seq, len(lens))):
-        n = (int(lens[b]) + 15) // 16
-        pages = pt[b, :n]
-        kb = kc[torch.from_numpy(pages).long().to(kc.device)].float().cpu().numpy()   # this sequence's pages
-        vb = vc[torch.from_numpy(pages).long().to(vc.device)].float().cpu().numpy()
-        t0 = time.perf_counter()
-        O.attn_decode_paged(qf[b], kb, vb, np.arange(n, dtype=np.int32), int(lens[b]), scale)
-        t_cpu += time.perf_counter() - t0
-        tok += int(lens[b])
-    per_tok = t_cpu / tok
-    return {"kind": "port", "cores": 1, "sample": f"{min(n_seq, len(lens))} of {len(lens)} sequences ({tok} tokens)",
-            "step_ms_est": per_tok * float(lens.sum()) * 1e3,
-            "kv_gbs": tok * kc.shape[2] * 128 * 2 * 2 / t_cpu / 1e9}
 
 
 def attn_block(batch: int, ctx_min: int, ctx_max: int, iters: int, tp: int = 8, use_graph: bool = False) -> dict:
@@ -396,7 +368,6 @@ def main() -> int:
     ap.add_argument("--ctx-max", type=int, default=32768)
     ap.add_argument("--split", type=int, default=512)
     ap.add_argument("--graph", action="store_true", help="attn_block: replay each step from a CUDA graph")
-    ap.add_argument("--cpu-sample", type=int, default=0, help="attention: time the CPU oracle on this many sequences")
     ap.add_argument("--tokens", type=int, default=4096)
     ap.add_argument("--experts", type=int, default=32)
     ap.add_argument("--iters", type=int, default=3)
@@ -407,7 +378,7 @@ def main() -> int:
     a = ap.parse_args()
     torch.cuda.set_device(0)
     if a.case == "attention":
-        res = attention(a.batch, a.ctx_min, a.ctx_max, a.split, a.iters, cpu_sample=a.cpu_sample)
+        res = attention(a.batch, a.ctx_min, a.ctx_max, a.split, a.iters)
     elif a.case == "attn_block":
         res = attn_block(a.batch, a.ctx_min, a.ctx_max, a.iters, use_graph=a.graph)
     elif a.case == "serving":

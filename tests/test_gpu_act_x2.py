@@ -46,7 +46,8 @@ def _split(v):
     return torch.from_numpy(q), torch.from_numpy(ql), torch.from_numpy(np.ascontiguousarray(s.T))
 
 
-@pytest.mark.parametrize("T,H,rc", [(1, 256, 0), (37, 512, 1), (300, 5120, 1), (2500, 1280, 0)])
+@pytest.mark.parametrize("T,H,rc", [(1, 256, 0), (37, 512, 1), (300, 5120, 1), (2500, 1280, 0), (2049, 640, 0),
+                                    (4096, 5120, 1)])
 def test_rmsnorm_quant_x2_bit_exact(gpu, oracle, T, H, rc):
     """hi plane identical to the one-plane quantiser, lo plane and scales
     bit-exact to the oracle; n written as moe_rmsnorm_quant_n / _rc write it."""

@@ -40,7 +40,7 @@ def stream():
 
 # ---------------------------------------------------------------- stages
 
-@pytest.mark.parametrize("T,H", [(1, 256), (37, 512), (64, 5120)])
+@pytest.mark.parametrize("T,H", [(1, 256), (37, 512), (64, 5120), (2100, 640), (4096, 5120)])
 def test_rmsnorm_quant_bit_exact(gpu, oracle, T, H):
     k = M.libs()["libkernels.so"]
     g = torch.Generator().manual_seed(T + H)

@@ -64,7 +64,7 @@ def test_router_columns_matches_the_layout(gpu, rows, H):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("T,H", [(1, 256), (37, 512), (300, 5120), (2500, 1280)])
+@pytest.mark.parametrize("T,H", [(1, 256), (37, 512), (300, 5120), (2500, 1280), (2304, 768), (4096, 5120)])
 def test_rmsnorm_rc_is_the_reordered_plain_output(gpu, T, H):
     """moe_rmsnorm_quant_rc: n bit-identical to moe_rmsnorm_quant_n's n put
     in the router column order; rms, e4m3 bytes and scales identical (both

@@ -50,35 +50,84 @@ __device__ __forceinline__ void store_n(float* row, int c, int H, float v0, floa
 // Sum of squares of one row in the reference's order
 // (csrc/kernels.cu:67-79 with blockDim 256): the 256 partials
 // p[L] = fma-chain over i = L, L+256, ... are reduced by the pairwise tree
-// p[L] += p[L+s], s = 128..1.  Lane l of the warp owns L = l + 32m, m = 0..7,
-// so strides 128, 64, 32 are lane-local and 16..1 are shuffles; every
-// addition pairs the same operands as the reference's tree.
+// p[L] += p[L+s], s = 128..1.  Lane l of the warp owns L = 8l + u, u = 0..7,
+// so one 16-byte load gives a lane the eight elements of its partials in a
+// 256-element chunk; strides 128..8 of the tree are shuffles (lane l + 16 ..
+// l + 1, same u) and 4, 2, 1 are lane-local.  Every addition pairs the same
+// operands as the reference's tree.  H % 128 == 0: a last half chunk is held
+// by lanes 0-15.
 __device__ __forceinline__ float rowsumsq_ref_order(const __nv_bfloat16* x, int H, int lane) {
     float p[8];
 #pragma unroll
-    for (int m = 0; m < 8; ++m) p[m] = 0.0f;
-    for (int j = 0; j < H; j += 256) {
+    for (int u = 0; u < 8; ++u) p[u] = 0.0f;
+    const int full = H >> 8;            // whole 256-element chunks
+    int j = 0;
+    for (; j + 4 <= full; j += 4) {     // four 16-byte loads in flight per lane
+        uint4 r[4];
 #pragma unroll
-        for (int m = 0; m < 8; ++m) {
-            const int i = j + 32 * m + lane;
-            if (i < H) {
-                const float v = __bfloat162float(x[i]);
-                p[m] = __fmaf_rn(v, v, p[m]);
+        for (int a = 0; a < 4; ++a) r[a] = *reinterpret_cast<const uint4*>(x + (j + a) * 256 + lane * 8);
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+            const uint32_t w[4] = {r[a].x, r[a].y, r[a].z, r[a].w};
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+                const float lo = bf16_lo(w[h]), hi = bf16_hi(w[h]);
+                p[2 * h] = __fmaf_rn(lo, lo, p[2 * h]);
+                p[2 * h + 1] = __fmaf_rn(hi, hi, p[2 * h + 1]);
+            }
+        }
+    }
+    for (; j * 256 < H; ++j) {
+        const int c = j * 256 + lane * 8;
+        if (c < H) {
+            const uint4 r = *reinterpret_cast<const uint4*>(x + c);
+            const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+                const float lo = bf16_lo(w[h]), hi = bf16_hi(w[h]);
+                p[2 * h] = __fmaf_rn(lo, lo, p[2 * h]);
+                p[2 * h + 1] = __fmaf_rn(hi, hi, p[2 * h + 1]);
             }
         }
     }
 #pragma unroll
-    for (int m = 0; m < 4; ++m) p[m] = __fadd_rn(p[m], p[m + 4]);
+    for (int o = 16; o > 0; o >>= 1) {
 #pragma unroll
-    for (int m = 0; m < 2; ++m) p[m] = __fadd_rn(p[m], p[m + 2]);
-    float s = __fadd_rn(p[0], p[1]);
+        for (int u = 0; u < 8; ++u) {
+            const float v = __shfl_down_sync(0xffffffffu, p[u], o);
+            if (lane < o) p[u] = __fadd_rn(p[u], v);
+        }
+    }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_down_sync(0xffffffffu, s, o));
-    return __shfl_sync(0xffffffffu, s, 0);
+    for (int u = 0; u < 4; ++u) p[u] = __fadd_rn(p[u], p[u + 4]);
+#pragma unroll
+    for (int u = 0; u < 2; ++u) p[u] = __fadd_rn(p[u], p[u + 2]);
+    return __shfl_sync(0xffffffffu, __fadd_rn(p[0], p[1]), 0);
+}
+
+// n[c .. c+7] of one row (c = 256 j + 8 lane), in the plain or the router
+// column order.  In the router order elements c + u and c + u + 4 (u < 4)
+// land in adjacent columns, so the lane writes four 8-byte pairs.
+template <bool kRc>
+__device__ __forceinline__ void store_n8(float* row, int c, int H, const float (&v)[8]) {
+    if constexpr (kRc) {
+        const int J = H >> 8, j = c >> 8, l = (c >> 3) & 31;
+        const int base = (l >> 2) * 16 * J + 16 * j + 2 * (l & 3);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            *reinterpret_cast<float2*>(row + (u & 1) * 128 * J + base + 8 * (u >> 1)) = make_float2(v[u], v[u + 4]);
+    } else {
+        *reinterpret_cast<float4*>(row + c) = make_float4(v[0], v[1], v[2], v[3]);
+        *reinterpret_cast<float4*>(row + c + 4) = make_float4(v[4], v[5], v[6], v[7]);
+    }
 }
 
 // One warp per token: rms, n = (x/rms)*gamma (stored in fp32 when n_out is
-// given, for the router), 1x128 e4m3 quantisation of n.
+// given, for the router), 1x128 e4m3 quantisation of n (one or two planes).
+// Both passes over the row use 16-byte loads: lane l holds elements
+// 256j + 8l .. +7 of chunk j, so lanes 0-15 form quantisation block 2j and
+// lanes 16-31 block 2j + 1 (an amax over 16 lanes).  The second pass re-reads
+// the row, which the first pass has just brought into L2.
 template <bool kRc>
 __global__ void __launch_bounds__(256)
 rmsnorm_quant_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ gamma, int T, int H,
@@ -93,36 +142,50 @@ rmsnorm_quant_kernel(const __nv_bfloat16* __restrict__ x, const float* __restric
     if (rms_out && lane == 0) rms_out[warp] = rms;
     uint8_t* qr = xq + static_cast<size_t>(warp) * H;
     uint8_t* lr = xq_lo ? xq_lo + static_cast<size_t>(warp) * H : nullptr;
-    for (int b = 0; b < H / 128; ++b) {
-        const int c = b * 128 + lane * 4;
-        const uint2 raw = *reinterpret_cast<const uint2*>(xr + c);
-        const float4 g = *reinterpret_cast<const float4*>(gamma + c);
-        float v0 = __fmul_rn(__fdiv_rn(bf16_lo(raw.x), rms), g.x);
-        float v1 = __fmul_rn(__fdiv_rn(bf16_hi(raw.x), rms), g.y);
-        float v2 = __fmul_rn(__fdiv_rn(bf16_lo(raw.y), rms), g.z);
-        float v3 = __fmul_rn(__fdiv_rn(bf16_hi(raw.y), rms), g.w);
-        if (n_out) store_n<kRc>(n_out + static_cast<size_t>(warp) * H, c, H, v0, v1, v2, v3);
-        float amax = fmaxf(fmaxf(fabsf(v0), fabsf(v1)), fmaxf(fabsf(v2), fabsf(v3)));
+    float* nr = n_out ? n_out + static_cast<size_t>(warp) * H : nullptr;
+#pragma unroll 2
+    for (int j = 0; j * 256 < H; ++j) {
+        const int c = j * 256 + lane * 8;
+        const bool live = c < H;            // false only for lanes 16-31 of a last half chunk
+        float v[8];
+        float amax = 0.0f;
+        if (live) {
+            const uint4 raw = *reinterpret_cast<const uint4*>(xr + c);
+            const float4 g0 = *reinterpret_cast<const float4*>(gamma + c);
+            const float4 g1 = *reinterpret_cast<const float4*>(gamma + c + 4);
+            const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+            const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        uint32_t packed = 0, packed_lo = 0;
+            for (int h = 0; h < 4; ++h) {
+                v[2 * h] = __fmul_rn(__fdiv_rn(bf16_lo(w[h]), rms), g[2 * h]);
+                v[2 * h + 1] = __fmul_rn(__fdiv_rn(bf16_hi(w[h]), rms), g[2 * h + 1]);
+            }
+            if (nr) store_n8<kRc>(nr, c, H, v);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) amax = fmaxf(amax, fabsf(v[u]));
+        }
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        if (!live) continue;
+        uint2 packed = make_uint2(0u, 0u), packed_lo = make_uint2(0u, 0u);
         float scale = 0.0f;
         if (amax > 0.0f) {
             const float inv = __fdiv_rn(448.0f, amax);
-            if (lr) {   // two planes: hi, and the e4m3 residual (one scale)
-                const uint32_t s0 = cvt_e4m3x2_split(__fmul_rn(v0, inv), __fmul_rn(v1, inv));
-                const uint32_t s1 = cvt_e4m3x2_split(__fmul_rn(v2, inv), __fmul_rn(v3, inv));
-                packed = (s0 & 0xFFFFu) | (s1 << 16);
-                packed_lo = (s0 >> 16) | (s1 & 0xFFFF0000u);
-            } else {
-                packed = static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v0, inv), __fmul_rn(v1, inv))) |
-                         (static_cast<uint32_t>(cvt_e4m3x2(__fmul_rn(v2, inv), __fmul_rn(v3, inv))) << 16);
+            uint32_t q[4];
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+                const float a = __fmul_rn(v[2 * h], inv), b = __fmul_rn(v[2 * h + 1], inv);
+                q[h] = lr ? cvt_e4m3x2_split(a, b) : static_cast<uint32_t>(cvt_e4m3x2(a, b));
             }
+            packed.x = (q[0] & 0xFFFFu) | (q[1] << 16);
+            packed.y = (q[2] & 0xFFFFu) | (q[3] << 16);
+            packed_lo.x = (q[0] >> 16) | (q[1] & 0xFFFF0000u);
+            packed_lo.y = (q[2] >> 16) | (q[3] & 0xFFFF0000u);
             scale = __fdiv_rn(amax, 448.0f);
         }
-        *reinterpret_cast<uint32_t*>(qr + c) = packed;
-        if (lr) *reinterpret_cast<uint32_t*>(lr + c) = packed_lo;
-        if (lane == 0) xs[static_cast<size_t>(b) * xs_ld + warp] = scale;
+        *reinterpret_cast<uint2*>(qr + c) = packed;
+        if (lr) *reinterpret_cast<uint2*>(lr + c) = packed_lo;
+        if ((lane & 15) == 0) xs[static_cast<size_t>(2 * j + (lane >> 4)) * xs_ld + warp] = scale;
     }
 }
 
