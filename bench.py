@@ -687,9 +687,23 @@ def run_ours(args):
         dist.all_reduce(t[:1], op=dist.ReduceOp.MAX)
         dist.all_reduce(tm[1:], op=dist.ReduceOp.SUM)
         rows_max, rows_mean = int(t[0].item()), float(tm[1].item()) / world
-    rb = M.libs()["libkernels.so"].moe_ep_row_bytes(shape.hidden)
-    a2a_bytes = max(sent_remote * rb + recv_remote * shape.hidden * 2,
-                    recv_remote * rb + sent_remote * shape.hidden * 2) if world > 1 else 0
+    # the dispatch moves one packed row per (token, remote rank that owns at
+    # least one of its experts) -- the peer exchange sends each token once per
+    # destination; the return moves one bf16 row per remote pair
+    rb = M.libs()["libkernels.so"].moe_ep_row_bytes(shape.hidden) + (shape.hidden if act_planes == 2 else 0)
+    a2a_bytes = 0
+    if world > 1:
+        K_ = shape.top_k
+        rows_to = [0] * world
+        for t_ in range(len(idx_h) // K_):
+            for d_ in {owner[e] for e in idx_h[t_ * K_:(t_ + 1) * K_] if e >= 0}:
+                rows_to[d_] += 1
+        got = torch.tensor(rows_to, dtype=torch.float64, device=dev)
+        dist.all_reduce(got, op=dist.ReduceOp.SUM)
+        uniq_sent = sum(rows_to) - rows_to[rank]
+        uniq_recv = int(got[rank].item()) - rows_to[rank]
+        a2a_bytes = max(uniq_sent * rb + recv_remote * shape.hidden * 2,
+                        uniq_recv * rb + sent_remote * shape.hidden * 2)
     fp8_peak = 2 * peaks["bf16_tflops"]
     t_hbm = lb / (peaks["hbm_gbs"] * 1e9)
     t_fp8 = lf / (fp8_peak * 1e12)
@@ -716,13 +730,14 @@ def run_ours(args):
     # our kernels per forward: rmsnorm, router logits, top-k, 3 permutation kernels (count, scan,
     # scatter), gather, 2 GEMMs, combine = 10 (8 with supplied routing); EP replaces gather/combine
     # and adds (NCCL) row pack, receive plan, gather, output pack, split combine = 13 or (peer memory)
-    # counts, dispatch, 2 signal/waits, receive plan, gather, output send, split combine = 16; the
+    # per-destination token numbering, counts, dispatch, 2 signal/waits, receive plan, gather, output
+    # send, split combine = 17; the
     # expert placement adds its remap kernel.  NCCL's own kernels are not counted.
     # (The prefill router is three launches since the router reads column-ordered inputs: the
     # reorder of W, the logits, the top-k; the decode workload supplies its routing.)
     router_launches = 0 if decode else 3
     launches_per_step = (1 + router_launches + 3 + 1 + 2 + 1 if world == 1 else
-                         1 + router_launches + (10 if args.exchange == "nccl" else 13) + (1 if placement else 0))
+                         1 + router_launches + (10 if args.exchange == "nccl" else 14) + (1 if placement else 0))
 
     # ---- the one-plane activation format on the same layer and inputs, for comparison
     one_plane = None
@@ -748,10 +763,12 @@ def run_ours(args):
         launches_per_step -= 2
     dispatch = None
     if world > 1:
-        dispatch = ("fp8 rows + 1x128 scales (5,280 B per row at H = 5120; BASELINE configs[2] names bf16 hidden "
-                    "states -- a deviation: the GEMM reads e4m3 rows, so sending them halves the bytes), combine "
-                    "bf16, " + ("NVLink peer-memory stores from own kernels, no host sync" if args.exchange == "peer"
-                                else "NCCL send/recv, one host sync"))
+        dispatch = ("fp8 rows + 1x128 scales (5,280 B per row and plane at H = 5120; BASELINE configs[2] names "
+                    "bf16 hidden states -- a deviation: the GEMM reads e4m3 rows, so sending them halves the bytes), "
+                    "combine bf16, " + ("NVLink peer-memory stores from own kernels, no host sync, one row per "
+                                        "(token, destination rank) however many of its experts live there"
+                                        if args.exchange == "peer"
+                                        else "NCCL send/recv, one host sync, one row per (token, expert) pair"))
     line = {"metric": METRIC, "value": T * 1000.0 / ms_per_step, "unit": UNIT, "n_gpus": world,
             "steps": K, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None,

@@ -35,14 +35,21 @@
 // NCCL and no host synchronisation.  Every rank owns a symmetric buffer that
 // all ranks have mapped (NVLink peer memory):
 //   flags [3][kMaxEpRanks] u32   counts / dispatch / combine epochs, one per source
-//   table [ep][E] i32            every rank's per-expert send counts
-//   recv  [recv_cap][rb]         packed rows dispatched to this rank
+//   table [ep][E + ep] i32       every rank's per-expert send counts, then its
+//                                row counts per destination rank
+//   recv  [recv_cap][rb]         packed rows dispatched to this rank: one per
+//                                (source token, this rank), source-major
+//   pmap  [recv_cap] i32         per received pair (source-major, the sender's
+//                                expert order): its row in recv
 //   yrecv [T*k][H] bf16          expert outputs returned to this rank
 // Per forward (epoch e = 1, 2, ..., counted on the device): ep_counts_kernel writes this rank's
 // counts into every table and raises flags[0][me] = e on every rank, waits for
 // all ranks' flags, then derives the whole exchange plan on the device;
-// ep_dispatch_kernel packs each sent row straight into its destination's recv
-// buffer; ep_signal_wait_kernel raises flags[1][me] and waits for every
+// ep_dispatch_kernel packs each token that has a pair for a destination
+// straight into that destination's recv buffer, once however many of the
+// token's experts live there (ep_unique_kernel numbers those tokens), and
+// writes every pair's row index into the destination's pmap, so the receiving
+// gather builds the same expert segments from fewer transferred rows; ep_signal_wait_kernel raises flags[1][me] and waits for every
 // source; each expert output row then goes into its token owner's yrecv --
 // copied there by ep_combine_send_kernel after the GEMM, or (optional,
 // token-major down form) stored there by the down GEMM's own epilogue, which
@@ -177,7 +184,8 @@ __global__ void __launch_bounds__(256)
 ep_gather_kernel(const uint8_t* __restrict__ packed, size_t row_bytes, const uint8_t* __restrict__ xq,
                  const float* __restrict__ xs, int xs_ld, const int32_t* __restrict__ row_src,
                  const int32_t* __restrict__ total_rows, int row_capacity, int H, uint8_t* __restrict__ xp,
-                 float* __restrict__ xps, int xps_ld, const uint8_t* __restrict__ xq_lo, uint8_t* __restrict__ xp_lo) {
+                 float* __restrict__ xps, int xps_ld, const uint8_t* __restrict__ xq_lo, uint8_t* __restrict__ xp_lo,
+                 const int32_t* __restrict__ pmap = nullptr, int pmap_bound = 0) {
     const int R = min(*total_rows, row_capacity);
     const int lane = threadIdx.x & 31;
     const int nwarps = (gridDim.x * blockDim.x) >> 5;
@@ -185,7 +193,11 @@ ep_gather_kernel(const uint8_t* __restrict__ packed, size_t row_bytes, const uin
     const int nblk = H / 128;
     const int planes = xp_lo ? 2 : 1;
     for (int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < R; r += nwarps) {
-        const int v = row_src[r];
+        int v = row_src[r];
+        if (pmap && v >= 0) {               // received pair -> its (token, this rank) row
+            v = v < pmap_bound ? pmap[v] : -1;
+            if (v < 0 || v >= pmap_bound) v = -1;   // cannot happen for a well-formed exchange: a zero row
+        }
         int4* dst = reinterpret_cast<int4*>(xp + static_cast<size_t>(r) * H);
         int4* dlo = xp_lo ? reinterpret_cast<int4*>(xp_lo + static_cast<size_t>(r) * H) : nullptr;
         if (v >= 0) {
@@ -232,15 +244,21 @@ ep_pack_y_kernel(const uint8_t* __restrict__ y, const int32_t* __restrict__ recv
 
 constexpr int kMaxEpRanks = 64;
 enum { kFlagCounts = 0, kFlagDispatch = 1, kFlagCombine = 2 };
-// plan[] layout (int32, device): per rank d: soff, srows, roff_in (where my
-// rows land in d's recv), recv_off, rrows (from d), ysoff (where d's outputs
-// for my experts land in d's send order); then stot, rtot.
-enum { kPlanSoff = 0, kPlanSrows = 1, kPlanRoffIn = 2, kPlanRecvOff = 3, kPlanRrows = 4, kPlanYsoff = 5 };
+// plan[] layout (int32, device): per rank d (kPlanStride entries): soff,
+// srows (my pairs for d, in my send order), roff_in (where my pairs land in
+// d's pair positions), recv_off, rrows (pairs from d), ysoff (where d's
+// outputs for my experts land in d's send order), usoff, usrows (my rows for
+// d: tokens with a pair there), uoff_in (where my rows land in d's recv);
+// then stot, rtot, utot.
+enum {
+    kPlanSoff = 0, kPlanSrows = 1, kPlanRoffIn = 2, kPlanRecvOff = 3, kPlanRrows = 4, kPlanYsoff = 5,
+    kPlanUsoff = 6, kPlanUsrows = 7, kPlanUoffIn = 8, kPlanStride = 9
+};
 
 struct EpPeers {
     uint8_t* base[kMaxEpRanks];   // rank r's symmetric buffer as mapped in this process
     int ep, me, E, epr;
-    size_t off_flags, off_table, off_recv, off_yrecv;
+    size_t off_flags, off_table, off_recv, off_pmap, off_yrecv;
     unsigned long long timeout_ns;
 };
 
@@ -274,15 +292,92 @@ __device__ bool signal_and_wait(const EpPeers& P, int phase, uint32_t epoch) {
     return true;
 }
 
+// Single block of kUniqueThreads.  For every destination rank d, the tokens
+// of this rank with at least one pair routed to d (vid = virtual expert, rank
+// vid / epr), numbered in token order: uidx[d][t] (-1 when none) and
+// utok[d][u]; ucount[d] rows.  Per 1024-token chunk one block scan per group
+// of four destinations, each destination a 16-bit field of a 64-bit sum (a
+// chunk counts at most 1024 tokens, so the fields never carry).
+constexpr int kUniqueThreads = 1024;
+
+__global__ void __launch_bounds__(kUniqueThreads)
+ep_unique_kernel(const int32_t* __restrict__ vid, int T, int K, int ep, int epr, int32_t* __restrict__ uidx,
+                 int32_t* __restrict__ utok, int32_t* __restrict__ ucount) {
+    __shared__ unsigned long long wsum[kUniqueThreads / 32];
+    __shared__ int run[kMaxEpRanks];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int d = tid; d < ep; d += kUniqueThreads) run[d] = 0;
+    __syncthreads();
+    const int groups = (ep + 3) / 4;
+    for (int c0 = 0; c0 < T; c0 += kUniqueThreads) {
+        const int t = c0 + tid;
+        unsigned long long mask = 0;
+        if (t < T)
+            for (int s = 0; s < K; ++s) {
+                const int v = vid[static_cast<size_t>(t) * K + s];
+                if (v >= 0 && v < ep * epr) mask |= 1ull << (v / epr);
+            }
+        for (int g = 0; g < groups; ++g) {
+            unsigned long long x = 0;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int d = 4 * g + q;
+                if (d < ep && ((mask >> d) & 1ull)) x |= 1ull << (16 * q);
+            }
+            unsigned long long inc = x;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const unsigned long long y = __shfl_up_sync(0xffffffffu, inc, o);
+                if (lane >= o) inc += y;
+            }
+            if (lane == 31) wsum[warp] = inc;
+            __syncthreads();
+            if (warp == 0) {
+                unsigned long long w = wsum[lane];
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const unsigned long long y = __shfl_up_sync(0xffffffffu, w, o);
+                    if (lane >= o) w += y;
+                }
+                wsum[lane] = w;
+            }
+            __syncthreads();
+            const unsigned long long excl = inc - x + (warp ? wsum[warp - 1] : 0ull);
+            if (t < T) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int d = 4 * g + q;
+                    if (d >= ep) break;
+                    if ((mask >> d) & 1ull) {
+                        const int u = run[d] + static_cast<int>((excl >> (16 * q)) & 0xFFFFull);
+                        uidx[static_cast<size_t>(d) * T + t] = u;
+                        utok[static_cast<size_t>(d) * T + u] = t;
+                    } else {
+                        uidx[static_cast<size_t>(d) * T + t] = -1;
+                    }
+                }
+            }
+            __syncthreads();   // every thread has read run[] and wsum[]
+            if (tid < 4 && 4 * g + tid < ep)
+                run[4 * g + tid] += static_cast<int>((wsum[kUniqueThreads / 32 - 1] >> (16 * tid)) & 0xFFFFull);
+            __syncthreads();
+        }
+    }
+    for (int d = tid; d < ep; d += kUniqueThreads) ucount[d] = run[d];
+}
+
 // Single block: counts into every table, barrier, then the exchange plan.
+// A table row is [E per-expert pair counts][ep row counts per destination].
 __global__ void __launch_bounds__(256)
-ep_counts_kernel(const EpPeers P, const int32_t* __restrict__ ecounts, uint32_t* __restrict__ epoch_dev,
-                 int32_t* __restrict__ plan,
+ep_counts_kernel(const EpPeers P, const int32_t* __restrict__ ecounts, const int32_t* __restrict__ ucounts,
+                 uint32_t* __restrict__ epoch_dev, int32_t* __restrict__ plan,
                  int32_t* __restrict__ rcounts, int* __restrict__ error_word) {
     const int tid = threadIdx.x;
+    const int W = P.E + P.ep;   // table row stride
     for (int d = 0; d < P.ep; ++d) {
-        int32_t* tab = reinterpret_cast<int32_t*>(P.base[d] + P.off_table) + static_cast<size_t>(P.me) * P.E;
+        int32_t* tab = reinterpret_cast<int32_t*>(P.base[d] + P.off_table) + static_cast<size_t>(P.me) * W;
         for (int e = tid; e < P.E; e += blockDim.x) tab[e] = ecounts[e];
+        for (int e = tid; e < P.ep; e += blockDim.x) tab[P.E + e] = ucounts[e];
     }
     __threadfence_system();
     __syncthreads();
@@ -297,7 +392,7 @@ ep_counts_kernel(const EpPeers P, const int32_t* __restrict__ ecounts, uint32_t*
     if (!ok) {
         if (tid == 0) {
             if (error_word) atomicExch(error_word, 3);
-            for (int i = 0; i < 6 * P.ep + 2; ++i) plan[i] = 0;   // nothing moves
+            for (int i = 0; i < kPlanStride * P.ep + 3; ++i) plan[i] = 0;   // nothing moves
         }
         for (int i = tid; i < P.ep * P.epr; i += blockDim.x) rcounts[i] = 0;
         return;
@@ -307,91 +402,119 @@ ep_counts_kernel(const EpPeers P, const int32_t* __restrict__ ecounts, uint32_t*
     // are integers: the order does not matter)
     extern __shared__ int sh_counts[];
     const int EE = P.E, ep = P.ep, epr = P.epr, me = P.me;
-    int* stab = sh_counts;              // [ep][E]
-    int* mine_c = sh_counts + ep * EE;  // [E]
-    const int32_t* tab = reinterpret_cast<const int32_t*>(P.base[P.me] + P.off_table);   // [ep][E], all sources
-    for (int i = tid; i < ep * EE; i += blockDim.x) stab[i] = tab[i];
+    int* stab = sh_counts;              // [ep][W]
+    int* mine_c = sh_counts + ep * W;   // [E]
+    const int32_t* tab = reinterpret_cast<const int32_t*>(P.base[P.me] + P.off_table);   // [ep][W], all sources
+    for (int i = tid; i < ep * W; i += blockDim.x) stab[i] = tab[i];
     for (int i = tid; i < EE; i += blockDim.x) mine_c[i] = ecounts[i];
     __syncthreads();
     for (int i = tid; i < ep * epr; i += blockDim.x) {
         const int s = i / epr, j = i % epr;
-        rcounts[i] = stab[s * EE + me * epr + j];
+        rcounts[i] = stab[s * W + me * epr + j];
     }
     __shared__ int v_sn[kMaxEpRanks], v_rn[kMaxEpRanks], v_before[kMaxEpRanks], v_ys[kMaxEpRanks];
+    __shared__ int v_ubefore[kMaxEpRanks];
     const int warp = tid >> 5, lane = tid & 31, nwarps = blockDim.x >> 5;
     for (int d = warp; d < ep; d += nwarps) {
-        int sn = 0, rn = 0, before = 0, ys = 0;
+        int sn = 0, rn = 0, before = 0, ys = 0, ubefore = 0;
         for (int j = lane; j < epr; j += 32) {
-            sn += mine_c[d * epr + j];                   // my rows for d
-            rn += stab[d * EE + me * epr + j];           // d's rows for me
+            sn += mine_c[d * epr + j];                   // my pairs for d
+            rn += stab[d * W + me * epr + j];            // d's pairs for me
         }
         for (int i = lane; i < me * epr; i += 32) {
-            before += stab[(i / epr) * EE + d * epr + i % epr];   // earlier sources' rows for d
-            ys += stab[d * EE + i];                                // d's rows before mine
+            before += stab[(i / epr) * W + d * epr + i % epr];   // earlier sources' pairs for d
+            ys += stab[d * W + i];                                // d's pairs before mine
         }
+        for (int s = lane; s < me; s += 32) ubefore += stab[s * W + EE + d];   // earlier sources' rows for d
         for (int o = 16; o > 0; o >>= 1) {
             sn += __shfl_xor_sync(0xffffffffu, sn, o);
             rn += __shfl_xor_sync(0xffffffffu, rn, o);
             before += __shfl_xor_sync(0xffffffffu, before, o);
             ys += __shfl_xor_sync(0xffffffffu, ys, o);
+            ubefore += __shfl_xor_sync(0xffffffffu, ubefore, o);
         }
         if (lane == 0) {
             v_sn[d] = sn;
             v_rn[d] = rn;
             v_before[d] = before;
             v_ys[d] = ys;
+            v_ubefore[d] = ubefore;
         }
     }
     __syncthreads();
     if (tid == 0) {
         int32_t* pl = plan;
-        int so = 0, ro = 0;
+        int so = 0, ro = 0, uo = 0;
         for (int d = 0; d < ep; ++d) {
-            pl[6 * d + kPlanSoff] = so;
-            pl[6 * d + kPlanSrows] = v_sn[d];
-            pl[6 * d + kPlanRoffIn] = v_before[d];
-            pl[6 * d + kPlanRecvOff] = ro;
-            pl[6 * d + kPlanRrows] = v_rn[d];
-            pl[6 * d + kPlanYsoff] = v_ys[d];
+            int32_t* q = pl + kPlanStride * d;
+            const int un = stab[me * W + EE + d];   // my rows for d
+            q[kPlanSoff] = so;
+            q[kPlanSrows] = v_sn[d];
+            q[kPlanRoffIn] = v_before[d];
+            q[kPlanRecvOff] = ro;
+            q[kPlanRrows] = v_rn[d];
+            q[kPlanYsoff] = v_ys[d];
+            q[kPlanUsoff] = uo;
+            q[kPlanUsrows] = un;
+            q[kPlanUoffIn] = v_ubefore[d];
             so += v_sn[d];
             ro += v_rn[d];
+            uo += un;
         }
-        pl[6 * ep] = so;       // stot
-        pl[6 * ep + 1] = ro;   // rtot
+        pl[kPlanStride * ep] = so;       // stot
+        pl[kPlanStride * ep + 1] = ro;   // rtot
+        pl[kPlanStride * ep + 2] = uo;   // utot
     }
 }
 
-// Warp per sent row: pack (values + scales) straight into the destination's recv.
+// Warp per sent row -- one per (destination, token with a pair there) --
+// packs values + scales straight into the destination's recv; then a thread
+// per sent pair writes the pair's row index into the destination's pmap.
 __global__ void __launch_bounds__(256)
 ep_dispatch_kernel(const EpPeers P, const uint8_t* __restrict__ xq, const float* __restrict__ xs, int xs_ld,
-                   const int32_t* __restrict__ stok, const int32_t* __restrict__ plan, int H, size_t row_bytes,
+                   const int32_t* __restrict__ stok, const int32_t* __restrict__ uidx,
+                   const int32_t* __restrict__ utok, int T, const int32_t* __restrict__ plan, int H, size_t row_bytes,
                    int recv_cap, const uint8_t* __restrict__ xq_lo) {
-    __shared__ int s_soff[kMaxEpRanks], s_roff[kMaxEpRanks];
+    __shared__ int s_soff[kMaxEpRanks], s_roff[kMaxEpRanks], s_usoff[kMaxEpRanks], s_uoff[kMaxEpRanks];
     for (int d = threadIdx.x; d < P.ep; d += blockDim.x) {
-        s_soff[d] = plan[6 * d + kPlanSoff];
-        s_roff[d] = plan[6 * d + kPlanRoffIn];
+        s_soff[d] = plan[kPlanStride * d + kPlanSoff];
+        s_roff[d] = plan[kPlanStride * d + kPlanRoffIn];
+        s_usoff[d] = plan[kPlanStride * d + kPlanUsoff];
+        s_uoff[d] = plan[kPlanStride * d + kPlanUoffIn];
     }
     __syncthreads();
-    const int stot = plan[6 * P.ep];
+    const int stot = plan[kPlanStride * P.ep];
+    const int utot = plan[kPlanStride * P.ep + 2];
     const int lane = threadIdx.x & 31;
     const int nwarps = (gridDim.x * blockDim.x) >> 5;
     const int vec = H / 16, nblk = H / 128;
     const int nscale_padded = (nblk * 4 + 15) / 16 * 4;
-    for (int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < stot; r += nwarps) {
+    for (int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < utot; i += nwarps) {
         int d = P.ep - 1;
-        while (d > 0 && s_soff[d] > r) --d;
-        const int dest = s_roff[d] + (r - s_soff[d]);
-        if (dest >= recv_cap) continue;          // cannot happen within max_tokens (checked by the plan)
+        while (d > 0 && s_usoff[d] > i) --d;
+        const int u = i - s_usoff[d];
+        const int dest = s_uoff[d] + u;
+        if (u >= T || dest >= recv_cap) continue;   // cannot happen within max_tokens (checked by the plan)
+        const int t = utok[static_cast<size_t>(d) * T + u];
+        if (t < 0 || t >= T) continue;
         uint8_t* dst = P.base[d] + P.off_recv + static_cast<size_t>(dest) * row_bytes;
-        const int t = stok[r];
         const int4* src = reinterpret_cast<const int4*>(xq + static_cast<size_t>(t) * H);
-        for (int i = lane; i < vec; i += 32) reinterpret_cast<int4*>(dst)[i] = src[i];
+        for (int c = lane; c < vec; c += 32) reinterpret_cast<int4*>(dst)[c] = src[c];
         if (xq_lo) {
             const int4* slo = reinterpret_cast<const int4*>(xq_lo + static_cast<size_t>(t) * H);
-            for (int i = lane; i < vec; i += 32) reinterpret_cast<int4*>(dst + H)[i] = slo[i];
+            for (int c = lane; c < vec; c += 32) reinterpret_cast<int4*>(dst + H)[c] = slo[c];
         }
         float* ds = reinterpret_cast<float*>(dst + static_cast<size_t>(xq_lo ? 2 : 1) * H);
         for (int b = lane; b < nscale_padded; b += 32) ds[b] = (b < nblk) ? xs[static_cast<size_t>(b) * xs_ld + t] : 0.0f;
+    }
+    for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < stot; r += gridDim.x * blockDim.x) {
+        int d = P.ep - 1;
+        while (d > 0 && s_soff[d] > r) --d;
+        const int pos = s_roff[d] + (r - s_soff[d]);
+        if (pos >= recv_cap) continue;
+        const int t = stok[r];
+        const int u = (t >= 0 && t < T) ? uidx[static_cast<size_t>(d) * T + t] : -1;
+        reinterpret_cast<int32_t*>(P.base[d] + P.off_pmap)[pos] = u >= 0 ? s_uoff[d] + u : recv_cap;
     }
     __threadfence_system();
 }
@@ -402,11 +525,11 @@ ep_combine_send_kernel(const EpPeers P, const uint8_t* __restrict__ y, const int
                        const int32_t* __restrict__ plan, size_t row_bytes, int ycap, int y_rows) {
     __shared__ int s_roff[kMaxEpRanks], s_ys[kMaxEpRanks];
     for (int d = threadIdx.x; d < P.ep; d += blockDim.x) {
-        s_roff[d] = plan[6 * d + kPlanRecvOff];
-        s_ys[d] = plan[6 * d + kPlanYsoff];
+        s_roff[d] = plan[kPlanStride * d + kPlanRecvOff];
+        s_ys[d] = plan[kPlanStride * d + kPlanYsoff];
     }
     __syncthreads();
-    const int rtot = plan[6 * P.ep + 1];
+    const int rtot = plan[kPlanStride * P.ep + 1];
     const int lane = threadIdx.x & 31;
     const int nwarps = (gridDim.x * blockDim.x) >> 5;
     const int vec = static_cast<int>(row_bytes / 16);
@@ -433,8 +556,8 @@ ep_return_rows_kernel(const EpPeers P, const int32_t* __restrict__ row_src, cons
                       void** __restrict__ row_out) {
     __shared__ int s_roff[kMaxEpRanks], s_ys[kMaxEpRanks];
     for (int d = threadIdx.x; d < P.ep; d += blockDim.x) {
-        s_roff[d] = plan[6 * d + kPlanRecvOff];
-        s_ys[d] = plan[6 * d + kPlanYsoff];
+        s_roff[d] = plan[kPlanStride * d + kPlanRecvOff];
+        s_ys[d] = plan[kPlanStride * d + kPlanYsoff];
     }
     __syncthreads();
     const int R = min(*total_rows, row_capacity);
@@ -599,6 +722,7 @@ EpPeers to_dev(const Peers& P) {
     d.off_flags = P.lay.off_flags;
     d.off_table = P.lay.off_table;
     d.off_recv = P.lay.off_recv;
+    d.off_pmap = P.lay.off_pmap;
     d.off_yrecv = P.lay.off_yrecv;
     d.timeout_ns = P.timeout_ns;
     return d;
@@ -614,34 +738,55 @@ Layout layout(int ep, int E, int recv_cap, size_t row_bytes, size_t y_rows, int 
     L.off_flags = o;
     o = up256(o + 3 * kMaxEpRanks * sizeof(uint32_t));
     L.off_table = o;
-    o = up256(o + static_cast<size_t>(ep) * E * sizeof(int32_t));
+    o = up256(o + static_cast<size_t>(ep) * (E + ep) * sizeof(int32_t));
     L.off_recv = o;
     o = up256(o + static_cast<size_t>(recv_cap) * row_bytes);
+    L.off_pmap = o;
+    o = up256(o + static_cast<size_t>(recv_cap) * sizeof(int32_t));
     L.off_yrecv = o;
     o = up256(o + y_rows * static_cast<size_t>(H) * 2);
     L.bytes = o;
     return L;
 }
 
-moe_status_t counts(const Peers& P, const int32_t* ecounts, uint32_t* epoch_dev, int32_t* plan, int32_t* rcounts,
-                    int* error_word, cudaStream_t st) {
+moe_status_t unique_rows(const Peers& P, const int32_t* vid, int T, int K, int32_t* uidx, int32_t* utok,
+                         int32_t* ucounts, cudaStream_t st) {
+    if (T < 0 || K <= 0 || P.ep <= 0 || P.ep > kMaxEpRanks || P.epr <= 0) return MOE_ERR_INVALID_ARGUMENT;
+    ep_unique_kernel<<<1, kUniqueThreads, 0, st>>>(vid, T, K, P.ep, P.epr, uidx, utok, ucounts);
+    return launch_status();
+}
+
+moe_status_t counts(const Peers& P, const int32_t* ecounts, const int32_t* ucounts, uint32_t* epoch_dev,
+                    int32_t* plan, int32_t* rcounts, int* error_word, cudaStream_t st) {
     // the counts of every source and this rank's own, staged in shared memory
     // (the opt-in is to the largest size once per device, so any layer fits)
-    const size_t smem = (static_cast<size_t>(P.ep) + 1) * P.E * sizeof(int);
+    const size_t smem = (static_cast<size_t>(P.ep) * (P.E + P.ep) + P.E) * sizeof(int);
     if (smem > 227 * 1024) return MOE_ERR_UNSUPPORTED;
     static bool attr[kMaxDevices] = {};
     if (smem > 48 * 1024 && smem_optin_once(ep_counts_kernel, 227 * 1024, attr) != cudaSuccess) return MOE_ERR_CUDA;
-    ep_counts_kernel<<<1, 256, smem, st>>>(to_dev(P), ecounts, epoch_dev, plan, rcounts, error_word);
+    ep_counts_kernel<<<1, 256, smem, st>>>(to_dev(P), ecounts, ucounts, epoch_dev, plan, rcounts, error_word);
     return launch_status();
 }
 
 moe_status_t dispatch(const Peers& P, const void* xq, const void* xq_lo, const float* xs, int xs_ld,
-                      const int32_t* stok, const int32_t* plan, int H, size_t row_bytes, int recv_cap, int max_rows,
-                      cudaStream_t st) {
+                      const int32_t* stok, const int32_t* uidx, const int32_t* utok, int T, const int32_t* plan, int H,
+                      size_t row_bytes, int recv_cap, int max_rows, cudaStream_t st) {
     if (max_rows <= 0) return MOE_OK;
     ep_dispatch_kernel<<<grid_for_rows(max_rows), 256, 0, st>>>(to_dev(P), static_cast<const uint8_t*>(xq), xs,
-                                                                 xs_ld, stok, plan, H, row_bytes, recv_cap,
-                                                                 static_cast<const uint8_t*>(xq_lo));
+                                                                 xs_ld, stok, uidx, utok, T, plan, H, row_bytes,
+                                                                 recv_cap, static_cast<const uint8_t*>(xq_lo));
+    return launch_status();
+}
+
+moe_status_t gather(const Peers& P, const void* xq, const void* xq_lo, const float* xs, int xs_ld,
+                    const int32_t* row_src, const int32_t* total_rows, int row_capacity, int H, size_t row_bytes,
+                    int recv_cap, void* xp, void* xp_lo, float* xps, int xps_ld, cudaStream_t st) {
+    if (row_capacity <= 0) return MOE_OK;
+    const uint8_t* mine = static_cast<const uint8_t*>(P.base[P.me]);
+    ep_gather_kernel<<<grid_for_rows(row_capacity), 256, 0, st>>>(
+        mine + P.lay.off_recv, row_bytes, static_cast<const uint8_t*>(xq), xs, xs_ld, row_src, total_rows,
+        row_capacity, H, static_cast<uint8_t*>(xp), xps, xps_ld, static_cast<const uint8_t*>(xq_lo),
+        static_cast<uint8_t*>(xp_lo), reinterpret_cast<const int32_t*>(mine + P.lay.off_pmap), recv_cap);
     return launch_status();
 }
 

@@ -33,6 +33,8 @@
 //   ysend  [recv_cap][H] bf16 / yrecv [T*k][H] bf16  combine exchange
 //   row_out [R_cap] pointers        peer exchange: each GEMM row's output
 //                                  address (the owner's yrecv slot or local y)
+//   uidx/utok [ep][T] i32, ucount [ep]  peer exchange: this rank's tokens
+//                                  with a pair for each destination rank
 // and R_cap = recv_cap + S*T + 16*G (rounded to 16).
 #include <cuda_runtime.h>
 
@@ -67,6 +69,7 @@ struct moe_layer {
     int xs_ld, rcap;
     // expert parallelism
     size_t off_ecounts, off_estart, off_stotal, off_stok, off_psend, off_precv, off_rdst, off_ysend, off_yrecv;
+    size_t off_uidx, off_utok, off_ucount;   // peer exchange: tokens per destination rank
     size_t row_bytes, off_vidx;
     int recv_cap;
     int32_t* h_counts;    // pinned [2E]
@@ -143,6 +146,9 @@ void plan_workspace(moe_layer* L) {
         L->off_plan = take(tbep::plan_ints(c.ep_size) * 4);
         L->off_vidx = take(T * K * 4);
         L->off_rowout = take(R * sizeof(void*));
+        L->off_uidx = take(static_cast<size_t>(c.ep_size) * T * 4);
+        L->off_utok = take(static_cast<size_t>(c.ep_size) * T * 4);
+        L->off_ucount = take(static_cast<size_t>(c.ep_size) * 4);
     }
     L->bytes = o;
 }
@@ -296,19 +302,24 @@ moe_status_t run_experts_ep(moe_layer* L, const int32_t* idx, const float* wts, 
         mark(L, 2, st);
         MOE_TRY(moe_permute_mb(sort_ids, T, K, 0, E, 0, ecounts, at<int32_t>(ws, L->off_estart), spos, stok, stotal,
                                    T * K, L->error_word, 1, at<void>(ws, L->off_bcounts), L->bcounts_bytes, st));
-        MOE_TRY(tbep::counts(P, ecounts, epoch, plan, rcounts, L->error_word, st));
+        // each token travels once per destination rank, however many of its experts live there
+        int32_t* uidx = at<int32_t>(ws, L->off_uidx);
+        int32_t* utok = at<int32_t>(ws, L->off_utok);
+        int32_t* ucount = at<int32_t>(ws, L->off_ucount);
+        MOE_TRY(tbep::unique_rows(P, sort_ids, T, K, uidx, utok, ucount, st));
+        MOE_TRY(tbep::counts(P, ecounts, ucount, epoch, plan, rcounts, L->error_word, st));
         mark(L, 3, st);
         const bool x2 = L->act_planes == 2;
         void* xq_lo = x2 ? at<void>(ws, L->off_xq_lo) : nullptr;
         void* xp_lo = x2 ? at<void>(ws, L->off_xp + L->rcap * static_cast<size_t>(H)) : nullptr;
-        MOE_TRY(tbep::dispatch(P, at<void>(ws, L->off_xq), xq_lo, at<float>(ws, L->off_xs), L->xs_ld, stok, plan, H,
-                               rb, L->recv_cap, T * K, st));
+        MOE_TRY(tbep::dispatch(P, at<void>(ws, L->off_xq), xq_lo, at<float>(ws, L->off_xs), L->xs_ld, stok, uidx,
+                               utok, T, plan, H, rb, L->recv_cap, T * K, st));
         MOE_TRY(tbep::signal_wait(P, tbep::kDispatch, epoch, L->error_word, st));
         MOE_TRY(moe_ep_recv_plan(rcounts, ep, epr, T, S, counts, start, total, row_src, recv_dst, L->rcap, L->recv_cap,
                                  L->error_word, st));
-        MOE_TRY(moe_ep_gather_x2(mine + P.lay.off_recv, at<void>(ws, L->off_xq), xq_lo, at<float>(ws, L->off_xs),
-                                 L->xs_ld, row_src, total, L->rcap, H, at<void>(ws, L->off_xp), xp_lo,
-                                 at<float>(ws, L->off_xps), L->rcap, st));
+        MOE_TRY(tbep::gather(P, at<void>(ws, L->off_xq), xq_lo, at<float>(ws, L->off_xs), L->xs_ld, row_src, total,
+                             L->rcap, H, rb, L->recv_cap, at<void>(ws, L->off_xp), xp_lo, at<float>(ws, L->off_xps),
+                             L->rcap, st));
         // fused return: every received row's output address in its owner's
         // return buffer, for the down GEMM's epilogue
         const bool fused = L->fused_return && down_token_major(L, T);
