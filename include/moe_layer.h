@@ -400,6 +400,16 @@ moe_status_t moe_ep_gather_x2(const void* packed, const void* xq, const void* xq
 moe_status_t moe_ep_remap_experts(const int32_t* topk_idx, int num_pairs, int E,
                                   const int32_t* slot_of_expert, int32_t* vidx, cwStream_t stream);
 
+/* The peer exchange's per-destination numbering (one packed row per token
+ * and destination rank): for every rank d < ep_size, this rank's tokens with
+ * at least one pair whose expert id v (vidx, [T][k], -1 = none) lives on d
+ * (v / experts_per_rank == d), in token order.  Outputs (device):
+ * uidx [ep_size][T] (the token's row number for d, -1 when none),
+ * utok [ep_size][T] (the token of each row number; entries past ucount[d]
+ * are left as they were), ucount [ep_size].  ep_size <= 64. */
+moe_status_t moe_ep_token_rows(const int32_t* vidx, int T, int k, int ep_size, int experts_per_rank,
+                               int32_t* uidx, int32_t* utok, int32_t* ucount, cwStream_t stream);
+
 /* ysend[i] = y[recv_dst[i]] for i < n (bf16 rows of H). */
 moe_status_t moe_ep_pack_y(const void* y_bf16, const int32_t* recv_dst, int n, int H,
                            void* ysend_bf16, cwStream_t stream);

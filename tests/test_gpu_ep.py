@@ -283,6 +283,40 @@ def test_remap_experts_matches_table(gpu):
     assert torch.equal(vidx.cpu(), ref)
 
 
+@pytest.mark.parametrize("ep,E,T,K", [(2, 160, 2048, 8), (4, 160, 1024, 8), (8, 160, 512, 8), (8, 160, 2500, 8),
+                                      (5, 20, 3000, 4), (6, 162, 777, 8), (64, 128, 100, 8), (3, 9, 0, 2)])
+def test_ep_token_rows_numbering(gpu, ep, E, T, K):
+    """moe_ep_token_rows (the peer dispatch's one row per token and
+    destination rank): for every destination, the tokens with a pair there in
+    token order, against a direct count; several 1024-token chunks and more
+    than four destinations (several 64-bit scan groups) included."""
+    k = M.libs()["libkernels.so"]
+    epr = E // ep
+    g = torch.Generator().manual_seed(ep * 1000 + T)
+    vidx = torch.randint(-1, ep * epr, (T, K), generator=g, dtype=torch.int32)
+    if T > 3:
+        vidx[0] = 0                                   # every slot on rank 0
+        vidx[1] = -1                                  # no valid slot
+        vidx[2, :] = ep * epr - 1                     # the last rank only
+    d_v = vidx.to(gpu)
+    uidx = torch.full((ep, max(T, 1)), -9, dtype=torch.int32, device=gpu)
+    utok = torch.full((ep, max(T, 1)), -9, dtype=torch.int32, device=gpu)
+    ucnt = torch.full((ep,), -9, dtype=torch.int32, device=gpu)
+    M.check("token_rows", k.moe_ep_token_rows(M.ptr(d_v) if T else None, T, K, ep, epr, M.ptr(uidx), M.ptr(utok),
+                                              M.ptr(ucnt), st()))
+    torch.cuda.synchronize()
+    v = vidx.numpy()
+    ui, ut, uc = uidx.cpu().numpy(), utok.cpu().numpy(), ucnt.cpu().numpy()
+    for d in range(ep):
+        has = ((v >= d * epr) & (v < (d + 1) * epr)).any(axis=1) if T else np.zeros(0, bool)
+        toks = np.nonzero(has)[0]
+        assert uc[d] == len(toks)
+        assert np.array_equal(ut[d, :len(toks)], toks)
+        ref = np.full(T, -1)
+        ref[toks] = np.arange(len(toks))
+        assert np.array_equal(ui[d, :T], ref)
+
+
 @pytest.mark.parametrize("ep,T", [(2, 64), (4, 37)])
 def test_ep_emulated_placement_tiny_bit_identical(gpu, ep, T):
     shape = synth.TINY

@@ -634,6 +634,15 @@ moe_status_t moe_ep_remap_experts(const int32_t* topk_idx, int num_pairs, int E,
     return launch_status();
 }
 
+moe_status_t moe_ep_token_rows(const int32_t* vidx, int T, int k, int ep_size, int experts_per_rank, int32_t* uidx,
+                               int32_t* utok, int32_t* ucount, cwStream_t stream) {
+    if (T < 0 || k <= 0 || ep_size <= 0 || ep_size > kMaxEpRanks || experts_per_rank <= 0) return MOE_ERR_INVALID_ARGUMENT;
+    if (!ucount || (T > 0 && (!vidx || !uidx || !utok))) return MOE_ERR_INVALID_ARGUMENT;
+    ep_unique_kernel<<<1, kUniqueThreads, 0, static_cast<cudaStream_t>(stream)>>>(vidx, T, k, ep_size,
+                                                                                 experts_per_rank, uidx, utok, ucount);
+    return launch_status();
+}
+
 moe_status_t moe_ep_pack_rows_x2(const void* xq, const void* xq_lo, const float* xs, int xs_ld,
                                  const int32_t* row_token, const int32_t* num_rows, int row_capacity, int H,
                                  void* packed, cwStream_t stream) {
@@ -751,9 +760,7 @@ Layout layout(int ep, int E, int recv_cap, size_t row_bytes, size_t y_rows, int 
 
 moe_status_t unique_rows(const Peers& P, const int32_t* vid, int T, int K, int32_t* uidx, int32_t* utok,
                          int32_t* ucounts, cudaStream_t st) {
-    if (T < 0 || K <= 0 || P.ep <= 0 || P.ep > kMaxEpRanks || P.epr <= 0) return MOE_ERR_INVALID_ARGUMENT;
-    ep_unique_kernel<<<1, kUniqueThreads, 0, st>>>(vid, T, K, P.ep, P.epr, uidx, utok, ucounts);
-    return launch_status();
+    return moe_ep_token_rows(vid, T, K, P.ep, P.epr, uidx, utok, ucounts, st);
 }
 
 moe_status_t counts(const Peers& P, const int32_t* ecounts, const int32_t* ucounts, uint32_t* epoch_dev,
