@@ -224,7 +224,7 @@ def test_permute_bit_exact(gpu, oracle, T, K, E, shared):
 @pytest.mark.parametrize("T,K,E,eb,ee,shared,pad", [(1, 1, 4, 0, 4, 1, 16), (37, 4, 9, 0, 9, 1, 16),
                                                      (4096, 8, 160, 0, 160, 1, 16), (4096, 8, 160, 0, 160, 0, 1),
                                                      (2048, 8, 160, 40, 60, 1, 16), (300, 2, 8, 0, 8, 0, 1),
-                                                     (513, 8, 160, 0, 160, 1, 16)])
+                                                     (513, 8, 160, 0, 160, 1, 16), (5000, 8, 160, 0, 160, 1, 16)])
 def test_permute_multiblock_matches_single_block(gpu, oracle, T, K, E, eb, ee, shared, pad):
     """moe_permute_mb (the layer's permutation) against moe_permute_padded:
     identical counts, segment starts, pair rows and row tokens; and against

@@ -1147,13 +1147,22 @@ mp_scan_kernel(int32_t* __restrict__ bcounts, int nblocks, int Gr, int num_share
     int* start = cnt + G;      // [G]
     __shared__ int s_total;
     const int tid = threadIdx.x;
+    // a thread per group (consecutive groups: coalesced rows of bcounts); the
+    // counts of 16 blocks are loaded before any of them is overwritten, so a
+    // group costs nblocks / 16 memory round trips instead of nblocks; each
+    // block's count becomes its first rank within the group
     for (int g = tid; g < Gr; g += blockDim.x) {
         int run = 0;
-        for (int b = 0; b < nblocks; ++b) {
-            int32_t* c = bcounts + static_cast<size_t>(b) * Gr + g;
-            const int v = *c;
-            *c = run;                 // this block's first rank within group g
-            run += v;
+        for (int b0 = 0; b0 < nblocks; b0 += 16) {
+            int v[16];
+#pragma unroll
+            for (int u = 0; u < 16; ++u)
+                v[u] = b0 + u < nblocks ? bcounts[static_cast<size_t>(b0 + u) * Gr + g] : 0;
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+                if (b0 + u < nblocks) bcounts[static_cast<size_t>(b0 + u) * Gr + g] = run;
+                run += v[u];
+            }
         }
         cnt[g] = run;
     }
