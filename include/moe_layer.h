@@ -246,6 +246,18 @@ moe_status_t moe_gather_rows_x2(const void* xq, const void* xq_lo, const float* 
                                 const int32_t* row_token, const int32_t* total_rows, int row_capacity,
                                 int H, void* xp, void* xp_lo, float* xps, int xps_ld, cwStream_t stream);
 
+/* The rows of moe_gather_rows_x2, written token by token: token t's row
+ * (planes and scales) goes to each of its routed rows pos[t*k + s] >= 0 and to
+ * its shared-expert rows shared_start[g] + t (g < num_shared <= 2; device
+ * array); rows with row_token < 0 are zeroed.  xp, xp_lo and xps end up
+ * identical to moe_gather_rows_x2's for the same permutation, with each token
+ * read once.  k <= 16. */
+moe_status_t moe_scatter_rows_x2(const void* xq, const void* xq_lo, const float* xs, int xs_ld,
+                                 const int32_t* pos, int T, int k, const int32_t* shared_start,
+                                 int num_shared, const int32_t* row_token, const int32_t* total_rows,
+                                 int row_capacity, int H, void* xp, void* xp_lo, float* xps, int xps_ld,
+                                 cwStream_t stream);
+
 /* Top-k + weights of given logits [T][E] with the same rule as
  * moe_router_topk. */
 moe_status_t moe_topk_softmax(const float* logits, int T, int E, int k, int32_t* topk_idx,

@@ -101,6 +101,59 @@ def test_gather_rows_x2(gpu):
             assert torch.equal(xps[:, r], xs[:, t])
 
 
+
+@pytest.mark.parametrize("T,K,E,shared,planes,H", [(4096, 8, 160, 1, 2, 5120), (300, 8, 160, 1, 1, 512),
+                                                   (37, 4, 9, 0, 2, 640), (1, 16, 32, 1, 2, 512)])
+def test_scatter_rows_matches_gather(gpu, T, K, E, shared, planes, H):
+    """moe_scatter_rows_x2 (token-major: each token read once, stored to its
+    routed and shared rows) writes exactly the bytes of moe_gather_rows_x2 for
+    the layer's permutation, padding rows zeroed, over every row of the
+    layout (H = 5120: two 8-piece batches per lane, the second partial)."""
+    k = M.libs()["libkernels.so"]
+    g = torch.Generator().manual_seed(T * 3 + K)
+    idx = torch.randint(0, E, (T, K), generator=g, dtype=torch.int32)
+    if T > 2:
+        idx[1, 0] = -1                                   # an empty slot
+    d_idx = idx.to(gpu)
+    G = E + shared
+    cap = (T * K + shared * T + 16 * G + 15) // 16 * 16
+    counts = torch.zeros(G, dtype=torch.int32, device=gpu)
+    start = torch.zeros(G, dtype=torch.int32, device=gpu)
+    pos = torch.full((T * K,), -9, dtype=torch.int32, device=gpu)
+    rowtok = torch.full((cap,), -9, dtype=torch.int32, device=gpu)
+    total = torch.zeros(1, dtype=torch.int32, device=gpu)
+    err = torch.zeros(1, dtype=torch.int32, device=gpu)
+    nbytes = k.moe_permute_mb_scratch_bytes(T, K, 0, E)
+    scratch = torch.empty(max(nbytes, 4), dtype=torch.uint8, device=gpu)
+    M.check("permute_mb", k.moe_permute_mb(M.ptr(d_idx), T, K, 0, E, shared, M.ptr(counts), M.ptr(start), M.ptr(pos),
+                                           M.ptr(rowtok), M.ptr(total), cap, M.ptr(err), 16, M.ptr(scratch), nbytes,
+                                           stream()))
+    ld = (T + 3) // 4 * 4
+    xq = torch.randint(0, 255, (T, H), generator=g, dtype=torch.uint8).to(gpu)
+    xl = torch.randint(0, 255, (T, H), generator=g, dtype=torch.uint8).to(gpu) if planes == 2 else None
+    xs = torch.rand(H // 128, ld, generator=g).to(gpu)
+    outs = []
+    for fn in ("gather", "scatter"):
+        xp = torch.full((2, cap, H), 0x33, dtype=torch.uint8, device=gpu)
+        xps = torch.full((H // 128, cap), -1.0, device=gpu)
+        lo_in = M.ptr(xl) if xl is not None else None
+        lo_out = M.ptr(xp[1]) if xl is not None else None
+        if fn == "gather":
+            M.check("gather", k.moe_gather_rows_x2(M.ptr(xq), lo_in, M.ptr(xs), ld, M.ptr(rowtok), M.ptr(total), cap,
+                                                   H, M.ptr(xp[0]), lo_out, M.ptr(xps), cap, stream()))
+        else:
+            M.check("scatter", k.moe_scatter_rows_x2(M.ptr(xq), lo_in, M.ptr(xs), ld, M.ptr(pos), T, K,
+                                                     M.ptr(start[E:]) if shared else None, shared, M.ptr(rowtok),
+                                                     M.ptr(total), cap, H, M.ptr(xp[0]), lo_out, M.ptr(xps), cap,
+                                                     stream()))
+        torch.cuda.synchronize()
+        outs.append((xp.cpu(), xps.cpu()))
+    R = int(total.item())
+    assert err.item() == 0 and R > 0
+    assert torch.equal(outs[0][0][:, :R], outs[1][0][:, :R])
+    assert torch.equal(outs[0][1][:, :R], outs[1][1][:, :R])
+
+
 def _groups_x2(counts, K, Nw, g):
     G = len(counts)
     starts, row = [], 0

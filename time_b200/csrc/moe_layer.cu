@@ -249,10 +249,13 @@ moe_status_t run_experts(moe_layer* L, const void* x, const int32_t* idx, const 
                            L->error_word, 16, at<void>(ws, L->off_bcounts), L->bcounts_bytes, st));
     mark(L, 3, st);
     const bool x2 = L->act_planes == 2;
-    MOE_TRY(moe_gather_rows_x2(at<void>(ws, L->off_xq), x2 ? at<void>(ws, L->off_xq_lo) : nullptr,
-                               at<float>(ws, L->off_xs), L->xs_ld, rowtok, total, L->rcap, H, at<void>(ws, L->off_xp),
-                               x2 ? at<void>(ws, L->off_xp + L->rcap * static_cast<size_t>(H)) : nullptr,
-                               at<float>(ws, L->off_xps), L->rcap, st));
+    // token-major: each token's row is read once and stored to its k routed
+    // rows and its shared-expert rows (the same bytes as the row-major gather)
+    MOE_TRY(moe_scatter_rows_x2(at<void>(ws, L->off_xq), x2 ? at<void>(ws, L->off_xq_lo) : nullptr,
+                                at<float>(ws, L->off_xs), L->xs_ld, pos, T, K, start + (L->e_end - L->e_begin), S,
+                                rowtok, total, L->rcap, H, at<void>(ws, L->off_xp),
+                                x2 ? at<void>(ws, L->off_xp + L->rcap * static_cast<size_t>(H)) : nullptr,
+                                at<float>(ws, L->off_xps), L->rcap, st));
     cbwGroupedGemmArgs g1 = gemm_args(L, ws, false, T), g2 = gemm_args(L, ws, true, T);
     mark(L, 4, st);
     MOE_TRY(cbw_to_moe(cbwFp8BlockScaledGroupedGemm(&g1, L->error_word, st)));

@@ -1270,6 +1270,92 @@ gather_rows_kernel(const uint8_t* __restrict__ xq, const float* __restrict__ xs,
     }
 }
 
+// Token-major form of gather_rows_kernel for the layer: a warp takes token t
+// and stores its row (both planes and its 1x128 scales) into each of its
+// routed rows pos[t*K + s] >= 0 and its shared-expert rows shared_start[g] + t,
+// reading the token once (the row-major gather re-reads a token for every row
+// it fills, and its write stream pushes the token out of L2 in between).  A
+// lane loads 8 of the row's 16-byte pieces before storing them to every
+// destination.  Rows that no pair fills (row_token < 0: segment padding) are
+// zeroed as the gather zeroes them, so xp and xps come out identical to
+// gather_rows_kernel's.
+constexpr int kScatterMaxK = 16, kScatterMaxShared = 2, kScatterPieces = 8;
+
+__device__ __forceinline__ void scatter_plane(const int4* __restrict__ src, uint8_t* __restrict__ base, int H,
+                                              int vec, int lane, const int (&r)[kScatterMaxK + kScatterMaxShared]) {
+    for (int c0 = lane; c0 < vec; c0 += 32 * kScatterPieces) {
+        int4 v[kScatterPieces];
+#pragma unroll
+        for (int u = 0; u < kScatterPieces; ++u) {
+            const int c = c0 + 32 * u;
+            if (c < vec) v[u] = src[c];
+        }
+#pragma unroll
+        for (int d = 0; d < kScatterMaxK + kScatterMaxShared; ++d) {
+            if (r[d] < 0) continue;
+            int4* dst = reinterpret_cast<int4*>(base + static_cast<size_t>(r[d]) * H);
+#pragma unroll
+            for (int u = 0; u < kScatterPieces; ++u) {
+                const int c = c0 + 32 * u;
+                if (c < vec) dst[c] = v[u];
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256)
+scatter_rows_kernel(const uint8_t* __restrict__ xq, const float* __restrict__ xs, int xs_ld,
+                    const int32_t* __restrict__ pos, int T, int K, const int32_t* __restrict__ shared_start,
+                    int num_shared, const int32_t* __restrict__ row_token, const int32_t* __restrict__ total_rows,
+                    int row_capacity, int H, uint8_t* __restrict__ xp, float* __restrict__ xps, int xps_ld,
+                    const uint8_t* __restrict__ xq_lo, uint8_t* __restrict__ xp_lo) {
+    const int R = min(*total_rows, row_capacity);
+    if (R <= 0) return;
+    const int lane = threadIdx.x & 31;
+    const int nwarps = (gridDim.x * blockDim.x) >> 5;
+    const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int vec = H / 16, nblk = H / 128;
+    for (int t = gw; t < T; t += nwarps) {
+        int r[kScatterMaxK + kScatterMaxShared];
+#pragma unroll
+        for (int s = 0; s < kScatterMaxK; ++s) {
+            const int v = s < K ? pos[static_cast<size_t>(t) * K + s] : -1;
+            r[s] = (v >= 0 && v < R) ? v : -1;
+        }
+#pragma unroll
+        for (int g = 0; g < kScatterMaxShared; ++g) {
+            const int v = g < num_shared ? shared_start[g] + t : -1;
+            r[kScatterMaxK + g] = (v >= 0 && v < R) ? v : -1;
+        }
+        scatter_plane(reinterpret_cast<const int4*>(xq + static_cast<size_t>(t) * H), xp, H, vec, lane, r);
+        if (xp_lo) scatter_plane(reinterpret_cast<const int4*>(xq_lo + static_cast<size_t>(t) * H), xp_lo, H, vec, lane, r);
+        for (int b = lane; b < nblk; b += 32) {
+            const float v = xs[static_cast<size_t>(b) * xs_ld + t];
+#pragma unroll
+            for (int d = 0; d < kScatterMaxK + kScatterMaxShared; ++d)
+                if (r[d] >= 0) xps[static_cast<size_t>(b) * xps_ld + r[d]] = v;
+        }
+    }
+    // padding rows: zero, 32 rows looked up per step
+    const int4 z = make_int4(0, 0, 0, 0);
+    for (int r0 = gw * 32; r0 < R; r0 += nwarps * 32) {
+        const int rr = r0 + lane;
+        unsigned pad = __ballot_sync(0xffffffffu, rr < R && row_token[rr] < 0);
+        while (pad) {
+            const int i = __ffs(pad) - 1;
+            pad &= pad - 1;
+            const int row = r0 + i;
+            int4* dst = reinterpret_cast<int4*>(xp + static_cast<size_t>(row) * H);
+            for (int c = lane; c < vec; c += 32) dst[c] = z;
+            if (xp_lo) {
+                int4* dlo = reinterpret_cast<int4*>(xp_lo + static_cast<size_t>(row) * H);
+                for (int c = lane; c < vec; c += 32) dlo[c] = z;
+            }
+            for (int b = lane; b < nblk; b += 32) xps[static_cast<size_t>(b) * xps_ld + row] = 0.0f;
+        }
+    }
+}
+
 // ---------------------------------------------------------------- combine
 // out[t] = bf16(x + sum shared ys[shared_rows[g] + t] + sum_s fma(w, y[pos]) ),
 // 8 columns per thread.  y holds the routed rows, ys the shared expert's (the
@@ -1663,6 +1749,29 @@ moe_status_t moe_gather_rows_x2(const void* xq, const void* xq_lo, const float* 
     gather_rows_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const uint8_t*>(xq), xs, xs_ld, row_token, total_rows, row_capacity, H,
         static_cast<uint8_t*>(xp), xps, xps_ld, static_cast<const uint8_t*>(xq_lo), static_cast<uint8_t*>(xp_lo));
+    return launch_status();
+}
+
+moe_status_t moe_scatter_rows_x2(const void* xq, const void* xq_lo, const float* xs, int xs_ld, const int32_t* pos,
+                                 int T, int k, const int32_t* shared_start, int num_shared, const int32_t* row_token,
+                                 const int32_t* total_rows, int row_capacity, int H, void* xp, void* xp_lo, float* xps,
+                                 int xps_ld, cwStream_t stream) {
+    if (H <= 0 || H % 128 || T < 0 || k <= 0 || k > kScatterMaxK || num_shared < 0 || num_shared > kScatterMaxShared ||
+        row_capacity < 0 || xps_ld < row_capacity)
+        return MOE_ERR_INVALID_ARGUMENT;
+    if (!xq || !xs || !row_token || !total_rows || !xp || !xps || (T > 0 && !pos) || (num_shared > 0 && !shared_start))
+        return MOE_ERR_INVALID_ARGUMENT;
+    if (!aligned16(xq) || !aligned16(xp)) return MOE_ERR_INVALID_ARGUMENT;
+    if (!xq_lo != !xp_lo || (xq_lo && (!aligned16(xq_lo) || !aligned16(xp_lo)))) return MOE_ERR_INVALID_ARGUMENT;
+    if (row_capacity == 0) return MOE_OK;
+    long long blocks = (static_cast<long long>(T) + 7) / 8;
+    const long long pad_blocks = (static_cast<long long>(row_capacity) + 255) / 256;
+    if (blocks < pad_blocks) blocks = pad_blocks;
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    scatter_rows_kernel<<<static_cast<int>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint8_t*>(xq), xs, xs_ld, pos, T, k, shared_start, num_shared, row_token, total_rows,
+        row_capacity, H, static_cast<uint8_t*>(xp), xps, xps_ld, static_cast<const uint8_t*>(xq_lo),
+        static_cast<uint8_t*>(xp_lo));
     return launch_status();
 }
 

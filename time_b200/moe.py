@@ -114,6 +114,9 @@ def libs():
         k.moe_gather_rows_x2.argtypes = [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int, c_int,
                                          c_void_p, c_void_p, c_void_p, c_int, c_void_p]
         k.moe_ep_remap_experts.argtypes = [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p]
+        k.moe_scatter_rows_x2.argtypes = [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_int,
+                                          c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int,
+                                          c_void_p]
         k.moe_ep_token_rows.argtypes = [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p]
         k.moe_layer_peer_bytes.argtypes = [c_void_p]
         k.moe_layer_peer_bytes.restype = c_size_t
