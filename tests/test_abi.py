@@ -102,3 +102,40 @@ def test_engine_wrapper_symbols(libdir):
     assert all(n in syms for n in ENGINE_WRAPPER_SYMBOLS), [n for n in ENGINE_WRAPPER_SYMBOLS if n not in syms]
     names = declared_functions(INCLUDE / "engine.h")
     assert names[:7] == ENGINE_WRAPPER_SYMBOLS, names[:7]
+
+
+def test_row_entry_points_refuse_bad_arguments_without_launching(libdir):
+    """moe_scatter_rows_x2 and moe_ep_token_rows check every argument before
+    any CUDA call, so a refused call returns MOE_ERR_INVALID_ARGUMENT (1) on
+    a machine without a GPU; none of these pointers is ever dereferenced."""
+    import time_b200
+    k = time_b200.load()["libkernels.so"]
+    vp, ci = ctypes.c_void_p, ctypes.c_int
+    k.moe_scatter_rows_x2.argtypes = [vp, vp, vp, ci, vp, ci, ci, vp, ci, vp, vp, ci, ci, vp, vp, vp, ci, vp]
+    k.moe_ep_token_rows.argtypes = [vp, ci, ci, ci, ci, vp, vp, vp, vp]
+    fake = 0x1000                                     # 16-byte aligned, never dereferenced
+
+    def scatter(**over):
+        a = dict(xq=fake, xq_lo=None, xs=fake, xs_ld=64, pos=fake, T=64, k=8, shared=fake, ns=1, rowtok=fake,
+                 total=fake, cap=1024, H=512, xp=fake, xp_lo=None, xps=fake, xps_ld=1024)
+        a.update(over)
+        return k.moe_scatter_rows_x2(a["xq"], a["xq_lo"], a["xs"], a["xs_ld"], a["pos"], a["T"], a["k"], a["shared"],
+                                     a["ns"], a["rowtok"], a["total"], a["cap"], a["H"], a["xp"], a["xp_lo"], a["xps"],
+                                     a["xps_ld"], None)
+    assert scatter(k=17) == 1                          # more slots than a token can have
+    assert scatter(k=0) == 1
+    assert scatter(ns=3) == 1                          # at most two shared experts
+    assert scatter(H=500) == 1                         # H % 128
+    assert scatter(xps_ld=1000) == 1                   # scale rows shorter than the layout
+    assert scatter(xq=fake + 8) == 1                   # misaligned rows
+    assert scatter(xq_lo=fake) == 1                    # one lo pointer without the other
+    assert scatter(shared=None) == 1                   # shared rows without their starts
+    assert scatter(cap=0) == 0                         # nothing to write: no launch
+
+    def token_rows(ep, epr=20, T=64, K=8, ptrs=True):
+        p = fake if ptrs else None
+        return k.moe_ep_token_rows(p, T, K, ep, epr, p, p, fake, None)
+    assert token_rows(65) == 1                         # more ranks than the numbering supports
+    assert token_rows(0) == 1
+    assert token_rows(8, epr=0) == 1
+    assert token_rows(8, ptrs=False) == 1              # T > 0 needs vidx, uidx, utok
