@@ -158,3 +158,88 @@ def test_expert_slice_follows_placement():
         for j, e in enumerate(experts):
             assert torch.equal(ws["w13"][j], w["w13"][e]) and torch.equal(ws["s2"][j], w["s2"][e])
         assert torch.equal(ws["w13"][4], w["w13"][8])          # shared expert last
+
+
+def _worker_token_rows(rank, world, port, T, E, K, seed, q):
+    """The NVLink peer exchange's layout on gloo ranks: each token travels once
+    per destination rank (numbered per destination in token order), every
+    pair carries the index of its row in the destination's receive buffer
+    (the pair map), and the receiver reading pair i's row through the map
+    finds the token of the pair-level exchange's row i."""
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        from time_b200 import synth
+        epr = E // world
+        idx_all = _global_routing(T, E, K, seed)
+        t0, t1 = synth.token_slice(T, world, rank)
+        idx = idx_all[t0:t1]
+        Tr = t1 - t0
+        flat = idx.reshape(-1)
+        pairs = np.nonzero(flat >= 0)[0]
+        order = pairs[np.argsort(flat[pairs], kind="stable")]          # dense send order
+        ecounts = np.bincount(flat[flat >= 0], minlength=E).astype(np.int64)
+        srows = [int(ecounts[d * epr:(d + 1) * epr].sum()) for d in range(world)]
+        # per-destination numbering of this rank's tokens (ep_unique_kernel)
+        uidx = np.full((world, Tr), -1, dtype=np.int64)
+        utok = [[] for _ in range(world)]
+        for t in range(Tr):
+            for d in sorted({int(e) // epr for e in idx[t] if e >= 0}):
+                uidx[d, t] = len(utok[d])
+                utok[d].append(t)
+        ucount = torch.tensor([len(u) for u in utok], dtype=torch.int64)
+        table = [torch.empty_like(ucount) for _ in range(world)]            # every rank's row counts
+        dist.all_gather(table, ucount)
+        U = torch.stack(table).numpy()                                       # U[s][d]
+        ubefore = [int(U[:rank, d].sum()) for d in range(world)]            # where my rows land on d
+        # rows: one per (destination, token), carrying the global token id
+        rows_out = torch.tensor([t0 + t for d in range(world) for t in utok[d]], dtype=torch.int64)
+        rrows_u = [int(U[s, rank]) for s in range(world)]
+        rows_in = torch.empty(sum(rrows_u), dtype=torch.int64)
+        dist.all_to_all_single(rows_in, rows_out, output_split_sizes=rrows_u,
+                               input_split_sizes=[len(u) for u in utok])
+        # pair map: for every sent pair (send order), its row in the destination's recv
+        pmap_out = []
+        for r in order:
+            d = int(flat[r]) // epr
+            pmap_out.append(ubefore[d] + int(uidx[d, r // K]))
+        recv = torch.empty(E, dtype=torch.int64)
+        dist.all_to_all_single(recv, torch.from_numpy(ecounts))
+        rrows = [int(v) for v in recv.view(world, epr).sum(1)]
+        pmap_in = torch.empty(sum(rrows), dtype=torch.int64)
+        dist.all_to_all_single(pmap_in, torch.tensor(pmap_out, dtype=torch.int64), output_split_sizes=rrows,
+                               input_split_sizes=srows)
+        # the pair-level exchange of the same pairs, for comparison
+        gid = torch.from_numpy((t0 * K + order).astype(np.int64))
+        got = torch.empty(sum(rrows), dtype=torch.int64)
+        dist.all_to_all_single(got, gid, output_split_sizes=rrows, input_split_sizes=srows)
+        pm, rin = pmap_in.numpy(), rows_in.numpy()
+        assert (pm >= 0).all() and (pm < len(rin)).all()
+        assert np.array_equal(rin[pm], got.numpy() // K), rank
+        assert len(rin) <= len(got)                                          # never more rows than pairs
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, "ok"))
+    except BaseException as exc:   # report to the parent instead of hanging it
+        q.put((rank, repr(exc)))
+
+
+@pytest.mark.parametrize("world,T,E,K", [(2, 200, 160, 8), (4, 64, 160, 8), (2, 1, 16, 4)])
+def test_ep_token_rows_layout_gloo(world, T, E, K):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_token_rows, args=(r, world, port, T, E, K, 13, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    try:
+        for _ in range(world):
+            r, msg = q.get(timeout=180)
+            results[r] = msg
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    assert results == {r: "ok" for r in range(world)}, results
